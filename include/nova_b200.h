@@ -1,0 +1,144 @@
+/*
+ * nova_b200 -- C ABI of the B200 (sm_100a) kernels for Nova's quantized decode
+ * hot path.  Plain pointers, int64 sizes/strides and a cudaStream_t passed as
+ * `void*`; no torch types.  Every call is asynchronous on `stream`, allocates
+ * nothing and never synchronizes, so all of them can be captured in a CUDA
+ * graph.  Every call returns a status code (NOVA_OK == 0); on failure
+ * nova_last_error() returns a message (thread-local).  Argument problems are
+ * detected on the host before anything is launched.
+ *
+ * Reference citations are paths inside captain-wangrun-cn/Nova.
+ */
+#ifndef NOVA_B200_H
+#define NOVA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NOVA_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define NOVA_API __attribute__((visibility("default")))
+#else
+#define NOVA_API
+#endif
+
+enum nova_status {
+    NOVA_OK = 0,
+    NOVA_ERR_INVALID = 1,     /* bad shape / size / range  -> Python ValueError   */
+    NOVA_ERR_ALIGN = 2,       /* pointer or stride alignment -> ValueError         */
+    NOVA_ERR_UNSUPPORTED = 3, /* valid but not built for (e.g. head_dim != 128)    */
+    NOVA_ERR_CUDA = 4         /* launch / runtime failure   -> Python RuntimeError */
+};
+
+/* Library identification and the last error message of the calling thread. */
+NOVA_API const char* nova_version(void);
+NOVA_API const char* nova_last_error(void);
+
+/* ------------------------------------------------------------------ int8 KV */
+
+/*
+ * Token-axis int8 quantization ("int8t64"): for each of `rows` independent
+ * [n, dim] fp16 matrices, per channel and per group of `group` consecutive
+ * tokens: step = max((max-min)/255, 1e-8), q = clamp(rne((x-min)/step), 0, 255);
+ * min/step stored as fp16 [ceil(n/group), dim].  A ragged last group uses only
+ * its real tokens (the reference pads by repeating the last token, which does
+ * not change min/max).  Strides are in elements between consecutive rows.
+ * Replaces src/nova/kvquant.py:118-149 quantize_int8(x, group, "token") and the
+ * prefill path KVInt8Cache.finish_prefill (src/nova/kvattn.py:745-783).
+ */
+NOVA_API int nova_kv_quant_int8(const void* x, int64_t x_row_stride, void* q, int64_t q_row_stride, void* mins,
+                       void* steps, int64_t s_row_stride, int64_t rows, int64_t n, int64_t dim, int64_t group,
+                       void* stream);
+
+/*
+ * Inverse of nova_kv_quant_int8: x = fp16(q * step + min).
+ * Replaces src/nova/kvquant.py:152-176 dequantize_int8(..., axis="token").
+ */
+NOVA_API int nova_kv_dequant_int8(const void* q, int64_t q_row_stride, const void* mins, const void* steps,
+                         int64_t s_row_stride, void* x, int64_t x_row_stride, int64_t rows, int64_t n, int64_t dim,
+                         int64_t group, void* stream);
+
+/*
+ * Decode-step append into the streaming int8 cache of one layer.
+ * k_new/v_new: fp16 [batch, kv_heads, dim] (strides in elements); the token
+ * goes to ring slot pos % group of tail_k/tail_v (fp16 [batch, kv_heads,
+ * group, dim]).  When that write completes a group (pos % group == group-1)
+ * the ring is requantized into group pos / group of kq/vq (uint8 [batch,
+ * kv_heads, max_len, dim]) and kmn/kst/vmn/vst (fp16 [batch, kv_heads,
+ * ceil(max_len/group), dim]).  The device scalars become written = pos+1,
+ * qlen = group*floor(written/group), pg = qlen/group.  `pos` is read on the
+ * device, so one captured graph stays valid as the context grows.
+ * Replaces KVInt8Cache.update decode branch (src/nova/kvattn.py:668-691),
+ * _quantize_ring (:716-743) and _sync_scalars (:699-710).  The reference
+ * requantizes the partially filled ring at every step into a group that is
+ * not read until it is full; this call writes it once, when it is full, so
+ * every byte that attention reads is identical.
+ */
+NOVA_API int nova_kv_append_int8(const void* k_new, const void* v_new, int64_t new_b_stride, int64_t new_h_stride,
+                        void* tail_k, void* tail_v, void* kq, void* vq, void* kmn, void* kst, void* vmn, void* vst,
+                        const int64_t* pos, int64_t* written, int64_t* qlen, int64_t* pg, int64_t batch,
+                        int64_t kv_heads, int64_t max_len, int64_t dim, int64_t group, void* stream);
+
+/* ------------------------------------------------------------ attention */
+
+/*
+ * Fused GQA decode attention over the streaming int8 cache: int8 prefix
+ * [0, min(qlen, pg*group, max_len)) dequantized in registers, plus (when
+ * tail_k != NULL) the fp16 ring tail (slot i holds position
+ * u - ((u - i) mod group), u = written-1, valid when qlen <= p <= u), one
+ * softmax over both, split-K over `chunk`-token splits with the combine done
+ * by the last CTA of each (batch, kv head).  window > 0 keeps positions
+ * p > u - window (prefix and tail); first (optional) drops p < first.
+ * Lengths are device scalars so a captured graph stays valid; n_splits fixes
+ * the grid (ceil(max_len/chunk) for a graph).  lse (optional) receives
+ * log-sum-exp of the scaled scores (-inf and out = 0 when nothing is valid).
+ * Requires head_dim == 128, group == 64, chunk % 64 == 0, q_heads/kv_heads <= 4.
+ * Replaces int8_attn_decode (src/nova/kvattn.py:281-427: partial kernel
+ * :110-203, combine :206-253), tail_attend (:447-482) and the merge in
+ * KVInt8Cache.attend (:835-862).
+ */
+typedef struct nova_attn_int8_args {
+    const void* q;          /* fp16 [batch, q_heads, 128]                      */
+    int64_t q_b_stride, q_h_stride;
+    const void* kq;         /* uint8 [batch, kv_heads, max_len, 128], contiguous */
+    const void* vq;
+    const void* kmn;        /* fp16 [batch, kv_heads, groups, 128], contiguous   */
+    const void* kst;
+    const void* vmn;
+    const void* vst;
+    const void* tail_k;     /* fp16 [batch, kv_heads, 64, 128] or NULL          */
+    const void* tail_v;
+    void* out;              /* fp16 [batch, q_heads, 128]                      */
+    int64_t o_b_stride, o_h_stride;
+    void* lse;              /* fp32 [batch, q_heads] or NULL                   */
+    int64_t lse_b_stride;
+    const int64_t* qlen;    /* device scalar: int8 prefix length (tokens)     */
+    const int64_t* pg;      /* device scalar: valid scale groups              */
+    const int64_t* written; /* device scalar or NULL (= qlen): tokens written */
+    const int64_t* first;   /* device scalar or NULL (= 0)                    */
+    void* workspace;        /* nova_attn_workspace_bytes() bytes, zeroed once  */
+    int64_t workspace_bytes;
+    int64_t batch, q_heads, kv_heads, max_len, groups, head_dim, group, chunk, n_splits, window;
+} nova_attn_int8_args;
+
+/* Bytes of workspace nova_attn_decode_int8 needs (split partials, per-head
+ * arrival counters and an error word).  Zero it once; the kernel leaves the
+ * counters at zero when it finishes. */
+NOVA_API int nova_attn_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t n_splits, int has_tail,
+                              int64_t* bytes);
+
+NOVA_API int nova_attn_decode_int8(const nova_attn_int8_args* args, void* stream);
+
+/* Device error word inside an attention workspace (non-zero = a bounded wait
+ * gave up); copies it to *host_value synchronously and clears it. */
+NOVA_API int nova_attn_read_error(void* workspace, int64_t batch, int64_t kv_heads, int* host_value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NOVA_B200_H */

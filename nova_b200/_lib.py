@@ -1,0 +1,121 @@
+"""ctypes binding of ``libnova_b200.so`` (declared in ``include/nova_b200.h``).
+
+The library is loaded from the package directory (built in-tree by
+``python -m nova_b200.build``).  There is no fallback: if the shared object is
+missing, or the tensors are not on a CUDA device, the calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().with_name("libnova_b200.so")
+
+NOVA_OK, NOVA_ERR_INVALID, NOVA_ERR_ALIGN, NOVA_ERR_UNSUPPORTED, NOVA_ERR_CUDA = range(5)
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int64
+_i = ctypes.c_int
+
+
+class AttnArgs(ctypes.Structure):
+    """Mirror of ``nova_attn_int8_args``."""
+
+    _fields_ = [
+        ("q", _P), ("q_b_stride", _I), ("q_h_stride", _I),
+        ("kq", _P), ("vq", _P), ("kmn", _P), ("kst", _P), ("vmn", _P), ("vst", _P),
+        ("tail_k", _P), ("tail_v", _P),
+        ("out", _P), ("o_b_stride", _I), ("o_h_stride", _I),
+        ("lse", _P), ("lse_b_stride", _I),
+        ("qlen", _P), ("pg", _P), ("written", _P), ("first", _P),
+        ("workspace", _P), ("workspace_bytes", _I),
+        ("batch", _I), ("q_heads", _I), ("kv_heads", _I), ("max_len", _I), ("groups", _I),
+        ("head_dim", _I), ("group", _I), ("chunk", _I), ("n_splits", _I), ("window", _I),
+    ]
+
+
+# name -> argtypes (every entry point returns int status unless noted)
+_SIGNATURES: dict[str, list] = {
+    "nova_kv_quant_int8": [_P, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P],
+    "nova_kv_dequant_int8": [_P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
+    "nova_kv_append_int8": [_P, _P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                            _I, _I, _I, _I, _I, _P],
+    "nova_attn_workspace_bytes": [_I, _I, _I, _I, _i, ctypes.POINTER(_I)],
+    "nova_attn_decode_int8": [ctypes.POINTER(AttnArgs), _P],
+    "nova_attn_read_error": [_P, _I, _I, ctypes.POINTER(_i)],
+}
+_STRING_FNS = ("nova_version", "nova_last_error")
+
+_lib: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the CUDA library.  Raises RuntimeError when the
+    shared object has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH.name} is not built; run `python -m nova_b200.build`")
+        h = ctypes.CDLL(str(LIB_PATH))
+        for name, argtypes in _SIGNATURES.items():
+            fn = getattr(h, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_int
+        for name in _STRING_FNS:
+            fn = getattr(h, name)
+            fn.argtypes = []
+            fn.restype = ctypes.c_char_p
+        _lib = h
+    return _lib
+
+
+def exported_names() -> list[str]:
+    return list(_SIGNATURES) + list(_STRING_FNS)
+
+
+def version() -> str:
+    return lib().nova_version().decode()
+
+
+def last_error() -> str:
+    return lib().nova_last_error().decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc == NOVA_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc in (NOVA_ERR_INVALID, NOVA_ERR_ALIGN, NOVA_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def available() -> bool:
+    """True when the library loads and a CUDA device is visible."""
+    try:
+        lib()
+    except (RuntimeError, OSError):
+        return False
+    return torch.cuda.is_available()
+
+
+def require_cuda(*tensors: torch.Tensor, names: tuple[str, ...] = ()) -> None:
+    for i, t in enumerate(tensors):
+        if t is not None and not t.is_cuda:
+            name = names[i] if i < len(names) else f"arg{i}"
+            raise ValueError(f"{name} must be a CUDA tensor (the B200 path has no CPU fallback)")

@@ -1,0 +1,68 @@
+// Library identification, thread-local error reporting and tensor-map
+// encoding shared by every entry point.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace nova {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(NOVA_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+    return NOVA_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+int make_tmap_u8_rows128(CUtensorMap* tm, const void* base, uint64_t rows, uint32_t box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(NOVA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (no CUDA driver?)");
+    if (reinterpret_cast<uintptr_t>(base) % 16) return fail(NOVA_ERR_ALIGN, "tensor map base not 16-byte aligned");
+    cuuint64_t gdim[2] = {128, rows};
+    cuuint64_t gstride[1] = {128};
+    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NOVA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return NOVA_OK;
+}
+
+}  // namespace nova
+
+extern "C" const char* nova_version(void) { return "nova_b200 0.1 (sm_100a, abi 1)"; }
+
+extern "C" const char* nova_last_error(void) { return nova::g_last_error; }

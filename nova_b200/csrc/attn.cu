@@ -1,0 +1,576 @@
+// Fused GQA decode attention over the streaming int8 KV cache (sm_100a).
+//
+// One CTA = (split, kv head, batch row).  Splits 0..n_splits-1 cover `chunk`
+// tokens of the int8 prefix each; split n_splits (when the fp16 tail ring is
+// given) covers the 64-slot ring.  Four warps per CTA; each warp owns one
+// 18 KiB shared-memory stage and walks the 64-token scale groups of its split
+// with stride 4:
+//   * the elected lane issues one mbarrier-tracked TMA tile load for the K
+//     codes and one for the V codes (64 rows x 128 B, 128-byte swizzle, so the
+//     fragment reads below are bank-conflict free) plus four 256-byte bulk
+//     copies for the group's fp16 min/step vectors;
+//   * codes are turned into fp16 in registers (byte permute with the 0x64
+//     exponent, subtract 1024, then one f16x2 FMA q*step+min -- the same value
+//     the reference's fp32 multiply-add rounded to fp16 produces);
+//   * S^T = K Q^T and O^T += V^T P^T run on mma.sync m16n8k16 (fp16 in, fp32
+//     accumulate).  The 8 MMA columns carry the 4 query heads twice: for QK
+//     both copies hold q (products are exact in fp32), for PV they hold the
+//     fp16 high and low parts of each softmax weight, so P keeps ~22 bits;
+//   * online softmax in fp32 (exp2 domain) with warp-shuffle max reductions.
+// The four warps merge in shared memory, the CTA stores one partial
+// (m, l, acc[128]) per query head, and the last CTA of each (batch, kv head)
+// -- found with an arrival counter -- merges all partials, writes fp16 out and
+// the fp32 log-sum-exp, and re-arms the counter.
+//
+// Reference semantics: src/nova/kvattn.py:110-253 (partial + combine kernels),
+// :447-482 + :819-862 (fp16 tail ring and LSE merge), src/nova/decode.py:207-220
+// (window mask).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace nova {
+namespace attn {
+
+constexpr int D = 128;
+constexpr int GT = 64;
+constexpr int NW = 4;
+constexpr int THREADS = NW * 32;
+constexpr int STAGE = 18432;      // K 8192 + V 8192 + 4 x 256 scales, rounded to 1 KiB
+constexpr int SC_OFF = 16384;     // kst, kmn, vst, vmn (256 B each)
+constexpr int TX_BYTES = 8192 + 8192 + 4 * 256;
+constexpr int SMEM_BYTES = NW * STAGE + 1024;
+constexpr int PART = 132;         // floats per (split, head): m, l, pad, pad, acc[128]
+constexpr int MAX_GQ = 4;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+struct Params {
+    const __half* q;
+    int64_t q_b, q_h;
+    const __half* kmn;
+    const __half* kst;
+    const __half* vmn;
+    const __half* vst;
+    const __half* tail_k;
+    const __half* tail_v;
+    __half* out;
+    int64_t o_b, o_h;
+    float* lse;
+    int64_t lse_b;
+    const int64_t* qlen;
+    const int64_t* pg;
+    const int64_t* written;
+    const int64_t* first;
+    int* err;
+    unsigned* counters;
+    float* part;
+    int kv_heads, gq, max_len, groups, chunk, n_splits, s_total, window;
+    float scale_log2;
+};
+
+__device__ __forceinline__ float warp_max_g(float v) {  // across the 8 lanes sharing lane&3
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+    return v;
+}
+__device__ __forceinline__ float warp_sum_g(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    return v;
+}
+
+// fp16 high part (e == 0) or low part (e == 1) of a softmax weight.
+__device__ __forceinline__ __half split_part(float p, int e) {
+    __half hi = __float2half_rn(p);
+    return e ? __float2half_rn(p - __half2float(hi)) : hi;
+}
+
+// P^T B-fragment for one 16-token tile: this lane (g, t) supplies column g =
+// (head g>>1, part g&1) for tokens 2t, 2t+1 (b0) and 2t+8, 2t+9 (b1).  The
+// weights live in lane (token&7)*4 + head as p_lo (token < 8) / p_hi (>= 8).
+__device__ __forceinline__ void p_fragment(float p_lo, float p_hi, int g, int t, uint32_t& b0, uint32_t& b1) {
+    const int h = g >> 1, e = g & 1;
+    const int la = (2 * t) * 4 + h, lb = (2 * t + 1) * 4 + h;
+    const float a0 = __shfl_sync(0xffffffffu, p_lo, la);
+    const float a1 = __shfl_sync(0xffffffffu, p_lo, lb);
+    const float a2 = __shfl_sync(0xffffffffu, p_hi, la);
+    const float a3 = __shfl_sync(0xffffffffu, p_hi, lb);
+    __half2 x0 = __halves2half2(split_part(a0, e), split_part(a1, e));
+    __half2 x1 = __halves2half2(split_part(a2, e), split_part(a3, e));
+    b0 = *reinterpret_cast<uint32_t*>(&x0);
+    b1 = *reinterpret_cast<uint32_t*>(&x1);
+}
+
+// Online-softmax update for `n` scores (already in the log2 domain, -inf for
+// masked tokens).  m_run is uniform over lanes with the same t (= head).
+template <int N>
+__device__ __forceinline__ void softmax_update(float (&x)[N], float& m_run, float& l_run, float (&acc)[8][4]) {
+    float mloc = x[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i) mloc = fmaxf(mloc, x[i]);
+    mloc = warp_max_g(mloc);
+    const float m_new = fmaxf(m_run, mloc);
+    if (m_new == -INFINITY) {  // nothing valid yet for this head
+#pragma unroll
+        for (int i = 0; i < N; ++i) x[i] = 0.0f;
+        return;
+    }
+    const float alpha = exp2f(m_run - m_new);  // m_run == -inf -> 0
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        x[i] = exp2f(x[i] - m_new);
+        sum += x[i];
+    }
+    l_run = l_run * alpha + sum;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[j][c] *= alpha;
+    m_run = m_new;
+}
+
+// Issue the loads of scale group `grp` of head row `bh` into `stage`.
+__device__ __forceinline__ void issue_group(const Params& p, const CUtensorMap* tmK, const CUtensorMap* tmV,
+                                            uint8_t* stage, uint64_t* bar, int64_t bh, int grp) {
+    mbar_arrive_expect_tx(bar, TX_BYTES);
+    const int row = int(bh * p.max_len + int64_t(grp) * GT);
+    tma_load_2d(stage, tmK, 0, row, bar);
+    tma_load_2d(stage + 8192, tmV, 0, row, bar);
+    const int64_t so = (bh * p.groups + grp) * D;
+    bulk_g2s(stage + SC_OFF, p.kst + so, 256, bar);
+    bulk_g2s(stage + SC_OFF + 256, p.kmn + so, 256, bar);
+    bulk_g2s(stage + SC_OFF + 512, p.vst + so, 256, bar);
+    bulk_g2s(stage + SC_OFF + 768, p.vmn + so, 256, bar);
+}
+
+// One 64-token int8 group held in `stage`; tokens outside [lo, hi) are masked.
+__device__ __forceinline__ void process_group(const uint8_t* stage, int gbase, int lo, int hi,
+                                              const uint32_t (&qf)[16], float scale_log2, float (&acc)[8][4],
+                                              float& m_run, float& l_run, int g, int t) {
+    const uint8_t* Ks = stage;
+    const uint8_t* Vs = stage + 8192;
+    const uint8_t* sc = stage + SC_OFF;
+    // K scales for dims 32t..32t+31 (word w = dims 32t+2w, +1).
+    uint32_t kst2[16], kmn2[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint4 a = lds128(sc + 64 * t + 16 * i);
+        uint4 b = lds128(sc + 256 + 64 * t + 16 * i);
+        kst2[4 * i] = a.x; kst2[4 * i + 1] = a.y; kst2[4 * i + 2] = a.z; kst2[4 * i + 3] = a.w;
+        kmn2[4 * i] = b.x; kmn2[4 * i + 1] = b.y; kmn2[4 * i + 2] = b.z; kmn2[4 * i + 3] = b.w;
+    }
+    // V scales for dims 16g..16g+15, broadcast to both halves:
+    // index j -> dim 16g+2j (row g of m-tile j), dim 16g+2j+1 (row g+8).
+    uint32_t vsA[8], vsB[8], vmA[8], vmB[8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        uint4 a = lds128(sc + 512 + 32 * g + 16 * i);
+        uint4 b = lds128(sc + 768 + 32 * g + 16 * i);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int j = 4 * i + k;
+            vsA[j] = __byte_perm(aw[k], 0, 0x1010);
+            vsB[j] = __byte_perm(aw[k], 0, 0x3232);
+            vmA[j] = __byte_perm(bw[k], 0, 0x1010);
+            vmB[j] = __byte_perm(bw[k], 0, 0x3232);
+        }
+    }
+
+    // ---- scores for the 4 tiles of 16 tokens
+    float x[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r0 = 16 * i + g;
+        const uint4 k0a = lds128(Ks + r0 * 128 + (((2 * t) ^ g) << 4));
+        const uint4 k0b = lds128(Ks + r0 * 128 + (((2 * t + 1) ^ g) << 4));
+        const uint4 k1a = lds128(Ks + (r0 + 8) * 128 + (((2 * t) ^ g) << 4));
+        const uint4 k1b = lds128(Ks + (r0 + 8) * 128 + (((2 * t + 1) ^ g) << 4));
+        const uint32_t w0[8] = {k0a.x, k0a.y, k0a.z, k0a.w, k0b.x, k0b.y, k0b.z, k0b.w};
+        const uint32_t w1[8] = {k1a.x, k1a.y, k1a.z, k1a.w, k1b.x, k1b.y, k1b.z, k1b.w};
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const uint32_t a0 = hfma2(u8x2_lo_to_f16x2(w0[s]), kst2[2 * s], kmn2[2 * s]);
+            const uint32_t a2 = hfma2(u8x2_hi_to_f16x2(w0[s]), kst2[2 * s + 1], kmn2[2 * s + 1]);
+            const uint32_t a1 = hfma2(u8x2_lo_to_f16x2(w1[s]), kst2[2 * s], kmn2[2 * s]);
+            const uint32_t a3 = hfma2(u8x2_hi_to_f16x2(w1[s]), kst2[2 * s + 1], kmn2[2 * s + 1]);
+            mma_16816(c, a0, a1, a2, a3, qf[2 * s], qf[2 * s + 1]);
+        }
+        const int p0 = gbase + r0, p1 = p0 + 8;
+        x[2 * i] = (p0 >= lo && p0 < hi) ? c[0] * scale_log2 : -INFINITY;
+        x[2 * i + 1] = (p1 >= lo && p1 < hi) ? c[2] * scale_log2 : -INFINITY;
+    }
+    softmax_update<8>(x, m_run, l_run, acc);
+
+    // ---- O^T += V^T P^T, one 16-token tile at a time
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t b0, b1;
+        p_fragment(x[2 * i], x[2 * i + 1], g, t, b0, b1);
+        const int ta = 16 * i + 2 * t;
+        const uint4 vA = lds128(Vs + ta * 128 + ((g ^ (ta & 7)) << 4));
+        const uint4 vB = lds128(Vs + (ta + 1) * 128 + ((g ^ ((ta + 1) & 7)) << 4));
+        const uint4 vC = lds128(Vs + (ta + 8) * 128 + ((g ^ (ta & 7)) << 4));
+        const uint4 vD = lds128(Vs + (ta + 9) * 128 + ((g ^ ((ta + 1) & 7)) << 4));
+        const uint32_t wa[4] = {vA.x, vA.y, vA.z, vA.w}, wb[4] = {vB.x, vB.y, vB.z, vB.w};
+        const uint32_t wc[4] = {vC.x, vC.y, vC.z, vC.w}, wd[4] = {vD.x, vD.y, vD.z, vD.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t ab01 = __byte_perm(wa[wi], wb[wi], 0x5140);
+            const uint32_t ab23 = __byte_perm(wa[wi], wb[wi], 0x7362);
+            const uint32_t cd01 = __byte_perm(wc[wi], wd[wi], 0x5140);
+            const uint32_t cd23 = __byte_perm(wc[wi], wd[wi], 0x7362);
+            int j = 2 * wi;
+            mma_16816(acc[j], hfma2(u8x2_lo_to_f16x2(ab01), vsA[j], vmA[j]),
+                      hfma2(u8x2_hi_to_f16x2(ab01), vsB[j], vmB[j]), hfma2(u8x2_lo_to_f16x2(cd01), vsA[j], vmA[j]),
+                      hfma2(u8x2_hi_to_f16x2(cd01), vsB[j], vmB[j]), b0, b1);
+            j = 2 * wi + 1;
+            mma_16816(acc[j], hfma2(u8x2_lo_to_f16x2(ab23), vsA[j], vmA[j]),
+                      hfma2(u8x2_hi_to_f16x2(ab23), vsB[j], vmB[j]), hfma2(u8x2_lo_to_f16x2(cd23), vsA[j], vmA[j]),
+                      hfma2(u8x2_hi_to_f16x2(cd23), vsB[j], vmB[j]), b0, b1);
+        }
+    }
+}
+
+__device__ __forceinline__ int64_t pos_mod(int64_t a, int m) {
+    int64_t r = a % m;
+    return r < 0 ? r + m : r;
+}
+
+// The 16 ring slots [16w, 16w+16) of the fp16 tail, read straight from global.
+__device__ __forceinline__ void process_tail_tile(const Params& p, int64_t bh, int w, int64_t u, int64_t tlo,
+                                                  const uint32_t (&qf)[16], float (&acc)[8][4], float& m_run,
+                                                  float& l_run, int g, int t) {
+    const __half* tk = p.tail_k + bh * GT * D;
+    const __half* tv = p.tail_v + bh * GT * D;
+    auto slot_valid = [&](int i) -> bool {
+        if (u < 0) return false;
+        const int64_t pos = u - pos_mod(u - i, GT);
+        return pos >= tlo && pos <= u;
+    };
+    const int r0 = 16 * w + g, r1 = r0 + 8;
+    uint32_t k0[16], k1[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 a = *reinterpret_cast<const uint4*>(tk + r0 * D + 32 * t + 8 * i);
+        const uint4 b = *reinterpret_cast<const uint4*>(tk + r1 * D + 32 * t + 8 * i);
+        k0[4 * i] = a.x; k0[4 * i + 1] = a.y; k0[4 * i + 2] = a.z; k0[4 * i + 3] = a.w;
+        k1[4 * i] = b.x; k1[4 * i + 1] = b.y; k1[4 * i + 2] = b.z; k1[4 * i + 3] = b.w;
+    }
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 8; ++s) mma_16816(c, k0[2 * s], k1[2 * s], k0[2 * s + 1], k1[2 * s + 1], qf[2 * s], qf[2 * s + 1]);
+    float x[2];
+    x[0] = slot_valid(r0) ? c[0] * p.scale_log2 : -INFINITY;
+    x[1] = slot_valid(r1) ? c[2] * p.scale_log2 : -INFINITY;
+    softmax_update<2>(x, m_run, l_run, acc);
+
+    uint32_t b0, b1;
+    p_fragment(x[0], x[1], g, t, b0, b1);
+    const int ta = 16 * w + 2 * t;
+    const int tok[4] = {ta, ta + 1, ta + 8, ta + 9};
+    uint32_t v[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const bool ok = slot_valid(tok[k]);
+        const uint4 a = *reinterpret_cast<const uint4*>(tv + tok[k] * D + 16 * g);
+        const uint4 b = *reinterpret_cast<const uint4*>(tv + tok[k] * D + 16 * g + 8);
+        v[k][0] = ok ? a.x : 0u; v[k][1] = ok ? a.y : 0u; v[k][2] = ok ? a.z : 0u; v[k][3] = ok ? a.w : 0u;
+        v[k][4] = ok ? b.x : 0u; v[k][5] = ok ? b.y : 0u; v[k][6] = ok ? b.z : 0u; v[k][7] = ok ? b.w : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        mma_16816(acc[j], __byte_perm(v[0][j], v[1][j], 0x5410), __byte_perm(v[0][j], v[1][j], 0x7632),
+                  __byte_perm(v[2][j], v[3][j], 0x5410), __byte_perm(v[2][j], v[3][j], 0x7632), b0, b1);
+    }
+}
+
+__global__ void __launch_bounds__(THREADS, 3)
+    attn_decode_int8_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t bars[NW];
+    __shared__ float sm_m[NW][MAX_GQ], sm_l[NW][MAX_GQ];
+    __shared__ int sm_last;
+
+    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int64_t bh = int64_t(b) * p.kv_heads + h;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+
+    const int64_t qlen = *p.qlen, pgv = *p.pg;
+    const int64_t written = p.written ? *p.written : qlen;
+    const int64_t first = p.first ? *p.first : 0;
+    const int64_t u = written - 1;
+    int64_t lo = first > 0 ? first : 0;
+    if (p.window > 0) lo = max(lo, u - p.window + 1);
+    const int64_t pend = min(min(qlen, pgv * GT), int64_t(p.max_len));
+
+    // Q^T B-fragments: column g carries head g>>1; dims 32t..32t+31.
+    uint32_t qf[16];
+    {
+        const int hq = g >> 1;
+        if (hq < p.gq) {
+            const __half* qp = p.q + b * p.q_b + int64_t(h * p.gq + hq) * p.q_h + 32 * t;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 v = *reinterpret_cast<const uint4*>(qp + 8 * i);
+                qf[4 * i] = v.x; qf[4 * i + 1] = v.y; qf[4 * i + 2] = v.z; qf[4 * i + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) qf[i] = 0u;
+        }
+    }
+
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    if (split < p.n_splits) {
+        const int64_t t_begin = max(int64_t(split) * p.chunk, lo);
+        const int64_t t_end = min(int64_t(split) * p.chunk + p.chunk, pend);
+        if (t_begin < t_end) {
+            const int g_first = int(t_begin / GT), g_last = int((t_end - 1) / GT);
+            uint8_t* stage = smem + warp * STAGE;
+            uint64_t* bar = &bars[warp];
+            int gi = g_first + warp;
+            if (gi <= g_last) {
+                if (lane == 0) {
+                    mbar_init(bar, 1);
+                    fence_mbar_init();
+                    issue_group(p, &tmK, &tmV, stage, bar, bh, gi);
+                }
+                __syncwarp();
+                uint32_t parity = 0;
+                for (; gi <= g_last; gi += NW) {
+                    if (!mbar_wait(bar, parity, p.err, 1)) break;
+                    parity ^= 1u;
+                    process_group(stage, gi * GT, int(t_begin), int(t_end), qf, p.scale_log2, acc, m_run, l_run,
+                                  g, t);
+                    __syncwarp();
+                    if (lane == 0 && gi + NW <= g_last) {
+                        fence_proxy_async();
+                        issue_group(p, &tmK, &tmV, stage, bar, bh, gi + NW);
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+    } else {
+        int64_t tlo = max(lo, qlen);
+        process_tail_tile(p, bh, warp, u, tlo, qf, acc, m_run, l_run, g, t);
+    }
+
+    // ---- merge the 4 warps of this CTA
+    const float l_warp = warp_sum_g(l_run);
+    __syncthreads();  // every warp is done with its stage: reuse it as obuf
+    float* obuf = reinterpret_cast<float*>(smem);  // [NW][MAX_GQ][D]
+    if (t < p.gq) {
+        if (g == 0) {
+            sm_m[warp][t] = m_run;
+            sm_l[warp][t] = l_warp;
+        }
+        float* ob = obuf + (warp * MAX_GQ + t) * D + 16 * g;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            ob[2 * j] = acc[j][0] + acc[j][1];
+            ob[2 * j + 1] = acc[j][2] + acc[j][3];
+        }
+    }
+    __syncthreads();
+    const int hh = threadIdx.x >> 5, d0 = (threadIdx.x & 31) * 4;
+    float* part_bh = p.part + bh * int64_t(p.s_total) * p.gq * PART;
+    if (hh < p.gq) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][hh]);
+        float L = 0.f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float mw = sm_m[w][hh];
+                if (mw == -INFINITY) continue;
+                const float wt = exp2f(mw - M);
+                L += wt * sm_l[w][hh];
+                const float4 a = *reinterpret_cast<const float4*>(obuf + (w * MAX_GQ + hh) * D + d0);
+                o.x += wt * a.x; o.y += wt * a.y; o.z += wt * a.z; o.w += wt * a.w;
+            }
+        }
+        float* dst = part_bh + (int64_t(split) * p.gq + hh) * PART;
+        if (d0 == 0) {
+            dst[0] = M;
+            dst[1] = L;
+        }
+        if (M != -INFINITY) *reinterpret_cast<float4*>(dst + 4 + d0) = o;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(p.counters + bh, 1u);
+        sm_last = (prev == unsigned(p.s_total - 1));
+    }
+    __syncthreads();
+    if (!sm_last) return;
+    __threadfence();
+
+    // ---- last CTA of this (batch, kv head): merge all splits
+    if (hh < p.gq) {
+        float M = -INFINITY;
+        for (int s = 0; s < p.s_total; ++s) M = fmaxf(M, __ldcg(part_bh + (int64_t(s) * p.gq + hh) * PART));
+        float L = 0.f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (M != -INFINITY) {
+            for (int s = 0; s < p.s_total; ++s) {
+                const float* src = part_bh + (int64_t(s) * p.gq + hh) * PART;
+                const float ms = __ldcg(src);
+                if (ms == -INFINITY) continue;
+                const float wt = exp2f(ms - M);
+                L += wt * __ldcg(src + 1);
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(src + 4 + d0));
+                o.x += wt * a.x; o.y += wt * a.y; o.z += wt * a.z; o.w += wt * a.w;
+            }
+        }
+        const int qh = h * p.gq + hh;
+        __half* op = p.out + b * p.o_b + int64_t(qh) * p.o_h + d0;
+        if (L > 0.f) {  // acc / l then one rounding to fp16, like the reference combine
+            *reinterpret_cast<__half2*>(op) = __floats2half2_rn(__fdiv_rn(o.x, L), __fdiv_rn(o.y, L));
+            *reinterpret_cast<__half2*>(op + 2) = __floats2half2_rn(__fdiv_rn(o.z, L), __fdiv_rn(o.w, L));
+        } else {
+            *reinterpret_cast<__half2*>(op) = __floats2half2_rn(0.f, 0.f);
+            *reinterpret_cast<__half2*>(op + 2) = __floats2half2_rn(0.f, 0.f);
+        }
+        if (p.lse && d0 == 0) p.lse[b * p.lse_b + qh] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
+    }
+    if (threadIdx.x == 0) p.counters[bh] = 0u;
+}
+
+}  // namespace attn
+}  // namespace nova
+
+using namespace nova;
+
+static int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+extern "C" int nova_attn_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t n_splits,
+                                         int has_tail, int64_t* bytes) {
+    if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
+    if (batch <= 0 || kv_heads <= 0 || q_heads <= 0 || q_heads % kv_heads || n_splits < 0)
+        return fail(NOVA_ERR_INVALID, "bad batch/heads/n_splits");
+    const int64_t bh = batch * kv_heads;
+    const int64_t s_total = n_splits + (has_tail ? 1 : 0);
+    *bytes = 256 + align_up(bh * 4, 256) + bh * s_total * (q_heads / kv_heads) * attn::PART * 4;
+    return NOVA_OK;
+}
+
+extern "C" int nova_attn_read_error(void* workspace, int64_t, int64_t, int* host_value) {
+    if (!workspace || !host_value) return fail(NOVA_ERR_INVALID, "NULL argument");
+    if (cudaMemcpy(host_value, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(NOVA_ERR_CUDA, "reading the attention error word failed");
+    if (*host_value && cudaMemset(workspace, 0, sizeof(int)) != cudaSuccess)
+        return fail(NOVA_ERR_CUDA, "clearing the attention error word failed");
+    return NOVA_OK;
+}
+
+extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream) {
+    using namespace nova::attn;
+    if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
+    if (a->head_dim != D) return fail(NOVA_ERR_UNSUPPORTED, "head_dim must be 128, got %lld", (long long)a->head_dim);
+    if (a->group != GT) return fail(NOVA_ERR_UNSUPPORTED, "group must be 64, got %lld", (long long)a->group);
+    if (a->batch <= 0 || a->kv_heads <= 0 || a->q_heads <= 0 || a->q_heads % a->kv_heads)
+        return fail(NOVA_ERR_INVALID, "bad batch/heads (%lld, %lld, %lld)", (long long)a->batch,
+                    (long long)a->q_heads, (long long)a->kv_heads);
+    const int64_t gq = a->q_heads / a->kv_heads;
+    if (gq > MAX_GQ) return fail(NOVA_ERR_UNSUPPORTED, "q_heads/kv_heads must be <= 4, got %lld", (long long)gq);
+    if (a->chunk <= 0 || a->chunk % GT) return fail(NOVA_ERR_INVALID, "chunk must be a positive multiple of 64");
+    if (a->max_len <= 0 || a->groups != (a->max_len + GT - 1) / GT)
+        return fail(NOVA_ERR_INVALID, "groups must equal ceil(max_len/64)");
+    if (a->n_splits < 0 || (a->n_splits == 0 && !a->tail_k)) return fail(NOVA_ERR_INVALID, "n_splits must be >= 1");
+    if (a->n_splits > 65535 || a->batch > 65535 || a->kv_heads > 65535)
+        return fail(NOVA_ERR_INVALID, "grid too large");
+    if (!a->q || !a->out || !a->qlen || !a->pg || !a->workspace)
+        return fail(NOVA_ERR_INVALID, "q/out/qlen/pg/workspace must not be NULL");
+    if (a->n_splits && (!a->kq || !a->vq || !a->kmn || !a->kst || !a->vmn || !a->vst))
+        return fail(NOVA_ERR_INVALID, "int8 buffers must not be NULL");
+    if ((a->tail_k == nullptr) != (a->tail_v == nullptr)) return fail(NOVA_ERR_INVALID, "tail_k/tail_v: both or none");
+    if (a->tail_k && !a->written) return fail(NOVA_ERR_INVALID, "the tail ring needs the `written` scalar");
+    if (a->window < 0) return fail(NOVA_ERR_INVALID, "window must be >= 0");
+    auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
+    if (mis(a->q, 16) || mis(a->out, 8) || mis(a->kq, 16) || mis(a->vq, 16) || mis(a->kmn, 16) ||
+        mis(a->kst, 16) || mis(a->vmn, 16) || mis(a->vst, 16) || mis(a->tail_k, 16) || mis(a->tail_v, 16) ||
+        mis(a->workspace, 256))
+        return fail(NOVA_ERR_ALIGN, "q/kv/scale/tail pointers must be 16-byte aligned (out 8, workspace 256)");
+    if ((a->q_h_stride % 8) || (a->q_b_stride % 8) || (a->o_h_stride % 4) || (a->o_b_stride % 4))
+        return fail(NOVA_ERR_ALIGN, "q strides must be multiples of 8 elements, out strides of 4");
+    const int64_t bh = a->batch * a->kv_heads;
+    const int64_t s_total = a->n_splits + (a->tail_k ? 1 : 0);
+    int64_t need = 0;
+    nova_attn_workspace_bytes(a->batch, a->q_heads, a->kv_heads, a->n_splits, a->tail_k != nullptr, &need);
+    if (a->workspace_bytes < need)
+        return fail(NOVA_ERR_INVALID, "workspace too small: %lld < %lld bytes", (long long)a->workspace_bytes,
+                    (long long)need);
+    if (bh * a->max_len > 0x7fffffffLL) return fail(NOVA_ERR_INVALID, "batch*kv_heads*max_len must fit in int32");
+
+    CUtensorMap tmK, tmV;
+    const uint64_t rows = uint64_t(bh * a->max_len);
+    if (a->n_splits) {
+        if (int rc = make_tmap_u8_rows128(&tmK, a->kq, rows, GT)) return rc;
+        if (int rc = make_tmap_u8_rows128(&tmV, a->vq, rows, GT)) return rc;
+    } else {
+        memset(&tmK, 0, sizeof(tmK));
+        memset(&tmV, 0, sizeof(tmV));
+    }
+
+    Params p;
+    p.q = (const __half*)a->q;
+    p.q_b = a->q_b_stride;
+    p.q_h = a->q_h_stride;
+    p.kmn = (const __half*)a->kmn;
+    p.kst = (const __half*)a->kst;
+    p.vmn = (const __half*)a->vmn;
+    p.vst = (const __half*)a->vst;
+    p.tail_k = (const __half*)a->tail_k;
+    p.tail_v = (const __half*)a->tail_v;
+    p.out = (__half*)a->out;
+    p.o_b = a->o_b_stride;
+    p.o_h = a->o_h_stride;
+    p.lse = (float*)a->lse;
+    p.lse_b = a->lse_b_stride;
+    p.qlen = a->qlen;
+    p.pg = a->pg;
+    p.written = a->written;
+    p.first = a->first;
+    uint8_t* ws = (uint8_t*)a->workspace;
+    p.err = (int*)ws;
+    p.counters = (unsigned*)(ws + 256);
+    p.part = (float*)(ws + 256 + align_up(bh * 4, 256));
+    p.kv_heads = int(a->kv_heads);
+    p.gq = int(gq);
+    p.max_len = int(a->max_len);
+    p.groups = int(a->groups);
+    p.chunk = int(a->chunk);
+    p.n_splits = int(a->n_splits);
+    p.s_total = int(s_total);
+    p.window = int(std::min<int64_t>(a->window, 0x7fffffff));
+    p.scale_log2 = float(1.0 / sqrt(double(D))) * LOG2E;
+
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(attn_decode_int8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+            cudaSuccess)
+            return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
+        attr_set = true;
+    }
+    dim3 grid(unsigned(s_total), unsigned(a->kv_heads), unsigned(a->batch));
+    attn_decode_int8_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(p, tmK, tmV);
+    return check_launch("nova_attn_decode_int8");
+}

@@ -1,0 +1,230 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE's own
+Python code (captain-wangrun-cn/Nova, ``src/nova``) on seeded inputs.
+
+Run in a checkout that has the reference source available:
+
+    NOVA_REF_SRC=/path/to/Nova/src python tests/golden/make_golden.py
+
+The fixtures pin the CPU oracle (``oracle/``) to the reference; the GPU tests
+then compare the CUDA kernels with the oracle.  Only the reference functions
+that run without Triton/CUDA/bitsandbytes are used (kvquant, the KVInt8Cache
+prefill + ring path on CPU, SDPA math on CPU, LeanRMSNorm "exact",
+apply_rotary_pos_emb with the transformers Qwen3-VL rotary, build_nf4_lut,
+extract_nf4 with a non-nested quant state, and -- for the decoder fixture --
+a random-init reference NovaTextModel whose linears run the NF4 dequant formula
+of tests/test_nf4_linear.py:46-57 and whose KVInt8Cache.attend is the
+reference's own single-softmax ground truth (tests/test_kvattn_stream.py:68-83)).
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, os.environ.get("NOVA_REF_SRC", "/root/reference/src"))
+
+from torch.nn.attention import SDPBackend, sdpa_kernel  # noqa: E402
+
+from nova.kernels import build_nf4_lut as ref_build_nf4_lut  # noqa: E402
+from nova.kvattn import KVInt8Cache as RefCache  # noqa: E402
+from nova.kvquant import dequantize_int8 as ref_dequant  # noqa: E402
+from nova.kvquant import quantize_int8 as ref_quant  # noqa: E402
+from nova.layers import apply_rotary_pos_emb as ref_rope  # noqa: E402
+from nova.norm import LeanRMSNorm  # noqa: E402
+from nova.quant import extract_nf4 as ref_extract_nf4  # noqa: E402
+
+from oracle.nf4 import nf4_codebook, quantize_nf4  # noqa: E402  (inputs only)
+
+H_KV, HQ, D, GT = 8, 32, 128, 64
+
+
+def _save(name: str, **arrays) -> None:
+    path = HERE / name
+    np.savez_compressed(path, **{k: (v.numpy() if isinstance(v, torch.Tensor) else np.asarray(v))
+                                 for k, v in arrays.items()})
+    print(f"wrote {path.name}: {', '.join(arrays)}")
+
+
+def kvquant_fixture() -> None:
+    """quantize_int8 / dequantize_int8, token axis, group 64 (src/nova/kvquant.py:118-176)."""
+    torch.manual_seed(0)
+    out = {}
+    cases = {
+        "rand": (torch.randn(1, 3, 150, D) * 3.0).to(torch.float16),          # ragged last group
+        "outlier": None,
+        "const": torch.full((1, 2, 70, D), 0.5, dtype=torch.float16),
+    }
+    x = (torch.randn(1, 2, 129, D) * 0.7)
+    x[..., [3, 71, 120]] *= 65.0
+    cases["outlier"] = x.to(torch.float16)
+    for name, x in cases.items():
+        q, mn, st = ref_quant(x, GT, "token")
+        deq = ref_dequant(q, mn, st, GT, "token")
+        out.update({f"{name}_x": x, f"{name}_q": q, f"{name}_mn": mn, f"{name}_st": st, f"{name}_deq": deq})
+    _save("kvquant_token.npz", **out)
+
+
+def ring_fixture() -> None:
+    """KVInt8Cache prefill + decode updates on CPU (src/nova/kvattn.py:645-783)."""
+    torch.manual_seed(1)
+    slots, hkv, max_len, n0, steps = 2, 2, 320, 100, 100
+    cache = RefCache(num_slots=slots, num_kv_heads=hkv, head_dim=D, max_len=max_len, num_q_heads=4 * hkv,
+                     device="cpu")
+    k = (torch.randn(slots, 1, hkv, n0 + steps, D) * 0.7).to(torch.float16)
+    v = (torch.randn(slots, 1, hkv, n0 + steps, D) * 0.7).to(torch.float16)
+    cache.begin_prefill(n0)
+    cache.set_prefill_pos(0)
+    for layer in range(slots):
+        cache.update(k[layer, :, :, :n0], v[layer, :, :, :n0], layer)
+    cache.finish_prefill(n0)
+    for p in range(n0, n0 + steps):
+        cache.pos.fill_(p)
+        for layer in range(slots):
+            cache.update(k[layer, :, :, p:p + 1], v[layer, :, :, p:p + 1], layer)
+    qlen = int(cache._qlen.item())
+    out = {"k": k, "v": v, "n0": n0, "steps": steps, "max_len": max_len,
+           "written": int(cache._written.item()), "qlen": qlen, "pg": int(cache._pg.item())}
+    for layer in range(slots):
+        out[f"kq{layer}"] = cache.kq[layer][:, :, :qlen]
+        out[f"vq{layer}"] = cache.vq[layer][:, :, :qlen]
+        for nm in ("kmn", "kst", "vmn", "vst"):
+            out[f"{nm}{layer}"] = getattr(cache, nm)[layer][:, :, :qlen // GT]
+        out[f"tail_k{layer}"] = cache.tail_k[layer]
+        out[f"tail_v{layer}"] = cache.tail_v[layer]
+    out["ring_mask"] = cache.ring_mask().view(-1)
+    _save("kv_ring.npz", **out)
+
+
+def _sdpa_math(q, k, v):
+    gq = q.shape[1] // k.shape[1]
+    b, h, n, d = k.shape
+    k = k[:, :, None].expand(b, h, gq, n, d).reshape(b, h * gq, n, d)
+    v = v[:, :, None].expand(b, h, gq, n, d).reshape(b, h * gq, n, d)
+    with sdpa_kernel([SDPBackend.MATH]):
+        return F.scaled_dot_product_attention(q, k, v, scale=d ** -0.5)
+
+
+def attention_fixture() -> None:
+    """The reference attention ground truths: fused kernel (dequantize_int8 ->
+    SDPA math, tests/test_kvattn.py:62-71) and streaming cache (int8 prefix +
+    fp16 tail -> SDPA math, tests/test_kvattn_stream.py:68-83)."""
+    out = {}
+    hkv, hq = 2, 8   # 4 query heads per KV head like Qwen3-4B, fewer heads to keep the fixture small
+    for used in (7, 64, 65, 513, 1000):
+        torch.manual_seed(used)
+        k = (torch.randn(1, hkv, used, D) * 0.7).to(torch.float16)
+        v = (torch.randn(1, hkv, used, D) * 0.7).to(torch.float16)
+        q = (torch.randn(1, hq, 1, D) * 0.7).to(torch.float16)
+        kq, kmn, kst = ref_quant(k, GT, "token")
+        vq, vmn, vst = ref_quant(v, GT, "token")
+        kk = ref_dequant(kq, kmn, kst, GT, "token")
+        vv = ref_dequant(vq, vmn, vst, GT, "token")
+        want = _sdpa_math(q, kk, vv)
+        out.update({f"fused{used}_q": q, f"fused{used}_k": k, f"fused{used}_v": v, f"fused{used}_out": want})
+    for used in (40, 100, 320):
+        torch.manual_seed(1000 + used)
+        k = (torch.randn(1, hkv, used, D) * 0.7).to(torch.float16)
+        v = (torch.randn(1, hkv, used, D) * 0.7).to(torch.float16)
+        q = (torch.randn(1, hq, 1, D) * 0.7).to(torch.float16)
+        prefix = used // GT * GT
+        if prefix:
+            kq, kmn, kst = ref_quant(k[:, :, :prefix], GT, "token")
+            vq, vmn, vst = ref_quant(v[:, :, :prefix], GT, "token")
+            kk = torch.cat([ref_dequant(kq, kmn, kst, GT, "token"), k[:, :, prefix:]], dim=2)
+            vv = torch.cat([ref_dequant(vq, vmn, vst, GT, "token"), v[:, :, prefix:]], dim=2)
+        else:
+            kk, vv = k, v
+        out.update({f"stream{used}_q": q, f"stream{used}_k": k, f"stream{used}_v": v,
+                    f"stream{used}_out": _sdpa_math(q, kk, vv)})
+    _save("attention.npz", **out)
+
+
+def nf4_fixture() -> None:
+    """LUT packing (src/nova/kernels.py:170-182) and the extract_nf4 layout
+    transform (src/nova/quant.py:39-69) applied to a non-nested quant state
+    built from our own quantizer's output, plus the dequant formula of
+    tests/test_nf4_linear.py:46-57."""
+    code = nf4_codebook()
+    lut = ref_build_nf4_lut(torch.from_numpy(code))
+    rng = np.random.default_rng(7)
+    n, k = 96, 256
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float16)
+    packed, absmax = quantize_nf4(w, code, absmax_dtype=np.float32)   # [N, K/2], [K/64, N]
+
+    class _QS:   # the fields extract_nf4 reads from a bitsandbytes QuantState
+        nested = False
+
+    qs = _QS()
+    qs.shape = torch.Size([n, k])
+    qs.absmax = torch.from_numpy(np.ascontiguousarray(absmax.T).reshape(-1))    # bnb order: block-major per row
+    qs.code = torch.from_numpy(code)
+    weight = torch.from_numpy(packed.reshape(-1).copy())
+    r_packed, r_absmax, r_code, shape = ref_extract_nf4(weight, qs)
+    # tests/test_nf4_linear.py:_torch_dequant, restated on CPU tensors
+    hi = r_packed.long() >> 4
+    lo = r_packed.long() & 0x0F
+    vals = torch.empty(n, k, dtype=torch.float32)
+    vals[:, 0::2] = r_code[hi]
+    vals[:, 1::2] = r_code[lo]
+    deq16 = (vals * r_absmax.t().repeat_interleave(64, dim=1)).to(torch.float16)
+    _save("nf4.npz", code=code, lut=lut, w=w, packed=r_packed, absmax=r_absmax, deq16=deq16,
+          shape=np.array(shape))
+
+
+def norm_rope_fixture() -> None:
+    """LeanRMSNorm "exact" (src/nova/norm.py:34-42) and RoPE with the
+    transformers Qwen3-VL rotary (src/nova/model.py:144, src/nova/layers.py:24-36)."""
+    from transformers import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextRotaryEmbedding
+
+    torch.manual_seed(3)
+    out = {}
+    for dim, rows in ((2560, 5), (128, 40)):
+        norm = LeanRMSNorm(dim, eps=1e-6, impl="exact", dtype=torch.float16)
+        with torch.no_grad():
+            norm.weight.copy_((1.0 + 0.1 * torch.randn(dim)).to(torch.float16))
+        x = (torch.randn(rows, dim) * 2.0).to(torch.float16)
+        out[f"norm{dim}_x"] = x
+        out[f"norm{dim}_w"] = norm.weight.detach()
+        out[f"norm{dim}_y"] = norm(x).detach()
+    cfg = Qwen3VLTextConfig(hidden_size=4096, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                            rope_parameters={"rope_type": "default", "rope_theta": 5_000_000.0,
+                                             "mrope_section": [24, 20, 20], "mrope_interleaved": True})
+    rot = Qwen3VLTextRotaryEmbedding(cfg)
+    pos = torch.tensor([0, 1, 2, 63, 100, 4096, 8191, 8447, 32767, 131071])
+    position_ids = pos.view(1, 1, -1).expand(3, 1, -1)
+    dummy = torch.zeros(1, dtype=torch.float16)
+    cos, sin = rot(dummy, position_ids)
+    q = (torch.randn(1, 4, len(pos), 128)).to(torch.float16)
+    k = (torch.randn(1, 2, len(pos), 128)).to(torch.float16)
+    qe, ke = ref_rope(q, k, cos, sin)
+    out.update({"rope_pos": pos, "rope_cos": cos[0], "rope_sin": sin[0], "rope_q": q, "rope_k": k,
+                "rope_qe": qe, "rope_ke": ke})
+    _save("norm_rope.npz", **out)
+
+
+def main() -> None:
+    which = set(sys.argv[1:]) or {"kvquant", "ring", "attention", "nf4", "norm_rope"}
+    if "kvquant" in which:
+        kvquant_fixture()
+    if "ring" in which:
+        ring_fixture()
+    if "attention" in which:
+        attention_fixture()
+    if "nf4" in which:
+        nf4_fixture()
+    if "norm_rope" in which:
+        norm_rope_fixture()
+
+
+if __name__ == "__main__":
+    main()

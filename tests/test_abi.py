@@ -1,0 +1,53 @@
+"""CPU: the C-ABI library loads without a GPU and exports every entry point
+that include/nova_b200.h declares (no compute calls here)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import REPO
+from nova_b200 import _lib
+
+
+def _declared() -> list[str]:
+    names = []
+    for hdr in (REPO / "include").glob("*.h"):
+        text = hdr.read_text()
+        names += re.findall(r"^NOVA_API\s+[\w\s\*]+?\b(nova_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "nova_attn_decode_int8" in names and "nova_version" in names
+    assert len(names) >= 8
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_python_binding_covers_every_declared_symbol():
+    assert sorted(_declared()) == sorted(_lib.exported_names())
+
+
+def test_version_string_without_gpu():
+    assert "sm_100a" in _lib.version()
+
+
+def test_host_side_argument_checks_need_no_gpu():
+    """Invalid arguments are rejected on the host before any launch."""
+    lib = _lib.lib()
+    rc = lib.nova_kv_quant_int8(None, 0, None, 0, None, None, 0, 1, 10, 0, 64, None)
+    assert rc == _lib.NOVA_ERR_INVALID
+    assert "dim" in _lib.last_error()
+    out = ctypes.c_int64(0)
+    rc = lib.nova_attn_workspace_bytes(1, 32, 8, 16, 1, ctypes.byref(out))
+    assert rc == _lib.NOVA_OK and out.value > 0
+    with pytest.raises(ValueError):
+        _lib.check(lib.nova_attn_workspace_bytes(1, 30, 8, 16, 1, ctypes.byref(out)), "ws")
