@@ -137,6 +137,143 @@ NOVA_API int nova_attn_decode_int8(const nova_attn_int8_args* args, void* stream
  * gave up); copies it to *host_value synchronously and clears it. */
 NOVA_API int nova_attn_read_error(void* workspace, int64_t batch, int64_t kv_heads, int* host_value);
 
+/* ------------------------------------------------------------------ NF4 */
+
+/* Epilogues of nova_nf4_gemv. */
+enum nova_nf4_epilogue {
+    NOVA_NF4_PLAIN = 0,    /* out = fp16(acc + bias)                                      */
+    NOVA_NF4_RESIDUAL = 1, /* out = fp16(residual + fp16(acc))  (decoder residual add)     */
+    NOVA_NF4_SILU_MUL = 2, /* rows interleaved per 16-row tile: 8 gate rows, then the 8
+                              matching up rows; out[:, n] = fp16(silu(fp16 gate)) * fp16 up,
+                              out has N/2 columns (LeanMLP act_fn(gate) * up)              */
+    NOVA_NF4_ARGMAX = 3    /* PLAIN, plus atomicMax of a packed (fp16 logit, -index) key
+                              into argmax[m] (uint64, zero before the call): greedy token  */
+};
+
+/* Workspace bytes for nova_nf4_gemv with N output rows on the current device
+ * (stream-K partial slots + per-row-tile counters).  Zero it once. */
+NOVA_API int nova_nf4_workspace_bytes(int64_t n, int64_t* bytes);
+
+/*
+ * y[M, N] = x[M, K] (fp16) * W^T with W in NF4: packed uint8 [N, K/2], absmax
+ * [K/64, N] (fp32 if absmax_fp32 else fp16), lut = the 256-entry fp16x2
+ * codebook table (low half code[b>>4], high half code[b&15]).  fp32
+ * accumulation.  M <= 8, N % 16 == 0, K % 64 == 0, M*K*2 + 64 KiB <= 227 KiB.
+ *   norm_weight != NULL: x is normalised first (RMSNorm, HF order, eps) --
+ *       the input_layernorm / post_attention_layernorm / final norm folded in;
+ *   residual/out/argmax per the epilogue; bias (fp16 [N]) only with PLAIN;
+ *   token_out != NULL (ARGMAX only): the last warp writes the argmax index of
+ *       each row to token_out[m], re-zeroes argmax[m], increments *pos (if
+ *       given) and, with embed != NULL, copies embed[token] (fp16 rows of
+ *       embed_dim) to embed_out -- the next step's hidden state.
+ * Replaces fused_nf4_linear / _nf4_gemv_kernel (src/nova/kernels.py:187-289),
+ * NF4Linear.forward (src/nova/quant.py:101-102), fused_rms_norm in front of
+ * the projections (src/nova/kernels.py:97-115, src/nova/layers.py:199, :216,
+ * src/nova/model.py:179), the 4-bit lm_head (src/nova/model.py:200-204) with
+ * the greedy argmax / input_ids / pos update of GraphDecoder._body
+ * (src/nova/decode.py:318-319) and the embedding lookup (src/nova/model.py:131),
+ * and the residual adds / SiLU*up of src/nova/layers.py:174, :213, :218.
+ */
+typedef struct nova_nf4_args {
+    const void* x;            /* fp16 [m, k]                                   */
+    int64_t x_stride;
+    const void* norm_weight;  /* fp16 [k] or NULL                              */
+    double eps;
+    const void* packed;       /* uint8 [n, k/2]                                */
+    const void* absmax;       /* [k/64, n]                                      */
+    int64_t absmax_fp32;
+    const void* lut;          /* uint32 [256]                                  */
+    const void* bias;         /* fp16 [n] or NULL                              */
+    const void* residual;     /* fp16 [m, n] (RESIDUAL)                        */
+    int64_t res_stride;
+    void* out;                /* fp16 [m, n] ([m, n/2] for SILU_MUL)           */
+    int64_t out_stride;
+    void* argmax;             /* uint64 [m] (ARGMAX)                           */
+    int64_t* token_out;       /* int64 [m] or NULL                             */
+    int64_t* pos;             /* device scalar or NULL                         */
+    const void* embed;        /* fp16 [vocab, embed_dim] or NULL               */
+    void* embed_out;          /* fp16 [m, embed_dim]                           */
+    int64_t embed_out_stride;
+    int64_t embed_dim;
+    void* workspace;          /* nova_nf4_workspace_bytes(n), zeroed once      */
+    int64_t workspace_bytes;
+    int64_t m, n, k;
+    int64_t epilogue;         /* enum nova_nf4_epilogue                        */
+} nova_nf4_args;
+
+NOVA_API int nova_nf4_gemv(const nova_nf4_args* args, void* stream);
+
+/*
+ * Blockwise NF4 quantizer: w fp16 [N, K] -> packed uint8 [N, K/2], absmax
+ * [K/64, N].  Level = number of the 15 fp32 `midpoints` below w/absmax (ties
+ * to the lower level); an all-zero block uses absmax 1 for the division.
+ * Stands in for bitsandbytes quantize_4bit used by the reference loader
+ * (src/nova/loader.py:20-42, :86-119), which is not part of the reference tree.
+ */
+NOVA_API int nova_nf4_quantize(const void* w, int64_t n, int64_t k, const void* midpoints, void* packed, void* absmax,
+                               int absmax_fp32, void* stream);
+
+/*
+ * NF4 -> fp16 weights [N, K] (code16 * absmax rounded to fp16), for the
+ * prefill path.  Same result as the reference test's dequant with the fp16
+ * codebook (tests/test_nf4_linear.py:46-57).
+ */
+NOVA_API int nova_nf4_dequant(const void* packed, const void* absmax, int absmax_fp32, const void* lut, void* out,
+                              int64_t n, int64_t k, void* stream);
+
+/* ------------------------------------------------------------ RMSNorm / RoPE */
+
+/*
+ * y = RMSNorm(h) * weight in HF order (fp32 mean of squares, 1/sqrt(var+eps),
+ * h*r rounded to fp16, times the fp16 weight, rounded to fp16), one row of n
+ * per block.  With residual_in: h = fp16(x + residual_in) and, if
+ * residual_out != NULL, h is stored there too (fused residual add).
+ * Replaces fused_rms_norm / _rms_norm_fwd (src/nova/kernels.py:51-69, :97-115),
+ * LeanRMSNorm.forward (src/nova/norm.py:34-42) and the residual add of
+ * LeanDecoderLayer.forward (src/nova/layers.py:213).
+ */
+NOVA_API int nova_rmsnorm(const void* x, int64_t x_stride, const void* residual_in, int64_t rin_stride,
+                          void* residual_out, int64_t rout_stride, const void* weight, void* y, int64_t y_stride,
+                          int64_t rows, int64_t n, double eps, void* stream);
+
+/*
+ * The decoder's per-head step after the fused q/k/v projection, one launch:
+ * qkv row m = [q (q_heads*128) | k (kv_heads*128) | v (kv_heads*128)] fp16;
+ * q heads -> q_norm, RoPE at position *pos -> q_out; k heads -> k_norm, RoPE;
+ * K and V -> ring slot *pos % 64 and, when that completes a group, the group's
+ * int8 requantization, exactly as nova_kv_append_int8; device scalars
+ * written/qlen/pg updated.  cos/sin: fp16 [rope_len, 128] tables.
+ * Replaces LeanAttention.forward's q_norm / k_norm / apply_rotary_pos_emb /
+ * cache.update (src/nova/layers.py:108-133, :24-36; src/nova/kvattn.py:668-743).
+ */
+typedef struct nova_qk_args {
+    const void* qkv;            /* fp16 [batch, (q_heads + 2*kv_heads)*128]      */
+    int64_t qkv_stride;
+    const void* q_norm_weight;  /* fp16 [128]                                    */
+    const void* k_norm_weight;  /* fp16 [128]                                    */
+    double eps;
+    const void* cos;            /* fp16 [rope_len, 128]                          */
+    const void* sin;
+    int64_t rope_len;
+    void* q_out;                /* fp16 [batch, q_heads*128]                     */
+    int64_t q_out_stride;
+    void* tail_k;               /* cache of this layer, as nova_kv_append_int8   */
+    void* tail_v;
+    void* kq;
+    void* vq;
+    void* kmn;
+    void* kst;
+    void* vmn;
+    void* vst;
+    const int64_t* pos;
+    int64_t* written;
+    int64_t* qlen;
+    int64_t* pg;
+    int64_t batch, q_heads, kv_heads, head_dim, max_len, group;
+} nova_qk_args;
+
+NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

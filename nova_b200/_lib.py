@@ -15,6 +15,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().with_name("libnova_b200.so")
 
 NOVA_OK, NOVA_ERR_INVALID, NOVA_ERR_ALIGN, NOVA_ERR_UNSUPPORTED, NOVA_ERR_CUDA = range(5)
+NF4_PLAIN, NF4_RESIDUAL, NF4_SILU_MUL, NF4_ARGMAX = range(4)
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int64
@@ -37,6 +38,31 @@ class AttnArgs(ctypes.Structure):
     ]
 
 
+class NF4Args(ctypes.Structure):
+    """Mirror of ``nova_nf4_args``."""
+
+    _fields_ = [
+        ("x", _P), ("x_stride", _I), ("norm_weight", _P), ("eps", ctypes.c_double),
+        ("packed", _P), ("absmax", _P), ("absmax_fp32", _I), ("lut", _P), ("bias", _P),
+        ("residual", _P), ("res_stride", _I), ("out", _P), ("out_stride", _I), ("argmax", _P),
+        ("token_out", _P), ("pos", _P), ("embed", _P), ("embed_out", _P), ("embed_out_stride", _I),
+        ("embed_dim", _I), ("workspace", _P), ("workspace_bytes", _I),
+        ("m", _I), ("n", _I), ("k", _I), ("epilogue", _I),
+    ]
+
+
+class QKArgs(ctypes.Structure):
+    """Mirror of ``nova_qk_args``."""
+
+    _fields_ = [
+        ("qkv", _P), ("qkv_stride", _I), ("q_norm_weight", _P), ("k_norm_weight", _P), ("eps", ctypes.c_double),
+        ("cos", _P), ("sin", _P), ("rope_len", _I), ("q_out", _P), ("q_out_stride", _I),
+        ("tail_k", _P), ("tail_v", _P), ("kq", _P), ("vq", _P), ("kmn", _P), ("kst", _P), ("vmn", _P), ("vst", _P),
+        ("pos", _P), ("written", _P), ("qlen", _P), ("pg", _P),
+        ("batch", _I), ("q_heads", _I), ("kv_heads", _I), ("head_dim", _I), ("max_len", _I), ("group", _I),
+    ]
+
+
 # name -> argtypes (every entry point returns int status unless noted)
 _SIGNATURES: dict[str, list] = {
     "nova_kv_quant_int8": [_P, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P],
@@ -46,6 +72,12 @@ _SIGNATURES: dict[str, list] = {
     "nova_attn_workspace_bytes": [_I, _I, _I, _I, _i, ctypes.POINTER(_I)],
     "nova_attn_decode_int8": [ctypes.POINTER(AttnArgs), _P],
     "nova_attn_read_error": [_P, _I, _I, ctypes.POINTER(_i)],
+    "nova_nf4_workspace_bytes": [_I, ctypes.POINTER(_I)],
+    "nova_nf4_gemv": [ctypes.POINTER(NF4Args), _P],
+    "nova_nf4_quantize": [_P, _I, _I, _P, _P, _P, _i, _P],
+    "nova_nf4_dequant": [_P, _P, _i, _P, _P, _I, _I, _P],
+    "nova_rmsnorm": [_P, _I, _P, _I, _P, _I, _P, _P, _I, _I, _I, ctypes.c_double, _P],
+    "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
 }
 _STRING_FNS = ("nova_version", "nova_last_error")
 

@@ -1,0 +1,426 @@
+"""Lean Qwen3-VL-4B text decoder on B200: NF4 weights, streaming int8 KV,
+greedy decode captured in one CUDA graph.
+
+This is the B200 counterpart of the reference's graph-decode path:
+``GraphDecoder`` (src/nova/decode.py:87-526) driving ``NovaTextModel`` /
+``LeanDecoderLayer`` (src/nova/model.py:115-204, src/nova/layers.py:99-218)
+with ``KVInt8Cache`` (src/nova/kvattn.py:488-880) and NF4 linears
+(src/nova/quant.py).  One decode step is 6 kernel launches per layer plus one
+for the lm_head:
+
+    1. nova_nf4_gemv      input_layernorm (prologue) + fused q|k|v projection
+    2. nova_qk_norm_rope_append   q_norm/k_norm, RoPE, ring write, group requant
+    3. nova_attn_decode_int8      int8 prefix + fp16 ring, split-K, merged
+    4. nova_nf4_gemv      o_proj + residual add (epilogue, in place)
+    5. nova_nf4_gemv      post_attention_layernorm (prologue) + gate|up + SiLU*up
+    6. nova_nf4_gemv      down_proj + residual add
+    final: nova_nf4_gemv  final norm (prologue) + 4-bit lm_head + greedy argmax
+           + input_ids / pos update + next-token embedding gather (last warp)
+
+Weights: the reference keeps q/k/v and gate/up as separate modules; here
+q|k|v are concatenated row-wise and gate|up are interleaved per 16-row tile
+(8 gate rows, then the same 8 up rows) so one GEMV produces SiLU(gate)*up.
+The tied lm_head is the NF4 copy of ``embed_tokens`` (src/nova/loader.py:67-119).
+
+Prefill (not the hot path) runs the reference's math eagerly on the GPU:
+NF4 -> fp16 dequant + fp16 matmul, fp16 SDPA with the causal mask, then the
+complete 64-token groups of every layer's K/V are quantized with
+``nova_kv_quant_int8`` and the tail goes to the fp16 ring (same result as
+``KVInt8Cache.finish_prefill``).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from .kernels import build_nf4_lut, fused_rms_norm, gemv_workspace, nf4_gemv
+from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention
+from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
+
+
+@dataclass
+class DecoderConfig:
+    """Qwen3-VL-4B text tower dimensions (src/nova/config.py:14-37)."""
+
+    vocab_size: int = 151936
+    hidden_size: int = 2560
+    num_hidden_layers: int = 36
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 9728
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 5_000_000.0
+
+    @property
+    def q_dim(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+
+def interleave_gate_up(gate_p, gate_a, up_p, up_a):
+    """Interleave gate and up NF4 weights per 16-row tile: rows 16r..16r+7 =
+    gate rows 8r..8r+7, rows 16r+8..16r+15 = up rows 8r..8r+7 (the layout the
+    SILU_MUL epilogue expects).  packed ``[N, K/2]``, absmax ``[K/64, N]``."""
+    n, k2 = gate_p.shape
+    if n % 8:
+        raise ValueError("intermediate size must be a multiple of 8")
+    packed = torch.stack([gate_p.view(n // 8, 8, k2), up_p.view(n // 8, 8, k2)], dim=1).reshape(2 * n, k2)
+    kb = gate_a.shape[0]
+    absmax = torch.stack([gate_a.view(kb, n // 8, 8), up_a.view(kb, n // 8, 8)], dim=2).reshape(kb, 2 * n)
+    return packed.contiguous(), absmax.contiguous()
+
+
+def deinterleave_gate_up(packed, absmax):
+    """Inverse of :func:`interleave_gate_up` -> (gate_p, gate_a, up_p, up_a)."""
+    n2, k2 = packed.shape
+    n = n2 // 2
+    p = packed.view(n // 8, 2, 8, k2)
+    kb = absmax.shape[0]
+    a = absmax.view(kb, n // 8, 2, 8)
+    return (p[:, 0].reshape(n, k2), a[:, :, 0].reshape(kb, n), p[:, 1].reshape(n, k2), a[:, :, 1].reshape(kb, n))
+
+
+@dataclass
+class NF4Weight:
+    packed: torch.Tensor   # uint8 [N, K/2]
+    absmax: torch.Tensor   # fp16 [K/64, N]
+
+    @property
+    def shape(self):
+        return self.packed.shape[0], self.packed.shape[1] * 2
+
+
+@dataclass
+class LayerWeights:
+    qkv: NF4Weight          # [q_dim + 2 kv_dim, hidden]
+    o: NF4Weight            # [hidden, q_dim]
+    gate_up: NF4Weight      # [2 inter, hidden], interleaved
+    down: NF4Weight         # [hidden, inter]
+    input_ln: torch.Tensor  # fp16 [hidden]
+    post_ln: torch.Tensor
+    q_norm: torch.Tensor    # fp16 [head_dim]
+    k_norm: torch.Tensor
+
+
+@dataclass
+class DecoderWeights:
+    cfg: DecoderConfig
+    embed: torch.Tensor          # fp16 [vocab, hidden]
+    lm_head: NF4Weight           # NF4 copy of embed (tied)
+    final_norm: torch.Tensor
+    layers: list = field(default_factory=list)
+    code: torch.Tensor | None = None
+
+    @classmethod
+    def random_init(cls, cfg: DecoderConfig, seed: int = 0, device="cuda", std: float = 0.02,
+                    norm_jitter: float = 0.0) -> "DecoderWeights":
+        """Random-init weights like the HF initializer (normal(0, std) for
+        linear and embedding weights, RMSNorm weights 1), quantized to NF4
+        (blocksize 64, fp16 absmax).  ``norm_jitter`` > 0 perturbs the norm
+        weights (1 + jitter*N(0,1)) to exercise them in tests."""
+        g = torch.Generator(device=device).manual_seed(seed)
+        code = nf4_codebook()
+
+        def lin(n, k):
+            w = (torch.randn(n, k, generator=g, device=device, dtype=torch.float32) * std).to(torch.float16)
+            p, a = quantize_nf4(w, code)
+            return p, a
+
+        def nw(n):
+            if norm_jitter:
+                return (1.0 + norm_jitter * torch.randn(n, generator=g, device=device)).to(torch.float16)
+            return torch.ones(n, dtype=torch.float16, device=device)
+
+        layers = []
+        for _ in range(cfg.num_hidden_layers):
+            qp, qa = lin(cfg.q_dim, cfg.hidden_size)
+            kp, ka = lin(cfg.kv_dim, cfg.hidden_size)
+            vp, va = lin(cfg.kv_dim, cfg.hidden_size)
+            op, oa = lin(cfg.hidden_size, cfg.q_dim)
+            gp, ga = lin(cfg.intermediate_size, cfg.hidden_size)
+            up, ua = lin(cfg.intermediate_size, cfg.hidden_size)
+            dp, da = lin(cfg.hidden_size, cfg.intermediate_size)
+            gu_p, gu_a = interleave_gate_up(gp, ga, up, ua)
+            layers.append(LayerWeights(
+                qkv=NF4Weight(torch.cat([qp, kp, vp]), torch.cat([qa, ka, va], dim=1).contiguous()),
+                o=NF4Weight(op, oa), gate_up=NF4Weight(gu_p, gu_a), down=NF4Weight(dp, da),
+                input_ln=nw(cfg.hidden_size), post_ln=nw(cfg.hidden_size),
+                q_norm=nw(cfg.head_dim), k_norm=nw(cfg.head_dim)))
+        embed = (torch.randn(cfg.vocab_size, cfg.hidden_size, generator=g, device=device) * std).to(torch.float16)
+        lp, la = quantize_nf4(embed, code)
+        return cls(cfg=cfg, embed=embed, lm_head=NF4Weight(lp, la), final_norm=nw(cfg.hidden_size), layers=layers,
+                   code=code)
+
+    def nbytes_per_token(self) -> int:
+        """Weight bytes one decode step streams (NF4 codes + fp16 absmax)."""
+        tot = 0
+        for lw in self.layers:
+            for w in (lw.qkv, lw.o, lw.gate_up, lw.down):
+                tot += w.packed.numel() + w.absmax.numel() * w.absmax.element_size()
+        tot += self.lm_head.packed.numel() + self.lm_head.absmax.numel() * 2
+        return tot
+
+
+def rope_tables(max_pos: int, head_dim: int = 128, theta: float = 5_000_000.0, device="cuda"):
+    """fp16 cos/sin ``[max_pos, head_dim]`` computed exactly like the HF
+    rotary for text tokens (fp32 inv_freq = 1/theta**(2i/d), fp32 pos*inv_freq,
+    cat(freqs, freqs), fp32 cos/sin, cast to fp16), on the CPU."""
+    e = torch.arange(0, head_dim, 2, dtype=torch.int64).to(dtype=torch.float) / head_dim
+    inv = 1.0 / (theta ** e)
+    pos = torch.arange(max_pos, dtype=torch.float32)
+    freqs = pos[:, None] * inv[None, :]
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos().to(torch.float16).to(device), emb.sin().to(torch.float16).to(device)
+
+
+class NovaDecoder:
+    """Greedy graph decoder (src/nova/decode.py:87-526) for the NF4 / int8-KV
+    Qwen3-VL text model.
+
+        dec = NovaDecoder(weights, max_len=8448, batch=1)
+        dec.prefill(prompt_ids)      # eager; fills the int8 cache, sets input_ids
+        dec.capture()                # one decode step -> CUDA graph
+        for _ in range(n): dec.step()  # one replay = one token per row
+
+    ``input_ids`` (int64 ``[batch]``) holds the latest greedy token and ``pos``
+    the next position, like the reference's ``GraphDecoder``; ``logits``
+    (fp16 ``[batch, vocab]``) the last step's logits.
+    """
+
+    def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
+                 device="cuda") -> None:
+        cfg = weights.cfg
+        if batch < 1 or batch > 8:
+            raise ValueError("the GEMV decode path handles batch 1..8")
+        self.w = weights
+        self.cfg = cfg
+        self.batch = int(batch)
+        self.max_len = int(max_len)
+        self.device = torch.device(device)
+        if chunk is None:
+            chunk = self._pick_chunk()
+        self.cache = KVInt8Cache(num_slots=cfg.num_hidden_layers, num_kv_heads=cfg.num_key_value_heads,
+                                 head_dim=cfg.head_dim, max_len=self.max_len, num_q_heads=cfg.num_attention_heads,
+                                 batch=self.batch, device=self.device, chunk=chunk)
+        self.lut = build_nf4_lut(weights.code if weights.code is not None else nf4_codebook()).to(self.device)
+        self.cos, self.sin = rope_tables(self.max_len + 1, cfg.head_dim, cfg.rope_theta, self.device)
+        B, dev, f16 = self.batch, self.device, torch.float16
+        self.resid = torch.zeros(B, cfg.hidden_size, dtype=f16, device=dev)
+        self.qkv = torch.zeros(B, cfg.q_dim + 2 * cfg.kv_dim, dtype=f16, device=dev)
+        self.q_rot = torch.zeros(B, cfg.q_dim, dtype=f16, device=dev)
+        self.attn = torch.zeros(B, cfg.q_dim, dtype=f16, device=dev)
+        self.act = torch.zeros(B, cfg.intermediate_size, dtype=f16, device=dev)
+        self.logits = torch.zeros(B, cfg.vocab_size, dtype=f16, device=dev)
+        self.argmax_slot = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.input_ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.gemv_ws = gemv_workspace(dev, cfg.vocab_size).clone()
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    def _pick_chunk(self) -> int:
+        """Split size for the attention: about two CTAs per SM at full capacity."""
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        per_head = max(1, (2 * sms) // (self.batch * self.cfg.num_key_value_heads))
+        chunk = -(-self.max_len // per_head)
+        chunk = max(GROUP_T * 4, -(-chunk // GROUP_T) * GROUP_T)
+        return chunk
+
+    @property
+    def pos(self) -> torch.Tensor:
+        return self.cache.pos
+
+    # ---------------------------------------------------------------- prefill
+
+    def _linear16(self, x: torch.Tensor, w: NF4Weight) -> torch.Tensor:
+        w16 = dequantize_nf4(w.packed, w.absmax, self.lut)
+        return torch.matmul(x, w16.t())
+
+    @torch.inference_mode()
+    def prefill(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """Eager prefill of ``input_ids`` ``[batch, T]`` from position 0;
+        returns the first greedy token ``[batch]`` (also left in ``input_ids``,
+        src/nova/decode.py:224-297)."""
+        cfg, cache = self.cfg, self.cache
+        B, T = input_ids.shape
+        if B != self.batch or T < 1 or T >= self.max_len:
+            raise ValueError(f"prompt shape {tuple(input_ids.shape)} does not fit batch={self.batch}, "
+                             f"max_len={self.max_len}")
+        cache.reset()
+        ids = input_ids.to(self.device)
+        h = self.w.embed[ids]                                     # [B, T, H]
+        cos, sin = self.cos[:T][None, None], self.sin[:T][None, None]
+        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        q_full = (T // GROUP_T) * GROUP_T
+        stream = _lib.stream_of(self.device)
+        for li, lw in enumerate(self.w.layers):
+            x = fused_rms_norm(h, lw.input_ln, cfg.rms_norm_eps)
+            qkv = self._linear16(x, lw.qkv)
+            q = qkv[..., :cfg.q_dim].reshape(B, T, hq, d)
+            k = qkv[..., cfg.q_dim:cfg.q_dim + cfg.kv_dim].reshape(B, T, hkv, d)
+            v = qkv[..., cfg.q_dim + cfg.kv_dim:].reshape(B, T, hkv, d).transpose(1, 2)
+            q = fused_rms_norm(q, lw.q_norm, cfg.rms_norm_eps).transpose(1, 2)
+            k = fused_rms_norm(k, lw.k_norm, cfg.rms_norm_eps).transpose(1, 2)
+            q = q * cos + _rotate_half(q) * sin
+            k = (k * cos + _rotate_half(k) * sin).contiguous()
+            v = v.contiguous()
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=d ** -0.5, enable_gqa=True)
+            o = o.transpose(1, 2).reshape(B, T, cfg.q_dim)
+            h = h + self._linear16(o, lw.o)
+            x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
+            gu = self._linear16(x, lw.gate_up).view(B, T, -1, 2, 8)
+            gate = gu[:, :, :, 0].reshape(B, T, -1)
+            up = gu[:, :, :, 1].reshape(B, T, -1)
+            h = h + self._linear16(F.silu(gate) * up, lw.down)
+            # int8 cache: complete groups quantized, the rest into the ring
+            if q_full:
+                for src, dst, mn, st in ((k, cache.kq[li], cache.kmn[li], cache.kst[li]),
+                                         (v, cache.vq[li], cache.vmn[li], cache.vst[li])):
+                    _lib.call("nova_kv_quant_int8", src.data_ptr(), T * d, dst.data_ptr(), self.max_len * d,
+                              mn.data_ptr(), st.data_ptr(), mn.shape[2] * d, B * hkv, q_full, d, GROUP_T, stream)
+            take = min(T, GROUP_T)
+            slots = torch.remainder(torch.arange(T - take, T, device=self.device), GROUP_T)
+            cache.tail_k[li].index_copy_(2, slots, k[:, :, T - take:T])
+            cache.tail_v[li].index_copy_(2, slots, v[:, :, T - take:T])
+        x = fused_rms_norm(h[:, -1], self.w.final_norm, cfg.rms_norm_eps)
+        logits = self._linear16(x, self.w.lm_head)
+        first = torch.argmax(logits, dim=-1)
+        self.logits.copy_(logits)
+        self.input_ids.copy_(first)
+        self.resid.copy_(self.w.embed[first])
+        cache.pos.fill_(T)
+        cache.first.fill_(0)
+        cache._written.fill_(T)
+        cache._qlen.fill_(q_full)
+        cache._pg.fill_(q_full // GROUP_T)
+        self.argmax_slot.zero_()
+        return first
+
+    # ---------------------------------------------------------------- decode
+
+    def _step_body(self) -> None:
+        cfg, cache, lut = self.cfg, self.cache, self.lut
+        eps = cfg.rms_norm_eps
+        B = self.batch
+        stream = _lib.stream_of(self.device)
+        q3 = self.q_rot.view(B, cfg.num_attention_heads, cfg.head_dim)
+        a3 = self.attn.view(B, cfg.num_attention_heads, cfg.head_dim)
+        ws = self.gemv_ws
+        for li, lw in enumerate(self.w.layers):
+            nf4_gemv(self.resid, lw.qkv.packed, lw.qkv.absmax, lut, self.qkv, norm_weight=lw.input_ln, eps=eps,
+                     workspace=ws)
+            qa = _lib.QKArgs()
+            qa.qkv, qa.qkv_stride = self.qkv.data_ptr(), self.qkv.stride(0)
+            qa.q_norm_weight, qa.k_norm_weight, qa.eps = lw.q_norm.data_ptr(), lw.k_norm.data_ptr(), eps
+            qa.cos, qa.sin, qa.rope_len = self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0]
+            qa.q_out, qa.q_out_stride = self.q_rot.data_ptr(), self.q_rot.stride(0)
+            qa.tail_k, qa.tail_v = cache.tail_k[li].data_ptr(), cache.tail_v[li].data_ptr()
+            qa.kq, qa.vq = cache.kq[li].data_ptr(), cache.vq[li].data_ptr()
+            qa.kmn, qa.kst = cache.kmn[li].data_ptr(), cache.kst[li].data_ptr()
+            qa.vmn, qa.vst = cache.vmn[li].data_ptr(), cache.vst[li].data_ptr()
+            qa.pos, qa.written = cache.pos.data_ptr(), cache._written.data_ptr()
+            qa.qlen, qa.pg = cache._qlen.data_ptr(), cache._pg.data_ptr()
+            qa.batch, qa.q_heads, qa.kv_heads = B, cfg.num_attention_heads, cfg.num_key_value_heads
+            qa.head_dim, qa.max_len, qa.group = cfg.head_dim, self.max_len, GROUP_T
+            _lib.check(_lib.lib().nova_qk_norm_rope_append(_lib.ctypes.byref(qa), stream), "qk_norm_rope_append")
+            launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
+                                  cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
+                             cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
+                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window)
+            nf4_gemv(self.attn, lw.o.packed, lw.o.absmax, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
+                     residual=self.resid, workspace=ws)
+            nf4_gemv(self.resid, lw.gate_up.packed, lw.gate_up.absmax, lut, self.act, epilogue=_lib.NF4_SILU_MUL,
+                     norm_weight=lw.post_ln, eps=eps, workspace=ws)
+            nf4_gemv(self.act, lw.down.packed, lw.down.absmax, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
+                     residual=self.resid, workspace=ws)
+        nf4_gemv(self.resid, self.w.lm_head.packed, self.w.lm_head.absmax, lut, self.logits,
+                 epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm, eps=eps, argmax=self.argmax_slot,
+                 token_out=self.input_ids, pos=cache.pos, embed=self.w.embed, embed_out=self.resid, workspace=ws)
+
+    def launches_per_step(self) -> int:
+        return 6 * self.cfg.num_hidden_layers + 1
+
+    @torch.inference_mode()
+    def step_eager(self) -> torch.Tensor:
+        """One decode step without a graph (same kernels); returns input_ids."""
+        self._step_body()
+        return self.input_ids
+
+    @torch.inference_mode()
+    def capture(self) -> None:
+        """Capture one decode step.  Capture does not execute anything, so the
+        decode state is untouched."""
+        self.graph = None
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._step_body()
+        self.graph = g
+
+    def step(self) -> torch.Tensor:
+        """One greedy token per row: a single graph replay."""
+        if self.graph is None:
+            raise RuntimeError("call capture() first")
+        self.graph.replay()
+        return self.input_ids
+
+    def step_host(self, tokens_in: torch.Tensor, tokens_out: torch.Tensor) -> torch.Tensor:
+        """Streaming API with host buffers (pinned for async copies): the step's
+        input tokens are copied in, their embedding rows gathered, the decode
+        graph replayed and the greedy tokens copied back; returns
+        ``tokens_out`` once the stream has finished the step."""
+        if self.graph is None:
+            raise RuntimeError("call capture() first")
+        self.input_ids.copy_(tokens_in, non_blocking=True)
+        torch.index_select(self.w.embed, 0, self.input_ids, out=self.resid)
+        self.graph.replay()
+        tokens_out.copy_(self.input_ids, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return tokens_out
+
+    def state(self) -> dict:
+        """Host copy of the decode state (cache + scalars), e.g. to seed the
+        CPU oracle."""
+        c = self.cache
+        arr = lambda t: t.cpu().numpy()  # noqa: E731
+        return {
+            "pos": int(c.pos.item()), "written": int(c._written.item()), "qlen": int(c._qlen.item()),
+            "input_ids": arr(self.input_ids), "resid": arr(self.resid),
+            "kq": [arr(t) for t in c.kq], "vq": [arr(t) for t in c.vq], "kmn": [arr(t) for t in c.kmn],
+            "kst": [arr(t) for t in c.kst], "vmn": [arr(t) for t in c.vmn], "vst": [arr(t) for t in c.vst],
+            "tail_k": [arr(t) for t in c.tail_k], "tail_v": [arr(t) for t in c.tail_v],
+        }
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    x1 = x[..., : x.shape[-1] // 2]
+    x2 = x[..., x.shape[-1] // 2:]
+    return torch.cat((-x2, x1), dim=-1)
+
+
+def weights_to_numpy(w: DecoderWeights) -> dict:
+    """Host copies of the NF4 weights (for the CPU oracle in tests)."""
+    out = {"embed": w.embed.cpu().numpy(), "lm_head": (w.lm_head.packed.cpu().numpy(), w.lm_head.absmax.cpu().numpy()),
+           "final_norm": w.final_norm.cpu().numpy(), "code": (w.code if w.code is not None else nf4_codebook()).numpy(),
+           "layers": []}
+    for lw in w.layers:
+        gp, ga, up, ua = deinterleave_gate_up(lw.gate_up.packed, lw.gate_up.absmax)
+        out["layers"].append({
+            "qkv": (lw.qkv.packed.cpu().numpy(), lw.qkv.absmax.cpu().numpy()),
+            "o": (lw.o.packed.cpu().numpy(), lw.o.absmax.cpu().numpy()),
+            "gate": (gp.cpu().numpy(), ga.cpu().numpy()), "up": (up.cpu().numpy(), ua.cpu().numpy()),
+            "down": (lw.down.packed.cpu().numpy(), lw.down.absmax.cpu().numpy()),
+            "input_ln": lw.input_ln.cpu().numpy(), "post_ln": lw.post_ln.cpu().numpy(),
+            "q_norm": lw.q_norm.cpu().numpy(), "k_norm": lw.k_norm.cpu().numpy()})
+    return out
+
+
+__all__ = ["DecoderConfig", "DecoderWeights", "NovaDecoder", "interleave_gate_up", "deinterleave_gate_up",
+           "rope_tables", "weights_to_numpy"]

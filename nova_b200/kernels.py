@@ -1,0 +1,170 @@
+"""RMSNorm and NF4 GEMV on B200, keeping the reference entry points of
+``nova.kernels`` (src/nova/kernels.py): ``triton_available``,
+``fused_rms_norm``, ``build_nf4_lut``, ``fused_nf4_linear``,
+``nf4_launch_config`` / ``set_nf4_launch_config``.
+
+The reference implements these as Triton kernels; here they call the sm_100a
+kernels of ``libnova_b200.so`` (``nova_rmsnorm``, ``nova_nf4_gemv``).  There is
+no fallback: CPU tensors or a missing library raise.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+NF4_BLOCK = 64
+NF4_BYTES = 32
+MAX_GEMV_M = 8
+
+_NF4_DEFAULTS: dict[str, int] = {"block_n": 64, "block_m": 1, "num_warps": 2, "num_stages": 2}
+_nf4_launch: dict[str, int] = dict(_NF4_DEFAULTS)
+
+_WORKSPACES: dict[tuple[str, int], torch.Tensor] = {}
+_ARGMAX_SLOTS: dict[str, torch.Tensor] = {}
+
+
+def triton_available() -> bool:
+    """Name kept from the reference (src/nova/kernels.py:75-94): True when the
+    B200 kernel library is loaded and a CUDA device is present."""
+    return _lib.available()
+
+
+def nf4_launch_config() -> dict[str, int]:
+    """The reference's Triton launch knobs; accepted for compatibility, the
+    B200 GEMV sizes its persistent grid from the SM count."""
+    return dict(_nf4_launch)
+
+
+def set_nf4_launch_config(**kwargs: int) -> dict[str, int]:
+    for key, value in kwargs.items():
+        if key not in _NF4_DEFAULTS:
+            raise KeyError(f"unknown launch parameter: {key}")
+        _nf4_launch[key] = int(value)
+    return dict(_nf4_launch)
+
+
+def fused_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm over the last dimension, HF order (src/nova/kernels.py:97-115)."""
+    _lib.require_cuda(x, weight, names=("x", "weight"))
+    n = weight.shape[0]
+    if x.shape[-1] != n:
+        raise ValueError(f"last dim {x.shape[-1]} does not match weight length {n}")
+    if x.dtype != torch.float16 or weight.dtype != torch.float16:
+        raise ValueError("fused_rms_norm takes float16 x and weight")
+    x = x.contiguous()
+    weight = weight.contiguous()
+    rows = x.numel() // n
+    y = torch.empty_like(x)
+    _lib.call("nova_rmsnorm", x.data_ptr(), n, None, 0, None, 0, weight.data_ptr(), y.data_ptr(), n, rows, n,
+              float(eps), _lib.stream_of(x.device))
+    return y
+
+
+def residual_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float):
+    """``h = residual + x`` (fp16) and ``RMSNorm(h)`` in one launch -> (h, y)."""
+    _lib.require_cuda(x, residual, weight, names=("x", "residual", "weight"))
+    n = weight.shape[0]
+    x, residual = x.contiguous(), residual.contiguous()
+    rows = x.numel() // n
+    h = torch.empty_like(x)
+    y = torch.empty_like(x)
+    _lib.call("nova_rmsnorm", x.data_ptr(), n, residual.data_ptr(), n, h.data_ptr(), n, weight.data_ptr(),
+              y.data_ptr(), n, rows, n, float(eps), _lib.stream_of(x.device))
+    return h, y
+
+
+def build_nf4_lut(code: torch.Tensor) -> torch.Tensor:
+    """256-entry int32 table: low 16 bits = fp16(code[a >> 4]), high 16 bits =
+    fp16(code[a & 15]) (src/nova/kernels.py:170-182)."""
+    c16 = code.detach().to(torch.float16).cpu()
+    idx = torch.arange(256, dtype=torch.int64)
+    even_bits = c16[idx >> 4].view(torch.int16).to(torch.int64) & 0xFFFF
+    odd_bits = c16[idx & 15].view(torch.int16).to(torch.int64) & 0xFFFF
+    val = (even_bits | (odd_bits << 16)) & 0xFFFFFFFF
+    val = torch.where(val >= 2 ** 31, val - 2 ** 32, val)
+    return val.to(torch.int32)
+
+
+def gemv_workspace(device: torch.device, n: int) -> torch.Tensor:
+    """Cached zeroed workspace for ``nova_nf4_gemv`` with N rows (eager path;
+    calls on one stream may share it)."""
+    out = _lib.ctypes.c_int64(0)
+    _lib.call("nova_nf4_workspace_bytes", int(n), _lib.ctypes.byref(out))
+    key = (str(device), int(out.value))
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        ws = torch.zeros(int(out.value), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, lut: torch.Tensor, out: torch.Tensor, *,
+             epilogue: int = _lib.NF4_PLAIN, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+             norm_weight: torch.Tensor | None = None, eps: float = 1e-6, argmax: torch.Tensor | None = None,
+             token_out: torch.Tensor | None = None, pos: torch.Tensor | None = None,
+             embed: torch.Tensor | None = None, embed_out: torch.Tensor | None = None,
+             workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Launch ``nova_nf4_gemv`` on 2-D views (x ``[M, K]``, out ``[M, N or N/2]``)."""
+    m, k = x.shape
+    n = packed.shape[0]
+    if packed.shape[1] * 2 != k or absmax.shape != (k // NF4_BLOCK, n):
+        raise ValueError(f"weight shapes packed {tuple(packed.shape)} / absmax {tuple(absmax.shape)} "
+                         f"do not match K={k}, N={n}")
+    if absmax.dtype not in (torch.float32, torch.float16):
+        raise ValueError("absmax must be float32 or float16")
+    for t, nm in ((x, "x"), (out, "out")):
+        if t.stride(1) != 1:
+            raise ValueError(f"{nm} must have a contiguous last dimension")
+    ws = gemv_workspace(x.device, n) if workspace is None else workspace
+    a = _lib.NF4Args()
+    a.x, a.x_stride = x.data_ptr(), x.stride(0)
+    a.norm_weight, a.eps = _lib.ptr(norm_weight), float(eps)
+    a.packed, a.absmax, a.absmax_fp32 = packed.data_ptr(), absmax.data_ptr(), int(absmax.dtype == torch.float32)
+    a.lut = lut.data_ptr()
+    a.bias = _lib.ptr(bias)
+    a.residual, a.res_stride = (_lib.ptr(residual), residual.stride(0) if residual is not None else 0)
+    a.out, a.out_stride = out.data_ptr(), out.stride(0)
+    a.argmax, a.token_out, a.pos = _lib.ptr(argmax), _lib.ptr(token_out), _lib.ptr(pos)
+    a.embed = _lib.ptr(embed)
+    a.embed_out = _lib.ptr(embed_out)
+    a.embed_out_stride = embed_out.stride(0) if embed_out is not None else 0
+    a.embed_dim = embed.shape[1] if embed is not None else 0
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.m, a.n, a.k, a.epilogue = m, n, k, int(epilogue)
+    _lib.check(_lib.lib().nova_nf4_gemv(_lib.ctypes.byref(a), _lib.stream_of(x.device)), "nova_nf4_gemv")
+    return out
+
+
+def fused_nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, lut: torch.Tensor,
+                     out_features: int, bias: torch.Tensor | None = None, **launch_overrides: int) -> torch.Tensor:
+    """NF4 linear ``x @ dequant(packed, absmax, code).T + bias``
+    (src/nova/kernels.py:243-289).  ``x`` fp16 ``[..., K]``; packed uint8
+    ``[N, K/2]``; absmax ``[K/64, N]`` fp32 (reference) or fp16 (native).
+    Rows are processed 8 at a time by the GEMV kernel."""
+    _lib.require_cuda(x, packed, absmax, lut, names=("x", "packed", "absmax", "lut"))
+    k = x.shape[-1]
+    k2 = packed.shape[-1]
+    n_blocks = absmax.shape[0]
+    if k2 * 2 != k:
+        raise ValueError(f"packed last dim {k2} does not match K={k} (should be K//2)")
+    if n_blocks * NF4_BLOCK != k:
+        raise ValueError(f"absmax rows {n_blocks} do not match K={k} (should be K//64)")
+    if packed.shape[0] != out_features or absmax.shape[1] != out_features:
+        raise ValueError(f"weight shapes do not match out_features={out_features}")
+    if x.dtype != torch.float16:
+        raise ValueError("x must be float16")
+    n = out_features
+    orig = x.shape
+    x2 = x.reshape(-1, k)
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    out = torch.empty((m, n), device=x.device, dtype=torch.float16)
+    packed = packed.contiguous()
+    absmax = absmax.contiguous()
+    lut = lut.contiguous()
+    for r in range(0, m, MAX_GEMV_M):
+        nf4_gemv(x2[r:r + MAX_GEMV_M], packed, absmax, lut, out[r:r + MAX_GEMV_M], bias=bias)
+    return out.view(*orig[:-1], n)

@@ -1,0 +1,239 @@
+"""GPU: NF4 quantizer / dequant / GEMV (nova_nf4_*) against the CPU oracle.
+
+Tolerances: the GEMV accumulates exact fp16 products in fp32 like the
+reference kernel, so each fp16 output must be within 1 fp16 ULP of the
+oracle's fp32 result or within 1e-5 * max|y| absolute
+(1e-2 relative to the dequant-matmul) is asserted as well.  The quantizer
+and dequant are bit-exact."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_ulp_or_abs
+from oracle import nf4 as onf4
+from oracle import norm as onorm
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = {  # name: (N, K) -- Qwen3-4B decode projections
+    "q_proj": (4096, 2560), "k_proj": (1024, 2560), "v_proj": (1024, 2560), "o_proj": (2560, 4096),
+    "gate_proj": (9728, 2560), "up_proj": (9728, 2560), "down_proj": (2560, 9728),
+}
+
+
+def _weights(n, k, seed, absmax_dtype=torch.float16):
+    from nova_b200.quant import nf4_codebook, quantize_nf4
+
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn(n, k, generator=g) * 0.02).half()
+    packed, absmax = quantize_nf4(w.cuda(), nf4_codebook(), absmax_dtype)
+    return w, packed, absmax
+
+
+def _lut(device="cuda"):
+    from nova_b200.kernels import build_nf4_lut
+    from nova_b200.quant import nf4_codebook
+
+    return build_nf4_lut(nf4_codebook()).to(device)
+
+
+def _oracle_y(x, packed, absmax, rows=None):
+    p, a = packed.cpu().numpy(), absmax.cpu().numpy()
+    if rows is not None:
+        p, a = p[rows], a[:, rows]
+    return onf4.nf4_linear(x.float().cpu().numpy(), p, a, onf4.nf4_codebook())
+
+
+def _check(got, want32, tag):
+    got = got.float().cpu().numpy()
+    scale = float(np.abs(want32).max())
+    assert_ulp_or_abs(got, want32.astype(np.float16), 1.0, 1e-5 * scale, tag)
+    assert np.abs(got - want32).max() <= 1e-2 * scale, f"{tag}: beyond 1e-2 relative"
+
+
+def test_codebook_matches_oracle(cuda_lib):
+    from nova_b200.quant import nf4_codebook
+
+    np.testing.assert_array_equal(nf4_codebook().numpy(), onf4.nf4_codebook())
+    from nova_b200.kernels import build_nf4_lut
+
+    np.testing.assert_array_equal(build_nf4_lut(nf4_codebook()).numpy(), onf4.build_nf4_lut(onf4.nf4_codebook()))
+
+
+@pytest.mark.parametrize("absmax_dtype", [torch.float16, torch.float32])
+def test_quantizer_bit_exact(cuda_lib, absmax_dtype):
+    w, packed, absmax = _weights(320, 1024, 1, absmax_dtype)
+    w[5, :64] = 0   # an all-zero block
+    from nova_b200.quant import nf4_codebook, quantize_nf4
+
+    packed, absmax = quantize_nf4(w.cuda(), nf4_codebook(), absmax_dtype)
+    op, oa = onf4.quantize_nf4(w.numpy(), onf4.nf4_codebook(),
+                               np.float16 if absmax_dtype == torch.float16 else np.float32)
+    np.testing.assert_array_equal(packed.cpu().numpy(), op)
+    np.testing.assert_array_equal(absmax.cpu().numpy(), oa)
+
+
+def test_dequant_bit_exact(cuda_lib):
+    from nova_b200.quant import dequantize_nf4
+
+    _, packed, absmax = _weights(256, 512, 2)
+    got = dequantize_nf4(packed, absmax, _lut())
+    want = onf4.dequantize_nf4(packed.cpu().numpy(), absmax.cpu().numpy(), onf4.nf4_codebook(), round_fp16=True)
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint16), want.view(np.uint16))
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+def test_gemv_qwen_shapes_m1(cuda_lib, name):
+    from nova_b200.kernels import nf4_gemv
+
+    n, k = SHAPES[name]
+    _, packed, absmax = _weights(n, k, hash(name) % 1000)
+    x = (torch.randn(1, k, generator=torch.Generator().manual_seed(3))).half()
+    out = torch.empty(1, n, dtype=torch.float16, device="cuda")
+    nf4_gemv(x.cuda(), packed, absmax, _lut(), out)
+    _check(out, _oracle_y(x, packed, absmax), name)
+
+
+def test_gemv_lm_head_shape_sampled_rows(cuda_lib):
+    """151936 x 2560 (the 4-bit lm_head): all rows computed on the GPU, 4096
+    random rows checked against the oracle."""
+    from nova_b200.kernels import nf4_gemv
+
+    n, k = 151936, 2560
+    _, packed, absmax = _weights(n, k, 11)
+    x = torch.randn(1, k, generator=torch.Generator().manual_seed(4)).half()
+    out = torch.empty(1, n, dtype=torch.float16, device="cuda")
+    nf4_gemv(x.cuda(), packed, absmax, _lut(), out)
+    rows = np.sort(np.random.default_rng(0).choice(n, 4096, replace=False))
+    _check(out[:, rows], _oracle_y(x, packed, absmax, rows), "lm_head")
+
+
+@pytest.mark.parametrize("m", [2, 5, 8])
+def test_gemv_small_batch(cuda_lib, m):
+    from nova_b200.kernels import nf4_gemv
+
+    _, packed, absmax = _weights(1024, 2560, 5)
+    x = torch.randn(m, 2560, generator=torch.Generator().manual_seed(m)).half()
+    out = torch.empty(m, 1024, dtype=torch.float16, device="cuda")
+    nf4_gemv(x.cuda(), packed, absmax, _lut(), out)
+    _check(out, _oracle_y(x, packed, absmax), f"m={m}")
+
+
+def test_gemv_is_deterministic(cuda_lib):
+    """The split-K reduction adds partials in a fixed order: repeated launches
+    are bit-identical."""
+    from nova_b200.kernels import nf4_gemv
+
+    _, packed, absmax = _weights(2560, 4096, 6)
+    x = torch.randn(1, 4096, generator=torch.Generator().manual_seed(7)).half().cuda()
+    a = nf4_gemv(x, packed, absmax, _lut(), torch.empty(1, 2560, dtype=torch.float16, device="cuda"))
+    b = nf4_gemv(x, packed, absmax, _lut(), torch.empty(1, 2560, dtype=torch.float16, device="cuda"))
+    assert torch.equal(a, b)
+
+
+def test_residual_epilogue(cuda_lib):
+    from nova_b200 import _lib
+    from nova_b200.kernels import nf4_gemv
+
+    _, packed, absmax = _weights(2560, 4096, 8)
+    x = torch.randn(1, 4096, generator=torch.Generator().manual_seed(8)).half()
+    res = torch.randn(1, 2560, generator=torch.Generator().manual_seed(9)).half()
+    out = res.clone().cuda()
+    nf4_gemv(x.cuda(), packed, absmax, _lut(), out, epilogue=_lib.NF4_RESIDUAL, residual=out)   # in place
+    y16 = _oracle_y(x, packed, absmax).astype(np.float16)
+    want = (res.numpy().astype(np.float32) + y16.astype(np.float32)).astype(np.float16)
+    got = out.cpu().numpy()
+    assert_ulp_or_abs(got, want, 1.0, 0.0, "residual")
+
+
+def test_silu_mul_epilogue_interleaved(cuda_lib):
+    from nova_b200 import _lib
+    from nova_b200.decoder import interleave_gate_up
+    from nova_b200.kernels import nf4_gemv
+
+    n, k = 1024, 2560
+    _, gp, ga = _weights(n, k, 12)
+    _, up, ua = _weights(n, k, 13)
+    packed, absmax = interleave_gate_up(gp, ga, up, ua)
+    x = torch.randn(1, k, generator=torch.Generator().manual_seed(14)).half()
+    out = torch.empty(1, n, dtype=torch.float16, device="cuda")
+    nf4_gemv(x.cuda(), packed, absmax, _lut(), out, epilogue=_lib.NF4_SILU_MUL)
+    g16 = _oracle_y(x, gp, ga).astype(np.float16)
+    u16 = _oracle_y(x, up, ua).astype(np.float16)
+    want = onorm.silu_mul(g16, u16)
+    assert_ulp_or_abs(out.cpu().numpy(), want, 1.0, 1e-6, "silu_mul")
+
+
+def test_norm_prologue(cuda_lib):
+    from nova_b200.kernels import nf4_gemv
+
+    _, packed, absmax = _weights(6144, 2560, 15)
+    h = (torch.randn(3, 2560, generator=torch.Generator().manual_seed(16)) * 3).half()
+    w = (1 + 0.1 * torch.randn(2560, generator=torch.Generator().manual_seed(17))).half()
+    out = torch.empty(3, 6144, dtype=torch.float16, device="cuda")
+    nf4_gemv(h.cuda(), packed, absmax, _lut(), out, norm_weight=w.cuda(), eps=1e-6)
+    xn = onorm.rms_norm(h.numpy(), w.numpy(), 1e-6)
+    _check(out, _oracle_y(torch.from_numpy(xn), packed, absmax), "norm prologue")
+
+
+def test_argmax_epilogue_and_step_finalize(cuda_lib):
+    from nova_b200 import _lib
+    from nova_b200.kernels import nf4_gemv
+
+    n, k, vocab_embed = 8192, 2560, 8192
+    _, packed, absmax = _weights(n, k, 18)
+    x = torch.randn(2, k, generator=torch.Generator().manual_seed(19)).half()
+    embed = (torch.randn(vocab_embed, k, generator=torch.Generator().manual_seed(20)) * 0.02).half().cuda()
+    logits = torch.empty(2, n, dtype=torch.float16, device="cuda")
+    slot = torch.zeros(2, dtype=torch.int64, device="cuda")
+    tokens = torch.full((2,), -1, dtype=torch.int64, device="cuda")
+    pos = torch.tensor([41], dtype=torch.int64, device="cuda")
+    hidden = torch.empty(2, k, dtype=torch.float16, device="cuda")
+    nf4_gemv(x.cuda(), packed, absmax, _lut(), logits, epilogue=_lib.NF4_ARGMAX, argmax=slot, token_out=tokens,
+             pos=pos, embed=embed, embed_out=hidden)
+    torch.cuda.synchronize()
+    # greedy token = first index of the maximal fp16 logit (torch.argmax semantics)
+    want_tok = torch.argmax(logits, dim=-1)
+    assert torch.equal(tokens, want_tok)
+    assert int(pos.item()) == 42
+    assert torch.count_nonzero(slot).item() == 0
+    assert torch.equal(hidden, embed[want_tok])
+    _check(logits, _oracle_y(x, packed, absmax), "logits")
+
+
+def test_fused_nf4_linear_reference_layout(cuda_lib):
+    """Reference calling convention: fp32 absmax [K/64, N], bias, M = 7 and 20."""
+    from nova_b200.kernels import build_nf4_lut, fused_nf4_linear
+    from nova_b200.quant import nf4_codebook
+
+    _, packed, absmax = _weights(512, 256, 21, torch.float32)
+    lut = build_nf4_lut(nf4_codebook()).cuda()
+    bias = (torch.randn(512, generator=torch.Generator().manual_seed(22)) * 0.01).half()
+    for m in (7, 20):
+        x = (torch.randn(1, m, 256, generator=torch.Generator().manual_seed(m)) * 0.5).half()
+        got = fused_nf4_linear(x.cuda(), packed, absmax, lut, 512, bias.cuda())
+        assert got.shape == (1, m, 512)
+        want = onf4.nf4_linear(x[0].float().numpy(), packed.cpu().numpy(), absmax.cpu().numpy(),
+                               onf4.nf4_codebook(), bias.float().numpy())
+        _check(got[0], want, f"fused_nf4_linear m={m}")
+
+
+def test_nf4linear_module_and_rejects_bad_inputs(cuda_lib):
+    from nova_b200.kernels import fused_nf4_linear
+    from nova_b200.quant import NF4Linear
+
+    w = (torch.randn(256, 512, generator=torch.Generator().manual_seed(23)) * 0.02).half().cuda()
+    lin = NF4Linear.from_float(w)
+    x = torch.randn(1, 1, 512, generator=torch.Generator().manual_seed(24)).half().cuda()
+    y = lin(x)
+    want = _oracle_y(x[0].cpu(), lin.packed, lin.absmax)
+    _check(y[0], want, "NF4Linear")
+    with pytest.raises(ValueError):
+        fused_nf4_linear(x[..., :256], lin.packed, lin.absmax, lin.lut, 256)
+    with pytest.raises(ValueError):
+        fused_nf4_linear(x, lin.packed, lin.absmax, lin.lut, 128)
+    with pytest.raises(ValueError):
+        fused_nf4_linear(x.cpu(), lin.packed, lin.absmax, lin.lut, 256)
