@@ -214,9 +214,9 @@ def _time_kernels(dec, reps: int = 3) -> dict:
     ms = e0.elapsed_time(e1) / n
     qlen, written = int(c._qlen.item()), int(c._written.item())
     hkv = cfg.num_key_value_heads
-    # algorithmic bytes: K+V codes (2*128 B) + fp16 min/step per 64 tokens (4*128*2/64 B) per cached int8
-    # token and KV head, the fp16 ring slots in use, q in, out
-    ab = B * hkv * (qlen * 2176 + (written - qlen) * 2 * 128 * 2) + 2 * B * cfg.q_dim * 2
+    # algorithmic bytes: per cached int8 token and KV head 272 B = K+V codes (2*128 B) + the fp16
+    # min/step vectors amortised over 64 tokens (4*128*2/64 B); the fp16 ring slots in use; q in, out
+    ab = B * hkv * (qlen * 272 + (written - qlen) * 2 * 128 * 2) + 2 * B * cfg.q_dim * 2
     out["attention"] = {"launches": n, "ms": ms, "bytes": ab, "gbs": ab / (ms * 1e-3) / 1e9, "ctx": written}
     return out
 

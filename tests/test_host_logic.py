@@ -66,5 +66,5 @@ def test_bytes_accounting_matches_format():
     from nova_b200.kvquant import bytes_per_token
 
     c = bytes_per_token(num_slots=1, num_kv_heads=8, head_dim=128)
-    assert c["int8t64_kv"] == 8 * 2176         # 2048 B codes + 128 B scales per KV head
-    assert c["fp16_kv"] == 8 * 512
+    assert c["int8t64_kv"] == 2176             # per token per layer: 2048 B codes + 128 B scales (8 KV heads)
+    assert c["fp16_kv"] == 4096
