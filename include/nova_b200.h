@@ -151,7 +151,9 @@ enum nova_nf4_epilogue {
 };
 
 /* Workspace bytes for nova_nf4_gemv with N output rows on the current device
- * (stream-K partial slots + per-row-tile counters).  Zero it once. */
+ * (stream-K partial slots + per-row-tile counters).  Zero it once; a
+ * workspace sized for the largest N can be shared by every GEMV launched on
+ * one stream (each launch leaves its counters at zero). */
 NOVA_API int nova_nf4_workspace_bytes(int64_t n, int64_t* bytes);
 
 /*

@@ -25,7 +25,7 @@ int fail(int code, const char* fmt, ...) {
 }
 
 int check_launch(const char* what) {
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = cudaGetLastError();   // also consumes the error, so it is not reported twice
     if (e != cudaSuccess) return fail(NOVA_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
     return NOVA_OK;
 }

@@ -566,8 +566,10 @@ extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream)
     static bool attr_set = false;
     if (!attr_set) {
         if (cudaFuncSetAttribute(attn_decode_int8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess)
+            cudaSuccess) {
+            cudaGetLastError();
             return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
+        }
         attr_set = true;
     }
     dim3 grid(unsigned(s_total), unsigned(a->kv_heads), unsigned(a->batch));

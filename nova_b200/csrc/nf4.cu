@@ -409,13 +409,16 @@ static int sm_count() {
     return n;
 }
 
-static int64_t counters_bytes(int64_t n) { return ((n / 16) * 4 + 4 + 255) / 256 * 256; }
+// Workspace layout: [partial slots of every warp of the persistent grid |
+// per-row-tile arrival counters + the finalize counter].  The partial region
+// has the same size for every N, so one workspace sized for the largest N can
+// be shared by all GEMVs on a stream: each launch leaves its counters at zero.
+static int64_t partial_bytes() { return int64_t(sm_count()) * WARPS * 2 * 32 * 16; }
 
 extern "C" int nova_nf4_workspace_bytes(int64_t n, int64_t* bytes) {
     if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
     if (n <= 0 || n % 16) return fail(NOVA_ERR_INVALID, "N must be a positive multiple of 16");
-    const int64_t warps = int64_t(sm_count()) * WARPS;
-    *bytes = counters_bytes(n) + warps * 2 * 32 * 16;
+    *bytes = partial_bytes() + ((n / 16) * 4 + 4 + 255) / 256 * 256;
     return NOVA_OK;
 }
 
@@ -426,9 +429,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     if (n <= 0 || n % 16) return fail(NOVA_ERR_INVALID, "N must be a positive multiple of 16, got %lld", (long long)n);
     if (k <= 0 || k % 64) return fail(NOVA_ERR_INVALID, "K must be a positive multiple of 64, got %lld", (long long)k);
     if (n > (1 << 30) || k > (1 << 20)) return fail(NOVA_ERR_INVALID, "N/K too large");
-    const int64_t smem = int64_t(SMEM_BYTES) + m * k * 2;
-    if (smem > 227 * 1024)
-        return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld exceeds the shared-memory staging limit", (long long)(m * k));
+    const int64_t smem = int64_t(SMEM_BYTES) + m * k * 2;   // LUT + staged x
     if (!a->x || !a->packed || !a->absmax || !a->lut || !a->out || !a->workspace)
         return fail(NOVA_ERR_INVALID, "NULL pointer");
     const int epi = int(a->epilogue);
@@ -479,22 +480,35 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     const int64_t max_warps = int64_t(sm_count()) * WARPS;
     p.total_warps = int(std::min<int64_t>(max_warps, p.units));
     uint8_t* ws = (uint8_t*)a->workspace;
-    p.counters = (unsigned*)ws;
-    p.done = (unsigned*)ws + p.n_tiles;
-    p.partial = (float4*)(ws + counters_bytes(n));
+    p.partial = (float4*)ws;
+    p.counters = (unsigned*)(ws + partial_bytes());
+    p.done = p.counters + p.n_tiles;
     const unsigned grid = unsigned((p.total_warps + WARPS - 1) / WARPS);
 
     using Kern = void (*)(Params);
     static const Kern kernels[2][4] = {
         {nf4_gemv_kernel<__half, 0>, nf4_gemv_kernel<__half, 1>, nf4_gemv_kernel<__half, 2>, nf4_gemv_kernel<__half, 3>},
         {nf4_gemv_kernel<float, 0>, nf4_gemv_kernel<float, 1>, nf4_gemv_kernel<float, 2>, nf4_gemv_kernel<float, 3>}};
-    static bool attr_set[2][4] = {};
+    static int64_t smem_set[2][4] = {};
     const int ai = a->absmax_fp32 ? 1 : 0;
     Kern kern = kernels[ai][epi];
-    if (!attr_set[ai][epi]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
-            return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(smem) failed");
-        attr_set[ai][epi] = true;
+    if (smem > smem_set[ai][epi]) {
+        int dev = 0, optin = 0;
+        cudaFuncAttributes fa;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+            cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(NOVA_ERR_CUDA, "querying shared-memory limits failed");
+        }
+        if (smem + int64_t(fa.sharedSizeBytes) > optin)
+            return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld needs %lld B of shared memory, the device allows %d",
+                        (long long)(m * k), (long long)(smem + fa.sharedSizeBytes), optin);
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(dynamic smem %lld) failed", (long long)smem);
+        }
+        smem_set[ai][epi] = smem;
     }
     kern<<<grid, THREADS, size_t(smem), (cudaStream_t)stream>>>(p);
     return check_launch("nova_nf4_gemv");

@@ -222,7 +222,8 @@ class NovaDecoder:
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=f16, device=dev)
         self.argmax_slot = torch.zeros(B, dtype=torch.int64, device=dev)
         self.input_ids = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.gemv_ws = gemv_workspace(dev, cfg.vocab_size).clone()
+        n_max = max(cfg.vocab_size, 2 * cfg.intermediate_size, cfg.q_dim + 2 * cfg.kv_dim, cfg.hidden_size)
+        self.gemv_ws = gemv_workspace(dev, n_max).clone()   # shared by every GEMV of the step
         self.graph: torch.cuda.CUDAGraph | None = None
 
     def _pick_chunk(self) -> int:
@@ -271,7 +272,9 @@ class NovaDecoder:
             q = q * cos + _rotate_half(q) * sin
             k = (k * cos + _rotate_half(k) * sin).contiguous()
             v = v.contiguous()
-            o = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=d ** -0.5, enable_gqa=True)
+            gq = hq // hkv
+            o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
+                                               is_causal=True, scale=d ** -0.5)
             o = o.transpose(1, 2).reshape(B, T, cfg.q_dim)
             h = h + self._linear16(o, lw.o)
             x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)

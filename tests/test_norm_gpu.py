@@ -14,11 +14,12 @@ from oracle import norm as onorm
 pytestmark = pytest.mark.gpu
 
 
-def _close_fp16(got, want, tag, min_exact=0.99):
+def _close_fp16(got, want, tag, min_exact=0.99, max_ulp=1.0):
     """RMSNorm: a different fp32 summation order can move 1/sqrt(var) by an
     ulp, which flips an fp16 rounding now and then: <= 1 ULP everywhere and
-    bit-exact almost everywhere."""
-    st = assert_ulp_or_abs(got, want, 1.0, 0.0, tag)
+    bit-exact almost everywhere.  After RoPE (two more fp16-rounded products
+    and a sum, as in the reference) such a flip can reach 2 ULP."""
+    st = assert_ulp_or_abs(got, want, max_ulp, 0.0, tag)
     assert st["exact"] >= min_exact, f"{tag}: only {st['exact']:.4f} bit-exact"
 
 
@@ -100,10 +101,10 @@ def test_qk_norm_rope_append(cuda_lib):
         c, s = cos[pos].cpu().numpy(), sin[pos].cpu().numpy()
         q_want = onorm.apply_rope(onorm.rms_norm(x[:, :hq], qn.numpy(), 1e-6), c, s)
         k_want = onorm.apply_rope(onorm.rms_norm(x[:, hq:hq + hkv], kn.numpy(), 1e-6), c, s)
-        _close_fp16(q_out.cpu().numpy().reshape(b, hq, d), q_want, f"q pos={pos}", min_exact=0.98)
+        _close_fp16(q_out.cpu().numpy().reshape(b, hq, d), q_want, f"q pos={pos}", min_exact=0.98, max_ulp=2.0)
         ring_k[:, :, pos % 64] = cache.tail_k[0][:, :, pos % 64].cpu().numpy()
         ring_v[:, :, pos % 64] = x[:, hq + hkv:]
-        _close_fp16(ring_k[:, :, pos % 64], k_want, f"k pos={pos}", min_exact=0.98)
+        _close_fp16(ring_k[:, :, pos % 64], k_want, f"k pos={pos}", min_exact=0.98, max_ulp=2.0)
         np.testing.assert_array_equal(cache.tail_v[0][:, :, pos % 64].cpu().numpy(), x[:, hq + hkv:])
     assert int(cache._qlen.item()) == 128 and int(cache._written.item()) == 128 and int(cache._pg.item()) == 2
     # group 1 (positions 64..127) was requantized from the ring at position 127
