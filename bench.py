@@ -126,11 +126,11 @@ def run_reference(args, rank: int) -> None:
 # ---------------------------------------------------------------- B200 arm
 
 
-def _time_kernels(dec, reps: int = 3) -> dict:
-    """Per-kernel device time of one decode step's launch families, measured
-    eagerly with CUDA events on the launching stream; each family runs over
-    all 36 layers in turn (1.9 GB of distinct weights, so every launch reads
-    HBM, not L2)."""
+def _time_kernels(dec, reps: int = 10) -> dict:
+    """Per-kernel device time of one decode step's launch families: each
+    family is captured as a CUDA graph of one launch per layer (36 distinct
+    weight sets / KV caches, so every launch reads HBM, not L2) and replayed
+    ``reps`` times between CUDA events on the launching stream."""
     import torch
 
     from nova_b200 import _lib
@@ -143,54 +143,40 @@ def _time_kernels(dec, reps: int = 3) -> dict:
     stream = torch.cuda.current_stream()
 
     def bytes_of(w):
-        return w.packed.numel() + w.absmax.numel() * w.absmax.element_size()
+        return w.stream_bytes
 
     scratch = {"qkv": dec.qkv.clone(), "resid": dec.resid.clone(), "act": dec.act.clone(), "attn": dec.attn.clone()}
     fams = {
-        "qkv": (lambda lw: nf4_gemv(scratch["resid"], lw.qkv.packed, lw.qkv.absmax, lut, scratch["qkv"],
-                                    norm_weight=lw.input_ln, eps=eps, workspace=ws), lambda lw: bytes_of(lw.qkv)),
-        "o_proj": (lambda lw: nf4_gemv(scratch["attn"], lw.o.packed, lw.o.absmax, lut, scratch["resid"],
-                                       epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"], workspace=ws),
+        "qkv": (lambda lw: nf4_gemv(scratch["resid"], lw.qkv.units, None, lut, scratch["qkv"],
+                                    norm_weight=lw.input_ln, eps=eps, workspace=ws, n=lw.qkv.n),
+                lambda lw: bytes_of(lw.qkv)),
+        "o_proj": (lambda lw: nf4_gemv(scratch["attn"], lw.o.units, None, lut, scratch["resid"],
+                                       epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"], workspace=ws, n=lw.o.n),
                    lambda lw: bytes_of(lw.o)),
-        "gate_up": (lambda lw: nf4_gemv(scratch["resid"], lw.gate_up.packed, lw.gate_up.absmax, lut, scratch["act"],
-                                        epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln, eps=eps, workspace=ws),
+        "gate_up": (lambda lw: nf4_gemv(scratch["resid"], lw.gate_up.units, None, lut, scratch["act"],
+                                        epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln, eps=eps, workspace=ws,
+                                        n=lw.gate_up.n),
                     lambda lw: bytes_of(lw.gate_up)),
-        "down": (lambda lw: nf4_gemv(scratch["act"], lw.down.packed, lw.down.absmax, lut, scratch["resid"],
-                                     epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"], workspace=ws),
+        "down": (lambda lw: nf4_gemv(scratch["act"], lw.down.units, None, lut, scratch["resid"],
+                                     epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"], workspace=ws, n=lw.down.n),
                  lambda lw: bytes_of(lw.down)),
     }
+    from nova_b200.bench_kernels import _graph_time
+
+    layers = dec.w.layers
     for name, (fn, nbytes) in fams.items():
-        for lw in dec.w.layers[:2]:
-            fn(lw)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            for lw in dec.w.layers:
-                fn(lw)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        n = reps * len(dec.w.layers)
-        ms = e0.elapsed_time(e1) / n
-        out[name] = {"launches": n, "ms": ms, "bytes": nbytes(dec.w.layers[0]),
-                     "gbs": nbytes(dec.w.layers[0]) / (ms * 1e-3) / 1e9}
-    # lm_head (a single 207 MB matrix: reps launches)
+        us = _graph_time(lambda i: fn(layers[i]), len(layers), reps)
+        out[name] = {"launches": reps * len(layers), "ms": us * 1e-3, "bytes": nbytes(layers[0]),
+                     "gbs": nbytes(layers[0]) / (us * 1e-6) / 1e9}
+    # lm_head (a single 207 MB matrix, above L2)
     hw = dec.w.lm_head
     logits = dec.logits.clone()
     slot = torch.zeros_like(dec.argmax_slot)
-    fn = lambda: nf4_gemv(scratch["resid"], hw.packed, hw.absmax, lut, logits,  # noqa: E731
-                          epilogue=_lib.NF4_ARGMAX, norm_weight=dec.w.final_norm, eps=eps, argmax=slot, workspace=ws)
-    fn()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps * 4):
-        fn()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / (reps * 4)
+    us = _graph_time(lambda i: nf4_gemv(scratch["resid"], hw.units, None, lut, logits, epilogue=_lib.NF4_ARGMAX,
+                                        norm_weight=dec.w.final_norm, eps=eps, argmax=slot, workspace=ws, n=hw.n),
+                     4, reps)
     hb = bytes_of(hw)
-    out["lm_head"] = {"launches": reps * 4, "ms": ms, "bytes": hb, "gbs": hb / (ms * 1e-3) / 1e9}
+    out["lm_head"] = {"launches": reps * 4, "ms": us * 1e-3, "bytes": hb, "gbs": hb / (us * 1e-6) / 1e9}
     # int8-KV attention over every layer's cache at the current context
     c = dec.cache
     q3 = dec.q_rot.view(B, cfg.num_attention_heads, cfg.head_dim)
@@ -201,17 +187,9 @@ def _time_kernels(dec, reps: int = 3) -> dict:
                          (c.tail_k[li], c.tail_v[li]), a3, None, c._qlen, c._pg, c._written, c.first, c.workspace,
                          max_len=dec.max_len, n_splits=c.n_splits, chunk=c.chunk, window=c.window)
 
-    attn(0)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        for li in range(cfg.num_hidden_layers):
-            attn(li)
-    e1.record(stream)
-    torch.cuda.synchronize()
+    us = _graph_time(attn, cfg.num_hidden_layers, reps)
     n = reps * cfg.num_hidden_layers
-    ms = e0.elapsed_time(e1) / n
+    ms = us * 1e-3
     qlen, written = int(c._qlen.item()), int(c._written.item())
     hkv = cfg.num_key_value_heads
     # algorithmic bytes: per cached int8 token and KV head 272 B = K+V codes (2*128 B) + the fp16

@@ -38,6 +38,14 @@ enum nova_status {
 NOVA_API const char* nova_version(void);
 NOVA_API const char* nova_last_error(void);
 
+/* Process-wide launch flags.  Bit 0: launch every kernel with programmatic
+ * stream serialization (programmatic dependent launch), so a kernel's
+ * prologue -- weight prefetch, LUT build -- overlaps the previous kernel's
+ * tail; every kernel waits (griddepcontrol.wait) before touching data a
+ * previous kernel writes.  Default 0.  No counterpart in the reference. */
+NOVA_API int nova_set_launch_flags(int flags);
+NOVA_API int nova_get_launch_flags(void);
+
 /* ------------------------------------------------------------------ int8 KV */
 
 /*
@@ -201,9 +209,23 @@ typedef struct nova_nf4_args {
     int64_t workspace_bytes;
     int64_t m, n, k;
     int64_t epilogue;         /* enum nova_nf4_epilogue                        */
+    int64_t layout;           /* 0: reference packed/absmax; 1: native units   */
 } nova_nf4_args;
 
 NOVA_API int nova_nf4_gemv(const nova_nf4_args* args, void* stream);
+
+/*
+ * B200-native NF4 layout: the [N, K] matrix as 32-row x 64-k units, row-group
+ * major, each one contiguous 1088-byte record (1024 code bytes in MMA-lane
+ * order, then the 32 fp16 absmax values).  nova_nf4_native_bytes gives the
+ * size; nova_nf4_pack_native converts the reference layout (packed [N, K/2],
+ * absmax [K/64, N]) into it.  Needs N % 32 == 0.  With layout = 1,
+ * nova_nf4_gemv takes the unit stream in `packed` and ignores `absmax`.
+ * The reference has no counterpart (its GEMV reads the bitsandbytes layout).
+ */
+NOVA_API int nova_nf4_native_bytes(int64_t n, int64_t k, int64_t* bytes);
+NOVA_API int nova_nf4_pack_native(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n,
+                                  int64_t k, void* stream);
 
 /*
  * Blockwise NF4 quantizer: w fp16 [N, K] -> packed uint8 [N, K/2], absmax

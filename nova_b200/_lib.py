@@ -47,7 +47,7 @@ class NF4Args(ctypes.Structure):
         ("residual", _P), ("res_stride", _I), ("out", _P), ("out_stride", _I), ("argmax", _P),
         ("token_out", _P), ("pos", _P), ("embed", _P), ("embed_out", _P), ("embed_out_stride", _I),
         ("embed_dim", _I), ("workspace", _P), ("workspace_bytes", _I),
-        ("m", _I), ("n", _I), ("k", _I), ("epilogue", _I),
+        ("m", _I), ("n", _I), ("k", _I), ("epilogue", _I), ("layout", _I),
     ]
 
 
@@ -76,10 +76,14 @@ _SIGNATURES: dict[str, list] = {
     "nova_nf4_gemv": [ctypes.POINTER(NF4Args), _P],
     "nova_nf4_quantize": [_P, _I, _I, _P, _P, _P, _i, _P],
     "nova_nf4_dequant": [_P, _P, _i, _P, _P, _I, _I, _P],
+    "nova_nf4_native_bytes": [_I, _I, ctypes.POINTER(_I)],
+    "nova_nf4_pack_native": [_P, _P, _i, _P, _I, _I, _P],
+    "nova_set_launch_flags": [_i],
     "nova_rmsnorm": [_P, _I, _P, _I, _P, _I, _P, _P, _I, _I, _I, ctypes.c_double, _P],
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
 }
 _STRING_FNS = ("nova_version", "nova_last_error")
+_INT_FNS = ("nova_get_launch_flags",)
 
 _lib: ctypes.CDLL | None = None
 
@@ -100,12 +104,25 @@ def lib() -> ctypes.CDLL:
             fn = getattr(h, name)
             fn.argtypes = []
             fn.restype = ctypes.c_char_p
+        for name in _INT_FNS:
+            fn = getattr(h, name)
+            fn.argtypes = []
+            fn.restype = ctypes.c_int
         _lib = h
     return _lib
 
 
 def exported_names() -> list[str]:
-    return list(_SIGNATURES) + list(_STRING_FNS)
+    return list(_SIGNATURES) + list(_STRING_FNS) + list(_INT_FNS)
+
+
+def set_pdl(enabled: bool) -> None:
+    """Programmatic dependent launch for every kernel launched afterwards."""
+    call("nova_set_launch_flags", 1 if enabled else 0)
+
+
+def pdl_enabled() -> bool:
+    return bool(lib().nova_get_launch_flags() & 1)
 
 
 def version() -> str:

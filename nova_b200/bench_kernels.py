@@ -1,0 +1,194 @@
+"""Per-kernel microbenchmarks of the decode hot path (device time via CUDA
+events around CUDA-graph replays; each launch in the graph reads its own
+weight / KV set so that the working set exceeds the 126 MB L2).
+
+    python -m nova_b200.bench_kernels gemv --n 19456 --k 2560 --epilogue silu --norm
+    python -m nova_b200.bench_kernels attn --ctx 32768 --batch 1
+    python -m nova_b200.bench_kernels all          # the config-2 shapes + config-3 sweep
+
+Prints one JSON line per case with the launch time and achieved GB/s
+(algorithmic bytes: NF4 codes + fp16 absmax for the GEMV; 272 B per cached
+token and KV head + the fp16 ring + q/out for the attention).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib
+from .decoder import interleave_gate_up
+from .kernels import build_nf4_lut, gemv_workspace, nf4_gemv, pack_native
+from .kvattn import GROUP_T, launch_attention, new_workspace
+from .quant import nf4_codebook, quantize_nf4
+
+EPI = {"plain": _lib.NF4_PLAIN, "residual": _lib.NF4_RESIDUAL, "silu": _lib.NF4_SILU_MUL, "argmax": _lib.NF4_ARGMAX}
+
+
+def _graph_time(fn, sets: int, iters: int) -> float:
+    """Microseconds per launch of ``fn(i)`` for i over ``sets``, from graph replays."""
+    for i in range(sets):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(sets):
+                fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / (iters * sets)
+
+
+def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool = False, sets: int = 0,
+               iters: int = 20, seed: int = 0, layout: str = "native") -> dict:
+    dev = torch.device("cuda")
+    code = nf4_codebook()
+    lut = build_nf4_lut(code).to(dev)
+    nbytes = n * k // 2 + (k // 64) * n * 2
+    sets = sets or max(2, min(64, (512 << 20) // nbytes + 1))
+    g = torch.Generator(device=dev).manual_seed(seed)
+    weights = []
+    for _ in range(sets):
+        w = (torch.randn(n, k, generator=g, device=dev) * 0.02).half()
+        if epilogue == "silu":
+            gp, ga = quantize_nf4(w[: n // 2].contiguous(), code)
+            up, ua = quantize_nf4(w[n // 2:].contiguous(), code)
+            pa = interleave_gate_up(gp, ga, up, ua)
+        else:
+            pa = quantize_nf4(w, code)
+        weights.append((pack_native(*pa), None) if layout == "native" else pa)
+        del w
+    x = torch.randn(m, k, generator=g, device=dev).half()
+    nw = torch.ones(k, dtype=torch.float16, device=dev) if norm else None
+    nout = n // 2 if epilogue == "silu" else n
+    out = torch.zeros(m, nout, dtype=torch.float16, device=dev)
+    ws = gemv_workspace(dev, n).clone()
+    kw = {}
+    if epilogue == "residual":
+        kw["residual"] = out
+    if epilogue == "argmax":
+        kw["argmax"] = torch.zeros(m, dtype=torch.int64, device=dev)
+
+    def fn(i):
+        p, a = weights[i]
+        nf4_gemv(x, p, a, lut, out, epilogue=EPI[epilogue], norm_weight=nw, workspace=ws, n=n, **kw)
+
+    us = _graph_time(fn, sets, iters)
+    return {"kernel": "nf4_gemv", "layout": layout, "n": n, "k": k, "m": m, "epilogue": epilogue, "norm": norm,
+            "sets": sets, "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+
+
+def bench_attn(ctx: int, batch: int = 1, q_heads: int = 32, kv_heads: int = 8, window: int = 0, chunk: int = 0,
+               sets: int = 0, iters: int = 20, seed: int = 0) -> dict:
+    dev = torch.device("cuda")
+    d = 128
+    max_len = ctx + GROUP_T
+    qlen = ctx // GROUP_T * GROUP_T
+    written = ctx
+    per_set = batch * kv_heads * max_len * 2 * d
+    sets = sets or max(2, min(32, (768 << 20) // per_set + 1))
+    if not chunk:
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        per_head = max(1, (2 * sms) // (batch * kv_heads))
+        chunk = max(GROUP_T * 4, -(-(-(-max_len // per_head)) // GROUP_T) * GROUP_T)
+    n_splits = -(-max_len // chunk)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    ng = -(-max_len // GROUP_T)
+    caches = []
+    for _ in range(sets):
+        kq = torch.randint(0, 256, (batch, kv_heads, max_len, d), generator=g, device=dev, dtype=torch.uint8)
+        vq = torch.randint(0, 256, (batch, kv_heads, max_len, d), generator=g, device=dev, dtype=torch.uint8)
+        sc = [(torch.rand(batch, kv_heads, ng, d, generator=g, device=dev) * 0.01).half() for _ in range(4)]
+        tail = [(torch.randn(batch, kv_heads, GROUP_T, d, generator=g, device=dev)).half() for _ in range(2)]
+        caches.append((kq, sc[0], sc[1], vq, sc[2], sc[3], tail))
+    q = torch.randn(batch, q_heads, d, generator=g, device=dev).half()
+    out = torch.zeros(batch, q_heads, d, dtype=torch.float16, device=dev)
+    qlen_t = torch.tensor([qlen], device=dev)
+    pg_t = torch.tensor([qlen // GROUP_T], device=dev)
+    written_t = torch.tensor([written], device=dev)
+    ws = new_workspace(batch, q_heads, kv_heads, n_splits, True, dev)
+
+    def fn(i):
+        kq, kmn, kst, vq, vmn, vst, tail = caches[i]
+        launch_attention(q, (kq, kmn, kst, vq, vmn, vst), tuple(tail), out, None, qlen_t, pg_t, written_t, None, ws,
+                         max_len=max_len, n_splits=n_splits, chunk=chunk, window=window)
+
+    us = _graph_time(fn, sets, iters)
+    valid = min(qlen, window) if window else qlen
+    ring = min(written - qlen, window) if window else written - qlen
+    nbytes = batch * kv_heads * (valid * 272 + ring * 2 * d * 2) + 2 * batch * q_heads * d * 2
+    return {"kernel": "attn_decode_int8", "ctx": ctx, "batch": batch, "window": window, "chunk": chunk,
+            "n_splits": n_splits, "sets": sets, "us": round(us, 3), "bytes": nbytes,
+            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+
+
+CONFIG2 = [("q_proj", 4096, 2560), ("k_proj", 1024, 2560), ("v_proj", 1024, 2560), ("o_proj", 2560, 4096),
+           ("gate_proj", 9728, 2560), ("up_proj", 9728, 2560), ("down_proj", 2560, 9728),
+           ("lm_head", 151936, 2560)]
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    a = sub.add_parser("gemv")
+    a.add_argument("--n", type=int, required=True)
+    a.add_argument("--k", type=int, required=True)
+    a.add_argument("--m", type=int, default=1)
+    a.add_argument("--epilogue", choices=list(EPI), default="plain")
+    a.add_argument("--norm", action="store_true")
+    a.add_argument("--sets", type=int, default=0)
+    a.add_argument("--iters", type=int, default=20)
+    a.add_argument("--layout", choices=["native", "ref"], default="native")
+    a.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
+    b = sub.add_parser("attn")
+    b.add_argument("--ctx", type=int, required=True)
+    b.add_argument("--batch", type=int, default=1)
+    b.add_argument("--window", type=int, default=0)
+    b.add_argument("--chunk", type=int, default=0)
+    b.add_argument("--sets", type=int, default=0)
+    b.add_argument("--iters", type=int, default=20)
+    sub.add_parser("all")
+    args = ap.parse_args()
+    _lib.lib()
+    if args.cmd == "gemv":
+        _lib.set_pdl(args.pdl)
+        print(json.dumps(bench_gemv(args.n, args.k, args.m, args.epilogue, args.norm, args.sets, args.iters,
+                                    layout=args.layout)))
+    elif args.cmd == "attn":
+        print(json.dumps(bench_attn(args.ctx, args.batch, window=args.window, chunk=args.chunk, sets=args.sets,
+                                    iters=args.iters)))
+    else:
+        for pdl in (False, True):
+            _lib.set_pdl(pdl)
+            for name, n, k in CONFIG2:
+                r = bench_gemv(n, k)
+                r["name"], r["pdl"] = name, pdl
+                print(json.dumps(r), flush=True)
+        _lib.set_pdl(True)
+        for name, n, k, epi, nrm in (("qkv_fused", 6144, 2560, "plain", True), ("gate_up_fused", 19456, 2560, "silu",
+                                                                                 True)):
+            r = bench_gemv(n, k, epilogue=epi, norm=nrm)
+            r["name"] = name
+            print(json.dumps(r), flush=True)
+        for ctx in (4096, 8192, 32768, 65536, 131072):
+            for batch in (1, 4, 16):
+                if batch * ctx > 16 * 65536:
+                    continue
+                print(json.dumps(bench_attn(ctx, batch)), flush=True)
+        print(json.dumps(bench_attn(131072, 4, window=4096)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

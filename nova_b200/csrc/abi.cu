@@ -8,6 +8,9 @@
 namespace nova {
 
 static thread_local char g_last_error[512] = "";
+static int g_launch_flags = 0;
+
+int launch_flags() { return __atomic_load_n(&g_launch_flags, __ATOMIC_RELAXED); }
 
 void set_error(const char* fmt, ...) {
     va_list ap;
@@ -66,3 +69,11 @@ int make_tmap_u8_rows128(CUtensorMap* tm, const void* base, uint64_t rows, uint3
 extern "C" const char* nova_version(void) { return "nova_b200 0.1 (sm_100a, abi 1)"; }
 
 extern "C" const char* nova_last_error(void) { return nova::g_last_error; }
+
+extern "C" int nova_set_launch_flags(int flags) {
+    if (flags & ~1) return nova::fail(NOVA_ERR_INVALID, "unknown launch flags 0x%x", flags);
+    __atomic_store_n(&nova::g_launch_flags, flags, __ATOMIC_RELAXED);
+    return NOVA_OK;
+}
+
+extern "C" int nova_get_launch_flags(void) { return nova::launch_flags(); }

@@ -302,6 +302,12 @@ __global__ void __launch_bounds__(THREADS, 3)
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int64_t bh = int64_t(b) * p.kv_heads + h;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
+    }
+    pdl_trigger();
+    pdl_wait();   // q, the cache and the lengths come from the previous kernels
 
     const int64_t qlen = *p.qlen, pgv = *p.pg;
     const int64_t written = p.written ? *p.written : qlen;
@@ -573,6 +579,11 @@ extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream)
         attr_set = true;
     }
     dim3 grid(unsigned(s_total), unsigned(a->kv_heads), unsigned(a->batch));
-    attn_decode_int8_kernel<<<grid, THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(p, tmK, tmV);
-    return check_launch("nova_attn_decode_int8");
+    const cudaError_t err =
+        launch(attn_decode_int8_kernel, grid, dim3(THREADS), size_t(SMEM_BYTES), (cudaStream_t)stream, p, tmK, tmV);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_attn_decode_int8: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }

@@ -10,6 +10,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <utility>
 
 #include "../../include/nova_b200.h"
 
@@ -24,7 +25,42 @@ int check_launch(const char* what);
 // box and the 128-byte swizzle (used for int8 K/V code tiles).
 int make_tmap_u8_rows128(CUtensorMap* tm, const void* base, uint64_t rows, uint32_t box_rows);
 
+// Launch flags (nova_set_launch_flags): bit 0 = programmatic dependent launch.
+int launch_flags();
+
+// Launch `kernel` on `stream`, with programmatic stream serialization when
+// enabled so that the kernel's prologue (everything before pdl_wait()) can
+// overlap the tail of the previous kernel on the stream.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    cfg.numAttrs = 0;
+    if (launch_flags() & 1) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 1;
+    }
+    cfg.attrs = attr;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ---------------------------------------------------------------- device side
+
+// Programmatic dependent launch: wait until the previous kernel on the stream
+// has completed and its memory is visible (a no-op without a programmatic
+// dependency); allow the next kernel to be scheduled.  Nothing before
+// pdl_wait() may write global memory or read anything a previous kernel writes.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -35,6 +35,8 @@ __global__ void kv_quant_int8_kernel(const __half* __restrict__ x, int64_t xs, u
                                      int dim, int group) {
     const int g = blockIdx.x;
     const int64_t row = blockIdx.y;
+    pdl_trigger();
+    pdl_wait();
     const int t0 = g * group;
     const int cnt = min(group, n - t0);
     for (int d = threadIdx.x; d < dim; d += blockDim.x) {
@@ -47,6 +49,8 @@ __global__ void kv_dequant_int8_kernel(const uint8_t* __restrict__ q, int64_t qs
                                        const __half* __restrict__ steps, int64_t ss, __half* __restrict__ x,
                                        int64_t xs, int n, int dim, int group) {
     const int64_t row = blockIdx.y;
+    pdl_trigger();
+    pdl_wait();
     const int64_t total = int64_t(n) * dim;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
         const int t = int(i / dim), d = int(i % dim);
@@ -66,6 +70,8 @@ __global__ void kv_append_int8_kernel(const __half* __restrict__ k_new, const __
                                       int64_t max_len, int dim, int group) {
     const int bh = blockIdx.x;
     const int b = bh / kv_heads, h = bh % kv_heads;
+    pdl_trigger();
+    pdl_wait();
     const int64_t pos = *pos_p;
     if (bh == 0 && threadIdx.x == 0) {
         const int64_t w = pos + 1;
@@ -115,10 +121,14 @@ extern "C" int nova_kv_quant_int8(const void* x, int64_t x_row_stride, void* q, 
     const int64_t ng = (n + group - 1) / group;
     if (ng > 0x7fffffff) return fail(NOVA_ERR_INVALID, "too many groups");
     dim3 grid{unsigned(ng), unsigned(rows), 1u};
-    kv_quant_int8_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
-        (const __half*)x, x_row_stride, (uint8_t*)q, q_row_stride, (__half*)mins, (__half*)steps, s_row_stride,
-        int(n), int(dim), int(group));
-    return check_launch("nova_kv_quant_int8");
+    const cudaError_t err = launch(kv_quant_int8_kernel, grid, dim3(128), 0, (cudaStream_t)stream, (const __half*)x,
+                                   x_row_stride, (uint8_t*)q, q_row_stride, (__half*)mins, (__half*)steps,
+                                   s_row_stride, int(n), int(dim), int(group));
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_kv_quant_int8: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }
 
 extern "C" int nova_kv_dequant_int8(const void* q, int64_t q_row_stride, const void* mins, const void* steps,
@@ -129,10 +139,15 @@ extern "C" int nova_kv_dequant_int8(const void* q, int64_t q_row_stride, const v
     const int64_t total = n * dim;
     unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, 4096));
     dim3 grid{blocks, unsigned(rows), 1u};
-    kv_dequant_int8_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-        (const uint8_t*)q, q_row_stride, (const __half*)mins, (const __half*)steps, s_row_stride, (__half*)x,
-        x_row_stride, int(n), int(dim), int(group));
-    return check_launch("nova_kv_dequant_int8");
+    const cudaError_t err =
+        launch(kv_dequant_int8_kernel, grid, dim3(256), 0, (cudaStream_t)stream, (const uint8_t*)q, q_row_stride,
+               (const __half*)mins, (const __half*)steps, s_row_stride, (__half*)x, x_row_stride, int(n), int(dim),
+               int(group));
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_kv_dequant_int8: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }
 
 extern "C" int nova_kv_append_int8(const void* k_new, const void* v_new, int64_t new_b_stride, int64_t new_h_stride,
@@ -145,9 +160,14 @@ extern "C" int nova_kv_append_int8(const void* k_new, const void* v_new, int64_t
     if (dim <= 0 || dim > 1024) return fail(NOVA_ERR_INVALID, "dim must be in [1, 1024]");
     if (group <= 0 || group > 1024 || max_len <= 0) return fail(NOVA_ERR_INVALID, "group/max_len out of range");
     if (!pos || !written || !qlen || !pg) return fail(NOVA_ERR_INVALID, "device scalars must not be NULL");
-    kv_append_int8_kernel<<<unsigned(batch * kv_heads), 128, 0, (cudaStream_t)stream>>>(
+    const cudaError_t err = launch(
+        kv_append_int8_kernel, dim3(unsigned(batch * kv_heads)), dim3(128), 0, (cudaStream_t)stream,
         (const __half*)k_new, (const __half*)v_new, new_b_stride, new_h_stride, (__half*)tail_k, (__half*)tail_v,
         (uint8_t*)kq, (uint8_t*)vq, (__half*)kmn, (__half*)kst, (__half*)vmn, (__half*)vst, pos, written, qlen, pg,
         int(kv_heads), max_len, int(dim), int(group));
-    return check_launch("nova_kv_append_int8");
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_kv_append_int8: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }

@@ -1,41 +1,49 @@
-// NF4 weight GEMV / skinny GEMM (M <= 8) for sm_100a, plus the NF4 quantizer
-// and dequantizer.
+// NF4 weight GEMV / skinny GEMM (M <= 8) for sm_100a, plus the NF4 quantizer,
+// dequantizer and the packer into the B200-native weight layout.
 //
-// Weight format (reference src/nova/quant.py:39-69): packed uint8 [N, K/2],
+// Reference weight format (src/nova/quant.py:39-69): packed uint8 [N, K/2],
 // K-contiguous, byte j of a row = element 2j in the high nibble, 2j+1 in the
-// low nibble; absmax [K/64, N] (fp32 in the reference, fp16 in the native
-// format); 16-entry NF4 codebook given as the reference's 256-entry fp16x2
-// LUT (src/nova/kernels.py:170-182: low half = code[b>>4], high = code[b&15]).
+// low nibble; absmax [K/64, N] (fp32 in the reference, fp16 here); the
+// codebook as the reference's 256-entry fp16x2 LUT (src/nova/kernels.py:
+// 170-182: low half = code[b>>4], high half = code[b&15]).
 //
-// y[m, n] = sum_blocks absmax[blk, n] * sum_{k in blk} x[m, k] * code16[idx(n, k)]
+//   y[m, n] = sum_blocks absmax[blk, n] * sum_{k in blk} x[m, k] * code16[idx(n, k)]
 //
-// Work split ("stream-K"): the (16-row tile, 64-k block) units of the whole
-// matrix are dealt out in equal contiguous ranges to every warp of a
-// persistent grid (one 16-warp CTA per SM), so all SMs stream the same number
-// of weight bytes whatever N and K are.  A warp that covers a whole row tile
-// finishes it; partial tiles leave their MMA accumulator fragment in a
-// workspace slot and the last of the tile's warps to arrive (arrival counter)
-// adds the slots in warp order -- deterministic -- and runs the epilogue.
+// Native layout ("units"): the matrix is cut into 32-row x 64-k units, stored
+// row-group major, block minor, each as one contiguous 1088-byte record.
+// Bytes [16L, 16L+16) hold, for MMA lane L = 4g + t, bytes [8t, 8t+8) of the
+// 32-byte blocks (the k values 16t..16t+15) of rows g and g+8 of the group;
+// bytes [512 + 16L, +16) the same for rows g+16 and g+24; bytes 1024..1087 the
+// 32 fp16 absmax values ordered so lane group g finds rows g, g+8, g+16, g+24
+// at [4g, 4g+4).  Every 16-byte lane read of a warp covers 512 contiguous
+// bytes (one wavefront per quarter warp), and a warp's range of consecutive
+// units is one contiguous stretch of memory that a single bulk copy fetches.
 //
-// Per unit and lane: two 8-byte streaming loads of packed weights; each byte
-// becomes one f16x2 A-fragment register via one byte-permute (forms the LUT
-// address from the byte and the lane id) and one bank-conflict-free
-// shared-memory load (the LUT is replicated once per lane).  The products
-// code16 * x16 are exact in fp32 and accumulated in fp32 by mma.sync
+// Work split ("stream-K"): the units are dealt out in equal contiguous ranges
+// to every warp of a persistent grid, so all SMs stream the same number of
+// bytes whatever N and K are.  A warp that covers a whole row group finishes
+// it; a partial group leaves its accumulator fragments in a workspace slot and
+// the last of the group's warps to arrive (arrival counter) adds the slots in
+// warp order -- deterministic -- and runs the epilogue.
+//
+// Decode: each byte becomes one f16x2 A-fragment register through one byte
+// permute (forms a LUT address from the byte and the lane id) and one
+// bank-conflict-free shared-memory load (the LUT is replicated per lane).  The
+// products code16 * x16 are exact in fp32 and accumulated in fp32 by mma.sync
 // m16n8k16 (x in the B operand, columns = the M <= 8 rows); each 64-element
-// block gets a fresh accumulator that is scaled by its absmax, as in the
-// reference kernel (src/nova/kernels.py:213-232).
+// block gets a fresh accumulator scaled by its absmax, as in the reference
+// kernel (src/nova/kernels.py:213-232).
 #include "common.cuh"
 
 namespace nova {
 namespace nf4 {
 
-constexpr int WARPS = 16;
-constexpr int THREADS = WARPS * 32;
 constexpr int LUT_WORDS = 256 * 64;      // entry v at word v*64 + lane (256-byte rows)
-constexpr int SMEM_BYTES = LUT_WORDS * 4;
-constexpr int BATCH = 8;                 // units whose loads are issued together
+constexpr int LUT_BYTES = LUT_WORDS * 4;
 constexpr int MAX_M = 8;
+constexpr int UNIT_ROWS = 32;
+constexpr int UNIT_CODE_BYTES = 1024;
+constexpr int UNIT_BYTES = 1088;
 
 enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3 };
 
@@ -44,8 +52,8 @@ struct Params {
     int64_t x_stride;
     const __half* norm_w;     // fp16 [K] RMSNorm weight or nullptr
     float eps;
-    const uint8_t* packed;
-    const void* absmax;
+    const uint8_t* packed;    // reference layout [N, K/2] or native units
+    const void* absmax;       // reference layout only
     const uint32_t* lut;
     const __half* bias;
     const __half* residual;
@@ -59,7 +67,7 @@ struct Params {
     __half* embed_out;        // finalize: next-step hidden [M, embed_dim]
     int64_t embed_out_stride;
     int embed_dim;
-    float4* partial;          // [total_warps][2][32] float4
+    float4* partial;          // [total_warps][2][32][2] float4
     unsigned* counters;       // [n_tiles]
     unsigned* done;           // finalize arrival counter
     int M, N, K, KB, n_tiles, total_warps;
@@ -88,6 +96,8 @@ __device__ __forceinline__ unsigned long long argmax_key(__half v, int idx) {
     return (static_cast<unsigned long long>(o) << 32) | static_cast<unsigned long long>(0xffffffffu - unsigned(idx));
 }
 
+// Epilogue of one 16-row tile: lane (g, t) holds rows 16*tile+g (c[0], c[1])
+// and 16*tile+g+8 (c[2], c[3]) for batch rows m = 2t, 2t+1.
 template <int EPI>
 __device__ __forceinline__ void epilogue(const Params& p, int tile, const float (&c)[4], int g, int t) {
     if (EPI == EPI_SILU_MUL) {
@@ -167,15 +177,23 @@ __device__ __forceinline__ void finalize_step(const Params& p, int lane) {
     }
 }
 
-template <typename AbsT, int EPI>
-__global__ void __launch_bounds__(THREADS, 1) nf4_gemv_kernel(const __grid_constant__ Params p) {
-    extern __shared__ __align__(16) uint32_t lut_s[];
-    __half* xs = reinterpret_cast<__half*>(lut_s + LUT_WORDS);   // [M][K]
-    __shared__ float red[WARPS][MAX_M];
-    __shared__ float rstd[MAX_M];
-    for (int i = threadIdx.x; i < 256 * 32; i += THREADS) lut_s[(i >> 5) * 64 + (i & 31)] = __ldg(p.lut + (i >> 5));
+// Per-lane replicated LUT: entry v for lane l at word v*64 + l (l < 32).
+template <int THREADS>
+__device__ __forceinline__ void build_lut(uint32_t* lut_s, const uint32_t* lut) {
+    for (int v = threadIdx.x; v < 256 * 4; v += THREADS) {
+        const int e = v >> 2, q = v & 3;
+        const uint32_t w = __ldg(lut + e);
+        uint4* dst = reinterpret_cast<uint4*>(lut_s + e * 64 + 8 * q);
+        dst[0] = make_uint4(w, w, w, w);
+        dst[1] = make_uint4(w, w, w, w);
+    }
+}
 
-    // ---- stage x (optionally RMS-normalised, HF order) in shared memory
+// Stage x in shared memory, optionally RMS-normalised in HF order.
+template <int THREADS>
+__device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
+    __shared__ float red[THREADS / 32][MAX_M];
+    __shared__ float rstd[MAX_M];
     const int kv8 = p.K / 8;
     if (p.norm_w) {
         float ss[MAX_M];
@@ -204,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1) nf4_gemv_kernel(const __grid_const
         __syncthreads();
         if (threadIdx.x < MAX_M) {
             float v = 0.f;
-            for (int w = 0; w < WARPS; ++w) v += red[w][threadIdx.x];
+            for (int w = 0; w < THREADS / 32; ++w) v += red[w][threadIdx.x];
             rstd[threadIdx.x] = rsqrt_ieee(__fdiv_rn(v, float(p.K)) + p.eps);
         }
         __syncthreads();
@@ -221,8 +239,7 @@ __global__ void __launch_bounds__(THREADS, 1) nf4_gemv_kernel(const __grid_const
                 for (int q = 0; q < 4; ++q) {
                     const float2 f = __half22float2(h[q]);
                     const float2 wf = __half22float2(wh[q]);
-                    const __half2 n16 = __floats2half2_rn(f.x * r, f.y * r);
-                    const float2 nf = __half22float2(n16);
+                    const float2 nf = __half22float2(__floats2half2_rn(f.x * r, f.y * r));
                     oh[q] = __floats2half2_rn(wf.x * nf.x, wf.y * nf.y);
                 }
                 *reinterpret_cast<uint4*>(xs + m * p.K + 8 * i) = o;
@@ -232,13 +249,258 @@ __global__ void __launch_bounds__(THREADS, 1) nf4_gemv_kernel(const __grid_const
         for (int i = threadIdx.x; i < p.M * kv8; i += THREADS) {
             const int m = i / kv8, j = i % kv8;
             *reinterpret_cast<uint4*>(xs + m * p.K + 8 * j) =
-                __ldg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride) + j);
+                *(reinterpret_cast<const uint4*>(p.x + m * p.x_stride) + j);
         }
     }
+}
+
+// Partial-tile protocol: store this warp's fragments, count arrivals, and let
+// the last contributor add all fragments in warp order and run the epilogue.
+template <int EPI, int NT>
+__device__ __forceinline__ void flush_partial(const Params& p, int rg, const float (&acc)[NT][4], int w,
+                                              int first_rg, int lane, int g, int t) {
+    const int W = p.total_warps;
+    const int slot = 2 * w + (rg == first_rg ? 0 : 1);
+    float4* dst = p.partial + (int64_t(slot) * 32 + lane) * 2;
+#pragma unroll
+    for (int i = 0; i < NT; ++i) dst[i] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    fence_acq_rel_gpu();
+    __syncwarp();
+    const int64_t u0 = int64_t(rg) * p.KB;
+    const int w_first = owner_of(u0, p.units, W);
+    const int w_last = owner_of(u0 + p.KB - 1, p.units, W);
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(p.counters + rg, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != unsigned(w_last - w_first)) return;
+    fence_acq_rel_gpu();
+    float c[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.f;
+    // contributors are added in warp order; the loads of four of them are in flight at once
+    for (int w0 = w_first; w0 <= w_last; w0 += 4) {
+        float4 v[4][NT];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int ww = w0 + q;
+            if (ww > w_last) break;
+            const int frg = int(unit_begin(p.units, ww, W) / p.KB);
+            const int sl = 2 * ww + (rg == frg ? 0 : 1);
+            const float4* src = p.partial + (int64_t(sl) * 32 + lane) * 2;
+#pragma unroll
+            for (int i = 0; i < NT; ++i) v[q][i] = __ldcg(src + i);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (w0 + q > w_last) break;
+#pragma unroll
+            for (int i = 0; i < NT; ++i) {
+                c[i][0] += v[q][i].x; c[i][1] += v[q][i].y; c[i][2] += v[q][i].z; c[i][3] += v[q][i].w;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NT; ++i) epilogue<EPI>(p, rg * NT + i, c[i], g, t);
+    if (lane == 0) p.counters[rg] = 0u;
+}
+
+template <int EPI>
+__device__ __forceinline__ void finish_launch(const Params& p, int lane) {
+    if (EPI != EPI_ARGMAX || !p.token_out) return;
+    fence_acq_rel_gpu();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(p.done, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev == unsigned(p.total_warps - 1)) {
+        fence_acq_rel_gpu();
+        finalize_step(p, lane);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Native-layout kernel: one 16-warp CTA per SM.  Each warp owns a contiguous
+// range of units, which is one contiguous stretch of the unit stream, and
+// streams it through a private two-stage shared-memory ring: one bulk copy
+// (cp.async.bulk, mbarrier-tracked) per stage of up to `stage_units` units.
+// The first two stages are requested before the prologue (they are weights,
+// independent of every previous kernel), so the LUT build and x staging
+// overlap the first DRAM round trip.
+
+constexpr int NAT_WARPS = 16;
+constexpr int NAT_THREADS = NAT_WARPS * 32;
+constexpr int NAT_STAGES = 2;
+constexpr int NAT_MIN_UNITS = 8;   // units per warp at least (few contributors per row group)
+
+__device__ __forceinline__ void mma_unit_smem(const uint8_t* unit, const uint32_t (&xb)[8], uint32_t lut_base,
+                                              uint32_t laneword, int lane, int g, float (&acc)[2][4]) {
+    const uint4 c0 = lds128(unit + 16 * lane);          // rows g, g+8
+    const uint4 c1 = lds128(unit + 512 + 16 * lane);    // rows g+16, g+24
+    uint2 am;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(am.x), "=r"(am.y)
+                 : "r"(smem_u32(unit + UNIT_CODE_BYTES + 8 * g)));
+    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    float blk[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int wi = s >> 1;
+        const uint32_t sel0 = 0x5504u | (uint32_t((s & 1) * 2) << 4);
+        const uint32_t sel1 = sel0 + 0x10u;
+#pragma unroll
+        for (int tile = 0; tile < 2; ++tile) {
+            const uint32_t r0w = w[4 * tile + wi], r1w = w[4 * tile + 2 + wi];
+            const uint32_t a0 = lds32(lut_base + __byte_perm(r0w, laneword, sel0));
+            const uint32_t a2 = lds32(lut_base + __byte_perm(r0w, laneword, sel1));
+            const uint32_t a1 = lds32(lut_base + __byte_perm(r1w, laneword, sel0));
+            const uint32_t a3 = lds32(lut_base + __byte_perm(r1w, laneword, sel1));
+            mma_16816(blk[tile], a0, a1, a2, a3, xb[2 * s], xb[2 * s + 1]);
+        }
+    }
+    const float2 a01 = __half22float2(*reinterpret_cast<const __half2*>(&am.x));
+    const float2 a23 = __half22float2(*reinterpret_cast<const __half2*>(&am.y));
+    acc[0][0] += a01.x * blk[0][0];
+    acc[0][1] += a01.x * blk[0][1];
+    acc[0][2] += a01.y * blk[0][2];
+    acc[0][3] += a01.y * blk[0][3];
+    acc[1][0] += a23.x * blk[1][0];
+    acc[1][1] += a23.x * blk[1][1];
+    acc[1][2] += a23.y * blk[1][2];
+    acc[1][3] += a23.y * blk[1][3];
+}
+
+// XG: x is read through L1 from global memory instead of being staged (large
+// M*K without the norm prologue, where the staged copy would crowd out the
+// weight rings).  Warp w of the launch is warp w / gridDim.x of CTA
+// w % gridDim.x, so small launches spread their warps over all SMs.
+template <int EPI, bool XG>
+__global__ void __launch_bounds__(NAT_THREADS, 1)
+    nf4_gemv_native_kernel(const __grid_constant__ Params p, int stage_units, int* err) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[NAT_WARPS][NAT_STAGES];
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
+    __half* xs = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
+    const int xs_bytes = XG ? 0 : (p.M * p.K * 2 + 127) / 128 * 128;
+    const int stage_bytes = stage_units * UNIT_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint8_t* ring = smem_raw + LUT_BYTES + xs_bytes + size_t(warp) * NAT_STAGES * stage_bytes;
+    const int w = warp * int(gridDim.x) + int(blockIdx.x);
+    const int W = p.total_warps;
+    const bool active = w < W;
+    const int64_t u_begin = active ? unit_begin(p.units, w, W) : 0;
+    const int64_t u_end = active ? unit_begin(p.units, w + 1, W) : 0;
+    const int n_chunks = int((u_end - u_begin + stage_units - 1) / stage_units);
+
+    auto issue = [&](int chunk) {   // lane 0 only
+        const int64_t u0 = u_begin + int64_t(chunk) * stage_units;
+        const int cnt = int(min(int64_t(stage_units), u_end - u0));
+        uint64_t* bar = &bars[warp][chunk % NAT_STAGES];
+        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(ring + (chunk % NAT_STAGES) * stage_bytes, p.packed + u0 * UNIT_BYTES, bytes, bar);
+    };
+
+    // Prologue, overlapping the previous kernel: weights only.
+    if (lane == 0 && active) {
+#pragma unroll
+        for (int s = 0; s < NAT_STAGES; ++s) mbar_init(&bars[warp][s], 1);
+        fence_mbar_init();
+        for (int c = 0; c < NAT_STAGES && c < n_chunks; ++c) issue(c);
+    }
+    build_lut<NAT_THREADS>(lut_s, p.lut);
+    pdl_trigger();
+    pdl_wait();
+    if (!XG) stage_x<NAT_THREADS>(p, xs);
+    __syncthreads();
+    if (!active) return;
+
+    const uint32_t lut_base = smem_u32(lut_s);
+    const uint32_t laneword = uint32_t(lane) << 2;
+    const int first_rg = int(u_begin / p.KB);
+    const bool xlane = g < p.M;
+    const __half* xrow = XG ? p.x + (xlane ? g : 0) * p.x_stride + 16 * t : xs + (xlane ? g : 0) * p.K + 16 * t;
+    uint32_t xb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    int cur_rg = first_rg;
+    int seg_b0 = int(u_begin % p.KB);
+
+    for (int c = 0; c < n_chunks; ++c) {
+        const int stage = c % NAT_STAGES;
+        if (!mbar_wait(&bars[warp][stage], uint32_t((c / NAT_STAGES) & 1), err, 2)) {
+            // give the other copy in flight a bounded chance to land, then leave
+            if (c + 1 < n_chunks) mbar_wait(&bars[warp][(c + 1) % NAT_STAGES], uint32_t(((c + 1) / NAT_STAGES) & 1),
+                                            err, 2);
+            return;
+        }
+        const int64_t u0 = u_begin + int64_t(c) * stage_units;
+        const int cnt = int(min(int64_t(stage_units), u_end - u0));
+        const uint8_t* sbuf = ring + stage * stage_bytes;
+        for (int j = 0; j < cnt; ++j) {
+            const int64_t u = u0 + j;
+            const int rg = int(u / p.KB), b = int(u % p.KB);
+            if (rg != cur_rg) {   // the previous group ended inside this range at block KB-1
+                if (seg_b0 == 0) {
+                    epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
+                    epilogue<EPI>(p, 2 * cur_rg + 1, acc[1], g, t);
+                } else {
+                    flush_partial<EPI, 2>(p, cur_rg, acc, w, first_rg, lane, g, t);
+                }
+#pragma unroll
+                for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+                cur_rg = rg;
+                seg_b0 = 0;
+            }
+            if (xlane) {
+                uint4 x0, x1;
+                if (XG) {
+                    x0 = __ldg(reinterpret_cast<const uint4*>(xrow + 64 * b));
+                    x1 = __ldg(reinterpret_cast<const uint4*>(xrow + 64 * b + 8));
+                } else {
+                    x0 = lds128(xrow + 64 * b);
+                    x1 = lds128(xrow + 64 * b + 8);
+                }
+                xb[0] = x0.x; xb[1] = x0.y; xb[2] = x0.z; xb[3] = x0.w;
+                xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
+            }
+            mma_unit_smem(sbuf + j * UNIT_BYTES, xb, lut_base, laneword, lane, g, acc);
+        }
+        __syncwarp();
+        if (lane == 0 && c + NAT_STAGES < n_chunks) {
+            fence_proxy_async();
+            issue(c + NAT_STAGES);
+        }
+    }
+    if (u_end > u_begin) {
+        const int last_b = int((u_end - 1) % p.KB);
+        if (seg_b0 == 0 && last_b == p.KB - 1) {
+            epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
+            epilogue<EPI>(p, 2 * cur_rg + 1, acc[1], g, t);
+        } else {
+            flush_partial<EPI, 2>(p, cur_rg, acc, w, first_rg, lane, g, t);
+        }
+    }
+    finish_launch<EPI>(p, lane);
+}
+
+// ---------------------------------------------------------------------------
+// Reference-layout kernel (packed [N, K/2], absmax [K/64, N]) for callers that
+// hand over the reference's tensors per call; 16-row x 64-k units.
+
+constexpr int REF_WARPS = 16;
+constexpr int REF_THREADS = REF_WARPS * 32;
+constexpr int REF_BATCH = 8;
+
+template <typename AbsT, int EPI>
+__global__ void __launch_bounds__(REF_THREADS, 1) nf4_gemv_ref_kernel(const __grid_constant__ Params p) {
+    extern __shared__ __align__(16) uint32_t lut_s[];
+    __half* xs = reinterpret_cast<__half*>(lut_s + LUT_WORDS);
+    build_lut<REF_THREADS>(lut_s, p.lut);
+    pdl_trigger();
+    pdl_wait();
+    stage_x<REF_THREADS>(p, xs);
     __syncthreads();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int w = blockIdx.x * WARPS + warp;
+    const int w = blockIdx.x * REF_WARPS + warp;
     if (w >= p.total_warps) return;
     const int W = p.total_warps;
     const int64_t u_begin = unit_begin(p.units, w, W), u_end = unit_begin(p.units, w + 1, W);
@@ -255,14 +517,14 @@ __global__ void __launch_bounds__(THREADS, 1) nf4_gemv_kernel(const __grid_const
         const int r0 = tile * 16;
         const uint8_t* wrow0 = p.packed + int64_t(r0 + g) * row_bytes + 8 * t;
         const uint8_t* wrow1 = wrow0 + 8 * row_bytes;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
 
-        for (int i = 0; i < span; i += BATCH) {
-            const int nb = min(BATCH, span - i);
-            uint2 wa[BATCH], wb[BATCH];
-            float am0[BATCH], am1[BATCH];
+        for (int i = 0; i < span; i += REF_BATCH) {
+            const int nb = min(REF_BATCH, span - i);
+            uint2 wa[REF_BATCH], wb[REF_BATCH];
+            float am0[REF_BATCH], am1[REF_BATCH];
 #pragma unroll
-            for (int j = 0; j < BATCH; ++j) {
+            for (int j = 0; j < REF_BATCH; ++j) {
                 if (j < nb) {
                     const int b = b0 + i + j;
                     wa[j] = ldg_stream64(wrow0 + 32 * b);
@@ -272,87 +534,47 @@ __global__ void __launch_bounds__(THREADS, 1) nf4_gemv_kernel(const __grid_const
                 }
             }
 #pragma unroll
-            for (int j = 0; j < BATCH; ++j) {
+            for (int j = 0; j < REF_BATCH; ++j) {
                 if (j < nb) {
                     const int b = b0 + i + j;
-                    // B fragments: x[m = g][64b + 16t .. +15] (zero columns for g >= M)
-                    uint32_t xb[8];
-                    {
-                        const uint4 x0 = lds128(xrow + 64 * b), x1 = lds128(xrow + 64 * b + 8);
-                        const bool on = g < p.M;
-                        xb[0] = on ? x0.x : 0u; xb[1] = on ? x0.y : 0u; xb[2] = on ? x0.z : 0u; xb[3] = on ? x0.w : 0u;
-                        xb[4] = on ? x1.x : 0u; xb[5] = on ? x1.y : 0u; xb[6] = on ? x1.z : 0u; xb[7] = on ? x1.w : 0u;
-                    }
+                    const uint4 x0 = lds128(xrow + 64 * b), x1 = lds128(xrow + 64 * b + 8);
+                    const uint32_t xb[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                     const uint32_t ww[4] = {wa[j].x, wa[j].y, wb[j].x, wb[j].y};
                     float blk[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
-                        // bytes 2s, 2s+1 of this lane's 8 bytes of each row
                         const uint32_t r0w = ww[s >> 1], r1w = ww[2 + (s >> 1)];
-                        const int bl = (s & 1) * 2;
-                        const uint32_t a0 = lds32(lut_base + __byte_perm(r0w, laneword, 0x5504 | (bl << 4)));
-                        const uint32_t a2 = lds32(lut_base + __byte_perm(r0w, laneword, 0x5504 | ((bl + 1) << 4)));
-                        const uint32_t a1 = lds32(lut_base + __byte_perm(r1w, laneword, 0x5504 | (bl << 4)));
-                        const uint32_t a3 = lds32(lut_base + __byte_perm(r1w, laneword, 0x5504 | ((bl + 1) << 4)));
+                        const uint32_t sel0 = 0x5504u | (uint32_t((s & 1) * 2) << 4);
+                        const uint32_t a0 = lds32(lut_base + __byte_perm(r0w, laneword, sel0));
+                        const uint32_t a2 = lds32(lut_base + __byte_perm(r0w, laneword, sel0 + 0x10u));
+                        const uint32_t a1 = lds32(lut_base + __byte_perm(r1w, laneword, sel0));
+                        const uint32_t a3 = lds32(lut_base + __byte_perm(r1w, laneword, sel0 + 0x10u));
                         mma_16816(blk, a0, a1, a2, a3, xb[2 * s], xb[2 * s + 1]);
                     }
-                    acc[0] += am0[j] * blk[0];
-                    acc[1] += am0[j] * blk[1];
-                    acc[2] += am1[j] * blk[2];
-                    acc[3] += am1[j] * blk[3];
+                    acc[0][0] += am0[j] * blk[0];
+                    acc[0][1] += am0[j] * blk[1];
+                    acc[0][2] += am1[j] * blk[2];
+                    acc[0][3] += am1[j] * blk[3];
                 }
             }
         }
-
-        if (span == p.KB) {
-            epilogue<EPI>(p, tile, acc, g, t);
-        } else {
-            const int slot = 2 * w + (tile == first_tile ? 0 : 1);
-            p.partial[int64_t(slot) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            __threadfence();
-            __syncwarp();
-            const int64_t tu0 = int64_t(tile) * p.KB;
-            const int w_first = owner_of(tu0, p.units, W);
-            const int w_last = owner_of(tu0 + p.KB - 1, p.units, W);
-            unsigned prev = 0;
-            if (lane == 0) prev = atomicAdd(p.counters + tile, 1u);
-            prev = __shfl_sync(0xffffffffu, prev, 0);
-            if (prev == unsigned(w_last - w_first)) {
-                __threadfence();
-                float c[4] = {0.f, 0.f, 0.f, 0.f};
-                for (int ww2 = w_first; ww2 <= w_last; ++ww2) {
-                    const int ft = int(unit_begin(p.units, ww2, W) / p.KB);
-                    const int sl = 2 * ww2 + (tile == ft ? 0 : 1);
-                    const float4 v = __ldcg(p.partial + int64_t(sl) * 32 + lane);
-                    c[0] += v.x; c[1] += v.y; c[2] += v.z; c[3] += v.w;
-                }
-                epilogue<EPI>(p, tile, c, g, t);
-                if (lane == 0) p.counters[tile] = 0u;
-            }
-        }
+        if (span == p.KB)
+            epilogue<EPI>(p, tile, acc[0], g, t);
+        else
+            flush_partial<EPI, 1>(p, tile, acc, w, first_tile, lane, g, t);
         u += span;
     }
-
-    if (EPI == EPI_ARGMAX && p.token_out) {
-        __threadfence();
-        __syncwarp();
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(p.done, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == unsigned(W - 1)) {
-            __threadfence();
-            finalize_step(p, lane);
-        }
-    }
+    finish_launch<EPI>(p, lane);
 }
 
-// ---------------------------------------------------------------- quantizer
+// ---------------------------------------------------------------- quantizer / packer
 
-// One block of 64 weights per warp-half... kept simple: one thread per block.
 __global__ void nf4_quantize_kernel(const __half* __restrict__ w, int64_t n_blocks, int kb, int N,
                                     const float* __restrict__ mid, uint8_t* __restrict__ packed, void* absmax,
                                     int absmax_fp32) {
     __shared__ float smid[15];
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x < 15) smid[threadIdx.x] = mid[threadIdx.x];
     __syncthreads();
     for (int64_t blk = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; blk < n_blocks;
@@ -385,6 +607,8 @@ __global__ void nf4_quantize_kernel(const __half* __restrict__ w, int64_t n_bloc
 template <typename AbsT>
 __global__ void nf4_dequant_kernel(const uint8_t* __restrict__ packed, const void* absmax,
                                    const uint32_t* __restrict__ lut, __half* __restrict__ out, int64_t N, int K) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t total = N * (K / 2);
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
         const int64_t n = i / (K / 2);
@@ -396,6 +620,35 @@ __global__ void nf4_dequant_kernel(const uint8_t* __restrict__ packed, const voi
     }
 }
 
+// One thread per (unit, lane): the lane's 2 x 16 code bytes and, for t == 0,
+// the four absmax values of its lane group.
+template <typename AbsT>
+__global__ void nf4_pack_native_kernel(const uint8_t* __restrict__ packed, const void* absmax,
+                                       uint8_t* __restrict__ out, int64_t n_units, int KB, int N) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t row_bytes = int64_t(KB) * 32;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n_units * 32;
+         i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t u = i >> 5;
+        const int lane = int(i & 31), g = lane >> 2, t = lane & 3;
+        const int64_t rg = u / KB;
+        const int b = int(u % KB);
+        uint8_t* rec = out + u * UNIT_BYTES;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t row = rg * UNIT_ROWS + g + 8 * r;
+            const uint2 v = *reinterpret_cast<const uint2*>(packed + row * row_bytes + 32 * b + 8 * t);
+            // rows g, g+8 -> first half, rows g+16, g+24 -> second half; 16 bytes per lane in each
+            *reinterpret_cast<uint2*>(rec + (r >> 1) * 512 + 16 * lane + 8 * (r & 1)) = v;
+            if (t == 0) {
+                const float a = absmax_at<AbsT>(absmax, int64_t(b) * N + row);
+                reinterpret_cast<__half*>(out + u * UNIT_BYTES + UNIT_CODE_BYTES)[4 * g + r] = __float2half_rn(a);
+            }
+        }
+    }
+}
+
 }  // namespace nf4
 }  // namespace nova
 
@@ -404,33 +657,103 @@ using namespace nova::nf4;
 
 static int sm_count() {
     int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 148;
+    }
     return n;
 }
 
 // Workspace layout: [partial slots of every warp of the persistent grid |
 // per-row-tile arrival counters + the finalize counter].  The partial region
-// has the same size for every N, so one workspace sized for the largest N can
-// be shared by all GEMVs on a stream: each launch leaves its counters at zero.
-static int64_t partial_bytes() { return int64_t(sm_count()) * WARPS * 2 * 32 * 16; }
+// has the same size for every N (it is sized for the largest grid either
+// kernel uses), so one workspace sized for the largest N serves every GEMV
+// on a stream: each launch leaves its counters at zero.
+static int64_t max_warps() { return int64_t(sm_count()) * 16; }
+static int64_t partial_bytes() { return max_warps() * 2 * 32 * 32; }
 
 extern "C" int nova_nf4_workspace_bytes(int64_t n, int64_t* bytes) {
     if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
     if (n <= 0 || n % 16) return fail(NOVA_ERR_INVALID, "N must be a positive multiple of 16");
-    *bytes = partial_bytes() + ((n / 16) * 4 + 4 + 255) / 256 * 256;
+    *bytes = partial_bytes() + ((n / 16) * 4 + 8 + 255) / 256 * 256;   // counters, done, error word
     return NOVA_OK;
+}
+
+extern "C" int nova_nf4_native_bytes(int64_t n, int64_t k, int64_t* bytes) {
+    if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
+    if (n <= 0 || n % UNIT_ROWS || k <= 0 || k % 64)
+        return fail(NOVA_ERR_INVALID, "native layout needs N %% 32 == 0 and K %% 64 == 0");
+    *bytes = (n / UNIT_ROWS) * (k / 64) * UNIT_BYTES;
+    return NOVA_OK;
+}
+
+extern "C" int nova_nf4_pack_native(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n,
+                                    int64_t k, void* stream) {
+    if (n <= 0 || n % UNIT_ROWS || k <= 0 || k % 64)
+        return fail(NOVA_ERR_INVALID, "native layout needs N %% 32 == 0 and K %% 64 == 0");
+    if (!packed || !absmax || !out) return fail(NOVA_ERR_INVALID, "NULL pointer");
+    auto mis = [](const void* ptr, int al) { return reinterpret_cast<uintptr_t>(ptr) % al != 0; };
+    if (mis(packed, 8) || mis(out, 16)) return fail(NOVA_ERR_ALIGN, "packed must be 8-byte, out 16-byte aligned");
+    const int64_t n_units = (n / UNIT_ROWS) * (k / 64);
+    const unsigned grid = unsigned(std::min<int64_t>((n_units * 32 + 255) / 256, 65535 * 8));
+    if (absmax_fp32)
+        nf4_pack_native_kernel<float><<<grid, 256, 0, (cudaStream_t)stream>>>(
+            (const uint8_t*)packed, absmax, (uint8_t*)out, n_units, int(k / 64), int(n));
+    else
+        nf4_pack_native_kernel<__half><<<grid, 256, 0, (cudaStream_t)stream>>>(
+            (const uint8_t*)packed, absmax, (uint8_t*)out, n_units, int(k / 64), int(n));
+    return check_launch("nova_nf4_pack_native");
+}
+
+template <typename Kern>
+static int prepare_smem(Kern kern, int64_t smem, int64_t* set_to) {
+    if (smem <= *set_to) return NOVA_OK;
+    int dev = 0, optin = 0;
+    cudaFuncAttributes fa;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "querying shared-memory limits failed");
+    }
+    if (smem + int64_t(fa.sharedSizeBytes) > optin)
+        return fail(NOVA_ERR_UNSUPPORTED, "M*K needs %lld B of shared memory, the device allows %d",
+                    (long long)(smem + fa.sharedSizeBytes), optin);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(dynamic smem %lld) failed", (long long)smem);
+    }
+    *set_to = smem;
+    return NOVA_OK;
+}
+
+template <typename Kern>
+static int resident_ctas(Kern kern, int threads, int64_t smem) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, size_t(smem)) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        return 1;
+    }
+    return n;
 }
 
 extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
     const int64_t m = a->m, n = a->n, k = a->k;
+    const bool native = a->layout == 1;
+    if (a->layout != 0 && a->layout != 1) return fail(NOVA_ERR_INVALID, "layout must be 0 or 1");
     if (m < 1 || m > MAX_M) return fail(NOVA_ERR_UNSUPPORTED, "M must be in [1, %d], got %lld", MAX_M, (long long)m);
-    if (n <= 0 || n % 16) return fail(NOVA_ERR_INVALID, "N must be a positive multiple of 16, got %lld", (long long)n);
+    if (n <= 0 || n % (native ? UNIT_ROWS : 16))
+        return fail(NOVA_ERR_INVALID, "N must be a positive multiple of %d, got %lld", native ? UNIT_ROWS : 16,
+                    (long long)n);
     if (k <= 0 || k % 64) return fail(NOVA_ERR_INVALID, "K must be a positive multiple of 64, got %lld", (long long)k);
     if (n > (1 << 30) || k > (1 << 20)) return fail(NOVA_ERR_INVALID, "N/K too large");
-    const int64_t smem = int64_t(SMEM_BYTES) + m * k * 2;   // LUT + staged x
-    if (!a->x || !a->packed || !a->absmax || !a->lut || !a->out || !a->workspace)
+    const int64_t smem = int64_t(LUT_BYTES) + m * k * 2;   // LUT + staged x
+    if (!a->x || !a->packed || (!native && !a->absmax) || !a->lut || !a->out || !a->workspace)
         return fail(NOVA_ERR_INVALID, "NULL pointer");
     const int epi = int(a->epilogue);
     if (epi < EPI_PLAIN || epi > EPI_ARGMAX) return fail(NOVA_ERR_INVALID, "bad epilogue %d", epi);
@@ -441,11 +764,11 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     if (a->embed && (!a->token_out || !a->embed_out || a->embed_dim <= 0 || a->embed_dim % 8))
         return fail(NOVA_ERR_INVALID, "embedding gather needs token_out, embed_out and embed_dim % 8 == 0");
     auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
-    if (mis(a->x, 16) || (a->x_stride % 8) || mis(a->norm_weight, 16) || mis(a->packed, 8) || mis(a->absmax, 4) ||
-        mis(a->workspace, 256) || mis(a->argmax, 8) || mis(a->embed, 16) || mis(a->embed_out, 16) ||
-        (a->embed_out_stride % 8))
-        return fail(NOVA_ERR_ALIGN, "x/norm_weight/embed must be 16-byte aligned (row strides multiples of 8), packed "
-                                    "8, workspace 256");
+    if (mis(a->x, 16) || (a->x_stride % 8) || mis(a->norm_weight, 16) || mis(a->packed, native ? 16 : 8) ||
+        mis(a->absmax, 4) || mis(a->workspace, 256) || mis(a->argmax, 8) || mis(a->embed, 16) ||
+        mis(a->embed_out, 16) || (a->embed_out_stride % 8))
+        return fail(NOVA_ERR_ALIGN, "x/norm_weight/embed must be 16-byte aligned (row strides multiples of 8), "
+                                    "packed 8 (native 16), workspace 256");
     int64_t need = 0;
     nova_nf4_workspace_bytes(n, &need);
     if (a->workspace_bytes < need)
@@ -476,42 +799,80 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     p.K = int(k);
     p.KB = int(k / 64);
     p.n_tiles = int(n / 16);
-    p.units = int64_t(p.n_tiles) * p.KB;
-    const int64_t max_warps = int64_t(sm_count()) * WARPS;
-    p.total_warps = int(std::min<int64_t>(max_warps, p.units));
     uint8_t* ws = (uint8_t*)a->workspace;
     p.partial = (float4*)ws;
     p.counters = (unsigned*)(ws + partial_bytes());
     p.done = p.counters + p.n_tiles;
-    const unsigned grid = unsigned((p.total_warps + WARPS - 1) / WARPS);
 
     using Kern = void (*)(Params);
-    static const Kern kernels[2][4] = {
-        {nf4_gemv_kernel<__half, 0>, nf4_gemv_kernel<__half, 1>, nf4_gemv_kernel<__half, 2>, nf4_gemv_kernel<__half, 3>},
-        {nf4_gemv_kernel<float, 0>, nf4_gemv_kernel<float, 1>, nf4_gemv_kernel<float, 2>, nf4_gemv_kernel<float, 3>}};
-    static int64_t smem_set[2][4] = {};
-    const int ai = a->absmax_fp32 ? 1 : 0;
-    Kern kern = kernels[ai][epi];
-    if (smem > smem_set[ai][epi]) {
-        int dev = 0, optin = 0;
-        cudaFuncAttributes fa;
-        if (cudaGetDevice(&dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-            cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(NOVA_ERR_CUDA, "querying shared-memory limits failed");
+    cudaError_t err;
+    if (native) {
+        using NKern = void (*)(Params, int, int*);
+        static const NKern kernels[2][4] = {
+            {nf4_gemv_native_kernel<0, false>, nf4_gemv_native_kernel<1, false>, nf4_gemv_native_kernel<2, false>,
+             nf4_gemv_native_kernel<3, false>},
+            {nf4_gemv_native_kernel<0, true>, nf4_gemv_native_kernel<1, true>, nf4_gemv_native_kernel<2, true>,
+             nf4_gemv_native_kernel<3, true>}};
+        static int64_t smem_set[2][4] = {};
+        static int optin = 0;
+        if (!optin) {
+            int dev = 0;
+            if (cudaGetDevice(&dev) != cudaSuccess ||
+                cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+                cudaGetLastError();
+                optin = 0;
+                return fail(NOVA_ERR_CUDA, "querying the shared-memory limit failed");
+            }
         }
-        if (smem + int64_t(fa.sharedSizeBytes) > optin)
-            return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld needs %lld B of shared memory, the device allows %d",
-                        (long long)(m * k), (long long)(smem + fa.sharedSizeBytes), optin);
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(dynamic smem %lld) failed", (long long)smem);
+        // LUT + staged x, then the per-warp rings with as many units per stage
+        // as fit (at most 4); x stays in global memory when staging it would
+        // leave less than 2 units per stage and there is no norm prologue.
+        const int64_t ring_unit = int64_t(NAT_WARPS) * NAT_STAGES * UNIT_BYTES;
+        const int64_t slack = 1024;   // static shared memory
+        auto units_for = [&](int64_t xs_bytes) {
+            return std::min<int64_t>(4, (optin - int64_t(LUT_BYTES) - xs_bytes - slack) / ring_unit);
+        };
+        int64_t xs_bytes = (m * k * 2 + 127) / 128 * 128;
+        int64_t stage_units = units_for(xs_bytes);
+        int xg = 0;
+        if (stage_units < 2 && !a->norm_weight) {
+            xg = 1;
+            xs_bytes = 0;
+            stage_units = units_for(0);
         }
-        smem_set[ai][epi] = smem;
+        if (stage_units < 1)
+            return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld with the norm prologue leaves no shared memory for the "
+                                              "weight ring", (long long)(m * k));
+        NKern kern = kernels[xg][epi];
+        const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + stage_units * ring_unit;
+        if (int rc = prepare_smem(kern, nsmem, &smem_set[xg][epi])) return rc;
+        p.units = int64_t(n / UNIT_ROWS) * p.KB;
+        const int64_t want = (p.units + NAT_MIN_UNITS - 1) / NAT_MIN_UNITS;
+        p.total_warps = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sm_count()) * NAT_WARPS, want)));
+        const unsigned grid = unsigned(std::min<int64_t>(sm_count(), p.total_warps));
+        int* errp = reinterpret_cast<int*>(p.done + 1);
+        err = launch(kern, dim3(grid), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p, int(stage_units),
+                     errp);
+    } else {
+        static const Kern kernels[2][4] = {
+            {nf4_gemv_ref_kernel<__half, 0>, nf4_gemv_ref_kernel<__half, 1>, nf4_gemv_ref_kernel<__half, 2>,
+             nf4_gemv_ref_kernel<__half, 3>},
+            {nf4_gemv_ref_kernel<float, 0>, nf4_gemv_ref_kernel<float, 1>, nf4_gemv_ref_kernel<float, 2>,
+             nf4_gemv_ref_kernel<float, 3>}};
+        static int64_t smem_set[2][4] = {};
+        const int ai = a->absmax_fp32 ? 1 : 0;
+        Kern kern = kernels[ai][epi];
+        if (int rc = prepare_smem(kern, smem, &smem_set[ai][epi])) return rc;
+        p.units = int64_t(p.n_tiles) * p.KB;
+        p.total_warps = int(std::min<int64_t>(int64_t(sm_count()) * REF_WARPS, p.units));
+        const unsigned grid = unsigned((p.total_warps + REF_WARPS - 1) / REF_WARPS);
+        err = launch(kern, dim3(grid), dim3(REF_THREADS), size_t(smem), (cudaStream_t)stream, p);
     }
-    kern<<<grid, THREADS, size_t(smem), (cudaStream_t)stream>>>(p);
-    return check_launch("nova_nf4_gemv");
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_nf4_gemv: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }
 
 extern "C" int nova_nf4_quantize(const void* w, int64_t n, int64_t k, const void* midpoints, void* packed,

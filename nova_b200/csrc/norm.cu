@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __half* __res
                                                              const __half* __restrict__ w, __half* __restrict__ y,
                                                              int64_t ys, int n, float eps) {
     __shared__ float red[RN_THREADS / 32];
+    pdl_trigger();
+    pdl_wait();
     const int64_t row = blockIdx.x;
     const __half* xr = x + row * xs;
     float ss = 0.f;
@@ -115,6 +117,8 @@ __global__ void __launch_bounds__(D) qk_norm_rope_append_kernel(const __grid_con
     const int m = blockIdx.y;
     const int head = blockIdx.x;
     const int d = threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
     const int64_t pos = *p.pos;
     if (m == 0 && head == 0 && d == 0) {
         const int64_t w = pos + 1;
@@ -178,10 +182,15 @@ extern "C" int nova_rmsnorm(const void* x, int64_t x_stride, const void* residua
     if (residual_out && !residual_in) return fail(NOVA_ERR_INVALID, "residual_out needs residual_in");
     if (rows == 0) return NOVA_OK;
     if (rows > 0x7fffffff) return fail(NOVA_ERR_INVALID, "too many rows");
-    norm::rmsnorm_kernel<<<unsigned(rows), norm::RN_THREADS, 0, (cudaStream_t)stream>>>(
-        (const __half*)x, x_stride, (const __half*)residual_in, rin_stride, (__half*)residual_out, rout_stride,
-        (const __half*)weight, (__half*)y, y_stride, int(n), float(eps));
-    return check_launch("nova_rmsnorm");
+    const cudaError_t err =
+        launch(norm::rmsnorm_kernel, dim3(unsigned(rows)), dim3(norm::RN_THREADS), 0, (cudaStream_t)stream,
+               (const __half*)x, x_stride, (const __half*)residual_in, rin_stride, (__half*)residual_out, rout_stride,
+               (const __half*)weight, (__half*)y, y_stride, int(n), float(eps));
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_rmsnorm: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }
 
 extern "C" int nova_qk_norm_rope_append(const nova_qk_args* a, void* stream) {
@@ -222,6 +231,10 @@ extern "C" int nova_qk_norm_rope_append(const nova_qk_args* a, void* stream) {
     p.max_len = a->max_len;
     p.eps = float(a->eps);
     dim3 grid{unsigned(a->q_heads + a->kv_heads), unsigned(a->batch), 1u};
-    norm::qk_norm_rope_append_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(p);
-    return check_launch("nova_qk_norm_rope_append");
+    const cudaError_t err = launch(norm::qk_norm_rope_append_kernel, grid, dim3(128), 0, (cudaStream_t)stream, p);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_qk_norm_rope_append: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }

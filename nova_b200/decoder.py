@@ -38,7 +38,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .kernels import build_nf4_lut, fused_rms_norm, gemv_workspace, nf4_gemv
+from .kernels import build_nf4_lut, fused_rms_norm, gemv_workspace, nf4_gemv, pack_native
 from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention
 from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
 
@@ -91,12 +91,26 @@ def deinterleave_gate_up(packed, absmax):
 
 @dataclass
 class NF4Weight:
-    packed: torch.Tensor   # uint8 [N, K/2]
-    absmax: torch.Tensor   # fp16 [K/64, N]
+    packed: torch.Tensor               # uint8 [N, K/2] (reference layout; prefill, tests)
+    absmax: torch.Tensor               # fp16 [K/64, N]
+    units: torch.Tensor | None = None  # B200-native unit stream (decode GEMVs)
+
+    def __post_init__(self) -> None:
+        if self.units is None:
+            self.units = pack_native(self.packed, self.absmax)
+
+    @property
+    def n(self) -> int:
+        return int(self.packed.shape[0])
 
     @property
     def shape(self):
         return self.packed.shape[0], self.packed.shape[1] * 2
+
+    @property
+    def stream_bytes(self) -> int:
+        """Bytes one GEMV streams: NF4 codes + fp16 absmax."""
+        return int(self.units.numel())
 
 
 @dataclass
@@ -162,12 +176,8 @@ class DecoderWeights:
 
     def nbytes_per_token(self) -> int:
         """Weight bytes one decode step streams (NF4 codes + fp16 absmax)."""
-        tot = 0
-        for lw in self.layers:
-            for w in (lw.qkv, lw.o, lw.gate_up, lw.down):
-                tot += w.packed.numel() + w.absmax.numel() * w.absmax.element_size()
-        tot += self.lm_head.packed.numel() + self.lm_head.absmax.numel() * 2
-        return tot
+        tot = sum(w.stream_bytes for lw in self.layers for w in (lw.qkv, lw.o, lw.gate_up, lw.down))
+        return tot + self.lm_head.stream_bytes
 
 
 def rope_tables(max_pos: int, head_dim: int = 128, theta: float = 5_000_000.0, device="cuda"):
@@ -197,7 +207,7 @@ class NovaDecoder:
     """
 
     def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
-                 device="cuda") -> None:
+                 device="cuda", pdl: bool = True) -> None:
         cfg = weights.cfg
         if batch < 1 or batch > 8:
             raise ValueError("the GEMV decode path handles batch 1..8")
@@ -225,6 +235,7 @@ class NovaDecoder:
         n_max = max(cfg.vocab_size, 2 * cfg.intermediate_size, cfg.q_dim + 2 * cfg.kv_dim, cfg.hidden_size)
         self.gemv_ws = gemv_workspace(dev, n_max).clone()   # shared by every GEMV of the step
         self.graph: torch.cuda.CUDAGraph | None = None
+        self.pdl = bool(pdl)
 
     def _pick_chunk(self) -> int:
         """Split size for the attention: about two CTAs per SM at full capacity."""
@@ -317,8 +328,8 @@ class NovaDecoder:
         a3 = self.attn.view(B, cfg.num_attention_heads, cfg.head_dim)
         ws = self.gemv_ws
         for li, lw in enumerate(self.w.layers):
-            nf4_gemv(self.resid, lw.qkv.packed, lw.qkv.absmax, lut, self.qkv, norm_weight=lw.input_ln, eps=eps,
-                     workspace=ws)
+            nf4_gemv(self.resid, lw.qkv.units, None, lut, self.qkv, norm_weight=lw.input_ln, eps=eps,
+                     workspace=ws, n=lw.qkv.n)
             qa = _lib.QKArgs()
             qa.qkv, qa.qkv_stride = self.qkv.data_ptr(), self.qkv.stride(0)
             qa.q_norm_weight, qa.k_norm_weight, qa.eps = lw.q_norm.data_ptr(), lw.k_norm.data_ptr(), eps
@@ -337,15 +348,16 @@ class NovaDecoder:
                                   cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
                              n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window)
-            nf4_gemv(self.attn, lw.o.packed, lw.o.absmax, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
-                     residual=self.resid, workspace=ws)
-            nf4_gemv(self.resid, lw.gate_up.packed, lw.gate_up.absmax, lut, self.act, epilogue=_lib.NF4_SILU_MUL,
-                     norm_weight=lw.post_ln, eps=eps, workspace=ws)
-            nf4_gemv(self.act, lw.down.packed, lw.down.absmax, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
-                     residual=self.resid, workspace=ws)
-        nf4_gemv(self.resid, self.w.lm_head.packed, self.w.lm_head.absmax, lut, self.logits,
-                 epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm, eps=eps, argmax=self.argmax_slot,
-                 token_out=self.input_ids, pos=cache.pos, embed=self.w.embed, embed_out=self.resid, workspace=ws)
+            nf4_gemv(self.attn, lw.o.units, None, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
+                     residual=self.resid, workspace=ws, n=lw.o.n)
+            nf4_gemv(self.resid, lw.gate_up.units, None, lut, self.act, epilogue=_lib.NF4_SILU_MUL,
+                     norm_weight=lw.post_ln, eps=eps, workspace=ws, n=lw.gate_up.n)
+            nf4_gemv(self.act, lw.down.units, None, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
+                     residual=self.resid, workspace=ws, n=lw.down.n)
+        hw = self.w.lm_head
+        nf4_gemv(self.resid, hw.units, None, lut, self.logits, epilogue=_lib.NF4_ARGMAX,
+                 norm_weight=self.w.final_norm, eps=eps, argmax=self.argmax_slot, token_out=self.input_ids,
+                 pos=cache.pos, embed=self.w.embed, embed_out=self.resid, workspace=ws, n=hw.n)
 
     def launches_per_step(self) -> int:
         return 6 * self.cfg.num_hidden_layers + 1
@@ -359,12 +371,19 @@ class NovaDecoder:
     @torch.inference_mode()
     def capture(self) -> None:
         """Capture one decode step.  Capture does not execute anything, so the
-        decode state is untouched."""
+        decode state is untouched.  With ``pdl`` the kernels are captured with
+        programmatic dependencies: each one's weight prefetch and LUT build
+        overlap the previous kernel."""
         self.graph = None
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self._step_body()
+        prev = _lib.pdl_enabled()
+        _lib.set_pdl(self.pdl)
+        try:
+            with torch.cuda.graph(g):
+                self._step_body()
+        finally:
+            _lib.set_pdl(prev)
         self.graph = g
 
     def step(self) -> torch.Tensor:

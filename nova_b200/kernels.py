@@ -100,20 +100,43 @@ def gemv_workspace(device: torch.device, n: int) -> torch.Tensor:
     return ws
 
 
-def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, lut: torch.Tensor, out: torch.Tensor, *,
+def pack_native(packed: torch.Tensor, absmax: torch.Tensor) -> torch.Tensor:
+    """Reference NF4 layout (packed ``[N, K/2]``, absmax ``[K/64, N]``) -> the
+    B200-native unit stream (uint8, 1088 bytes per 32-row x 64-k unit)."""
+    _lib.require_cuda(packed, absmax, names=("packed", "absmax"))
+    n, k2 = packed.shape
+    nbytes = _lib.ctypes.c_int64(0)
+    _lib.call("nova_nf4_native_bytes", n, 2 * k2, _lib.ctypes.byref(nbytes))
+    out = torch.empty(int(nbytes.value), dtype=torch.uint8, device=packed.device)
+    _lib.call("nova_nf4_pack_native", packed.contiguous().data_ptr(), absmax.contiguous().data_ptr(),
+              int(absmax.dtype == torch.float32), out.data_ptr(), n, 2 * k2, _lib.stream_of(packed.device))
+    return out
+
+
+def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None, lut: torch.Tensor,
+             out: torch.Tensor, *,
              epilogue: int = _lib.NF4_PLAIN, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
              norm_weight: torch.Tensor | None = None, eps: float = 1e-6, argmax: torch.Tensor | None = None,
              token_out: torch.Tensor | None = None, pos: torch.Tensor | None = None,
              embed: torch.Tensor | None = None, embed_out: torch.Tensor | None = None,
-             workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Launch ``nova_nf4_gemv`` on 2-D views (x ``[M, K]``, out ``[M, N or N/2]``)."""
+             workspace: torch.Tensor | None = None, n: int | None = None) -> torch.Tensor:
+    """Launch ``nova_nf4_gemv`` on 2-D views (x ``[M, K]``, out ``[M, N or N/2]``).
+
+    Reference layout: ``packed`` uint8 ``[N, K/2]`` with ``absmax``
+    ``[K/64, N]``.  Native layout: ``packed`` is the 1-D unit stream from
+    :func:`pack_native`, ``absmax`` is None and ``n`` gives N."""
     m, k = x.shape
-    n = packed.shape[0]
-    if packed.shape[1] * 2 != k or absmax.shape != (k // NF4_BLOCK, n):
-        raise ValueError(f"weight shapes packed {tuple(packed.shape)} / absmax {tuple(absmax.shape)} "
-                         f"do not match K={k}, N={n}")
-    if absmax.dtype not in (torch.float32, torch.float16):
-        raise ValueError("absmax must be float32 or float16")
+    native = absmax is None
+    if native:
+        if n is None or packed.dim() != 1:
+            raise ValueError("the native layout needs the 1-D unit stream and n")
+    else:
+        n = packed.shape[0]
+        if packed.shape[1] * 2 != k or absmax.shape != (k // NF4_BLOCK, n):
+            raise ValueError(f"weight shapes packed {tuple(packed.shape)} / absmax {tuple(absmax.shape)} "
+                             f"do not match K={k}, N={n}")
+        if absmax.dtype not in (torch.float32, torch.float16):
+            raise ValueError("absmax must be float32 or float16")
     for t, nm in ((x, "x"), (out, "out")):
         if t.stride(1) != 1:
             raise ValueError(f"{nm} must have a contiguous last dimension")
@@ -121,7 +144,10 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, lut: t
     a = _lib.NF4Args()
     a.x, a.x_stride = x.data_ptr(), x.stride(0)
     a.norm_weight, a.eps = _lib.ptr(norm_weight), float(eps)
-    a.packed, a.absmax, a.absmax_fp32 = packed.data_ptr(), absmax.data_ptr(), int(absmax.dtype == torch.float32)
+    a.packed = packed.data_ptr()
+    a.absmax = None if native else absmax.data_ptr()
+    a.absmax_fp32 = 0 if native else int(absmax.dtype == torch.float32)
+    a.layout = 1 if native else 0
     a.lut = lut.data_ptr()
     a.bias = _lib.ptr(bias)
     a.residual, a.res_stride = (_lib.ptr(residual), residual.stride(0) if residual is not None else 0)

@@ -47,6 +47,18 @@ def _oracle_y(x, packed, absmax, rows=None):
     return onf4.nf4_linear(x.float().cpu().numpy(), p, a, onf4.nf4_codebook())
 
 
+LAYOUTS = ["ref", "native"]
+
+
+def _gemv(layout, x, packed, absmax, out, **kw):
+    """Run the GEMV on the reference layout or on the packed native unit stream."""
+    from nova_b200.kernels import nf4_gemv, pack_native
+
+    if layout == "native":
+        return nf4_gemv(x, pack_native(packed, absmax), None, _lut(), out, n=packed.shape[0], **kw)
+    return nf4_gemv(x, packed, absmax, _lut(), out, **kw)
+
+
 def _check(got, want32, tag):
     got = got.float().cpu().numpy()
     scale = float(np.abs(want32).max())
@@ -85,64 +97,67 @@ def test_dequant_bit_exact(cuda_lib):
     np.testing.assert_array_equal(got.cpu().numpy().view(np.uint16), want.view(np.uint16))
 
 
+@pytest.mark.parametrize("layout", LAYOUTS)
 @pytest.mark.parametrize("name", list(SHAPES))
-def test_gemv_qwen_shapes_m1(cuda_lib, name):
-    from nova_b200.kernels import nf4_gemv
-
+def test_gemv_qwen_shapes_m1(cuda_lib, name, layout):
     n, k = SHAPES[name]
-    _, packed, absmax = _weights(n, k, hash(name) % 1000)
+    _, packed, absmax = _weights(n, k, sum(map(ord, name)))
     x = (torch.randn(1, k, generator=torch.Generator().manual_seed(3))).half()
     out = torch.empty(1, n, dtype=torch.float16, device="cuda")
-    nf4_gemv(x.cuda(), packed, absmax, _lut(), out)
-    _check(out, _oracle_y(x, packed, absmax), name)
+    _gemv(layout, x.cuda(), packed, absmax, out)
+    _check(out, _oracle_y(x, packed, absmax), f"{name} {layout}")
 
 
-def test_gemv_lm_head_shape_sampled_rows(cuda_lib):
+@pytest.mark.parametrize("layout", LAYOUTS)
+def test_gemv_lm_head_shape_sampled_rows(cuda_lib, layout):
     """151936 x 2560 (the 4-bit lm_head): all rows computed on the GPU, 4096
     random rows checked against the oracle."""
-    from nova_b200.kernels import nf4_gemv
-
     n, k = 151936, 2560
     _, packed, absmax = _weights(n, k, 11)
     x = torch.randn(1, k, generator=torch.Generator().manual_seed(4)).half()
     out = torch.empty(1, n, dtype=torch.float16, device="cuda")
-    nf4_gemv(x.cuda(), packed, absmax, _lut(), out)
+    _gemv(layout, x.cuda(), packed, absmax, out)
     rows = np.sort(np.random.default_rng(0).choice(n, 4096, replace=False))
     _check(out[:, rows], _oracle_y(x, packed, absmax, rows), "lm_head")
 
 
+@pytest.mark.parametrize("layout", LAYOUTS)
 @pytest.mark.parametrize("m", [2, 5, 8])
-def test_gemv_small_batch(cuda_lib, m):
-    from nova_b200.kernels import nf4_gemv
-
+def test_gemv_small_batch(cuda_lib, m, layout):
     _, packed, absmax = _weights(1024, 2560, 5)
     x = torch.randn(m, 2560, generator=torch.Generator().manual_seed(m)).half()
     out = torch.empty(m, 1024, dtype=torch.float16, device="cuda")
-    nf4_gemv(x.cuda(), packed, absmax, _lut(), out)
-    _check(out, _oracle_y(x, packed, absmax), f"m={m}")
+    _gemv(layout, x.cuda(), packed, absmax, out)
+    _check(out, _oracle_y(x, packed, absmax), f"m={m} {layout}")
 
 
-def test_gemv_is_deterministic(cuda_lib):
+@pytest.mark.parametrize("layout", LAYOUTS)
+def test_gemv_is_deterministic(cuda_lib, layout):
     """The split-K reduction adds partials in a fixed order: repeated launches
-    are bit-identical."""
-    from nova_b200.kernels import nf4_gemv
+    are bit-identical, with and without programmatic dependent launch."""
+    from nova_b200 import _lib
 
     _, packed, absmax = _weights(2560, 4096, 6)
     x = torch.randn(1, 4096, generator=torch.Generator().manual_seed(7)).half().cuda()
-    a = nf4_gemv(x, packed, absmax, _lut(), torch.empty(1, 2560, dtype=torch.float16, device="cuda"))
-    b = nf4_gemv(x, packed, absmax, _lut(), torch.empty(1, 2560, dtype=torch.float16, device="cuda"))
-    assert torch.equal(a, b)
+    a = _gemv(layout, x, packed, absmax, torch.empty(1, 2560, dtype=torch.float16, device="cuda"))
+    b = _gemv(layout, x, packed, absmax, torch.empty(1, 2560, dtype=torch.float16, device="cuda"))
+    _lib.set_pdl(True)
+    try:
+        c = _gemv(layout, x, packed, absmax, torch.empty(1, 2560, dtype=torch.float16, device="cuda"))
+    finally:
+        _lib.set_pdl(False)
+    assert torch.equal(a, b) and torch.equal(a, c)
 
 
-def test_residual_epilogue(cuda_lib):
+@pytest.mark.parametrize("layout", LAYOUTS)
+def test_residual_epilogue(cuda_lib, layout):
     from nova_b200 import _lib
-    from nova_b200.kernels import nf4_gemv
 
     _, packed, absmax = _weights(2560, 4096, 8)
     x = torch.randn(1, 4096, generator=torch.Generator().manual_seed(8)).half()
     res = torch.randn(1, 2560, generator=torch.Generator().manual_seed(9)).half()
     out = res.clone().cuda()
-    nf4_gemv(x.cuda(), packed, absmax, _lut(), out, epilogue=_lib.NF4_RESIDUAL, residual=out)   # in place
+    _gemv(layout, x.cuda(), packed, absmax, out, epilogue=_lib.NF4_RESIDUAL, residual=out)   # in place
     y16 = _oracle_y(x, packed, absmax).astype(np.float16)
     want = (res.numpy().astype(np.float32) + y16.astype(np.float32)).astype(np.float16)
     got = out.cpu().numpy().astype(np.float32)
@@ -155,10 +170,10 @@ def test_residual_epilogue(cuda_lib):
     assert (got == want.astype(np.float32)).mean() > 0.99
 
 
-def test_silu_mul_epilogue_interleaved(cuda_lib):
+@pytest.mark.parametrize("layout", LAYOUTS)
+def test_silu_mul_epilogue_interleaved(cuda_lib, layout):
     from nova_b200 import _lib
     from nova_b200.decoder import interleave_gate_up
-    from nova_b200.kernels import nf4_gemv
 
     n, k = 1024, 2560
     _, gp, ga = _weights(n, k, 12)
@@ -166,28 +181,27 @@ def test_silu_mul_epilogue_interleaved(cuda_lib):
     packed, absmax = interleave_gate_up(gp, ga, up, ua)
     x = torch.randn(1, k, generator=torch.Generator().manual_seed(14)).half()
     out = torch.empty(1, n, dtype=torch.float16, device="cuda")
-    nf4_gemv(x.cuda(), packed, absmax, _lut(), out, epilogue=_lib.NF4_SILU_MUL)
+    _gemv(layout, x.cuda(), packed, absmax, out, epilogue=_lib.NF4_SILU_MUL)
     g16 = _oracle_y(x, gp, ga).astype(np.float16)
     u16 = _oracle_y(x, up, ua).astype(np.float16)
     want = onorm.silu_mul(g16, u16)
     assert_ulp_or_abs(out.cpu().numpy(), want, 1.0, 1e-6, "silu_mul")
 
 
-def test_norm_prologue(cuda_lib):
-    from nova_b200.kernels import nf4_gemv
-
+@pytest.mark.parametrize("layout", LAYOUTS)
+def test_norm_prologue(cuda_lib, layout):
     _, packed, absmax = _weights(6144, 2560, 15)
     h = (torch.randn(3, 2560, generator=torch.Generator().manual_seed(16)) * 3).half()
     w = (1 + 0.1 * torch.randn(2560, generator=torch.Generator().manual_seed(17))).half()
     out = torch.empty(3, 6144, dtype=torch.float16, device="cuda")
-    nf4_gemv(h.cuda(), packed, absmax, _lut(), out, norm_weight=w.cuda(), eps=1e-6)
+    _gemv(layout, h.cuda(), packed, absmax, out, norm_weight=w.cuda(), eps=1e-6)
     xn = onorm.rms_norm(h.numpy(), w.numpy(), 1e-6)
     _check(out, _oracle_y(torch.from_numpy(xn), packed, absmax), "norm prologue")
 
 
-def test_argmax_epilogue_and_step_finalize(cuda_lib):
+@pytest.mark.parametrize("layout", LAYOUTS)
+def test_argmax_epilogue_and_step_finalize(cuda_lib, layout):
     from nova_b200 import _lib
-    from nova_b200.kernels import nf4_gemv
 
     n, k, vocab_embed = 8192, 2560, 8192
     _, packed, absmax = _weights(n, k, 18)
@@ -198,8 +212,8 @@ def test_argmax_epilogue_and_step_finalize(cuda_lib):
     tokens = torch.full((2,), -1, dtype=torch.int64, device="cuda")
     pos = torch.tensor([41], dtype=torch.int64, device="cuda")
     hidden = torch.empty(2, k, dtype=torch.float16, device="cuda")
-    nf4_gemv(x.cuda(), packed, absmax, _lut(), logits, epilogue=_lib.NF4_ARGMAX, argmax=slot, token_out=tokens,
-             pos=pos, embed=embed, embed_out=hidden)
+    _gemv(layout, x.cuda(), packed, absmax, logits, epilogue=_lib.NF4_ARGMAX, argmax=slot, token_out=tokens,
+          pos=pos, embed=embed, embed_out=hidden)
     torch.cuda.synchronize()
     # greedy token = first index of the maximal fp16 logit (torch.argmax semantics)
     want_tok = torch.argmax(logits, dim=-1)
@@ -210,12 +224,13 @@ def test_argmax_epilogue_and_step_finalize(cuda_lib):
     _check(logits, _oracle_y(x, packed, absmax), "logits")
 
 
-def test_shared_workspace_across_shapes(cuda_lib):
+@pytest.mark.parametrize("layout", LAYOUTS)
+def test_shared_workspace_across_shapes(cuda_lib, layout):
     """GEMVs with different N on one workspace (as the decoder launches them)
     give the same results as with private workspaces, including the argmax
     finalize."""
     from nova_b200 import _lib
-    from nova_b200.kernels import gemv_workspace, nf4_gemv
+    from nova_b200.kernels import gemv_workspace
 
     shapes = [(512, 1024, _lib.NF4_RESIDUAL), (2048, 512, _lib.NF4_SILU_MUL), (1536, 512, _lib.NF4_PLAIN),
               (4096, 512, _lib.NF4_ARGMAX)]
@@ -234,12 +249,37 @@ def test_shared_workspace_across_shapes(cuda_lib):
                 kw.update(argmax=torch.zeros(1, dtype=torch.int64, device="cuda"),
                           token_out=torch.full((1,), -1, dtype=torch.int64, device="cuda"),
                           pos=torch.zeros(1, dtype=torch.int64, device="cuda"))
-            nf4_gemv(x, packed, absmax, _lut(), out, epilogue=epi, workspace=ws, **kw)
+            _gemv(layout, x, packed, absmax, out, epilogue=epi, workspace=ws, **kw)
             outs.append((out, kw))
         assert torch.equal(outs[0][0], outs[1][0]), f"N={n} epilogue {epi}"
         if epi == _lib.NF4_ARGMAX:
             for o, kw in outs:
                 assert int(kw["pos"].item()) == 1 and int(kw["token_out"].item()) == int(torch.argmax(o).item())
+
+
+def test_native_packer_layout(cuda_lib):
+    """Unit record = two lane-major halves of code bytes (rows g, g+8 then rows
+    g+16, g+24; 16 bytes per lane in each), then absmax in lane-group order."""
+    from nova_b200.kernels import pack_native
+
+    _, packed, absmax = _weights(64, 128, 31)
+    u = pack_native(packed, absmax).cpu().numpy()
+    p, a = packed.cpu().numpy(), absmax.cpu().numpy()
+    assert u.size == 2 * 2 * 1088
+    for unit in range(4):
+        rg, b = divmod(unit, 2)
+        rec = u[unit * 1088:(unit + 1) * 1088]
+        for lane in range(32):
+            g, t = divmod(lane, 4)
+            for r in range(4):
+                row = 32 * rg + g + 8 * r
+                off = 512 * (r // 2) + 16 * lane + 8 * (r % 2)
+                np.testing.assert_array_equal(rec[off: off + 8],
+                                              p[row, 32 * b + 8 * t: 32 * b + 8 * t + 8])
+        am = rec[1024:].view(np.float16)
+        for g in range(8):
+            for r in range(4):
+                assert am[4 * g + r] == a[b, 32 * rg + g + 8 * r]
 
 
 def test_fused_nf4_linear_reference_layout(cuda_lib):
