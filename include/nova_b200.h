@@ -145,6 +145,24 @@ NOVA_API int nova_attn_decode_int8(const nova_attn_int8_args* args, void* stream
  * gave up); copies it to *host_value synchronously and clears it. */
 NOVA_API int nova_attn_read_error(void* workspace, int64_t batch, int64_t kv_heads, int* host_value);
 
+/* Size of the built-in scratch array of nova_attn_decode_int8_noalloc. */
+#define NOVA_ATTN_NOALLOC_SCRATCH_BYTES (4 << 20)
+
+/* nova_attn_decode_int8 for callers that cannot allocate device memory (an
+ * allocator-free runtime, or a host whose device memory is all in its own
+ * pools): args->workspace and args->workspace_bytes are ignored and the
+ * split partials, arrival counters and error word live in a 4 MiB array
+ * built into the library, one per device.  Nothing is allocated.  Shapes
+ * whose nova_attn_workspace_bytes() exceeds NOVA_ATTN_NOALLOC_SCRATCH_BYTES
+ * are rejected with NOVA_ERR_UNSUPPORTED.  The first call on a device looks
+ * up the array's address (cudaGetSymbolAddress, with that device current):
+ * make it before any stream capture.  Each call clears the counters and the
+ * error word on `stream` before the kernel; the array is shared by all calls
+ * on the device, so calls that overlap in time (other streams, other host
+ * threads) race on it.  No counterpart in the reference, whose decode
+ * attention allocates its scratch through torch (src/nova/kvattn.py:281-427). */
+NOVA_API int nova_attn_decode_int8_noalloc(const nova_attn_int8_args* args, void* stream);
+
 /* ------------------------------------------------------------------ NF4 */
 
 /* Epilogues of nova_nf4_gemv. */

@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libnova_b200.so")
 
 NOVA_OK, NOVA_ERR_INVALID, NOVA_ERR_ALIGN, NOVA_ERR_UNSUPPORTED, NOVA_ERR_CUDA = range(5)
 NF4_PLAIN, NF4_RESIDUAL, NF4_SILU_MUL, NF4_ARGMAX = range(4)
+NOVA_ATTN_NOALLOC_SCRATCH_BYTES = 4 << 20   # built-in scratch of nova_attn_decode_int8_noalloc
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int64
@@ -72,6 +73,7 @@ _SIGNATURES: dict[str, list] = {
     "nova_attn_workspace_bytes": [_I, _I, _I, _I, _i, ctypes.POINTER(_I)],
     "nova_attn_decode_int8": [ctypes.POINTER(AttnArgs), _P],
     "nova_attn_read_error": [_P, _I, _I, ctypes.POINTER(_i)],
+    "nova_attn_decode_int8_noalloc": [ctypes.POINTER(AttnArgs), _P],
     "nova_nf4_workspace_bytes": [_I, ctypes.POINTER(_I)],
     "nova_nf4_gemv": [ctypes.POINTER(NF4Args), _P],
     "nova_nf4_quantize": [_P, _I, _I, _P, _P, _P, _i, _P],
