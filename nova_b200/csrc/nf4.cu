@@ -277,15 +277,17 @@ __device__ __forceinline__ void flush_partial(const Params& p, int rg, const flo
     float c[NT][4];
 #pragma unroll
     for (int i = 0; i < NT; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.f;
-    // contributors are added in warp order; the loads of four of them are in flight at once
+    // Contributors are added in warp order; the loads of four of them are in
+    // flight at once.  Every contributor after the first starts inside rg (its
+    // slot 0); the first one used slot 1 if its range began in an earlier group.
+    const int first_slot1 = unit_begin(p.units, w_first, W) < u0 ? 1 : 0;
     for (int w0 = w_first; w0 <= w_last; w0 += 4) {
         float4 v[4][NT];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int ww = w0 + q;
             if (ww > w_last) break;
-            const int frg = int(unit_begin(p.units, ww, W) / p.KB);
-            const int sl = 2 * ww + (rg == frg ? 0 : 1);
+            const int sl = 2 * ww + (ww == w_first ? first_slot1 : 0);
             const float4* src = p.partial + (int64_t(sl) * 32 + lane) * 2;
 #pragma unroll
             for (int i = 0; i < NT; ++i) v[q][i] = __ldcg(src + i);
@@ -421,7 +423,8 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     uint32_t xb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     int cur_rg = first_rg;
-    int seg_b0 = int(u_begin % p.KB);
+    int seg_b0 = int(u_begin - int64_t(first_rg) * p.KB);
+    int rg = first_rg, b = seg_b0;   // (row group, block) of the next unit, advanced incrementally
 
     for (int c = 0; c < n_chunks; ++c) {
         const int stage = c % NAT_STAGES;
@@ -435,8 +438,6 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         const int cnt = int(min(int64_t(stage_units), u_end - u0));
         const uint8_t* sbuf = ring + stage * stage_bytes;
         for (int j = 0; j < cnt; ++j) {
-            const int64_t u = u0 + j;
-            const int rg = int(u / p.KB), b = int(u % p.KB);
             if (rg != cur_rg) {   // the previous group ended inside this range at block KB-1
                 if (seg_b0 == 0) {
                     epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
@@ -462,6 +463,10 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
                 xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
             }
             mma_unit_smem(sbuf + j * UNIT_BYTES, xb, lut_base, laneword, lane, g, acc);
+            if (++b == p.KB) {
+                b = 0;
+                ++rg;
+            }
         }
         __syncwarp();
         if (lane == 0 && c + NAT_STAGES < n_chunks) {
@@ -470,8 +475,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         }
     }
     if (u_end > u_begin) {
-        const int last_b = int((u_end - 1) % p.KB);
-        if (seg_b0 == 0 && last_b == p.KB - 1) {
+        if (seg_b0 == 0 && b == 0) {   // the range ended exactly at the end of cur_rg
             epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
             epilogue<EPI>(p, 2 * cur_rg + 1, acc[1], g, t);
         } else {
