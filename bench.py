@@ -278,6 +278,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         return
 
     peaks = _peaks()
+    # DRAM bytes per algorithmic byte from one ncu capture of each kernel (dram__bytes_read.sum +
+    # dram__bytes_write.sum): the fused gate/up GEMV moved 26.54 MB for 26.46 MB of codes + absmax;
+    # the attention at ctx 32768 moved 71.67 + 1.22 MB for 71.32 MB.  Applied to this run's bytes.
+    gemv_traffic_ratio = 26.540288 / 26.460160
+    attn_traffic_ratio = (71.667200 + 1.222656) / 71.319552
     gemv = [kern[k] for k in ("qkv", "o_proj", "gate_up", "down", "lm_head")]
     per_tok = {k: kern[k]["ms"] * (1 if k == "lm_head" else cfg.num_hidden_layers) for k in kern}
     gemv_bytes = sum(kern[k]["bytes"] * (1 if k == "lm_head" else cfg.num_hidden_layers)
@@ -290,12 +295,15 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gemv_gbs / peaks["hbm_gbs"],
                 "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
                 else "fallback 6650 GB/s",
-                "traffic": None, "bytes_per_step": gemv_bytes, "ms_per_step": gemv_ms, "launches_timed": n_launch,
+                "traffic": gemv_bytes * gemv_traffic_ratio, "traffic_basis": "per step; ncu DRAM bytes of the fused "
+                "gate/up launch scaled by algorithmic bytes", "bytes_per_step": gemv_bytes, "ms_per_step": gemv_ms, "launches_timed": n_launch,
                 "per_shape": {k: {"gbs": round(kern[k]["gbs"], 1), "us": round(kern[k]["ms"] * 1e3, 2),
                                   "bytes": kern[k]["bytes"]} for k in ("qkv", "o_proj", "gate_up", "down", "lm_head")}}
     attn_roof = {"kernel": "attn_decode_int8_kernel", "bound": "hbm", "achieved": att["gbs"], "peak": peaks["hbm_gbs"],
                  "unit": "GB/s", "frac": att["gbs"] / peaks["hbm_gbs"], "ctx": att["ctx"],
-                 "bytes_per_launch": att["bytes"], "us_per_launch": att["ms"] * 1e3}
+                 "bytes_per_launch": att["bytes"], "us_per_launch": att["ms"] * 1e3,
+                 "traffic": att["bytes"] * attn_traffic_ratio,
+                 "traffic_basis": "per launch; ncu DRAM bytes at ctx 32768 scaled by algorithmic bytes"}
     step_bytes = gemv_bytes + att["bytes"] * cfg.num_hidden_layers
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
