@@ -42,7 +42,11 @@ NOVA_API const char* nova_last_error(void);
  * stream serialization (programmatic dependent launch), so a kernel's
  * prologue -- weight prefetch, LUT build -- overlaps the previous kernel's
  * tail; every kernel waits (griddepcontrol.wait) before touching data a
- * previous kernel writes.  Default 0.  No counterpart in the reference. */
+ * previous kernel writes.  Bit 1: every native-layout NF4 GEMV splits K over
+ * the warps of the whole grid (warp-level stream-K); by default only GEMVs
+ * with at least two 32-row groups per SM do, smaller ones split each row
+ * group over the warps of one CTA.  Default 0.  No counterpart in the
+ * reference. */
 NOVA_API int nova_set_launch_flags(int flags);
 NOVA_API int nova_get_launch_flags(void);
 

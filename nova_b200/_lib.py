@@ -118,9 +118,19 @@ def exported_names() -> list[str]:
     return list(_SIGNATURES) + list(_STRING_FNS) + list(_INT_FNS)
 
 
+LAUNCH_PDL = 1          # programmatic dependent launch
+LAUNCH_WARP_SPLITK = 2  # native-layout GEMV: warp-level instead of CTA-level split-K
+
+
 def set_pdl(enabled: bool) -> None:
-    """Programmatic dependent launch for every kernel launched afterwards."""
-    call("nova_set_launch_flags", 1 if enabled else 0)
+    """Programmatic dependent launch for every kernel launched afterwards
+    (other launch flags are kept)."""
+    flags = lib().nova_get_launch_flags()
+    call("nova_set_launch_flags", (flags | LAUNCH_PDL) if enabled else (flags & ~LAUNCH_PDL))
+
+
+def set_launch_flags(flags: int) -> None:
+    call("nova_set_launch_flags", int(flags))
 
 
 def pdl_enabled() -> bool:

@@ -152,6 +152,8 @@ def main() -> None:
     a.add_argument("--iters", type=int, default=20)
     a.add_argument("--layout", choices=["native", "ref"], default="native")
     a.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
+    a.add_argument("--variant", choices=["cta", "warp"], default="cta",
+                   help="native GEMV split-K at CTA level (default) or warp level")
     b = sub.add_parser("attn")
     b.add_argument("--ctx", type=int, required=True)
     b.add_argument("--batch", type=int, default=1)
@@ -163,25 +165,26 @@ def main() -> None:
     args = ap.parse_args()
     _lib.lib()
     if args.cmd == "gemv":
-        _lib.set_pdl(args.pdl)
+        _lib.set_launch_flags((_lib.LAUNCH_PDL if args.pdl else 0) |
+                              (_lib.LAUNCH_WARP_SPLITK if args.variant == "warp" else 0))
         print(json.dumps(bench_gemv(args.n, args.k, args.m, args.epilogue, args.norm, args.sets, args.iters,
                                     layout=args.layout)))
     elif args.cmd == "attn":
         print(json.dumps(bench_attn(args.ctx, args.batch, window=args.window, chunk=args.chunk, sets=args.sets,
                                     iters=args.iters)))
     else:
-        for pdl in (False, True):
-            _lib.set_pdl(pdl)
+        for variant in ("warp", "cta"):
+            _lib.set_launch_flags(_lib.LAUNCH_PDL | (_lib.LAUNCH_WARP_SPLITK if variant == "warp" else 0))
             for name, n, k in CONFIG2:
                 r = bench_gemv(n, k)
-                r["name"], r["pdl"] = name, pdl
+                r["name"], r["variant"] = name, variant
                 print(json.dumps(r), flush=True)
-        _lib.set_pdl(True)
-        for name, n, k, epi, nrm in (("qkv_fused", 6144, 2560, "plain", True), ("gate_up_fused", 19456, 2560, "silu",
-                                                                                 True)):
-            r = bench_gemv(n, k, epilogue=epi, norm=nrm)
-            r["name"] = name
-            print(json.dumps(r), flush=True)
+            for name, n, k, epi, nrm in (("qkv_fused", 6144, 2560, "plain", True),
+                                         ("gate_up_fused", 19456, 2560, "silu", True)):
+                r = bench_gemv(n, k, epilogue=epi, norm=nrm)
+                r["name"], r["variant"] = name, variant
+                print(json.dumps(r), flush=True)
+        _lib.set_launch_flags(_lib.LAUNCH_PDL)
         for ctx in (4096, 8192, 32768, 65536, 131072):
             for batch in (1, 4, 16):
                 if batch * ctx > 16 * 65536:

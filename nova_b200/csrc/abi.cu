@@ -71,7 +71,7 @@ extern "C" const char* nova_version(void) { return "nova_b200 0.1 (sm_100a, abi 
 extern "C" const char* nova_last_error(void) { return nova::g_last_error; }
 
 extern "C" int nova_set_launch_flags(int flags) {
-    if (flags & ~1) return nova::fail(NOVA_ERR_INVALID, "unknown launch flags 0x%x", flags);
+    if (flags & ~3) return nova::fail(NOVA_ERR_INVALID, "unknown launch flags 0x%x", flags);
     __atomic_store_n(&nova::g_launch_flags, flags, __ATOMIC_RELAXED);
     return NOVA_OK;
 }

@@ -429,21 +429,61 @@ __global__ void __launch_bounds__(THREADS, 3)
     if (!sm_last) return;
     __threadfence();
 
-    // ---- last CTA of this (batch, kv head): merge all splits
+    // ---- last CTA of this (batch, kv head): merge all splits.  Every (m, l)
+    // pair is fetched at once into shared memory (the stages are free now);
+    // warp hh then turns its head's maxima into weights and sums the
+    // accumulators in split order, eight loads in flight per lane.
+    const int n_ml = p.s_total * p.gq;
+    float2* ml = reinterpret_cast<float2*>(smem);
+    const bool parallel = n_ml * int(sizeof(float2)) <= NW * STAGE;
+    if (parallel) {
+        for (int i = threadIdx.x; i < n_ml; i += THREADS)
+            ml[i] = __ldcg(reinterpret_cast<const float2*>(part_bh + int64_t(i) * PART));
+        __syncthreads();
+    }
     if (hh < p.gq) {
-        float M = -INFINITY;
-        for (int s = 0; s < p.s_total; ++s) M = fmaxf(M, __ldcg(part_bh + (int64_t(s) * p.gq + hh) * PART));
-        float L = 0.f;
+        float M = -INFINITY, L = 0.f;
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (M != -INFINITY) {
-            for (int s = 0; s < p.s_total; ++s) {
-                const float* src = part_bh + (int64_t(s) * p.gq + hh) * PART;
-                const float ms = __ldcg(src);
-                if (ms == -INFINITY) continue;
-                const float wt = exp2f(ms - M);
-                L += wt * __ldcg(src + 1);
-                const float4 a = __ldcg(reinterpret_cast<const float4*>(src + 4 + d0));
-                o.x += wt * a.x; o.y += wt * a.y; o.z += wt * a.z; o.w += wt * a.w;
+        if (parallel) {
+            for (int s = lane; s < p.s_total; s += 32) M = fmaxf(M, ml[s * p.gq + hh].x);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            if (M != -INFINITY) {
+                for (int s = lane; s < p.s_total; s += 32) {
+                    const float2 v = ml[s * p.gq + hh];
+                    const float wt = v.x == -INFINITY ? 0.f : exp2f(v.x - M);
+                    ml[s * p.gq + hh].x = wt;
+                }
+                __syncwarp();
+                for (int s = 0; s < p.s_total; ++s) L += ml[s * p.gq + hh].x * ml[s * p.gq + hh].y;
+                for (int s0 = 0; s0 < p.s_total; s0 += 8) {
+                    float4 a[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (s0 + k < p.s_total && ml[(s0 + k) * p.gq + hh].x != 0.f)
+                            a[k] = __ldcg(reinterpret_cast<const float4*>(part_bh + (int64_t(s0 + k) * p.gq + hh) *
+                                                                                       PART + 4 + d0));
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        if (s0 + k >= p.s_total) break;
+                        const float wt = ml[(s0 + k) * p.gq + hh].x;
+                        if (wt == 0.f) continue;
+                        o.x += wt * a[k].x; o.y += wt * a[k].y; o.z += wt * a[k].z; o.w += wt * a[k].w;
+                    }
+                }
+            }
+        } else {
+            for (int s = 0; s < p.s_total; ++s) M = fmaxf(M, __ldcg(part_bh + (int64_t(s) * p.gq + hh) * PART));
+            if (M != -INFINITY) {
+                for (int s = 0; s < p.s_total; ++s) {
+                    const float* src = part_bh + (int64_t(s) * p.gq + hh) * PART;
+                    const float ms = __ldcg(src);
+                    if (ms == -INFINITY) continue;
+                    const float wt = exp2f(ms - M);
+                    L += wt * __ldcg(src + 1);
+                    const float4 a = __ldcg(reinterpret_cast<const float4*>(src + 4 + d0));
+                    o.x += wt * a.x; o.y += wt * a.y; o.z += wt * a.z; o.w += wt * a.w;
+                }
             }
         }
         const int qh = h * p.gq + hh;

@@ -189,26 +189,54 @@ __device__ __forceinline__ void build_lut(uint32_t* lut_s, const uint32_t* lut) 
     }
 }
 
-// Stage x in shared memory, optionally RMS-normalised in HF order.
+// Stage x in shared memory, optionally RMS-normalised in HF order.  When
+// every thread holds at most one 8-element chunk per row (K <= 8 * THREADS),
+// the chunk stays in registers between the sum of squares and the scaling,
+// so x and the norm weight are read once.
 template <int THREADS>
 __device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
     __shared__ float red[THREADS / 32][MAX_M];
     __shared__ float rstd[MAX_M];
     const int kv8 = p.K / 8;
     if (p.norm_w) {
+        const bool one = kv8 <= THREADS;
         float ss[MAX_M];
+        uint4 xv[MAX_M];
+        uint4 wv = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-        for (int m = 0; m < MAX_M; ++m) ss[m] = 0.f;
-        for (int i = threadIdx.x; i < kv8; i += THREADS) {
+        for (int m = 0; m < MAX_M; ++m) {
+            ss[m] = 0.f;
+            xv[m] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        auto add_sq = [&](const uint4& v, float& acc) {
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
 #pragma unroll
-            for (int m = 0; m < MAX_M; ++m) {
-                if (m >= p.M) break;
-                const uint4 v = *reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i);
-                const __half2* h = reinterpret_cast<const __half2*>(&v);
+            for (int q = 0; q < 4; ++q) {
+                const float2 f = __half22float2(h[q]);
+                acc += f.x * f.x + f.y * f.y;
+            }
+        };
+        if (one) {
+            const int i = threadIdx.x;
+            if (i < kv8) {
+                wv = *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float2 f = __half22float2(h[q]);
-                    ss[m] += f.x * f.x + f.y * f.y;
+                for (int m = 0; m < MAX_M; ++m) {
+                    if (m >= p.M) break;
+                    xv[m] = *reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i);
+                }
+#pragma unroll
+                for (int m = 0; m < MAX_M; ++m) {
+                    if (m >= p.M) break;
+                    add_sq(xv[m], ss[m]);
+                }
+            }
+        } else {
+            for (int i = threadIdx.x; i < kv8; i += THREADS) {
+#pragma unroll
+                for (int m = 0; m < MAX_M; ++m) {
+                    if (m >= p.M) break;
+                    add_sq(*reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i), ss[m]);
                 }
             }
         }
@@ -226,23 +254,35 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
             rstd[threadIdx.x] = rsqrt_ieee(__fdiv_rn(v, float(p.K)) + p.eps);
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < kv8; i += THREADS) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
-            const __half2* wh = reinterpret_cast<const __half2*>(&wv);
-            for (int m = 0; m < p.M; ++m) {
-                const uint4 v = *reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i);
-                const __half2* h = reinterpret_cast<const __half2*>(&v);
-                uint4 o;
-                __half2* oh = reinterpret_cast<__half2*>(&o);
-                const float r = rstd[m];
+        auto scale = [&](const uint4& v, const uint4& w8, float r) {
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
+            const __half2* wh = reinterpret_cast<const __half2*>(&w8);
+            uint4 o;
+            __half2* oh = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float2 f = __half22float2(h[q]);
-                    const float2 wf = __half22float2(wh[q]);
-                    const float2 nf = __half22float2(__floats2half2_rn(f.x * r, f.y * r));
-                    oh[q] = __floats2half2_rn(wf.x * nf.x, wf.y * nf.y);
+            for (int q = 0; q < 4; ++q) {
+                const float2 f = __half22float2(h[q]);
+                const float2 wf = __half22float2(wh[q]);
+                const float2 nf = __half22float2(__floats2half2_rn(f.x * r, f.y * r));
+                oh[q] = __floats2half2_rn(wf.x * nf.x, wf.y * nf.y);
+            }
+            return o;
+        };
+        if (one) {
+            const int i = threadIdx.x;
+            if (i < kv8) {
+#pragma unroll
+                for (int m = 0; m < MAX_M; ++m) {
+                    if (m >= p.M) break;
+                    *reinterpret_cast<uint4*>(xs + m * p.K + 8 * i) = scale(xv[m], wv, rstd[m]);
                 }
-                *reinterpret_cast<uint4*>(xs + m * p.K + 8 * i) = o;
+            }
+        } else {
+            for (int i = threadIdx.x; i < kv8; i += THREADS) {
+                const uint4 w8 = *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
+                for (int m = 0; m < p.M; ++m)
+                    *reinterpret_cast<uint4*>(xs + m * p.K + 8 * i) =
+                        scale(*reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i), w8, rstd[m]);
             }
         }
     } else {
@@ -483,6 +523,187 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         }
     }
     finish_launch<EPI>(p, lane);
+}
+
+// ---------------------------------------------------------------------------
+// Native-layout kernel, CTA-level split-K, for launches with fewer than two
+// row groups per SM: CTA c owns the whole row groups
+// [R*c/G, R*(c+1)/G).  Each row group is split over the 16 warps by blocks,
+// every warp streams its slice through its private two-stage ring (one bulk
+// copy per chunk of up to `stage_units` units), and the 16 partial fragments
+// are added in shared memory in warp order by the group's reducer warp (group
+// index mod 16), which runs the epilogue.  No cross-CTA reduction.
+//
+// The red buffer [16 warps][32 lanes][8 floats] is single-buffered:
+// `full` completes when all 16 warps wrote segment j, `empty` when its reducer
+// has read it, and no warp writes segment j + 1 before that.
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int EPI, bool XG>
+__global__ void __launch_bounds__(NAT_THREADS, 1)
+    nf4_gemv_cta_kernel(const __grid_constant__ Params p, int stage_units, int* err) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[NAT_WARPS][NAT_STAGES];
+    __shared__ __align__(8) uint64_t bar_full, bar_empty;
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
+    __half* xs = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
+    const int xs_bytes = XG ? 0 : (p.M * p.K * 2 + 127) / 128 * 128;
+    float4* red = reinterpret_cast<float4*>(smem_raw + LUT_BYTES + xs_bytes);   // [16][32][2]
+    const int stage_bytes = stage_units * UNIT_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint8_t* ring = smem_raw + LUT_BYTES + xs_bytes + NAT_WARPS * 32 * 32 + size_t(warp) * NAT_STAGES * stage_bytes;
+    const int c = blockIdx.x;
+    const int G = gridDim.x;
+    const int KB = p.KB;
+    const int64_t n_rg = p.units / KB;
+    const int64_t u_begin = n_rg * c / G * KB, u_end = n_rg * (c + 1) / G * KB;   // whole row groups
+    const int rg_first = int(u_begin / KB);
+    const int rg_last = u_end > u_begin ? int((u_end - 1) / KB) : rg_first - 1;
+
+    // this warp's block slice [a, b) of segment rg
+    auto slice = [&](int rg, int& a, int& b) {
+        const int64_t base = int64_t(rg) * KB;
+        const int s0 = int(max(u_begin, base) - base);
+        const int s1 = int(min(u_end, base + KB) - base);
+        const int len = s1 - s0;
+        a = s0 + len * warp / NAT_WARPS;
+        b = s0 + len * (warp + 1) / NAT_WARPS;
+    };
+    // issue cursor over this warp's chunks (segment by segment)
+    int is_rg = rg_first, is_off = 0, is_b = 0;
+    {
+        int a, b;
+        if (is_rg <= rg_last) {
+            slice(is_rg, a, b);
+            is_off = a;
+            is_b = b;
+        }
+    }
+    int issued = 0;
+    auto issue_next = [&]() {   // lane 0 only; returns false when no chunk is left
+        while (is_rg <= rg_last && is_off >= is_b) {
+            ++is_rg;
+            if (is_rg > rg_last) return false;
+            int a, b;
+            slice(is_rg, a, b);
+            is_off = a;
+            is_b = b;
+        }
+        if (is_rg > rg_last) return false;
+        const int cnt = min(stage_units, is_b - is_off);
+        const int st = issued % NAT_STAGES;
+        uint64_t* bar = &bars[warp][st];
+        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(ring + st * stage_bytes, p.packed + (int64_t(is_rg) * KB + is_off) * UNIT_BYTES, bytes, bar);
+        is_off += cnt;
+        ++issued;
+        return true;
+    };
+
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
+        if (warp == 0) {
+            mbar_init(&bar_full, NAT_WARPS);
+            mbar_init(&bar_empty, 1);
+        }
+        fence_mbar_init();
+        for (int k = 0; k < NAT_STAGES; ++k)
+            if (!issue_next()) break;
+    }
+    build_lut<NAT_THREADS>(lut_s, p.lut);
+    pdl_trigger();
+    pdl_wait();
+    if (!XG) stage_x<NAT_THREADS>(p, xs);
+    __syncthreads();
+
+    const uint32_t lut_base = smem_u32(lut_s);
+    const uint32_t laneword = uint32_t(lane) << 2;
+    const bool xlane = g < p.M;
+    const __half* xrow = XG ? p.x + (xlane ? g : 0) * p.x_stride + 16 * t : xs + (xlane ? g : 0) * p.K + 16 * t;
+    uint32_t xb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    int consumed = 0;
+    bool ok = true;
+
+    for (int rg = rg_first, j = 0; rg <= rg_last; ++rg, ++j) {
+        int a, b;
+        slice(rg, a, b);
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        for (int off = a; off < b && ok;) {
+            const int cnt = min(stage_units, b - off);
+            const int st = consumed % NAT_STAGES;
+            if (!mbar_wait(&bars[warp][st], uint32_t((consumed / NAT_STAGES) & 1), err, 2)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* sbuf = ring + st * stage_bytes;
+            for (int jj = 0; jj < cnt; ++jj) {
+                const int blk = off + jj;
+                if (xlane) {
+                    uint4 x0, x1;
+                    if (XG) {
+                        x0 = __ldg(reinterpret_cast<const uint4*>(xrow + 64 * blk));
+                        x1 = __ldg(reinterpret_cast<const uint4*>(xrow + 64 * blk + 8));
+                    } else {
+                        x0 = lds128(xrow + 64 * blk);
+                        x1 = lds128(xrow + 64 * blk + 8);
+                    }
+                    xb[0] = x0.x; xb[1] = x0.y; xb[2] = x0.z; xb[3] = x0.w;
+                    xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
+                }
+                mma_unit_smem(sbuf + jj * UNIT_BYTES, xb, lut_base, laneword, lane, g, acc);
+            }
+            ++consumed;
+            off += cnt;
+            __syncwarp();
+            if (lane == 0) {
+                fence_proxy_async();
+                issue_next();
+            }
+        }
+        if (!ok) break;
+        // ---- segment reduction in shared memory
+        if (j > 0 && !mbar_wait(&bar_empty, uint32_t((j - 1) & 1), err, 3)) {
+            ok = false;
+            break;
+        }
+        red[(warp * 32 + lane) * 2] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+        red[(warp * 32 + lane) * 2 + 1] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_full);
+        if (warp == (j & (NAT_WARPS - 1))) {
+            if (!mbar_wait(&bar_full, uint32_t(j & 1), err, 3)) {
+                ok = false;
+                break;
+            }
+            float r[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+            for (int ww = 0; ww < NAT_WARPS; ++ww) {
+                const float4 v0 = red[(ww * 32 + lane) * 2], v1 = red[(ww * 32 + lane) * 2 + 1];
+                r[0][0] += v0.x; r[0][1] += v0.y; r[0][2] += v0.z; r[0][3] += v0.w;
+                r[1][0] += v1.x; r[1][1] += v1.y; r[1][2] += v1.z; r[1][3] += v1.w;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_empty);
+            const int64_t base = int64_t(rg) * KB;
+            if (u_begin <= base && u_end >= base + KB) {
+                epilogue<EPI>(p, 2 * rg, r[0], g, t);
+                epilogue<EPI>(p, 2 * rg + 1, r[1], g, t);
+            } else {
+                flush_partial<EPI, 2>(p, rg, r, c, rg_first, lane, g, t);
+            }
+        }
+    }
+    // every copy this warp issued has been consumed unless a wait gave up
+    if (!ok && lane == 0)
+        for (; consumed < issued; ++consumed)
+            mbar_wait(&bars[warp][consumed % NAT_STAGES], uint32_t((consumed / NAT_STAGES) & 1), err, 2);
+    __syncthreads();
+    if (warp == 0 && ok) finish_launch<EPI>(p, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -847,16 +1068,41 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         if (stage_units < 1)
             return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld with the norm prologue leaves no shared memory for the "
                                               "weight ring", (long long)(m * k));
-        NKern kern = kernels[xg][epi];
-        const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + stage_units * ring_unit;
-        if (int rc = prepare_smem(kern, nsmem, &smem_set[xg][epi])) return rc;
         p.units = int64_t(n / UNIT_ROWS) * p.KB;
-        const int64_t want = (p.units + NAT_MIN_UNITS - 1) / NAT_MIN_UNITS;
-        p.total_warps = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sm_count()) * NAT_WARPS, want)));
-        const unsigned grid = unsigned(std::min<int64_t>(sm_count(), p.total_warps));
         int* errp = reinterpret_cast<int*>(p.done + 1);
-        err = launch(kern, dim3(grid), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p, int(stage_units),
-                     errp);
+        // Warp-level stream-K from two row groups per SM up (gate/up, the
+        // lm_head: the stream-K tail is short next to the stream); CTA-level
+        // split-K on whole row groups below that (no cross-CTA reduction).
+        const bool warp_level = (launch_flags() & 2) || n / UNIT_ROWS >= 2 * int64_t(sm_count());
+        if (warp_level) {
+            NKern kern = kernels[xg][epi];
+            const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + stage_units * ring_unit;
+            if (int rc = prepare_smem(kern, nsmem, &smem_set[xg][epi])) return rc;
+            const int64_t want = (p.units + NAT_MIN_UNITS - 1) / NAT_MIN_UNITS;
+            p.total_warps = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sm_count()) * NAT_WARPS, want)));
+            const unsigned grid = unsigned(std::min<int64_t>(sm_count(), p.total_warps));
+            err = launch(kern, dim3(grid), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p, int(stage_units),
+                         errp);
+        } else {   // CTA-level split-K
+            static const NKern cta_kernels[2][4] = {
+                {nf4_gemv_cta_kernel<0, false>, nf4_gemv_cta_kernel<1, false>, nf4_gemv_cta_kernel<2, false>,
+                 nf4_gemv_cta_kernel<3, false>},
+                {nf4_gemv_cta_kernel<0, true>, nf4_gemv_cta_kernel<1, true>, nf4_gemv_cta_kernel<2, true>,
+                 nf4_gemv_cta_kernel<3, true>}};
+            static int64_t cta_smem_set[2][4] = {};
+            const int64_t red_bytes = int64_t(NAT_WARPS) * 32 * 32;
+            const int64_t cu = std::min<int64_t>(4, (optin - int64_t(LUT_BYTES) - xs_bytes - red_bytes - slack) / ring_unit);
+            if (cu < 1)
+                return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld leaves no shared memory for the weight ring",
+                            (long long)(m * k));
+            NKern kern = cta_kernels[xg][epi];
+            const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + red_bytes + cu * ring_unit;
+            if (int rc = prepare_smem(kern, nsmem, &cta_smem_set[xg][epi])) return rc;
+            const int64_t grid = std::min<int64_t>(sm_count(), n / UNIT_ROWS);
+            p.total_warps = int(grid);   // contributors and finalize arrivals are counted per CTA
+            err = launch(kern, dim3(unsigned(grid)), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p,
+                         int(cu), errp);
+        }
     } else {
         static const Kern kernels[2][4] = {
             {nf4_gemv_ref_kernel<__half, 0>, nf4_gemv_ref_kernel<__half, 1>, nf4_gemv_ref_kernel<__half, 2>,

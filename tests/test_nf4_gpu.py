@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import assert_ulp_or_abs
+from conftest import assert_ulp_or_abs, fp16_ulp
 from oracle import nf4 as onf4
 from oracle import norm as onorm
 
@@ -315,3 +315,63 @@ def test_nf4linear_module_and_rejects_bad_inputs(cuda_lib):
         fused_nf4_linear(x, lin.packed, lin.absmax, lin.lut, 128)
     with pytest.raises(ValueError):
         fused_nf4_linear(x.cpu(), lin.packed, lin.absmax, lin.lut, 256)
+
+
+@pytest.mark.parametrize("variant", ["cta", "warp"])
+@pytest.mark.parametrize("n,k,epi", [(1024, 2560, "plain"), (2560, 9728, "residual"), (96, 192, "plain"),
+                                     (19456, 2560, "silu")])
+def test_native_split_k_variants(cuda_lib, variant, n, k, epi):
+    """Both native split-K schedules (CTA-level on whole row groups, warp-level
+    stream-K) match the oracle on shapes that select each by default; M = 2."""
+    from nova_b200 import _lib
+    from nova_b200.decoder import interleave_gate_up
+    from nova_b200.kernels import nf4_gemv, pack_native
+
+    x = (torch.randn(2, k, generator=torch.Generator().manual_seed(5))).half()
+    if epi == "silu":
+        _, gp, ga = _weights(n // 2, k, 31)
+        _, up, ua = _weights(n // 2, k, 32)
+        packed, absmax = interleave_gate_up(gp, ga, up, ua)
+    else:
+        _, packed, absmax = _weights(n, k, n + k)
+    nout = n // 2 if epi == "silu" else n
+    res = (torch.randn(2, nout, generator=torch.Generator().manual_seed(6)) * 0.1).half().cuda()
+    out = res.clone() if epi == "residual" else torch.empty(2, nout, dtype=torch.float16, device="cuda")
+    kw = {}
+    if epi == "residual":
+        kw = {"epilogue": _lib.NF4_RESIDUAL, "residual": out}
+    elif epi == "silu":
+        kw = {"epilogue": _lib.NF4_SILU_MUL}
+    flags = _lib.lib().nova_get_launch_flags()
+    try:
+        _lib.set_launch_flags((flags & _lib.LAUNCH_PDL) | (_lib.LAUNCH_WARP_SPLITK if variant == "warp" else 0))
+        nf4_gemv(x.cuda(), pack_native(packed, absmax), None, _lut(), out, n=n, **kw)
+    finally:
+        _lib.set_launch_flags(flags)
+    got = out.float().cpu().numpy()
+    if epi == "plain":
+        _check(out, _oracle_y(x, packed, absmax), f"{variant} {n}x{k}")
+    elif epi == "residual":
+        y = _oracle_y(x, packed, absmax)
+        want = (res.float().cpu().numpy() + y.astype(np.float16).astype(np.float32)).astype(np.float16)
+        # fp16(y) may land one ulp(y) away, then the add rounds again: ulp(y) + ulp(result)
+        bound = fp16_ulp(y) + fp16_ulp(want) + 1e-5 * np.abs(y).max()
+        assert np.all(np.abs(got - want.astype(np.float32)) <= bound), variant
+    else:
+        # gate and up are rounded to fp16 before SiLU*up, and each may sit one ulp (or, where the dot product
+        # cancels, 1e-5 * max|y|: the GEMV criterion) away from the oracle's; SiLU amplifies that by up to |g|
+        # where it is flat.  Bound: the oracle evaluated at gate/up moved by that much either way.
+        g32, u32 = _oracle_y(x, gp, ga), _oracle_y(x, up, ua)
+        g16, u16 = g32.astype(np.float16), u32.astype(np.float16)
+        want = onorm.silu_mul(g16, u16).astype(np.float32)
+        eg = np.maximum(fp16_ulp(g16), 1e-5 * np.abs(g32).max())
+        eu = np.maximum(fp16_ulp(u16), 1e-5 * np.abs(u32).max())
+        dev = np.zeros_like(want)
+        for dg in (-1, 0, 1):
+            for du in (-1, 0, 1):
+                gg = g16.astype(np.float32) + dg * eg
+                uu = u16.astype(np.float32) + du * eu
+                alt = gg / (1.0 + np.exp(-gg)) * uu
+                dev = np.maximum(dev, np.abs(alt - want))
+        assert np.all(np.abs(got - want) <= dev + 2 * fp16_ulp(want)), f"silu {variant}"
+        assert (got == want).mean() > 0.99, f"silu {variant}: too few exact"
