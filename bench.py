@@ -8,9 +8,12 @@ the NF4 GEMV and the int8-KV attention measured live.
 
 One step = one decode token for every row (one CUDA-graph replay).  The step
 streams ~2.8 GB (weights + KV), far above the 126 MB L2, so no flush is needed
-between steps.  N > 1 (torchrun, one process per GPU): independent replicas,
-one sequence each (weak scaling); the timed region is bracketed by barriers
-and the max over ranks is reported.
+between steps.  N > 1 (torchrun, one process per GPU): by default the same
+decode sharded over the N GPUs by tensor parallelism (KV heads / intermediate
+columns, NCCL all-reduce after o_proj and down_proj inside the graph; strong
+scaling: one sequence, whole-job tok/s); ``--parallel replicas`` runs N
+independent copies instead (weak scaling).  The timed region is bracketed by
+barriers and the max over ranks is reported.
 """
 
 from __future__ import annotations
@@ -42,6 +45,8 @@ def _args():
     ap.add_argument("--layers", type=int, default=36, help="36 for the headline config")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp",
+                    help="N > 1: tensor parallelism over the N GPUs (default) or N independent replicas")
     return ap.parse_args()
 
 
@@ -146,20 +151,25 @@ def _time_kernels(dec, reps: int = 10) -> dict:
         return w.stream_bytes
 
     scratch = {"qkv": dec.qkv.clone(), "resid": dec.resid.clone(), "act": dec.act.clone(), "attn": dec.attn.clone()}
+    if dec.tp.active:   # row-parallel projections write fp32 partial sums
+        part = dec.part32.clone()
+
+        def row_par(x, w):
+            nf4_gemv(x, w.units, None, lut, part, epilogue=_lib.NF4_F32, workspace=ws, n=w.n)
+    else:
+        def row_par(x, w):
+            nf4_gemv(x, w.units, None, lut, scratch["resid"], epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"],
+                     workspace=ws, n=w.n)
     fams = {
         "qkv": (lambda lw: nf4_gemv(scratch["resid"], lw.qkv.units, None, lut, scratch["qkv"],
                                     norm_weight=lw.input_ln, eps=eps, workspace=ws, n=lw.qkv.n),
                 lambda lw: bytes_of(lw.qkv)),
-        "o_proj": (lambda lw: nf4_gemv(scratch["attn"], lw.o.units, None, lut, scratch["resid"],
-                                       epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"], workspace=ws, n=lw.o.n),
-                   lambda lw: bytes_of(lw.o)),
+        "o_proj": (lambda lw: row_par(scratch["attn"], lw.o), lambda lw: bytes_of(lw.o)),
         "gate_up": (lambda lw: nf4_gemv(scratch["resid"], lw.gate_up.units, None, lut, scratch["act"],
                                         epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln, eps=eps, workspace=ws,
                                         n=lw.gate_up.n),
                     lambda lw: bytes_of(lw.gate_up)),
-        "down": (lambda lw: nf4_gemv(scratch["act"], lw.down.units, None, lut, scratch["resid"],
-                                     epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"], workspace=ws, n=lw.down.n),
-                 lambda lw: bytes_of(lw.down)),
+        "down": (lambda lw: row_par(scratch["act"], lw.down), lambda lw: bytes_of(lw.down)),
     }
     from nova_b200.bench_kernels import _graph_time
 
@@ -179,8 +189,8 @@ def _time_kernels(dec, reps: int = 10) -> dict:
     out["lm_head"] = {"launches": reps * 4, "ms": us * 1e-3, "bytes": hb, "gbs": hb / (us * 1e-6) / 1e9}
     # int8-KV attention over every layer's cache at the current context
     c = dec.cache
-    q3 = dec.q_rot.view(B, cfg.num_attention_heads, cfg.head_dim)
-    a3 = scratch["attn"].view(B, cfg.num_attention_heads, cfg.head_dim)
+    q3 = dec.q_rot.view(B, dec.hq, cfg.head_dim)
+    a3 = scratch["attn"].view(B, dec.hq, cfg.head_dim)
 
     def attn(li):
         launch_attention(q3, (c.kq[li], c.kmn[li], c.kst[li], c.vq[li], c.vmn[li], c.vst[li]),
@@ -191,10 +201,10 @@ def _time_kernels(dec, reps: int = 10) -> dict:
     n = reps * cfg.num_hidden_layers
     ms = us * 1e-3
     qlen, written = int(c._qlen.item()), int(c._written.item())
-    hkv = cfg.num_key_value_heads
+    hkv = dec.hkv
     # algorithmic bytes: per cached int8 token and KV head 272 B = K+V codes (2*128 B) + the fp16
     # min/step vectors amortised over 64 tokens (4*128*2/64 B); the fp16 ring slots in use; q in, out
-    ab = B * hkv * (qlen * 272 + (written - qlen) * 2 * 128 * 2) + 2 * B * cfg.q_dim * 2
+    ab = B * hkv * (qlen * 272 + (written - qlen) * 2 * 128 * 2) + 2 * B * dec.q_dim * 2
     out["attention"] = {"launches": n, "ms": ms, "bytes": ab, "gbs": ab / (ms * 1e-3) / 1e9, "ctx": written}
     return out
 
@@ -206,6 +216,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     from nova_b200 import _lib
     from nova_b200.decoder import DecoderConfig, DecoderWeights, NovaDecoder
 
+    from nova_b200.tp import TPContext
+
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     _lib.lib()
@@ -213,8 +225,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     t0 = time.time()
     W = DecoderWeights.random_init(cfg, seed=args.seed, device=dev)
     max_len = args.ctx + 2 * (args.warmup + args.steps) + 64
-    dec = NovaDecoder(W, max_len=max_len, batch=args.batch, device=dev)
-    g = torch.Generator().manual_seed(args.seed + 1 + rank)
+    use_tp = world > 1 and args.parallel == "tp"
+    tp = TPContext(rank, world, dist.group.WORLD) if use_tp else None
+    dec = NovaDecoder(W, max_len=max_len, batch=args.batch, device=dev, tp=tp)
+    del W
+    copies = 1 if use_tp else world   # independent sequences in the job
+    g = torch.Generator().manual_seed(args.seed + 1 + (0 if use_tp else rank))
     prompt = torch.randint(0, cfg.vocab_size, (args.batch, args.ctx), generator=g)
     dec.prefill(prompt)
     dec.capture()
@@ -247,7 +263,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * args.batch * args.steps / (ms_max * 1e-3)
+    value = copies * args.batch * args.steps / (ms_max * 1e-3)
 
     # ---- e2e through the public API: pinned host token in, greedy token out, every step
     tok_in = torch.empty(args.batch, dtype=torch.int64, pin_memory=True)
@@ -269,7 +285,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     te = torch.tensor([f0.elapsed_time(f1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_v = world * args.batch * args.steps / (float(te.item()) * 1e-3)
+    e2e_v = copies * args.batch * args.steps / (float(te.item()) * 1e-3)
 
     kern = _time_kernels(dec)
     if world > 1:
@@ -307,21 +323,24 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     step_bytes = gemv_bytes + att["bytes"] * cfg.num_hidden_layers
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "strong" if use_tp else "weak", "vs_baseline": None,
         "dtype": "fp16", "data": "synthetic",
         "config": {"workload": "qwen3vl4b-text greedy decode, NF4 weights (blocksize 64, fp16 absmax) incl. 4-bit "
                                "lm_head, int8 KV (int8t64), ctx 8192 prefilled with uniform random tokens "
                                "(BASELINE config 4)", "model": "Qwen3-VL-4B text (random init N(0,0.02))",
-                   "global_batch": args.batch * world, "ctx": args.ctx, "layers": cfg.num_hidden_layers,
-                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "global_batch": args.batch * copies, "ctx": args.ctx, "layers": cfg.num_hidden_layers,
+                   "parallelism": f"tp{world} (KV-head / column-row split, NCCL all-reduce after o_proj and "
+                                  f"down_proj)" if use_tp else ("replicas" if world > 1 else "single GPU"),
                    "l2": "inputs larger than L2 (2.8 GB streamed per step)", "graph": "one CUDA graph per step"},
         "roofline": roofline,
         "attn_roofline": attn_roof,
-        "step_roofline": {"bytes_per_token": step_bytes,
+        # bytes one GPU streams per step (its shard with tensor parallelism) against one GPU's peak
+        "step_roofline": {"bytes_per_token": step_bytes, "per": "GPU",
                           "tok_s_at_peak": peaks["hbm_gbs"] * 1e9 / step_bytes,
-                          "frac": (value / world / args.batch) / (peaks["hbm_gbs"] * 1e9 / step_bytes)},
+                          "frac": (value / copies / args.batch) / (peaks["hbm_gbs"] * 1e9 / step_bytes)},
         "e2e": {"value": e2e_v, "unit": UNIT, "h2d_bytes_per_step": 8 * args.batch, "d2h_bytes_per_step": 8 * args.batch},
-        "gpu_launches": dec.launches_per_step() * args.steps,
+        "gpu_launches": dec.launches_per_step() * args.steps * world,
         "clocks": clk,
         "setup_s": round(setup_s, 1),
     }

@@ -176,8 +176,10 @@ enum nova_nf4_epilogue {
     NOVA_NF4_SILU_MUL = 2, /* rows interleaved per 16-row tile: 8 gate rows, then the 8
                               matching up rows; out[:, n] = fp16(silu(fp16 gate)) * fp16 up,
                               out has N/2 columns (LeanMLP act_fn(gate) * up)              */
-    NOVA_NF4_ARGMAX = 3    /* PLAIN, plus atomicMax of a packed (fp16 logit, -index) key
+    NOVA_NF4_ARGMAX = 3,   /* PLAIN, plus atomicMax of a packed (fp16 logit, -index) key
                               into argmax[m] (uint64, zero before the call): greedy token  */
+    NOVA_NF4_F32 = 4       /* out is fp32 [M, out_stride]: the accumulators unrounded, the
+                              partial sum of one tensor-parallel rank before the all-reduce */
 };
 
 /* Workspace bytes for nova_nf4_gemv with N output rows on the current device
@@ -283,6 +285,16 @@ NOVA_API int nova_rmsnorm(const void* x, int64_t x_stride, const void* residual_
                           int64_t rows, int64_t n, double eps, void* stream);
 
 /*
+ * residual[r, i] = fp16(residual[r, i] + fp16(x[r, i])) for fp32 x (strides in
+ * elements): the decoder residual add after the tensor-parallel all-reduce of
+ * the o_proj / down_proj partial sums, rounded like the single-GPU residual
+ * epilogue.  rows <= 65535.  Replaces the residual adds of
+ * LeanDecoderLayer.forward (src/nova/layers.py:213, :218) on the sharded path.
+ */
+NOVA_API int nova_residual_add_f32(const void* x, int64_t x_stride, void* residual, int64_t r_stride, int64_t rows,
+                                   int64_t n, void* stream);
+
+/*
  * The decoder's per-head step after the fused q/k/v projection, one launch:
  * qkv row m = [q (q_heads*128) | k (kv_heads*128) | v (kv_heads*128)] fp16;
  * q heads -> q_norm, RoPE at position *pos -> q_out; k heads -> k_norm, RoPE;
@@ -319,6 +331,48 @@ typedef struct nova_qk_args {
 } nova_qk_args;
 
 NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
+
+/* --------------------------------------------------- tensor parallelism */
+
+/*
+ * All-reduce of the tensor-parallel partial sums of o_proj / down_proj fused
+ * with the decoder residual add, over NVLink peer memory:
+ *     residual = fp16(residual + fp16(sum over ranks of partial))
+ * with the rank sum taken in rank order, so every rank computes identical
+ * bits.  Each rank allocates a receive buffer of nova_tp_recv_bytes() bytes
+ * (zeroed), shares it with nova_ipc_handle / nova_ipc_open, and passes every
+ * rank's buffer (its own included) in recv[0..world-1], in rank order.  The
+ * call stores this rank's partial, stamped with a device epoch (advanced by
+ * the call itself, so graph replays work), into every buffer and polls its
+ * own buffer until every rank's stamped values have arrived; a wait that
+ * exceeds timeout_ns (default 2 s) sets *err to 1 and leaves the rest of the
+ * residual unchanged instead of hanging.  Every rank must make the same
+ * sequence of calls.  n even; epoch (int64), counter (uint32) and err (int32)
+ * are device words of this rank, zeroed once.  Replaces the residual adds of
+ * src/nova/layers.py:213, :218 on the sharded path; the all-reduce itself has
+ * no counterpart in the single-GPU reference.
+ */
+typedef struct nova_tp_allreduce_args {
+    const void* partial;      /* fp32 [rows, n], contiguous, 8-byte aligned    */
+    void* residual;           /* fp16 [rows, res_stride]                       */
+    int64_t res_stride;
+    void* recv[8];            /* receive buffer of every rank, in rank order   */
+    int64_t* epoch;
+    void* counter;
+    int* err;
+    int64_t rows, n, rank, world;
+    int64_t timeout_ns;       /* 0 = 2 s                                       */
+} nova_tp_allreduce_args;
+
+NOVA_API int nova_tp_recv_bytes(int64_t world, int64_t rows, int64_t n, int64_t* bytes);
+NOVA_API int nova_tp_allreduce_add(const nova_tp_allreduce_args* args, void* stream);
+
+/* CUDA IPC of a device buffer: handle (64 bytes) + offset of ptr inside its
+ * allocation; open maps a peer's buffer into this process (returns the
+ * buffer pointer and the mapping base to pass to nova_ipc_close). */
+NOVA_API int nova_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+NOVA_API int nova_ipc_open(const void* handle, int64_t offset, void** ptr, void** base);
+NOVA_API int nova_ipc_close(void* base);
 
 #ifdef __cplusplus
 }

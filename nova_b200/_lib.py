@@ -15,7 +15,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().with_name("libnova_b200.so")
 
 NOVA_OK, NOVA_ERR_INVALID, NOVA_ERR_ALIGN, NOVA_ERR_UNSUPPORTED, NOVA_ERR_CUDA = range(5)
-NF4_PLAIN, NF4_RESIDUAL, NF4_SILU_MUL, NF4_ARGMAX = range(4)
+NF4_PLAIN, NF4_RESIDUAL, NF4_SILU_MUL, NF4_ARGMAX, NF4_F32 = range(5)
 NOVA_ATTN_NOALLOC_SCRATCH_BYTES = 4 << 20   # built-in scratch of nova_attn_decode_int8_noalloc
 
 _P = ctypes.c_void_p
@@ -64,6 +64,15 @@ class QKArgs(ctypes.Structure):
     ]
 
 
+class TPAllReduceArgs(ctypes.Structure):
+    """Mirror of ``nova_tp_allreduce_args``."""
+
+    _fields_ = [
+        ("partial", _P), ("residual", _P), ("res_stride", _I), ("recv", _P * 8), ("epoch", _P), ("counter", _P),
+        ("err", _P), ("rows", _I), ("n", _I), ("rank", _I), ("world", _I), ("timeout_ns", _I),
+    ]
+
+
 # name -> argtypes (every entry point returns int status unless noted)
 _SIGNATURES: dict[str, list] = {
     "nova_kv_quant_int8": [_P, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P],
@@ -82,6 +91,12 @@ _SIGNATURES: dict[str, list] = {
     "nova_nf4_pack_native": [_P, _P, _i, _P, _I, _I, _P],
     "nova_set_launch_flags": [_i],
     "nova_rmsnorm": [_P, _I, _P, _I, _P, _I, _P, _P, _I, _I, _I, ctypes.c_double, _P],
+    "nova_residual_add_f32": [_P, _I, _P, _I, _I, _I, _P],
+    "nova_tp_recv_bytes": [_I, _I, _I, ctypes.POINTER(_I)],
+    "nova_tp_allreduce_add": [ctypes.POINTER(TPAllReduceArgs), _P],
+    "nova_ipc_handle": [_P, _P, ctypes.POINTER(_I)],
+    "nova_ipc_open": [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)],
+    "nova_ipc_close": [_P],
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
 }
 _STRING_FNS = ("nova_version", "nova_last_error")

@@ -45,7 +45,7 @@ constexpr int UNIT_ROWS = 32;
 constexpr int UNIT_CODE_BYTES = 1024;
 constexpr int UNIT_BYTES = 1088;
 
-enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3 };
+enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_F32 = 4 };
 
 struct Params {
     const __half* x;          // fp16 [M, K] (the residual when norm_w != nullptr)
@@ -100,6 +100,17 @@ __device__ __forceinline__ unsigned long long argmax_key(__half v, int idx) {
 // and 16*tile+g+8 (c[2], c[3]) for batch rows m = 2t, 2t+1.
 template <int EPI>
 __device__ __forceinline__ void epilogue(const Params& p, int tile, const float (&c)[4], int g, int t) {
+    if (EPI == EPI_F32) {   // fp32 accumulators as they are (tensor-parallel partial sums)
+        float* o = reinterpret_cast<float*>(p.out);
+#pragma unroll
+        for (int hrow = 0; hrow < 2; ++hrow)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int m = 2 * t + e;
+                if (m < p.M) o[m * p.out_stride + tile * 16 + g + 8 * hrow] = c[2 * hrow + e];
+            }
+        return;
+    }
     if (EPI == EPI_SILU_MUL) {
         // tile rows 0..7 are gate rows 8*tile+g, rows 8..15 the matching up rows
         const int n = tile * 8 + g;
@@ -981,7 +992,9 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     if (!a->x || !a->packed || (!native && !a->absmax) || !a->lut || !a->out || !a->workspace)
         return fail(NOVA_ERR_INVALID, "NULL pointer");
     const int epi = int(a->epilogue);
-    if (epi < EPI_PLAIN || epi > EPI_ARGMAX) return fail(NOVA_ERR_INVALID, "bad epilogue %d", epi);
+    if (epi < EPI_PLAIN || epi > EPI_F32) return fail(NOVA_ERR_INVALID, "bad epilogue %d", epi);
+    if (epi == EPI_F32 && (reinterpret_cast<uintptr_t>(a->out) % 4))
+        return fail(NOVA_ERR_ALIGN, "the fp32 epilogue needs a 4-byte aligned out");
     if (epi == EPI_RESIDUAL && !a->residual) return fail(NOVA_ERR_INVALID, "residual epilogue needs residual");
     if (epi == EPI_ARGMAX && !a->argmax) return fail(NOVA_ERR_INVALID, "argmax epilogue needs argmax");
     if (epi != EPI_PLAIN && a->bias) return fail(NOVA_ERR_UNSUPPORTED, "bias only with the plain epilogue");
@@ -1033,12 +1046,12 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     cudaError_t err;
     if (native) {
         using NKern = void (*)(Params, int, int*);
-        static const NKern kernels[2][4] = {
+        static const NKern kernels[2][5] = {
             {nf4_gemv_native_kernel<0, false>, nf4_gemv_native_kernel<1, false>, nf4_gemv_native_kernel<2, false>,
-             nf4_gemv_native_kernel<3, false>},
+             nf4_gemv_native_kernel<3, false>, nf4_gemv_native_kernel<4, false>},
             {nf4_gemv_native_kernel<0, true>, nf4_gemv_native_kernel<1, true>, nf4_gemv_native_kernel<2, true>,
-             nf4_gemv_native_kernel<3, true>}};
-        static int64_t smem_set[2][4] = {};
+             nf4_gemv_native_kernel<3, true>, nf4_gemv_native_kernel<4, true>}};
+        static int64_t smem_set[2][5] = {};
         static int optin = 0;
         if (!optin) {
             int dev = 0;
@@ -1084,12 +1097,12 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
             err = launch(kern, dim3(grid), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p, int(stage_units),
                          errp);
         } else {   // CTA-level split-K
-            static const NKern cta_kernels[2][4] = {
+            static const NKern cta_kernels[2][5] = {
                 {nf4_gemv_cta_kernel<0, false>, nf4_gemv_cta_kernel<1, false>, nf4_gemv_cta_kernel<2, false>,
-                 nf4_gemv_cta_kernel<3, false>},
+                 nf4_gemv_cta_kernel<3, false>, nf4_gemv_cta_kernel<4, false>},
                 {nf4_gemv_cta_kernel<0, true>, nf4_gemv_cta_kernel<1, true>, nf4_gemv_cta_kernel<2, true>,
-                 nf4_gemv_cta_kernel<3, true>}};
-            static int64_t cta_smem_set[2][4] = {};
+                 nf4_gemv_cta_kernel<3, true>, nf4_gemv_cta_kernel<4, true>}};
+            static int64_t cta_smem_set[2][5] = {};
             const int64_t red_bytes = int64_t(NAT_WARPS) * 32 * 32;
             const int64_t cu = std::min<int64_t>(4, (optin - int64_t(LUT_BYTES) - xs_bytes - red_bytes - slack) / ring_unit);
             if (cu < 1)
@@ -1104,12 +1117,12 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
                          int(cu), errp);
         }
     } else {
-        static const Kern kernels[2][4] = {
+        static const Kern kernels[2][5] = {
             {nf4_gemv_ref_kernel<__half, 0>, nf4_gemv_ref_kernel<__half, 1>, nf4_gemv_ref_kernel<__half, 2>,
-             nf4_gemv_ref_kernel<__half, 3>},
+             nf4_gemv_ref_kernel<__half, 3>, nf4_gemv_ref_kernel<__half, 4>},
             {nf4_gemv_ref_kernel<float, 0>, nf4_gemv_ref_kernel<float, 1>, nf4_gemv_ref_kernel<float, 2>,
-             nf4_gemv_ref_kernel<float, 3>}};
-        static int64_t smem_set[2][4] = {};
+             nf4_gemv_ref_kernel<float, 3>, nf4_gemv_ref_kernel<float, 4>}};
+        static int64_t smem_set[2][5] = {};
         const int ai = a->absmax_fp32 ? 1 : 0;
         Kern kern = kernels[ai][epi];
         if (int rc = prepare_smem(kern, smem, &smem_set[ai][epi])) return rc;

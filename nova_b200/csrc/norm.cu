@@ -57,6 +57,20 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __half* __res
     }
 }
 
+// resid = fp16(resid + fp16(x)) for an fp32 x: the residual add after the
+// all-reduce of tensor-parallel partial sums, rounded like the single-GPU
+// epilogue (fp16 projection output, then the fp16 add).
+__global__ void residual_add_f32_kernel(const float* __restrict__ x, int64_t xs, __half* __restrict__ r, int64_t rs,
+                                        int n) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t row = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float o = __half2float(__float2half_rn(x[row * xs + i]));
+        r[row * rs + i] = __float2half_rn(__half2float(r[row * rs + i]) + o);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // One CTA per (batch row, head) over q heads then kv heads; 128 threads = one
 // per channel.  q heads: q_norm + RoPE -> q_out.  kv heads: k_norm + RoPE on
@@ -235,6 +249,21 @@ extern "C" int nova_qk_norm_rope_append(const nova_qk_args* a, void* stream) {
     if (err != cudaSuccess) {
         cudaGetLastError();
         return fail(NOVA_ERR_CUDA, "nova_qk_norm_rope_append: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
+}
+
+extern "C" int nova_residual_add_f32(const void* x, int64_t x_stride, void* residual, int64_t r_stride, int64_t rows,
+                                     int64_t n, void* stream) {
+    if (rows < 0 || n <= 0 || n > (1 << 24) || rows > 65535) return fail(NOVA_ERR_INVALID, "bad rows/n");
+    if (!x || !residual) return fail(NOVA_ERR_INVALID, "NULL pointer");
+    if (rows == 0) return NOVA_OK;
+    const unsigned blocks = unsigned(std::min<int64_t>((n + 255) / 256, 64));
+    const cudaError_t err = launch(norm::residual_add_f32_kernel, dim3(blocks, unsigned(rows)), dim3(256), 0,
+                                   (cudaStream_t)stream, (const float*)x, x_stride, (__half*)residual, r_stride, int(n));
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_residual_add_f32: launch failed: %s", cudaGetErrorString(err));
     }
     return NOVA_OK;
 }

@@ -22,6 +22,12 @@ q|k|v are concatenated row-wise and gate|up are interleaved per 16-row tile
 (8 gate rows, then the same 8 up rows) so one GEMV produces SiLU(gate)*up.
 The tied lm_head is the NF4 copy of ``embed_tokens`` (src/nova/loader.py:67-119).
 
+Tensor parallelism (``tp=TPContext(rank, world, group)``): each rank holds
+its KV heads and intermediate slice (``nova_b200.tp``); o_proj and down_proj
+write fp32 partial sums (``NOVA_NF4_F32``), an NCCL all-reduce inside the
+graph sums them and ``nova_residual_add_f32`` adds them to the replicated
+residual stream: 8 launches per layer of this library plus 2 all-reduces.
+
 Prefill (not the hot path) runs the reference's math eagerly on the GPU:
 NF4 -> fp16 dequant + fp16 matmul, fp16 SDPA with the causal mask, then the
 complete 64-token groups of every layer's K/V are quantized with
@@ -41,6 +47,7 @@ from . import _lib
 from .kernels import build_nf4_lut, fused_rms_norm, gemv_workspace, nf4_gemv, pack_native
 from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention
 from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
+from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
 
 
 @dataclass
@@ -207,32 +214,42 @@ class NovaDecoder:
     """
 
     def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
-                 device="cuda", pdl: bool = True) -> None:
+                 device="cuda", pdl: bool = True, tp: TPContext | None = None) -> None:
         cfg = weights.cfg
         if batch < 1 or batch > 8:
             raise ValueError("the GEMV decode path handles batch 1..8")
-        self.w = weights
+        self.tp = tp if tp is not None else TPContext()
+        sr = shard_ranges(cfg, self.tp.rank, self.tp.world)
+        self.w = shard_weights(weights, self.tp.rank, self.tp.world) if self.tp.active else weights
         self.cfg = cfg
+        # this rank's dimensions (the whole model without tensor parallelism)
+        self.hq = sr.q_heads[1] - sr.q_heads[0]
+        self.hkv = sr.kv_heads[1] - sr.kv_heads[0]
+        self.q_dim, self.kv_dim = self.hq * cfg.head_dim, self.hkv * cfg.head_dim
+        self.inter = sr.inter[1] - sr.inter[0]
         self.batch = int(batch)
         self.max_len = int(max_len)
         self.device = torch.device(device)
         if chunk is None:
             chunk = self._pick_chunk()
-        self.cache = KVInt8Cache(num_slots=cfg.num_hidden_layers, num_kv_heads=cfg.num_key_value_heads,
-                                 head_dim=cfg.head_dim, max_len=self.max_len, num_q_heads=cfg.num_attention_heads,
+        self.cache = KVInt8Cache(num_slots=cfg.num_hidden_layers, num_kv_heads=self.hkv,
+                                 head_dim=cfg.head_dim, max_len=self.max_len, num_q_heads=self.hq,
                                  batch=self.batch, device=self.device, chunk=chunk)
         self.lut = build_nf4_lut(weights.code if weights.code is not None else nf4_codebook()).to(self.device)
         self.cos, self.sin = rope_tables(self.max_len + 1, cfg.head_dim, cfg.rope_theta, self.device)
         B, dev, f16 = self.batch, self.device, torch.float16
         self.resid = torch.zeros(B, cfg.hidden_size, dtype=f16, device=dev)
-        self.qkv = torch.zeros(B, cfg.q_dim + 2 * cfg.kv_dim, dtype=f16, device=dev)
-        self.q_rot = torch.zeros(B, cfg.q_dim, dtype=f16, device=dev)
-        self.attn = torch.zeros(B, cfg.q_dim, dtype=f16, device=dev)
-        self.act = torch.zeros(B, cfg.intermediate_size, dtype=f16, device=dev)
+        self.qkv = torch.zeros(B, self.q_dim + 2 * self.kv_dim, dtype=f16, device=dev)
+        self.q_rot = torch.zeros(B, self.q_dim, dtype=f16, device=dev)
+        self.attn = torch.zeros(B, self.q_dim, dtype=f16, device=dev)
+        self.act = torch.zeros(B, self.inter, dtype=f16, device=dev)
+        self.part32 = torch.zeros(B, cfg.hidden_size, dtype=torch.float32, device=dev) if self.tp.active else None
+        self.p2p = (P2PAllReduce(self.tp, B, cfg.hidden_size, dev)
+                    if self.tp.active and self.tp.allreduce == "p2p" else None)
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=f16, device=dev)
         self.argmax_slot = torch.zeros(B, dtype=torch.int64, device=dev)
         self.input_ids = torch.zeros(B, dtype=torch.int64, device=dev)
-        n_max = max(cfg.vocab_size, 2 * cfg.intermediate_size, cfg.q_dim + 2 * cfg.kv_dim, cfg.hidden_size)
+        n_max = max(cfg.vocab_size, 2 * self.inter, self.q_dim + 2 * self.kv_dim, cfg.hidden_size)
         self.gemv_ws = gemv_workspace(dev, n_max).clone()   # shared by every GEMV of the step
         self.graph: torch.cuda.CUDAGraph | None = None
         self.pdl = bool(pdl)
@@ -240,7 +257,7 @@ class NovaDecoder:
     def _pick_chunk(self) -> int:
         """Split size for the attention: about two CTAs per SM at full capacity."""
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        per_head = max(1, (2 * sms) // (self.batch * self.cfg.num_key_value_heads))
+        per_head = max(1, (2 * sms) // (self.batch * self.hkv))
         chunk = -(-self.max_len // per_head)
         chunk = max(GROUP_T * 4, -(-chunk // GROUP_T) * GROUP_T)
         return chunk
@@ -254,6 +271,16 @@ class NovaDecoder:
     def _linear16(self, x: torch.Tensor, w: NF4Weight) -> torch.Tensor:
         w16 = dequantize_nf4(w.packed, w.absmax, self.lut)
         return torch.matmul(x, w16.t())
+
+    def _row_parallel(self, x: torch.Tensor, w: NF4Weight) -> torch.Tensor:
+        """o_proj / down_proj: one matmul, or with tensor parallelism the fp32
+        partial sums of every rank all-reduced and rounded to fp16 once."""
+        if not self.tp.active:
+            return self._linear16(x, w)
+        w16 = dequantize_nf4(w.packed, w.absmax, self.lut)
+        part = torch.matmul(x.float(), w16.float().t())
+        all_reduce_sum(part, self.tp)
+        return part.to(torch.float16)
 
     @torch.inference_mode()
     def prefill(self, input_ids: torch.Tensor) -> torch.Tensor:
@@ -269,15 +296,16 @@ class NovaDecoder:
         ids = input_ids.to(self.device)
         h = self.w.embed[ids]                                     # [B, T, H]
         cos, sin = self.cos[:T][None, None], self.sin[:T][None, None]
-        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        hq, hkv, d = self.hq, self.hkv, cfg.head_dim
+        qd, kvd = self.q_dim, self.kv_dim
         q_full = (T // GROUP_T) * GROUP_T
         stream = _lib.stream_of(self.device)
         for li, lw in enumerate(self.w.layers):
             x = fused_rms_norm(h, lw.input_ln, cfg.rms_norm_eps)
             qkv = self._linear16(x, lw.qkv)
-            q = qkv[..., :cfg.q_dim].reshape(B, T, hq, d)
-            k = qkv[..., cfg.q_dim:cfg.q_dim + cfg.kv_dim].reshape(B, T, hkv, d)
-            v = qkv[..., cfg.q_dim + cfg.kv_dim:].reshape(B, T, hkv, d).transpose(1, 2)
+            q = qkv[..., :qd].reshape(B, T, hq, d)
+            k = qkv[..., qd:qd + kvd].reshape(B, T, hkv, d)
+            v = qkv[..., qd + kvd:].reshape(B, T, hkv, d).transpose(1, 2)
             q = fused_rms_norm(q, lw.q_norm, cfg.rms_norm_eps).transpose(1, 2)
             k = fused_rms_norm(k, lw.k_norm, cfg.rms_norm_eps).transpose(1, 2)
             q = q * cos + _rotate_half(q) * sin
@@ -286,13 +314,13 @@ class NovaDecoder:
             gq = hq // hkv
             o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
                                                is_causal=True, scale=d ** -0.5)
-            o = o.transpose(1, 2).reshape(B, T, cfg.q_dim)
-            h = h + self._linear16(o, lw.o)
+            o = o.transpose(1, 2).reshape(B, T, qd)
+            h = h + self._row_parallel(o, lw.o)
             x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
             gu = self._linear16(x, lw.gate_up).view(B, T, -1, 2, 8)
             gate = gu[:, :, :, 0].reshape(B, T, -1)
             up = gu[:, :, :, 1].reshape(B, T, -1)
-            h = h + self._linear16(F.silu(gate) * up, lw.down)
+            h = h + self._row_parallel(F.silu(gate) * up, lw.down)
             # int8 cache: complete groups quantized, the rest into the ring
             if q_full:
                 for src, dst, mn, st in ((k, cache.kq[li], cache.kmn[li], cache.kst[li]),
@@ -324,9 +352,24 @@ class NovaDecoder:
         eps = cfg.rms_norm_eps
         B = self.batch
         stream = _lib.stream_of(self.device)
-        q3 = self.q_rot.view(B, cfg.num_attention_heads, cfg.head_dim)
-        a3 = self.attn.view(B, cfg.num_attention_heads, cfg.head_dim)
+        q3 = self.q_rot.view(B, self.hq, cfg.head_dim)
+        a3 = self.attn.view(B, self.hq, cfg.head_dim)
         ws = self.gemv_ws
+        tp = self.tp
+
+        def row_parallel(x, w):   # o_proj / down_proj + residual add
+            if not tp.active:
+                nf4_gemv(x, w.units, None, lut, self.resid, epilogue=_lib.NF4_RESIDUAL, residual=self.resid,
+                         workspace=ws, n=w.n)
+                return
+            nf4_gemv(x, w.units, None, lut, self.part32, epilogue=_lib.NF4_F32, workspace=ws, n=w.n)
+            if self.p2p is not None:   # fused NVLink all-reduce + residual add
+                self.p2p(self.part32, self.resid)
+                return
+            all_reduce_sum(self.part32, tp)
+            _lib.call("nova_residual_add_f32", self.part32.data_ptr(), self.part32.stride(0), self.resid.data_ptr(),
+                      self.resid.stride(0), B, cfg.hidden_size, stream)
+
         for li, lw in enumerate(self.w.layers):
             nf4_gemv(self.resid, lw.qkv.units, None, lut, self.qkv, norm_weight=lw.input_ln, eps=eps,
                      workspace=ws, n=lw.qkv.n)
@@ -341,26 +384,33 @@ class NovaDecoder:
             qa.vmn, qa.vst = cache.vmn[li].data_ptr(), cache.vst[li].data_ptr()
             qa.pos, qa.written = cache.pos.data_ptr(), cache._written.data_ptr()
             qa.qlen, qa.pg = cache._qlen.data_ptr(), cache._pg.data_ptr()
-            qa.batch, qa.q_heads, qa.kv_heads = B, cfg.num_attention_heads, cfg.num_key_value_heads
+            qa.batch, qa.q_heads, qa.kv_heads = B, self.hq, self.hkv
             qa.head_dim, qa.max_len, qa.group = cfg.head_dim, self.max_len, GROUP_T
             _lib.check(_lib.lib().nova_qk_norm_rope_append(_lib.ctypes.byref(qa), stream), "qk_norm_rope_append")
             launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
                                   cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
                              n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window)
-            nf4_gemv(self.attn, lw.o.units, None, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
-                     residual=self.resid, workspace=ws, n=lw.o.n)
+            row_parallel(self.attn, lw.o)
             nf4_gemv(self.resid, lw.gate_up.units, None, lut, self.act, epilogue=_lib.NF4_SILU_MUL,
                      norm_weight=lw.post_ln, eps=eps, workspace=ws, n=lw.gate_up.n)
-            nf4_gemv(self.act, lw.down.units, None, lut, self.resid, epilogue=_lib.NF4_RESIDUAL,
-                     residual=self.resid, workspace=ws, n=lw.down.n)
+            row_parallel(self.act, lw.down)
         hw = self.w.lm_head
         nf4_gemv(self.resid, hw.units, None, lut, self.logits, epilogue=_lib.NF4_ARGMAX,
                  norm_weight=self.w.final_norm, eps=eps, argmax=self.argmax_slot, token_out=self.input_ids,
                  pos=cache.pos, embed=self.w.embed, embed_out=self.resid, workspace=ws, n=hw.n)
 
+    def close(self) -> None:
+        """Release the graph and the peer mappings of the tensor-parallel
+        all-reduce (before the process group is destroyed)."""
+        self.graph = None
+        if self.p2p is not None:
+            torch.cuda.synchronize(self.device)
+            self.p2p.close()
+
     def launches_per_step(self) -> int:
-        return 6 * self.cfg.num_hidden_layers + 1
+        """Kernels of this library per step (the NCCL all-reduces not counted)."""
+        return (8 if self.tp.active else 6) * self.cfg.num_hidden_layers + 1
 
     @torch.inference_mode()
     def step_eager(self) -> torch.Tensor:
@@ -375,6 +425,8 @@ class NovaDecoder:
         programmatic dependencies: each one's weight prefetch and LUT build
         overlap the previous kernel."""
         self.graph = None
+        if self.tp.active:   # the communicator must exist before its first captured collective
+            all_reduce_sum(torch.zeros_like(self.part32), self.tp)
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         prev = _lib.pdl_enabled()
