@@ -21,7 +21,7 @@ import torch
 from . import _lib
 from .decoder import interleave_gate_up
 from .kernels import build_nf4_lut, gemv_workspace, nf4_gemv, pack_native
-from .kvattn import GROUP_T, launch_attention, new_workspace
+from .kvattn import GROUP_T, launch_attention, new_workspace, pick_chunk
 from .quant import nf4_codebook, quantize_nf4
 
 EPI = {"plain": _lib.NF4_PLAIN, "residual": _lib.NF4_RESIDUAL, "silu": _lib.NF4_SILU_MUL, "argmax": _lib.NF4_ARGMAX}
@@ -100,9 +100,7 @@ def bench_attn(ctx: int, batch: int = 1, q_heads: int = 32, kv_heads: int = 8, w
     per_set = batch * kv_heads * max_len * 2 * d
     sets = sets or max(2, min(32, (768 << 20) // per_set + 1))
     if not chunk:
-        sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        per_head = max(1, (2 * sms) // (batch * kv_heads))
-        chunk = max(GROUP_T * 4, -(-(-(-max_len // per_head)) // GROUP_T) * GROUP_T)
+        chunk = pick_chunk(max_len, batch, kv_heads, q_heads, torch.cuda.get_device_properties(dev).multi_processor_count)
     n_splits = -(-max_len // chunk)
     g = torch.Generator(device=dev).manual_seed(seed)
     ng = -(-max_len // GROUP_T)

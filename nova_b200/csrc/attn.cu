@@ -309,6 +309,23 @@ __global__ void __launch_bounds__(THREADS, 3)
     pdl_trigger();
     pdl_wait();   // q, the cache and the lengths come from the previous kernels
 
+    // Speculative first load, issued before the lengths are read: the group
+    // this warp takes first when no prefix is masked (every group of the
+    // chunk lies inside the cache allocation, so the copy is always in bounds).
+    uint8_t* stage = smem + warp * STAGE;
+    uint64_t* bar = &bars[warp];
+    const int spec = int(int64_t(split) * p.chunk / GT) + warp;
+    const bool spec_on = split < p.n_splits && spec < p.groups &&
+                         int64_t(spec) * GT < int64_t(split) * p.chunk + p.chunk;
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        if (spec_on) issue_group(p, &tmK, &tmV, stage, bar, bh, spec);
+    }
+    __syncwarp();
+    uint32_t phase = 0;        // completed waits on bar
+    bool pending = spec_on;    // a copy is in flight on bar
+
     const int64_t qlen = *p.qlen, pgv = *p.pg;
     const int64_t written = p.written ? *p.written : qlen;
     const int64_t first = p.first ? *p.first : 0;
@@ -346,31 +363,39 @@ __global__ void __launch_bounds__(THREADS, 3)
         const int64_t t_end = min(int64_t(split) * p.chunk + p.chunk, pend);
         if (t_begin < t_end) {
             const int g_first = int(t_begin / GT), g_last = int((t_end - 1) / GT);
-            uint8_t* stage = smem + warp * STAGE;
-            uint64_t* bar = &bars[warp];
             int gi = g_first + warp;
             if (gi <= g_last) {
-                if (lane == 0) {
-                    mbar_init(bar, 1);
-                    fence_mbar_init();
-                    issue_group(p, &tmK, &tmV, stage, bar, bh, gi);
+                if (!(pending && spec == gi)) {   // masked prefix: drain the speculative copy, load gi
+                    if (pending) {
+                        mbar_wait(bar, phase & 1u, p.err, 1);
+                        ++phase;
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        fence_proxy_async();
+                        issue_group(p, &tmK, &tmV, stage, bar, bh, gi);
+                    }
+                    pending = true;
                 }
-                __syncwarp();
-                uint32_t parity = 0;
                 for (; gi <= g_last; gi += NW) {
-                    if (!mbar_wait(bar, parity, p.err, 1)) break;
-                    parity ^= 1u;
+                    if (!mbar_wait(bar, phase & 1u, p.err, 1)) break;
+                    ++phase;
+                    pending = false;
                     process_group(stage, gi * GT, int(t_begin), int(t_end), qf, p.scale_log2, acc, m_run, l_run,
                                   g, t);
                     __syncwarp();
-                    if (lane == 0 && gi + NW <= g_last) {
-                        fence_proxy_async();
-                        issue_group(p, &tmK, &tmV, stage, bar, bh, gi + NW);
+                    if (gi + NW <= g_last) {
+                        if (lane == 0) {
+                            fence_proxy_async();
+                            issue_group(p, &tmK, &tmV, stage, bar, bh, gi + NW);
+                        }
+                        pending = true;
                     }
                     __syncwarp();
                 }
             }
         }
+        if (pending) mbar_wait(bar, phase & 1u, p.err, 1);   // a copy nobody used must land before exit
     } else {
         int64_t tlo = max(lo, qlen);
         process_tail_tile(p, bh, warp, u, tlo, qf, acc, m_run, l_run, g, t);
@@ -429,60 +454,83 @@ __global__ void __launch_bounds__(THREADS, 3)
     if (!sm_last) return;
     __threadfence();
 
-    // ---- last CTA of this (batch, kv head): merge all splits.  Every (m, l)
-    // pair is fetched at once into shared memory (the stages are free now);
-    // warp hh then turns its head's maxima into weights and sums the
-    // accumulators in split order, eight loads in flight per lane.
-    const int n_ml = p.s_total * p.gq;
-    float2* ml = reinterpret_cast<float2*>(smem);
-    const bool parallel = n_ml * int(sizeof(float2)) <= NW * STAGE;
-    if (parallel) {
-        for (int i = threadIdx.x; i < n_ml; i += THREADS)
+    // ---- last CTA of this (batch, kv head): merge all splits.  When the
+    // partials of the head fit in the (now idle) stage memory, one bulk copy
+    // brings them all in and warp hh merges its head from shared memory:
+    // weights from the split maxima, then the accumulators in split order.
+    // Otherwise the partials are read from global memory split by split.
+    const int64_t part_bytes = int64_t(p.s_total) * p.gq * PART * 4;
+    const bool staged = part_bytes <= NW * STAGE;
+    const float* src_base = part_bh;
+    if (staged) {
+        __shared__ __align__(8) uint64_t bar_comb;
+        if (threadIdx.x == 0) {
+            mbar_init(&bar_comb, 1);
+            fence_mbar_init();
+            asm volatile("fence.proxy.async.global;" ::: "memory");   // the partials were written by other CTAs
+            fence_proxy_async();   // and this CTA's merge buffer in the same shared memory was written generically
+            mbar_arrive_expect_tx(&bar_comb, uint32_t(part_bytes));
+            bulk_g2s(smem, part_bh, uint32_t(part_bytes), &bar_comb);
+        }
+        __syncthreads();
+        mbar_wait(&bar_comb, 0u, p.err, 4);
+        src_base = reinterpret_cast<const float*>(smem);
+    } else {   // every (m, l) pair at once into shared memory (host checks s_total * gq <= 9216)
+        float2* ml = reinterpret_cast<float2*>(smem);
+        for (int i = threadIdx.x; i < p.s_total * p.gq; i += THREADS)
             ml[i] = __ldcg(reinterpret_cast<const float2*>(part_bh + int64_t(i) * PART));
         __syncthreads();
     }
     if (hh < p.gq) {
         float M = -INFINITY, L = 0.f;
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (parallel) {
-            for (int s = lane; s < p.s_total; s += 32) M = fmaxf(M, ml[s * p.gq + hh].x);
+        if (staged) {
+            float* sp = reinterpret_cast<float*>(smem);
+            for (int s2 = lane; s2 < p.s_total; s2 += 32) M = fmaxf(M, sp[(s2 * p.gq + hh) * PART]);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
             if (M != -INFINITY) {
-                for (int s = lane; s < p.s_total; s += 32) {
-                    const float2 v = ml[s * p.gq + hh];
-                    const float wt = v.x == -INFINITY ? 0.f : exp2f(v.x - M);
-                    ml[s * p.gq + hh].x = wt;
+                for (int s2 = lane; s2 < p.s_total; s2 += 32) {
+                    float* e = sp + (s2 * p.gq + hh) * PART;
+                    e[2] = e[0] == -INFINITY ? 0.f : exp2f(e[0] - M);   // weight into the pad slot
                 }
                 __syncwarp();
-                for (int s = 0; s < p.s_total; ++s) L += ml[s * p.gq + hh].x * ml[s * p.gq + hh].y;
-                for (int s0 = 0; s0 < p.s_total; s0 += 8) {
-                    float4 a[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if (s0 + k < p.s_total && ml[(s0 + k) * p.gq + hh].x != 0.f)
-                            a[k] = __ldcg(reinterpret_cast<const float4*>(part_bh + (int64_t(s0 + k) * p.gq + hh) *
-                                                                                       PART + 4 + d0));
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        if (s0 + k >= p.s_total) break;
-                        const float wt = ml[(s0 + k) * p.gq + hh].x;
-                        if (wt == 0.f) continue;
-                        o.x += wt * a[k].x; o.y += wt * a[k].y; o.z += wt * a[k].z; o.w += wt * a[k].w;
-                    }
+                for (int s2 = 0; s2 < p.s_total; ++s2) {
+                    const float* e = sp + (s2 * p.gq + hh) * PART;
+                    const float wt = e[2];
+                    if (wt == 0.f) continue;
+                    L += wt * e[1];
+                    const float4 a = *reinterpret_cast<const float4*>(e + 4 + d0);
+                    o.x += wt * a.x; o.y += wt * a.y; o.z += wt * a.z; o.w += wt * a.w;
                 }
             }
-        } else {
-            for (int s = 0; s < p.s_total; ++s) M = fmaxf(M, __ldcg(part_bh + (int64_t(s) * p.gq + hh) * PART));
+        } else {   // (m, l) pairs were fetched into shared memory above; accumulators 8 loads in flight
+            const float2* ml = reinterpret_cast<const float2*>(smem);
+            for (int s2 = lane; s2 < p.s_total; s2 += 32) M = fmaxf(M, ml[s2 * p.gq + hh].x);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
             if (M != -INFINITY) {
-                for (int s = 0; s < p.s_total; ++s) {
-                    const float* src = part_bh + (int64_t(s) * p.gq + hh) * PART;
-                    const float ms = __ldcg(src);
-                    if (ms == -INFINITY) continue;
-                    const float wt = exp2f(ms - M);
-                    L += wt * __ldcg(src + 1);
-                    const float4 a = __ldcg(reinterpret_cast<const float4*>(src + 4 + d0));
-                    o.x += wt * a.x; o.y += wt * a.y; o.z += wt * a.z; o.w += wt * a.w;
+                for (int s0 = 0; s0 < p.s_total; s0 += 8) {
+                    float4 a[8];
+                    float wt[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        wt[k] = 0.f;
+                        if (s0 + k < p.s_total) {
+                            const float2 v = ml[(s0 + k) * p.gq + hh];
+                            if (v.x != -INFINITY) {
+                                wt[k] = exp2f(v.x - M);
+                                a[k] = __ldcg(reinterpret_cast<const float4*>(
+                                    src_base + (int64_t(s0 + k) * p.gq + hh) * PART + 4 + d0));
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        if (wt[k] == 0.f) continue;
+                        L += wt[k] * ml[(s0 + k) * p.gq + hh].y;
+                        o.x += wt[k] * a[k].x; o.y += wt[k] * a[k].y; o.z += wt[k] * a[k].z; o.w += wt[k] * a[k].w;
+                    }
                 }
             }
         }
@@ -543,6 +591,8 @@ extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream)
     if (a->n_splits < 0 || (a->n_splits == 0 && !a->tail_k)) return fail(NOVA_ERR_INVALID, "n_splits must be >= 1");
     if (a->n_splits > 65535 || a->batch > 65535 || a->kv_heads > 65535)
         return fail(NOVA_ERR_INVALID, "grid too large");
+    if ((a->n_splits + 1) * gq > NW * STAGE / 8)
+        return fail(NOVA_ERR_UNSUPPORTED, "n_splits * q_heads/kv_heads must be at most %d", NW * STAGE / 8 - gq);
     if (!a->q || !a->out || !a->qlen || !a->pg || !a->workspace)
         return fail(NOVA_ERR_INVALID, "q/out/qlen/pg/workspace must not be NULL");
     if (a->n_splits && (!a->kq || !a->vq || !a->kmn || !a->kst || !a->vmn || !a->vst))

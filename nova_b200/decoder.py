@@ -45,7 +45,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .kernels import build_nf4_lut, fused_rms_norm, gemv_workspace, nf4_gemv, pack_native
-from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention
+from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk
 from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
 
@@ -255,12 +255,9 @@ class NovaDecoder:
         self.pdl = bool(pdl)
 
     def _pick_chunk(self) -> int:
-        """Split size for the attention: about two CTAs per SM at full capacity."""
+        """Split size for the attention (``kvattn.pick_chunk``)."""
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        per_head = max(1, (2 * sms) // (self.batch * self.hkv))
-        chunk = -(-self.max_len // per_head)
-        chunk = max(GROUP_T * 4, -(-chunk // GROUP_T) * GROUP_T)
-        return chunk
+        return pick_chunk(self.max_len, self.batch, self.hkv, self.hq, sms)
 
     @property
     def pos(self) -> torch.Tensor:

@@ -37,6 +37,18 @@ HEAD_DIM = 128
 MAX_GQ = 4
 
 
+def pick_chunk(max_len: int, batch: int, kv_heads: int, q_heads: int, sms: int = 148) -> int:
+    """Split size (tokens, a multiple of 64, at least 256) for the decode
+    attention at capacity ``max_len``: about two CTAs per SM, and at most
+    ``73728 // (q_heads/kv_heads * 528) - 1`` splits per head, so the last CTA
+    of a head merges all split partials from one shared-memory copy."""
+    gq = max(1, q_heads // kv_heads)
+    per_head = max(1, (2 * sms) // (batch * kv_heads))
+    per_head = min(per_head, 73728 // (gq * 528) - 1)
+    chunk = -(-max_len // per_head)
+    return max(GROUP_T * 4, -(-chunk // GROUP_T) * GROUP_T)
+
+
 def attn_workspace_bytes(batch: int, q_heads: int, kv_heads: int, n_splits: int, has_tail: bool) -> int:
     out = _lib.ctypes.c_int64(0)
     _lib.call("nova_attn_workspace_bytes", int(batch), int(q_heads), int(kv_heads), int(n_splits),
