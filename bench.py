@@ -34,6 +34,14 @@ METRIC = "decode tok/s (Qwen3-VL-4B text, NF4+int8 KV); int8-KV attn HBM GB/s vs
 UNIT = "tok/s"
 
 
+def _workload(args) -> str:
+    """The BASELINE configuration a run measures."""
+    which = ("BASELINE config 4" if (args.batch, args.ctx) == (1, 8192) else
+             "BASELINE config 5" if (args.batch, args.ctx) == (64, 32768) else "custom")
+    return (f"qwen3vl4b-text greedy decode, NF4 weights (blocksize 64, fp16 absmax) incl. 4-bit lm_head, int8 KV "
+            f"(int8t64), batch {args.batch}, ctx {args.ctx} ({which})")
+
+
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -45,6 +53,9 @@ def _args():
     ap.add_argument("--layers", type=int, default=36, help="36 for the headline config")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--kv-fill", choices=["auto", "prefill", "random"], default="auto",
+                    help="context: eager prefill of random tokens, or random int8 codes written straight into the "
+                         "cache (auto: prefill up to batch*ctx = 65536 tokens)")
     ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp",
                     help="N > 1: tensor parallelism over the N GPUs (default) or N independent replicas")
     return ap.parse_args()
@@ -112,17 +123,18 @@ def run_reference(args, rank: int) -> None:
     for _ in range(max(1, args.warmup)):
         s.run()
     times = [s.run() for _ in range(args.steps)]
-    sec_tok = float(np.mean(times)) * s.seconds_scale / args.batch
+    sec_tok = float(np.mean(times)) * s.seconds_scale   # one sequence; the host does B sequences one after another
     v = 1.0 / sec_tok
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": float(np.mean(times)) * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "qwen3vl4b-text decode, NF4 + int8 KV, ctx 8192, batch 1 (BASELINE config 4)",
-                   "ctx": args.ctx, "global_batch": args.batch, "layers": 36, "parallelism": "host cores"},
+        "config": {"workload": _workload(args), "ctx": args.ctx, "global_batch": args.batch, "layers": 36,
+                   "parallelism": "host cores"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
-                         "sample": "per step: 1 decoder layer at ctx 8192 with 1/8 of each linear's rows and of the "
-                                   "KV heads + 1/288 of the lm_head, NF4 dequant per call + fp32 numpy; scaled x288"},
+                         "sample": f"per step: 1 decoder layer at ctx {args.ctx} with 1/8 of each linear's rows and "
+                                   "of the KV heads + 1/288 of the lm_head, NF4 dequant per call + fp32 numpy; "
+                                   "scaled x288 (one sequence; tok/s of a batch is the same on the host)"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -155,19 +167,16 @@ def _time_kernels(dec, reps: int = 10) -> dict:
         part = dec.part32.clone()
 
         def row_par(x, w):
-            nf4_gemv(x, w.units, None, lut, part, epilogue=_lib.NF4_F32, workspace=ws, n=w.n)
+            dec._gemv(x, w, part, epilogue=_lib.NF4_F32)
     else:
         def row_par(x, w):
-            nf4_gemv(x, w.units, None, lut, scratch["resid"], epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"],
-                     workspace=ws, n=w.n)
+            dec._gemv(x, w, scratch["resid"], epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"])
     fams = {
-        "qkv": (lambda lw: nf4_gemv(scratch["resid"], lw.qkv.units, None, lut, scratch["qkv"],
-                                    norm_weight=lw.input_ln, eps=eps, workspace=ws, n=lw.qkv.n),
+        "qkv": (lambda lw: dec._gemv(scratch["resid"], lw.qkv, scratch["qkv"], norm_weight=lw.input_ln),
                 lambda lw: bytes_of(lw.qkv)),
         "o_proj": (lambda lw: row_par(scratch["attn"], lw.o), lambda lw: bytes_of(lw.o)),
-        "gate_up": (lambda lw: nf4_gemv(scratch["resid"], lw.gate_up.units, None, lut, scratch["act"],
-                                        epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln, eps=eps, workspace=ws,
-                                        n=lw.gate_up.n),
+        "gate_up": (lambda lw: dec._gemv(scratch["resid"], lw.gate_up, scratch["act"], epilogue=_lib.NF4_SILU_MUL,
+                                         norm_weight=lw.post_ln),
                     lambda lw: bytes_of(lw.gate_up)),
         "down": (lambda lw: row_par(scratch["act"], lw.down), lambda lw: bytes_of(lw.down)),
     }
@@ -182,9 +191,8 @@ def _time_kernels(dec, reps: int = 10) -> dict:
     hw = dec.w.lm_head
     logits = dec.logits.clone()
     slot = torch.zeros_like(dec.argmax_slot)
-    us = _graph_time(lambda i: nf4_gemv(scratch["resid"], hw.units, None, lut, logits, epilogue=_lib.NF4_ARGMAX,
-                                        norm_weight=dec.w.final_norm, eps=eps, argmax=slot, workspace=ws, n=hw.n),
-                     4, reps)
+    us = _graph_time(lambda i: dec._gemv(scratch["resid"], hw, logits, epilogue=_lib.NF4_ARGMAX,
+                                         norm_weight=dec.w.final_norm, argmax=slot), 4, reps)
     hb = bytes_of(hw)
     out["lm_head"] = {"launches": reps * 4, "ms": us * 1e-3, "bytes": hb, "gbs": hb / (us * 1e-6) / 1e9}
     # int8-KV attention over every layer's cache at the current context
@@ -231,8 +239,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     del W
     copies = 1 if use_tp else world   # independent sequences in the job
     g = torch.Generator().manual_seed(args.seed + 1 + (0 if use_tp else rank))
-    prompt = torch.randint(0, cfg.vocab_size, (args.batch, args.ctx), generator=g)
-    dec.prefill(prompt)
+    fill = args.kv_fill if args.kv_fill != "auto" else ("prefill" if args.batch * args.ctx <= 65536 else "random")
+    if fill == "prefill":
+        prompt = torch.randint(0, cfg.vocab_size, (args.batch, args.ctx), generator=g)
+        dec.prefill(prompt)
+    else:
+        dec.fill_random(args.ctx, seed=args.seed + 1)
     dec.capture()
     torch.cuda.synchronize()
     setup_s = time.time() - t0
@@ -326,13 +338,13 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "strong" if use_tp else "weak", "vs_baseline": None,
         "dtype": "fp16", "data": "synthetic",
-        "config": {"workload": "qwen3vl4b-text greedy decode, NF4 weights (blocksize 64, fp16 absmax) incl. 4-bit "
-                               "lm_head, int8 KV (int8t64), ctx 8192 prefilled with uniform random tokens "
-                               "(BASELINE config 4)", "model": "Qwen3-VL-4B text (random init N(0,0.02))",
+        "config": {"workload": _workload(args),
+                   "kv_fill": "random int8 codes" if fill == "random" else "prefill of uniform random tokens",
+                   "model": "Qwen3-VL-4B text (random init N(0,0.02))",
                    "global_batch": args.batch * copies, "ctx": args.ctx, "layers": cfg.num_hidden_layers,
                    "parallelism": f"tp{world} (KV-head / column-row split, NCCL all-reduce after o_proj and "
                                   f"down_proj)" if use_tp else ("replicas" if world > 1 else "single GPU"),
-                   "l2": "inputs larger than L2 (2.8 GB streamed per step)", "graph": "one CUDA graph per step"},
+                   "l2": "inputs larger than L2 (>= 2.8 GB streamed per step)", "graph": "one CUDA graph per step"},
         "roofline": roofline,
         "attn_roofline": attn_roof,
         # bytes one GPU streams per step (its shard with tensor parallelism) against one GPU's peak

@@ -50,6 +50,10 @@ from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
 
 
+MAX_BATCH = 64
+GEMV_ROWS = 8   # rows per nova_nf4_gemv launch (larger batches run in slices of 8 rows)
+
+
 @dataclass
 class DecoderConfig:
     """Qwen3-VL-4B text tower dimensions (src/nova/config.py:14-37)."""
@@ -216,8 +220,8 @@ class NovaDecoder:
     def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
                  device="cuda", pdl: bool = True, tp: TPContext | None = None) -> None:
         cfg = weights.cfg
-        if batch < 1 or batch > 8:
-            raise ValueError("the GEMV decode path handles batch 1..8")
+        if batch < 1 or batch > MAX_BATCH:
+            raise ValueError(f"the decode path handles batch 1..{MAX_BATCH}")
         self.tp = tp if tp is not None else TPContext()
         sr = shard_ranges(cfg, self.tp.rank, self.tp.world)
         self.w = shard_weights(weights, self.tp.rank, self.tp.world) if self.tp.active else weights
@@ -344,6 +348,22 @@ class NovaDecoder:
 
     # ---------------------------------------------------------------- decode
 
+    def _gemv(self, x, w: NF4Weight, out, *, epilogue: int = _lib.NF4_PLAIN, norm_weight=None, residual=None,
+              argmax=None, token_out=None, pos=None, embed=None, embed_out=None) -> None:
+        """nova_nf4_gemv over the batch in slices of GEMV_ROWS rows (one launch
+        per slice; the step-finalize position update runs on the last one)."""
+        B = x.shape[0]
+        eps = self.cfg.rms_norm_eps
+        for r in range(0, B, GEMV_ROWS):
+            sl = slice(r, min(B, r + GEMV_ROWS))
+            last = sl.stop == B
+            nf4_gemv(x[sl], w.units, None, self.lut, out[sl], epilogue=epilogue, norm_weight=norm_weight, eps=eps,
+                     residual=None if residual is None else residual[sl],
+                     argmax=None if argmax is None else argmax[sl],
+                     token_out=None if token_out is None else token_out[sl], pos=pos if last else None,
+                     embed=embed, embed_out=None if embed_out is None else embed_out[sl],
+                     workspace=self.gemv_ws, n=w.n)
+
     def _step_body(self) -> None:
         cfg, cache, lut = self.cfg, self.cache, self.lut
         eps = cfg.rms_norm_eps
@@ -356,10 +376,9 @@ class NovaDecoder:
 
         def row_parallel(x, w):   # o_proj / down_proj + residual add
             if not tp.active:
-                nf4_gemv(x, w.units, None, lut, self.resid, epilogue=_lib.NF4_RESIDUAL, residual=self.resid,
-                         workspace=ws, n=w.n)
+                self._gemv(x, w, self.resid, epilogue=_lib.NF4_RESIDUAL, residual=self.resid)
                 return
-            nf4_gemv(x, w.units, None, lut, self.part32, epilogue=_lib.NF4_F32, workspace=ws, n=w.n)
+            self._gemv(x, w, self.part32, epilogue=_lib.NF4_F32)
             if self.p2p is not None:   # fused NVLink all-reduce + residual add
                 self.p2p(self.part32, self.resid)
                 return
@@ -368,8 +387,7 @@ class NovaDecoder:
                       self.resid.stride(0), B, cfg.hidden_size, stream)
 
         for li, lw in enumerate(self.w.layers):
-            nf4_gemv(self.resid, lw.qkv.units, None, lut, self.qkv, norm_weight=lw.input_ln, eps=eps,
-                     workspace=ws, n=lw.qkv.n)
+            self._gemv(self.resid, lw.qkv, self.qkv, norm_weight=lw.input_ln)
             qa = _lib.QKArgs()
             qa.qkv, qa.qkv_stride = self.qkv.data_ptr(), self.qkv.stride(0)
             qa.q_norm_weight, qa.k_norm_weight, qa.eps = lw.q_norm.data_ptr(), lw.k_norm.data_ptr(), eps
@@ -389,13 +407,11 @@ class NovaDecoder:
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
                              n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window)
             row_parallel(self.attn, lw.o)
-            nf4_gemv(self.resid, lw.gate_up.units, None, lut, self.act, epilogue=_lib.NF4_SILU_MUL,
-                     norm_weight=lw.post_ln, eps=eps, workspace=ws, n=lw.gate_up.n)
+            self._gemv(self.resid, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln)
             row_parallel(self.act, lw.down)
-        hw = self.w.lm_head
-        nf4_gemv(self.resid, hw.units, None, lut, self.logits, epilogue=_lib.NF4_ARGMAX,
-                 norm_weight=self.w.final_norm, eps=eps, argmax=self.argmax_slot, token_out=self.input_ids,
-                 pos=cache.pos, embed=self.w.embed, embed_out=self.resid, workspace=ws, n=hw.n)
+        self._gemv(self.resid, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
+                   argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
+                   embed_out=self.resid)
 
     def close(self) -> None:
         """Release the graph and the peer mappings of the tensor-parallel
@@ -406,8 +422,42 @@ class NovaDecoder:
             self.p2p.close()
 
     def launches_per_step(self) -> int:
-        """Kernels of this library per step (the NCCL all-reduces not counted)."""
-        return (8 if self.tp.active else 6) * self.cfg.num_hidden_layers + 1
+        """Kernels of this library per step (NCCL all-reduces not counted)."""
+        sl = -(-self.batch // GEMV_ROWS)
+        per_layer = 4 * sl + 2   # GEMV slices + q/k norm-RoPE-append + attention
+        if self.tp.active:
+            per_layer += 2       # fused all-reduce + residual add (or the residual add after NCCL), twice
+        return per_layer * self.cfg.num_hidden_layers + sl
+
+    @torch.inference_mode()
+    def fill_random(self, ctx: int, seed: int = 0) -> None:
+        """Decode state after a ``ctx``-token context without running the
+        prefill: uniform random int8 codes and small random min/step scales in
+        every layer's cache, a random fp16 ring, random current tokens.  For
+        throughput measurement at batch sizes / contexts where an eager prefill
+        would take minutes (the kernels' cost does not depend on the values)."""
+        c = self.cache
+        if ctx < 1 or ctx >= self.max_len:
+            raise ValueError(f"ctx {ctx} outside [1, {self.max_len})")
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        for li in range(self.cfg.num_hidden_layers):
+            for t in (c.kq[li], c.vq[li]):
+                t.random_(0, 256, generator=g)
+            for t in (c.kst[li], c.vst[li]):
+                t.uniform_(0.0, 0.02, generator=g)
+            for t in (c.kmn[li], c.vmn[li]):
+                t.uniform_(-2.5, -1.5, generator=g)
+            for t in (c.tail_k[li], c.tail_v[li]):
+                t.normal_(0.0, 1.0, generator=g)
+        q_full = (ctx // GROUP_T) * GROUP_T
+        c.pos.fill_(ctx)
+        c.first.fill_(0)
+        c._written.fill_(ctx)
+        c._qlen.fill_(q_full)
+        c._pg.fill_(q_full // GROUP_T)
+        self.input_ids.copy_(torch.randint(0, self.cfg.vocab_size, (self.batch,), generator=g, device=self.device))
+        self.resid.copy_(self.w.embed[self.input_ids])
+        self.argmax_slot.zero_()
 
     @torch.inference_mode()
     def step_eager(self) -> torch.Tensor:

@@ -39,11 +39,12 @@ MAX_GQ = 4
 
 def pick_chunk(max_len: int, batch: int, kv_heads: int, q_heads: int, sms: int = 148) -> int:
     """Split size (tokens, a multiple of 64, at least 256) for the decode
-    attention at capacity ``max_len``: about two CTAs per SM, and at most
+    attention at capacity ``max_len``: about two CTAs per SM (splits of at
+    most 8192 tokens at large batch), and at most
     ``73728 // (q_heads/kv_heads * 528) - 1`` splits per head, so the last CTA
     of a head merges all split partials from one shared-memory copy."""
     gq = max(1, q_heads // kv_heads)
-    per_head = max(1, (2 * sms) // (batch * kv_heads))
+    per_head = max(1, (2 * sms) // (batch * kv_heads), -(-max_len // 8192))   # and splits of at most 8192 tokens
     per_head = min(per_head, 73728 // (gq * 528) - 1)
     chunk = -(-max_len // per_head)
     return max(GROUP_T * 4, -(-chunk // GROUP_T) * GROUP_T)

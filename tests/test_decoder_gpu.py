@@ -44,7 +44,7 @@ def _setup(kind, batch, prompt_len, max_len, seed=1):
     return cfg, W, dec, orc, prompt
 
 
-@pytest.mark.parametrize("kind,batch,steps", [("small", 1, 70), ("small", 3, 20), ("real", 1, 12)])
+@pytest.mark.parametrize("kind,batch,steps", [("small", 1, 70), ("small", 3, 20), ("small", 11, 6), ("real", 1, 12)])
 def test_graph_decode_matches_oracle(cuda_lib, kind, batch, steps):
     cfg, W, dec, orc, _ = _setup(kind, batch, prompt_len=150, max_len=320)
     orc.load_state(dec.state())
@@ -110,3 +110,27 @@ def test_graph_equals_eager_bit_exact(cuda_lib):
     for li in range(cfg.num_hidden_layers):
         assert torch.equal(dec.cache.kq[li], dec2.cache.kq[li])
         assert torch.equal(dec.cache.tail_v[li], dec2.cache.tail_v[li])
+
+
+def test_random_fill_batch_decodes(cuda_lib):
+    """fill_random (the synthetic context of the batched throughput config):
+    batch 20 over two GEMV slices and a partial one, graph replay equal to
+    eager replay of the same state, positions advanced once per step."""
+    from nova_b200.decoder import DecoderWeights, NovaDecoder
+
+    cfg = _cfg("small")
+    W = DecoderWeights.random_init(cfg, seed=5)
+    outs = []
+    for graph in (False, True):
+        dec = NovaDecoder(W, max_len=600, batch=20)
+        dec.fill_random(500, seed=9)
+        if graph:
+            dec.capture()
+        toks = []
+        for _ in range(3):
+            toks.append((dec.step() if graph else dec.step_eager()).cpu().clone())
+        assert int(dec.pos.item()) == 503 and int(dec.cache._written.item()) == 503
+        assert torch.isfinite(dec.logits.float()).all()
+        outs.append((torch.stack(toks), dec.logits.float().cpu()))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
