@@ -332,6 +332,50 @@ typedef struct nova_qk_args {
 
 NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
 
+/* ------------------------------------------------------- fused phases */
+
+/*
+ * One cooperative launch (one CTA per SM) that runs up to 6 phases in order
+ * with grid barriers between them: NF4 GEMVs on native-layout weights (M <= 2
+ * rows, epilogues PLAIN / RESIDUAL / SILU_MUL / F32, optional RMSNorm
+ * prologue, the CTA-level split-K schedule) and at most one q/k norm + RoPE +
+ * int8 KV append phase (the work of nova_qk_norm_rope_append).  The decoder
+ * runs a layer's o_proj -> gate|up -> down -> next layer's q|k|v -> q/k norm
+ * as one launch.  Each warp requests the next GEMV's first weight chunks
+ * before it waits at a barrier.  Grid-barrier waits give up after timeout_ns
+ * (0 = 1 s) and record an error word in the workspace; mbarrier waits are
+ * bounded as everywhere else.  No counterpart in the reference, whose layer
+ * runs these ops as separate kernels (src/nova/layers.py:99-218).
+ */
+typedef struct nova_gemv_phase {
+    const void* x;            /* fp16 [m, x_stride] input rows                  */
+    int64_t x_stride;
+    const void* norm_weight;  /* fp16 [k] RMSNorm prologue or NULL              */
+    const void* units;        /* native unit stream (nova_nf4_pack_native)      */
+    int64_t n, k;
+    void* out;                /* fp16 (fp32 for NOVA_NF4_F32) [m, out_stride]  */
+    int64_t out_stride;
+    const void* residual;     /* RESIDUAL epilogue                              */
+    int64_t res_stride;
+    int64_t epilogue;
+} nova_gemv_phase;
+
+typedef struct nova_fused_args {
+    int64_t n_phases;
+    int64_t kind[6];          /* 0 = GEMV (gemv[i]), 1 = q/k norm + RoPE + append (qk) */
+    nova_gemv_phase gemv[6];
+    nova_qk_args qk;
+    const void* lut;          /* NF4 LUT (build_nf4_lut)                        */
+    double eps;               /* RMSNorm eps of every phase                     */
+    int64_t m;                /* rows (batch), 1 or 2                           */
+    void* workspace;          /* nova_fused_workspace_bytes(), zeroed once      */
+    int64_t workspace_bytes;
+    int64_t timeout_ns;
+} nova_fused_args;
+
+NOVA_API int nova_fused_workspace_bytes(int64_t* bytes);
+NOVA_API int nova_fused_phases(const nova_fused_args* args, void* stream);
+
 /* --------------------------------------------------- tensor parallelism */
 
 /*

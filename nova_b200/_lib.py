@@ -64,6 +64,27 @@ class QKArgs(ctypes.Structure):
     ]
 
 
+class GemvPhase(ctypes.Structure):
+    """Mirror of ``nova_gemv_phase``."""
+
+    _fields_ = [
+        ("x", _P), ("x_stride", _I), ("norm_weight", _P), ("units", _P), ("n", _I), ("k", _I),
+        ("out", _P), ("out_stride", _I), ("residual", _P), ("res_stride", _I), ("epilogue", _I),
+    ]
+
+
+class FusedArgs(ctypes.Structure):
+    """Mirror of ``nova_fused_args``."""
+
+    _fields_ = [
+        ("n_phases", _I), ("kind", _I * 6), ("gemv", GemvPhase * 6), ("qk", QKArgs), ("lut", _P),
+        ("eps", ctypes.c_double), ("m", _I), ("workspace", _P), ("workspace_bytes", _I), ("timeout_ns", _I),
+    ]
+
+
+PHASE_GEMV, PHASE_QK = 0, 1
+
+
 class TPAllReduceArgs(ctypes.Structure):
     """Mirror of ``nova_tp_allreduce_args``."""
 
@@ -97,6 +118,8 @@ _SIGNATURES: dict[str, list] = {
     "nova_ipc_handle": [_P, _P, ctypes.POINTER(_I)],
     "nova_ipc_open": [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)],
     "nova_ipc_close": [_P],
+    "nova_fused_workspace_bytes": [ctypes.POINTER(_I)],
+    "nova_fused_phases": [ctypes.POINTER(FusedArgs), _P],
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
 }
 _STRING_FNS = ("nova_version", "nova_last_error")

@@ -136,7 +136,7 @@ __device__ __forceinline__ void epilogue(const Params& p, int tile, const float 
             float v = c[2 * hrow + e];
             __half h;
             if (EPI == EPI_RESIDUAL) {
-                h = __float2half_rn(__half2float(p.residual[m * p.res_stride + n]) +
+                h = __float2half_rn(__half2float(__ldcg(p.residual + m * p.res_stride + n)) +
                                     __half2float(__float2half_rn(v)));
             } else {
                 if (p.bias) v += __half2float(p.bias[n]);
@@ -200,7 +200,9 @@ __device__ __forceinline__ void build_lut(uint32_t* lut_s, const uint32_t* lut) 
     }
 }
 
-// Stage x in shared memory, optionally RMS-normalised in HF order.  When
+// Stage x in shared memory, optionally RMS-normalised in HF order (x read
+// through L2 only: in the fused phase program it was written by other CTAs
+// earlier in the same launch).  When
 // every thread holds at most one 8-element chunk per row (K <= 8 * THREADS),
 // the chunk stays in registers between the sum of squares and the scaling,
 // so x and the norm weight are read once.
@@ -234,7 +236,7 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
 #pragma unroll
                 for (int m = 0; m < MAX_M; ++m) {
                     if (m >= p.M) break;
-                    xv[m] = *reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i);
+                    xv[m] = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i));
                 }
 #pragma unroll
                 for (int m = 0; m < MAX_M; ++m) {
@@ -247,7 +249,7 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
 #pragma unroll
                 for (int m = 0; m < MAX_M; ++m) {
                     if (m >= p.M) break;
-                    add_sq(*reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i), ss[m]);
+                    add_sq(__ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i)), ss[m]);
                 }
             }
         }
@@ -293,14 +295,14 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
                 const uint4 w8 = *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
                 for (int m = 0; m < p.M; ++m)
                     *reinterpret_cast<uint4*>(xs + m * p.K + 8 * i) =
-                        scale(*reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i), w8, rstd[m]);
+                        scale(__ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i)), w8, rstd[m]);
             }
         }
     } else {
         for (int i = threadIdx.x; i < p.M * kv8; i += THREADS) {
             const int m = i / kv8, j = i % kv8;
             *reinterpret_cast<uint4*>(xs + m * p.K + 8 * j) =
-                *(reinterpret_cast<const uint4*>(p.x + m * p.x_stride) + j);
+                __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride) + j);
         }
     }
 }
@@ -803,6 +805,394 @@ __global__ void __launch_bounds__(REF_THREADS, 1) nf4_gemv_ref_kernel(const __gr
     finish_launch<EPI>(p, lane);
 }
 
+// ---------------------------------------------------------------------------
+// Fused phase program: one cooperative launch (one 16-warp CTA per SM) runs a
+// short list of phases -- NF4 GEMVs and the per-head q/k norm + RoPE + int8 KV
+// append -- separated by grid barriers, so a decoder layer's
+// o_proj -> gate|up -> down -> next q|k|v -> q/k-norm+RoPE+append is one
+// launch instead of five.  Every GEMV phase uses the CTA-level split-K
+// schedule (whole row groups per CTA, warps split the k-blocks, fragments added
+// in shared memory).  The per-warp weight cursor runs across phase boundaries:
+// before a warp waits at a barrier it has already requested the first chunks of
+// the next GEMV's weights (constant data), so that DRAM round trip overlaps the
+// barrier.  The LUT is built once per launch.
+
+constexpr int MAX_PHASES = 6;
+enum PhaseKind { PH_GEMV = 0, PH_QK = 1 };
+
+struct GemvPhase {
+    const __half* x;
+    int64_t x_stride;
+    const __half* norm_w;
+    const uint8_t* units;
+    __half* out;
+    int64_t out_stride;
+    const __half* residual;
+    int64_t res_stride;
+    int N, K, epi;
+};
+
+struct QkPhase {
+    const __half* qkv;
+    int64_t qkv_stride;
+    const __half* q_norm_w;
+    const __half* k_norm_w;
+    const __half* cos;
+    const __half* sin;
+    int64_t rope_len;
+    __half* q_out;
+    int64_t q_out_stride;
+    __half* tail_k;
+    __half* tail_v;
+    uint8_t* kq;
+    uint8_t* vq;
+    __half* kmn;
+    __half* kst;
+    __half* vmn;
+    __half* vst;
+    const int64_t* pos;
+    int64_t* written;
+    int64_t* qlen;
+    int64_t* pg;
+    int q_heads, kv_heads;
+    int64_t max_len;
+};
+
+struct FusedParams {
+    int n_phases;
+    int kind[MAX_PHASES];
+    GemvPhase g[MAX_PHASES];
+    QkPhase qk;
+    const uint32_t* lut;
+    float eps;
+    int M;
+    int stage_units;
+    int xs_bytes;
+    unsigned* bar_count;
+    unsigned* bar_gen;
+    int* err;
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ unsigned long long gtime_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu_u32(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid barrier k (1-based) of this launch: arrivals are counted cumulatively,
+// the last arriver of barrier k publishes generation base + k (and, at the
+// launch's last barrier, re-arms the counter for the next launch).  The wait
+// gives up after timeout_ns, recording the error word.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void grid_barrier(const FusedParams& fp, unsigned base, int k, bool last) {
+    __syncthreads();   // the CTA's writes happen before thread 0's release
+    if (threadIdx.x == 0) {
+        const unsigned prev = atom_add_acq_rel_gpu(fp.bar_count, 1u);
+        const unsigned target = base + unsigned(k);
+        if (prev == unsigned(k) * gridDim.x - 1u) {
+            if (last) *fp.bar_count = 0u;
+            st_release_gpu_u32(fp.bar_gen, target);
+        } else {
+            const unsigned long long t0 = gtime_ns();
+            while (int(ld_acquire_gpu_u32(fp.bar_gen) - target) < 0) {
+                if (gtime_ns() - t0 > fp.timeout_ns) {
+                    atomicExch(fp.err, 5);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();   // ... and the other CTAs' writes happen before this CTA's later reads
+}
+
+__device__ __forceinline__ void epilogue_rt(const Params& p, int epi, int tile, const float (&c)[4], int g, int t) {
+    switch (epi) {
+        case EPI_RESIDUAL: epilogue<EPI_RESIDUAL>(p, tile, c, g, t); break;
+        case EPI_SILU_MUL: epilogue<EPI_SILU_MUL>(p, tile, c, g, t); break;
+        case EPI_F32: epilogue<EPI_F32>(p, tile, c, g, t); break;
+        default: epilogue<EPI_PLAIN>(p, tile, c, g, t); break;
+    }
+}
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// q/k norm + RoPE (+ ring write and group requantization for KV heads) of one
+// (head, batch row) by 128 threads (d = channel) on named barrier `bar`:
+// the same arithmetic, in the same order, as qk_norm_rope_append_kernel.
+__device__ void qk_item(const QkPhase& q, float eps, int head, int m, int d, int bar, float* red4, __half* ybuf) {
+    const int64_t pos = *q.pos;
+    if (m == 0 && head == 0 && d == 0) {
+        const int64_t w = pos + 1;
+        const int64_t ql = (w / 64) * 64;
+        *q.written = w;
+        *q.qlen = ql;
+        *q.pg = ql / 64;
+    }
+    const bool is_q = head < q.q_heads;
+    const int kvh = head - q.q_heads;
+    const __half* src = q.qkv + m * q.qkv_stride + int64_t(head) * 128;
+    const __half* nw = is_q ? q.q_norm_w : q.k_norm_w;
+    const float x = __half2float(__ldcg(src + d));   // written by other CTAs in the previous phase
+    float v = x * x;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    named_sync(bar, 128);   // red4 / ybuf may still be read by the previous item
+    if ((d & 31) == 0) red4[d >> 5] = v;
+    named_sync(bar, 128);
+    const float total = red4[0] + red4[1] + red4[2] + red4[3];
+    const float r = rsqrt_ieee(__fdiv_rn(total, 128.0f) + eps);
+    const float hn = __half2float(__float2half_rn(x * r));
+    const __half y = __float2half_rn(__half2float(nw[d]) * hn);
+    ybuf[d] = y;
+    named_sync(bar, 128);
+    const float yr = d < 64 ? -__half2float(ybuf[d + 64]) : __half2float(ybuf[d - 64]);
+    const int64_t cp = pos < q.rope_len ? pos : q.rope_len - 1;
+    const float cc = __half2float(q.cos[cp * 128 + d]), ss = __half2float(q.sin[cp * 128 + d]);
+    const float a = __half2float(__float2half_rn(__half2float(y) * cc));
+    const float b = __half2float(__float2half_rn(yr * ss));
+    const __half emb = __float2half_rn(a + b);
+    if (is_q) {
+        q.q_out[m * q.q_out_stride + int64_t(head) * 128 + d] = emb;
+        return;
+    }
+    if (pos < 0 || pos >= q.max_len) return;
+    const __half vv = __ldcg(q.qkv + m * q.qkv_stride + int64_t(q.q_heads + q.kv_heads + kvh) * 128 + d);
+    const int64_t bh = int64_t(m) * q.kv_heads + kvh;
+    const int slot = int(pos % 64);
+    __half* tk = q.tail_k + bh * 64 * 128;
+    __half* tv = q.tail_v + bh * 64 * 128;
+    tk[slot * 128 + d] = emb;
+    tv[slot * 128 + d] = vv;
+    if (slot != 63) return;
+    named_sync(bar, 128);   // every channel of the ring row is written before the group is requantized
+    const int64_t grp = pos / 64;
+    const int64_t ngroups = (q.max_len + 63) / 64;
+    const int64_t code_off = bh * q.max_len * 128 + grp * 64 * 128 + d;
+    const int64_t sc_off = (bh * ngroups + grp) * 128 + d;
+    for (int pass = 0; pass < 2; ++pass) {
+        const __half* col = (pass ? tv : tk) + d;
+        uint8_t* qd = (pass ? q.vq : q.kq) + code_off;
+        float mn = INFINITY, mx = -INFINITY;
+        for (int tt = 0; tt < 64; ++tt) {
+            const float e = __half2float(col[tt * 128]);
+            mn = fminf(mn, e);
+            mx = fmaxf(mx, e);
+        }
+        const float step = fmaxf(__fdiv_rn(mx - mn, 255.0f), 1e-8f);
+        for (int tt = 0; tt < 64; ++tt) {
+            float cq = rintf(__fdiv_rn(__half2float(col[tt * 128]) - mn, step));
+            cq = fminf(fmaxf(cq, 0.0f), 255.0f);
+            qd[tt * 128] = static_cast<uint8_t>(cq);
+        }
+        (pass ? q.vmn : q.kmn)[sc_off] = __float2half_rn(mn);
+        (pass ? q.vst : q.kst)[sc_off] = __float2half_rn(step);
+    }
+}
+
+__global__ void __launch_bounds__(NAT_THREADS, 1) nf4_fused_phases_kernel(const __grid_constant__ FusedParams fp) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[NAT_WARPS][NAT_STAGES];
+    __shared__ __align__(8) uint64_t bar_full[2], bar_empty[2];
+    __shared__ float qk_red[4][4];
+    __shared__ __align__(16) __half qk_y[4][128];
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
+    __half* xs = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
+    float4* red = reinterpret_cast<float4*>(smem_raw + LUT_BYTES + fp.xs_bytes);
+    const int su = fp.stage_units;
+    const int stage_bytes = su * UNIT_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint8_t* ring = smem_raw + LUT_BYTES + fp.xs_bytes + 2 * NAT_WARPS * 32 * 32 + size_t(warp) * NAT_STAGES * stage_bytes;
+    const int c = blockIdx.x, G = gridDim.x;
+    const unsigned base = *fp.bar_gen;   // generations published by earlier launches
+
+    // This CTA's row groups of GEMV phase ph, and this warp's k-block slice of each.
+    auto groups = [&](int ph, int& r0, int& r1) {
+        const int n_rg = fp.g[ph].N / UNIT_ROWS;
+        r0 = int(int64_t(n_rg) * c / G);
+        r1 = int(int64_t(n_rg) * (c + 1) / G);
+    };
+    auto warp_slice = [&](int ph, int& a, int& b) {
+        const int KB = fp.g[ph].K / 64;
+        a = KB * warp / NAT_WARPS;
+        b = KB * (warp + 1) / NAT_WARPS;
+    };
+    // issue cursor: (phase, row group, block) of the next chunk to request (lane 0)
+    int is_ph = -1, is_rg = 0, is_r1 = 0, is_off = 0, is_a = 0, is_b = 0;
+    auto advance_phase = [&](int from) {   // first GEMV phase >= from with work for this warp
+        for (int ph = from; ph < fp.n_phases; ++ph) {
+            if (fp.kind[ph] != PH_GEMV) continue;
+            int r0, r1, a, b;
+            groups(ph, r0, r1);
+            warp_slice(ph, a, b);
+            if (r0 < r1 && a < b) {
+                is_ph = ph; is_rg = r0; is_r1 = r1; is_a = a; is_b = b; is_off = a;
+                return;
+            }
+        }
+        is_ph = fp.n_phases;
+    };
+    int issued = 0, consumed = 0;
+    auto issue_next = [&]() {   // lane 0; false when nothing is left in the program
+        if (is_ph >= fp.n_phases) return false;
+        if (is_off >= is_b) {
+            if (++is_rg >= is_r1) {
+                advance_phase(is_ph + 1);
+                if (is_ph >= fp.n_phases) return false;
+            } else {
+                is_off = is_a;
+            }
+        }
+        const int KB = fp.g[is_ph].K / 64;
+        const int cnt = min(su, is_b - is_off);
+        const int st = issued % NAT_STAGES;
+        uint64_t* bar = &bars[warp][st];
+        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(ring + st * stage_bytes, fp.g[is_ph].units + (int64_t(is_rg) * KB + is_off) * UNIT_BYTES, bytes, bar);
+        is_off += cnt;
+        ++issued;
+        return true;
+    };
+
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
+        if (warp == 0) {
+            mbar_init(&bar_full[0], NAT_WARPS);
+            mbar_init(&bar_full[1], NAT_WARPS);
+            mbar_init(&bar_empty[0], 1);
+            mbar_init(&bar_empty[1], 1);
+        }
+        fence_mbar_init();
+        advance_phase(0);
+        for (int k = 0; k < NAT_STAGES; ++k)
+            if (!issue_next()) break;
+    }
+    build_lut<NAT_THREADS>(lut_s, fp.lut);
+    __syncthreads();
+
+    const uint32_t lut_base = smem_u32(lut_s);
+    const uint32_t laneword = uint32_t(lane) << 2;
+    const bool xlane = g < fp.M;
+    int jseg = 0;   // reduction segments (row groups) of this CTA so far
+    bool ok = true;
+
+    for (int ph = 0; ph < fp.n_phases && ok; ++ph) {
+        if (ph > 0) grid_barrier(fp, base, ph, ph == fp.n_phases - 1);
+        if (fp.kind[ph] == PH_QK) {
+            const int sub = threadIdx.x >> 7, d = threadIdx.x & 127;
+            const int heads = fp.qk.q_heads + fp.qk.kv_heads;
+            const int items = heads * fp.M;
+            for (int it = c * 4 + sub; it < items; it += G * 4)
+                qk_item(fp.qk, fp.eps, it % heads, it / heads, d, 1 + sub, qk_red[sub], qk_y[sub]);
+            continue;
+        }
+        const GemvPhase& gp = fp.g[ph];
+        Params p;
+        p.x = gp.x;
+        p.x_stride = gp.x_stride;
+        p.norm_w = gp.norm_w;
+        p.eps = fp.eps;
+        p.bias = nullptr;
+        p.residual = gp.residual;
+        p.res_stride = gp.res_stride;
+        p.out = gp.out;
+        p.out_stride = gp.out_stride;
+        p.argmax = nullptr;
+        p.M = fp.M;
+        p.N = gp.N;
+        p.K = gp.K;
+        p.KB = gp.K / 64;
+        stage_x<NAT_THREADS>(p, xs);
+        __syncthreads();
+        const __half* xrow = xs + (xlane ? g : 0) * p.K + 16 * t;
+        int r0, r1, a, b;
+        groups(ph, r0, r1);
+        warp_slice(ph, a, b);
+        for (int rg = r0; rg < r1 && ok; ++rg, ++jseg) {
+            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            uint32_t xb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            for (int off = a; off < b;) {
+                const int cnt = min(su, b - off);
+                const int st = consumed % NAT_STAGES;
+                if (!mbar_wait(&bars[warp][st], uint32_t((consumed / NAT_STAGES) & 1), fp.err, 2)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* sbuf = ring + st * stage_bytes;
+                for (int jj = 0; jj < cnt; ++jj) {
+                    const int blk = off + jj;
+                    if (xlane) {
+                        const uint4 x0 = lds128(xrow + 64 * blk), x1 = lds128(xrow + 64 * blk + 8);
+                        xb[0] = x0.x; xb[1] = x0.y; xb[2] = x0.z; xb[3] = x0.w;
+                        xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
+                    }
+                    mma_unit_smem(sbuf + jj * UNIT_BYTES, xb, lut_base, laneword, lane, g, acc);
+                }
+                ++consumed;
+                off += cnt;
+                __syncwarp();
+                if (lane == 0) {
+                    fence_proxy_async();
+                    issue_next();
+                }
+            }
+            if (!ok) break;
+            // two reduction buffers: segment j uses buffer j & 1, whose previous use (segment j - 2) must
+            // have been read by its reducer
+            const int rb = jseg & 1;
+            float4* rbuf = red + rb * NAT_WARPS * 32 * 2;
+            if (jseg >= 2 && !mbar_wait(&bar_empty[rb], uint32_t(((jseg - 2) >> 1) & 1), fp.err, 3)) {
+                ok = false;
+                break;
+            }
+            rbuf[(warp * 32 + lane) * 2] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+            rbuf[(warp * 32 + lane) * 2 + 1] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_full[rb]);
+            if (warp == (jseg & (NAT_WARPS - 1))) {
+                if (!mbar_wait(&bar_full[rb], uint32_t((jseg >> 1) & 1), fp.err, 3)) {
+                    ok = false;
+                    break;
+                }
+                float r[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+                for (int ww = 0; ww < NAT_WARPS; ++ww) {
+                    const float4 v0 = rbuf[(ww * 32 + lane) * 2], v1 = rbuf[(ww * 32 + lane) * 2 + 1];
+                    r[0][0] += v0.x; r[0][1] += v0.y; r[0][2] += v0.z; r[0][3] += v0.w;
+                    r[1][0] += v1.x; r[1][1] += v1.y; r[1][2] += v1.z; r[1][3] += v1.w;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_empty[rb]);
+                epilogue_rt(p, gp.epi, 2 * rg, r[0], g, t);
+                epilogue_rt(p, gp.epi, 2 * rg + 1, r[1], g, t);
+            }
+        }
+        // the next phase reads xs again: every warp is done with this one
+        __syncthreads();
+    }
+    // copies requested ahead but never consumed (a wait gave up) must land before exit
+    if (lane == 0)
+        for (; consumed < issued; ++consumed)
+            mbar_wait(&bars[warp][consumed % NAT_STAGES], uint32_t((consumed / NAT_STAGES) & 1), fp.err, 2);
+}
+
 // ---------------------------------------------------------------- quantizer / packer
 
 __global__ void nf4_quantize_kernel(const __half* __restrict__ w, int64_t n_blocks, int kb, int N,
@@ -1164,4 +1554,117 @@ extern "C" int nova_nf4_dequant(const void* packed, const void* absmax, int absm
         nf4_dequant_kernel<__half><<<grid, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)packed, absmax,
                                                                            (const uint32_t*)lut, (__half*)out, n, int(k));
     return check_launch("nova_nf4_dequant");
+}
+
+// ---------------------------------------------------------------- fused phases (host)
+
+extern "C" int nova_fused_workspace_bytes(int64_t* bytes) {
+    if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
+    *bytes = 256;   // barrier counter, generation, error word
+    return NOVA_OK;
+}
+
+extern "C" int nova_fused_phases(const nova_fused_args* a, void* stream) {
+    if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
+    if (a->n_phases < 1 || a->n_phases > MAX_PHASES) return fail(NOVA_ERR_INVALID, "1..6 phases");
+    if (a->m < 1 || a->m > 2) return fail(NOVA_ERR_UNSUPPORTED, "fused phases take 1 or 2 rows");
+    if (!a->lut || !a->workspace || a->workspace_bytes < 256) return fail(NOVA_ERR_INVALID, "lut / workspace");
+    if (reinterpret_cast<uintptr_t>(a->workspace) % 256) return fail(NOVA_ERR_ALIGN, "workspace 256-byte aligned");
+    FusedParams fp;
+    memset(&fp, 0, sizeof(fp));
+    fp.n_phases = int(a->n_phases);
+    fp.lut = (const uint32_t*)a->lut;
+    fp.eps = float(a->eps);
+    fp.M = int(a->m);
+    int64_t max_xs = 0;
+    int n_qk = 0;
+    for (int i = 0; i < fp.n_phases; ++i) {
+        fp.kind[i] = int(a->kind[i]);
+        if (fp.kind[i] == PH_QK) {
+            const nova_qk_args& q = a->qk;
+            if (++n_qk > 1) return fail(NOVA_ERR_INVALID, "at most one q/k phase");
+            if (q.head_dim != 128 || q.group != 64 || q.batch != a->m)
+                return fail(NOVA_ERR_UNSUPPORTED, "q/k phase: head_dim 128, group 64, batch == m");
+            if (!q.qkv || !q.q_norm_weight || !q.k_norm_weight || !q.cos || !q.sin || !q.q_out || !q.tail_k ||
+                !q.tail_v || !q.kq || !q.vq || !q.kmn || !q.kst || !q.vmn || !q.vst || !q.pos || !q.written ||
+                !q.qlen || !q.pg || q.rope_len <= 0 || q.max_len <= 0)
+                return fail(NOVA_ERR_INVALID, "q/k phase: NULL pointer or bad length");
+            QkPhase& o = fp.qk;
+            o.qkv = (const __half*)q.qkv; o.qkv_stride = q.qkv_stride;
+            o.q_norm_w = (const __half*)q.q_norm_weight; o.k_norm_w = (const __half*)q.k_norm_weight;
+            o.cos = (const __half*)q.cos; o.sin = (const __half*)q.sin; o.rope_len = q.rope_len;
+            o.q_out = (__half*)q.q_out; o.q_out_stride = q.q_out_stride;
+            o.tail_k = (__half*)q.tail_k; o.tail_v = (__half*)q.tail_v;
+            o.kq = (uint8_t*)q.kq; o.vq = (uint8_t*)q.vq;
+            o.kmn = (__half*)q.kmn; o.kst = (__half*)q.kst; o.vmn = (__half*)q.vmn; o.vst = (__half*)q.vst;
+            o.pos = q.pos; o.written = q.written; o.qlen = q.qlen; o.pg = q.pg;
+            o.q_heads = int(q.q_heads); o.kv_heads = int(q.kv_heads); o.max_len = q.max_len;
+            continue;
+        }
+        if (fp.kind[i] != PH_GEMV) return fail(NOVA_ERR_INVALID, "phase kind must be 0 or 1");
+        const nova_gemv_phase& g = a->gemv[i];
+        const int epi = int(g.epilogue);
+        if (epi != EPI_PLAIN && epi != EPI_RESIDUAL && epi != EPI_SILU_MUL && epi != EPI_F32)
+            return fail(NOVA_ERR_UNSUPPORTED, "phase %d: epilogue %d not available in fused phases", i, epi);
+        if (g.n <= 0 || g.n % UNIT_ROWS || g.n > (1 << 26) || g.k <= 0 || g.k % 64 || g.k > (1 << 16))
+            return fail(NOVA_ERR_INVALID, "phase %d: N multiple of 32, K multiple of 64", i);
+        if (!g.x || !g.units || !g.out || (epi == EPI_RESIDUAL && !g.residual))
+            return fail(NOVA_ERR_INVALID, "phase %d: NULL pointer", i);
+        auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
+        if (mis(g.x, 16) || (g.x_stride % 8) || mis(g.norm_weight, 16) || mis(g.units, 16) ||
+            (epi == EPI_F32 && mis(g.out, 4)))
+            return fail(NOVA_ERR_ALIGN, "phase %d: x / norm_weight / units 16-byte aligned, x_stride % 8", i);
+        GemvPhase& o = fp.g[i];
+        o.x = (const __half*)g.x; o.x_stride = g.x_stride; o.norm_w = (const __half*)g.norm_weight;
+        o.units = (const uint8_t*)g.units; o.out = (__half*)g.out; o.out_stride = g.out_stride;
+        o.residual = (const __half*)g.residual; o.res_stride = g.res_stride;
+        o.N = int(g.n); o.K = int(g.k); o.epi = epi;
+        max_xs = std::max<int64_t>(max_xs, (a->m * g.k * 2 + 127) / 128 * 128);
+    }
+    int dev = 0, optin = 0, sms = 0, coop = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "device queries failed");
+    }
+    if (!coop) return fail(NOVA_ERR_UNSUPPORTED, "the device does not support cooperative launches");
+    const int64_t ring_unit = int64_t(NAT_WARPS) * NAT_STAGES * UNIT_BYTES;
+    const int64_t red_bytes = 2 * int64_t(NAT_WARPS) * 32 * 32;
+    const int64_t static_smem = 2048;
+    const int64_t su = std::min<int64_t>(3, (optin - int64_t(LUT_BYTES) - max_xs - red_bytes - static_smem) / ring_unit);
+    if (su < 1) return fail(NOVA_ERR_UNSUPPORTED, "fused phases: K too large for shared memory");
+    fp.stage_units = int(su);
+    fp.xs_bytes = int(max_xs);
+    uint8_t* ws = (uint8_t*)a->workspace;
+    fp.bar_count = (unsigned*)ws;
+    fp.bar_gen = (unsigned*)(ws + 4);
+    fp.err = (int*)(ws + 8);
+    fp.timeout_ns = a->timeout_ns > 0 ? (unsigned long long)a->timeout_ns : 1000000000ull;
+    const int64_t nsmem = int64_t(LUT_BYTES) + max_xs + red_bytes + su * ring_unit;
+    static int64_t smem_set = 0;
+    if (int rc = prepare_smem(nf4_fused_phases_kernel, nsmem, &smem_set)) return rc;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, nf4_fused_phases_kernel, NAT_THREADS, size_t(nsmem)) !=
+            cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_UNSUPPORTED, "fused phases: one CTA per SM does not fit");
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(sms));
+    cfg.blockDim = dim3(NAT_THREADS);
+    cfg.dynamicSmemBytes = size_t(nsmem);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident at once: the grid barriers rely on it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, nf4_fused_phases_kernel, fp);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_fused_phases: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
 }

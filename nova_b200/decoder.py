@@ -218,7 +218,7 @@ class NovaDecoder:
     """
 
     def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
-                 device="cuda", pdl: bool = True, tp: TPContext | None = None) -> None:
+                 device="cuda", pdl: bool = True, tp: TPContext | None = None, fused: bool | None = None) -> None:
         cfg = weights.cfg
         if batch < 1 or batch > MAX_BATCH:
             raise ValueError(f"the decode path handles batch 1..{MAX_BATCH}")
@@ -257,6 +257,13 @@ class NovaDecoder:
         self.gemv_ws = gemv_workspace(dev, n_max).clone()   # shared by every GEMV of the step
         self.graph: torch.cuda.CUDAGraph | None = None
         self.pdl = bool(pdl)
+        # fused=True: one cooperative launch per layer for o -> gate|up -> down -> next q|k|v -> q/k norm
+        # (batch <= 2, one GPU).  Off by default: its grid barriers (~1.5-2 us each) and per-phase x
+        # staging cost as much as the kernel boundaries they replace.
+        self.fused = False if fused is None else bool(fused)
+        if self.fused and (self.batch > 2 or self.tp.active):
+            raise ValueError("fused phases need batch <= 2 and no tensor parallelism")
+        self.fused_ws = torch.zeros(256, dtype=torch.uint8, device=dev)
 
     def _pick_chunk(self) -> int:
         """Split size for the attention (``kvattn.pick_chunk``)."""
@@ -364,7 +371,75 @@ class NovaDecoder:
                      embed=embed, embed_out=None if embed_out is None else embed_out[sl],
                      workspace=self.gemv_ws, n=w.n)
 
+    def _qk_args(self, li: int, lw) -> "_lib.QKArgs":
+        cfg, cache = self.cfg, self.cache
+        qa = _lib.QKArgs()
+        qa.qkv, qa.qkv_stride = self.qkv.data_ptr(), self.qkv.stride(0)
+        qa.q_norm_weight, qa.k_norm_weight, qa.eps = lw.q_norm.data_ptr(), lw.k_norm.data_ptr(), cfg.rms_norm_eps
+        qa.cos, qa.sin, qa.rope_len = self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0]
+        qa.q_out, qa.q_out_stride = self.q_rot.data_ptr(), self.q_rot.stride(0)
+        qa.tail_k, qa.tail_v = cache.tail_k[li].data_ptr(), cache.tail_v[li].data_ptr()
+        qa.kq, qa.vq = cache.kq[li].data_ptr(), cache.vq[li].data_ptr()
+        qa.kmn, qa.kst = cache.kmn[li].data_ptr(), cache.kst[li].data_ptr()
+        qa.vmn, qa.vst = cache.vmn[li].data_ptr(), cache.vst[li].data_ptr()
+        qa.pos, qa.written = cache.pos.data_ptr(), cache._written.data_ptr()
+        qa.qlen, qa.pg = cache._qlen.data_ptr(), cache._pg.data_ptr()
+        qa.batch, qa.q_heads, qa.kv_heads = self.batch, self.hq, self.hkv
+        qa.head_dim, qa.max_len, qa.group = cfg.head_dim, self.max_len, GROUP_T
+        return qa
+
+    def _fused(self, phases: list, qk_layer: int | None = None) -> None:
+        """One nova_fused_phases launch.  phases: ("gemv", x, w, out, epilogue, norm_weight, residual) or
+        ("qk",); the q/k phase uses layer ``qk_layer``."""
+        a = _lib.FusedArgs()
+        a.n_phases = len(phases)
+        for i, ph in enumerate(phases):
+            if ph[0] == "qk":
+                a.kind[i] = _lib.PHASE_QK
+                a.qk = self._qk_args(qk_layer, self.w.layers[qk_layer])
+                continue
+            _, x, w, out, epi, nw, res = ph
+            a.kind[i] = _lib.PHASE_GEMV
+            g = a.gemv[i]
+            g.x, g.x_stride = x.data_ptr(), x.stride(0)
+            g.norm_weight = _lib.ptr(nw)
+            g.units, g.n, g.k = w.units.data_ptr(), w.n, w.shape[1]
+            g.out, g.out_stride = out.data_ptr(), out.stride(0)
+            g.residual, g.res_stride = (_lib.ptr(res), res.stride(0) if res is not None else 0)
+            g.epilogue = epi
+        a.lut, a.eps, a.m = self.lut.data_ptr(), self.cfg.rms_norm_eps, self.batch
+        a.workspace, a.workspace_bytes = self.fused_ws.data_ptr(), self.fused_ws.numel()
+        _lib.check(_lib.lib().nova_fused_phases(_lib.ctypes.byref(a), _lib.stream_of(self.device)), "fused phases")
+
+    def _step_body_fused(self) -> None:
+        cfg, cache = self.cfg, self.cache
+        B = self.batch
+        q3 = self.q_rot.view(B, self.hq, cfg.head_dim)
+        a3 = self.attn.view(B, self.hq, cfg.head_dim)
+        layers = self.w.layers
+        NF4 = _lib
+        self._fused([("gemv", self.resid, layers[0].qkv, self.qkv, NF4.NF4_PLAIN, layers[0].input_ln, None), ("qk",)],
+                    qk_layer=0)
+        for li, lw in enumerate(layers):
+            launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
+                                  cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
+                             cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
+                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window)
+            phases = [("gemv", self.attn, lw.o, self.resid, NF4.NF4_RESIDUAL, None, self.resid),
+                      ("gemv", self.resid, lw.gate_up, self.act, NF4.NF4_SILU_MUL, lw.post_ln, None),
+                      ("gemv", self.act, lw.down, self.resid, NF4.NF4_RESIDUAL, None, self.resid)]
+            if li + 1 < len(layers):
+                nxt = layers[li + 1]
+                phases += [("gemv", self.resid, nxt.qkv, self.qkv, NF4.NF4_PLAIN, nxt.input_ln, None), ("qk",)]
+            self._fused(phases, qk_layer=li + 1 if li + 1 < len(layers) else None)
+        self._gemv(self.resid, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
+                   argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
+                   embed_out=self.resid)
+
     def _step_body(self) -> None:
+        if self.fused:
+            self._step_body_fused()
+            return
         cfg, cache, lut = self.cfg, self.cache, self.lut
         eps = cfg.rms_norm_eps
         B = self.batch
@@ -423,6 +498,8 @@ class NovaDecoder:
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step (NCCL all-reduces not counted)."""
+        if self.fused:   # q|k|v + q/k of layer 0, then attention + one fused launch per layer, then the lm_head
+            return 1 + 2 * self.cfg.num_hidden_layers + 1
         sl = -(-self.batch // GEMV_ROWS)
         per_layer = 4 * sl + 2   # GEMV slices + q/k norm-RoPE-append + attention
         if self.tp.active:
