@@ -56,6 +56,8 @@ def _args():
     ap.add_argument("--kv-fill", choices=["auto", "prefill", "random"], default="auto",
                     help="context: eager prefill of random tokens, or random int8 codes written straight into the "
                          "cache (auto: prefill up to batch*ctx = 65536 tokens)")
+    ap.add_argument("--qkv-fused", action="store_true",
+                    help="q|k|v GEMV and q/k norm + RoPE + append as one launch (one CTA per head)")
     ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp",
                     help="N > 1: tensor parallelism over the N GPUs (default) or N independent replicas")
     return ap.parse_args()
@@ -163,6 +165,7 @@ def _time_kernels(dec, reps: int = 10) -> dict:
         return w.stream_bytes
 
     scratch = {"qkv": dec.qkv.clone(), "resid": dec.resid.clone(), "act": dec.act.clone(), "attn": dec.attn.clone()}
+    layer_index = {id(lw): i for i, lw in enumerate(dec.w.layers)}
     if dec.tp.active:   # row-parallel projections write fp32 partial sums
         part = dec.part32.clone()
 
@@ -172,8 +175,9 @@ def _time_kernels(dec, reps: int = 10) -> dict:
         def row_par(x, w):
             dec._gemv(x, w, scratch["resid"], epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"])
     fams = {
-        "qkv": (lambda lw: dec._gemv(scratch["resid"], lw.qkv, scratch["qkv"], norm_weight=lw.input_ln),
-                lambda lw: bytes_of(lw.qkv)),
+        # the step's q|k|v launch (with q/k norm + RoPE + ring write; pos does not move, so the same ring slot
+        # is rewritten)
+        "qkv": (lambda lw: dec._qkv_step(layer_index[id(lw)], lw), lambda lw: bytes_of(lw.qkv)),
         "o_proj": (lambda lw: row_par(scratch["attn"], lw.o), lambda lw: bytes_of(lw.o)),
         "gate_up": (lambda lw: dec._gemv(scratch["resid"], lw.gate_up, scratch["act"], epilogue=_lib.NF4_SILU_MUL,
                                          norm_weight=lw.post_ln),
@@ -235,7 +239,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     max_len = args.ctx + 2 * (args.warmup + args.steps) + 64
     use_tp = world > 1 and args.parallel == "tp"
     tp = TPContext(rank, world, dist.group.WORLD) if use_tp else None
-    dec = NovaDecoder(W, max_len=max_len, batch=args.batch, device=dev, tp=tp)
+    dec = NovaDecoder(W, max_len=max_len, batch=args.batch, device=dev, tp=tp, qkv_fused=args.qkv_fused)
     del W
     copies = 1 if use_tp else world   # independent sequences in the job
     g = torch.Generator().manual_seed(args.seed + 1 + (0 if use_tp else rank))

@@ -332,6 +332,20 @@ typedef struct nova_qk_args {
 
 NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
 
+/*
+ * The decoder's q|k|v projection and q/k norm + RoPE + int8 KV append in one
+ * launch: gemv describes the NF4 GEMV of the concatenated q|k|v weight
+ * (native layout, N = (q_heads + 2*kv_heads) * 128, optional RMSNorm
+ * prologue, epilogue ignored, out unused), qk the rest as for
+ * nova_qk_norm_rope_append (its qkv field unused).  One CTA per head keeps the
+ * head's projection in shared memory; results are identical to
+ * nova_nf4_gemv (plain epilogue, CTA-level schedule) followed by
+ * nova_qk_norm_rope_append.  Replaces the q/k/v projections, q_norm/k_norm,
+ * RoPE and cache update of LeanAttention.forward (src/nova/layers.py:99-133,
+ * :24-36; src/nova/kvattn.py:668-743).
+ */
+NOVA_API int nova_qkv_norm_rope_append(const nova_nf4_args* gemv, const nova_qk_args* qk, void* stream);
+
 /* ------------------------------------------------------- fused phases */
 
 /*

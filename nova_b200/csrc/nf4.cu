@@ -1193,6 +1193,222 @@ __global__ void __launch_bounds__(NAT_THREADS, 1) nf4_fused_phases_kernel(const 
             mbar_wait(&bars[warp][consumed % NAT_STAGES], uint32_t((consumed / NAT_STAGES) & 1), fp.err, 2);
 }
 
+// ---------------------------------------------------------------------------
+// q|k|v projection fused with q/k norm + RoPE + int8 KV append: one CTA per
+// head (q heads, then k heads, then v heads of the q|k|v weight), owning the
+// head's four 32-row groups.  The 16 warps split each group's k-blocks exactly
+// like the CTA-level GEMV; the reduced head (fp16, as the plain epilogue would
+// store it) stays in shared memory, and the CTA then applies q_norm / k_norm
+// and RoPE (q -> q_out, k -> ring) or copies v into the ring, requantizing the
+// 64-token group when this step completes it.  Same arithmetic as
+// nf4_gemv_cta_kernel followed by qk_norm_rope_append_kernel.
+
+// post-processing of one (head, row) by 128 threads on named barrier `bar`
+__device__ void head_post(const QkPhase& q, float eps, int head, int m, int d, int bar, const __half* hv,
+                          float* red4, __half* ybuf) {
+    const int64_t pos = *q.pos;
+    if (m == 0 && head == 0 && d == 0) {
+        const int64_t w = pos + 1;
+        const int64_t ql = (w / 64) * 64;
+        *q.written = w;
+        *q.qlen = ql;
+        *q.pg = ql / 64;
+    }
+    const int kind = head < q.q_heads ? 0 : (head < q.q_heads + q.kv_heads ? 1 : 2);   // q / k / v
+    const __half val = hv[d];
+    __half emb = val;
+    if (kind < 2) {
+        const __half* nw = kind == 0 ? q.q_norm_w : q.k_norm_w;
+        const float x = __half2float(val);
+        float v = x * x;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        named_sync(bar, 128);
+        if ((d & 31) == 0) red4[d >> 5] = v;
+        named_sync(bar, 128);
+        const float total = red4[0] + red4[1] + red4[2] + red4[3];
+        const float r = rsqrt_ieee(__fdiv_rn(total, 128.0f) + eps);
+        const float hn = __half2float(__float2half_rn(x * r));
+        const __half y = __float2half_rn(__half2float(nw[d]) * hn);
+        ybuf[d] = y;
+        named_sync(bar, 128);
+        const float yr = d < 64 ? -__half2float(ybuf[d + 64]) : __half2float(ybuf[d - 64]);
+        const int64_t cp = pos < q.rope_len ? pos : q.rope_len - 1;
+        const float cc = __half2float(q.cos[cp * 128 + d]), ss = __half2float(q.sin[cp * 128 + d]);
+        const float a = __half2float(__float2half_rn(__half2float(y) * cc));
+        const float b = __half2float(__float2half_rn(yr * ss));
+        emb = __float2half_rn(a + b);
+    }
+    if (kind == 0) {
+        q.q_out[m * q.q_out_stride + int64_t(head) * 128 + d] = emb;
+        return;
+    }
+    if (pos < 0 || pos >= q.max_len) return;
+    const int kvh = head - q.q_heads - (kind == 2 ? q.kv_heads : 0);
+    const int64_t bh = int64_t(m) * q.kv_heads + kvh;
+    const int slot = int(pos % 64);
+    __half* ring = (kind == 1 ? q.tail_k : q.tail_v) + bh * 64 * 128;
+    ring[slot * 128 + d] = emb;
+    if (slot != 63) return;
+    named_sync(bar, 128);   // the whole ring row is written before the group is requantized
+    const int64_t grp = pos / 64;
+    const int64_t ngroups = (q.max_len + 63) / 64;
+    const int64_t code_off = bh * q.max_len * 128 + grp * 64 * 128 + d;
+    const int64_t sc_off = (bh * ngroups + grp) * 128 + d;
+    const __half* col = ring + d;
+    uint8_t* qd = (kind == 1 ? q.kq : q.vq) + code_off;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int tt = 0; tt < 64; ++tt) {
+        const float e = __half2float(col[tt * 128]);
+        mn = fminf(mn, e);
+        mx = fmaxf(mx, e);
+    }
+    const float step = fmaxf(__fdiv_rn(mx - mn, 255.0f), 1e-8f);
+    for (int tt = 0; tt < 64; ++tt) {
+        float cq = rintf(__fdiv_rn(__half2float(col[tt * 128]) - mn, step));
+        cq = fminf(fmaxf(cq, 0.0f), 255.0f);
+        qd[tt * 128] = static_cast<uint8_t>(cq);
+    }
+    (kind == 1 ? q.kmn : q.vmn)[sc_off] = __float2half_rn(mn);
+    (kind == 1 ? q.kst : q.vst)[sc_off] = __float2half_rn(step);
+}
+
+__global__ void __launch_bounds__(NAT_THREADS, 1)
+    nf4_qkv_heads_kernel(const __grid_constant__ Params p, const __grid_constant__ QkPhase q, int stage_units,
+                         int* err) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[NAT_WARPS][NAT_STAGES];
+    __shared__ __align__(8) uint64_t bar_full[2], bar_empty[2];
+    __shared__ float qk_red[4][4];
+    __shared__ __align__(16) __half qk_y[4][128];
+    __shared__ __align__(16) __half head_out[MAX_M][128];
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
+    __half* xs = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
+    const int xs_bytes = (p.M * p.K * 2 + 127) / 128 * 128;
+    float4* red = reinterpret_cast<float4*>(smem_raw + LUT_BYTES + xs_bytes);   // [2][16][32][2]
+    const int su = stage_units;
+    const int stage_bytes = su * UNIT_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint8_t* ring = smem_raw + LUT_BYTES + xs_bytes + 2 * NAT_WARPS * 32 * 32 + size_t(warp) * NAT_STAGES * stage_bytes;
+    const int head = blockIdx.x;
+    const int KB = p.KB;
+    const int a = KB * warp / NAT_WARPS, b = KB * (warp + 1) / NAT_WARPS;   // this warp's k-blocks of every group
+    const int rg0 = 4 * head;
+
+    int is_j = 0, is_off = a, issued = 0, consumed = 0;
+    auto issue_next = [&]() {   // lane 0
+        if (a >= b) return false;
+        if (is_off >= b) {
+            if (++is_j >= 4) return false;
+            is_off = a;
+        }
+        const int cnt = min(su, b - is_off);
+        const int st = issued % NAT_STAGES;
+        uint64_t* bar = &bars[warp][st];
+        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(ring + st * stage_bytes, p.packed + (int64_t(rg0 + is_j) * KB + is_off) * UNIT_BYTES, bytes, bar);
+        is_off += cnt;
+        ++issued;
+        return true;
+    };
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
+        if (warp == 0) {
+            mbar_init(&bar_full[0], NAT_WARPS);
+            mbar_init(&bar_full[1], NAT_WARPS);
+            mbar_init(&bar_empty[0], 1);
+            mbar_init(&bar_empty[1], 1);
+        }
+        fence_mbar_init();
+        for (int k = 0; k < NAT_STAGES; ++k)
+            if (!issue_next()) break;
+    }
+    build_lut<NAT_THREADS>(lut_s, p.lut);
+    pdl_trigger();
+    pdl_wait();
+    stage_x<NAT_THREADS>(p, xs);
+    __syncthreads();
+
+    const uint32_t lut_base = smem_u32(lut_s);
+    const uint32_t laneword = uint32_t(lane) << 2;
+    const bool xlane = g < p.M;
+    const __half* xrow = xs + (xlane ? g : 0) * p.K + 16 * t;
+    bool ok = true;
+    for (int j = 0; j < 4 && ok; ++j) {
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        uint32_t xb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        for (int off = a; off < b;) {
+            const int cnt = min(su, b - off);
+            const int st = consumed % NAT_STAGES;
+            if (!mbar_wait(&bars[warp][st], uint32_t((consumed / NAT_STAGES) & 1), err, 2)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* sbuf = ring + st * stage_bytes;
+            for (int jj = 0; jj < cnt; ++jj) {
+                const int blk = off + jj;
+                if (xlane) {
+                    const uint4 x0 = lds128(xrow + 64 * blk), x1 = lds128(xrow + 64 * blk + 8);
+                    xb[0] = x0.x; xb[1] = x0.y; xb[2] = x0.z; xb[3] = x0.w;
+                    xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
+                }
+                mma_unit_smem(sbuf + jj * UNIT_BYTES, xb, lut_base, laneword, lane, g, acc);
+            }
+            ++consumed;
+            off += cnt;
+            __syncwarp();
+            if (lane == 0) {
+                fence_proxy_async();
+                issue_next();
+            }
+        }
+        if (!ok) break;
+        const int rb = j & 1;
+        float4* rbuf = red + rb * NAT_WARPS * 32 * 2;
+        if (j >= 2 && !mbar_wait(&bar_empty[rb], 0u, err, 3)) {
+            ok = false;
+            break;
+        }
+        rbuf[(warp * 32 + lane) * 2] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+        rbuf[(warp * 32 + lane) * 2 + 1] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_full[rb]);
+        if (warp == j) {   // reducer of group j
+            if (!mbar_wait(&bar_full[rb], uint32_t(j >> 1), err, 3)) {
+                ok = false;
+                break;
+            }
+            float r[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+            for (int ww = 0; ww < NAT_WARPS; ++ww) {
+                const float4 v0 = rbuf[(ww * 32 + lane) * 2], v1 = rbuf[(ww * 32 + lane) * 2 + 1];
+                r[0][0] += v0.x; r[0][1] += v0.y; r[0][2] += v0.z; r[0][3] += v0.w;
+                r[1][0] += v1.x; r[1][1] += v1.y; r[1][2] += v1.z; r[1][3] += v1.w;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_empty[rb]);
+#pragma unroll
+            for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+                for (int hrow = 0; hrow < 2; ++hrow)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int m = 2 * t + e;
+                        if (m < p.M) head_out[m][j * 32 + tile * 16 + g + 8 * hrow] = __float2half_rn(r[tile][2 * hrow + e]);
+                    }
+        }
+    }
+    if (!ok && lane == 0)
+        for (; consumed < issued; ++consumed)
+            mbar_wait(&bars[warp][consumed % NAT_STAGES], uint32_t((consumed / NAT_STAGES) & 1), err, 2);
+    __syncthreads();
+    if (!ok) return;
+    const int sub = threadIdx.x >> 7, d = threadIdx.x & 127;
+    for (int m = sub; m < p.M; m += 4) head_post(q, p.eps, head, m, d, 1 + sub, head_out[m], qk_red[sub], qk_y[sub]);
+}
+
 // ---------------------------------------------------------------- quantizer / packer
 
 __global__ void nf4_quantize_kernel(const __half* __restrict__ w, int64_t n_blocks, int kb, int N,
@@ -1665,6 +1881,71 @@ extern "C" int nova_fused_phases(const nova_fused_args* a, void* stream) {
     if (err != cudaSuccess) {
         cudaGetLastError();
         return fail(NOVA_ERR_CUDA, "nova_fused_phases: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
+}
+
+extern "C" int nova_qkv_norm_rope_append(const nova_nf4_args* g, const nova_qk_args* q, void* stream) {
+    if (!g || !q) return fail(NOVA_ERR_INVALID, "args must not be NULL");
+    if (g->layout != 1) return fail(NOVA_ERR_UNSUPPORTED, "native-layout weights only");
+    const int64_t heads = q->q_heads + 2 * q->kv_heads;
+    if (q->head_dim != 128 || q->group != 64 || q->q_heads <= 0 || q->kv_heads <= 0 || q->q_heads % q->kv_heads)
+        return fail(NOVA_ERR_UNSUPPORTED, "head_dim 128, group 64, q_heads a multiple of kv_heads");
+    if (g->n != heads * 128) return fail(NOVA_ERR_INVALID, "N must be (q_heads + 2*kv_heads) * 128");
+    if (g->m < 1 || g->m > MAX_M || q->batch != g->m) return fail(NOVA_ERR_INVALID, "M in [1, 8] and batch == M");
+    if (g->k <= 0 || g->k % 64 || g->k > (1 << 16)) return fail(NOVA_ERR_INVALID, "K a multiple of 64");
+    if (!g->x || !g->packed || !g->lut || !g->workspace || !q->q_norm_weight || !q->k_norm_weight || !q->cos ||
+        !q->sin || !q->q_out || !q->tail_k || !q->tail_v || !q->kq || !q->vq || !q->kmn || !q->kst || !q->vmn ||
+        !q->vst || !q->pos || !q->written || !q->qlen || !q->pg || q->rope_len <= 0 || q->max_len <= 0)
+        return fail(NOVA_ERR_INVALID, "NULL pointer or bad length");
+    auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
+    if (mis(g->x, 16) || (g->x_stride % 8) || mis(g->norm_weight, 16) || mis(g->packed, 16) || mis(g->workspace, 256))
+        return fail(NOVA_ERR_ALIGN, "x / norm_weight / packed 16-byte aligned, workspace 256");
+    int64_t need = 0;
+    nova_nf4_workspace_bytes(g->n, &need);
+    if (g->workspace_bytes < need) return fail(NOVA_ERR_INVALID, "workspace too small");
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.x = (const __half*)g->x;
+    p.x_stride = g->x_stride;
+    p.norm_w = (const __half*)g->norm_weight;
+    p.eps = float(g->eps);
+    p.packed = (const uint8_t*)g->packed;
+    p.lut = (const uint32_t*)g->lut;
+    p.M = int(g->m);
+    p.N = int(g->n);
+    p.K = int(g->k);
+    p.KB = int(g->k / 64);
+    QkPhase o;
+    o.qkv = nullptr; o.qkv_stride = 0;
+    o.q_norm_w = (const __half*)q->q_norm_weight; o.k_norm_w = (const __half*)q->k_norm_weight;
+    o.cos = (const __half*)q->cos; o.sin = (const __half*)q->sin; o.rope_len = q->rope_len;
+    o.q_out = (__half*)q->q_out; o.q_out_stride = q->q_out_stride;
+    o.tail_k = (__half*)q->tail_k; o.tail_v = (__half*)q->tail_v;
+    o.kq = (uint8_t*)q->kq; o.vq = (uint8_t*)q->vq;
+    o.kmn = (__half*)q->kmn; o.kst = (__half*)q->kst; o.vmn = (__half*)q->vmn; o.vst = (__half*)q->vst;
+    o.pos = q->pos; o.written = q->written; o.qlen = q->qlen; o.pg = q->pg;
+    o.q_heads = int(q->q_heads); o.kv_heads = int(q->kv_heads); o.max_len = q->max_len;
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "device queries failed");
+    }
+    const int64_t xs_bytes = (g->m * g->k * 2 + 127) / 128 * 128;
+    const int64_t ring_unit = int64_t(NAT_WARPS) * NAT_STAGES * UNIT_BYTES;
+    const int64_t red_bytes = 2 * int64_t(NAT_WARPS) * 32 * 32;
+    const int64_t su = std::min<int64_t>(3, (optin - int64_t(LUT_BYTES) - xs_bytes - red_bytes - 4096) / ring_unit);
+    if (su < 1) return fail(NOVA_ERR_UNSUPPORTED, "M*K too large for shared memory");
+    const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + red_bytes + su * ring_unit;
+    static int64_t smem_set = 0;
+    if (int rc = prepare_smem(nf4_qkv_heads_kernel, nsmem, &smem_set)) return rc;
+    int* errp = reinterpret_cast<int*>((uint8_t*)g->workspace + partial_bytes() + ((g->n / 16) * 4 + 4));
+    const cudaError_t err = launch(nf4_qkv_heads_kernel, dim3(unsigned(heads)), dim3(NAT_THREADS), size_t(nsmem),
+                                   (cudaStream_t)stream, p, o, int(su), errp);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_qkv_norm_rope_append: launch failed: %s", cudaGetErrorString(err));
     }
     return NOVA_OK;
 }

@@ -5,8 +5,8 @@ This is the B200 counterpart of the reference's graph-decode path:
 ``GraphDecoder`` (src/nova/decode.py:87-526) driving ``NovaTextModel`` /
 ``LeanDecoderLayer`` (src/nova/model.py:115-204, src/nova/layers.py:99-218)
 with ``KVInt8Cache`` (src/nova/kvattn.py:488-880) and NF4 linears
-(src/nova/quant.py).  One decode step is 6 kernel launches per layer plus one
-for the lm_head:
+(src/nova/quant.py).  One decode step is 6 kernel launches per layer plus
+one for the lm_head:
 
     1. nova_nf4_gemv      input_layernorm (prologue) + fused q|k|v projection
     2. nova_qk_norm_rope_append   q_norm/k_norm, RoPE, ring write, group requant
@@ -14,6 +14,8 @@ for the lm_head:
     4. nova_nf4_gemv      o_proj + residual add (epilogue, in place)
     5. nova_nf4_gemv      post_attention_layernorm (prologue) + gate|up + SiLU*up
     6. nova_nf4_gemv      down_proj + residual add
+
+(``qkv_fused=True`` merges 1 and 2 into nova_qkv_norm_rope_append.)
     final: nova_nf4_gemv  final norm (prologue) + 4-bit lm_head + greedy argmax
            + input_ids / pos update + next-token embedding gather (last warp)
 
@@ -218,7 +220,8 @@ class NovaDecoder:
     """
 
     def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
-                 device="cuda", pdl: bool = True, tp: TPContext | None = None, fused: bool | None = None) -> None:
+                 device="cuda", pdl: bool = True, tp: TPContext | None = None, fused: bool | None = None,
+                 qkv_fused: bool = False) -> None:
         cfg = weights.cfg
         if batch < 1 or batch > MAX_BATCH:
             raise ValueError(f"the decode path handles batch 1..{MAX_BATCH}")
@@ -264,6 +267,10 @@ class NovaDecoder:
         if self.fused and (self.batch > 2 or self.tp.active):
             raise ValueError("fused phases need batch <= 2 and no tensor parallelism")
         self.fused_ws = torch.zeros(256, dtype=torch.uint8, device=dev)
+        # qkv_fused=True: q|k|v projection + q/k norm + RoPE + append in one launch, one CTA per head
+        # (batch <= 8).  Off by default: with 48 head-owning CTAs most SMs idle, and measured in the decode
+        # step the two launches (q|k|v GEMV on every SM, then the q/k kernel) are faster.
+        self.qkv_fused = bool(qkv_fused) and self.batch <= GEMV_ROWS
 
     def _pick_chunk(self) -> int:
         """Split size for the attention (``kvattn.pick_chunk``)."""
@@ -462,21 +469,7 @@ class NovaDecoder:
                       self.resid.stride(0), B, cfg.hidden_size, stream)
 
         for li, lw in enumerate(self.w.layers):
-            self._gemv(self.resid, lw.qkv, self.qkv, norm_weight=lw.input_ln)
-            qa = _lib.QKArgs()
-            qa.qkv, qa.qkv_stride = self.qkv.data_ptr(), self.qkv.stride(0)
-            qa.q_norm_weight, qa.k_norm_weight, qa.eps = lw.q_norm.data_ptr(), lw.k_norm.data_ptr(), eps
-            qa.cos, qa.sin, qa.rope_len = self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0]
-            qa.q_out, qa.q_out_stride = self.q_rot.data_ptr(), self.q_rot.stride(0)
-            qa.tail_k, qa.tail_v = cache.tail_k[li].data_ptr(), cache.tail_v[li].data_ptr()
-            qa.kq, qa.vq = cache.kq[li].data_ptr(), cache.vq[li].data_ptr()
-            qa.kmn, qa.kst = cache.kmn[li].data_ptr(), cache.kst[li].data_ptr()
-            qa.vmn, qa.vst = cache.vmn[li].data_ptr(), cache.vst[li].data_ptr()
-            qa.pos, qa.written = cache.pos.data_ptr(), cache._written.data_ptr()
-            qa.qlen, qa.pg = cache._qlen.data_ptr(), cache._pg.data_ptr()
-            qa.batch, qa.q_heads, qa.kv_heads = B, self.hq, self.hkv
-            qa.head_dim, qa.max_len, qa.group = cfg.head_dim, self.max_len, GROUP_T
-            _lib.check(_lib.lib().nova_qk_norm_rope_append(_lib.ctypes.byref(qa), stream), "qk_norm_rope_append")
+            self._qkv_step(li, lw)
             launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
                                   cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
@@ -487,6 +480,25 @@ class NovaDecoder:
         self._gemv(self.resid, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
                    argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
                    embed_out=self.resid)
+
+    def _qkv_step(self, li: int, lw) -> None:
+        """input norm + q|k|v projection + q/k norm + RoPE + KV append of layer li: one launch
+        (nova_qkv_norm_rope_append) up to 8 rows, else the GEMV in 8-row slices and the q/k kernel."""
+        stream = _lib.stream_of(self.device)
+        qa = self._qk_args(li, lw)
+        if self.qkv_fused:
+            ga = _lib.NF4Args()
+            ga.x, ga.x_stride = self.resid.data_ptr(), self.resid.stride(0)
+            ga.norm_weight, ga.eps = lw.input_ln.data_ptr(), self.cfg.rms_norm_eps
+            ga.packed, ga.absmax, ga.absmax_fp32, ga.layout = lw.qkv.units.data_ptr(), None, 0, 1
+            ga.lut = self.lut.data_ptr()
+            ga.workspace, ga.workspace_bytes = self.gemv_ws.data_ptr(), self.gemv_ws.numel()
+            ga.m, ga.n, ga.k, ga.epilogue = self.batch, lw.qkv.n, lw.qkv.shape[1], _lib.NF4_PLAIN
+            _lib.check(_lib.lib().nova_qkv_norm_rope_append(_lib.ctypes.byref(ga), _lib.ctypes.byref(qa), stream),
+                       "qkv_norm_rope_append")
+            return
+        self._gemv(self.resid, lw.qkv, self.qkv, norm_weight=lw.input_ln)
+        _lib.check(_lib.lib().nova_qk_norm_rope_append(_lib.ctypes.byref(qa), stream), "qk_norm_rope_append")
 
     def close(self) -> None:
         """Release the graph and the peer mappings of the tensor-parallel
@@ -501,7 +513,10 @@ class NovaDecoder:
         if self.fused:   # q|k|v + q/k of layer 0, then attention + one fused launch per layer, then the lm_head
             return 1 + 2 * self.cfg.num_hidden_layers + 1
         sl = -(-self.batch // GEMV_ROWS)
-        per_layer = 4 * sl + 2   # GEMV slices + q/k norm-RoPE-append + attention
+        if self.qkv_fused:
+            per_layer = 5          # q|k|v + q/k norm-RoPE-append, attention, o, gate|up, down
+        else:
+            per_layer = 4 * sl + 2   # GEMV slices + q/k norm-RoPE-append + attention
         if self.tp.active:
             per_layer += 2       # fused all-reduce + residual add (or the residual add after NCCL), twice
         return per_layer * self.cfg.num_hidden_layers + sl

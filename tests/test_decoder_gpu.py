@@ -168,3 +168,41 @@ def test_fused_phases_match_per_op_launches(cuda_lib, kind):
             top2 = np.sort(l0[i])[-2:]
             assert top2[1] - top2[0] < 2e-2 * scale, f"step {i}: token differs without a near-tie"
             break
+
+
+@pytest.mark.parametrize("prompt_len", [150, 191])
+def test_qkv_norm_rope_append_equals_gemv_then_qk(cuda_lib, prompt_len):
+    """nova_qkv_norm_rope_append (one CTA per head) against nova_nf4_gemv +
+    nova_qk_norm_rope_append on the same state, bit for bit: q, the fp16 ring,
+    the int8 group written when the step completes one (prompt 191 -> position
+    191 is slot 63) and the device scalars; batch 2 on the real head layout."""
+    from nova_b200 import _lib
+    from nova_b200.decoder import DecoderWeights, NovaDecoder
+
+    cfg = _cfg("real")
+    W = DecoderWeights.random_init(cfg, seed=11, norm_jitter=0.1)
+    dec = NovaDecoder(W, max_len=320, batch=2, qkv_fused=True)
+    dec.prefill(torch.randint(0, cfg.vocab_size, (2, prompt_len), generator=torch.Generator().manual_seed(12)))
+    c = dec.cache
+    state = [t.clone() for t in (c.tail_k[0], c.tail_v[0], c.kq[0], c.vq[0], c.kmn[0], c.kst[0], c.vmn[0], c.vst[0],
+                                 c._written, c._qlen, c._pg)]
+
+    def snap():
+        return [dec.q_rot.clone()] + [t.clone() for t in (c.tail_k[0], c.tail_v[0], c.kq[0], c.vq[0], c.kmn[0],
+                                                           c.kst[0], c.vmn[0], c.vst[0], c._written, c._qlen, c._pg)]
+
+    dec._qkv_step(0, dec.w.layers[0])
+    fused = snap()
+    for t, v in zip((c.tail_k[0], c.tail_v[0], c.kq[0], c.vq[0], c.kmn[0], c.kst[0], c.vmn[0], c.vst[0],
+                     c._written, c._qlen, c._pg), state):
+        t.copy_(v)
+    dec.q_rot.zero_()
+    lw = dec.w.layers[0]
+    dec._gemv(dec.resid, lw.qkv, dec.qkv, norm_weight=lw.input_ln)
+    qa = dec._qk_args(0, lw)
+    _lib.check(_lib.lib().nova_qk_norm_rope_append(_lib.ctypes.byref(qa), _lib.stream_of()), "qk")
+    ref = snap()
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(zip(fused, ref)):
+        assert torch.equal(a, b), f"tensor {i} differs"
+    assert int(c._written.item()) == prompt_len + 1
