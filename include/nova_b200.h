@@ -346,6 +346,22 @@ NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
  */
 NOVA_API int nova_qkv_norm_rope_append(const nova_nf4_args* gemv, const nova_qk_args* qk, void* stream);
 
+/*
+ * Batched NF4 GEMM for M = 1..64 rows on native-layout weights:
+ * y = x @ dequant(W)^T with dequant = fp16(code * absmax) (the reference's
+ * dequantized weight, src/nova/quant.py:39-69 + the dequant-matmul of
+ * tests/test_nf4_linear.py), fp32 accumulation, the epilogues of
+ * nova_nf4_gemv (PLAIN without bias, RESIDUAL, SILU_MUL, ARGMAX with the
+ * step finalize, F32).  No norm prologue (normalize x with nova_rmsnorm).
+ * Decoded weight fragments are reused across the batch on mma.sync; the
+ * k-blocks are split over CTAs so every SM has work, with deterministic
+ * partial sums.  Workspace: nova_nf4_gemm_workspace_bytes(), zeroed once.
+ * Replaces NF4Linear.forward / fused_nf4_linear for batched rows
+ * (src/nova/quant.py:101-102, src/nova/kernels.py:243-289).
+ */
+NOVA_API int nova_nf4_gemm_workspace_bytes(int64_t n, int64_t k, int64_t* bytes);
+NOVA_API int nova_nf4_gemm(const nova_nf4_args* args, void* stream);
+
 /* ------------------------------------------------------- fused phases */
 
 /*

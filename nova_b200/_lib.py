@@ -119,6 +119,8 @@ _SIGNATURES: dict[str, list] = {
     "nova_ipc_open": [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)],
     "nova_ipc_close": [_P],
     "nova_fused_workspace_bytes": [ctypes.POINTER(_I)],
+    "nova_nf4_gemm_workspace_bytes": [_I, _I, ctypes.POINTER(_I)],
+    "nova_nf4_gemm": [ctypes.POINTER(NF4Args), _P],
     "nova_qkv_norm_rope_append": [ctypes.POINTER(NF4Args), ctypes.POINTER(QKArgs), _P],
     "nova_fused_phases": [ctypes.POINTER(FusedArgs), _P],
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],

@@ -97,16 +97,16 @@ __device__ __forceinline__ unsigned long long argmax_key(__half v, int idx) {
 }
 
 // Epilogue of one 16-row tile: lane (g, t) holds rows 16*tile+g (c[0], c[1])
-// and 16*tile+g+8 (c[2], c[3]) for batch rows m = 2t, 2t+1.
+// and 16*tile+g+8 (c[2], c[3]) for batch rows m = m0 + 2t, m0 + 2t + 1.
 template <int EPI>
-__device__ __forceinline__ void epilogue(const Params& p, int tile, const float (&c)[4], int g, int t) {
+__device__ __forceinline__ void epilogue(const Params& p, int tile, const float (&c)[4], int g, int t, int m0 = 0) {
     if (EPI == EPI_F32) {   // fp32 accumulators as they are (tensor-parallel partial sums)
         float* o = reinterpret_cast<float*>(p.out);
 #pragma unroll
         for (int hrow = 0; hrow < 2; ++hrow)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                const int m = 2 * t + e;
+                const int m = m0 + 2 * t + e;
                 if (m < p.M) o[m * p.out_stride + tile * 16 + g + 8 * hrow] = c[2 * hrow + e];
             }
         return;
@@ -116,7 +116,7 @@ __device__ __forceinline__ void epilogue(const Params& p, int tile, const float 
         const int n = tile * 8 + g;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const int m = 2 * t + e;
+            const int m = m0 + 2 * t + e;
             if (m >= p.M) continue;
             const float gate = __half2float(__float2half_rn(c[e]));
             const float up = __half2float(__float2half_rn(c[2 + e]));
@@ -131,7 +131,7 @@ __device__ __forceinline__ void epilogue(const Params& p, int tile, const float 
         const int n = tile * 16 + g + 8 * hrow;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const int m = 2 * t + e;
+            const int m = m0 + 2 * t + e;
             if (m >= p.M) continue;
             float v = c[2 * hrow + e];
             __half h;
@@ -158,7 +158,7 @@ __device__ __forceinline__ void epilogue(const Params& p, int tile, const float 
                 const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
                 k = o > k ? o : k;
             }
-            const int m = 2 * t + e;
+            const int m = m0 + 2 * t + e;
             if (g == 0 && m < p.M) atomicMax(p.argmax + m, k);
         }
     }
@@ -1409,6 +1409,239 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     for (int m = sub; m < p.M; m += 4) head_post(q, p.eps, head, m, d, 1 + sub, head_out[m], qk_red[sub], qk_y[sub]);
 }
 
+// ---------------------------------------------------------------------------
+// Batched NF4 GEMM (M <= 64 rows, native layout): y = x @ dequant(W)^T.
+// CTA = 16 warps = 512 output rows (warp w owns 32-row group 16*tile + w);
+// blockIdx.y splits the k-blocks (split-K) so every SM has work.  Per 64-wide
+// k-block all warps share one x tile [M x 64] staged by cp.async into padded
+// shared memory (rows 136 bytes apart: the 8-byte B-fragment loads of a
+// half-warp hit distinct bank pairs); each warp's weight units arrive through
+// its bulk-copy ring.  A fragments are decoded through the LUT and scaled by
+// the block's absmax in fp16 -- fp16(code * absmax), the reference's
+// dequantized weight -- and reused across up to 8 mma.sync column groups of 8
+// batch rows, accumulating in fp32.  Split-K partials go to workspace slots;
+// the last CTA of a tile adds them in split order (deterministic) and runs the
+// epilogue.  Row-wise RMSNorm is not fused here (normalize x first).
+
+constexpr int GM_WARPS = 16;
+constexpr int GM_THREADS = GM_WARPS * 32;
+constexpr int GM_MAX_M = 64;
+constexpr int GM_XSTRIDE = 68;   // halves per staged x row
+constexpr int GM_XBUF = 3;
+constexpr int GM_SLOT_FLOATS = GM_WARPS * 32 * 64;
+
+__device__ __forceinline__ uint32_t dup_lo(uint32_t v) { return __byte_perm(v, 0, 0x1010); }
+__device__ __forceinline__ uint32_t dup_hi(uint32_t v) { return __byte_perm(v, 0, 0x3232); }
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+template <int EPI>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    nf4_gemm_kernel(const __grid_constant__ Params p, int S, int stage_units, float* part, unsigned* tile_cnt,
+                    unsigned* done, int* err) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[GM_WARPS][NAT_STAGES];
+    __shared__ int s_last;
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
+    __half* xt = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
+    const int xt_elems = p.M * GM_XSTRIDE;
+    const int xt_bytes = (GM_XBUF * xt_elems * 2 + 127) / 128 * 128;
+    const int su = stage_units, stage_bytes = su * UNIT_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint8_t* ring = smem_raw + LUT_BYTES + xt_bytes + size_t(warp) * NAT_STAGES * stage_bytes;
+    const int tile = blockIdx.x, split = blockIdx.y;
+    const int KB = p.KB;
+    const int n_rg = p.N / UNIT_ROWS;
+    const int rg = tile * GM_WARPS + warp;
+    const bool has_rg = rg < n_rg;
+    const int kb0 = int(int64_t(KB) * split / S), kb1 = int(int64_t(KB) * (split + 1) / S);
+    const int nkb = kb1 - kb0;
+    const int ncg = (p.M + 7) / 8;
+
+    int issued = 0, is_b = kb0;
+    auto issue_next = [&]() {   // lane 0
+        if (!has_rg || is_b >= kb1) return;
+        const int cnt = min(su, kb1 - is_b);
+        const int st = issued % NAT_STAGES;
+        uint64_t* bar = &bars[warp][st];
+        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(ring + st * stage_bytes, p.packed + (int64_t(rg) * KB + is_b) * UNIT_BYTES, bytes, bar);
+        is_b += cnt;
+        ++issued;
+    };
+    auto load_x = [&](int i) {   // all threads: k-block kb0 + i into buffer i % GM_XBUF, one commit group
+        if (i < nkb) {
+            __half* dst = xt + (i % GM_XBUF) * xt_elems;
+            const __half* src = p.x + int64_t(kb0 + i) * 64;
+            for (int q = threadIdx.x; q < p.M * 16; q += GM_THREADS) {
+                const int m = q >> 4, j = q & 15;
+                cp_async8(dst + m * GM_XSTRIDE + 4 * j, src + m * p.x_stride + 4 * j);
+            }
+        }
+        cp_async_commit();
+    };
+
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
+        fence_mbar_init();
+        issue_next();
+        issue_next();
+    }
+    build_lut<GM_THREADS>(lut_s, p.lut);
+    pdl_trigger();
+    pdl_wait();
+    load_x(0);
+    load_x(1);
+
+    const uint32_t lut_base = smem_u32(lut_s);
+    const uint32_t laneword = uint32_t(lane) << 2;
+    float acc[2][8][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[a][c][0] = acc[a][c][1] = acc[a][c][2] = acc[a][c][3] = 0.f;
+    bool ok = true;
+    int waited = 0;
+
+    for (int i = 0; i < nkb; ++i) {
+        cp_async_wait1();
+        __syncthreads();   // x tile i visible to all warps; every warp is done with tile i - 1
+        load_x(i + 2);
+        if (!has_rg || !ok) continue;
+        const int chunk = i / su, pos = i % su;
+        if (pos == 0) {
+            if (!mbar_wait(&bars[warp][chunk % NAT_STAGES], uint32_t((chunk / NAT_STAGES) & 1), err, 2)) {
+                ok = false;
+                continue;
+            }
+            ++waited;
+        }
+        const uint8_t* unit = ring + (chunk % NAT_STAGES) * stage_bytes + pos * UNIT_BYTES;
+        const __half* xb = xt + (i % GM_XBUF) * xt_elems;
+        const uint4 c0 = lds128(unit + 16 * lane), c1 = lds128(unit + 512 + 16 * lane);
+        uint2 am;
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(am.x), "=r"(am.y)
+                     : "r"(smem_u32(unit + UNIT_CODE_BYTES + 8 * g)));
+        const uint32_t sc[4] = {dup_lo(am.x), dup_hi(am.x), dup_lo(am.y), dup_hi(am.y)};   // rows g, g+8, g+16, g+24
+        const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) {
+            const int wi = s2 >> 1;
+            const uint32_t sel0 = 0x5504u | (uint32_t((s2 & 1) * 2) << 4);
+            const uint32_t sel1 = sel0 + 0x10u;
+            uint32_t af[2][4];
+#pragma unroll
+            for (int tl = 0; tl < 2; ++tl) {
+                const uint32_t r0w = w[4 * tl + wi], r1w = w[4 * tl + 2 + wi];
+                af[tl][0] = hmul2_u32(lds32(lut_base + __byte_perm(r0w, laneword, sel0)), sc[2 * tl]);
+                af[tl][2] = hmul2_u32(lds32(lut_base + __byte_perm(r0w, laneword, sel1)), sc[2 * tl]);
+                af[tl][1] = hmul2_u32(lds32(lut_base + __byte_perm(r1w, laneword, sel0)), sc[2 * tl + 1]);
+                af[tl][3] = hmul2_u32(lds32(lut_base + __byte_perm(r1w, laneword, sel1)), sc[2 * tl + 1]);
+            }
+#pragma unroll
+            for (int cg = 0; cg < 8; ++cg) {
+                if (cg >= ncg) break;
+                const int m = 8 * cg + g;
+                uint2 bv = make_uint2(0u, 0u);
+                if (m < p.M)
+                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(bv.x), "=r"(bv.y)
+                                 : "r"(smem_u32(xb + m * GM_XSTRIDE + 16 * t + 4 * s2)));
+                mma_16816(acc[0][cg], af[0][0], af[0][1], af[0][2], af[0][3], bv.x, bv.y);
+                mma_16816(acc[1][cg], af[1][0], af[1][1], af[1][2], af[1][3], bv.x, bv.y);
+            }
+        }
+        if (pos == su - 1 || i == nkb - 1) {
+            __syncwarp();
+            if (lane == 0) {
+                fence_proxy_async();
+                issue_next();
+            }
+        }
+    }
+    if (lane == 0)   // copies issued but never waited for (only after a failed wait) land before exit
+        for (int c = waited; c < issued; ++c)
+            mbar_wait(&bars[warp][c % NAT_STAGES], uint32_t((c / NAT_STAGES) & 1), err, 2);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+
+    // split-K: every split CTA stores its fragments, the S CTAs of the tile meet (cooperative launch:
+    // all resident; the wait is bounded), then CTA `split` adds, in split order, the fragments of its
+    // share of the tile's row groups (warps [16*split/S, 16*(split+1)/S)) and runs their epilogue.
+    bool reducer = has_rg;
+    if (S > 1) {
+        float4* slot = reinterpret_cast<float4*>(part) + ((int64_t(tile) * S + split) * GM_WARPS * 32 + warp * 32 + lane) * 16;
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                if (c < ncg) slot[a * 8 + c] = make_float4(acc[a][c][0], acc[a][c][1], acc[a][c][2], acc[a][c][3]);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned* arrive = tile_cnt + 2 * tile;
+            unsigned* depart = arrive + 1;
+            __threadfence();
+            atomicAdd(arrive, 1u);
+            const unsigned long long t0 = gtime_ns();
+            while (ld_acquire_gpu_u32(arrive) < unsigned(S)) {
+                if (gtime_ns() - t0 > 1000000000ull) {
+                    atomicExch(err, 6);
+                    break;
+                }
+            }
+            __threadfence();
+            if (atomicAdd(depart, 1u) == unsigned(S - 1)) {   // every CTA of the tile is past the wait
+                *arrive = 0u;
+                *depart = 0u;
+            }
+        }
+        __syncthreads();
+        reducer = has_rg && warp >= GM_WARPS * split / S && warp < GM_WARPS * (split + 1) / S;
+        if (reducer) {
+#pragma unroll
+            for (int a = 0; a < 2; ++a)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[a][c][0] = acc[a][c][1] = acc[a][c][2] = acc[a][c][3] = 0.f;
+            for (int sp = 0; sp < S; ++sp) {
+                const float4* src = reinterpret_cast<const float4*>(part) + ((int64_t(tile) * S + sp) * GM_WARPS * 32 + warp * 32 + lane) * 16;
+                float4 v[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) v[q] = (q % 8) < ncg ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    float* a4 = acc[q / 8][q % 8];
+                    a4[0] += v[q].x; a4[1] += v[q].y; a4[2] += v[q].z; a4[3] += v[q].w;
+                }
+            }
+        }
+    }
+    if (reducer) {
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                if (c < ncg) epilogue<EPI>(p, 2 * rg + a, acc[a][c], g, t, 8 * c);
+    }
+    if (EPI == EPI_ARGMAX && p.token_out) {   // the last CTA to finish runs the step finalize
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x * gridDim.y - 1u;
+        __syncthreads();
+        if (s_last && warp == 0) {
+            __threadfence();
+            finalize_step(p, lane);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- quantizer / packer
 
 __global__ void nf4_quantize_kernel(const __half* __restrict__ w, int64_t n_blocks, int kb, int N,
@@ -1946,6 +2179,129 @@ extern "C" int nova_qkv_norm_rope_append(const nova_nf4_args* g, const nova_qk_a
     if (err != cudaSuccess) {
         cudaGetLastError();
         return fail(NOVA_ERR_CUDA, "nova_qkv_norm_rope_append: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
+}
+
+// ---------------------------------------------------------------- batched GEMM (host)
+
+// Workspace: [tile counters (up to 1000 tiles), finalize counter, error word | split-K slots].  The counters
+// sit at the same place for every shape, so one workspace sized for the largest GEMM serves them all.
+constexpr int64_t GM_COUNTER_BYTES = 4096;
+
+// Split count: no more CTAs than SMs (one wave), and about sqrt(3 * k-blocks): each split adds
+// ~KB/S k-block steps of work per CTA but one more 128 KB partial for the last CTA to add.
+static void gemm_shape(int64_t n, int64_t k, int64_t* tiles, int64_t* splits) {
+    const int64_t n_rg = n / UNIT_ROWS;
+    const int64_t t = (n_rg + GM_WARPS - 1) / GM_WARPS;
+    const int64_t kb = k / 64;
+    int64_t s = int64_t(sm_count()) / t;
+    s = std::min<int64_t>(s, int64_t(sqrt(3.0 * double(kb))));
+    s = std::max<int64_t>(1, std::min<int64_t>(s, kb / 2));
+    *tiles = t;
+    *splits = s;
+}
+
+extern "C" int nova_nf4_gemm_workspace_bytes(int64_t n, int64_t k, int64_t* bytes) {
+    if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
+    if (n <= 0 || n % UNIT_ROWS || k <= 0 || k % 64) return fail(NOVA_ERR_INVALID, "N multiple of 32, K of 64");
+    int64_t t = 0, s = 0;
+    gemm_shape(n, k, &t, &s);
+    const int64_t slots = s > 1 ? t * s * int64_t(GM_SLOT_FLOATS) * 4 : 0;
+    *bytes = GM_COUNTER_BYTES + slots;   // counters first (fixed place for every shape), then the split slots
+    return NOVA_OK;
+}
+
+extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
+    if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
+    const int64_t m = a->m, n = a->n, k = a->k;
+    if (a->layout != 1) return fail(NOVA_ERR_UNSUPPORTED, "native-layout weights only");
+    if (m < 1 || m > GM_MAX_M) return fail(NOVA_ERR_UNSUPPORTED, "M must be in [1, 64], got %lld", (long long)m);
+    if (n <= 0 || n % UNIT_ROWS || n > (1 << 30) || k <= 0 || k % 64 || k > (1 << 20))
+        return fail(NOVA_ERR_INVALID, "N multiple of 32, K multiple of 64");
+    if (a->norm_weight) return fail(NOVA_ERR_UNSUPPORTED, "no norm prologue in the batched GEMM (normalize x first)");
+    if (a->bias) return fail(NOVA_ERR_UNSUPPORTED, "no bias in the batched GEMM");
+    const int epi = int(a->epilogue);
+    if (epi < EPI_PLAIN || epi > EPI_F32) return fail(NOVA_ERR_INVALID, "bad epilogue %d", epi);
+    if (!a->x || !a->packed || !a->lut || !a->out || !a->workspace) return fail(NOVA_ERR_INVALID, "NULL pointer");
+    if (epi == EPI_RESIDUAL && !a->residual) return fail(NOVA_ERR_INVALID, "residual epilogue needs residual");
+    if (epi == EPI_ARGMAX && !a->argmax) return fail(NOVA_ERR_INVALID, "argmax epilogue needs argmax");
+    if (a->embed && (!a->token_out || !a->embed_out || a->embed_dim <= 0 || a->embed_dim % 8))
+        return fail(NOVA_ERR_INVALID, "embedding gather needs token_out, embed_out and embed_dim % 8 == 0");
+    auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
+    if (mis(a->x, 16) || (a->x_stride % 8) || mis(a->packed, 16) || mis(a->workspace, 256) || mis(a->argmax, 8) ||
+        mis(a->embed, 16) || mis(a->embed_out, 16) || (a->embed_out_stride % 8) || (epi == EPI_F32 && mis(a->out, 4)))
+        return fail(NOVA_ERR_ALIGN, "x / packed 16-byte aligned (x_stride % 8), workspace 256");
+    int64_t need = 0;
+    nova_nf4_gemm_workspace_bytes(n, k, &need);
+    if (a->workspace_bytes < need) return fail(NOVA_ERR_INVALID, "workspace too small: %lld < %lld",
+                                               (long long)a->workspace_bytes, (long long)need);
+    int64_t tiles = 0, splits = 0;
+    gemm_shape(n, k, &tiles, &splits);
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.x = (const __half*)a->x;
+    p.x_stride = a->x_stride;
+    p.packed = (const uint8_t*)a->packed;
+    p.lut = (const uint32_t*)a->lut;
+    p.residual = (const __half*)a->residual;
+    p.res_stride = a->res_stride;
+    p.out = (__half*)a->out;
+    p.out_stride = a->out_stride;
+    p.argmax = (unsigned long long*)a->argmax;
+    p.token_out = a->token_out;
+    p.pos = a->pos;
+    p.embed = (const __half*)a->embed;
+    p.embed_out = (__half*)a->embed_out;
+    p.embed_out_stride = a->embed_out_stride;
+    p.embed_dim = int(a->embed_dim);
+    p.M = int(m);
+    p.N = int(n);
+    p.K = int(k);
+    p.KB = int(k / 64);
+    if (tiles > 500) return fail(NOVA_ERR_INVALID, "N too large for the batched GEMM (at most 256000 rows)");
+    uint8_t* ws = (uint8_t*)a->workspace;
+    float* part = (float*)(ws + GM_COUNTER_BYTES);
+    unsigned* tile_cnt = (unsigned*)ws;   // arrive / depart per tile
+    unsigned* done = tile_cnt + 1000;
+    int* errp = (int*)(done + 1);
+    p.done = done;   // re-armed by the step finalize
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "device queries failed");
+    }
+    const int64_t xt_bytes = (GM_XBUF * m * GM_XSTRIDE * 2 + 127) / 128 * 128;
+    const int64_t ring_unit = int64_t(GM_WARPS) * NAT_STAGES * UNIT_BYTES;
+    const int64_t su = std::min<int64_t>(3, (optin - int64_t(LUT_BYTES) - xt_bytes - 1024) / ring_unit);
+    if (su < 1) return fail(NOVA_ERR_UNSUPPORTED, "shared memory");
+    const int64_t nsmem = int64_t(LUT_BYTES) + xt_bytes + su * ring_unit;
+    using GKern = void (*)(Params, int, int, float*, unsigned*, unsigned*, int*);
+    static const GKern kernels[5] = {nf4_gemm_kernel<0>, nf4_gemm_kernel<1>, nf4_gemm_kernel<2>, nf4_gemm_kernel<3>,
+                                     nf4_gemm_kernel<4>};
+    static int64_t smem_set[5] = {};
+    if (int rc = prepare_smem(kernels[epi], nsmem, &smem_set[epi])) return rc;
+    cudaError_t err;
+    if (splits > 1) {   // the split CTAs of a tile wait for one another: all must be resident
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(unsigned(tiles), unsigned(splits));
+        cfg.blockDim = dim3(GM_THREADS);
+        cfg.dynamicSmemBytes = size_t(nsmem);
+        cfg.stream = (cudaStream_t)stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        err = cudaLaunchKernelEx(&cfg, kernels[epi], p, int(splits), int(su), part, tile_cnt, done, errp);
+    } else {
+        err = launch(kernels[epi], dim3(unsigned(tiles), 1u), dim3(GM_THREADS), size_t(nsmem), (cudaStream_t)stream, p,
+                     1, int(su), part, tile_cnt, done, errp);
+    }
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_nf4_gemm: launch failed: %s", cudaGetErrorString(err));
     }
     return NOVA_OK;
 }

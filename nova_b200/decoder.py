@@ -46,14 +46,14 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .kernels import build_nf4_lut, fused_rms_norm, gemv_workspace, nf4_gemv, pack_native
+from .kernels import build_nf4_lut, fused_rms_norm, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native
 from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk
 from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
 
 
 MAX_BATCH = 64
-GEMV_ROWS = 8   # rows per nova_nf4_gemv launch (larger batches run in slices of 8 rows)
+GEMV_ROWS = 8   # rows per nova_nf4_gemv launch; larger batches use the batched GEMM (nova_nf4_gemm)
 
 
 @dataclass
@@ -258,6 +258,14 @@ class NovaDecoder:
         self.input_ids = torch.zeros(B, dtype=torch.int64, device=dev)
         n_max = max(cfg.vocab_size, 2 * self.inter, self.q_dim + 2 * self.kv_dim, cfg.hidden_size)
         self.gemv_ws = gemv_workspace(dev, n_max).clone()   # shared by every GEMV of the step
+        if self.batch > GEMV_ROWS:   # batched GEMM: one workspace for every shape, normalized-x scratch
+            shapes = [(self.q_dim + 2 * self.kv_dim, cfg.hidden_size), (cfg.hidden_size, self.q_dim),
+                      (2 * self.inter, cfg.hidden_size), (cfg.hidden_size, self.inter),
+                      (cfg.vocab_size, cfg.hidden_size)]
+            self.gemm_ws = max((gemm_workspace(dev, n, k) for n, k in shapes), key=lambda t: t.numel()).clone()
+            self.xn = torch.zeros(B, cfg.hidden_size, dtype=f16, device=dev)
+        else:
+            self.gemm_ws = self.xn = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.pdl = bool(pdl)
         # fused=True: one cooperative launch per layer for o -> gate|up -> down -> next q|k|v -> q/k norm
@@ -364,10 +372,19 @@ class NovaDecoder:
 
     def _gemv(self, x, w: NF4Weight, out, *, epilogue: int = _lib.NF4_PLAIN, norm_weight=None, residual=None,
               argmax=None, token_out=None, pos=None, embed=None, embed_out=None) -> None:
-        """nova_nf4_gemv over the batch in slices of GEMV_ROWS rows (one launch
-        per slice; the step-finalize position update runs on the last one)."""
+        """The step's NF4 projection: nova_nf4_gemv up to GEMV_ROWS rows, else
+        nova_nf4_gemm (after nova_rmsnorm when the projection has a norm prologue)."""
         B = x.shape[0]
         eps = self.cfg.rms_norm_eps
+        if B > GEMV_ROWS:   # batched GEMM: weights read once for all rows; the norm runs first
+            if norm_weight is not None:
+                n_in = x.shape[1]
+                _lib.call("nova_rmsnorm", x.data_ptr(), x.stride(0), None, 0, None, 0, norm_weight.data_ptr(),
+                          self.xn.data_ptr(), self.xn.stride(0), B, n_in, float(eps), _lib.stream_of(self.device))
+                x = self.xn[:, :n_in]
+            nf4_gemm(x, w.units, self.lut, out, n=w.n, epilogue=epilogue, residual=residual, argmax=argmax,
+                     token_out=token_out, pos=pos, embed=embed, embed_out=embed_out, workspace=self.gemm_ws)
+            return
         for r in range(0, B, GEMV_ROWS):
             sl = slice(r, min(B, r + GEMV_ROWS))
             last = sl.stop == B
@@ -512,14 +529,15 @@ class NovaDecoder:
         """Kernels of this library per step (NCCL all-reduces not counted)."""
         if self.fused:   # q|k|v + q/k of layer 0, then attention + one fused launch per layer, then the lm_head
             return 1 + 2 * self.cfg.num_hidden_layers + 1
-        sl = -(-self.batch // GEMV_ROWS)
         if self.qkv_fused:
             per_layer = 5          # q|k|v + q/k norm-RoPE-append, attention, o, gate|up, down
+        elif self.batch > GEMV_ROWS:
+            per_layer = 8          # 2 norms + 4 GEMMs + q/k norm-RoPE-append + attention
         else:
-            per_layer = 4 * sl + 2   # GEMV slices + q/k norm-RoPE-append + attention
+            per_layer = 6
         if self.tp.active:
             per_layer += 2       # fused all-reduce + residual add (or the residual add after NCCL), twice
-        return per_layer * self.cfg.num_hidden_layers + sl
+        return per_layer * self.cfg.num_hidden_layers + (2 if self.batch > GEMV_ROWS else 1)
 
     @torch.inference_mode()
     def fill_random(self, ctx: int, seed: int = 0) -> None:

@@ -163,6 +163,46 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
     return out
 
 
+def gemm_workspace(device: torch.device, n: int, k: int) -> torch.Tensor:
+    """Cached zeroed workspace for ``nova_nf4_gemm`` with N rows and K columns."""
+    out = _lib.ctypes.c_int64(0)
+    _lib.call("nova_nf4_gemm_workspace_bytes", int(n), int(k), _lib.ctypes.byref(out))
+    key = (str(device), -int(out.value))
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        ws = torch.zeros(int(out.value), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def nf4_gemm(x: torch.Tensor, units: torch.Tensor, lut: torch.Tensor, out: torch.Tensor, *, n: int,
+             epilogue: int = _lib.NF4_PLAIN, residual: torch.Tensor | None = None,
+             argmax: torch.Tensor | None = None, token_out: torch.Tensor | None = None,
+             pos: torch.Tensor | None = None, embed: torch.Tensor | None = None,
+             embed_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``nova_nf4_gemm``: x ``[M <= 64, K]`` against the native unit stream of an
+    ``[n, K]`` NF4 weight; out ``[M, n]`` (``[M, n/2]`` for SiLU*up)."""
+    m, k = x.shape
+    if x.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("x/out must have a contiguous last dimension")
+    ws = gemm_workspace(x.device, n, k) if workspace is None else workspace
+    a = _lib.NF4Args()
+    a.x, a.x_stride = x.data_ptr(), x.stride(0)
+    a.norm_weight, a.eps = None, 0.0
+    a.packed, a.absmax, a.absmax_fp32, a.layout = units.data_ptr(), None, 0, 1
+    a.lut, a.bias = lut.data_ptr(), None
+    a.residual, a.res_stride = (_lib.ptr(residual), residual.stride(0) if residual is not None else 0)
+    a.out, a.out_stride = out.data_ptr(), out.stride(0)
+    a.argmax, a.token_out, a.pos = _lib.ptr(argmax), _lib.ptr(token_out), _lib.ptr(pos)
+    a.embed, a.embed_out = _lib.ptr(embed), _lib.ptr(embed_out)
+    a.embed_out_stride = embed_out.stride(0) if embed_out is not None else 0
+    a.embed_dim = embed.shape[1] if embed is not None else 0
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.m, a.n, a.k, a.epilogue = m, n, k, int(epilogue)
+    _lib.check(_lib.lib().nova_nf4_gemm(_lib.ctypes.byref(a), _lib.stream_of(x.device)), "nova_nf4_gemm")
+    return out
+
+
 def fused_nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, lut: torch.Tensor,
                      out_features: int, bias: torch.Tensor | None = None, **launch_overrides: int) -> torch.Tensor:
     """NF4 linear ``x @ dequant(packed, absmax, code).T + bias``
