@@ -82,6 +82,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -94,14 +98,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: every spin in this library gives up after a fixed number of
-// polls, records `code` in the device error word and returns false.
-constexpr int kWaitPolls = 1 << 22;
+// Bounded wait: every spin in this library gives up after kWaitNs of wall
+// time (a try_wait may itself suspend for a system-dependent while, so the
+// bound is on the clock, not on the number of polls), records `code` in the
+// device error word and returns false.
+constexpr unsigned long long kWaitNs = 200ull * 1000 * 1000;
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-    for (int i = 0; i < kWaitPolls; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    if (err) atomicExch(err, code);
-    return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > kWaitNs) {
+            if (err) atomicExch(err, code);
+            return false;
+        }
+    }
 }
 
 // 1D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,

@@ -551,10 +551,6 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
 // `full` completes when all 16 warps wrote segment j, `empty` when its reducer
 // has read it, and no warp writes segment j + 1 before that.
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 template <int EPI, bool XG>
 __global__ void __launch_bounds__(NAT_THREADS, 1)
     nf4_gemv_cta_kernel(const __grid_constant__ Params p, int stage_units, int* err) {
