@@ -482,9 +482,9 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     for (int c = 0; c < n_chunks; ++c) {
         const int stage = c % NAT_STAGES;
         if (!mbar_wait(&bars[warp][stage], uint32_t((c / NAT_STAGES) & 1), err, 2)) {
-            // give the other copy in flight a bounded chance to land, then leave
-            if (c + 1 < n_chunks) mbar_wait(&bars[warp][(c + 1) % NAT_STAGES], uint32_t(((c + 1) / NAT_STAGES) & 1),
-                                            err, 2);
+            // give the other copies in flight a bounded chance to land, then leave
+            for (int c2 = c + 1; c2 < n_chunks && c2 < c + NAT_STAGES; ++c2)
+                mbar_wait(&bars[warp][c2 % NAT_STAGES], uint32_t((c2 / NAT_STAGES) & 1), err, 2);
             return;
         }
         const int64_t u0 = u_begin + int64_t(c) * stage_units;
@@ -1490,8 +1490,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
         for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
         fence_mbar_init();
-        issue_next();
-        issue_next();
+        for (int k2 = 0; k2 < NAT_STAGES; ++k2) issue_next();
     }
     build_lut<GM_THREADS>(lut_s, p.lut);
     pdl_trigger();
