@@ -252,6 +252,15 @@ NOVA_API int nova_nf4_pack_native(const void* packed, const void* absmax, int ab
                                   int64_t k, void* stream);
 
 /*
+ * The tcgen05 GEMM's unit layout (nf4 args layout = 2): the same 32-row x
+ * 64-k, 1088-byte units, except that MMA lane (g, t) holds for each of its
+ * rows the code bytes 2t + 8p and 2t + 8p + 1 (p = 0..3) instead of bytes
+ * 8t .. 8t + 7.  Same arguments as nova_nf4_pack_native.
+ */
+NOVA_API int nova_nf4_pack_tc(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n,
+                              int64_t k, void* stream);
+
+/*
  * Blockwise NF4 quantizer: w fp16 [N, K] -> packed uint8 [N, K/2], absmax
  * [K/64, N].  Level = number of the 15 fp32 `midpoints` below w/absmax (ties
  * to the lower level); an all-zero block uses absmax 1 for the division.
@@ -347,15 +356,18 @@ NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
 NOVA_API int nova_qkv_norm_rope_append(const nova_nf4_args* gemv, const nova_qk_args* qk, void* stream);
 
 /*
- * Batched NF4 GEMM for M = 1..64 rows on native-layout weights:
+ * Batched NF4 GEMM for M = 1..64 rows:
  * y = x @ dequant(W)^T with dequant = fp16(code * absmax) (the reference's
  * dequantized weight, src/nova/quant.py:39-69 + the dequant-matmul of
  * tests/test_nf4_linear.py), fp32 accumulation, the epilogues of
  * nova_nf4_gemv (PLAIN without bias, RESIDUAL, SILU_MUL, ARGMAX with the
  * step finalize, F32).  No norm prologue (normalize x with nova_rmsnorm).
- * Decoded weight fragments are reused across the batch on mma.sync; the
- * k-blocks are split over CTAs so every SM has work, with deterministic
- * partial sums.  Workspace: nova_nf4_gemm_workspace_bytes(), zeroed once.
+ * layout = 2 (units from nova_nf4_pack_tc): tcgen05 tensor cores -- weights
+ * decoded into tensor memory, x tiles by TMA, fp32 accumulators in tensor
+ * memory, (tile, k-block) work split evenly over one wave of CTAs with
+ * deterministic partial sums.  layout = 1 (nova_nf4_pack_native): mma.sync.
+ * x needs a 16-byte aligned base and a row stride that is a multiple of 8.
+ * Workspace: nova_nf4_gemm_workspace_bytes(), zeroed once.
  * Replaces NF4Linear.forward / fused_nf4_linear for batched rows
  * (src/nova/quant.py:101-102, src/nova/kernels.py:243-289).
  */

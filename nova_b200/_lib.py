@@ -110,6 +110,7 @@ _SIGNATURES: dict[str, list] = {
     "nova_nf4_dequant": [_P, _P, _i, _P, _P, _I, _I, _P],
     "nova_nf4_native_bytes": [_I, _I, ctypes.POINTER(_I)],
     "nova_nf4_pack_native": [_P, _P, _i, _P, _I, _I, _P],
+    "nova_nf4_pack_tc": [_P, _P, _i, _P, _I, _I, _P],
     "nova_set_launch_flags": [_i],
     "nova_rmsnorm": [_P, _I, _P, _I, _P, _I, _P, _P, _I, _I, _I, ctypes.c_double, _P],
     "nova_residual_add_f32": [_P, _I, _P, _I, _I, _I, _P],

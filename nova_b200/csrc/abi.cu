@@ -64,6 +64,23 @@ int make_tmap_u8_rows128(CUtensorMap* tm, const void* base, uint64_t rows, uint3
     return NOVA_OK;
 }
 
+int make_tmap_f16_rows64(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                         uint32_t box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(NOVA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (no CUDA driver?)");
+    if (reinterpret_cast<uintptr_t>(base) % 16 || row_stride % 8)
+        return fail(NOVA_ERR_ALIGN, "tensor map base 16-byte aligned and row stride a multiple of 8");
+    cuuint64_t gdim[2] = {cols, rows};
+    cuuint64_t gstride[1] = {row_stride * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NOVA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return NOVA_OK;
+}
+
 }  // namespace nova
 
 extern "C" const char* nova_version(void) { return "nova_b200 0.1 (sm_100a, abi 1)"; }

@@ -25,6 +25,12 @@ int check_launch(const char* what);
 // box and the 128-byte swizzle (used for int8 K/V code tiles).
 int make_tmap_u8_rows128(CUtensorMap* tm, const void* base, uint64_t rows, uint32_t box_rows);
 
+// Encodes a 2D fp16 tensor map [rows, cols] (row stride in elements, a
+// multiple of 8) with a (box_rows x 64) box and the 128-byte swizzle; rows
+// past `rows` read as zero.
+int make_tmap_f16_rows64(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                         uint32_t box_rows);
+
 // Launch flags (nova_set_launch_flags): bit 0 = programmatic dependent launch.
 int launch_flags();
 
@@ -129,6 +135,97 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+// 5th-generation tensor cores: tensor-memory (TMEM) allocation by one whole
+// warp, MMAs issued by one thread with shared-memory matrix descriptors,
+// completion signalled on an mbarrier by tcgen05.commit, accumulators read
+// back with tcgen05.ld (a warp reaches the 32 TMEM lanes of its quarter,
+// warp_id % 4).
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] = A * B^T (+ D when accumulate != 0), kind::f16 (A and B both fp16),
+// A and B given by shared-memory descriptors.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// One arrival on `bar` once every tcgen05 operation issued so far by this
+// thread has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns: thread i gets lane (taddr lane + i).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 16 lanes x 256 bits, 4 repeats along the columns: thread (g = lane / 4,
+// t = lane % 4) supplies, for repeat p, registers 4p..4p+3 = (lane g, columns
+// 8p + 2t, 8p + 2t + 1), (lane g + 8, the same columns), relative to taddr.
+__device__ __forceinline__ void tmem_st_16x256b_x4(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3,
+                                                   uint32_t r4, uint32_t r5, uint32_t r6, uint32_t r7, uint32_t r8,
+                                                   uint32_t r9, uint32_t r10, uint32_t r11, uint32_t r12, uint32_t r13,
+                                                   uint32_t r14, uint32_t r15) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(r4), "r"(r5), "r"(r6), "r"(r7), "r"(r8), "r"(r9), "r"(r10), "r"(r11),
+        "r"(r12), "r"(r13), "r"(r14), "r"(r15)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// As tc_mma_f16 with A read from tensor memory (lane = row, each 32-bit column
+// two consecutive k) at a_tmem.
+__device__ __forceinline__ void tc_mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte swizzle
+// layout: rows of 64 fp16 (128 B), 8-row groups 1024 B apart (stride byte
+// offset), atoms 1024-byte aligned; the start address may step by 32 B per
+// K = 16 slice inside the atom.  Fields: start >> 4 [0,14), leading byte
+// offset >> 4 [16,30) (unused for this layout, 1), stride byte offset >> 4
+// [32,46), descriptor version 1 [46,48), swizzle mode 2 = 128 B [61,64).
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, fp16 A and B, both
+// K-major, M x N.
+__host__ __device__ constexpr uint32_t tc_idesc_f16(int m, int n) {
+    return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
 // 2D tiled TMA load (no multicast).  x is the innermost coordinate in

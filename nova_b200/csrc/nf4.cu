@@ -1637,6 +1637,387 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Batched NF4 GEMM on the tcgen05 tensor cores (M = 1..64 batch rows).
+//
+// Tile = 128 weight rows (four 32-row groups) x all batch rows; the MMA is
+// M = 128 (weight rows) x N = M rounded up to 16 (batch rows) x K = 16, fp16
+// operands, fp32 accumulators in tensor memory.  The work items are the
+// (tile, k-block) pairs, tile-major; CTA c of the one-wave grid takes the
+// contiguous range [W*c/G, W*(c+1)/G) (stream-K), so every SM decodes the
+// same number of weight units whatever N and K are.  Per item:
+//   producer warp   bulk-copies the tile's 4 units of the k-block (4352 B)
+//                   into the weight ring and TMA-loads the x tile [N x 64]
+//                   (128-byte swizzle; rows past M read as zero);
+//   decode warps    warp d decodes row group d % 4 of the items with
+//                   parity d / 4: LUT -> fp16 code, times the row's absmax in
+//                   fp16 (fp16(code * absmax), the reference's dequantized
+//                   weight), stored as the A tile in the UMMA K-major
+//                   128-byte-swizzle layout;
+//   MMA thread      4 x tcgen05.mma (K = 16 slices of the 64-wide k-block)
+//                   into one of two TMEM accumulators, tcgen05.commit frees
+//                   the A and x stages;
+//   epilogue warps  at the end of a tile segment read their TMEM lane quarter
+//                   (thread = weight row, registers = batch rows) and either
+//                   run the epilogue (whole tile) or store the partial; the
+//                   last contributor of a split tile (arrival counter) adds
+//                   all partials in CTA order -- deterministic -- and runs it.
+// Every wait is bounded; on a failed wait the roles stop, the MMA thread
+// waits for its MMAs and the producer for its copies before TMEM is freed.
+
+constexpr int TC_ROWS = 128;
+constexpr int TC_GROUPS = 3;                       // decode warp groups (item j -> group j % 3)
+constexpr int TC_DEC_WARPS = 4 * TC_GROUPS;
+constexpr int TC_PROD_WARP = TC_DEC_WARPS;         // weight units
+constexpr int TC_MMA_WARP = TC_DEC_WARPS + 1;
+constexpr int TC_EPI_WARP0 = TC_DEC_WARPS + 2;     // 4 epilogue warps: lane quarters (w % 4) all covered
+constexpr int TC_XPROD_WARP = TC_EPI_WARP0 + 4;    // x tiles
+constexpr int TC_WARPS = TC_XPROD_WARP + 1;
+constexpr int TC_THREADS = TC_WARPS * 32;
+constexpr int TC_AS = 2 * TC_GROUPS, TC_XS = TC_AS;   // one stage-free barrier for both rings
+constexpr int TC_WS_MAX = 24;                      // weight ring depth: as many stages as shared memory holds
+constexpr int TC_KG = 2;                           // k-blocks per work item (one MMA-thread handoff)
+constexpr int TC_W_BYTES = 4 * TC_KG * UNIT_BYTES;
+constexpr int TC_ACC_COLS = 64;                    // TMEM columns: accumulators [0, 128), A stages from 128
+constexpr int TC_A_COL0 = 2 * TC_ACC_COLS;
+constexpr int TC_A_COLS = 32 * TC_KG;              // 128 rows x 64 k fp16 = 32 columns of fp16x2 per k-block
+constexpr int TC_TMEM_COLS = 512;
+constexpr int TC_SLOT_FLOATS = 64 * TC_ROWS;       // partial tile [batch row / 4][weight row][4]
+constexpr int TC_MAX_M = 64;
+constexpr int TC_MIN_ITEMS = 4;                    // work items per CTA at least (bounds the split fan-in)
+
+struct TcArgs {
+    int n_mma;            // MMA N: M rounded up to 16
+    int ws;               // weight ring stages (<= TC_WS_MAX)
+    int G;                // CTAs
+    int64_t W;            // work items = tiles * ceil(KB / TC_KG)
+    float* part;          // [G][2][TC_SLOT_FLOATS]
+    unsigned* tile_cnt;   // [tiles][4] arrivals of split tiles per lane quarter
+    int* err;
+};
+
+// Epilogue of one weight row n for batch rows 0..M-1 (v[m]); every lane of
+// the warp calls it (SiLU*up and argmax exchange values between lanes).
+template <int EPI>
+__device__ __forceinline__ void tc_epilogue_row(const Params& p, int n, int rho, const float (&v)[TC_MAX_M],
+                                                int lane) {
+    const bool valid = n < p.N;
+    if constexpr (EPI == EPI_SILU_MUL) {   // rows 16i..16i+7 gate, 16i+8..16i+15 the matching up rows
+        const bool gate_row = (rho & 15) < 8;
+        const int n_out = (n >> 4) * 8 + (n & 7);
+#pragma unroll
+        for (int m = 0; m < TC_MAX_M; ++m) {
+            if (m >= p.M) break;
+            const float upv = __shfl_down_sync(0xffffffffu, v[m], 8);
+            if (valid && gate_row) {
+                const float gate = __half2float(__float2half_rn(v[m]));
+                const float up = __half2float(__float2half_rn(upv));
+                const float s = __half2float(__float2half_rn(__fdiv_rn(gate, 1.0f + expf(-gate))));
+                p.out[m * p.out_stride + n_out] = __float2half_rn(s * up);
+            }
+        }
+        return;
+    } else if constexpr (EPI == EPI_F32) {
+        float* o = reinterpret_cast<float*>(p.out);
+#pragma unroll
+        for (int m = 0; m < TC_MAX_M; ++m) {
+            if (m >= p.M) break;
+            if (valid) o[m * p.out_stride + n] = v[m];
+        }
+        return;
+    } else {
+#pragma unroll
+        for (int m = 0; m < TC_MAX_M; ++m) {
+            if (m >= p.M) break;
+            __half h = __float2half_rn(v[m]);
+            if (EPI == EPI_RESIDUAL && valid)
+                h = __float2half_rn(__half2float(__ldcg(p.residual + m * p.res_stride + n)) + __half2float(h));
+            if (valid) p.out[m * p.out_stride + n] = h;
+            if (EPI == EPI_ARGMAX) {
+                unsigned long long k = valid ? argmax_key(h, n) : 0ull;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
+                    k = o > k ? o : k;
+                }
+                if (lane == 0 && k) atomicMax(p.argmax + m, k);
+            }
+        }
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    nf4_gemm_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap xmap, const TcArgs ta) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_w[TC_WS_MAX], empty_w[TC_WS_MAX], full_x[TC_XS];
+    __shared__ __align__(8) uint64_t full_a[TC_AS], empty_a[TC_AS], acc_full[2], acc_empty[2], drain;
+    __shared__ uint32_t tmem_s;
+    // 1024-byte aligned carve-up: x ring | LUT | weight ring
+    const uint32_t raw_s = smem_u32(smem_raw);
+    uint8_t* x_ring = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+    const int xs_bytes = ta.n_mma * 128;
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(x_ring + TC_XS * TC_KG * xs_bytes);
+    uint8_t* w_ring = reinterpret_cast<uint8_t*>(lut_s) + LUT_BYTES;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x;
+    const int KB = p.KB;
+    const int n_rg = p.N / UNIT_ROWS;
+    const int64_t u0 = ta.W * c / ta.G, u1 = ta.W * (c + 1) / ta.G;
+    const int n_items = int(u1 - u0);
+    const int NKG = (KB + TC_KG - 1) / TC_KG;   // items per tile
+    const int first_tile = int(u0 / NKG);
+    const int WS = ta.ws;
+
+    auto issue_w = [&](int j) {   // producer lane 0: the tile's units of item j (row group r: nk consecutive units)
+        const int64_t u = u0 + j;
+        const int T = int(u / NKG), kb0 = int(u % NKG) * TC_KG;
+        const int nk = min(TC_KG, KB - kb0);
+        const int rgs = min(4, n_rg - 4 * T);
+        const int s = j % WS;
+        mbar_arrive_expect_tx(&full_w[s], uint32_t(rgs * nk) * UNIT_BYTES);
+        for (int r = 0; r < rgs; ++r)
+            bulk_g2s(w_ring + s * TC_W_BYTES + r * TC_KG * UNIT_BYTES,
+                     p.packed + (int64_t(4 * T + r) * KB + kb0) * UNIT_BYTES, uint32_t(nk) * UNIT_BYTES, &full_w[s]);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < WS; ++s) {
+            mbar_init(&full_w[s], 1);
+            mbar_init(&empty_w[s], 4);
+        }
+        for (int s = 0; s < TC_XS; ++s) mbar_init(&full_x[s], 1);
+        for (int s = 0; s < TC_AS; ++s) {
+            mbar_init(&full_a[s], 4);
+            mbar_init(&empty_a[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(&drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == TC_MMA_WARP) {
+        tmem_alloc(&tmem_s, TC_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_s;
+    int issued_w = 0;
+    if (warp == TC_PROD_WARP && lane == 0)   // weights: independent of every earlier kernel
+        for (; issued_w < WS && issued_w < n_items; ++issued_w) issue_w(issued_w);
+    build_lut<TC_THREADS>(lut_s, p.lut);
+    pdl_trigger();
+    pdl_wait();
+    __syncthreads();
+
+    if (warp == TC_PROD_WARP) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int j = issued_w; j < n_items; ++j) {
+                if (!mbar_wait(&empty_w[j % WS], uint32_t(((j / WS) + 1) & 1), ta.err, 20)) {
+                    ok = false;
+                    break;
+                }
+                issue_w(j);
+                ++issued_w;
+            }
+            if (!ok)   // copies in flight land before the CTA ends
+                for (int j = max(0, issued_w - WS); j < issued_w; ++j)
+                    mbar_wait(&full_w[j % WS], uint32_t((j / WS) & 1), ta.err, 20);
+        }
+    } else if (warp == TC_XPROD_WARP) {
+        if (lane == 0) {
+            int issued_x = 0;
+            bool ok = true;
+            for (int j = 0; j < n_items; ++j) {
+                if (j >= TC_XS && !mbar_wait(&empty_a[j % TC_AS], uint32_t(((j / TC_AS) + 1) & 1), ta.err, 21)) {
+                    ok = false;
+                    break;
+                }
+                const int s = j % TC_XS;
+                const int kb0 = int((u0 + j) % NKG) * TC_KG, nk = min(TC_KG, KB - kb0);
+                mbar_arrive_expect_tx(&full_x[s], uint32_t(nk * xs_bytes));
+                for (int q = 0; q < nk; ++q)
+                    tma_load_2d(x_ring + (s * TC_KG + q) * xs_bytes, &xmap, (kb0 + q) * 64, 0, &full_x[s]);
+                ++issued_x;
+            }
+            if (!ok)
+                for (int j = max(0, issued_x - TC_XS); j < issued_x; ++j)
+                    mbar_wait(&full_x[j % TC_XS], uint32_t((j / TC_XS) & 1), ta.err, 21);
+        }
+    } else if (warp < TC_DEC_WARPS) {
+        const int grp = warp >> 2, r = warp & 3, g = lane >> 2, t = lane & 3;
+        const uint32_t lut_base = smem_u32(lut_s);
+        const uint32_t laneword = uint32_t(lane) << 2;
+        int T = int((u0 + grp) / NKG), kg = int((u0 + grp) % NKG);
+        for (int j = grp; j < n_items; j += TC_GROUPS) {
+            const int nk = min(TC_KG, KB - kg * TC_KG);
+            if (!mbar_wait(&full_w[j % WS], uint32_t((j / WS) & 1), ta.err, 22)) break;
+            if (j >= TC_AS && !mbar_wait(&empty_a[j % TC_AS], uint32_t(((j / TC_AS) + 1) & 1), ta.err, 23)) break;
+            for (int q = 0; q < nk && 4 * T + r < n_rg; ++q) {
+                const uint8_t* unit = w_ring + (j % WS) * TC_W_BYTES + (r * TC_KG + q) * UNIT_BYTES;
+                const uint4 c0 = lds128(unit + 16 * lane), c1 = lds128(unit + 512 + 16 * lane);
+                uint2 am;
+                asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(am.x), "=r"(am.y)
+                             : "r"(smem_u32(unit + UNIT_CODE_BYTES + 8 * g)));
+                // rows g, g+8, g+16, g+24 of the group: code words and fp16x2 absmax; all 32 LUT
+                // loads are issued before the first store
+                const uint32_t rw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const uint32_t sc[4] = {dup_lo(am.x), dup_hi(am.x), dup_lo(am.y), dup_hi(am.y)};
+                uint32_t d[32];   // row h: d[8h .. 8h+7] = k 16t .. 16t+15, fp16x2 in k order
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    d[i] = lds32(lut_base + __byte_perm(rw[i >> 2], laneword, 0x5504u | (uint32_t(i & 3) << 4)));
+#pragma unroll
+                for (int i = 0; i < 32; ++i) d[i] = hmul2_u32(d[i], sc[i >> 3]);
+                // rows g, g+8 -> TMEM lanes 32r + {g, g+8}; rows g+16, g+24 -> lanes 32r + 16 + {g, g+8}
+                const uint32_t ta0 =
+                    tmem + (uint32_t(32 * r) << 16) + uint32_t(TC_A_COL0 + TC_A_COLS * (j % TC_AS) + 32 * q);
+                tmem_st_16x256b_x4(ta0, d[0], d[1], d[8], d[9], d[2], d[3], d[10], d[11], d[4], d[5], d[12], d[13],
+                                   d[6], d[7], d[14], d[15]);
+                tmem_st_16x256b_x4(ta0 + (16u << 16), d[16], d[17], d[24], d[25], d[18], d[19], d[26], d[27], d[20],
+                                   d[21], d[28], d[29], d[22], d[23], d[30], d[31]);
+                tmem_wait_st();
+            }
+            kg += TC_GROUPS;
+            while (kg >= NKG) {
+                kg -= NKG;
+                ++T;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty_w[j % WS]);
+                mbar_arrive(&full_a[j % TC_AS]);
+            }
+        }
+    } else if (warp == TC_MMA_WARP) {   // the whole warp waits, one lane issues (warp kept converged)
+        const uint32_t idesc = tc_idesc_f16(TC_ROWS, ta.n_mma);
+        const uint64_t bdesc0 = sw128_kmajor_desc(smem_u32(x_ring));   // start address field steps by 16-byte units
+        int seg = 0;
+        int kg = int(u0 % NKG);
+        for (int j = 0; j < n_items; ++j, kg = kg + 1 == NKG ? 0 : kg + 1) {
+            const int nk = min(TC_KG, KB - kg * TC_KG);
+            const bool seg_first = j == 0 || kg == 0;
+            const bool seg_last = j == n_items - 1 || kg == NKG - 1;
+            const int buf = seg & 1;
+            if (seg_first && seg >= 2 && !mbar_wait(&acc_empty[buf], uint32_t(((seg >> 1) + 1) & 1), ta.err, 24))
+                break;
+            if (!mbar_wait(&full_a[j % TC_AS], uint32_t((j / TC_AS) & 1), ta.err, 25)) break;
+            if (!mbar_wait(&full_x[j % TC_XS], uint32_t((j / TC_XS) & 1), ta.err, 26)) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a0 = tmem + uint32_t(TC_A_COL0 + TC_A_COLS * (j % TC_AS));
+                const uint32_t d0 = tmem + uint32_t(buf * TC_ACC_COLS);
+                const uint64_t b0 = bdesc0 + uint64_t(((j % TC_XS) * TC_KG * xs_bytes) >> 4);
+                for (int q = 0; q < nk; ++q)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        tc_mma_f16_ta(d0, a0 + 32 * q + 8 * k, b0 + uint64_t((q * xs_bytes + 32 * k) >> 4), idesc,
+                                      (seg_first && q == 0 && k == 0) ? 0u : 1u);
+                tc_commit(&empty_a[j % TC_AS]);   // frees the item's A stage and x stage
+                if (seg_last) tc_commit(&acc_full[buf]);
+            }
+            __syncwarp();
+            if (seg_last) ++seg;
+        }
+        if (lane == 0) tc_commit(&drain);   // every MMA of this CTA has completed before TMEM is freed
+        __syncwarp();
+        mbar_wait(&drain, 0u, ta.err, 27);
+    } else {   // epilogue warps
+        const int q = warp & 3;
+        const int rho = 32 * q + lane;
+        int seg = 0;
+        float v[TC_MAX_M];
+        for (int j = 0; j < n_items;) {
+            const int64_t u = u0 + j;
+            const int T = int(u / NKG), kg0 = int(u % NKG);
+            const int len = min(n_items - j, NKG - kg0);
+            const bool whole = kg0 == 0 && len == NKG;
+            const int buf = seg & 1;
+            if (!mbar_wait(&acc_full[buf], uint32_t((seg >> 1) & 1), ta.err, 28)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int c16 = 0; c16 < TC_MAX_M / 16; ++c16) {
+                if (16 * c16 < ta.n_mma) {
+                    uint32_t rr[16];
+                    tmem_ld16(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * TC_ACC_COLS + 16 * c16), rr);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[16 * c16 + i] = __uint_as_float(rr[i]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            const int n = T * TC_ROWS + rho;
+            bool run = true;
+            if (!whole) {   // split tile: partial to this CTA's slot; per lane quarter, the last
+                            // contributing warp adds the partials in CTA order
+                float4* slot = reinterpret_cast<float4*>(ta.part + (int64_t(c) * 2 + (T == first_tile ? 0 : 1)) *
+                                                                         TC_SLOT_FLOATS);   // [m / 4][row][4]
+#pragma unroll
+                for (int q4 = 0; q4 < TC_MAX_M / 4; ++q4)
+                    if (4 * q4 < p.M)
+                        __stcg(slot + q4 * TC_ROWS + rho, make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
+                __threadfence();
+                __syncwarp();
+                const int cf = owner_of(int64_t(T) * NKG, ta.W, ta.G);
+                const int cl = owner_of(int64_t(T) * NKG + NKG - 1, ta.W, ta.G);
+                unsigned last = 0;
+                if (lane == 0) last = atomicAdd(ta.tile_cnt + 4 * T + q, 1u) == unsigned(cl - cf);
+                run = __shfl_sync(0xffffffffu, last, 0) != 0;
+                if (run) {
+                    __threadfence();
+#pragma unroll
+                    for (int m = 0; m < TC_MAX_M; ++m) v[m] = 0.f;
+                    for (int cc = cf; cc <= cl; ++cc) {
+                        const int ft = int((ta.W * cc / ta.G) / NKG);
+                        const float4* src = reinterpret_cast<const float4*>(
+                            ta.part + (int64_t(cc) * 2 + (T == ft ? 0 : 1)) * TC_SLOT_FLOATS);
+                        float4 t4[TC_MAX_M / 4];
+#pragma unroll
+                        for (int q4 = 0; q4 < TC_MAX_M / 4; ++q4)
+                            t4[q4] = 4 * q4 < p.M ? __ldcg(src + q4 * TC_ROWS + rho) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int q4 = 0; q4 < TC_MAX_M / 4; ++q4) {
+                            v[4 * q4] += t4[q4].x;
+                            v[4 * q4 + 1] += t4[q4].y;
+                            v[4 * q4 + 2] += t4[q4].z;
+                            v[4 * q4 + 3] += t4[q4].w;
+                        }
+                    }
+                    if (lane == 0) ta.tile_cnt[4 * T + q] = 0u;   // re-armed for the next launch
+                }
+            }
+            if (run) tc_epilogue_row<EPI>(p, n, rho, v, lane);
+            ++seg;
+            j += len;
+        }
+        if (EPI == EPI_ARGMAX && p.token_out) {   // the last epilogue warp to finish runs the step finalize
+            __threadfence();
+            __syncwarp();
+            unsigned last = 0;
+            if (lane == 0) last = atomicAdd(p.done, 1u) == unsigned(4 * ta.G - 1);
+            if (__shfl_sync(0xffffffffu, last, 0)) {
+                __threadfence();
+                finalize_step(p, lane);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == TC_MMA_WARP) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TC_TMEM_COLS);
+    }
+}
+
 // ---------------------------------------------------------------- quantizer / packer
 
 __global__ void nf4_quantize_kernel(const __half* __restrict__ w, int64_t n_blocks, int kb, int N,
@@ -1692,7 +2073,12 @@ __global__ void nf4_dequant_kernel(const uint8_t* __restrict__ packed, const voi
 
 // One thread per (unit, lane): the lane's 2 x 16 code bytes and, for t == 0,
 // the four absmax values of its lane group.
-template <typename AbsT>
+// TC = true: the tcgen05 GEMM's variant of the unit layout -- lane (g, t) holds,
+// for each of its rows, the code bytes 2t + 8p and 2t + 8p + 1 (p = 0..3; the
+// k values 4t + 16p .. 4t + 16p + 3) instead of bytes 8t .. 8t + 7, so that the
+// decoded fp16x2 values of a lane are exactly its share of a 16x256b tensor-
+// memory store in natural k order.
+template <typename AbsT, bool TC>
 __global__ void nf4_pack_native_kernel(const uint8_t* __restrict__ packed, const void* absmax,
                                        uint8_t* __restrict__ out, int64_t n_units, int KB, int N) {
     pdl_trigger();
@@ -1708,7 +2094,14 @@ __global__ void nf4_pack_native_kernel(const uint8_t* __restrict__ packed, const
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int64_t row = rg * UNIT_ROWS + g + 8 * r;
-            const uint2 v = *reinterpret_cast<const uint2*>(packed + row * row_bytes + 32 * b + 8 * t);
+            uint2 v;
+            if (TC) {
+                const uint16_t* src = reinterpret_cast<const uint16_t*>(packed + row * row_bytes + 32 * b + 2 * t);
+                v.x = uint32_t(src[0]) | (uint32_t(src[4]) << 16);
+                v.y = uint32_t(src[8]) | (uint32_t(src[12]) << 16);
+            } else {
+                v = *reinterpret_cast<const uint2*>(packed + row * row_bytes + 32 * b + 8 * t);
+            }
             // rows g, g+8 -> first half, rows g+16, g+24 -> second half; 16 bytes per lane in each
             *reinterpret_cast<uint2*>(rec + (r >> 1) * 512 + 16 * lane + 8 * (r & 1)) = v;
             if (t == 0) {
@@ -1761,8 +2154,9 @@ extern "C" int nova_nf4_native_bytes(int64_t n, int64_t k, int64_t* bytes) {
     return NOVA_OK;
 }
 
-extern "C" int nova_nf4_pack_native(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n,
-                                    int64_t k, void* stream) {
+template <bool TC>
+static int pack_units(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n, int64_t k,
+                      void* stream) {
     if (n <= 0 || n % UNIT_ROWS || k <= 0 || k % 64)
         return fail(NOVA_ERR_INVALID, "native layout needs N %% 32 == 0 and K %% 64 == 0");
     if (!packed || !absmax || !out) return fail(NOVA_ERR_INVALID, "NULL pointer");
@@ -1771,12 +2165,22 @@ extern "C" int nova_nf4_pack_native(const void* packed, const void* absmax, int 
     const int64_t n_units = (n / UNIT_ROWS) * (k / 64);
     const unsigned grid = unsigned(std::min<int64_t>((n_units * 32 + 255) / 256, 65535 * 8));
     if (absmax_fp32)
-        nf4_pack_native_kernel<float><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        nf4_pack_native_kernel<float, TC><<<grid, 256, 0, (cudaStream_t)stream>>>(
             (const uint8_t*)packed, absmax, (uint8_t*)out, n_units, int(k / 64), int(n));
     else
-        nf4_pack_native_kernel<__half><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        nf4_pack_native_kernel<__half, TC><<<grid, 256, 0, (cudaStream_t)stream>>>(
             (const uint8_t*)packed, absmax, (uint8_t*)out, n_units, int(k / 64), int(n));
-    return check_launch("nova_nf4_pack_native");
+    return check_launch(TC ? "nova_nf4_pack_tc" : "nova_nf4_pack_native");
+}
+
+extern "C" int nova_nf4_pack_native(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n,
+                                    int64_t k, void* stream) {
+    return pack_units<false>(packed, absmax, absmax_fp32, out, n, k, stream);
+}
+
+extern "C" int nova_nf4_pack_tc(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n,
+                                int64_t k, void* stream) {
+    return pack_units<true>(packed, absmax, absmax_fp32, out, n, k, stream);
 }
 
 template <typename Kern>
@@ -2186,6 +2590,21 @@ constexpr int64_t GM_COUNTER_BYTES = 4096;
 
 // Split count: no more CTAs than SMs (one wave), and about sqrt(3 * k-blocks): each split adds
 // ~KB/S k-block steps of work per CTA but one more 128 KB partial for the last CTA to add.
+static int64_t tc_grid(int64_t items) {
+    return std::max<int64_t>(1, std::min<int64_t>(sm_count(), (items + TC_MIN_ITEMS - 1) / TC_MIN_ITEMS));
+}
+
+// tcgen05 GEMM workspace: [0] finalize arrivals, [4] error word, [256..) per
+// tile and lane quarter split arrivals, then 2 partial slots per CTA.
+static int64_t tc_workspace_layout(int64_t n, int64_t k, int64_t* part_off) {
+    const int64_t tiles = (n + TC_ROWS - 1) / TC_ROWS;
+    const int64_t w = tiles * ((k / 64 + TC_KG - 1) / TC_KG);
+    const int64_t g = tc_grid(w);
+    const int64_t off = (256 + tiles * 16 + 1023) / 1024 * 1024;
+    if (part_off) *part_off = off;
+    return off + g * 2 * int64_t(TC_SLOT_FLOATS) * 4;
+}
+
 static void gemm_shape(int64_t n, int64_t k, int64_t* tiles, int64_t* splits) {
     const int64_t n_rg = n / UNIT_ROWS;
     const int64_t t = (n_rg + GM_WARPS - 1) / GM_WARPS;
@@ -2203,14 +2622,78 @@ extern "C" int nova_nf4_gemm_workspace_bytes(int64_t n, int64_t k, int64_t* byte
     int64_t t = 0, s = 0;
     gemm_shape(n, k, &t, &s);
     const int64_t slots = s > 1 ? t * s * int64_t(GM_SLOT_FLOATS) * 4 : 0;
-    *bytes = GM_COUNTER_BYTES + slots;   // counters first (fixed place for every shape), then the split slots
+    const int64_t legacy = GM_COUNTER_BYTES + slots;   // counters first, then the split slots
+    *bytes = std::max(legacy, tc_workspace_layout(n, k, nullptr));
+    return NOVA_OK;
+}
+
+// tcgen05 path of nova_nf4_gemm (arguments already validated).
+static int nf4_gemm_tc(const nova_nf4_args* a, int epi, cudaStream_t stream) {
+    const int64_t m = a->m, n = a->n, k = a->k;
+    Params p{};
+    p.x = (const __half*)a->x;
+    p.x_stride = a->x_stride;
+    p.packed = (const uint8_t*)a->packed;
+    p.lut = (const uint32_t*)a->lut;
+    p.residual = (const __half*)a->residual;
+    p.res_stride = a->res_stride;
+    p.out = (__half*)a->out;
+    p.out_stride = a->out_stride;
+    p.argmax = (unsigned long long*)a->argmax;
+    p.token_out = a->token_out;
+    p.pos = a->pos;
+    p.embed = (const __half*)a->embed;
+    p.embed_out = (__half*)a->embed_out;
+    p.embed_out_stride = a->embed_out_stride;
+    p.embed_dim = int(a->embed_dim);
+    p.M = int(m);
+    p.N = int(n);
+    p.K = int(k);
+    p.KB = int(k / 64);
+    const int64_t tiles = (n + TC_ROWS - 1) / TC_ROWS;
+    int64_t part_off = 0;
+    tc_workspace_layout(n, k, &part_off);
+    uint8_t* ws = (uint8_t*)a->workspace;
+    TcArgs ta;
+    ta.n_mma = int((m + 15) / 16 * 16);
+    ta.W = tiles * ((p.KB + TC_KG - 1) / TC_KG);
+    ta.G = int(tc_grid(ta.W));
+    ta.part = (float*)(ws + part_off);
+    ta.tile_cnt = (unsigned*)(ws + 256);
+    ta.err = (int*)(ws + 4);
+    p.done = (unsigned*)ws;
+    CUtensorMap xmap;
+    if (int rc = make_tmap_f16_rows64(&xmap, a->x, uint64_t(m), uint64_t(k), uint64_t(a->x_stride), uint32_t(ta.n_mma)))
+        return rc;
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "device queries failed");
+    }
+    const int64_t fixed = 1024 + int64_t(TC_XS) * TC_KG * ta.n_mma * 128 + LUT_BYTES;
+    ta.ws = int(std::min<int64_t>(TC_WS_MAX, (optin - 1024 - fixed) / TC_W_BYTES));   // 1 KB for static smem
+    if (ta.ws < 2) return fail(NOVA_ERR_UNSUPPORTED, "shared memory");
+    const int64_t nsmem = fixed + int64_t(ta.ws) * TC_W_BYTES;
+    using TKern = void (*)(Params, CUtensorMap, TcArgs);
+    static const TKern kernels[5] = {nf4_gemm_tc_kernel<0>, nf4_gemm_tc_kernel<1>, nf4_gemm_tc_kernel<2>,
+                                     nf4_gemm_tc_kernel<3>, nf4_gemm_tc_kernel<4>};
+    static int64_t smem_set[5] = {};
+    if (int rc = prepare_smem(kernels[epi], nsmem, &smem_set[epi])) return rc;
+    const cudaError_t err = launch(kernels[epi], dim3(unsigned(ta.G)), dim3(TC_THREADS), size_t(nsmem), stream, p,
+                                   xmap, ta);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_nf4_gemm: launch failed: %s", cudaGetErrorString(err));
+    }
     return NOVA_OK;
 }
 
 extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
     if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
     const int64_t m = a->m, n = a->n, k = a->k;
-    if (a->layout != 1) return fail(NOVA_ERR_UNSUPPORTED, "native-layout weights only");
+    if (a->layout != 1 && a->layout != 2)
+        return fail(NOVA_ERR_UNSUPPORTED, "native (1) or tcgen05 (2) unit layout only");
     if (m < 1 || m > GM_MAX_M) return fail(NOVA_ERR_UNSUPPORTED, "M must be in [1, 64], got %lld", (long long)m);
     if (n <= 0 || n % UNIT_ROWS || n > (1 << 30) || k <= 0 || k % 64 || k > (1 << 20))
         return fail(NOVA_ERR_INVALID, "N multiple of 32, K multiple of 64");
@@ -2231,6 +2714,7 @@ extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
     nova_nf4_gemm_workspace_bytes(n, k, &need);
     if (a->workspace_bytes < need) return fail(NOVA_ERR_INVALID, "workspace too small: %lld < %lld",
                                                (long long)a->workspace_bytes, (long long)need);
+    if (a->layout == 2) return nf4_gemm_tc(a, epi, (cudaStream_t)stream);
     int64_t tiles = 0, splits = 0;
     gemm_shape(n, k, &tiles, &splits);
     Params p;

@@ -46,7 +46,8 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .kernels import build_nf4_lut, fused_rms_norm, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native
+from .kernels import (build_nf4_lut, fused_rms_norm, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native,
+                      pack_tc)
 from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk
 from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
@@ -107,10 +108,16 @@ class NF4Weight:
     packed: torch.Tensor               # uint8 [N, K/2] (reference layout; prefill, tests)
     absmax: torch.Tensor               # fp16 [K/64, N]
     units: torch.Tensor | None = None  # B200-native unit stream (decode GEMVs)
+    tc: torch.Tensor | None = None     # unit stream of the tcgen05 GEMM (batched decode), made on demand
 
     def __post_init__(self) -> None:
         if self.units is None:
             self.units = pack_native(self.packed, self.absmax)
+
+    def tc_units(self) -> torch.Tensor:
+        if self.tc is None:
+            self.tc = pack_tc(self.packed, self.absmax)
+        return self.tc
 
     @property
     def n(self) -> int:
@@ -263,6 +270,8 @@ class NovaDecoder:
                       (2 * self.inter, cfg.hidden_size), (cfg.hidden_size, self.inter),
                       (cfg.vocab_size, cfg.hidden_size)]
             self.gemm_ws = max((gemm_workspace(dev, n, k) for n, k in shapes), key=lambda t: t.numel()).clone()
+            for w in [self.w.lm_head] + [x for lw in self.w.layers for x in (lw.qkv, lw.o, lw.gate_up, lw.down)]:
+                w.tc_units()   # packed before any graph capture
             self.xn = torch.zeros(B, cfg.hidden_size, dtype=f16, device=dev)
         else:
             self.gemm_ws = self.xn = None
@@ -382,7 +391,7 @@ class NovaDecoder:
                 _lib.call("nova_rmsnorm", x.data_ptr(), x.stride(0), None, 0, None, 0, norm_weight.data_ptr(),
                           self.xn.data_ptr(), self.xn.stride(0), B, n_in, float(eps), _lib.stream_of(self.device))
                 x = self.xn[:, :n_in]
-            nf4_gemm(x, w.units, self.lut, out, n=w.n, epilogue=epilogue, residual=residual, argmax=argmax,
+            nf4_gemm(x, w.tc_units(), self.lut, out, n=w.n, epilogue=epilogue, residual=residual, argmax=argmax,
                      token_out=token_out, pos=pos, embed=embed, embed_out=embed_out, workspace=self.gemm_ws)
             return
         for r in range(0, B, GEMV_ROWS):

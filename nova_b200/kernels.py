@@ -100,17 +100,27 @@ def gemv_workspace(device: torch.device, n: int) -> torch.Tensor:
     return ws
 
 
-def pack_native(packed: torch.Tensor, absmax: torch.Tensor) -> torch.Tensor:
-    """Reference NF4 layout (packed ``[N, K/2]``, absmax ``[K/64, N]``) -> the
-    B200-native unit stream (uint8, 1088 bytes per 32-row x 64-k unit)."""
+def _pack(entry: str, packed: torch.Tensor, absmax: torch.Tensor) -> torch.Tensor:
     _lib.require_cuda(packed, absmax, names=("packed", "absmax"))
     n, k2 = packed.shape
     nbytes = _lib.ctypes.c_int64(0)
     _lib.call("nova_nf4_native_bytes", n, 2 * k2, _lib.ctypes.byref(nbytes))
     out = torch.empty(int(nbytes.value), dtype=torch.uint8, device=packed.device)
-    _lib.call("nova_nf4_pack_native", packed.contiguous().data_ptr(), absmax.contiguous().data_ptr(),
+    _lib.call(entry, packed.contiguous().data_ptr(), absmax.contiguous().data_ptr(),
               int(absmax.dtype == torch.float32), out.data_ptr(), n, 2 * k2, _lib.stream_of(packed.device))
     return out
+
+
+def pack_native(packed: torch.Tensor, absmax: torch.Tensor) -> torch.Tensor:
+    """Reference NF4 layout (packed ``[N, K/2]``, absmax ``[K/64, N]``) -> the
+    B200-native unit stream (uint8, 1088 bytes per 32-row x 64-k unit)."""
+    return _pack("nova_nf4_pack_native", packed, absmax)
+
+
+def pack_tc(packed: torch.Tensor, absmax: torch.Tensor) -> torch.Tensor:
+    """Reference NF4 layout -> the unit stream of the tcgen05 GEMM
+    (``nova_nf4_gemm`` with layout 2)."""
+    return _pack("nova_nf4_pack_tc", packed, absmax)
 
 
 def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None, lut: torch.Tensor,
@@ -179,9 +189,12 @@ def nf4_gemm(x: torch.Tensor, units: torch.Tensor, lut: torch.Tensor, out: torch
              epilogue: int = _lib.NF4_PLAIN, residual: torch.Tensor | None = None,
              argmax: torch.Tensor | None = None, token_out: torch.Tensor | None = None,
              pos: torch.Tensor | None = None, embed: torch.Tensor | None = None,
-             embed_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """``nova_nf4_gemm``: x ``[M <= 64, K]`` against the native unit stream of an
-    ``[n, K]`` NF4 weight; out ``[M, n]`` (``[M, n/2]`` for SiLU*up)."""
+             embed_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+             layout: int = 2) -> torch.Tensor:
+    """``nova_nf4_gemm``: x ``[M <= 64, K]`` against the unit stream of an
+    ``[n, K]`` NF4 weight (layout 2: :func:`pack_tc`, tcgen05 tensor cores;
+    layout 1: :func:`pack_native`, mma.sync); out ``[M, n]`` (``[M, n/2]`` for
+    SiLU*up)."""
     m, k = x.shape
     if x.stride(1) != 1 or out.stride(1) != 1:
         raise ValueError("x/out must have a contiguous last dimension")
@@ -189,7 +202,7 @@ def nf4_gemm(x: torch.Tensor, units: torch.Tensor, lut: torch.Tensor, out: torch
     a = _lib.NF4Args()
     a.x, a.x_stride = x.data_ptr(), x.stride(0)
     a.norm_weight, a.eps = None, 0.0
-    a.packed, a.absmax, a.absmax_fp32, a.layout = units.data_ptr(), None, 0, 1
+    a.packed, a.absmax, a.absmax_fp32, a.layout = units.data_ptr(), None, 0, int(layout)
     a.lut, a.bias = lut.data_ptr(), None
     a.residual, a.res_stride = (_lib.ptr(residual), residual.stride(0) if residual is not None else 0)
     a.out, a.out_stride = out.data_ptr(), out.stride(0)

@@ -1,4 +1,5 @@
-"""GPU: batched NF4 GEMM (nova_nf4_gemm, M up to 64) against the CPU oracle.
+"""GPU: batched NF4 GEMM (nova_nf4_gemm, M up to 64; tcgen05 units from
+pack_tc and the mma.sync kernel on pack_native units) against the CPU oracle.
 
 The GEMM computes x @ dequant(W)^T with the reference's dequantized weight
 fp16(code * absmax) and fp32 accumulation, so each fp16 output must be within
@@ -39,15 +40,17 @@ def _oracle(x, packed, absmax):
     return x.float().cpu().numpy() @ w.astype(np.float32).T
 
 
+@pytest.mark.parametrize("layout", [2, 1])
 @pytest.mark.parametrize("m", [9, 16, 37, 64])
 @pytest.mark.parametrize("n,k", [(1024, 2560), (2560, 9728), (6144, 2560), (96, 192)])
-def test_gemm_plain_matches_dequant_matmul(cuda_lib, m, n, k):
-    from nova_b200.kernels import nf4_gemm, pack_native
+def test_gemm_plain_matches_dequant_matmul(cuda_lib, m, n, k, layout):
+    from nova_b200.kernels import nf4_gemm, pack_native, pack_tc
 
     packed, absmax = _weights(n, k, n + k + m)
     x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).half()
     out = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
-    nf4_gemm(x.cuda(), pack_native(packed, absmax), _lut(), out, n=n)
+    units = pack_tc(packed, absmax) if layout == 2 else pack_native(packed, absmax)
+    nf4_gemm(x.cuda(), units, _lut(), out, n=n, layout=layout)
     want = _oracle(x, packed, absmax)
     got = out.float().cpu().numpy()
     scale = float(np.abs(want).max())
@@ -61,7 +64,7 @@ def test_gemm_epilogues_and_repeat(cuda_lib):
     re-arm."""
     from nova_b200 import _lib
     from nova_b200.decoder import interleave_gate_up
-    from nova_b200.kernels import nf4_gemm, pack_native
+    from nova_b200.kernels import nf4_gemm, pack_tc
 
     m, k = 64, 2560
     lut = _lut()
@@ -69,7 +72,7 @@ def test_gemm_epilogues_and_repeat(cuda_lib):
     xc = x.cuda()
     # residual
     packed, absmax = _weights(2560, k, 2)
-    units = pack_native(packed, absmax)
+    units = pack_tc(packed, absmax)
     y = _oracle(x, packed, absmax)
     res = (torch.randn(m, 2560, generator=torch.Generator().manual_seed(3)) * 0.5).half()
     for _ in range(2):
@@ -87,7 +90,7 @@ def test_gemm_epilogues_and_repeat(cuda_lib):
     up, ua = _weights(1024, k, 5)
     ip, ia = interleave_gate_up(gp, ga, up, ua)
     act = torch.empty(m, 1024, dtype=torch.float16, device="cuda")
-    nf4_gemm(xc, pack_native(ip, ia), lut, act, n=2048, epilogue=_lib.NF4_SILU_MUL)
+    nf4_gemm(xc, pack_tc(ip, ia), lut, act, n=2048, epilogue=_lib.NF4_SILU_MUL)
     g32, u32 = _oracle(x, gp, ga), _oracle(x, up, ua)
     g16, u16 = g32.astype(np.float16), u32.astype(np.float16)
     want = onorm.silu_mul(g16, u16).astype(np.float32)
@@ -108,7 +111,7 @@ def test_gemm_epilogues_and_repeat(cuda_lib):
     tok = torch.zeros(m, dtype=torch.int64, device="cuda")
     pos = torch.tensor([10], dtype=torch.int64, device="cuda")
     nxt = torch.empty(m, k, dtype=torch.float16, device="cuda")
-    lu = pack_native(lp, la)
+    lu = pack_tc(lp, la)
     for step in range(2):
         nf4_gemm(xc, lu, lut, logits, n=vocab, epilogue=_lib.NF4_ARGMAX, argmax=slot, token_out=tok, pos=pos,
                  embed=embed, embed_out=nxt)
@@ -120,10 +123,10 @@ def test_gemm_epilogues_and_repeat(cuda_lib):
 
 
 def test_gemm_rejects(cuda_lib):
-    from nova_b200.kernels import nf4_gemm, pack_native
+    from nova_b200.kernels import nf4_gemm, pack_tc
 
     packed, absmax = _weights(64, 128, 9)
-    units = pack_native(packed, absmax)
+    units = pack_tc(packed, absmax)
     out = torch.empty(65, 64, dtype=torch.float16, device="cuda")
     with pytest.raises(ValueError):
         nf4_gemm(torch.zeros(65, 128, dtype=torch.float16, device="cuda"), units, _lut(), out, n=64)
