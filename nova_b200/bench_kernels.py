@@ -4,6 +4,7 @@ weight / KV set so that the working set exceeds the 126 MB L2).
 
     python -m nova_b200.bench_kernels gemv --n 19456 --k 2560 --epilogue silu --norm
     python -m nova_b200.bench_kernels attn --ctx 32768 --batch 1
+    python -m nova_b200.bench_kernels gemm --n 151936 --k 2560 --m 64   # batched tcgen05 GEMM
     python -m nova_b200.bench_kernels all          # the config-2 shapes + config-3 sweep
 
 Prints one JSON line per case with the launch time and achieved GB/s
@@ -20,7 +21,7 @@ import torch
 
 from . import _lib
 from .decoder import interleave_gate_up
-from .kernels import build_nf4_lut, gemv_workspace, nf4_gemv, pack_native
+from .kernels import build_nf4_lut, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native, pack_tc
 from .kvattn import GROUP_T, launch_attention, new_workspace, pick_chunk
 from .quant import nf4_codebook, quantize_nf4
 
@@ -90,6 +91,45 @@ def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool =
             "sets": sets, "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
 
 
+def bench_gemm(n: int, k: int, m: int = 64, epilogue: str = "plain", sets: int = 0, iters: int = 20,
+               seed: int = 0) -> dict:
+    """nova_nf4_gemm (tcgen05, layout 2) on M batch rows; algorithmic bytes =
+    the NF4 weight stream (x and the output are L2-resident)."""
+    dev = torch.device("cuda")
+    code = nf4_codebook()
+    lut = build_nf4_lut(code).to(dev)
+    nbytes = n * k // 2 + (k // 64) * n * 2
+    sets = sets or max(2, min(64, (512 << 20) // nbytes + 1))
+    g = torch.Generator(device=dev).manual_seed(seed)
+    weights = []
+    for _ in range(sets):
+        w = (torch.randn(n, k, generator=g, device=dev) * 0.02).half()
+        if epilogue == "silu":
+            gp, ga = quantize_nf4(w[: n // 2].contiguous(), code)
+            up, ua = quantize_nf4(w[n // 2:].contiguous(), code)
+            weights.append(pack_tc(*interleave_gate_up(gp, ga, up, ua)))
+        else:
+            weights.append(pack_tc(*quantize_nf4(w, code)))
+        del w
+    x = torch.randn(m, k, generator=g, device=dev).half()
+    nout = n // 2 if epilogue == "silu" else n
+    out = torch.zeros(m, nout, dtype=torch.float16, device=dev)
+    ws = gemm_workspace(dev, n, k)
+    kw = {}
+    if epilogue == "residual":
+        kw["residual"] = out
+    if epilogue == "argmax":
+        kw["argmax"] = torch.zeros(m, dtype=torch.int64, device=dev)
+
+    def fn(i):
+        nf4_gemm(x, weights[i], lut, out, n=n, epilogue=EPI[epilogue], workspace=ws, **kw)
+
+    us = _graph_time(fn, sets, iters)
+    flops = 2.0 * m * n * k
+    return {"kernel": "nf4_gemm_tc", "n": n, "k": k, "m": m, "epilogue": epilogue, "sets": sets, "us": round(us, 3),
+            "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "tflops": round(flops / (us * 1e-6) / 1e12, 1)}
+
+
 def bench_attn(ctx: int, batch: int = 1, q_heads: int = 32, kv_heads: int = 8, window: int = 0, chunk: int = 0,
                sets: int = 0, iters: int = 20, seed: int = 0) -> dict:
     dev = torch.device("cuda")
@@ -152,6 +192,13 @@ def main() -> None:
     a.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
     a.add_argument("--variant", choices=["cta", "warp"], default="cta",
                    help="native GEMV split-K at CTA level (default) or warp level")
+    c = sub.add_parser("gemm")
+    c.add_argument("--n", type=int, required=True)
+    c.add_argument("--k", type=int, required=True)
+    c.add_argument("--m", type=int, default=64)
+    c.add_argument("--epilogue", choices=list(EPI), default="plain")
+    c.add_argument("--sets", type=int, default=0)
+    c.add_argument("--iters", type=int, default=20)
     b = sub.add_parser("attn")
     b.add_argument("--ctx", type=int, required=True)
     b.add_argument("--batch", type=int, default=1)
@@ -167,6 +214,9 @@ def main() -> None:
                               (_lib.LAUNCH_WARP_SPLITK if args.variant == "warp" else 0))
         print(json.dumps(bench_gemv(args.n, args.k, args.m, args.epilogue, args.norm, args.sets, args.iters,
                                     layout=args.layout)))
+    elif args.cmd == "gemm":
+        _lib.set_launch_flags(_lib.LAUNCH_PDL)
+        print(json.dumps(bench_gemm(args.n, args.k, args.m, args.epilogue, args.sets, args.iters)))
     elif args.cmd == "attn":
         print(json.dumps(bench_attn(args.ctx, args.batch, window=args.window, chunk=args.chunk, sets=args.sets,
                                     iters=args.iters)))

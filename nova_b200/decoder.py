@@ -377,6 +377,21 @@ class NovaDecoder:
         self.argmax_slot.zero_()
         return first
 
+    def grow(self, new_max_len: int) -> None:
+        """Move the int8 KV cache into a larger capacity bucket without a
+        rebuild (src/nova/decode.py:444-500; the reference raises
+        NotImplementedError for its int8 cache): the written groups, scales,
+        ring and scalars are copied, the RoPE tables extended, and the decode
+        graph dropped -- call ``capture()`` again.  Decoding continues
+        bit-identically (the attention keeps its split size)."""
+        new_max_len = int(new_max_len)
+        if new_max_len <= self.max_len:
+            return
+        self.cache = self.cache.grow(new_max_len)
+        self.max_len = new_max_len
+        self.cos, self.sin = rope_tables(self.max_len + 1, self.cfg.head_dim, self.cfg.rope_theta, self.device)
+        self.graph = None
+
     # ---------------------------------------------------------------- decode
 
     def _gemv(self, x, w: NF4Weight, out, *, epilogue: int = _lib.NF4_PLAIN, norm_weight=None, residual=None,

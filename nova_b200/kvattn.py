@@ -543,6 +543,36 @@ class KVInt8Cache:
                          max_len=self.max_len, n_splits=self.n_splits, chunk=self.chunk, window=self.window)
         return self.out
 
+    # ---- capacity-bucket migration ----
+
+    def grow(self, new_max_len: int) -> "KVInt8Cache":
+        """A cache of capacity ``new_max_len`` holding this cache's contents:
+        the int8 codes and min/step scales of every written group, the fp16
+        ring and the device scalars, copied on the device (the reference moves
+        fp16 caches across buckets in ``GraphDecoder.grow``,
+        src/nova/decode.py:444-500, and raises NotImplementedError for the int8
+        cache).  The split size is kept, so the added splits are empty and
+        decoding continues bit-identically; a captured decode graph must be
+        captured again.  The staging area is not carried over."""
+        new_max_len = int(new_max_len)
+        if new_max_len < self.max_len:
+            raise ValueError(f"new capacity {new_max_len} is below the current {self.max_len}")
+        new = KVInt8Cache(self.num_slots, self.num_kv_heads, self.head_dim, new_max_len, self.num_q_heads,
+                          batch=self.batch, dtype=self.dtype, device=self.device, group=self.group, chunk=self.chunk,
+                          num_warps=self.num_warps, num_stages=self.num_stages, window=self.window)
+        g_old = self.kmn[0].shape[2]
+        for i in range(self.num_slots):
+            for src, dst in ((self.kq[i], new.kq[i]), (self.vq[i], new.vq[i])):
+                dst[:, :, :self.max_len].copy_(src)
+            for src, dst in ((self.kmn[i], new.kmn[i]), (self.kst[i], new.kst[i]), (self.vmn[i], new.vmn[i]),
+                             (self.vst[i], new.vst[i])):
+                dst[:, :, :g_old].copy_(src)
+            new.tail_k[i].copy_(self.tail_k[i])
+            new.tail_v[i].copy_(self.tail_v[i])
+        for name in ("pos", "first", "_written", "_qlen", "_pg"):
+            getattr(new, name).copy_(getattr(self, name))
+        return new
+
     # ---- memory ----
 
     def nbytes(self) -> int:

@@ -206,3 +206,59 @@ def test_qkv_norm_rope_append_equals_gemv_then_qk(cuda_lib, prompt_len):
     for i, (a, b) in enumerate(zip(fused, ref)):
         assert torch.equal(a, b), f"tensor {i} differs"
     assert int(c._written.item()) == prompt_len + 1
+
+
+def test_grow_copies_kv_prefix(cuda_lib):
+    """grow() keeps every written int8 group, its scales, the fp16 ring and the
+    device scalars, leaves the new capacity zero and drops the captured graph
+    (the reference's test_decode_mask_bucket.py::test_grow_copies_kv_prefix,
+    for the int8 cache its grow() does not support)."""
+    cfg, W, dec, _, prompt = _setup("small", 2, prompt_len=150, max_len=256)
+    dec.capture()
+    for _ in range(5):
+        dec.step()
+    c0 = dec.cache
+    before = {n: [t.clone() for t in getattr(c0, n)] for n in ("kq", "vq", "kmn", "kst", "vmn", "vst", "tail_k", "tail_v")}
+    scalars = [int(getattr(c0, n).item()) for n in ("pos", "first", "_written", "_qlen", "_pg")]
+    dec.grow(512)
+    c1 = dec.cache
+    assert dec.max_len == 512 and c1.max_len == 512 and dec.graph is None
+    assert [int(getattr(c1, n).item()) for n in ("pos", "first", "_written", "_qlen", "_pg")] == scalars
+    for li in range(cfg.num_hidden_layers):
+        for n in ("kq", "vq"):
+            assert torch.equal(getattr(c1, n)[li][:, :, :256], before[n][li])
+            assert getattr(c1, n)[li][:, :, 256:].abs().sum().item() == 0
+        for n in ("kmn", "kst", "vmn", "vst"):
+            assert torch.equal(getattr(c1, n)[li][:, :, :4], before[n][li])
+            assert getattr(c1, n)[li][:, :, 4:].abs().sum().item() == 0
+        for n in ("tail_k", "tail_v"):
+            assert torch.equal(getattr(c1, n)[li], before[n][li])
+    with pytest.raises(RuntimeError):
+        dec.step()
+    dec.grow(300)   # not larger: no change
+    assert dec.cache is c1
+
+
+def test_grow_preserves_decode(cuda_lib):
+    """Moving to a larger bucket mid-decode gives the same greedy tokens, bit
+    for bit, as never moving (the reference's test_grow_preserves_decode); the
+    moved decoder then runs past the old capacity."""
+    from nova_b200.decoder import NovaDecoder
+
+    cfg, W, dec, _, prompt = _setup("small", 1, prompt_len=120, max_len=192)
+    ref = NovaDecoder(W, max_len=192, batch=1)
+    ref.prefill(prompt)
+    ref.capture()
+    dec.capture()
+    for i in range(60):
+        if i == 5:
+            dec.grow(448)
+            dec.capture()
+        a = dec.step().clone()
+        b = ref.step().clone()
+        assert torch.equal(a, b), f"step {i}"
+        assert torch.equal(dec.logits, ref.logits), f"step {i}"
+    for _ in range(120):   # beyond the old capacity (192): 120 + 60 + 120 = 300 positions
+        dec.step()
+    assert int(dec.pos.item()) == 300
+    assert dec.input_ids.min().item() >= 0 and dec.input_ids.max().item() < cfg.vocab_size
