@@ -346,8 +346,9 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                    "kv_fill": "random int8 codes" if fill == "random" else "prefill of uniform random tokens",
                    "model": "Qwen3-VL-4B text (random init N(0,0.02))",
                    "global_batch": args.batch * copies, "ctx": args.ctx, "layers": cfg.num_hidden_layers,
-                   "parallelism": f"tp{world} (KV-head / column-row split, NCCL all-reduce after o_proj and "
-                                  f"down_proj)" if use_tp else ("replicas" if world > 1 else "single GPU"),
+                   "parallelism": f"tp{world} (KV-head / column-row split; all-reduce after o_proj and down_proj "
+                                  f"as one NVLink peer-memory kernel with the residual add)" if use_tp
+                                  else ("replicas" if world > 1 else "single GPU"),
                    "l2": "inputs larger than L2 (>= 2.8 GB streamed per step)", "graph": "one CUDA graph per step"},
         "roofline": roofline,
         "attn_roofline": attn_roof,

@@ -374,6 +374,41 @@ NOVA_API int nova_qkv_norm_rope_append(const nova_nf4_args* gemv, const nova_qk_
 NOVA_API int nova_nf4_gemm_workspace_bytes(int64_t n, int64_t k, int64_t* bytes);
 NOVA_API int nova_nf4_gemm(const nova_nf4_args* args, void* stream);
 
+/*
+ * Next-token sampling from the logits buffer, outside the decode graph
+ * (sample_next, src/chat.py:46-75): temperature <= 0 -> the first index of the
+ * largest logit; otherwise fp32 logits with the repetition penalty on seen
+ * tokens (l < 0 ? l * rp : l / rp), the top_k largest (ties at the boundary by
+ * lowest index), softmax(vals / temperature), tokens whose exclusive cumulative
+ * probability exceeds top_p dropped, renormalized, and the token picked by
+ * inverse CDF with uniform[row] in [0, 1) (the reference draws with
+ * torch.multinomial from the same probabilities).  Optional: the final
+ * probabilities and token ids in descending order (probs_out / idx_out,
+ * [rows, top_k]), the chosen token's embedding row gathered into embed_out
+ * (the next graph step's input), and seen_mark[row, token] = 1.
+ * top_k in [1, 256].  One CTA per row; no allocation.
+ */
+typedef struct nova_sample_args {
+    const void* logits;        /* fp16 [rows, vocab]                              */
+    int64_t logits_stride;
+    const void* seen;          /* uint8 [rows, vocab] or NULL                     */
+    int64_t seen_stride;
+    const void* uniform;       /* fp32 [rows] (unused when temperature <= 0)      */
+    int64_t* token_out;        /* int64 [rows]                                    */
+    const void* embed;         /* fp16 [vocab, embed_dim] or NULL                 */
+    void* embed_out;           /* fp16 [rows, embed_dim]                          */
+    int64_t embed_out_stride;
+    int64_t embed_dim;
+    void* probs_out;           /* fp32 [rows, top_k] or NULL                      */
+    int64_t* idx_out;          /* int64 [rows, top_k] or NULL                     */
+    void* seen_mark;           /* uint8 [rows, vocab] or NULL                     */
+    int64_t seen_mark_stride;
+    int64_t rows, vocab, top_k;
+    double temperature, top_p, repetition_penalty;
+} nova_sample_args;
+
+NOVA_API int nova_sample_topk(const nova_sample_args* args, void* stream);
+
 /* ------------------------------------------------------- fused phases */
 
 /*

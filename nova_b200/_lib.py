@@ -85,6 +85,18 @@ class FusedArgs(ctypes.Structure):
 PHASE_GEMV, PHASE_QK = 0, 1
 
 
+class SampleArgs(ctypes.Structure):
+    """Mirror of ``nova_sample_args``."""
+
+    _fields_ = [
+        ("logits", _P), ("logits_stride", _I), ("seen", _P), ("seen_stride", _I), ("uniform", _P),
+        ("token_out", _P), ("embed", _P), ("embed_out", _P), ("embed_out_stride", _I), ("embed_dim", _I),
+        ("probs_out", _P), ("idx_out", _P), ("seen_mark", _P), ("seen_mark_stride", _I),
+        ("rows", _I), ("vocab", _I), ("top_k", _I),
+        ("temperature", ctypes.c_double), ("top_p", ctypes.c_double), ("repetition_penalty", ctypes.c_double),
+    ]
+
+
 class TPAllReduceArgs(ctypes.Structure):
     """Mirror of ``nova_tp_allreduce_args``."""
 
@@ -125,6 +137,7 @@ _SIGNATURES: dict[str, list] = {
     "nova_qkv_norm_rope_append": [ctypes.POINTER(NF4Args), ctypes.POINTER(QKArgs), _P],
     "nova_fused_phases": [ctypes.POINTER(FusedArgs), _P],
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
+    "nova_sample_topk": [ctypes.POINTER(SampleArgs), _P],
 }
 _STRING_FNS = ("nova_version", "nova_last_error")
 _INT_FNS = ("nova_get_launch_flags",)

@@ -288,6 +288,7 @@ class NovaDecoder:
         # (batch <= 8).  Off by default: with 48 head-owning CTAs most SMs idle, and measured in the decode
         # step the two launches (q|k|v GEMV on every SM, then the q/k kernel) are faster.
         self.qkv_fused = bool(qkv_fused) and self.batch <= GEMV_ROWS
+        self._staged = None   # fp16 K/V per layer of the positions prefilled / injected since the last reset
 
     def _pick_chunk(self) -> int:
         """Split size for the attention (``kvattn.pick_chunk``)."""
@@ -314,68 +315,189 @@ class NovaDecoder:
         all_reduce_sum(part, self.tp)
         return part.to(torch.float16)
 
+    def _layer_qkv(self, li: int, lw, h: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+        """Prefill projections of layer li for hidden states h ``[B, T, H]``:
+        q (RoPE applied, ``[B, Hq, T, D]``), k before RoPE (after k_norm) and
+        after RoPE, v (``[B, Hkv, T, D]``)."""
+        cfg = self.cfg
+        B, T = h.shape[:2]
+        d, qd, kvd = cfg.head_dim, self.q_dim, self.kv_dim
+        x = fused_rms_norm(h, lw.input_ln, cfg.rms_norm_eps)
+        qkv = self._linear16(x, lw.qkv)
+        q = qkv[..., :qd].reshape(B, T, self.hq, d)
+        k = qkv[..., qd:qd + kvd].reshape(B, T, self.hkv, d)
+        v = qkv[..., qd + kvd:].reshape(B, T, self.hkv, d).transpose(1, 2).contiguous()
+        q = fused_rms_norm(q, lw.q_norm, cfg.rms_norm_eps).transpose(1, 2)
+        k_pre = fused_rms_norm(k, lw.k_norm, cfg.rms_norm_eps).transpose(1, 2)
+        q = q * cos + _rotate_half(q) * sin
+        k = (k_pre * cos + _rotate_half(k_pre) * sin).contiguous()
+        return q, k_pre, k, v
+
+    def _commit_kv(self, li: int, k: torch.Tensor, v: torch.Tensor, total: int) -> None:
+        """Quantize the complete 64-token groups of the fp16 K/V ``[B, Hkv, total, D]``
+        into layer li's int8 cache and put the last <= 64 tokens into the ring
+        (src/nova/kvattn.py:745-783)."""
+        cache, d = self.cache, self.cfg.head_dim
+        q_full = (total // GROUP_T) * GROUP_T
+        stream = _lib.stream_of(self.device)
+        if q_full:
+            for src, dst, mn, st in ((k, cache.kq[li], cache.kmn[li], cache.kst[li]),
+                                     (v, cache.vq[li], cache.vmn[li], cache.vst[li])):
+                _lib.call("nova_kv_quant_int8", src.data_ptr(), src.stride(1), dst.data_ptr(), self.max_len * d,
+                          mn.data_ptr(), st.data_ptr(), mn.shape[2] * d, self.batch * self.hkv, q_full, d, GROUP_T,
+                          stream)
+        take = min(total, GROUP_T)
+        slots = torch.remainder(torch.arange(total - take, total, device=self.device), GROUP_T)
+        cache.tail_k[li].index_copy_(2, slots, k[:, :, total - take:total])
+        cache.tail_v[li].index_copy_(2, slots, v[:, :, total - take:total])
+
+    def _set_scalars(self, total: int) -> None:
+        cache = self.cache
+        q_full = (total // GROUP_T) * GROUP_T
+        cache.pos.fill_(total)
+        cache.first.fill_(0)
+        cache._written.fill_(total)
+        cache._qlen.fill_(q_full)
+        cache._pg.fill_(q_full // GROUP_T)
+        self.argmax_slot.zero_()
+
     @torch.inference_mode()
-    def prefill(self, input_ids: torch.Tensor) -> torch.Tensor:
-        """Eager prefill of ``input_ids`` ``[batch, T]`` from position 0;
-        returns the first greedy token ``[batch]`` (also left in ``input_ids``,
-        src/nova/decode.py:224-297)."""
+    def prefill(self, input_ids: torch.Tensor, offset: int | None = None, reset: bool = True) -> torch.Tensor:
+        """Eager prefill of ``input_ids`` ``[batch, T]`` at positions
+        [offset, offset + T); returns the first greedy token ``[batch]`` (also
+        left in ``input_ids``, src/nova/decode.py:224-297).
+
+        ``reset=True`` (default) starts from an empty cache at offset 0.
+        ``reset=False`` continues after the positions written so far (a
+        previous prefill or ``inject``; ``offset`` defaults to ``pos``): the
+        new tokens attend to the staged fp16 K/V of those positions, as the
+        reference's staged prefill does, and the int8 cache is re-quantized
+        over all of them.  The staged fp16 K/V is kept until ``capture()``
+        (or ``release_staging()``)."""
         cfg, cache = self.cfg, self.cache
         B, T = input_ids.shape
-        if B != self.batch or T < 1 or T >= self.max_len:
-            raise ValueError(f"prompt shape {tuple(input_ids.shape)} does not fit batch={self.batch}, "
-                             f"max_len={self.max_len}")
-        cache.reset()
-        ids = input_ids.to(self.device)
-        h = self.w.embed[ids]                                     # [B, T, H]
-        cos, sin = self.cos[:T][None, None], self.sin[:T][None, None]
-        hq, hkv, d = self.hq, self.hkv, cfg.head_dim
-        qd, kvd = self.q_dim, self.kv_dim
-        q_full = (T // GROUP_T) * GROUP_T
-        stream = _lib.stream_of(self.device)
+        if reset:
+            cache.reset()
+            self._staged = None
+            offset = 0 if offset is None else int(offset)
+        elif offset is None:
+            offset = int(cache.pos.item())
+        offset = int(offset)
+        if B != self.batch or T < 1 or offset + T >= self.max_len:
+            raise ValueError(f"prompt shape {tuple(input_ids.shape)} at offset {offset} does not fit "
+                             f"batch={self.batch}, max_len={self.max_len}")
+        have = 0 if self._staged is None else self._staged[0][0].shape[2]
+        if offset != have:
+            raise ValueError(f"offset {offset} must equal the {have} positions written since the last reset")
+        total = offset + T
+        h = self.w.embed[input_ids.to(self.device)]                   # [B, T, H]
+        cos, sin = self.cos[offset:total][None, None], self.sin[offset:total][None, None]
+        gq = self.hq // self.hkv
+        staged = []
         for li, lw in enumerate(self.w.layers):
-            x = fused_rms_norm(h, lw.input_ln, cfg.rms_norm_eps)
-            qkv = self._linear16(x, lw.qkv)
-            q = qkv[..., :qd].reshape(B, T, hq, d)
-            k = qkv[..., qd:qd + kvd].reshape(B, T, hkv, d)
-            v = qkv[..., qd + kvd:].reshape(B, T, hkv, d).transpose(1, 2)
-            q = fused_rms_norm(q, lw.q_norm, cfg.rms_norm_eps).transpose(1, 2)
-            k = fused_rms_norm(k, lw.k_norm, cfg.rms_norm_eps).transpose(1, 2)
-            q = q * cos + _rotate_half(q) * sin
-            k = (k * cos + _rotate_half(k) * sin).contiguous()
-            v = v.contiguous()
-            gq = hq // hkv
-            o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
-                                               is_causal=True, scale=d ** -0.5)
-            o = o.transpose(1, 2).reshape(B, T, qd)
+            q, _, k, v = self._layer_qkv(li, lw, h, cos, sin)
+            if offset:
+                k = torch.cat([self._staged[li][0], k], dim=2)
+                v = torch.cat([self._staged[li][1], v], dim=2)
+                rows = torch.arange(offset, total, device=self.device)
+                keep = torch.arange(total, device=self.device).view(1, -1) <= rows.view(-1, 1)
+                mask = torch.zeros(T, total, dtype=torch.float16, device=self.device).masked_fill(~keep,
+                                                                                                  float("-inf"))
+                o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
+                                                   attn_mask=mask, scale=cfg.head_dim ** -0.5)
+            else:
+                o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
+                                                   is_causal=True, scale=cfg.head_dim ** -0.5)
+            o = o.transpose(1, 2).reshape(B, T, self.q_dim)
             h = h + self._row_parallel(o, lw.o)
             x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
             gu = self._linear16(x, lw.gate_up).view(B, T, -1, 2, 8)
             gate = gu[:, :, :, 0].reshape(B, T, -1)
             up = gu[:, :, :, 1].reshape(B, T, -1)
             h = h + self._row_parallel(F.silu(gate) * up, lw.down)
-            # int8 cache: complete groups quantized, the rest into the ring
-            if q_full:
-                for src, dst, mn, st in ((k, cache.kq[li], cache.kmn[li], cache.kst[li]),
-                                         (v, cache.vq[li], cache.vmn[li], cache.vst[li])):
-                    _lib.call("nova_kv_quant_int8", src.data_ptr(), T * d, dst.data_ptr(), self.max_len * d,
-                              mn.data_ptr(), st.data_ptr(), mn.shape[2] * d, B * hkv, q_full, d, GROUP_T, stream)
-            take = min(T, GROUP_T)
-            slots = torch.remainder(torch.arange(T - take, T, device=self.device), GROUP_T)
-            cache.tail_k[li].index_copy_(2, slots, k[:, :, T - take:T])
-            cache.tail_v[li].index_copy_(2, slots, v[:, :, T - take:T])
+            self._commit_kv(li, k, v, total)
+            staged.append((k, v))
+        self._staged = staged
         x = fused_rms_norm(h[:, -1], self.w.final_norm, cfg.rms_norm_eps)
         logits = self._linear16(x, self.w.lm_head)
         first = torch.argmax(logits, dim=-1)
         self.logits.copy_(logits)
         self.input_ids.copy_(first)
         self.resid.copy_(self.w.embed[first])
-        cache.pos.fill_(T)
-        cache.first.fill_(0)
-        cache._written.fill_(T)
-        cache._qlen.fill_(q_full)
-        cache._pg.fill_(q_full // GROUP_T)
-        self.argmax_slot.zero_()
+        self._set_scalars(total)
         return first
+
+    @torch.inference_mode()
+    def capture_kv(self, input_ids: torch.Tensor, span: tuple[int, int]) -> tuple[torch.Tensor, torch.Tensor]:
+        """K (after k_norm, before RoPE) and V of positions [span[0], span[1])
+        on every layer, from a forward over ``input_ids`` ``[1, T]`` that does
+        not touch the cache (capture_kv, src/nova/memory.py:176-217):
+        ``[layers, kv_heads, m, head_dim]`` fp16 each."""
+        cfg = self.cfg
+        B, T = input_ids.shape
+        s0, s1 = int(span[0]), int(span[1])
+        if B != 1 or not 0 <= s0 < s1 <= T:
+            raise ValueError(f"capture needs batch 1 and 0 <= {s0} < {s1} <= {T}")
+        h = self.w.embed[input_ids.to(self.device)]
+        cos, sin = self.cos[:T][None, None], self.sin[:T][None, None]
+        gq = self.hq // self.hkv
+        ks, vs = [], []
+        for li, lw in enumerate(self.w.layers):
+            q, k_pre, k, v = self._layer_qkv(li, lw, h, cos, sin)
+            ks.append(k_pre[0, :, s0:s1].clone())
+            vs.append(v[0, :, s0:s1].clone())
+            o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
+                                               is_causal=True, scale=cfg.head_dim ** -0.5)
+            o = o.transpose(1, 2).reshape(B, T, self.q_dim)
+            h = h + self._row_parallel(o, lw.o)
+            x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
+            gu = self._linear16(x, lw.gate_up).view(B, T, -1, 2, 8)
+            h = h + self._row_parallel(F.silu(gu[:, :, :, 0].reshape(B, T, -1)) * gu[:, :, :, 1].reshape(B, T, -1),
+                                       lw.down)
+        return torch.stack(ks), torch.stack(vs)
+
+    @torch.inference_mode()
+    def inject(self, k: torch.Tensor, v: torch.Tensor, offset: int = 0) -> int:
+        """Write captured K/V (``[layers, kv_heads, m, head_dim]``, K before
+        RoPE) into positions [offset, offset + m), K rotated to those
+        positions (MemoryStore.inject, src/nova/memory.py:447-475, which writes
+        the reference's fp16 cache only -- its int8 cache is documented as
+        incompatible, src/nova/kvattn.py:544-546); returns offset + m.  The
+        int8 cache holds the quantized groups and the ring exactly as after a
+        prefill of the same positions; the fp16 values stay staged for a
+        following ``prefill(..., reset=False)``.  ``offset`` 0 resets the
+        cache; otherwise it must equal the positions written so far.  Batch 1."""
+        L, hkv, m, d = k.shape
+        if self.batch != 1 or L != self.cfg.num_hidden_layers or hkv != self.hkv or d != self.cfg.head_dim:
+            raise ValueError(f"K/V shape {tuple(k.shape)} does not match the model (batch must be 1)")
+        if v.shape != k.shape:
+            raise ValueError("K and V shapes differ")
+        offset = int(offset)
+        if offset == 0:
+            self.cache.reset()
+            self._staged = None
+        have = 0 if self._staged is None else self._staged[0][0].shape[2]
+        if offset != have or offset + m >= self.max_len:
+            raise ValueError(f"offset {offset}: {have} positions written, capacity {self.max_len}")
+        total = offset + m
+        cos, sin = self.cos[offset:total][None], self.sin[offset:total][None]
+        staged = []
+        for li in range(L):
+            kk = k[li].to(self.device, torch.float16)
+            kr = (kk * cos + _rotate_half(kk) * sin)[None].contiguous()
+            vv = v[li].to(self.device, torch.float16)[None].contiguous()
+            if offset:
+                kr = torch.cat([self._staged[li][0], kr], dim=2)
+                vv = torch.cat([self._staged[li][1], vv], dim=2)
+            self._commit_kv(li, kr, vv, total)
+            staged.append((kr, vv))
+        self._staged = staged
+        self._set_scalars(total)
+        return total
+
+    def release_staging(self) -> None:
+        """Drop the fp16 K/V kept for segmented prefill / injection."""
+        self._staged = None
 
     def grow(self, new_max_len: int) -> None:
         """Move the int8 KV cache into a larger capacity bucket without a
@@ -606,6 +728,7 @@ class NovaDecoder:
         programmatic dependencies: each one's weight prefetch and LUT build
         overlap the previous kernel."""
         self.graph = None
+        self._staged = None   # a segmented prefill ends with the first captured step
         if self.tp.active:   # the communicator must exist before its first captured collective
             all_reduce_sum(torch.zeros_like(self.part32), self.tp)
         torch.cuda.synchronize(self.device)
@@ -624,6 +747,28 @@ class NovaDecoder:
         if self.graph is None:
             raise RuntimeError("call capture() first")
         self.graph.replay()
+        return self.input_ids
+
+    def step_sample(self, temperature: float, top_k: int = 20, top_p: float = 1.0, repetition_penalty: float = 1.0,
+                    seen: torch.Tensor | None = None, gen: torch.Generator | None = None) -> torch.Tensor:
+        """One graph replay, then the next token drawn outside the graph from
+        the step's logits (the chat CLI's pattern, src/chat.py:205-214): the
+        sampled token replaces the graph's argmax in ``input_ids`` and its
+        embedding row becomes the next step's input; ``seen`` (bool/uint8
+        ``[batch, vocab]`` or ``[vocab]``) is read for the repetition penalty
+        and gets the new token marked.  Temperature <= 0 keeps the argmax."""
+        from .sampling import sample_topk
+
+        if self.graph is None:
+            raise RuntimeError("call capture() first")
+        self.graph.replay()
+        u = None
+        if temperature > 0:
+            u = torch.rand(self.batch, generator=gen, device=self.device if gen is None else gen.device)
+            u = u.to(self.device, torch.float32)
+        sample_topk(self.logits, temperature=temperature, top_k=top_k, top_p=top_p,
+                    repetition_penalty=repetition_penalty, seen=seen, uniform=u, token_out=self.input_ids,
+                    embed=self.w.embed, embed_out=self.resid, seen_mark=seen)
         return self.input_ids
 
     def step_host(self, tokens_in: torch.Tensor, tokens_out: torch.Tensor) -> torch.Tensor:

@@ -10,7 +10,8 @@ then compare the CUDA kernels with the oracle.  Only the reference functions
 that run without Triton/CUDA/bitsandbytes are used (kvquant, the KVInt8Cache
 prefill + ring path on CPU, SDPA math on CPU, LeanRMSNorm "exact",
 apply_rotary_pos_emb with the transformers Qwen3-VL rotary, build_nf4_lut,
-extract_nf4 with a non-nested quant state, and -- for the decoder fixture --
+extract_nf4 with a non-nested quant state, the chat CLI's sample_next (its
+candidate ids and final probabilities), and -- for the decoder fixture --
 a random-init reference NovaTextModel whose linears run the NF4 dequant formula
 of tests/test_nf4_linear.py:46-57 and whose KVInt8Cache.attend is the
 reference's own single-softmax ground truth (tests/test_kvattn_stream.py:68-83)).
@@ -212,8 +213,56 @@ def norm_rope_fixture() -> None:
     _save("norm_rope.npz", **out)
 
 
+def sampling_fixture() -> None:
+    """sample_next (src/chat.py:46-75): the top-k candidate ids and the final
+    probabilities it hands to torch.multinomial (captured by wrapping
+    torch.topk / torch.multinomial), for several argument sets; greedy
+    (temperature 0) returns the argmax.  The 300 largest logits are distinct so
+    that no tie sits at the top-k boundary."""
+    import types
+    os.environ.setdefault("TMPDIR", "/tmp")
+    import chat as ref_chat
+
+    V = 32768
+    g = torch.Generator().manual_seed(5)
+    cases = [(0.7, 20, 0.8, 1.05), (1.0, 0, 1.0, 1.0), (0.3, 50, 0.95, 1.3), (1.3, 256, 0.5, 1.0), (0.0, 20, 0.8, 1.05)]
+    out = {}
+    orig_topk, orig_mult = torch.topk, torch.multinomial
+    for ci, (temp, top_k, top_p, rep) in enumerate(cases):
+        logits = (torch.randn(V, generator=g) * 2.0).to(torch.float16)
+        top = torch.randperm(V, generator=g)[:300]
+        logits[top] = (torch.arange(300, dtype=torch.float32) * 0.03125 + 9.0).to(torch.float16)[torch.randperm(300, generator=g)]
+        seen = torch.rand(V, generator=g) < 0.05
+        seen[top[:40]] = True
+        cap = {}
+
+        def topk(x, k, **kw):
+            r = orig_topk(x, k, **kw)
+            cap["idx"] = r[1].clone()
+            return r
+
+        def multinomial(p, *a, **kw):
+            cap["probs"] = p.clone()
+            return orig_mult(p, *a, **kw)
+
+        torch.topk, torch.multinomial = topk, multinomial
+        try:
+            args = types.SimpleNamespace(temperature=temp, top_k=top_k, top_p=top_p, repetition_penalty=rep)
+            tok = ref_chat.sample_next(logits.view(1, V), args, seen, torch.Generator().manual_seed(ci))
+        finally:
+            torch.topk, torch.multinomial = orig_topk, orig_mult
+        out[f"logits{ci}"] = logits
+        out[f"seen{ci}"] = seen
+        out[f"args{ci}"] = np.array([temp, top_k, top_p, rep], dtype=np.float64)
+        out[f"token{ci}"] = tok.view(-1)
+        if temp > 0:
+            out[f"idx{ci}"] = cap["idx"].view(-1)
+            out[f"probs{ci}"] = cap["probs"].view(-1)
+    _save("sampling.npz", **out)
+
+
 def main() -> None:
-    which = set(sys.argv[1:]) or {"kvquant", "ring", "attention", "nf4", "norm_rope"}
+    which = set(sys.argv[1:]) or {"kvquant", "ring", "attention", "nf4", "norm_rope", "sampling"}
     if "kvquant" in which:
         kvquant_fixture()
     if "ring" in which:
@@ -224,6 +273,8 @@ def main() -> None:
         nf4_fixture()
     if "norm_rope" in which:
         norm_rope_fixture()
+    if "sampling" in which:
+        sampling_fixture()
 
 
 if __name__ == "__main__":

@@ -262,3 +262,78 @@ def test_grow_preserves_decode(cuda_lib):
         dec.step()
     assert int(dec.pos.item()) == 300
     assert dec.input_ids.min().item() >= 0 and dec.input_ids.max().item() < cfg.vocab_size
+
+
+def _cache_bytes(dec):
+    c = dec.cache
+    out = {n: [t.clone() for t in getattr(c, n)] for n in ("kq", "vq", "kmn", "kst", "vmn", "vst", "tail_k", "tail_v")}
+    out["scalars"] = [int(getattr(c, n).item()) for n in ("pos", "first", "_written", "_qlen", "_pg")]
+    return out
+
+
+def test_injection_reproduces_prefill(cuda_lib):
+    """Captured K/V injected at the same positions leave the int8 cache
+    bit-identical to a real prefill (the reference's
+    test_memory.py::test_injection_reproduces_prefill, here for the int8 cache
+    its MemoryStore.inject cannot write)."""
+    from nova_b200.decoder import NovaDecoder
+
+    cfg, W, ref, _, prompt = _setup("small", 1, prompt_len=150, max_len=256)
+    dec = NovaDecoder(W, max_len=256, batch=1)
+    k, v = dec.capture_kv(prompt, (0, 150))
+    assert k.shape == (cfg.num_hidden_layers, cfg.num_key_value_heads, 150, cfg.head_dim)
+    assert dec.inject(k, v) == 150
+    a, b = _cache_bytes(ref), _cache_bytes(dec)
+    assert a["scalars"] == b["scalars"]
+    for n in ("kq", "vq", "kmn", "kst", "vmn", "vst", "tail_k", "tail_v"):
+        for li in range(cfg.num_hidden_layers):
+            assert torch.equal(a[n][li], b[n][li]), (n, li)
+
+
+def test_segmented_prefill_and_injection(cuda_lib):
+    """prefill(history) + inject(memory) + prefill(turn, reset=False) attends to
+    every earlier position through the staged fp16 K/V: the cache bytes match a
+    single prefill of the whole sequence except where the attention kernels'
+    summation order differs, the first token is the same, and decoding on
+    from the injected state equals decoding on from the whole prefill."""
+    from nova_b200.decoder import NovaDecoder
+
+    cfg, W, ref, _, _ = _setup("small", 1, prompt_len=8, max_len=320)
+    g = torch.Generator().manual_seed(7)
+    hist, mem, turn = (torch.randint(0, cfg.vocab_size, (1, n), generator=g) for n in (70, 90, 50))
+    whole = torch.cat([hist, mem, turn], dim=1)
+    first_ref = ref.prefill(whole).clone()
+    logits_ref = ref.logits.float().clone()
+
+    dec = NovaDecoder(W, max_len=320, batch=1)
+    k, v = dec.capture_kv(whole[:, :160], (70, 160))    # the memory span in its real context
+    dec.prefill(hist)
+    assert dec.inject(k, v, offset=70) == 160
+    first = dec.prefill(turn, reset=False)
+    assert int(dec.pos.item()) == 210
+    assert torch.equal(first, first_ref)
+    scale = logits_ref.abs().max().item()
+    assert (dec.logits.float() - logits_ref).abs().max().item() <= 2e-2 * scale
+    a, b = _cache_bytes(ref), _cache_bytes(dec)
+    assert a["scalars"] == b["scalars"]
+    # layer 0's K/V involve no attention: bit-identical; deeper layers see SDPA outputs computed over
+    # sequences of other lengths (70 / 160 / 210 tokens), so a few codes move by the last rounding step
+    for n in ("kq", "vq"):
+        assert torch.equal(a[n][0][:, :, :210], b[n][0][:, :, :210])
+        for li in range(1, cfg.num_hidden_layers):
+            diff = (a[n][li][:, :, :210].int() - b[n][li][:, :, :210].int()).abs()
+            assert diff.max().item() <= 2 and (diff > 0).float().mean().item() <= 0.05, (n, li)
+    with pytest.raises(ValueError):
+        dec.inject(k, v, offset=5)      # not where the written positions end
+    # decoding on from an injected-only state equals decoding on from the prefill it reproduces
+    d1 = NovaDecoder(W, max_len=320, batch=1)
+    d1.prefill(whole[:, :159])
+    d2 = NovaDecoder(W, max_len=320, batch=1)
+    k2, v2 = d2.capture_kv(whole[:, :159], (0, 159))
+    d2.inject(k2, v2)
+    d2.input_ids.copy_(d1.input_ids)
+    d2.resid.copy_(d1.resid)
+    d1.capture()
+    d2.capture()
+    for _ in range(20):
+        assert torch.equal(d1.step(), d2.step())
