@@ -1684,6 +1684,7 @@ constexpr int TC_A_COLS = 32 * TC_KG;              // 128 rows x 64 k fp16 = 32 
 constexpr int TC_TMEM_COLS = 512;
 constexpr int TC_SLOT_FLOATS = 64 * TC_ROWS;       // partial tile [batch row / 4][weight row][4]
 constexpr int TC_MAX_M = 64;
+constexpr int TC_MAX_TILES = 4096;                 // N up to 524288 rows
 constexpr int TC_MIN_ITEMS = 4;                    // work items per CTA at least (bounds the split fan-in)
 
 struct TcArgs {
@@ -2584,9 +2585,11 @@ extern "C" int nova_qkv_norm_rope_append(const nova_nf4_args* g, const nova_qk_a
 
 // ---------------------------------------------------------------- batched GEMM (host)
 
-// Workspace: [tile counters (up to 1000 tiles), finalize counter, error word | split-K slots].  The counters
-// sit at the same place for every shape, so one workspace sized for the largest GEMM serves them all.
-constexpr int64_t GM_COUNTER_BYTES = 4096;
+// mma.sync GEMM workspace: [tile counters (up to 1000 tiles), finalize counter, error word | split-K
+// slots].  The counters sit at the same place for every shape, so one workspace sized for the largest
+// GEMM serves them all; the slots start past the tcgen05 GEMM's counter region as well, so the two
+// kernels may also share a workspace (one launch at a time).
+constexpr int64_t GM_COUNTER_BYTES = (256 + int64_t(TC_MAX_TILES) * 16 + 1023) / 1024 * 1024;
 
 // Split count: no more CTAs than SMs (one wave), and about sqrt(3 * k-blocks): each split adds
 // ~KB/S k-block steps of work per CTA but one more 128 KB partial for the last CTA to add.
@@ -2594,13 +2597,16 @@ static int64_t tc_grid(int64_t items) {
     return std::max<int64_t>(1, std::min<int64_t>(sm_count(), (items + TC_MIN_ITEMS - 1) / TC_MIN_ITEMS));
 }
 
-// tcgen05 GEMM workspace: [0] finalize arrivals, [4] error word, [256..) per
-// tile and lane quarter split arrivals, then 2 partial slots per CTA.
+// tcgen05 GEMM workspace: [0] finalize arrivals, [4] error word, [256, 256 +
+// 16 * TC_MAX_TILES) split arrivals per tile and lane quarter, then 2 partial
+// slots per CTA.  The offsets are the same for every shape, so launches of
+// different shapes can share one workspace: each leaves its counters at zero,
+// and no shape's partials reach another's counters.
 static int64_t tc_workspace_layout(int64_t n, int64_t k, int64_t* part_off) {
     const int64_t tiles = (n + TC_ROWS - 1) / TC_ROWS;
     const int64_t w = tiles * ((k / 64 + TC_KG - 1) / TC_KG);
     const int64_t g = tc_grid(w);
-    const int64_t off = (256 + tiles * 16 + 1023) / 1024 * 1024;
+    const int64_t off = (256 + int64_t(TC_MAX_TILES) * 16 + 1023) / 1024 * 1024;
     if (part_off) *part_off = off;
     return off + g * 2 * int64_t(TC_SLOT_FLOATS) * 4;
 }
@@ -2714,7 +2720,11 @@ extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
     nova_nf4_gemm_workspace_bytes(n, k, &need);
     if (a->workspace_bytes < need) return fail(NOVA_ERR_INVALID, "workspace too small: %lld < %lld",
                                                (long long)a->workspace_bytes, (long long)need);
-    if (a->layout == 2) return nf4_gemm_tc(a, epi, (cudaStream_t)stream);
+    if (a->layout == 2) {
+        if ((n + TC_ROWS - 1) / TC_ROWS > TC_MAX_TILES)
+            return fail(NOVA_ERR_UNSUPPORTED, "N above %d rows", TC_MAX_TILES * TC_ROWS);
+        return nf4_gemm_tc(a, epi, (cudaStream_t)stream);
+    }
     int64_t tiles = 0, splits = 0;
     gemm_shape(n, k, &tiles, &splits);
     Params p;

@@ -21,6 +21,19 @@
 // start epoch e+2 only after every peer has sent epoch e+1, which each peer
 // does after finishing epoch e.  No TMA, no multicast: plain 16-byte stores to
 // peer memory and volatile polling of local memory.
+//
+// Large partials (batched decode) take two phases instead, cutting what each
+// rank sends from (world - 1) x count words to ~1.5 x count x (world - 1) /
+// world: rank r owns slice r of the elements;
+//   1. every rank stores slice d of its partial, stamped, into rank d's buffer;
+//   2. rank r sums its slice from every rank in rank order (the same bits as
+//      the one-shot path), applies the residual add, and stores the finished
+//      fp16 pairs (2 values + stamp per 8-byte word) into every rank's buffer;
+//   3. every rank copies the other slices' finished pairs into its residual.
+// A thread stores all it sends before it waits, phase 2 waits only on phase-1
+// stores and phase 3 only on phase-2 stores, and the grid is resident, so no
+// wait is circular; every rank's epoch e+1 still needs words that each peer
+// writes only after finishing epoch e, so the two parities stay sufficient.
 #include "common.cuh"
 
 namespace nova {
@@ -29,6 +42,7 @@ namespace tp {
 constexpr int MAX_WORLD = 8;
 constexpr int MAX_CHUNKS = 32;
 constexpr int THREADS = 128;
+constexpr int64_t TWO_PHASE_MIN = 16384;   // elements (rows * n) from which the two-phase exchange is used
 
 struct Params {
     const float* part;             // [rows, n] this rank's partial sums (contiguous)
@@ -39,6 +53,7 @@ struct Params {
     unsigned* done;                // CTA arrival counter (local)
     int* err;                      // error word (local)
     int64_t count, chunk;          // rows * n, elements per CTA (multiple of 4)
+    int64_t slice;                 // two-phase: elements per rank's slice (even)
     int rows, n, rank, world;
     unsigned long long timeout_ns;
 };
@@ -115,6 +130,91 @@ __global__ void __launch_bounds__(THREADS) allreduce_add_kernel(const __grid_con
     }
 }
 
+__global__ void __launch_bounds__(THREADS) allreduce_add_2phase_kernel(const __grid_constant__ Params p) {
+    __shared__ int s_last;
+    pdl_trigger();
+    pdl_wait();
+    const int64_t e = *p.epoch + 1;
+    const uint32_t st32 = uint32_t(e);
+    const uint64_t stamp = uint64_t(st32) << 32;
+    const int par = int(e & 1);
+    const int64_t npairs = p.count / 2;
+    const int64_t tid = int64_t(blockIdx.x) * THREADS + threadIdx.x, nthr = int64_t(gridDim.x) * THREADS;
+    const int64_t my_lo = int64_t(p.rank) * p.slice, my_hi = min(p.count, my_lo + p.slice);
+    // 1. slice d of this rank's partial into slot `rank` of rank d's buffer
+    for (int64_t q = tid; q < npairs; q += nthr) {
+        const int64_t i = 2 * q;
+        const int d = int(i / p.slice);
+        const float2 v = *reinterpret_cast<const float2*>(p.part + i);
+        st_ll(words_of(p.bufs[d], par, p.rank, p.count) + i, stamp | __float_as_uint(v.x), stamp | __float_as_uint(v.y));
+    }
+    const unsigned long long t0 = gtime();
+    bool ok = true;
+    // 2. this rank's slice: sum in rank order, residual add, finished pairs to every rank
+    for (int64_t i = my_lo + 2 * tid; i < my_hi && ok; i += 2 * nthr) {
+        float acc0 = 0.f, acc1 = 0.f;
+        for (int r = 0; r < p.world && ok; ++r) {
+            const uint64_t* w = words_of(p.bufs[p.rank], par, r, p.count) + i;
+            uint64_t a, b;
+            ld_ll(w, a, b);
+            while (uint32_t(a >> 32) != st32 || uint32_t(b >> 32) != st32) {
+                if (gtime() - t0 > p.timeout_ns) {
+                    atomicExch(p.err, 1);
+                    ok = false;
+                    break;
+                }
+                ld_ll(w, a, b);
+            }
+            acc0 += __uint_as_float(uint32_t(a));
+            acc1 += __uint_as_float(uint32_t(b));
+        }
+        if (!ok) break;
+        const int64_t row = i / p.n, col = i % p.n;
+        __half2* rp = reinterpret_cast<__half2*>(p.resid + row * p.r_stride + col);
+        const float2 r0 = __half22float2(*rp);
+        const __half2 h = __floats2half2_rn(r0.x + __half2float(__float2half_rn(acc0)),
+                                            r0.y + __half2float(__float2half_rn(acc1)));
+        *rp = h;
+        const uint64_t word = stamp | uint64_t(*reinterpret_cast<const uint32_t*>(&h));
+        for (int r = 0; r < p.world; ++r)
+            if (r != p.rank)
+                asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(words_of(p.bufs[r], par, p.rank, p.count) + i),
+                             "l"(word)
+                             : "memory");
+    }
+    // 3. the other ranks' finished pairs
+    for (int64_t q = tid; q < npairs && ok; q += nthr) {
+        const int64_t i = 2 * q;
+        const int src = int(i / p.slice);
+        if (src == p.rank) continue;
+        const uint64_t* w = words_of(p.bufs[p.rank], par, src, p.count) + i;
+        uint64_t a;
+        asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(w) : "memory");
+        while (uint32_t(a >> 32) != st32) {
+            if (gtime() - t0 > p.timeout_ns) {
+                atomicExch(p.err, 1);
+                ok = false;
+                break;
+            }
+            asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(w) : "memory");
+        }
+        if (!ok) break;
+        const int64_t row = i / p.n, col = i % p.n;
+        const uint32_t hv = uint32_t(a);
+        *reinterpret_cast<__half2*>(p.resid + row * p.r_stride + col) = *reinterpret_cast<const __half2*>(&hv);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(p.done, 1u);
+        s_last = prev == gridDim.x - 1;
+        if (s_last) {
+            *p.done = 0u;
+            *p.epoch = e;
+        }
+    }
+}
+
 }  // namespace tp
 }  // namespace nova
 
@@ -162,8 +262,14 @@ extern "C" int nova_tp_allreduce_add(const nova_tp_allreduce_args* a, void* stre
     const int64_t chunks = std::min<int64_t>(tp::MAX_CHUNKS, (p.count + 255) / 256);
     p.chunk = ((p.count + chunks - 1) / chunks + 1) / 2 * 2;
     const int64_t grid = (p.count + p.chunk - 1) / p.chunk;
+    p.slice = ((p.count + p.world - 1) / p.world + 1) / 2 * 2;
+    // one shot below 16K elements (latency: one exchange), two phases above (bandwidth)
+    const bool two_phase = p.world > 1 && p.count >= tp::TWO_PHASE_MIN;
     const cudaError_t err =
-        launch(tp::allreduce_add_kernel, dim3(unsigned(grid)), dim3(tp::THREADS), 0, (cudaStream_t)stream, p);
+        two_phase ? launch(tp::allreduce_add_2phase_kernel, dim3(unsigned(tp::MAX_CHUNKS)), dim3(tp::THREADS), 0,
+                           (cudaStream_t)stream, p)
+                  : launch(tp::allreduce_add_kernel, dim3(unsigned(grid)), dim3(tp::THREADS), 0, (cudaStream_t)stream,
+                           p);
     if (err != cudaSuccess) {
         cudaGetLastError();
         return fail(NOVA_ERR_CUDA, "nova_tp_allreduce_add: launch failed: %s", cudaGetErrorString(err));

@@ -44,7 +44,8 @@ def _setup(kind, batch, prompt_len, max_len, seed=1):
     return cfg, W, dec, orc, prompt
 
 
-@pytest.mark.parametrize("kind,batch,steps", [("small", 1, 70), ("small", 3, 20), ("small", 11, 6), ("real", 1, 12)])
+@pytest.mark.parametrize("kind,batch,steps", [("small", 1, 70), ("small", 3, 20), ("small", 11, 6), ("real", 1, 12),
+                                              ("real", 11, 3)])
 def test_graph_decode_matches_oracle(cuda_lib, kind, batch, steps):
     cfg, W, dec, orc, _ = _setup(kind, batch, prompt_len=150, max_len=320)
     orc.load_state(dec.state())

@@ -42,7 +42,8 @@ def _oracle(x, packed, absmax):
 
 @pytest.mark.parametrize("layout", [2, 1])
 @pytest.mark.parametrize("m", [9, 16, 37, 64])
-@pytest.mark.parametrize("n,k", [(1024, 2560), (2560, 9728), (6144, 2560), (96, 192)])
+@pytest.mark.parametrize("n,k", [(1024, 2560), (2560, 9728), (6144, 2560), (96, 192), (3072, 2560), (2560, 2048),
+                                 (2560, 4864), (2560, 1216)])
 def test_gemm_plain_matches_dequant_matmul(cuda_lib, m, n, k, layout):
     from nova_b200.kernels import nf4_gemm, pack_native, pack_tc
 

@@ -26,18 +26,18 @@ STEPS_EAGER, STEPS_GRAPH = 3, 13
 
 
 def _run(dec, prompt):
-    toks, logits = [int(dec.prefill(prompt)[0])], [dec.logits[0].float().cpu().numpy()]
+    toks, logits = [dec.prefill(prompt).cpu().numpy().copy()], [dec.logits.float().cpu().numpy()]
     for _ in range(STEPS_EAGER):
-        toks.append(int(dec.step_eager()[0]))
-        logits.append(dec.logits[0].float().cpu().numpy())
+        toks.append(dec.step_eager().cpu().numpy().copy())
+        logits.append(dec.logits.float().cpu().numpy())
     dec.capture()
     for _ in range(STEPS_GRAPH):
-        toks.append(int(dec.step()[0]))
-        logits.append(dec.logits[0].float().cpu().numpy())
-    return np.array(toks), np.stack(logits)
+        toks.append(dec.step().cpu().numpy().copy())
+        logits.append(dec.logits.float().cpu().numpy())
+    return np.stack(toks), np.stack(logits)   # [steps, batch], [steps, batch, vocab]
 
 
-def _worker(rank, world, port, out_dir, allreduce):
+def _worker(rank, world, port, out_dir, allreduce, batch=1):
     import torch.distributed as dist
 
     from nova_b200.decoder import DecoderConfig, DecoderWeights, NovaDecoder
@@ -51,8 +51,8 @@ def _worker(rank, world, port, out_dir, allreduce):
     try:
         cfg = DecoderConfig(num_hidden_layers=2, vocab_size=4096)
         w = DecoderWeights.random_init(cfg, seed=3, device=dev, norm_jitter=0.1)
-        prompt = torch.randint(0, cfg.vocab_size, (1, 300), generator=torch.Generator().manual_seed(4))
-        dec = NovaDecoder(w, max_len=512, batch=1, device=dev,
+        prompt = torch.randint(0, cfg.vocab_size, (batch, 300), generator=torch.Generator().manual_seed(4))
+        dec = NovaDecoder(w, max_len=512, batch=batch, device=dev,
                           tp=TPContext(rank, world, dist.group.WORLD, allreduce=allreduce))
         toks, logits = _run(dec, prompt)
         if dec.p2p is not None:
@@ -60,7 +60,7 @@ def _worker(rank, world, port, out_dir, allreduce):
         dec.close()
         np.savez(os.path.join(out_dir, f"tp{rank}.npz"), toks=toks, logits=logits)
         if rank == 0:
-            ref = NovaDecoder(w, max_len=512, batch=1, device=dev)
+            ref = NovaDecoder(w, max_len=512, batch=batch, device=dev)
             rt, rl = _run(ref, prompt)
             ref.graph = None
             np.savez(os.path.join(out_dir, "single.npz"), toks=rt, logits=rl)
@@ -77,34 +77,38 @@ def _free_port():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("allreduce", ["p2p", "nccl"])
-def test_tp2_decoder_matches_single_gpu(cuda_lib, tmp_path, allreduce):
+@pytest.mark.parametrize("allreduce,batch", [("p2p", 1), ("nccl", 1), ("p2p", 11)])
+def test_tp2_decoder_matches_single_gpu(cuda_lib, tmp_path, allreduce, batch):
+    """Batch 11 runs the batched GEMM and, with 11 x 2560 elements per
+    all-reduce, the two-phase peer-memory exchange."""
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), allreduce), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), allreduce, batch), nprocs=2, join=True)
     t0, t1, s = (np.load(tmp_path / f) for f in ("tp0.npz", "tp1.npz", "single.npz"))
     np.testing.assert_array_equal(t0["toks"], t1["toks"])
     np.testing.assert_array_equal(t0["logits"], t1["logits"])
     ref_t, ref_l = s["toks"], s["logits"]
-    for i in range(len(ref_t)):
-        scale = np.abs(ref_l[i]).max()
-        assert np.abs(t0["logits"][i] - ref_l[i]).max() <= 5e-3 * scale + 1e-2, f"step {i}: logits differ"
-        if t0["toks"][i] != ref_t[i]:
-            top2 = np.sort(ref_l[i])[-2:]
-            assert top2[1] - top2[0] < 1e-2, f"step {i}: token differs without a near-tie"
-            break
+    for b in range(batch):
+        for i in range(len(ref_t)):
+            scale = np.abs(ref_l[i, b]).max()
+            assert np.abs(t0["logits"][i, b] - ref_l[i, b]).max() <= 5e-3 * scale + 1e-2, f"row {b} step {i}"
+            if t0["toks"][i, b] != ref_t[i, b]:
+                top2 = np.sort(ref_l[i, b])[-2:]
+                assert top2[1] - top2[0] < 1e-2, f"row {b} step {i}: token differs without a near-tie"
+                break
 
 
-def test_allreduce_wait_gives_up_with_error(cuda_lib):
+@pytest.mark.parametrize("rows,n", [(1, 256), (64, 2560)])
+def test_allreduce_wait_gives_up_with_error(cuda_lib, rows, n):
     """Bounded wait of nova_tp_allreduce_add, on one GPU: a two-rank call whose
     second "rank" is a second local buffer that nobody stamps.  The wait runs
     out after 50 ms, the kernel sets the error word, skips the sum (residual
-    unchanged) and returns; the context stays usable."""
+    unchanged) and returns; the context stays usable.  64 x 2560 elements take
+    the two-phase exchange."""
     import ctypes
 
     from nova_b200 import _lib
 
-    rows, n = 1, 256
     nb = ctypes.c_int64(0)
     _lib.call("nova_tp_recv_bytes", 2, rows, n, ctypes.byref(nb))
     bufs = [torch.zeros(int(nb.value), dtype=torch.uint8, device="cuda") for _ in range(2)]
