@@ -72,6 +72,7 @@ struct Params {
     unsigned* done;           // finalize arrival counter
     int M, N, K, KB, n_tiles, total_warps;
     int64_t units;
+    int res_rows = 0;         // CTA kernel: residual rows staged in shared memory per CTA (0: read in the epilogue)
 };
 
 template <typename T>
@@ -98,8 +99,11 @@ __device__ __forceinline__ unsigned long long argmax_key(__half v, int idx) {
 
 // Epilogue of one 16-row tile: lane (g, t) holds rows 16*tile+g (c[0], c[1])
 // and 16*tile+g+8 (c[2], c[3]) for batch rows m = m0 + 2t, m0 + 2t + 1.
+// `rs`: the residual rows [rs_row0, rs_row0 + rs_rows) of every batch row,
+// staged in shared memory ([m][rs_rows]); nullptr reads p.residual.
 template <int EPI>
-__device__ __forceinline__ void epilogue(const Params& p, int tile, const float (&c)[4], int g, int t, int m0 = 0) {
+__device__ __forceinline__ void epilogue(const Params& p, int tile, const float (&c)[4], int g, int t, int m0 = 0,
+                                         const __half* rs = nullptr, int rs_row0 = 0, int rs_rows = 0) {
     if (EPI == EPI_F32) {   // fp32 accumulators as they are (tensor-parallel partial sums)
         float* o = reinterpret_cast<float*>(p.out);
 #pragma unroll
@@ -136,8 +140,8 @@ __device__ __forceinline__ void epilogue(const Params& p, int tile, const float 
             float v = c[2 * hrow + e];
             __half h;
             if (EPI == EPI_RESIDUAL) {
-                h = __float2half_rn(__half2float(__ldcg(p.residual + m * p.res_stride + n)) +
-                                    __half2float(__float2half_rn(v)));
+                const __half r = rs ? rs[m * rs_rows + (n - rs_row0)] : __ldcg(p.residual + m * p.res_stride + n);
+                h = __float2half_rn(__half2float(r) + __half2float(__float2half_rn(v)));
             } else {
                 if (p.bias) v += __half2float(p.bias[n]);
                 h = __float2half_rn(v);
@@ -206,8 +210,18 @@ __device__ __forceinline__ void build_lut(uint32_t* lut_s, const uint32_t* lut) 
 // every thread holds at most one 8-element chunk per row (K <= 8 * THREADS),
 // the chunk stays in registers between the sum of squares and the scaling,
 // so x and the norm weight are read once.
+// The RMSNorm weight slice stage_x's single-chunk path uses (thread i holds
+// elements 8i..8i+7).  A weight, so it may be read before the dependency wait.
 template <int THREADS>
-__device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
+__device__ __forceinline__ uint4 norm_w_chunk(const Params& p) {
+    const int i = threadIdx.x;
+    if (p.norm_w && p.K / 8 <= THREADS && i < p.K / 8) return *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
+    return make_uint4(0u, 0u, 0u, 0u);
+}
+
+// `wpre`: norm_w_chunk() loaded earlier (nullptr: loaded here).
+template <int THREADS>
+__device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4* wpre = nullptr) {
     __shared__ float red[THREADS / 32][MAX_M];
     __shared__ float rstd[MAX_M];
     const int kv8 = p.K / 8;
@@ -232,7 +246,7 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
         if (one) {
             const int i = threadIdx.x;
             if (i < kv8) {
-                wv = *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
+                wv = wpre ? *wpre : *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
 #pragma unroll
                 for (int m = 0; m < MAX_M; ++m) {
                     if (m >= p.M) break;
@@ -299,10 +313,21 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs) {
             }
         }
     } else {
-        for (int i = threadIdx.x; i < p.M * kv8; i += THREADS) {
-            const int m = i / kv8, j = i % kv8;
-            *reinterpret_cast<uint4*>(xs + m * p.K + 8 * j) =
-                __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride) + j);
+        // up to four 16-byte chunks per thread requested before any is stored: one L2 round trip
+        constexpr int XU = 4;
+        const int total = p.M * kv8;
+        for (int base = threadIdx.x; base < total; base += XU * THREADS) {
+            uint4 v[XU];
+#pragma unroll
+            for (int u = 0; u < XU; ++u) {
+                const int i = base + u * THREADS;
+                if (i < total) v[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (i / kv8) * p.x_stride) + i % kv8);
+            }
+#pragma unroll
+            for (int u = 0; u < XU; ++u) {
+                const int i = base + u * THREADS;
+                if (i < total) *reinterpret_cast<uint4*>(xs + (i / kv8) * p.K + 8 * (i % kv8)) = v[u];
+            }
         }
     }
 }
@@ -462,9 +487,10 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         for (int c = 0; c < NAT_STAGES && c < n_chunks; ++c) issue(c);
     }
     build_lut<NAT_THREADS>(lut_s, p.lut);
+    const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);
     pdl_trigger();
     pdl_wait();
-    if (!XG) stage_x<NAT_THREADS>(p, xs);
+    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre);
     __syncthreads();
     if (!active) return;
 
@@ -561,9 +587,12 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     __half* xs = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
     const int xs_bytes = XG ? 0 : (p.M * p.K * 2 + 127) / 128 * 128;
     float4* red = reinterpret_cast<float4*>(smem_raw + LUT_BYTES + xs_bytes);   // [16][32][2]
+    __half* res_s = reinterpret_cast<__half*>(smem_raw + LUT_BYTES + xs_bytes + NAT_WARPS * 32 * 32);
+    const int res_bytes = (p.res_rows * p.M * 2 + 127) / 128 * 128;
     const int stage_bytes = stage_units * UNIT_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint8_t* ring = smem_raw + LUT_BYTES + xs_bytes + NAT_WARPS * 32 * 32 + size_t(warp) * NAT_STAGES * stage_bytes;
+    uint8_t* ring = smem_raw + LUT_BYTES + xs_bytes + NAT_WARPS * 32 * 32 + res_bytes +
+                    size_t(warp) * NAT_STAGES * stage_bytes;
     const int c = blockIdx.x;
     const int G = gridDim.x;
     const int KB = p.KB;
@@ -625,9 +654,34 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             if (!issue_next()) break;
     }
     build_lut<NAT_THREADS>(lut_s, p.lut);
+    const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);
     pdl_trigger();
     pdl_wait();
-    if (!XG) stage_x<NAT_THREADS>(p, xs);
+    // The residual rows of this CTA's row groups, read with x so that the
+    // epilogue does not wait on L2 (out may alias residual: these rows are
+    // written only by this CTA, after this read).
+    const int res_row0 = rg_first * UNIT_ROWS;
+    const int res_n = (rg_last - rg_first + 1) * UNIT_ROWS;
+    // Up to 4 values per thread are requested before x and stored after it,
+    // so both reads share one L2 round trip.
+    const bool res_staged = EPI == EPI_RESIDUAL && p.res_rows > 0 && res_n <= p.res_rows &&
+                            p.M * res_n <= 4 * NAT_THREADS;
+    __half rv[4];
+    if (res_staged) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = threadIdx.x + u * NAT_THREADS;
+            if (i < p.M * res_n) rv[u] = __ldcg(p.residual + (i / res_n) * p.res_stride + res_row0 + i % res_n);
+        }
+    }
+    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre);
+    if (res_staged) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = threadIdx.x + u * NAT_THREADS;
+            if (i < p.M * res_n) res_s[(i / res_n) * p.res_rows + i % res_n] = rv[u];
+        }
+    }
     __syncthreads();
 
     const uint32_t lut_base = smem_u32(lut_s);
@@ -700,8 +754,9 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             if (lane == 0) mbar_arrive(&bar_empty);
             const int64_t base = int64_t(rg) * KB;
             if (u_begin <= base && u_end >= base + KB) {
-                epilogue<EPI>(p, 2 * rg, r[0], g, t);
-                epilogue<EPI>(p, 2 * rg + 1, r[1], g, t);
+                const __half* rs = res_staged ? res_s : nullptr;
+                epilogue<EPI>(p, 2 * rg, r[0], g, t, 0, rs, res_row0, p.res_rows);
+                epilogue<EPI>(p, 2 * rg + 1, r[1], g, t, 0, rs, res_row0, p.res_rows);
             } else {
                 flush_partial<EPI, 2>(p, rg, r, c, rg_first, lane, g, t);
             }
@@ -2323,7 +2378,8 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         p.units = int64_t(n / UNIT_ROWS) * p.KB;
         int* errp = reinterpret_cast<int*>(p.done + 1);
         // Warp-level stream-K from two row groups per SM up (gate/up, the
-        // lm_head: the stream-K tail is short next to the stream); CTA-level
+        // lm_head: with several row groups per CTA the CTA-level schedule
+        // would synchronise its 16 warps once per row group); CTA-level
         // split-K on whole row groups below that (no cross-CTA reduction).
         const bool warp_level = (launch_flags() & 2) || n / UNIT_ROWS >= 2 * int64_t(sm_count());
         if (warp_level) {
@@ -2343,14 +2399,19 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
                  nf4_gemv_cta_kernel<3, true>, nf4_gemv_cta_kernel<4, true>}};
             static int64_t cta_smem_set[2][5] = {};
             const int64_t red_bytes = int64_t(NAT_WARPS) * 32 * 32;
-            const int64_t cu = std::min<int64_t>(4, (optin - int64_t(LUT_BYTES) - xs_bytes - red_bytes - slack) / ring_unit);
+            const int64_t grid = std::min<int64_t>(sm_count(), n / UNIT_ROWS);
+            const int64_t rg_max = (n / UNIT_ROWS + grid - 1) / grid;   // row groups of the largest CTA share
+            // residual rows staged per CTA when they fit in 4 values per thread
+            p.res_rows = (epi == EPI_RESIDUAL && rg_max * UNIT_ROWS * m <= 4 * NAT_THREADS) ? int(rg_max * UNIT_ROWS) : 0;
+            const int64_t res_bytes = (int64_t(p.res_rows) * m * 2 + 127) / 128 * 128;
+            const int64_t cu = std::min<int64_t>(
+                4, (optin - int64_t(LUT_BYTES) - xs_bytes - red_bytes - res_bytes - slack) / ring_unit);
             if (cu < 1)
                 return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld leaves no shared memory for the weight ring",
                             (long long)(m * k));
             NKern kern = cta_kernels[xg][epi];
-            const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + red_bytes + cu * ring_unit;
+            const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + red_bytes + res_bytes + cu * ring_unit;
             if (int rc = prepare_smem(kern, nsmem, &cta_smem_set[xg][epi])) return rc;
-            const int64_t grid = std::min<int64_t>(sm_count(), n / UNIT_ROWS);
             p.total_warps = int(grid);   // contributors and finalize arrivals are counted per CTA
             err = launch(kern, dim3(unsigned(grid)), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p,
                          int(cu), errp);

@@ -361,8 +361,89 @@ class NovaDecoder:
         cache._pg.fill_(q_full // GROUP_T)
         self.argmax_slot.zero_()
 
+    def _dequant_prefix(self, li: int, n: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """fp16 K/V ``[B, Hkv, n, D]`` of the first n (a multiple of 64) cached
+        positions of layer li, dequantized from the int8 cache
+        (``nova_kv_dequant_int8``, src/nova/kvquant.py:152-176)."""
+        cache, d = self.cache, self.cfg.head_dim
+        stream = _lib.stream_of(self.device)
+        outs = []
+        for codes, mn, st in ((cache.kq[li], cache.kmn[li], cache.kst[li]), (cache.vq[li], cache.vmn[li], cache.vst[li])):
+            out = torch.empty(self.batch, self.hkv, n, d, dtype=torch.float16, device=self.device)
+            _lib.call("nova_kv_dequant_int8", codes.data_ptr(), self.max_len * d, mn.data_ptr(), st.data_ptr(),
+                      mn.shape[2] * d, out.data_ptr(), n * d, self.batch * self.hkv, n, d, GROUP_T, stream)
+            outs.append(out)
+        return outs[0], outs[1]
+
+    def _prefill_chunked(self, input_ids: torch.Tensor, chunk: int) -> torch.Tensor:
+        """Prefill in chunks of ``chunk`` tokens (a multiple of 64) straight into
+        the int8 cache, the reference's planned replacement of its whole-prompt
+        fp16 staging (reports/kv-int8-streaming-cache.md, section 5.1): each
+        chunk attends to the int8 prefix of the earlier chunks (dequantized one
+        layer at a time) and to its own fp16 K/V, causally; its complete
+        64-token groups are quantized when the layer is done, the last <= 64
+        tokens of the prompt go into the ring.  No fp16 K/V outlives a layer."""
+        cfg, cache = self.cfg, self.cache
+        B, T = input_ids.shape
+        ids = input_ids.to(self.device)
+        gq = self.hq // self.hkv
+        d = cfg.head_dim
+        stream = _lib.stream_of(self.device)
+        take0 = T - min(T, GROUP_T)   # first position that goes into the ring
+        h = None
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            n = c1 - c0
+            h = self.w.embed[ids[:, c0:c1]]
+            cos, sin = self.cos[c0:c1][None, None], self.sin[c0:c1][None, None]
+            for li, lw in enumerate(self.w.layers):
+                q, _, k, v = self._layer_qkv(li, lw, h, cos, sin)
+                if c0:
+                    pk, pv = self._dequant_prefix(li, c0)
+                    kk, vv = torch.cat([pk, k], dim=2), torch.cat([pv, v], dim=2)
+                    rows = torch.arange(c0, c1, device=self.device)
+                    keep = torch.arange(c1, device=self.device).view(1, -1) <= rows.view(-1, 1)
+                    mask = torch.zeros(n, c1, dtype=torch.float16, device=self.device).masked_fill(~keep,
+                                                                                                   float("-inf"))
+                    o = F.scaled_dot_product_attention(q, kk.repeat_interleave(gq, dim=1),
+                                                       vv.repeat_interleave(gq, dim=1), attn_mask=mask,
+                                                       scale=d ** -0.5)
+                    del pk, pv, kk, vv
+                else:
+                    o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1),
+                                                       v.repeat_interleave(gq, dim=1), is_causal=True,
+                                                       scale=d ** -0.5)
+                o = o.transpose(1, 2).reshape(B, n, self.q_dim)
+                h = h + self._row_parallel(o, lw.o)
+                x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
+                gu = self._linear16(x, lw.gate_up).view(B, n, -1, 2, 8)
+                h = h + self._row_parallel(F.silu(gu[:, :, :, 0].reshape(B, n, -1)) * gu[:, :, :, 1].reshape(B, n, -1),
+                                           lw.down)
+                full = (n // GROUP_T) * GROUP_T   # complete groups of this chunk (chunk starts are group-aligned)
+                if full:
+                    g0 = c0 // GROUP_T
+                    for src, dst, mn, st in ((k, cache.kq[li], cache.kmn[li], cache.kst[li]),
+                                             (v, cache.vq[li], cache.vmn[li], cache.vst[li])):
+                        _lib.call("nova_kv_quant_int8", src.data_ptr(), src.stride(1), dst[:, :, c0:].data_ptr(),
+                                  self.max_len * d, mn[:, :, g0:].data_ptr(), st[:, :, g0:].data_ptr(),
+                                  mn.shape[2] * d, B * self.hkv, full, d, GROUP_T, stream)
+                if c1 > take0:   # positions of the prompt's last <= 64 tokens into the ring
+                    p0 = max(c0, take0)
+                    slots = torch.remainder(torch.arange(p0, c1, device=self.device), GROUP_T)
+                    cache.tail_k[li].index_copy_(2, slots, k[:, :, p0 - c0:])
+                    cache.tail_v[li].index_copy_(2, slots, v[:, :, p0 - c0:])
+        x = fused_rms_norm(h[:, -1], self.w.final_norm, cfg.rms_norm_eps)
+        logits = self._linear16(x, self.w.lm_head)
+        first = torch.argmax(logits, dim=-1)
+        self.logits.copy_(logits)
+        self.input_ids.copy_(first)
+        self.resid.copy_(self.w.embed[first])
+        self._set_scalars(T)
+        return first
+
     @torch.inference_mode()
-    def prefill(self, input_ids: torch.Tensor, offset: int | None = None, reset: bool = True) -> torch.Tensor:
+    def prefill(self, input_ids: torch.Tensor, offset: int | None = None, reset: bool = True,
+                chunk: int | None = None) -> torch.Tensor:
         """Eager prefill of ``input_ids`` ``[batch, T]`` at positions
         [offset, offset + T); returns the first greedy token ``[batch]`` (also
         left in ``input_ids``, src/nova/decode.py:224-297).
@@ -373,9 +454,24 @@ class NovaDecoder:
         new tokens attend to the staged fp16 K/V of those positions, as the
         reference's staged prefill does, and the int8 cache is re-quantized
         over all of them.  The staged fp16 K/V is kept until ``capture()``
-        (or ``release_staging()``)."""
+        (or ``release_staging()``).
+
+        ``chunk`` (a multiple of 64, with ``reset=True``): prefill straight into
+        the int8 cache chunk by chunk, later chunks attending to the int8 prefix
+        (see ``_prefill_chunked``); a prompt no longer than ``chunk`` takes the
+        path above unchanged."""
         cfg, cache = self.cfg, self.cache
         B, T = input_ids.shape
+        if chunk is not None and T > int(chunk):
+            chunk = int(chunk)
+            if chunk < GROUP_T or chunk % GROUP_T or not reset or offset:
+                raise ValueError("chunked prefill needs a chunk that is a multiple of 64, from position 0")
+            if B != self.batch or T >= self.max_len:
+                raise ValueError(f"prompt shape {tuple(input_ids.shape)} does not fit batch={self.batch}, "
+                                 f"max_len={self.max_len}")
+            cache.reset()
+            self._staged = None
+            return self._prefill_chunked(input_ids, chunk)
         if reset:
             cache.reset()
             self._staged = None

@@ -122,6 +122,62 @@ class OracleDecoder:
         self.pos = pos + 1
         return logits, np.argmax(logits.astype(np.float32), axis=-1)
 
+    def prefill_chunked(self, ids: np.ndarray, chunk: int):
+        """Prefill straight into the int8 cache in chunks of ``chunk`` tokens
+        (a multiple of 64; reports/kv-int8-streaming-cache.md section 5.1 of
+        the reference): each chunk attends to the int8 prefix of the earlier
+        chunks, dequantized (src/nova/kvquant.py:166-176), and to its own fp16
+        K/V, causally; its complete groups are quantized (token axis, 64-token
+        groups) once the layer is done; the prompt's last <= 64 tokens go into
+        the ring.  Returns (last-position logits, first greedy token)."""
+        ids = np.asarray(ids)
+        B, T = ids.shape
+        hq, hkv, d = self.hq, self.hkv, self.d
+        take0 = T - min(T, GT)
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            n = c1 - c0
+            cos, sin = rope_cos_sin(np.arange(c0, c1), d, self.theta)
+            h = np.asarray(self.W["embed"])[ids[:, c0:c1]]
+            for li, lw in enumerate(self.W["layers"]):
+                x = rms_norm(h, lw["input_ln"], self.eps)
+                qkv = self._lin(x, ("qkv", li), lw["qkv"])
+                q = rms_norm(qkv[..., :hq * d].reshape(B, n, hq, d), lw["q_norm"], self.eps)
+                k = rms_norm(qkv[..., hq * d:(hq + hkv) * d].reshape(B, n, hkv, d), lw["k_norm"], self.eps)
+                v = qkv[..., (hq + hkv) * d:].reshape(B, n, hkv, d)
+                q = apply_rope(q, cos[None, :, None], sin[None, :, None]).transpose(0, 2, 1, 3)
+                k = apply_rope(k, cos[None, :, None], sin[None, :, None]).transpose(0, 2, 1, 3)
+                v = v.transpose(0, 2, 1, 3)
+                K, V = k, v
+                if c0:
+                    g0 = c0 // GT
+                    pk = okv.dequantize_int8_token(self.kq[li][:, :, :c0], self.kmn[li][:, :, :g0],
+                                                   self.kst[li][:, :, :g0], GT)
+                    pv = okv.dequantize_int8_token(self.vq[li][:, :, :c0], self.vmn[li][:, :, :g0],
+                                                   self.vst[li][:, :, :g0], GT)
+                    K, V = np.concatenate([pk, k], axis=2), np.concatenate([pv, v], axis=2)
+                o = np.empty((B, n, hq * d), np.float16)
+                for t in range(n):
+                    ot, _ = attend(q[:, :, t], K[:, :, :c0 + t + 1], V[:, :, :c0 + t + 1])
+                    o[:, t] = ot.reshape(B, hq * d)
+                h = _f16(h.astype(np.float32) + self._lin(o, ("o", li), lw["o"]).astype(np.float32))
+                h = _f16(h.astype(np.float32) + self._mlp(li, lw, h).astype(np.float32))
+                full = n // GT * GT
+                if full:
+                    for src, codes, mn, st in ((k, self.kq[li], self.kmn[li], self.kst[li]),
+                                               (v, self.vq[li], self.vmn[li], self.vst[li])):
+                        c, m, s_ = okv.quantize_int8_token(np.ascontiguousarray(src[:, :, :full]), GT)
+                        codes[:, :, c0:c0 + full] = c
+                        mn[:, :, c0 // GT:(c0 + full) // GT] = m
+                        st[:, :, c0 // GT:(c0 + full) // GT] = s_
+                for p in range(max(c0, take0), c1):
+                    self.tail_k[li][:, :, p % GT] = k[:, :, p - c0]
+                    self.tail_v[li][:, :, p % GT] = v[:, :, p - c0]
+        x = rms_norm(h[:, -1], self.W["final_norm"], self.eps)
+        logits = self._lin(x, ("lm_head", -1), self.W["lm_head"])
+        self.pos = T
+        return logits, np.argmax(logits.astype(np.float32), axis=-1)
+
     def prefill(self, ids: np.ndarray):
         """Causal prefill over fp16 K/V from position 0; fills the int8 cache
         and the ring; returns (last-position logits, first greedy token)."""
