@@ -342,6 +342,22 @@ typedef struct nova_qk_args {
 NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
 
 /*
+ * nova_qk_norm_rope_append followed by nova_attn_decode_int8, in one launch
+ * (the decode step's q/k norm + RoPE + ring append and the fused attention of
+ * src/nova/decode.py:207-220 / src/nova/kvattn.py:447-482).  attn describes
+ * the attention as for nova_attn_decode_int8 except that attn->q, qlen, pg
+ * and written are not read: q is normalised and rotated from qk->qkv, and the
+ * lengths follow from *qk->pos (written = pos + 1, qlen = written rounded down
+ * to 64, pg = qlen / 64; stored to qk->written / qlen / pg for later readers).
+ * Both structs must name the same ring and int8 cache, batch, heads and
+ * max_len; attn needs the ring (tail_k/tail_v) and n_splits >= 1.  When the
+ * new token completes a 64-token group, the group is requantized into the
+ * cache and attended in its int8 form, as after the two separate calls.
+ * qk->q_out is not written.
+ */
+NOVA_API int nova_qk_append_attn_int8(const nova_qk_args* qk, const nova_attn_int8_args* attn, void* stream);
+
+/*
  * The decoder's q|k|v projection and q/k norm + RoPE + int8 KV append in one
  * launch: gemv describes the NF4 GEMV of the concatenated q|k|v weight
  * (native layout, N = (q_heads + 2*kv_heads) * 128, optional RMSNorm

@@ -137,6 +137,7 @@ _SIGNATURES: dict[str, list] = {
     "nova_qkv_norm_rope_append": [ctypes.POINTER(NF4Args), ctypes.POINTER(QKArgs), _P],
     "nova_fused_phases": [ctypes.POINTER(FusedArgs), _P],
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
+    "nova_qk_append_attn_int8": [ctypes.POINTER(QKArgs), ctypes.POINTER(AttnArgs), _P],
     "nova_sample_topk": [ctypes.POINTER(SampleArgs), _P],
 }
 _STRING_FNS = ("nova_version", "nova_last_error")

@@ -28,6 +28,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "qk_common.cuh"
 
 namespace nova {
 namespace attn {
@@ -58,6 +59,8 @@ struct Params {
     int64_t o_b, o_h;
     float* lse;
     int64_t lse_b;
+    const uint8_t* kq;        // code rows (L2 prefetch only; the loads go through the tensor maps)
+    const uint8_t* vq;
     const int64_t* qlen;
     const int64_t* pg;
     const int64_t* written;
@@ -66,7 +69,31 @@ struct Params {
     unsigned* counters;
     float* part;
     int kv_heads, gq, max_len, groups, chunk, n_splits, s_total, window;
+    int prefetch_first;       // one-wave launches: each warp's first group is prefetched into L2 before the wait
     float scale_log2;
+    // Fused q/k norm + RoPE + ring append (the FUSED kernel only; the
+    // standalone kernel's job, src/nova/layers.py:24-36 + kvattn.py append):
+    // q comes from the raw q|k|v row instead of `q`, the lengths from `pos`.
+    const __half* qkv;        // fp16 [batch, (q_heads + 2 kv_heads) * 128]
+    int64_t qkv_b;
+    const __half* q_norm_w;
+    const __half* k_norm_w;
+    const __half* cos;
+    const __half* sin;
+    int64_t rope_len;
+    const int64_t* pos;
+    int64_t* written_out;
+    int64_t* qlen_out;
+    int64_t* pg_out;
+    __half* ring_k;           // the tail ring and int8 cache above, writable
+    __half* ring_v;
+    uint8_t* kq_w;
+    uint8_t* vq_w;
+    __half* kmn_w;
+    __half* kst_w;
+    __half* vmn_w;
+    __half* vst_w;
+    float eps;
 };
 
 __device__ __forceinline__ float warp_max_g(float v) {  // across the 8 lanes sharing lane&3
@@ -145,6 +172,26 @@ __device__ __forceinline__ void issue_group(const Params& p, const CUtensorMap* 
     bulk_g2s(stage + SC_OFF + 256, p.kmn + so, 256, bar);
     bulk_g2s(stage + SC_OFF + 512, p.vst + so, 256, bar);
     bulk_g2s(stage + SC_OFF + 768, p.vmn + so, 256, bar);
+}
+
+// L2 prefetch of scale group `grp` of head row `bh` (K and V code rows, the
+// four scale vectors).  A hint, safe before the dependency wait: L2 is the
+// point of coherence, so a later write to these lines is what a later load
+// sees.  One lane.
+__device__ __forceinline__ void prefetch_group_l2(const Params& p, int64_t bh, int grp) {
+    const int64_t row = bh * p.max_len + int64_t(grp) * GT;
+    const uint32_t bytes = uint32_t(min(GT, p.max_len - grp * GT)) * D;   // ragged last group
+    const int64_t so = (bh * p.groups + grp) * D;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.kq + row * D), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.vq + row * D), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(p.kst + so) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(p.kmn + so) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(p.vst + so) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(p.vmn + so) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr) : "memory");
 }
 
 // One 64-token int8 group held in `stage`; tokens outside [lo, hi) are masked.
@@ -290,6 +337,13 @@ __device__ __forceinline__ void process_tail_tile(const Params& p, int64_t bh, i
     }
 }
 
+// FUSED: the q/k norm + RoPE + ring append of this step runs in the
+// prologue.  Every CTA normalises and rotates its q heads; the ring CTA of
+// each (batch row, KV head) also does K, writes the ring slot and, when the
+// slot completes a group, requantizes the group into the int8 cache and
+// attends it from its own shared memory (the prefix splits stop before it,
+// so no CTA reads a group while it is written).
+template <bool FUSED>
 __global__ void __launch_bounds__(THREADS, 3)
     attn_decode_int8_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV) {
@@ -302,21 +356,39 @@ __global__ void __launch_bounds__(THREADS, 3)
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int64_t bh = int64_t(b) * p.kv_heads + h;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const bool is_tail = split == p.n_splits;
     if (threadIdx.x == 0) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
     }
-    pdl_trigger();
-    pdl_wait();   // q, the cache and the lengths come from the previous kernels
-
-    // Speculative first load, issued before the lengths are read: the group
-    // this warp takes first when no prefix is masked (every group of the
-    // chunk lies inside the cache allocation, so the copy is always in bounds).
-    uint8_t* stage = smem + warp * STAGE;
-    uint64_t* bar = &bars[warp];
+    // The group this warp takes first when no prefix is masked (every group
+    // of the chunk lies inside the cache allocation, so a copy is in bounds).
     const int spec = int(int64_t(split) * p.chunk / GT) + warp;
     const bool spec_on = split < p.n_splits && spec < p.groups &&
                          int64_t(spec) * GT < int64_t(split) * p.chunk + p.chunk;
+    __half nwq = __float2half_rn(0.f), nwk = __float2half_rn(0.f);
+    if (FUSED) {   // weights: read before the dependency wait
+        nwq = p.q_norm_w[threadIdx.x];
+        if (is_tail) nwk = p.k_norm_w[threadIdx.x];
+        if (threadIdx.x == 32) {
+            // The position read here may be stale (the wait has not happened);
+            // it only picks the RoPE rows to prefetch.
+            const int64_t pg = *reinterpret_cast<const volatile int64_t*>(p.pos);
+            const int64_t cp = pg < 0 ? 0 : (pg < p.rope_len ? pg : p.rope_len - 1);
+            prefetch_l2(p.cos + cp * D);
+            prefetch_l2(p.cos + cp * D + 64);
+            prefetch_l2(p.sin + cp * D);
+            prefetch_l2(p.sin + cp * D + 64);
+        }
+    }
+    if (threadIdx.x == 64 && p.first) prefetch_l2(p.first);
+    if (p.prefetch_first && spec_on && lane == 0) prefetch_group_l2(p, bh, spec);
+    pdl_trigger();
+    pdl_wait();   // q, the cache and the lengths come from the previous kernels
+
+    // Speculative first load, issued before the lengths are read.
+    uint8_t* stage = smem + warp * STAGE;
+    uint64_t* bar = &bars[warp];
     if (lane == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
@@ -326,17 +398,104 @@ __global__ void __launch_bounds__(THREADS, 3)
     uint32_t phase = 0;        // completed waits on bar
     bool pending = spec_on;    // a copy is in flight on bar
 
-    const int64_t qlen = *p.qlen, pgv = *p.pg;
-    const int64_t written = p.written ? *p.written : qlen;
+    int64_t qlen, pgv, written, pos = 0;
+    bool requant = false;   // FUSED: this step's token completes group pos / 64
+    if (FUSED) {
+        pos = *p.pos;
+        written = pos + 1;
+        qlen = (written / GT) * GT;
+        pgv = qlen / GT;
+        requant = pos >= 0 && pos < p.max_len && pos % GT == GT - 1;
+    } else {
+        qlen = *p.qlen;
+        pgv = *p.pg;
+        written = p.written ? *p.written : qlen;
+    }
     const int64_t first = p.first ? *p.first : 0;
     const int64_t u = written - 1;
     int64_t lo = first > 0 ? first : 0;
     if (p.window > 0) lo = max(lo, u - p.window + 1);
-    const int64_t pend = min(min(qlen, pgv * GT), int64_t(p.max_len));
+    const int64_t pend = min(min(requant ? qlen - GT : qlen, pgv * GT), int64_t(p.max_len));
 
     // Q^T B-fragments: column g carries head g>>1; dims 32t..32t+31.
     uint32_t qf[16];
-    {
+    if (FUSED) {
+        // scratch in the last KiB of stages 0-2, which no group copy writes
+        // (TX_BYTES of each stage are used); no longer needed once qf is built
+        auto qemb = reinterpret_cast<__half(*)[D]>(smem + TX_BYTES);                // [MAX_GQ][D]
+        auto qbuf = reinterpret_cast<__half(*)[D]>(smem + STAGE + TX_BYTES);        // [MAX_GQ][D]
+        auto qred = reinterpret_cast<float(*)[MAX_GQ]>(smem + 2 * STAGE + TX_BYTES);  // [NW][MAX_GQ]
+        auto kred = reinterpret_cast<float(*)[1]>(smem + 2 * STAGE + TX_BYTES + 64);  // [NW][1]
+        auto kbuf = reinterpret_cast<__half(*)[D]>(smem + 2 * STAGE + TX_BYTES + 128);  // [1][D]
+        static_assert(TX_BYTES % 16 == 0 && STAGE - TX_BYTES >= MAX_GQ * D * 2 && 128 + D * 2 <= STAGE - TX_BYTES,
+                      "prologue scratch must fit in the unused stage tails");
+        const int d = threadIdx.x;
+        const __half* row = p.qkv + b * p.qkv_b;
+        const int hq_all = p.kv_heads * p.gq;
+        __half xq[MAX_GQ];
+#pragma unroll
+        for (int hh = 0; hh < MAX_GQ; ++hh)
+            xq[hh] = hh < p.gq ? row[int64_t(h * p.gq + hh) * D + d] : __float2half_rn(0.f);
+        __half xk[1] = {__float2half_rn(0.f)}, xv = __float2half_rn(0.f);
+        if (is_tail) {
+            xk[0] = row[int64_t(hq_all + h) * D + d];
+            xv = row[int64_t(hq_all + p.kv_heads + h) * D + d];
+        }
+        const int64_t cp = pos < 0 ? 0 : (pos < p.rope_len ? pos : p.rope_len - 1);
+        const float c = __half2float(p.cos[cp * D + d]), sn = __half2float(p.sin[cp * D + d]);
+        __half eq[MAX_GQ];
+        qk::norm_rope<MAX_GQ>(xq, nwq, c, sn, p.eps, qred, qbuf, eq);
+#pragma unroll
+        for (int hh = 0; hh < MAX_GQ; ++hh) qemb[hh][d] = eq[hh];
+        if (is_tail) {   // uniform per CTA: norm_rope synchronises the CTA
+            __half ek[1];
+            qk::norm_rope<1>(xk, nwk, c, sn, p.eps, kred, kbuf, ek);
+            if (b == 0 && h == 0 && d == 0) {   // the lengths, for later readers (nothing in this launch reads them)
+                *p.written_out = written;
+                *p.qlen_out = qlen;
+                *p.pg_out = pgv;
+            }
+            if (pos >= 0 && pos < p.max_len) {
+                const int slot = int(pos % GT);
+                __half* tk = p.ring_k + bh * GT * D;
+                __half* tv = p.ring_v + bh * GT * D;
+                tk[slot * D + d] = ek[0];
+                tv[slot * D + d] = xv;
+                if (requant) {   // the group into the cache, and into stage 0 the way a TMA copy lays it out
+                    const int64_t gidx = pos / GT;
+                    const int64_t code_off = bh * p.max_len * D + gidx * GT * D + d;
+                    const int64_t sc_off = (bh * p.groups + gidx) * D + d;
+                    uint8_t* st = smem;
+                    auto at = [d](int tt) { return tt * 128 + ((((d >> 4) ^ (tt & 7))) << 4) + (d & 15); };
+                    qk::quant_col(tk + d, p.kmn_w + sc_off, p.kst_w + sc_off, [&](int tt, uint8_t c8) {
+                        p.kq_w[code_off + int64_t(tt) * D] = c8;
+                        st[at(tt)] = c8;
+                    });
+                    qk::quant_col(tv + d, p.vmn_w + sc_off, p.vst_w + sc_off, [&](int tt, uint8_t c8) {
+                        p.vq_w[code_off + int64_t(tt) * D] = c8;
+                        st[8192 + at(tt)] = c8;
+                    });
+                    __half* scs = reinterpret_cast<__half*>(smem + SC_OFF);   // kst, kmn, vst, vmn
+                    scs[d] = p.kst_w[sc_off];
+                    scs[D + d] = p.kmn_w[sc_off];
+                    scs[2 * D + d] = p.vst_w[sc_off];
+                    scs[3 * D + d] = p.vmn_w[sc_off];
+                }
+            }
+        }
+        __syncthreads();   // qemb, the ring slot and stage 0 are complete
+        const int hq = g >> 1;
+        if (hq < p.gq) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 v = *reinterpret_cast<const uint4*>(&qemb[hq][32 * t + 8 * i]);
+                qf[4 * i] = v.x; qf[4 * i + 1] = v.y; qf[4 * i + 2] = v.z; qf[4 * i + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) qf[i] = 0u;
+        }
+    } else {
         const int hq = g >> 1;
         if (hq < p.gq) {
             const __half* qp = p.q + b * p.q_b + int64_t(h * p.gq + hq) * p.q_h + 32 * t;
@@ -399,6 +558,9 @@ __global__ void __launch_bounds__(THREADS, 3)
     } else {
         int64_t tlo = max(lo, qlen);
         process_tail_tile(p, bh, warp, u, tlo, qf, acc, m_run, l_run, g, t);
+        if (FUSED && requant && warp == 0)   // the group this step completed, from stage 0
+            process_group(smem, int(qlen - GT), int(max(lo, qlen - GT)), int(qlen), qf, p.scale_log2, acc, m_run,
+                          l_run, g, t);
     }
 
     // ---- merge the 4 warps of this CTA
@@ -575,7 +737,10 @@ extern "C" int nova_attn_read_error(void* workspace, int64_t, int64_t, int* host
     return NOVA_OK;
 }
 
-extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream) {
+// Shared by nova_attn_decode_int8 (qk == nullptr) and
+// nova_qk_append_attn_int8 (qk: the fused q/k norm + RoPE + append, checked
+// by the caller against `a`).
+static int attn_launch(const nova_attn_int8_args* a, const nova_qk_args* qk, void* stream) {
     using namespace nova::attn;
     if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
     if (a->head_dim != D) return fail(NOVA_ERR_UNSUPPORTED, "head_dim must be 128, got %lld", (long long)a->head_dim);
@@ -593,7 +758,7 @@ extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream)
         return fail(NOVA_ERR_INVALID, "grid too large");
     if ((a->n_splits + 1) * gq > NW * STAGE / 8)
         return fail(NOVA_ERR_UNSUPPORTED, "n_splits * q_heads/kv_heads must be at most %d", NW * STAGE / 8 - gq);
-    if (!a->q || !a->out || !a->qlen || !a->pg || !a->workspace)
+    if ((!qk && (!a->q || !a->qlen || !a->pg)) || !a->out || !a->workspace)
         return fail(NOVA_ERR_INVALID, "q/out/qlen/pg/workspace must not be NULL");
     if (a->n_splits && (!a->kq || !a->vq || !a->kmn || !a->kst || !a->vmn || !a->vst))
         return fail(NOVA_ERR_INVALID, "int8 buffers must not be NULL");
@@ -658,22 +823,83 @@ extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream)
     p.s_total = int(s_total);
     p.window = int(std::min<int64_t>(a->window, 0x7fffffff));
     p.scale_log2 = float(1.0 / sqrt(double(D))) * LOG2E;
+    p.kq = (const uint8_t*)a->kq;
+    p.vq = (const uint8_t*)a->vq;
+    // every CTA resident at once (3 per SM): the first groups can be prefetched while the previous kernel ends
+    p.prefetch_first = (a->n_splits > 0 && s_total * a->kv_heads * a->batch <= 3 * int64_t(sm_count())) ? 1 : 0;
+    p.qkv = nullptr;
+    p.qkv_b = 0;
+    p.q_norm_w = p.k_norm_w = p.cos = p.sin = nullptr;
+    p.rope_len = 0;
+    p.pos = nullptr;
+    p.written_out = p.qlen_out = p.pg_out = nullptr;
+    p.ring_k = p.ring_v = nullptr;
+    p.kq_w = p.vq_w = nullptr;
+    p.kmn_w = p.kst_w = p.vmn_w = p.vst_w = nullptr;
+    p.eps = 0.f;
+    if (qk) {
+        p.qkv = (const __half*)qk->qkv;
+        p.qkv_b = qk->qkv_stride;
+        p.q_norm_w = (const __half*)qk->q_norm_weight;
+        p.k_norm_w = (const __half*)qk->k_norm_weight;
+        p.cos = (const __half*)qk->cos;
+        p.sin = (const __half*)qk->sin;
+        p.rope_len = qk->rope_len;
+        p.pos = qk->pos;
+        p.written_out = qk->written;
+        p.qlen_out = qk->qlen;
+        p.pg_out = qk->pg;
+        p.ring_k = (__half*)qk->tail_k;
+        p.ring_v = (__half*)qk->tail_v;
+        p.kq_w = (uint8_t*)qk->kq;
+        p.vq_w = (uint8_t*)qk->vq;
+        p.kmn_w = (__half*)qk->kmn;
+        p.kst_w = (__half*)qk->kst;
+        p.vmn_w = (__half*)qk->vmn;
+        p.vst_w = (__half*)qk->vst;
+        p.eps = float(qk->eps);
+    }
 
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(attn_decode_int8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess) {
+    using Kern = void (*)(Params, CUtensorMap, CUtensorMap);
+    Kern kern = qk ? attn_decode_int8_kernel<true> : attn_decode_int8_kernel<false>;
+    static bool attr_set[2] = {false, false};
+    if (!attr_set[qk ? 1 : 0]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
             cudaGetLastError();
             return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
         }
-        attr_set = true;
+        attr_set[qk ? 1 : 0] = true;
     }
     dim3 grid(unsigned(s_total), unsigned(a->kv_heads), unsigned(a->batch));
-    const cudaError_t err =
-        launch(attn_decode_int8_kernel, grid, dim3(THREADS), size_t(SMEM_BYTES), (cudaStream_t)stream, p, tmK, tmV);
+    const cudaError_t err = launch(kern, grid, dim3(THREADS), size_t(SMEM_BYTES), (cudaStream_t)stream, p, tmK, tmV);
     if (err != cudaSuccess) {
         cudaGetLastError();
-        return fail(NOVA_ERR_CUDA, "nova_attn_decode_int8: launch failed: %s", cudaGetErrorString(err));
+        return fail(NOVA_ERR_CUDA, "%s: launch failed: %s", qk ? "nova_qk_append_attn_int8" : "nova_attn_decode_int8",
+                    cudaGetErrorString(err));
     }
     return NOVA_OK;
+}
+
+extern "C" int nova_attn_decode_int8(const nova_attn_int8_args* a, void* stream) {
+    return attn_launch(a, nullptr, stream);
+}
+
+extern "C" int nova_qk_append_attn_int8(const nova_qk_args* qk, const nova_attn_int8_args* a, void* stream) {
+    if (!qk || !a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
+    if (qk->head_dim != 128 || qk->group != 64) return fail(NOVA_ERR_UNSUPPORTED, "head_dim must be 128 and group 64");
+    if (qk->batch != a->batch || qk->q_heads != a->q_heads || qk->kv_heads != a->kv_heads ||
+        qk->max_len != a->max_len)
+        return fail(NOVA_ERR_INVALID, "q/k args and attention args disagree on batch/heads/max_len");
+    if (!a->tail_k || a->n_splits < 1)
+        return fail(NOVA_ERR_INVALID, "the fused append needs the fp16 tail ring and at least one int8 split");
+    if (qk->tail_k != a->tail_k || qk->tail_v != a->tail_v || qk->kq != a->kq || qk->vq != a->vq ||
+        qk->kmn != a->kmn || qk->kst != a->kst || qk->vmn != a->vmn || qk->vst != a->vst)
+        return fail(NOVA_ERR_INVALID, "q/k args and attention args must name the same ring and int8 cache");
+    if (!qk->qkv || !qk->q_norm_weight || !qk->k_norm_weight || !qk->cos || !qk->sin || !qk->pos || !qk->written ||
+        !qk->qlen || !qk->pg)
+        return fail(NOVA_ERR_INVALID, "NULL pointer");
+    if (qk->rope_len <= 0) return fail(NOVA_ERR_INVALID, "bad rope_len");
+    if (qk->qkv_stride < (qk->q_heads + 2 * qk->kv_heads) * 128)
+        return fail(NOVA_ERR_INVALID, "qkv_stride shorter than a q|k|v row");
+    return attn_launch(a, qk, stream);
 }

@@ -104,6 +104,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// SMs of the current device (148 when the query fails).
+static inline int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 148;
+    }
+    return n;
+}
+
 // Bounded wait: every spin in this library gives up after kWaitNs of wall
 // time (a try_wait may itself suspend for a system-dependent while, so the
 // bound is on the clock, not on the number of polls), records `code` in the

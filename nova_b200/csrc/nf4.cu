@@ -2174,19 +2174,6 @@ __global__ void nf4_pack_native_kernel(const uint8_t* __restrict__ packed, const
 using namespace nova;
 using namespace nova::nf4;
 
-static int sm_count() {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) {
-        cudaGetLastError();
-        return 148;
-    }
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
-        cudaGetLastError();
-        return 148;
-    }
-    return n;
-}
-
 // Workspace layout: [partial slots of every warp of the persistent grid |
 // per-row-tile arrival counters + the finalize counter].  The partial region
 // has the same size for every N (it is sized for the largest grid either

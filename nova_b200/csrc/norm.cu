@@ -8,6 +8,7 @@
 // (src/nova/layers.py:24-36) = fp16(fp16(x*cos) + fp16(rotate_half(x)*sin))
 // with the fp16 cos/sin table the HF rotary produces.
 #include "common.cuh"
+#include "qk_common.cuh"
 
 namespace nova {
 namespace norm {
@@ -77,26 +78,8 @@ __global__ void residual_add_f32_kernel(const float* __restrict__ x, int64_t xs,
 // K, both K and V into ring slot pos % 64; when that slot completes the group,
 // the ring is requantized into the int8 cache (each thread its own column).
 
-constexpr int D = 128;
-constexpr int GT = 64;
-
-__device__ __forceinline__ void quant_col(const __half* src, uint8_t* q, __half* mn_out, __half* st_out) {
-    float mn = INFINITY, mx = -INFINITY;
-    for (int t = 0; t < GT; ++t) {
-        const float v = __half2float(src[t * D]);
-        mn = fminf(mn, v);
-        mx = fmaxf(mx, v);
-    }
-    const float step = fmaxf(__fdiv_rn(mx - mn, 255.0f), 1e-8f);
-    for (int t = 0; t < GT; ++t) {
-        const float v = __half2float(src[t * D]);
-        float c = rintf(__fdiv_rn(v - mn, step));
-        c = fminf(fmaxf(c, 0.0f), 255.0f);
-        q[t * D] = static_cast<uint8_t>(c);
-    }
-    *mn_out = __float2half_rn(mn);
-    *st_out = __float2half_rn(step);
-}
+constexpr int D = qk::D;
+constexpr int GT = qk::GT;
 
 struct QKParams {
     const __half* qkv;
@@ -126,8 +109,8 @@ struct QKParams {
 };
 
 __global__ void __launch_bounds__(D) qk_norm_rope_append_kernel(const __grid_constant__ QKParams p) {
-    __shared__ float red[D / 32];
-    __shared__ __half ybuf[D];
+    __shared__ float red[D / 32][1];
+    __shared__ __half ybuf[1][D];
     const int m = blockIdx.y;
     const int head = blockIdx.x;
     const int d = threadIdx.x;
@@ -146,21 +129,13 @@ __global__ void __launch_bounds__(D) qk_norm_rope_append_kernel(const __grid_con
     const __half* src = p.qkv + m * p.qkv_stride + int64_t(head) * D;
     const __half* nw = is_q ? p.q_norm_w : p.k_norm_w;
 
-    // per-head RMSNorm
-    const float x = __half2float(src[d]);
-    const float total = block_sum<D>(x * x, red);
-    const float r = rsqrt_ieee(__fdiv_rn(total, float(D)) + p.eps);
-    const float hn = __half2float(__float2half_rn(x * r));
-    const __half y = __float2half_rn(__half2float(nw[d]) * hn);
-    ybuf[d] = y;
-    __syncthreads();
-    // RoPE: rotate_half(y)[d] = -y[d + 64] (d < 64) or y[d - 64]
-    const float yr = d < D / 2 ? -__half2float(ybuf[d + D / 2]) : __half2float(ybuf[d - D / 2]);
-    const int64_t cp = pos < p.rope_len ? pos : p.rope_len - 1;
+    // per-head RMSNorm + RoPE
+    const __half xin[1] = {src[d]};
+    const int64_t cp = pos < 0 ? 0 : (pos < p.rope_len ? pos : p.rope_len - 1);
     const float c = __half2float(p.cos[cp * D + d]), s = __half2float(p.sin[cp * D + d]);
-    const float a = __half2float(__float2half_rn(__half2float(y) * c));
-    const float b = __half2float(__float2half_rn(yr * s));
-    const __half emb = __float2half_rn(a + b);
+    __half embv[1];
+    qk::norm_rope<1>(xin, nw[d], c, s, p.eps, red, ybuf, embv);
+    const __half emb = embv[0];
 
     if (is_q) {
         p.q_out[m * p.q_out_stride + int64_t(head) * D + d] = emb;
@@ -179,8 +154,8 @@ __global__ void __launch_bounds__(D) qk_norm_rope_append_kernel(const __grid_con
     const int64_t ngroups = (p.max_len + GT - 1) / GT;
     const int64_t code_off = bh * p.max_len * D + g * GT * D + d;
     const int64_t sc_off = (bh * ngroups + g) * D + d;
-    quant_col(tk + d, p.kq + code_off, p.kmn + sc_off, p.kst + sc_off);
-    quant_col(tv + d, p.vq + code_off, p.vmn + sc_off, p.vst + sc_off);
+    qk::quant_col(tk + d, p.kmn + sc_off, p.kst + sc_off, [&](int t, uint8_t c8) { p.kq[code_off + t * D] = c8; });
+    qk::quant_col(tv + d, p.vmn + sc_off, p.vst + sc_off, [&](int t, uint8_t c8) { p.vq[code_off + t * D] = c8; });
 }
 
 }  // namespace norm

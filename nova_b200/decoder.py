@@ -5,17 +5,20 @@ This is the B200 counterpart of the reference's graph-decode path:
 ``GraphDecoder`` (src/nova/decode.py:87-526) driving ``NovaTextModel`` /
 ``LeanDecoderLayer`` (src/nova/model.py:115-204, src/nova/layers.py:99-218)
 with ``KVInt8Cache`` (src/nova/kvattn.py:488-880) and NF4 linears
-(src/nova/quant.py).  One decode step is 6 kernel launches per layer plus
+(src/nova/quant.py).  One decode step is 5 kernel launches per layer plus
 one for the lm_head:
 
     1. nova_nf4_gemv      input_layernorm (prologue) + fused q|k|v projection
-    2. nova_qk_norm_rope_append   q_norm/k_norm, RoPE, ring write, group requant
-    3. nova_attn_decode_int8      int8 prefix + fp16 ring, split-K, merged
-    4. nova_nf4_gemv      o_proj + residual add (epilogue, in place)
-    5. nova_nf4_gemv      post_attention_layernorm (prologue) + gate|up + SiLU*up
-    6. nova_nf4_gemv      down_proj + residual add
+    2. nova_qk_append_attn_int8   q_norm/k_norm, RoPE, ring write, group requant
+                          (prologue), then int8 prefix + fp16 ring attention,
+                          split-K, merged
+    3. nova_nf4_gemv      o_proj + residual add (epilogue, in place)
+    4. nova_nf4_gemv      post_attention_layernorm (prologue) + gate|up + SiLU*up
+    5. nova_nf4_gemv      down_proj + residual add
 
-(``qkv_fused=True`` merges 1 and 2 into nova_qkv_norm_rope_append.)
+(``attn_fused=False`` runs step 2 as nova_qk_norm_rope_append followed by
+nova_attn_decode_int8; ``qkv_fused=True`` merges 1 with the q/k part into
+nova_qkv_norm_rope_append, then the attention alone.)
     final: nova_nf4_gemv  final norm (prologue) + 4-bit lm_head + greedy argmax
            + input_ids / pos update + next-token embedding gather (last warp)
 
@@ -228,7 +231,7 @@ class NovaDecoder:
 
     def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
                  device="cuda", pdl: bool = True, tp: TPContext | None = None, fused: bool | None = None,
-                 qkv_fused: bool = False) -> None:
+                 qkv_fused: bool = False, attn_fused: bool = True) -> None:
         cfg = weights.cfg
         if batch < 1 or batch > MAX_BATCH:
             raise ValueError(f"the decode path handles batch 1..{MAX_BATCH}")
@@ -288,6 +291,9 @@ class NovaDecoder:
         # (batch <= 8).  Off by default: with 48 head-owning CTAs most SMs idle, and measured in the decode
         # step the two launches (q|k|v GEMV on every SM, then the q/k kernel) are faster.
         self.qkv_fused = bool(qkv_fused) and self.batch <= GEMV_ROWS
+        # attn_fused=True: the q/k norm + RoPE + ring append runs in the attention's prologue (one launch
+        # and one kernel boundary fewer per layer)
+        self.attn_fused = bool(attn_fused) and not self.qkv_fused
         self._staged = None   # fp16 K/V per layer of the positions prefilled / injected since the last reset
 
     def _pick_chunk(self) -> int:
@@ -728,11 +734,16 @@ class NovaDecoder:
                       self.resid.stride(0), B, cfg.hidden_size, stream)
 
         for li, lw in enumerate(self.w.layers):
-            self._qkv_step(li, lw)
+            qk = None
+            if self.attn_fused:
+                self._gemv(self.resid, lw.qkv, self.qkv, norm_weight=lw.input_ln)
+                qk = self._qk_args(li, lw)
+            else:
+                self._qkv_step(li, lw)
             launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
                                   cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
-                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window)
+                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window, qk=qk)
             row_parallel(self.attn, lw.o)
             self._gemv(self.resid, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln)
             row_parallel(self.act, lw.down)
@@ -777,6 +788,8 @@ class NovaDecoder:
             per_layer = 8          # 2 norms + 4 GEMMs + q/k norm-RoPE-append + attention
         else:
             per_layer = 6
+        if self.attn_fused:
+            per_layer -= 1       # the q/k norm-RoPE-append runs inside the attention launch
         if self.tp.active:
             per_layer += 2       # fused all-reduce + residual add (or the residual add after NCCL), twice
         return per_layer * self.cfg.num_hidden_layers + (2 if self.batch > GEMV_ROWS else 1)

@@ -101,8 +101,13 @@ def _check(x: torch.Tensor, name: str, dtype: torch.dtype) -> None:
 def launch_attention(q: torch.Tensor, kv: tuple | None, tail: tuple | None, out: torch.Tensor,
                      lse: torch.Tensor | None, qlen_t: torch.Tensor, pg_t: torch.Tensor,
                      written_t: torch.Tensor | None, first_t: torch.Tensor | None, workspace: torch.Tensor,
-                     *, max_len: int, n_splits: int, chunk: int = CHUNK, window: int = 0) -> None:
-    """Thin launcher for ``nova_attn_decode_int8``.
+                     *, max_len: int, n_splits: int, chunk: int = CHUNK, window: int = 0,
+                     qk: "_lib.QKArgs | None" = None) -> None:
+    """Thin launcher for ``nova_attn_decode_int8``; with ``qk`` (the
+    arguments of ``nova_qk_norm_rope_append`` for the same ring and cache) the
+    q/k norm + RoPE + ring append runs in the same launch
+    (``nova_qk_append_attn_int8``): ``q`` is then not read, and neither are
+    ``qlen_t`` / ``pg_t`` / ``written_t``.
 
     q: fp16 ``[B, Hq, D]`` view (strides are passed through; last dim
     contiguous); kv: ``(kq, kmn, kst, vq, vmn, vst)`` contiguous
@@ -134,6 +139,10 @@ def launch_attention(q: torch.Tensor, kv: tuple | None, tail: tuple | None, out:
     a.batch, a.q_heads, a.kv_heads = B, Hq, Hkv
     a.max_len, a.groups, a.head_dim, a.group = int(max_len), int(groups), D, GROUP_T
     a.chunk, a.n_splits, a.window = int(chunk), int(n_splits), int(window)
+    if qk is not None:
+        _lib.check(_lib.lib().nova_qk_append_attn_int8(_lib.ctypes.byref(qk), _lib.ctypes.byref(a),
+                                                       _lib.stream_of(q.device)), "nova_qk_append_attn_int8")
+        return
     _lib.check(_lib.lib().nova_attn_decode_int8(_lib.ctypes.byref(a), _lib.stream_of(q.device)),
                "nova_attn_decode_int8")
 
