@@ -40,6 +40,7 @@ constexpr int THREADS = NW * 32;
 constexpr int STAGE = 18432;      // K 8192 + V 8192 + 4 x 256 scales, rounded to 1 KiB
 constexpr int SC_OFF = 16384;     // kst, kmn, vst, vmn (256 B each)
 constexpr int TX_BYTES = 8192 + 8192 + 4 * 256;
+constexpr int TX_HALF = 8192 + 2 * 256;   // the K half (codes + kst, kmn) or the V half of a group
 constexpr int SMEM_BYTES = NW * STAGE + 1024;
 constexpr int PART = 132;         // floats per (split, head): m, l, pad, pad, acc[128]
 constexpr int MAX_GQ = 4;
@@ -160,18 +161,25 @@ __device__ __forceinline__ void softmax_update(float (&x)[N], float& m_run, floa
     m_run = m_new;
 }
 
-// Issue the loads of scale group `grp` of head row `bh` into `stage`.
-__device__ __forceinline__ void issue_group(const Params& p, const CUtensorMap* tmK, const CUtensorMap* tmV,
-                                            uint8_t* stage, uint64_t* bar, int64_t bh, int grp) {
-    mbar_arrive_expect_tx(bar, TX_BYTES);
-    const int row = int(bh * p.max_len + int64_t(grp) * GT);
-    tma_load_2d(stage, tmK, 0, row, bar);
-    tma_load_2d(stage + 8192, tmV, 0, row, bar);
+// Issue the loads of scale group `grp` of head row `bh` into `stage`: the K
+// half (codes at 0, kst and kmn at SC_OFF) completes on bar_k, the V half
+// (codes at 8192, vst and vmn at SC_OFF + 512) on bar_v, so that the next
+// group's K can load while this group's V is still being read and vice versa.
+__device__ __forceinline__ void issue_k(const Params& p, const CUtensorMap* tmK, uint8_t* stage, uint64_t* bar_k,
+                                        int64_t bh, int grp) {
+    mbar_arrive_expect_tx(bar_k, TX_HALF);
+    tma_load_2d(stage, tmK, 0, int(bh * p.max_len + int64_t(grp) * GT), bar_k);
     const int64_t so = (bh * p.groups + grp) * D;
-    bulk_g2s(stage + SC_OFF, p.kst + so, 256, bar);
-    bulk_g2s(stage + SC_OFF + 256, p.kmn + so, 256, bar);
-    bulk_g2s(stage + SC_OFF + 512, p.vst + so, 256, bar);
-    bulk_g2s(stage + SC_OFF + 768, p.vmn + so, 256, bar);
+    bulk_g2s(stage + SC_OFF, p.kst + so, 256, bar_k);
+    bulk_g2s(stage + SC_OFF + 256, p.kmn + so, 256, bar_k);
+}
+__device__ __forceinline__ void issue_v(const Params& p, const CUtensorMap* tmV, uint8_t* stage, uint64_t* bar_v,
+                                        int64_t bh, int grp) {
+    mbar_arrive_expect_tx(bar_v, TX_HALF);
+    tma_load_2d(stage + 8192, tmV, 0, int(bh * p.max_len + int64_t(grp) * GT), bar_v);
+    const int64_t so = (bh * p.groups + grp) * D;
+    bulk_g2s(stage + SC_OFF + 512, p.vst + so, 256, bar_v);
+    bulk_g2s(stage + SC_OFF + 768, p.vmn + so, 256, bar_v);
 }
 
 // L2 prefetch of scale group `grp` of head row `bh` (K and V code rows, the
@@ -194,12 +202,13 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr) : "memory");
 }
 
-// One 64-token int8 group held in `stage`; tokens outside [lo, hi) are masked.
-__device__ __forceinline__ void process_group(const uint8_t* stage, int gbase, int lo, int hi,
-                                              const uint32_t (&qf)[16], float scale_log2, float (&acc)[8][4],
-                                              float& m_run, float& l_run, int g, int t) {
+// One 64-token int8 group held in `stage`; tokens outside [lo, hi) are
+// masked.  qk_part: scores from the K half and the online-softmax update
+// (x = the group's probabilities); pv_part: O^T += V^T P^T from the V half.
+__device__ __forceinline__ void qk_part(const uint8_t* stage, int gbase, int lo, int hi, const uint32_t (&qf)[16],
+                                        float scale_log2, float (&acc)[8][4], float& m_run, float& l_run, int g,
+                                        int t, float (&x)[8]) {
     const uint8_t* Ks = stage;
-    const uint8_t* Vs = stage + 8192;
     const uint8_t* sc = stage + SC_OFF;
     // K scales for dims 32t..32t+31 (word w = dims 32t+2w, +1).
     uint32_t kst2[16], kmn2[16];
@@ -210,26 +219,8 @@ __device__ __forceinline__ void process_group(const uint8_t* stage, int gbase, i
         kst2[4 * i] = a.x; kst2[4 * i + 1] = a.y; kst2[4 * i + 2] = a.z; kst2[4 * i + 3] = a.w;
         kmn2[4 * i] = b.x; kmn2[4 * i + 1] = b.y; kmn2[4 * i + 2] = b.z; kmn2[4 * i + 3] = b.w;
     }
-    // V scales for dims 16g..16g+15, broadcast to both halves:
-    // index j -> dim 16g+2j (row g of m-tile j), dim 16g+2j+1 (row g+8).
-    uint32_t vsA[8], vsB[8], vmA[8], vmB[8];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        uint4 a = lds128(sc + 512 + 32 * g + 16 * i);
-        uint4 b = lds128(sc + 768 + 32 * g + 16 * i);
-        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int j = 4 * i + k;
-            vsA[j] = __byte_perm(aw[k], 0, 0x1010);
-            vsB[j] = __byte_perm(aw[k], 0, 0x3232);
-            vmA[j] = __byte_perm(bw[k], 0, 0x1010);
-            vmB[j] = __byte_perm(bw[k], 0, 0x3232);
-        }
-    }
 
     // ---- scores for the 4 tiles of 16 tokens
-    float x[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int r0 = 16 * i + g;
@@ -253,6 +244,28 @@ __device__ __forceinline__ void process_group(const uint8_t* stage, int gbase, i
         x[2 * i + 1] = (p1 >= lo && p1 < hi) ? c[2] * scale_log2 : -INFINITY;
     }
     softmax_update<8>(x, m_run, l_run, acc);
+}
+
+__device__ __forceinline__ void pv_part(const uint8_t* stage, const float (&x)[8], float (&acc)[8][4], int g, int t) {
+    const uint8_t* Vs = stage + 8192;
+    const uint8_t* sc = stage + SC_OFF;
+    // V scales for dims 16g..16g+15, broadcast to both halves:
+    // index j -> dim 16g+2j (row g of m-tile j), dim 16g+2j+1 (row g+8).
+    uint32_t vsA[8], vsB[8], vmA[8], vmB[8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        uint4 a = lds128(sc + 512 + 32 * g + 16 * i);
+        uint4 b = lds128(sc + 768 + 32 * g + 16 * i);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int j = 4 * i + k;
+            vsA[j] = __byte_perm(aw[k], 0, 0x1010);
+            vsB[j] = __byte_perm(aw[k], 0, 0x3232);
+            vmA[j] = __byte_perm(bw[k], 0, 0x1010);
+            vmB[j] = __byte_perm(bw[k], 0, 0x3232);
+        }
+    }
 
     // ---- O^T += V^T P^T, one 16-token tile at a time
 #pragma unroll
@@ -282,6 +295,14 @@ __device__ __forceinline__ void process_group(const uint8_t* stage, int gbase, i
                       hfma2(u8x2_hi_to_f16x2(cd23), vsB[j], vmB[j]), b0, b1);
         }
     }
+}
+
+__device__ __forceinline__ void process_group(const uint8_t* stage, int gbase, int lo, int hi,
+                                              const uint32_t (&qf)[16], float scale_log2, float (&acc)[8][4],
+                                              float& m_run, float& l_run, int g, int t) {
+    float x[8];
+    qk_part(stage, gbase, lo, hi, qf, scale_log2, acc, m_run, l_run, g, t, x);
+    pv_part(stage, x, acc, g, t);
 }
 
 __device__ __forceinline__ int64_t pos_mod(int64_t a, int m) {
@@ -349,7 +370,7 @@ __global__ void __launch_bounds__(THREADS, 3)
                             const __grid_constant__ CUtensorMap tmV) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t bars[NW];
+    __shared__ __align__(8) uint64_t bars[2][NW];   // per warp: K half, V half of its stage
     __shared__ float sm_m[NW][MAX_GQ], sm_l[NW][MAX_GQ];
     __shared__ int sm_last;
 
@@ -388,15 +409,20 @@ __global__ void __launch_bounds__(THREADS, 3)
 
     // Speculative first load, issued before the lengths are read.
     uint8_t* stage = smem + warp * STAGE;
-    uint64_t* bar = &bars[warp];
+    uint64_t* bar_k = &bars[0][warp];
+    uint64_t* bar_v = &bars[1][warp];
     if (lane == 0) {
-        mbar_init(bar, 1);
+        mbar_init(bar_k, 1);
+        mbar_init(bar_v, 1);
         fence_mbar_init();
-        if (spec_on) issue_group(p, &tmK, &tmV, stage, bar, bh, spec);
+        if (spec_on) {
+            issue_k(p, &tmK, stage, bar_k, bh, spec);
+            issue_v(p, &tmV, stage, bar_v, bh, spec);
+        }
     }
     __syncwarp();
-    uint32_t phase = 0;        // completed waits on bar
-    bool pending = spec_on;    // a copy is in flight on bar
+    uint32_t phase_k = 0, phase_v = 0;   // completed waits on bar_k / bar_v
+    bool pend_k = spec_on, pend_v = spec_on;   // a copy is in flight on bar_k / bar_v
 
     int64_t qlen, pgv, written, pos = 0;
     bool requant = false;   // FUSED: this step's token completes group pos / 64
@@ -524,37 +550,56 @@ __global__ void __launch_bounds__(THREADS, 3)
             const int g_first = int(t_begin / GT), g_last = int((t_end - 1) / GT);
             int gi = g_first + warp;
             if (gi <= g_last) {
-                if (!(pending && spec == gi)) {   // masked prefix: drain the speculative copy, load gi
-                    if (pending) {
-                        mbar_wait(bar, phase & 1u, p.err, 1);
-                        ++phase;
+                if (!(pend_k && spec == gi)) {   // masked prefix: drain the speculative copy, load gi
+                    if (pend_k) {
+                        mbar_wait(bar_k, phase_k & 1u, p.err, 1);
+                        ++phase_k;
+                        mbar_wait(bar_v, phase_v & 1u, p.err, 1);
+                        ++phase_v;
                     }
                     __syncwarp();
                     if (lane == 0) {
                         fence_proxy_async();
-                        issue_group(p, &tmK, &tmV, stage, bar, bh, gi);
+                        issue_k(p, &tmK, stage, bar_k, bh, gi);
+                        issue_v(p, &tmV, stage, bar_v, bh, gi);
                     }
-                    pending = true;
+                    pend_k = pend_v = true;
                 }
+                // K of the next group loads during this group's PV, its V during the next QK
                 for (; gi <= g_last; gi += NW) {
-                    if (!mbar_wait(bar, phase & 1u, p.err, 1)) break;
-                    ++phase;
-                    pending = false;
-                    process_group(stage, gi * GT, int(t_begin), int(t_end), qf, p.scale_log2, acc, m_run, l_run,
-                                  g, t);
+                    if (!mbar_wait(bar_k, phase_k & 1u, p.err, 1)) break;
+                    ++phase_k;
+                    pend_k = false;
+                    float x[8];
+                    qk_part(stage, gi * GT, int(t_begin), int(t_end), qf, p.scale_log2, acc, m_run, l_run, g, t, x);
                     __syncwarp();
-                    if (gi + NW <= g_last) {
+                    const bool more = gi + NW <= g_last;
+                    if (more) {
                         if (lane == 0) {
                             fence_proxy_async();
-                            issue_group(p, &tmK, &tmV, stage, bar, bh, gi + NW);
+                            issue_k(p, &tmK, stage, bar_k, bh, gi + NW);
                         }
-                        pending = true;
+                        pend_k = true;
+                    }
+                    if (!mbar_wait(bar_v, phase_v & 1u, p.err, 1)) break;
+                    ++phase_v;
+                    pend_v = false;
+                    pv_part(stage, x, acc, g, t);
+                    __syncwarp();
+                    if (more) {
+                        if (lane == 0) {
+                            fence_proxy_async();
+                            issue_v(p, &tmV, stage, bar_v, bh, gi + NW);
+                        }
+                        pend_v = true;
                     }
                     __syncwarp();
                 }
             }
         }
-        if (pending) mbar_wait(bar, phase & 1u, p.err, 1);   // a copy nobody used must land before exit
+        // a copy nobody used must land before exit
+        if (pend_k) mbar_wait(bar_k, phase_k & 1u, p.err, 1);
+        if (pend_v) mbar_wait(bar_v, phase_v & 1u, p.err, 1);
     } else {
         int64_t tlo = max(lo, qlen);
         process_tail_tile(p, bh, warp, u, tlo, qf, acc, m_run, l_run, g, t);

@@ -193,14 +193,23 @@ __device__ __forceinline__ void finalize_step(const Params& p, int lane) {
 }
 
 // Per-lane replicated LUT: entry v for lane l at word v*64 + l (l < 32).
+// Every thread's loads are issued before its first store: one L2 round trip.
 template <int THREADS>
 __device__ __forceinline__ void build_lut(uint32_t* lut_s, const uint32_t* lut) {
-    for (int v = threadIdx.x; v < 256 * 4; v += THREADS) {
-        const int e = v >> 2, q = v & 3;
-        const uint32_t w = __ldg(lut + e);
-        uint4* dst = reinterpret_cast<uint4*>(lut_s + e * 64 + 8 * q);
-        dst[0] = make_uint4(w, w, w, w);
-        dst[1] = make_uint4(w, w, w, w);
+    constexpr int IT = (256 * 4 + THREADS - 1) / THREADS;
+    uint32_t w[IT];
+#pragma unroll
+    for (int i = 0; i < IT; ++i) {
+        const int v = threadIdx.x + i * THREADS;
+        w[i] = v < 256 * 4 ? __ldg(lut + (v >> 2)) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < IT; ++i) {
+        const int v = threadIdx.x + i * THREADS;
+        if (v >= 256 * 4) break;
+        uint4* dst = reinterpret_cast<uint4*>(lut_s + (v >> 2) * 64 + 8 * (v & 3));
+        dst[0] = make_uint4(w[i], w[i], w[i], w[i]);
+        dst[1] = make_uint4(w[i], w[i], w[i], w[i]);
     }
 }
 
@@ -486,8 +495,8 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         fence_mbar_init();
         for (int c = 0; c < NAT_STAGES && c < n_chunks; ++c) issue(c);
     }
+    const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);   // in flight with the LUT loads
     build_lut<NAT_THREADS>(lut_s, p.lut);
-    const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);
     pdl_trigger();
     pdl_wait();
     if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre);
@@ -653,8 +662,8 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         for (int k = 0; k < NAT_STAGES; ++k)
             if (!issue_next()) break;
     }
+    const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);   // in flight with the LUT loads
     build_lut<NAT_THREADS>(lut_s, p.lut);
-    const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);
     pdl_trigger();
     pdl_wait();
     // The residual rows of this CTA's row groups, read with x so that the
