@@ -312,9 +312,9 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     peaks = _peaks()
     # DRAM bytes per algorithmic byte from one ncu capture of each kernel (dram__bytes_read.sum +
     # dram__bytes_write.sum): the fused gate/up GEMV moved 26.54 MB for 26.46 MB of codes + absmax;
-    # the attention at ctx 32768 moved 71.67 + 1.22 MB for 71.32 MB.  Applied to this run's bytes.
+    # the attention at ctx 32768 moved 71.86 + 1.31 MB for 71.32 MB.  Applied to this run's bytes.
     gemv_traffic_ratio = 26.540288 / 26.460160
-    attn_traffic_ratio = (71.667200 + 1.222656) / 71.319552
+    attn_traffic_ratio = (71.857920 + 1.305600) / 71.319552
     gemv = [kern[k] for k in ("qkv", "o_proj", "gate_up", "down", "lm_head")]
     per_tok = {k: kern[k]["ms"] * (1 if k == "lm_head" else cfg.num_hidden_layers) for k in kern}
     gemv_bytes = sum(kern[k]["bytes"] * (1 if k == "lm_head" else cfg.num_hidden_layers)
