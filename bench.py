@@ -52,6 +52,8 @@ def _args():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=36, help="36 for the headline config")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-attn-sweep", action="store_true",
+                    help="skip the long-context attention sample (BASELINE config 3) added to the line")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--kv-fill", choices=["auto", "prefill", "random"], default="auto",
                     help="context: eager prefill of random tokens, or random int8 codes written straight into the "
@@ -361,6 +363,23 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         "clocks": clk,
         "setup_s": round(setup_s, 1),
     }
+    if world == 1 and not args.no_attn_sweep:
+        # BASELINE config 3 (long-context int8-KV decode attention, 32 q / 8 KV heads), measured live:
+        # device time per launch from graph replays over rotating KV caches larger than L2
+        from nova_b200.bench_kernels import bench_attn
+
+        del dec
+        torch.cuda.empty_cache()
+        cases = []
+        for ctx_l, b_l in ((32768, 1), (32768, 4), (32768, 16), (131072, 1)):
+            r = bench_attn(ctx_l, b_l, iters=10)
+            cases.append({"ctx": ctx_l, "batch": b_l, "us": r["us"], "gbs": r["gbs"],
+                          "frac": round(r["gbs"] / peaks["hbm_gbs"], 3)})
+            torch.cuda.empty_cache()
+        line["attn_long_ctx"] = {"kernel": "attn_decode_int8_kernel", "bound": "hbm", "unit": "GB/s",
+                                 "peak": peaks["hbm_gbs"], "cases": cases,
+                                 "basis": "algorithmic bytes (272 B per cached token and KV head + ring + q/out) "
+                                          "/ CUDA-event device time per launch"}
     if world == 1 and not args.no_cpu_baseline:
         from oracle.baseline import LayerSample, host_threads
 
