@@ -51,3 +51,31 @@ def test_host_side_argument_checks_need_no_gpu():
     assert rc == _lib.NOVA_OK and out.value > 0
     with pytest.raises(ValueError):
         _lib.check(lib.nova_attn_workspace_bytes(1, 30, 8, 16, 1, ctypes.byref(out)), "ws")
+
+
+def test_fused_append_attention_checks_need_no_gpu():
+    """nova_qk_append_attn_int8 rejects NULL arguments and q/k and attention
+    arguments that disagree, on the host (the pointers below are never read)."""
+    lib = _lib.lib()
+    assert lib.nova_qk_append_attn_int8(None, None, None) == _lib.NOVA_ERR_INVALID
+    qk, at = _lib.QKArgs(), _lib.AttnArgs()
+    for s in (qk, at):
+        s.batch, s.q_heads, s.kv_heads, s.max_len = 1, 32, 8, 256
+    qk.head_dim, qk.group = 128, 64
+    at.n_splits = 4
+    fake = [0x10000 * (i + 1) for i in range(8)]
+    qk.tail_k, qk.tail_v, qk.kq, qk.vq, qk.kmn, qk.kst, qk.vmn, qk.vst = fake
+    at.tail_k, at.tail_v, at.kq, at.vq, at.kmn, at.kst, at.vmn, at.vst = fake
+    at.batch = 2
+    rc = lib.nova_qk_append_attn_int8(ctypes.byref(qk), ctypes.byref(at), None)
+    assert rc == _lib.NOVA_ERR_INVALID and "disagree" in _lib.last_error()
+    at.batch = 1
+    at.vst = fake[0]
+    rc = lib.nova_qk_append_attn_int8(ctypes.byref(qk), ctypes.byref(at), None)
+    assert rc == _lib.NOVA_ERR_INVALID and "same ring" in _lib.last_error()
+    at.vst = fake[7]
+    at.tail_k = at.tail_v = None
+    rc = lib.nova_qk_append_attn_int8(ctypes.byref(qk), ctypes.byref(at), None)
+    assert rc == _lib.NOVA_ERR_INVALID and "tail ring" in _lib.last_error()
+    qk.head_dim = 64
+    assert lib.nova_qk_append_attn_int8(ctypes.byref(qk), ctypes.byref(at), None) == _lib.NOVA_ERR_UNSUPPORTED

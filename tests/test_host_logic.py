@@ -68,3 +68,20 @@ def test_bytes_accounting_matches_format():
     c = bytes_per_token(num_slots=1, num_kv_heads=8, head_dim=128)
     assert c["int8t64_kv"] == 2176             # per token per layer: 2048 B codes + 128 B scales (8 KV heads)
     assert c["fp16_kv"] == 4096
+
+
+@pytest.mark.parametrize("max_len,batch", [(8448, 1), (33024, 1), (131328, 1), (33024, 4), (33024, 64), (320, 2)])
+def test_pick_chunk_properties(max_len, batch):
+    """Attention split size: a multiple of 64, at least 256 tokens, at most 8192 tokens
+    once the context needs more than one split, and few enough splits that the last CTA
+    of a KV head can stage every split's partials in one shared-memory copy."""
+    from nova_b200.kvattn import GROUP_T, pick_chunk
+
+    hq, hkv = 32, 8
+    chunk = pick_chunk(max_len, batch, hkv, hq)
+    n_splits = -(-max_len // chunk)
+    cap = 73728 // ((hq // hkv) * 528) - 1
+    assert chunk % GROUP_T == 0 and chunk >= 4 * GROUP_T
+    assert n_splits <= cap
+    if -(-max_len // 8192) <= cap:
+        assert chunk <= 8192
