@@ -52,14 +52,12 @@ def _args():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=36, help="36 for the headline config")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-attn-sweep", action="store_true",
-                    help="skip the long-context attention sample (BASELINE config 3) added to the line")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the BASELINE config 1/2/3/5 sub-records added to the line")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--kv-fill", choices=["auto", "prefill", "random"], default="auto",
                     help="context: eager prefill of random tokens, or random int8 codes written straight into the "
                          "cache (auto: prefill up to batch*ctx = 65536 tokens)")
-    ap.add_argument("--qkv-fused", action="store_true",
-                    help="q|k|v GEMV and q/k norm + RoPE + append as one launch (one CTA per head)")
     ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp",
                     help="N > 1: tensor parallelism over the N GPUs (default) or N independent replicas")
     return ap.parse_args()
@@ -112,33 +110,35 @@ class ClockSampler:
 
 
 def run_reference(args, rank: int) -> None:
-    """The reference algorithm on the host cores (the CPU oracle port; the
-    reference itself is Python/Triton and its CPU path is what the oracle
-    restates).  Each step is a bounded sample: one decoder layer with 1/8 of
-    every linear's rows and of the KV heads, plus its lm_head share; tok/s
-    scales it by 36 * 8."""
+    """The reference algorithm on the host cores: the CPU oracle port of one
+    decode token (the reference's decode path is Python + Triton on CUDA; its
+    CPU path is the torch eager model, which the oracle restates in numpy).
+    Each step is a bounded sample of the same workload -- one full decoder
+    layer at the bench context plus 1/36 of the 4-bit lm_head, every linear
+    NF4-dequantized on the call -- and tok/s = 1 / (36 x the median sample),
+    the same figure as the B200 arm's ``cpu_baseline``."""
     if rank != 0:
         return
     import numpy as np
 
     from oracle.baseline import LayerSample, host_threads
 
-    s = LayerSample(ctx=args.ctx, slice=8, seed=args.seed)
+    s = LayerSample(ctx=args.ctx, seed=args.seed)
     for _ in range(max(1, args.warmup)):
         s.run()
     times = [s.run() for _ in range(args.steps)]
-    sec_tok = float(np.mean(times)) * s.seconds_scale   # one sequence; the host does B sequences one after another
+    sec_tok = float(np.median(times)) * s.layers   # one sequence; the host does B sequences one after another
     v = 1.0 / sec_tok
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": float(np.mean(times)) * 1e3, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": sec_tok * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": _workload(args), "ctx": args.ctx, "global_batch": args.batch, "layers": 36,
                    "parallelism": "host cores"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
-                         "sample": f"per step: 1 decoder layer at ctx {args.ctx} with 1/8 of each linear's rows and "
-                                   "of the KV heads + 1/288 of the lm_head, NF4 dequant per call + fp32 numpy; "
-                                   "scaled x288 (one sequence; tok/s of a batch is the same on the host)"},
+                         "sample": f"per step: one full decoder layer at ctx {args.ctx} + 1/36 of the lm_head (NF4 "
+                                   "dequant per call + fp32 numpy matmul, int8 KV dequant + fp32 attention); "
+                                   "tok/s = 1 / (36 x median step)"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -223,6 +223,133 @@ def _time_kernels(dec, reps: int = 10) -> dict:
     return out
 
 
+def _kernel_configs(peaks: dict, cpu: bool) -> dict:
+    """BASELINE configs 1-3 measured in this run on one GPU (device time per
+    launch from CUDA-graph replays over weight / KV sets larger than L2), each
+    next to its CPU figure (the oracle port on this host's cores)."""
+    import torch
+
+    from nova_b200.bench_kernels import CONFIG2, bench_append_attn, bench_attn, bench_gemv
+
+    from oracle.baseline import AttnSlice, Config1Sample, GemvSample, host_threads, median_time
+
+    hbm = peaks["hbm_gbs"]
+    out = {}
+    # config 1: one layer, batch 1, 32 q / 8 KV heads, ctx 4096: the append of the group-completing token + attention
+    r = bench_append_attn(4096, 1)
+    c1 = {"workload": "1 layer, batch 1, 32 q / 8 KV heads, ctx 4096: int8 KV append (group requantized) + decode "
+                      "attention", "kernel": r["kernel"], "us": r["us"], "bytes": r["bytes"], "gbs": r["gbs"],
+          "frac": round(r["gbs"] / hbm, 3)}
+    if cpu:
+        sec, runs = median_time(Config1Sample().run, budget_s=2.0)
+        c1["cpu"] = {"us": round(sec * 1e6, 1), "gbs": round(r["bytes"] / sec / 1e9, 2), "cores": host_threads(),
+                     "kind": "port", "sample": f"median of {runs}: ring requantization + int8 dequant + fp32 attention"}
+    out["c1"] = c1
+    torch.cuda.empty_cache()
+    # config 2: the NF4 GEMV shapes at batch 1 (native unit layout, as the decoder streams them)
+    shapes = []
+    for name, n, k in CONFIG2:
+        r = bench_gemv(n, k, iters=10)
+        rec = {"name": name, "n": n, "k": k, "us": r["us"], "bytes": r["bytes"], "gbs": r["gbs"],
+               "frac": round(r["gbs"] / hbm, 3)}
+        if cpu:
+            smp = GemvSample(n, k, rows=min(n, 9728))
+            sec, runs = median_time(smp.run, budget_s=1.0)
+            rec["cpu_us"] = round(sec * smp.scale * 1e6, 1)
+            rec["cpu_sample"] = (f"median of {runs}" if smp.scale == 1 else
+                                 f"median of {runs} over 9728 of the {n} rows, scaled x{smp.scale:.2f}")
+        shapes.append(rec)
+        torch.cuda.empty_cache()
+    out["c2"] = {"workload": "NF4 GEMV, batch 1, weights N(0,0.02) blocksize 64 fp16 absmax", "kernel": "nf4_gemv",
+                 "shapes": shapes, "cpu_cores": host_threads() if cpu else None,
+                 "cpu_kind": "port: NF4 dequant + fp32 numpy matmul per call" if cpu else None}
+    # config 3: long-context decode attention, full causal and window 4096
+    cases = []
+    slices = {}
+    for batch in (1, 4, 16):
+        for ctx in (32768, 65536, 131072):
+            for window in (0, 4096):
+                r = bench_attn(ctx, batch, window=window, iters=10)
+                rec = {"ctx": ctx, "batch": batch, "window": window, "us": r["us"], "bytes": r["bytes"],
+                       "gbs": r["gbs"], "frac": round(r["gbs"] / hbm, 3), "chunk": r["chunk"]}
+                if cpu:
+                    if (ctx, window) not in slices:
+                        slices[(ctx, window)] = median_time(AttnSlice(ctx, window).run, budget_s=0.5)[0]
+                    rec["cpu_us"] = round(slices[(ctx, window)] * batch * 8 * 1e6, 1)
+                cases.append(rec)
+                torch.cuda.empty_cache()
+    out["c3"] = {"workload": "int8-KV decode attention, 32 q / 8 KV heads", "kernel": "attn_decode_int8",
+                 "cases": cases,
+                 "basis": "algorithmic bytes (272 B per attended int8 token and KV head + ring + q/out) / CUDA-event "
+                          "device time per launch",
+                 "cpu_sample": "one batch row x one KV head (4 q heads) timed, x batch x 8" if cpu else None}
+    return out
+
+
+def _config5(args, rank: int, world: int, dev, use_tp: bool, cpu: bool) -> dict:
+    """BASELINE config 5 measured in the same run: batch 64, ctx 32768 per
+    sequence (random int8 codes written straight into the cache), the batched
+    NF4 GEMMs on the tcgen05 tensor cores, tensor-parallel over the job's GPUs
+    when the bench runs tensor parallelism.  Every rank takes part."""
+    import torch
+    import torch.distributed as dist
+
+    from nova_b200.decoder import DecoderConfig, DecoderWeights, NovaDecoder
+    from nova_b200.tp import TPContext
+
+    cfg = DecoderConfig()
+    batch, ctx, warm = 64, 32768, 2
+    steps = max(1, min(args.steps, 16))
+    W = DecoderWeights.random_init(cfg, seed=args.seed, device=dev)
+    tp = TPContext(rank, world, dist.group.WORLD) if use_tp else None
+    dec = NovaDecoder(W, max_len=ctx + warm + steps + 64, batch=batch, device=dev, tp=tp)
+    del W
+    dec.fill_random(ctx, seed=args.seed + 5)
+    dec.capture()
+    for _ in range(warm):
+        dec.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        dec.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dec.check_errors()
+    ms = float(t.item()) / steps
+    copies = 1 if use_tp else world
+    kv_bytes = batch * dec.hkv * ctx * 272 * cfg.num_hidden_layers    # this GPU's shard
+    step_bytes = kv_bytes + dec.w.nbytes_per_token()
+    peak = _peaks()["hbm_gbs"]
+    rec = {"workload": "batch 64, ctx 32768, random int8 KV, NF4 GEMMs on tcgen05" +
+                       (f", tp{world}" if use_tp else ""),
+           "value": copies * batch / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+           "n_gpus": world, "step_roofline": {"bytes_per_step": step_bytes, "per": "GPU",
+                                              "ms_at_peak": step_bytes / (peak * 1e9) * 1e3,
+                                              "frac": step_bytes / (peak * 1e9) / (ms * 1e-3)},
+           "gpu_launches_per_step": dec.launches_per_step()}
+    dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    if cpu and rank == 0:
+        from oracle.baseline import LayerSample, host_threads
+
+        smp = LayerSample(ctx=ctx, seed=args.seed, batch=batch, attn_rows=2)
+        sec = min(smp.run() for _ in range(2))
+        rec["cpu"] = {"value": batch / (sec * smp.layers), "unit": UNIT, "cores": host_threads(), "kind": "port",
+                      "sample": "best of 2 x one decoder layer for 64 rows at ctx 32768 (linears for all rows, "
+                                "2 rows' attentions timed and scaled to 64) + 1/36 of the lm_head; x 36 layers"}
+    return rec
+
+
 def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
@@ -241,7 +368,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     max_len = args.ctx + 2 * (args.warmup + args.steps) + 64
     use_tp = world > 1 and args.parallel == "tp"
     tp = TPContext(rank, world, dist.group.WORLD) if use_tp else None
-    dec = NovaDecoder(W, max_len=max_len, batch=args.batch, device=dev, tp=tp, qkv_fused=args.qkv_fused)
+    dec = NovaDecoder(W, max_len=max_len, batch=args.batch, device=dev, tp=tp)
     del W
     copies = 1 if use_tp else world   # independent sequences in the job
     g = torch.Generator().manual_seed(args.seed + 1 + (0 if use_tp else rank))
@@ -306,8 +433,18 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     e2e_v = copies * args.batch * args.steps / (float(te.item()) * 1e-3)
 
     kern = _time_kernels(dec)
+    dec.check_errors()   # a bounded wait that gave up in any launch invalidates the numbers
     if world > 1:
         dist.barrier()
+    launches = dec.launches_per_step()
+    configs = {}
+    if world == 1 and not args.no_configs:
+        configs.update(_kernel_configs(_peaks(), cpu=not args.no_cpu_baseline))
+    if not args.no_configs and (args.batch, args.ctx) == (1, 8192):
+        dec.close()
+        del dec
+        torch.cuda.empty_cache()
+        configs["c5"] = _config5(args, rank, world, dev, use_tp, cpu=world == 1 and not args.no_cpu_baseline)
     if rank != 0:
         return
 
@@ -331,6 +468,9 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                 else "fallback 6650 GB/s",
                 "traffic": gemv_bytes * gemv_traffic_ratio, "traffic_basis": "per step; ncu DRAM bytes of the fused "
                 "gate/up launch scaled by algorithmic bytes", "bytes_per_step": gemv_bytes, "ms_per_step": gemv_ms, "launches_timed": n_launch,
+                "per_shape_note": "each launch family replayed alone (one launch per layer in its own graph): no "
+                                  "overlap with the neighbouring kernels, so these times exceed the family's share "
+                                  "of the step",
                 "per_shape": {k: {"gbs": round(kern[k]["gbs"], 1), "us": round(kern[k]["ms"] * 1e3, 2),
                                   "bytes": kern[k]["bytes"]} for k in ("qkv", "o_proj", "gate_up", "down", "lm_head")}}
     attn_roof = {"kernel": "attn_decode_int8_kernel", "bound": "hbm", "achieved": att["gbs"], "peak": peaks["hbm_gbs"],
@@ -359,40 +499,20 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                           "tok_s_at_peak": peaks["hbm_gbs"] * 1e9 / step_bytes,
                           "frac": (value / copies / args.batch) / (peaks["hbm_gbs"] * 1e9 / step_bytes)},
         "e2e": {"value": e2e_v, "unit": UNIT, "h2d_bytes_per_step": 8 * args.batch, "d2h_bytes_per_step": 8 * args.batch},
-        "gpu_launches": dec.launches_per_step() * args.steps * world,
+        "gpu_launches": launches * args.steps * world,
         "clocks": clk,
         "setup_s": round(setup_s, 1),
     }
-    if world == 1 and not args.no_attn_sweep:
-        # BASELINE config 3 (long-context int8-KV decode attention, 32 q / 8 KV heads), measured live:
-        # device time per launch from graph replays over rotating KV caches larger than L2
-        from nova_b200.bench_kernels import bench_attn
-
-        del dec
-        torch.cuda.empty_cache()
-        cases = []
-        for ctx_l, b_l in ((32768, 1), (32768, 4), (32768, 16), (131072, 1)):
-            r = bench_attn(ctx_l, b_l, iters=10)
-            cases.append({"ctx": ctx_l, "batch": b_l, "us": r["us"], "gbs": r["gbs"],
-                          "frac": round(r["gbs"] / peaks["hbm_gbs"], 3)})
-            torch.cuda.empty_cache()
-        line["attn_long_ctx"] = {"kernel": "attn_decode_int8_kernel", "bound": "hbm", "unit": "GB/s",
-                                 "peak": peaks["hbm_gbs"], "cases": cases,
-                                 "basis": "algorithmic bytes (272 B per cached token and KV head + ring + q/out) "
-                                          "/ CUDA-event device time per launch"}
+    line.update(configs)
     if world == 1 and not args.no_cpu_baseline:
-        from oracle.baseline import LayerSample, host_threads
+        from oracle.baseline import LayerSample, host_threads, median_time
 
-        s = LayerSample(ctx=args.ctx, slice=1, seed=args.seed)
-        s.run()
-        times = []
-        t_end = time.time() + 20
-        while time.time() < t_end and len(times) < 20:
-            times.append(s.run())
-        tok_s = 1.0 / (statistics.median(times) * s.seconds_scale)
-        line["cpu_baseline"] = {"value": tok_s, "unit": UNIT, "cores": host_threads(), "kind": "port",
-                                "sample": f"{len(times)} x one full decoder layer at ctx {args.ctx} + 1/36 of the "
-                                          "lm_head (NF4 dequant per call + fp32 numpy matmul, int8 KV dequant + fp32 "
+        smp = LayerSample(ctx=args.ctx, seed=args.seed)
+        sec, runs = median_time(smp.run, budget_s=20.0, max_runs=20)
+        line["cpu_baseline"] = {"value": 1.0 / (sec * smp.layers), "unit": UNIT, "cores": host_threads(),
+                                "kind": "port",
+                                "sample": f"{runs} x one full decoder layer at ctx {args.ctx} + 1/36 of the lm_head "
+                                          "(NF4 dequant per call + fp32 numpy matmul, int8 KV dequant + fp32 "
                                           "attention); tok/s = 1 / (36 x median sample)"}
     print(json.dumps(line), flush=True)
 

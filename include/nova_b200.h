@@ -167,6 +167,13 @@ NOVA_API int nova_attn_read_error(void* workspace, int64_t batch, int64_t kv_hea
  * attention allocates its scratch through torch (src/nova/kvattn.py:281-427). */
 NOVA_API int nova_attn_decode_int8_noalloc(const nova_attn_int8_args* args, void* stream);
 
+/* Error word of nova_attn_decode_int8_noalloc on the current device (non-zero
+ * = a bounded wait in the latest call gave up and its output is not valid):
+ * copied to *host_value synchronously and cleared.  Each call of
+ * nova_attn_decode_int8_noalloc clears the word before its kernel, so this
+ * reports the most recent call only. */
+NOVA_API int nova_attn_noalloc_read_error(int* host_value);
+
 /* ------------------------------------------------------------------ NF4 */
 
 /* Epilogues of nova_nf4_gemv. */
@@ -237,6 +244,11 @@ typedef struct nova_nf4_args {
 } nova_nf4_args;
 
 NOVA_API int nova_nf4_gemv(const nova_nf4_args* args, void* stream);
+
+/* Error word inside a nova_nf4_gemv workspace (non-zero = a bounded wait of a
+ * launch that used it gave up and that launch's output is not valid): copied
+ * to *host_value synchronously and cleared. */
+NOVA_API int nova_nf4_gemv_read_error(void* workspace, int* host_value);
 
 /*
  * B200-native NF4 layout: the [N, K] matrix as 32-row x 64-k units, row-group
@@ -358,30 +370,16 @@ NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
 NOVA_API int nova_qk_append_attn_int8(const nova_qk_args* qk, const nova_attn_int8_args* attn, void* stream);
 
 /*
- * The decoder's q|k|v projection and q/k norm + RoPE + int8 KV append in one
- * launch: gemv describes the NF4 GEMV of the concatenated q|k|v weight
- * (native layout, N = (q_heads + 2*kv_heads) * 128, optional RMSNorm
- * prologue, epilogue ignored, out unused), qk the rest as for
- * nova_qk_norm_rope_append (its qkv field unused).  One CTA per head keeps the
- * head's projection in shared memory; results are identical to
- * nova_nf4_gemv (plain epilogue, CTA-level schedule) followed by
- * nova_qk_norm_rope_append.  Replaces the q/k/v projections, q_norm/k_norm,
- * RoPE and cache update of LeanAttention.forward (src/nova/layers.py:99-133,
- * :24-36; src/nova/kvattn.py:668-743).
- */
-NOVA_API int nova_qkv_norm_rope_append(const nova_nf4_args* gemv, const nova_qk_args* qk, void* stream);
-
-/*
  * Batched NF4 GEMM for M = 1..64 rows:
  * y = x @ dequant(W)^T with dequant = fp16(code * absmax) (the reference's
  * dequantized weight, src/nova/quant.py:39-69 + the dequant-matmul of
  * tests/test_nf4_linear.py), fp32 accumulation, the epilogues of
  * nova_nf4_gemv (PLAIN without bias, RESIDUAL, SILU_MUL, ARGMAX with the
  * step finalize, F32).  No norm prologue (normalize x with nova_rmsnorm).
- * layout = 2 (units from nova_nf4_pack_tc): tcgen05 tensor cores -- weights
+ * Weights in the tcgen05 unit layout (layout = 2, from nova_nf4_pack_tc):
  * decoded into tensor memory, x tiles by TMA, fp32 accumulators in tensor
  * memory, (tile, k-block) work split evenly over one wave of CTAs with
- * deterministic partial sums.  layout = 1 (nova_nf4_pack_native): mma.sync.
+ * deterministic partial sums.  Other layouts: NOVA_ERR_UNSUPPORTED.
  * x needs a 16-byte aligned base and a row stride that is a multiple of 8.
  * Workspace: nova_nf4_gemm_workspace_bytes(), zeroed once.
  * Replaces NF4Linear.forward / fused_nf4_linear for batched rows
@@ -389,6 +387,8 @@ NOVA_API int nova_qkv_norm_rope_append(const nova_nf4_args* gemv, const nova_qk_
  */
 NOVA_API int nova_nf4_gemm_workspace_bytes(int64_t n, int64_t k, int64_t* bytes);
 NOVA_API int nova_nf4_gemm(const nova_nf4_args* args, void* stream);
+/* Error word inside a nova_nf4_gemm workspace, as nova_nf4_gemv_read_error. */
+NOVA_API int nova_nf4_gemm_read_error(void* workspace, int* host_value);
 
 /*
  * Next-token sampling from the logits buffer, outside the decode graph
@@ -424,50 +424,6 @@ typedef struct nova_sample_args {
 } nova_sample_args;
 
 NOVA_API int nova_sample_topk(const nova_sample_args* args, void* stream);
-
-/* ------------------------------------------------------- fused phases */
-
-/*
- * One cooperative launch (one CTA per SM) that runs up to 6 phases in order
- * with grid barriers between them: NF4 GEMVs on native-layout weights (M <= 2
- * rows, epilogues PLAIN / RESIDUAL / SILU_MUL / F32, optional RMSNorm
- * prologue, the CTA-level split-K schedule) and at most one q/k norm + RoPE +
- * int8 KV append phase (the work of nova_qk_norm_rope_append).  The decoder
- * runs a layer's o_proj -> gate|up -> down -> next layer's q|k|v -> q/k norm
- * as one launch.  Each warp requests the next GEMV's first weight chunks
- * before it waits at a barrier.  Grid-barrier waits give up after timeout_ns
- * (0 = 1 s) and record an error word in the workspace; mbarrier waits are
- * bounded as everywhere else.  No counterpart in the reference, whose layer
- * runs these ops as separate kernels (src/nova/layers.py:99-218).
- */
-typedef struct nova_gemv_phase {
-    const void* x;            /* fp16 [m, x_stride] input rows                  */
-    int64_t x_stride;
-    const void* norm_weight;  /* fp16 [k] RMSNorm prologue or NULL              */
-    const void* units;        /* native unit stream (nova_nf4_pack_native)      */
-    int64_t n, k;
-    void* out;                /* fp16 (fp32 for NOVA_NF4_F32) [m, out_stride]  */
-    int64_t out_stride;
-    const void* residual;     /* RESIDUAL epilogue                              */
-    int64_t res_stride;
-    int64_t epilogue;
-} nova_gemv_phase;
-
-typedef struct nova_fused_args {
-    int64_t n_phases;
-    int64_t kind[6];          /* 0 = GEMV (gemv[i]), 1 = q/k norm + RoPE + append (qk) */
-    nova_gemv_phase gemv[6];
-    nova_qk_args qk;
-    const void* lut;          /* NF4 LUT (build_nf4_lut)                        */
-    double eps;               /* RMSNorm eps of every phase                     */
-    int64_t m;                /* rows (batch), 1 or 2                           */
-    void* workspace;          /* nova_fused_workspace_bytes(), zeroed once      */
-    int64_t workspace_bytes;
-    int64_t timeout_ns;
-} nova_fused_args;
-
-NOVA_API int nova_fused_workspace_bytes(int64_t* bytes);
-NOVA_API int nova_fused_phases(const nova_fused_args* args, void* stream);
 
 /* --------------------------------------------------- tensor parallelism */
 

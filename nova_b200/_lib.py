@@ -64,27 +64,6 @@ class QKArgs(ctypes.Structure):
     ]
 
 
-class GemvPhase(ctypes.Structure):
-    """Mirror of ``nova_gemv_phase``."""
-
-    _fields_ = [
-        ("x", _P), ("x_stride", _I), ("norm_weight", _P), ("units", _P), ("n", _I), ("k", _I),
-        ("out", _P), ("out_stride", _I), ("residual", _P), ("res_stride", _I), ("epilogue", _I),
-    ]
-
-
-class FusedArgs(ctypes.Structure):
-    """Mirror of ``nova_fused_args``."""
-
-    _fields_ = [
-        ("n_phases", _I), ("kind", _I * 6), ("gemv", GemvPhase * 6), ("qk", QKArgs), ("lut", _P),
-        ("eps", ctypes.c_double), ("m", _I), ("workspace", _P), ("workspace_bytes", _I), ("timeout_ns", _I),
-    ]
-
-
-PHASE_GEMV, PHASE_QK = 0, 1
-
-
 class SampleArgs(ctypes.Structure):
     """Mirror of ``nova_sample_args``."""
 
@@ -116,8 +95,10 @@ _SIGNATURES: dict[str, list] = {
     "nova_attn_decode_int8": [ctypes.POINTER(AttnArgs), _P],
     "nova_attn_read_error": [_P, _I, _I, ctypes.POINTER(_i)],
     "nova_attn_decode_int8_noalloc": [ctypes.POINTER(AttnArgs), _P],
+    "nova_attn_noalloc_read_error": [ctypes.POINTER(_i)],
     "nova_nf4_workspace_bytes": [_I, ctypes.POINTER(_I)],
     "nova_nf4_gemv": [ctypes.POINTER(NF4Args), _P],
+    "nova_nf4_gemv_read_error": [_P, ctypes.POINTER(_i)],
     "nova_nf4_quantize": [_P, _I, _I, _P, _P, _P, _i, _P],
     "nova_nf4_dequant": [_P, _P, _i, _P, _P, _I, _I, _P],
     "nova_nf4_native_bytes": [_I, _I, ctypes.POINTER(_I)],
@@ -131,11 +112,9 @@ _SIGNATURES: dict[str, list] = {
     "nova_ipc_handle": [_P, _P, ctypes.POINTER(_I)],
     "nova_ipc_open": [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P)],
     "nova_ipc_close": [_P],
-    "nova_fused_workspace_bytes": [ctypes.POINTER(_I)],
     "nova_nf4_gemm_workspace_bytes": [_I, _I, ctypes.POINTER(_I)],
     "nova_nf4_gemm": [ctypes.POINTER(NF4Args), _P],
-    "nova_qkv_norm_rope_append": [ctypes.POINTER(NF4Args), ctypes.POINTER(QKArgs), _P],
-    "nova_fused_phases": [ctypes.POINTER(FusedArgs), _P],
+    "nova_nf4_gemm_read_error": [_P, ctypes.POINTER(_i)],
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
     "nova_qk_append_attn_int8": [ctypes.POINTER(QKArgs), ctypes.POINTER(AttnArgs), _P],
     "nova_sample_topk": [ctypes.POINTER(SampleArgs), _P],

@@ -172,6 +172,59 @@ def bench_attn(ctx: int, batch: int = 1, q_heads: int = 32, kv_heads: int = 8, w
             "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
 
 
+def bench_append_attn(ctx: int = 4096, batch: int = 1, q_heads: int = 32, kv_heads: int = 8, sets: int = 0,
+                      iters: int = 20, seed: int = 0) -> dict:
+    """the decode append of the token at position ctx-1
+    (nova_kv_append_int8: ring slot write; the token completes a 64-token
+    group, so the group is requantized into the int8 cache) followed by the
+    decode attention of that token over all ctx positions
+    (nova_attn_decode_int8), one pair of launches per layer, rotating over
+    ``sets`` layers (more than L2 holds).  Algorithmic bytes: the int8 cache
+    read by the attention (272 B per token and KV head), the fp16 ring read by
+    the requantization, the group's codes and scales written, the new K/V, q
+    and the output."""
+    dev = torch.device("cuda")
+    d = 128
+    if ctx % GROUP_T:
+        raise ValueError("ctx must be a multiple of 64")
+    per_set = batch * kv_heads * ctx * 272
+    sets = sets or max(2, min(64, (320 << 20) // per_set + 1))
+    chunk = pick_chunk(ctx, batch, kv_heads, q_heads, torch.cuda.get_device_properties(dev).multi_processor_count)
+    n_splits = -(-ctx // chunk)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    ng = ctx // GROUP_T
+    layers = []
+    for _ in range(sets):
+        kq = torch.randint(0, 256, (batch, kv_heads, ctx, d), generator=g, device=dev, dtype=torch.uint8)
+        vq = torch.randint(0, 256, (batch, kv_heads, ctx, d), generator=g, device=dev, dtype=torch.uint8)
+        sc = [(torch.rand(batch, kv_heads, ng, d, generator=g, device=dev) * 0.01).half() for _ in range(4)]
+        tail = [torch.randn(batch, kv_heads, GROUP_T, d, generator=g, device=dev).half() for _ in range(2)]
+        new = [torch.randn(batch, kv_heads, d, generator=g, device=dev).half() for _ in range(2)]
+        layers.append((kq, sc[0], sc[1], vq, sc[2], sc[3], tail, new))
+    q = torch.randn(batch, q_heads, d, generator=g, device=dev).half()
+    out = torch.zeros(batch, q_heads, d, dtype=torch.float16, device=dev)
+    pos = torch.tensor([ctx - 1], device=dev)
+    written, qlen, pg = (torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(3))
+    ws = new_workspace(batch, q_heads, kv_heads, n_splits, True, dev)
+    stream = _lib.stream_of(dev)
+
+    def fn(i):
+        kq, kmn, kst, vq, vmn, vst, tail, (kn, vn) = layers[i]
+        _lib.call("nova_kv_append_int8", kn.data_ptr(), vn.data_ptr(), kn.stride(0), kn.stride(1),
+                  tail[0].data_ptr(), tail[1].data_ptr(), kq.data_ptr(), vq.data_ptr(), kmn.data_ptr(), kst.data_ptr(),
+                  vmn.data_ptr(), vst.data_ptr(), pos.data_ptr(), written.data_ptr(), qlen.data_ptr(), pg.data_ptr(),
+                  batch, kv_heads, ctx, d, GROUP_T, stream)
+        launch_attention(q, (kq, kmn, kst, vq, vmn, vst), tuple(tail), out, None, qlen, pg, written, None, ws,
+                         max_len=ctx, n_splits=n_splits, chunk=chunk)
+
+    us = _graph_time(fn, sets, iters)
+    bh = batch * kv_heads
+    nbytes = (bh * (ctx * 272 + 2 * GROUP_T * d * 2 + 2 * GROUP_T * d + 4 * d * 2 + 2 * d * 2)
+              + 2 * batch * q_heads * d * 2)
+    return {"kernel": "kv_append_int8 + attn_decode_int8", "ctx": ctx, "batch": batch, "sets": sets,
+            "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+
+
 CONFIG2 = [("q_proj", 4096, 2560), ("k_proj", 1024, 2560), ("v_proj", 1024, 2560), ("o_proj", 2560, 4096),
            ("gate_proj", 9728, 2560), ("up_proj", 9728, 2560), ("down_proj", 2560, 9728),
            ("lm_head", 151936, 2560)]

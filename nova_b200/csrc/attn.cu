@@ -907,13 +907,15 @@ static int attn_launch(const nova_attn_int8_args* a, const nova_qk_args* qk, voi
 
     using Kern = void (*)(Params, CUtensorMap, CUtensorMap);
     Kern kern = qk ? attn_decode_int8_kernel<true> : attn_decode_int8_kernel<false>;
-    static bool attr_set[2] = {false, false};
-    if (!attr_set[qk ? 1 : 0]) {
+    static bool attr_set[2][kMaxDevices] = {};   // the attribute is per device
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return fail(NOVA_ERR_CUDA, "no usable current device (%d)", dev);
+    if (!attr_set[qk ? 1 : 0][dev]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
             cudaGetLastError();
             return fail(NOVA_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
         }
-        attr_set[qk ? 1 : 0] = true;
+        attr_set[qk ? 1 : 0][dev] = true;
     }
     dim3 grid(unsigned(s_total), unsigned(a->kv_heads), unsigned(a->batch));
     const cudaError_t err = launch(kern, grid, dim3(THREADS), size_t(SMEM_BYTES), (cudaStream_t)stream, p, tmK, tmV);

@@ -77,3 +77,22 @@ extern "C" int nova_attn_decode_int8_noalloc(const nova_attn_int8_args* a, void*
     b.workspace_bytes = kScratchBytes;
     return nova_attn_decode_int8(&b, stream);
 }
+
+// The kernel's error word is the first word of the built-in array: copy it to
+// the host and clear it (synchronous; current device).  Every call of
+// nova_attn_decode_int8_noalloc clears it before its kernel, so this reports
+// the latest call only.
+extern "C" int nova_attn_noalloc_read_error(int* host_value) {
+    if (!host_value) return nova::fail(NOVA_ERR_INVALID, "host_value must not be NULL");
+    void* scratch = nullptr;
+    if (int rc = scratch_for_current_device(&scratch)) return rc;
+    if (cudaMemcpy(host_value, scratch, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return nova::fail(NOVA_ERR_CUDA, "reading the attention scratch error word failed");
+    }
+    if (*host_value && cudaMemset(scratch, 0, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        return nova::fail(NOVA_ERR_CUDA, "clearing the attention scratch error word failed");
+    }
+    return NOVA_OK;
+}

@@ -104,6 +104,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Ordinal of the current device, or -1 when the query fails.
+static inline int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return dev;
+}
+
+// Per-device record of a kernel attribute already set (cudaFuncSetAttribute
+// applies to the current device only): devices 0..kMaxDevices-1.
+constexpr int kMaxDevices = 64;
+
 // SMs of the current device (148 when the query fails).
 static inline int sm_count() {
     int dev = 0, n = 0;

@@ -866,842 +866,6 @@ __global__ void __launch_bounds__(REF_THREADS, 1) nf4_gemv_ref_kernel(const __gr
 }
 
 // ---------------------------------------------------------------------------
-// Fused phase program: one cooperative launch (one 16-warp CTA per SM) runs a
-// short list of phases -- NF4 GEMVs and the per-head q/k norm + RoPE + int8 KV
-// append -- separated by grid barriers, so a decoder layer's
-// o_proj -> gate|up -> down -> next q|k|v -> q/k-norm+RoPE+append is one
-// launch instead of five.  Every GEMV phase uses the CTA-level split-K
-// schedule (whole row groups per CTA, warps split the k-blocks, fragments added
-// in shared memory).  The per-warp weight cursor runs across phase boundaries:
-// before a warp waits at a barrier it has already requested the first chunks of
-// the next GEMV's weights (constant data), so that DRAM round trip overlaps the
-// barrier.  The LUT is built once per launch.
-
-constexpr int MAX_PHASES = 6;
-enum PhaseKind { PH_GEMV = 0, PH_QK = 1 };
-
-struct GemvPhase {
-    const __half* x;
-    int64_t x_stride;
-    const __half* norm_w;
-    const uint8_t* units;
-    __half* out;
-    int64_t out_stride;
-    const __half* residual;
-    int64_t res_stride;
-    int N, K, epi;
-};
-
-struct QkPhase {
-    const __half* qkv;
-    int64_t qkv_stride;
-    const __half* q_norm_w;
-    const __half* k_norm_w;
-    const __half* cos;
-    const __half* sin;
-    int64_t rope_len;
-    __half* q_out;
-    int64_t q_out_stride;
-    __half* tail_k;
-    __half* tail_v;
-    uint8_t* kq;
-    uint8_t* vq;
-    __half* kmn;
-    __half* kst;
-    __half* vmn;
-    __half* vst;
-    const int64_t* pos;
-    int64_t* written;
-    int64_t* qlen;
-    int64_t* pg;
-    int q_heads, kv_heads;
-    int64_t max_len;
-};
-
-struct FusedParams {
-    int n_phases;
-    int kind[MAX_PHASES];
-    GemvPhase g[MAX_PHASES];
-    QkPhase qk;
-    const uint32_t* lut;
-    float eps;
-    int M;
-    int stage_units;
-    int xs_bytes;
-    unsigned* bar_count;
-    unsigned* bar_gen;
-    int* err;
-    unsigned long long timeout_ns;
-};
-
-__device__ __forceinline__ unsigned long long gtime_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_gpu_u32(unsigned* p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Grid barrier k (1-based) of this launch: arrivals are counted cumulatively,
-// the last arriver of barrier k publishes generation base + k (and, at the
-// launch's last barrier, re-arms the counter for the next launch).  The wait
-// gives up after timeout_ns, recording the error word.
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
-    unsigned old;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-
-__device__ __forceinline__ void grid_barrier(const FusedParams& fp, unsigned base, int k, bool last) {
-    __syncthreads();   // the CTA's writes happen before thread 0's release
-    if (threadIdx.x == 0) {
-        const unsigned prev = atom_add_acq_rel_gpu(fp.bar_count, 1u);
-        const unsigned target = base + unsigned(k);
-        if (prev == unsigned(k) * gridDim.x - 1u) {
-            if (last) *fp.bar_count = 0u;
-            st_release_gpu_u32(fp.bar_gen, target);
-        } else {
-            const unsigned long long t0 = gtime_ns();
-            while (int(ld_acquire_gpu_u32(fp.bar_gen) - target) < 0) {
-                if (gtime_ns() - t0 > fp.timeout_ns) {
-                    atomicExch(fp.err, 5);
-                    break;
-                }
-            }
-        }
-    }
-    __syncthreads();   // ... and the other CTAs' writes happen before this CTA's later reads
-}
-
-__device__ __forceinline__ void epilogue_rt(const Params& p, int epi, int tile, const float (&c)[4], int g, int t) {
-    switch (epi) {
-        case EPI_RESIDUAL: epilogue<EPI_RESIDUAL>(p, tile, c, g, t); break;
-        case EPI_SILU_MUL: epilogue<EPI_SILU_MUL>(p, tile, c, g, t); break;
-        case EPI_F32: epilogue<EPI_F32>(p, tile, c, g, t); break;
-        default: epilogue<EPI_PLAIN>(p, tile, c, g, t); break;
-    }
-}
-
-__device__ __forceinline__ void named_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-// q/k norm + RoPE (+ ring write and group requantization for KV heads) of one
-// (head, batch row) by 128 threads (d = channel) on named barrier `bar`:
-// the same arithmetic, in the same order, as qk_norm_rope_append_kernel.
-__device__ void qk_item(const QkPhase& q, float eps, int head, int m, int d, int bar, float* red4, __half* ybuf) {
-    const int64_t pos = *q.pos;
-    if (m == 0 && head == 0 && d == 0) {
-        const int64_t w = pos + 1;
-        const int64_t ql = (w / 64) * 64;
-        *q.written = w;
-        *q.qlen = ql;
-        *q.pg = ql / 64;
-    }
-    const bool is_q = head < q.q_heads;
-    const int kvh = head - q.q_heads;
-    const __half* src = q.qkv + m * q.qkv_stride + int64_t(head) * 128;
-    const __half* nw = is_q ? q.q_norm_w : q.k_norm_w;
-    const float x = __half2float(__ldcg(src + d));   // written by other CTAs in the previous phase
-    float v = x * x;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    named_sync(bar, 128);   // red4 / ybuf may still be read by the previous item
-    if ((d & 31) == 0) red4[d >> 5] = v;
-    named_sync(bar, 128);
-    const float total = red4[0] + red4[1] + red4[2] + red4[3];
-    const float r = rsqrt_ieee(__fdiv_rn(total, 128.0f) + eps);
-    const float hn = __half2float(__float2half_rn(x * r));
-    const __half y = __float2half_rn(__half2float(nw[d]) * hn);
-    ybuf[d] = y;
-    named_sync(bar, 128);
-    const float yr = d < 64 ? -__half2float(ybuf[d + 64]) : __half2float(ybuf[d - 64]);
-    const int64_t cp = pos < q.rope_len ? pos : q.rope_len - 1;
-    const float cc = __half2float(q.cos[cp * 128 + d]), ss = __half2float(q.sin[cp * 128 + d]);
-    const float a = __half2float(__float2half_rn(__half2float(y) * cc));
-    const float b = __half2float(__float2half_rn(yr * ss));
-    const __half emb = __float2half_rn(a + b);
-    if (is_q) {
-        q.q_out[m * q.q_out_stride + int64_t(head) * 128 + d] = emb;
-        return;
-    }
-    if (pos < 0 || pos >= q.max_len) return;
-    const __half vv = __ldcg(q.qkv + m * q.qkv_stride + int64_t(q.q_heads + q.kv_heads + kvh) * 128 + d);
-    const int64_t bh = int64_t(m) * q.kv_heads + kvh;
-    const int slot = int(pos % 64);
-    __half* tk = q.tail_k + bh * 64 * 128;
-    __half* tv = q.tail_v + bh * 64 * 128;
-    tk[slot * 128 + d] = emb;
-    tv[slot * 128 + d] = vv;
-    if (slot != 63) return;
-    named_sync(bar, 128);   // every channel of the ring row is written before the group is requantized
-    const int64_t grp = pos / 64;
-    const int64_t ngroups = (q.max_len + 63) / 64;
-    const int64_t code_off = bh * q.max_len * 128 + grp * 64 * 128 + d;
-    const int64_t sc_off = (bh * ngroups + grp) * 128 + d;
-    for (int pass = 0; pass < 2; ++pass) {
-        const __half* col = (pass ? tv : tk) + d;
-        uint8_t* qd = (pass ? q.vq : q.kq) + code_off;
-        float mn = INFINITY, mx = -INFINITY;
-        for (int tt = 0; tt < 64; ++tt) {
-            const float e = __half2float(col[tt * 128]);
-            mn = fminf(mn, e);
-            mx = fmaxf(mx, e);
-        }
-        const float step = fmaxf(__fdiv_rn(mx - mn, 255.0f), 1e-8f);
-        for (int tt = 0; tt < 64; ++tt) {
-            float cq = rintf(__fdiv_rn(__half2float(col[tt * 128]) - mn, step));
-            cq = fminf(fmaxf(cq, 0.0f), 255.0f);
-            qd[tt * 128] = static_cast<uint8_t>(cq);
-        }
-        (pass ? q.vmn : q.kmn)[sc_off] = __float2half_rn(mn);
-        (pass ? q.vst : q.kst)[sc_off] = __float2half_rn(step);
-    }
-}
-
-__global__ void __launch_bounds__(NAT_THREADS, 1) nf4_fused_phases_kernel(const __grid_constant__ FusedParams fp) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t bars[NAT_WARPS][NAT_STAGES];
-    __shared__ __align__(8) uint64_t bar_full[2], bar_empty[2];
-    __shared__ float qk_red[4][4];
-    __shared__ __align__(16) __half qk_y[4][128];
-    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
-    __half* xs = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
-    float4* red = reinterpret_cast<float4*>(smem_raw + LUT_BYTES + fp.xs_bytes);
-    const int su = fp.stage_units;
-    const int stage_bytes = su * UNIT_BYTES;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint8_t* ring = smem_raw + LUT_BYTES + fp.xs_bytes + 2 * NAT_WARPS * 32 * 32 + size_t(warp) * NAT_STAGES * stage_bytes;
-    const int c = blockIdx.x, G = gridDim.x;
-    const unsigned base = *fp.bar_gen;   // generations published by earlier launches
-
-    // This CTA's row groups of GEMV phase ph, and this warp's k-block slice of each.
-    auto groups = [&](int ph, int& r0, int& r1) {
-        const int n_rg = fp.g[ph].N / UNIT_ROWS;
-        r0 = int(int64_t(n_rg) * c / G);
-        r1 = int(int64_t(n_rg) * (c + 1) / G);
-    };
-    auto warp_slice = [&](int ph, int& a, int& b) {
-        const int KB = fp.g[ph].K / 64;
-        a = KB * warp / NAT_WARPS;
-        b = KB * (warp + 1) / NAT_WARPS;
-    };
-    // issue cursor: (phase, row group, block) of the next chunk to request (lane 0)
-    int is_ph = -1, is_rg = 0, is_r1 = 0, is_off = 0, is_a = 0, is_b = 0;
-    auto advance_phase = [&](int from) {   // first GEMV phase >= from with work for this warp
-        for (int ph = from; ph < fp.n_phases; ++ph) {
-            if (fp.kind[ph] != PH_GEMV) continue;
-            int r0, r1, a, b;
-            groups(ph, r0, r1);
-            warp_slice(ph, a, b);
-            if (r0 < r1 && a < b) {
-                is_ph = ph; is_rg = r0; is_r1 = r1; is_a = a; is_b = b; is_off = a;
-                return;
-            }
-        }
-        is_ph = fp.n_phases;
-    };
-    int issued = 0, consumed = 0;
-    auto issue_next = [&]() {   // lane 0; false when nothing is left in the program
-        if (is_ph >= fp.n_phases) return false;
-        if (is_off >= is_b) {
-            if (++is_rg >= is_r1) {
-                advance_phase(is_ph + 1);
-                if (is_ph >= fp.n_phases) return false;
-            } else {
-                is_off = is_a;
-            }
-        }
-        const int KB = fp.g[is_ph].K / 64;
-        const int cnt = min(su, is_b - is_off);
-        const int st = issued % NAT_STAGES;
-        uint64_t* bar = &bars[warp][st];
-        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
-        mbar_arrive_expect_tx(bar, bytes);
-        bulk_g2s(ring + st * stage_bytes, fp.g[is_ph].units + (int64_t(is_rg) * KB + is_off) * UNIT_BYTES, bytes, bar);
-        is_off += cnt;
-        ++issued;
-        return true;
-    };
-
-    if (lane == 0) {
-#pragma unroll
-        for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
-        if (warp == 0) {
-            mbar_init(&bar_full[0], NAT_WARPS);
-            mbar_init(&bar_full[1], NAT_WARPS);
-            mbar_init(&bar_empty[0], 1);
-            mbar_init(&bar_empty[1], 1);
-        }
-        fence_mbar_init();
-        advance_phase(0);
-        for (int k = 0; k < NAT_STAGES; ++k)
-            if (!issue_next()) break;
-    }
-    build_lut<NAT_THREADS>(lut_s, fp.lut);
-    __syncthreads();
-
-    const uint32_t lut_base = smem_u32(lut_s);
-    const uint32_t laneword = uint32_t(lane) << 2;
-    const bool xlane = g < fp.M;
-    int jseg = 0;   // reduction segments (row groups) of this CTA so far
-    bool ok = true;
-
-    for (int ph = 0; ph < fp.n_phases && ok; ++ph) {
-        if (ph > 0) grid_barrier(fp, base, ph, ph == fp.n_phases - 1);
-        if (fp.kind[ph] == PH_QK) {
-            const int sub = threadIdx.x >> 7, d = threadIdx.x & 127;
-            const int heads = fp.qk.q_heads + fp.qk.kv_heads;
-            const int items = heads * fp.M;
-            for (int it = c * 4 + sub; it < items; it += G * 4)
-                qk_item(fp.qk, fp.eps, it % heads, it / heads, d, 1 + sub, qk_red[sub], qk_y[sub]);
-            continue;
-        }
-        const GemvPhase& gp = fp.g[ph];
-        Params p;
-        p.x = gp.x;
-        p.x_stride = gp.x_stride;
-        p.norm_w = gp.norm_w;
-        p.eps = fp.eps;
-        p.bias = nullptr;
-        p.residual = gp.residual;
-        p.res_stride = gp.res_stride;
-        p.out = gp.out;
-        p.out_stride = gp.out_stride;
-        p.argmax = nullptr;
-        p.M = fp.M;
-        p.N = gp.N;
-        p.K = gp.K;
-        p.KB = gp.K / 64;
-        stage_x<NAT_THREADS>(p, xs);
-        __syncthreads();
-        const __half* xrow = xs + (xlane ? g : 0) * p.K + 16 * t;
-        int r0, r1, a, b;
-        groups(ph, r0, r1);
-        warp_slice(ph, a, b);
-        for (int rg = r0; rg < r1 && ok; ++rg, ++jseg) {
-            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            uint32_t xb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-            for (int off = a; off < b;) {
-                const int cnt = min(su, b - off);
-                const int st = consumed % NAT_STAGES;
-                if (!mbar_wait(&bars[warp][st], uint32_t((consumed / NAT_STAGES) & 1), fp.err, 2)) {
-                    ok = false;
-                    break;
-                }
-                const uint8_t* sbuf = ring + st * stage_bytes;
-                for (int jj = 0; jj < cnt; ++jj) {
-                    const int blk = off + jj;
-                    if (xlane) {
-                        const uint4 x0 = lds128(xrow + 64 * blk), x1 = lds128(xrow + 64 * blk + 8);
-                        xb[0] = x0.x; xb[1] = x0.y; xb[2] = x0.z; xb[3] = x0.w;
-                        xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
-                    }
-                    mma_unit_smem(sbuf + jj * UNIT_BYTES, xb, lut_base, laneword, lane, g, acc);
-                }
-                ++consumed;
-                off += cnt;
-                __syncwarp();
-                if (lane == 0) {
-                    fence_proxy_async();
-                    issue_next();
-                }
-            }
-            if (!ok) break;
-            // two reduction buffers: segment j uses buffer j & 1, whose previous use (segment j - 2) must
-            // have been read by its reducer
-            const int rb = jseg & 1;
-            float4* rbuf = red + rb * NAT_WARPS * 32 * 2;
-            if (jseg >= 2 && !mbar_wait(&bar_empty[rb], uint32_t(((jseg - 2) >> 1) & 1), fp.err, 3)) {
-                ok = false;
-                break;
-            }
-            rbuf[(warp * 32 + lane) * 2] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-            rbuf[(warp * 32 + lane) * 2 + 1] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_full[rb]);
-            if (warp == (jseg & (NAT_WARPS - 1))) {
-                if (!mbar_wait(&bar_full[rb], uint32_t((jseg >> 1) & 1), fp.err, 3)) {
-                    ok = false;
-                    break;
-                }
-                float r[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 4
-                for (int ww = 0; ww < NAT_WARPS; ++ww) {
-                    const float4 v0 = rbuf[(ww * 32 + lane) * 2], v1 = rbuf[(ww * 32 + lane) * 2 + 1];
-                    r[0][0] += v0.x; r[0][1] += v0.y; r[0][2] += v0.z; r[0][3] += v0.w;
-                    r[1][0] += v1.x; r[1][1] += v1.y; r[1][2] += v1.z; r[1][3] += v1.w;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_empty[rb]);
-                epilogue_rt(p, gp.epi, 2 * rg, r[0], g, t);
-                epilogue_rt(p, gp.epi, 2 * rg + 1, r[1], g, t);
-            }
-        }
-        // the next phase reads xs again: every warp is done with this one
-        __syncthreads();
-    }
-    // copies requested ahead but never consumed (a wait gave up) must land before exit
-    if (lane == 0)
-        for (; consumed < issued; ++consumed)
-            mbar_wait(&bars[warp][consumed % NAT_STAGES], uint32_t((consumed / NAT_STAGES) & 1), fp.err, 2);
-}
-
-// ---------------------------------------------------------------------------
-// q|k|v projection fused with q/k norm + RoPE + int8 KV append: one CTA per
-// head (q heads, then k heads, then v heads of the q|k|v weight), owning the
-// head's four 32-row groups.  The 16 warps split each group's k-blocks exactly
-// like the CTA-level GEMV; the reduced head (fp16, as the plain epilogue would
-// store it) stays in shared memory, and the CTA then applies q_norm / k_norm
-// and RoPE (q -> q_out, k -> ring) or copies v into the ring, requantizing the
-// 64-token group when this step completes it.  Same arithmetic as
-// nf4_gemv_cta_kernel followed by qk_norm_rope_append_kernel.
-
-// post-processing of one (head, row) by 128 threads on named barrier `bar`
-__device__ void head_post(const QkPhase& q, float eps, int head, int m, int d, int bar, const __half* hv,
-                          float* red4, __half* ybuf) {
-    const int64_t pos = *q.pos;
-    if (m == 0 && head == 0 && d == 0) {
-        const int64_t w = pos + 1;
-        const int64_t ql = (w / 64) * 64;
-        *q.written = w;
-        *q.qlen = ql;
-        *q.pg = ql / 64;
-    }
-    const int kind = head < q.q_heads ? 0 : (head < q.q_heads + q.kv_heads ? 1 : 2);   // q / k / v
-    const __half val = hv[d];
-    __half emb = val;
-    if (kind < 2) {
-        const __half* nw = kind == 0 ? q.q_norm_w : q.k_norm_w;
-        const float x = __half2float(val);
-        float v = x * x;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        named_sync(bar, 128);
-        if ((d & 31) == 0) red4[d >> 5] = v;
-        named_sync(bar, 128);
-        const float total = red4[0] + red4[1] + red4[2] + red4[3];
-        const float r = rsqrt_ieee(__fdiv_rn(total, 128.0f) + eps);
-        const float hn = __half2float(__float2half_rn(x * r));
-        const __half y = __float2half_rn(__half2float(nw[d]) * hn);
-        ybuf[d] = y;
-        named_sync(bar, 128);
-        const float yr = d < 64 ? -__half2float(ybuf[d + 64]) : __half2float(ybuf[d - 64]);
-        const int64_t cp = pos < q.rope_len ? pos : q.rope_len - 1;
-        const float cc = __half2float(q.cos[cp * 128 + d]), ss = __half2float(q.sin[cp * 128 + d]);
-        const float a = __half2float(__float2half_rn(__half2float(y) * cc));
-        const float b = __half2float(__float2half_rn(yr * ss));
-        emb = __float2half_rn(a + b);
-    }
-    if (kind == 0) {
-        q.q_out[m * q.q_out_stride + int64_t(head) * 128 + d] = emb;
-        return;
-    }
-    if (pos < 0 || pos >= q.max_len) return;
-    const int kvh = head - q.q_heads - (kind == 2 ? q.kv_heads : 0);
-    const int64_t bh = int64_t(m) * q.kv_heads + kvh;
-    const int slot = int(pos % 64);
-    __half* ring = (kind == 1 ? q.tail_k : q.tail_v) + bh * 64 * 128;
-    ring[slot * 128 + d] = emb;
-    if (slot != 63) return;
-    named_sync(bar, 128);   // the whole ring row is written before the group is requantized
-    const int64_t grp = pos / 64;
-    const int64_t ngroups = (q.max_len + 63) / 64;
-    const int64_t code_off = bh * q.max_len * 128 + grp * 64 * 128 + d;
-    const int64_t sc_off = (bh * ngroups + grp) * 128 + d;
-    const __half* col = ring + d;
-    uint8_t* qd = (kind == 1 ? q.kq : q.vq) + code_off;
-    float mn = INFINITY, mx = -INFINITY;
-    for (int tt = 0; tt < 64; ++tt) {
-        const float e = __half2float(col[tt * 128]);
-        mn = fminf(mn, e);
-        mx = fmaxf(mx, e);
-    }
-    const float step = fmaxf(__fdiv_rn(mx - mn, 255.0f), 1e-8f);
-    for (int tt = 0; tt < 64; ++tt) {
-        float cq = rintf(__fdiv_rn(__half2float(col[tt * 128]) - mn, step));
-        cq = fminf(fmaxf(cq, 0.0f), 255.0f);
-        qd[tt * 128] = static_cast<uint8_t>(cq);
-    }
-    (kind == 1 ? q.kmn : q.vmn)[sc_off] = __float2half_rn(mn);
-    (kind == 1 ? q.kst : q.vst)[sc_off] = __float2half_rn(step);
-}
-
-__global__ void __launch_bounds__(NAT_THREADS, 1)
-    nf4_qkv_heads_kernel(const __grid_constant__ Params p, const __grid_constant__ QkPhase q, int stage_units,
-                         int* err) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t bars[NAT_WARPS][NAT_STAGES];
-    __shared__ __align__(8) uint64_t bar_full[2], bar_empty[2];
-    __shared__ float qk_red[4][4];
-    __shared__ __align__(16) __half qk_y[4][128];
-    __shared__ __align__(16) __half head_out[MAX_M][128];
-    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
-    __half* xs = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
-    const int xs_bytes = (p.M * p.K * 2 + 127) / 128 * 128;
-    float4* red = reinterpret_cast<float4*>(smem_raw + LUT_BYTES + xs_bytes);   // [2][16][32][2]
-    const int su = stage_units;
-    const int stage_bytes = su * UNIT_BYTES;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint8_t* ring = smem_raw + LUT_BYTES + xs_bytes + 2 * NAT_WARPS * 32 * 32 + size_t(warp) * NAT_STAGES * stage_bytes;
-    const int head = blockIdx.x;
-    const int KB = p.KB;
-    const int a = KB * warp / NAT_WARPS, b = KB * (warp + 1) / NAT_WARPS;   // this warp's k-blocks of every group
-    const int rg0 = 4 * head;
-
-    int is_j = 0, is_off = a, issued = 0, consumed = 0;
-    auto issue_next = [&]() {   // lane 0
-        if (a >= b) return false;
-        if (is_off >= b) {
-            if (++is_j >= 4) return false;
-            is_off = a;
-        }
-        const int cnt = min(su, b - is_off);
-        const int st = issued % NAT_STAGES;
-        uint64_t* bar = &bars[warp][st];
-        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
-        mbar_arrive_expect_tx(bar, bytes);
-        bulk_g2s(ring + st * stage_bytes, p.packed + (int64_t(rg0 + is_j) * KB + is_off) * UNIT_BYTES, bytes, bar);
-        is_off += cnt;
-        ++issued;
-        return true;
-    };
-    if (lane == 0) {
-#pragma unroll
-        for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
-        if (warp == 0) {
-            mbar_init(&bar_full[0], NAT_WARPS);
-            mbar_init(&bar_full[1], NAT_WARPS);
-            mbar_init(&bar_empty[0], 1);
-            mbar_init(&bar_empty[1], 1);
-        }
-        fence_mbar_init();
-        for (int k = 0; k < NAT_STAGES; ++k)
-            if (!issue_next()) break;
-    }
-    build_lut<NAT_THREADS>(lut_s, p.lut);
-    pdl_trigger();
-    pdl_wait();
-    stage_x<NAT_THREADS>(p, xs);
-    __syncthreads();
-
-    const uint32_t lut_base = smem_u32(lut_s);
-    const uint32_t laneword = uint32_t(lane) << 2;
-    const bool xlane = g < p.M;
-    const __half* xrow = xs + (xlane ? g : 0) * p.K + 16 * t;
-    bool ok = true;
-    for (int j = 0; j < 4 && ok; ++j) {
-        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        uint32_t xb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-        for (int off = a; off < b;) {
-            const int cnt = min(su, b - off);
-            const int st = consumed % NAT_STAGES;
-            if (!mbar_wait(&bars[warp][st], uint32_t((consumed / NAT_STAGES) & 1), err, 2)) {
-                ok = false;
-                break;
-            }
-            const uint8_t* sbuf = ring + st * stage_bytes;
-            for (int jj = 0; jj < cnt; ++jj) {
-                const int blk = off + jj;
-                if (xlane) {
-                    const uint4 x0 = lds128(xrow + 64 * blk), x1 = lds128(xrow + 64 * blk + 8);
-                    xb[0] = x0.x; xb[1] = x0.y; xb[2] = x0.z; xb[3] = x0.w;
-                    xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
-                }
-                mma_unit_smem(sbuf + jj * UNIT_BYTES, xb, lut_base, laneword, lane, g, acc);
-            }
-            ++consumed;
-            off += cnt;
-            __syncwarp();
-            if (lane == 0) {
-                fence_proxy_async();
-                issue_next();
-            }
-        }
-        if (!ok) break;
-        const int rb = j & 1;
-        float4* rbuf = red + rb * NAT_WARPS * 32 * 2;
-        if (j >= 2 && !mbar_wait(&bar_empty[rb], 0u, err, 3)) {
-            ok = false;
-            break;
-        }
-        rbuf[(warp * 32 + lane) * 2] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-        rbuf[(warp * 32 + lane) * 2 + 1] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar_full[rb]);
-        if (warp == j) {   // reducer of group j
-            if (!mbar_wait(&bar_full[rb], uint32_t(j >> 1), err, 3)) {
-                ok = false;
-                break;
-            }
-            float r[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 4
-            for (int ww = 0; ww < NAT_WARPS; ++ww) {
-                const float4 v0 = rbuf[(ww * 32 + lane) * 2], v1 = rbuf[(ww * 32 + lane) * 2 + 1];
-                r[0][0] += v0.x; r[0][1] += v0.y; r[0][2] += v0.z; r[0][3] += v0.w;
-                r[1][0] += v1.x; r[1][1] += v1.y; r[1][2] += v1.z; r[1][3] += v1.w;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_empty[rb]);
-#pragma unroll
-            for (int tile = 0; tile < 2; ++tile)
-#pragma unroll
-                for (int hrow = 0; hrow < 2; ++hrow)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int m = 2 * t + e;
-                        if (m < p.M) head_out[m][j * 32 + tile * 16 + g + 8 * hrow] = __float2half_rn(r[tile][2 * hrow + e]);
-                    }
-        }
-    }
-    if (!ok && lane == 0)
-        for (; consumed < issued; ++consumed)
-            mbar_wait(&bars[warp][consumed % NAT_STAGES], uint32_t((consumed / NAT_STAGES) & 1), err, 2);
-    __syncthreads();
-    if (!ok) return;
-    const int sub = threadIdx.x >> 7, d = threadIdx.x & 127;
-    for (int m = sub; m < p.M; m += 4) head_post(q, p.eps, head, m, d, 1 + sub, head_out[m], qk_red[sub], qk_y[sub]);
-}
-
-// ---------------------------------------------------------------------------
-// Batched NF4 GEMM (M <= 64 rows, native layout): y = x @ dequant(W)^T.
-// CTA = 16 warps = 512 output rows (warp w owns 32-row group 16*tile + w);
-// blockIdx.y splits the k-blocks (split-K) so every SM has work.  Per 64-wide
-// k-block all warps share one x tile [M x 64] staged by cp.async into padded
-// shared memory (rows 136 bytes apart: the 8-byte B-fragment loads of a
-// half-warp hit distinct bank pairs); each warp's weight units arrive through
-// its bulk-copy ring.  A fragments are decoded through the LUT and scaled by
-// the block's absmax in fp16 -- fp16(code * absmax), the reference's
-// dequantized weight -- and reused across up to 8 mma.sync column groups of 8
-// batch rows, accumulating in fp32.  Split-K partials go to workspace slots;
-// the last CTA of a tile adds them in split order (deterministic) and runs the
-// epilogue.  Row-wise RMSNorm is not fused here (normalize x first).
-
-constexpr int GM_WARPS = 16;
-constexpr int GM_THREADS = GM_WARPS * 32;
-constexpr int GM_MAX_M = 64;
-constexpr int GM_XSTRIDE = 68;   // halves per staged x row
-constexpr int GM_XBUF = 3;
-constexpr int GM_SLOT_FLOATS = GM_WARPS * 32 * 64;
-
-__device__ __forceinline__ uint32_t dup_lo(uint32_t v) { return __byte_perm(v, 0, 0x1010); }
-__device__ __forceinline__ uint32_t dup_hi(uint32_t v) { return __byte_perm(v, 0, 0x3232); }
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-
-template <int EPI>
-__global__ void __launch_bounds__(GM_THREADS, 1)
-    nf4_gemm_kernel(const __grid_constant__ Params p, int S, int stage_units, float* part, unsigned* tile_cnt,
-                    unsigned* done, int* err) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t bars[GM_WARPS][NAT_STAGES];
-    __shared__ int s_last;
-    uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem_raw);
-    __half* xt = reinterpret_cast<__half*>(smem_raw + LUT_BYTES);
-    const int xt_elems = p.M * GM_XSTRIDE;
-    const int xt_bytes = (GM_XBUF * xt_elems * 2 + 127) / 128 * 128;
-    const int su = stage_units, stage_bytes = su * UNIT_BYTES;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint8_t* ring = smem_raw + LUT_BYTES + xt_bytes + size_t(warp) * NAT_STAGES * stage_bytes;
-    const int tile = blockIdx.x, split = blockIdx.y;
-    const int KB = p.KB;
-    const int n_rg = p.N / UNIT_ROWS;
-    const int rg = tile * GM_WARPS + warp;
-    const bool has_rg = rg < n_rg;
-    const int kb0 = int(int64_t(KB) * split / S), kb1 = int(int64_t(KB) * (split + 1) / S);
-    const int nkb = kb1 - kb0;
-    const int ncg = (p.M + 7) / 8;
-
-    int issued = 0, is_b = kb0;
-    auto issue_next = [&]() {   // lane 0
-        if (!has_rg || is_b >= kb1) return;
-        const int cnt = min(su, kb1 - is_b);
-        const int st = issued % NAT_STAGES;
-        uint64_t* bar = &bars[warp][st];
-        const uint32_t bytes = uint32_t(cnt) * UNIT_BYTES;
-        mbar_arrive_expect_tx(bar, bytes);
-        bulk_g2s(ring + st * stage_bytes, p.packed + (int64_t(rg) * KB + is_b) * UNIT_BYTES, bytes, bar);
-        is_b += cnt;
-        ++issued;
-    };
-    auto load_x = [&](int i) {   // all threads: k-block kb0 + i into buffer i % GM_XBUF, one commit group
-        if (i < nkb) {
-            __half* dst = xt + (i % GM_XBUF) * xt_elems;
-            const __half* src = p.x + int64_t(kb0 + i) * 64;
-            for (int q = threadIdx.x; q < p.M * 16; q += GM_THREADS) {
-                const int m = q >> 4, j = q & 15;
-                cp_async8(dst + m * GM_XSTRIDE + 4 * j, src + m * p.x_stride + 4 * j);
-            }
-        }
-        cp_async_commit();
-    };
-
-    if (lane == 0) {
-#pragma unroll
-        for (int st = 0; st < NAT_STAGES; ++st) mbar_init(&bars[warp][st], 1);
-        fence_mbar_init();
-        for (int k2 = 0; k2 < NAT_STAGES; ++k2) issue_next();
-    }
-    build_lut<GM_THREADS>(lut_s, p.lut);
-    pdl_trigger();
-    pdl_wait();
-    load_x(0);
-    load_x(1);
-
-    const uint32_t lut_base = smem_u32(lut_s);
-    const uint32_t laneword = uint32_t(lane) << 2;
-    float acc[2][8][4];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[a][c][0] = acc[a][c][1] = acc[a][c][2] = acc[a][c][3] = 0.f;
-    bool ok = true;
-    int waited = 0;
-
-    for (int i = 0; i < nkb; ++i) {
-        cp_async_wait1();
-        __syncthreads();   // x tile i visible to all warps; every warp is done with tile i - 1
-        load_x(i + 2);
-        if (!has_rg || !ok) continue;
-        const int chunk = i / su, pos = i % su;
-        if (pos == 0) {
-            if (!mbar_wait(&bars[warp][chunk % NAT_STAGES], uint32_t((chunk / NAT_STAGES) & 1), err, 2)) {
-                ok = false;
-                continue;
-            }
-            ++waited;
-        }
-        const uint8_t* unit = ring + (chunk % NAT_STAGES) * stage_bytes + pos * UNIT_BYTES;
-        const __half* xb = xt + (i % GM_XBUF) * xt_elems;
-        const uint4 c0 = lds128(unit + 16 * lane), c1 = lds128(unit + 512 + 16 * lane);
-        uint2 am;
-        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(am.x), "=r"(am.y)
-                     : "r"(smem_u32(unit + UNIT_CODE_BYTES + 8 * g)));
-        const uint32_t sc[4] = {dup_lo(am.x), dup_hi(am.x), dup_lo(am.y), dup_hi(am.y)};   // rows g, g+8, g+16, g+24
-        const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) {
-            const int wi = s2 >> 1;
-            const uint32_t sel0 = 0x5504u | (uint32_t((s2 & 1) * 2) << 4);
-            const uint32_t sel1 = sel0 + 0x10u;
-            uint32_t af[2][4];
-#pragma unroll
-            for (int tl = 0; tl < 2; ++tl) {
-                const uint32_t r0w = w[4 * tl + wi], r1w = w[4 * tl + 2 + wi];
-                af[tl][0] = hmul2_u32(lds32(lut_base + __byte_perm(r0w, laneword, sel0)), sc[2 * tl]);
-                af[tl][2] = hmul2_u32(lds32(lut_base + __byte_perm(r0w, laneword, sel1)), sc[2 * tl]);
-                af[tl][1] = hmul2_u32(lds32(lut_base + __byte_perm(r1w, laneword, sel0)), sc[2 * tl + 1]);
-                af[tl][3] = hmul2_u32(lds32(lut_base + __byte_perm(r1w, laneword, sel1)), sc[2 * tl + 1]);
-            }
-#pragma unroll
-            for (int cg = 0; cg < 8; ++cg) {
-                if (cg >= ncg) break;
-                const int m = 8 * cg + g;
-                uint2 bv = make_uint2(0u, 0u);
-                if (m < p.M)
-                    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(bv.x), "=r"(bv.y)
-                                 : "r"(smem_u32(xb + m * GM_XSTRIDE + 16 * t + 4 * s2)));
-                mma_16816(acc[0][cg], af[0][0], af[0][1], af[0][2], af[0][3], bv.x, bv.y);
-                mma_16816(acc[1][cg], af[1][0], af[1][1], af[1][2], af[1][3], bv.x, bv.y);
-            }
-        }
-        if (pos == su - 1 || i == nkb - 1) {
-            __syncwarp();
-            if (lane == 0) {
-                fence_proxy_async();
-                issue_next();
-            }
-        }
-    }
-    if (lane == 0)   // copies issued but never waited for (only after a failed wait) land before exit
-        for (int c = waited; c < issued; ++c)
-            mbar_wait(&bars[warp][c % NAT_STAGES], uint32_t((c / NAT_STAGES) & 1), err, 2);
-    asm volatile("cp.async.wait_all;" ::: "memory");
-
-    // split-K: every split CTA stores its fragments, the S CTAs of the tile meet (cooperative launch:
-    // all resident; the wait is bounded), then CTA `split` adds, in split order, the fragments of its
-    // share of the tile's row groups (warps [16*split/S, 16*(split+1)/S)) and runs their epilogue.
-    bool reducer = has_rg;
-    if (S > 1) {
-        float4* slot = reinterpret_cast<float4*>(part) + ((int64_t(tile) * S + split) * GM_WARPS * 32 + warp * 32 + lane) * 16;
-#pragma unroll
-        for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                if (c < ncg) slot[a * 8 + c] = make_float4(acc[a][c][0], acc[a][c][1], acc[a][c][2], acc[a][c][3]);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned* arrive = tile_cnt + 2 * tile;
-            unsigned* depart = arrive + 1;
-            __threadfence();
-            atomicAdd(arrive, 1u);
-            const unsigned long long t0 = gtime_ns();
-            while (ld_acquire_gpu_u32(arrive) < unsigned(S)) {
-                if (gtime_ns() - t0 > 1000000000ull) {
-                    atomicExch(err, 6);
-                    break;
-                }
-            }
-            __threadfence();
-            if (atomicAdd(depart, 1u) == unsigned(S - 1)) {   // every CTA of the tile is past the wait
-                *arrive = 0u;
-                *depart = 0u;
-            }
-        }
-        __syncthreads();
-        reducer = has_rg && warp >= GM_WARPS * split / S && warp < GM_WARPS * (split + 1) / S;
-        if (reducer) {
-#pragma unroll
-            for (int a = 0; a < 2; ++a)
-#pragma unroll
-                for (int c = 0; c < 8; ++c) acc[a][c][0] = acc[a][c][1] = acc[a][c][2] = acc[a][c][3] = 0.f;
-            for (int sp = 0; sp < S; ++sp) {
-                const float4* src = reinterpret_cast<const float4*>(part) + ((int64_t(tile) * S + sp) * GM_WARPS * 32 + warp * 32 + lane) * 16;
-                float4 v[16];
-#pragma unroll
-                for (int q = 0; q < 16; ++q) v[q] = (q % 8) < ncg ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    float* a4 = acc[q / 8][q % 8];
-                    a4[0] += v[q].x; a4[1] += v[q].y; a4[2] += v[q].z; a4[3] += v[q].w;
-                }
-            }
-        }
-    }
-    if (reducer) {
-#pragma unroll
-        for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                if (c < ncg) epilogue<EPI>(p, 2 * rg + a, acc[a][c], g, t, 8 * c);
-    }
-    if (EPI == EPI_ARGMAX && p.token_out) {   // the last CTA to finish runs the step finalize
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x * gridDim.y - 1u;
-        __syncthreads();
-        if (s_last && warp == 0) {
-            __threadfence();
-            finalize_step(p, lane);
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------
 // Batched NF4 GEMM on the tcgen05 tensor cores (M = 1..64 batch rows).
 //
 // Tile = 128 weight rows (four 32-row groups) x all batch rows; the MMA is
@@ -1728,6 +892,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 //                   all partials in CTA order -- deterministic -- and runs it.
 // Every wait is bounded; on a failed wait the roles stop, the MMA thread
 // waits for its MMAs and the producer for its copies before TMEM is freed.
+
+__device__ __forceinline__ uint32_t dup_lo(uint32_t v) { return __byte_perm(v, 0, 0x1010); }
+__device__ __forceinline__ uint32_t dup_hi(uint32_t v) { return __byte_perm(v, 0, 0x3232); }
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
 
 constexpr int TC_ROWS = 128;
 constexpr int TC_GROUPS = 3;                       // decode warp groups (item j -> group j % 3)
@@ -2191,10 +1363,31 @@ using namespace nova::nf4;
 static int64_t max_warps() { return int64_t(sm_count()) * 16; }
 static int64_t partial_bytes() { return max_warps() * 2 * 32 * 32; }
 
+static int* gemv_error_word(void* ws) { return reinterpret_cast<int*>((uint8_t*)ws + partial_bytes() + 4); }
+
+// Copy a device error word to the host and clear it when set (synchronous).
+static int read_error_word(int* dev_word, int* host_value, const char* what) {
+    if (!dev_word || !host_value) return fail(NOVA_ERR_INVALID, "NULL argument");
+    if (cudaMemcpy(host_value, dev_word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "reading the %s error word failed", what);
+    }
+    if (*host_value && cudaMemset(dev_word, 0, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "clearing the %s error word failed", what);
+    }
+    return NOVA_OK;
+}
+
+extern "C" int nova_nf4_gemv_read_error(void* workspace, int* host_value) {
+    if (!workspace) return fail(NOVA_ERR_INVALID, "NULL workspace");
+    return read_error_word(gemv_error_word(workspace), host_value, "GEMV");
+}
+
 extern "C" int nova_nf4_workspace_bytes(int64_t n, int64_t* bytes) {
     if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
     if (n <= 0 || n % 16) return fail(NOVA_ERR_INVALID, "N must be a positive multiple of 16");
-    *bytes = partial_bytes() + ((n / 16) * 4 + 8 + 255) / 256 * 256;   // counters, done, error word
+    *bytes = partial_bytes() + 256 + ((n / 16) * 4 + 255) / 256 * 256;   // done + error word, counters
     return NOVA_OK;
 }
 
@@ -2236,12 +1429,14 @@ extern "C" int nova_nf4_pack_tc(const void* packed, const void* absmax, int absm
 }
 
 template <typename Kern>
-static int prepare_smem(Kern kern, int64_t smem, int64_t* set_to) {
+static int prepare_smem(Kern kern, int64_t smem, int64_t (&set_to_per_device)[kMaxDevices]) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return fail(NOVA_ERR_CUDA, "no usable current device (%d)", dev);
+    int64_t* set_to = &set_to_per_device[dev];   // the attribute is per device
     if (smem <= *set_to) return NOVA_OK;
-    int dev = 0, optin = 0;
+    int optin = 0;
     cudaFuncAttributes fa;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
         cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
         cudaGetLastError();
         return fail(NOVA_ERR_CUDA, "querying shared-memory limits failed");
@@ -2329,8 +1524,10 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     p.n_tiles = int(n / 16);
     uint8_t* ws = (uint8_t*)a->workspace;
     p.partial = (float4*)ws;
-    p.counters = (unsigned*)(ws + partial_bytes());
-    p.done = p.counters + p.n_tiles;
+    // [partial slots | finalize counter, error word (fixed offsets: every shape that shares the
+    //  workspace finds them at the same place) | per-row-tile counters]
+    p.done = (unsigned*)(ws + partial_bytes());
+    p.counters = (unsigned*)(ws + partial_bytes() + 256);
 
     using Kern = void (*)(Params);
     cudaError_t err;
@@ -2341,7 +1538,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
              nf4_gemv_native_kernel<3, false>, nf4_gemv_native_kernel<4, false>},
             {nf4_gemv_native_kernel<0, true>, nf4_gemv_native_kernel<1, true>, nf4_gemv_native_kernel<2, true>,
              nf4_gemv_native_kernel<3, true>, nf4_gemv_native_kernel<4, true>}};
-        static int64_t smem_set[2][5] = {};
+        static int64_t smem_set[2][5][kMaxDevices] = {};
         static int optin = 0;
         if (!optin) {
             int dev = 0;
@@ -2372,7 +1569,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
             return fail(NOVA_ERR_UNSUPPORTED, "M*K = %lld with the norm prologue leaves no shared memory for the "
                                               "weight ring", (long long)(m * k));
         p.units = int64_t(n / UNIT_ROWS) * p.KB;
-        int* errp = reinterpret_cast<int*>(p.done + 1);
+        int* errp = gemv_error_word(ws);
         // Warp-level stream-K from two row groups per SM up (gate/up, the
         // lm_head: with several row groups per CTA the CTA-level schedule
         // would synchronise its 16 warps once per row group); CTA-level
@@ -2381,7 +1578,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         if (warp_level) {
             NKern kern = kernels[xg][epi];
             const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + stage_units * ring_unit;
-            if (int rc = prepare_smem(kern, nsmem, &smem_set[xg][epi])) return rc;
+            if (int rc = prepare_smem(kern, nsmem, smem_set[xg][epi])) return rc;
             const int64_t want = (p.units + NAT_MIN_UNITS - 1) / NAT_MIN_UNITS;
             p.total_warps = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sm_count()) * NAT_WARPS, want)));
             const unsigned grid = unsigned(std::min<int64_t>(sm_count(), p.total_warps));
@@ -2393,7 +1590,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
                  nf4_gemv_cta_kernel<3, false>, nf4_gemv_cta_kernel<4, false>},
                 {nf4_gemv_cta_kernel<0, true>, nf4_gemv_cta_kernel<1, true>, nf4_gemv_cta_kernel<2, true>,
                  nf4_gemv_cta_kernel<3, true>, nf4_gemv_cta_kernel<4, true>}};
-            static int64_t cta_smem_set[2][5] = {};
+            static int64_t cta_smem_set[2][5][kMaxDevices] = {};
             const int64_t red_bytes = int64_t(NAT_WARPS) * 32 * 32;
             const int64_t grid = std::min<int64_t>(sm_count(), n / UNIT_ROWS);
             const int64_t rg_max = (n / UNIT_ROWS + grid - 1) / grid;   // row groups of the largest CTA share
@@ -2407,7 +1604,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
                             (long long)(m * k));
             NKern kern = cta_kernels[xg][epi];
             const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + red_bytes + res_bytes + cu * ring_unit;
-            if (int rc = prepare_smem(kern, nsmem, &cta_smem_set[xg][epi])) return rc;
+            if (int rc = prepare_smem(kern, nsmem, cta_smem_set[xg][epi])) return rc;
             p.total_warps = int(grid);   // contributors and finalize arrivals are counted per CTA
             err = launch(kern, dim3(unsigned(grid)), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p,
                          int(cu), errp);
@@ -2418,10 +1615,10 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
              nf4_gemv_ref_kernel<__half, 3>, nf4_gemv_ref_kernel<__half, 4>},
             {nf4_gemv_ref_kernel<float, 0>, nf4_gemv_ref_kernel<float, 1>, nf4_gemv_ref_kernel<float, 2>,
              nf4_gemv_ref_kernel<float, 3>, nf4_gemv_ref_kernel<float, 4>}};
-        static int64_t smem_set[2][5] = {};
+        static int64_t smem_set[2][5][kMaxDevices] = {};
         const int ai = a->absmax_fp32 ? 1 : 0;
         Kern kern = kernels[ai][epi];
-        if (int rc = prepare_smem(kern, smem, &smem_set[ai][epi])) return rc;
+        if (int rc = prepare_smem(kern, smem, smem_set[ai][epi])) return rc;
         p.units = int64_t(p.n_tiles) * p.KB;
         p.total_warps = int(std::min<int64_t>(int64_t(sm_count()) * REF_WARPS, p.units));
         const unsigned grid = unsigned((p.total_warps + REF_WARPS - 1) / REF_WARPS);
@@ -2462,191 +1659,7 @@ extern "C" int nova_nf4_dequant(const void* packed, const void* absmax, int absm
     return check_launch("nova_nf4_dequant");
 }
 
-// ---------------------------------------------------------------- fused phases (host)
-
-extern "C" int nova_fused_workspace_bytes(int64_t* bytes) {
-    if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
-    *bytes = 256;   // barrier counter, generation, error word
-    return NOVA_OK;
-}
-
-extern "C" int nova_fused_phases(const nova_fused_args* a, void* stream) {
-    if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
-    if (a->n_phases < 1 || a->n_phases > MAX_PHASES) return fail(NOVA_ERR_INVALID, "1..6 phases");
-    if (a->m < 1 || a->m > 2) return fail(NOVA_ERR_UNSUPPORTED, "fused phases take 1 or 2 rows");
-    if (!a->lut || !a->workspace || a->workspace_bytes < 256) return fail(NOVA_ERR_INVALID, "lut / workspace");
-    if (reinterpret_cast<uintptr_t>(a->workspace) % 256) return fail(NOVA_ERR_ALIGN, "workspace 256-byte aligned");
-    FusedParams fp;
-    memset(&fp, 0, sizeof(fp));
-    fp.n_phases = int(a->n_phases);
-    fp.lut = (const uint32_t*)a->lut;
-    fp.eps = float(a->eps);
-    fp.M = int(a->m);
-    int64_t max_xs = 0;
-    int n_qk = 0;
-    for (int i = 0; i < fp.n_phases; ++i) {
-        fp.kind[i] = int(a->kind[i]);
-        if (fp.kind[i] == PH_QK) {
-            const nova_qk_args& q = a->qk;
-            if (++n_qk > 1) return fail(NOVA_ERR_INVALID, "at most one q/k phase");
-            if (q.head_dim != 128 || q.group != 64 || q.batch != a->m)
-                return fail(NOVA_ERR_UNSUPPORTED, "q/k phase: head_dim 128, group 64, batch == m");
-            if (!q.qkv || !q.q_norm_weight || !q.k_norm_weight || !q.cos || !q.sin || !q.q_out || !q.tail_k ||
-                !q.tail_v || !q.kq || !q.vq || !q.kmn || !q.kst || !q.vmn || !q.vst || !q.pos || !q.written ||
-                !q.qlen || !q.pg || q.rope_len <= 0 || q.max_len <= 0)
-                return fail(NOVA_ERR_INVALID, "q/k phase: NULL pointer or bad length");
-            QkPhase& o = fp.qk;
-            o.qkv = (const __half*)q.qkv; o.qkv_stride = q.qkv_stride;
-            o.q_norm_w = (const __half*)q.q_norm_weight; o.k_norm_w = (const __half*)q.k_norm_weight;
-            o.cos = (const __half*)q.cos; o.sin = (const __half*)q.sin; o.rope_len = q.rope_len;
-            o.q_out = (__half*)q.q_out; o.q_out_stride = q.q_out_stride;
-            o.tail_k = (__half*)q.tail_k; o.tail_v = (__half*)q.tail_v;
-            o.kq = (uint8_t*)q.kq; o.vq = (uint8_t*)q.vq;
-            o.kmn = (__half*)q.kmn; o.kst = (__half*)q.kst; o.vmn = (__half*)q.vmn; o.vst = (__half*)q.vst;
-            o.pos = q.pos; o.written = q.written; o.qlen = q.qlen; o.pg = q.pg;
-            o.q_heads = int(q.q_heads); o.kv_heads = int(q.kv_heads); o.max_len = q.max_len;
-            continue;
-        }
-        if (fp.kind[i] != PH_GEMV) return fail(NOVA_ERR_INVALID, "phase kind must be 0 or 1");
-        const nova_gemv_phase& g = a->gemv[i];
-        const int epi = int(g.epilogue);
-        if (epi != EPI_PLAIN && epi != EPI_RESIDUAL && epi != EPI_SILU_MUL && epi != EPI_F32)
-            return fail(NOVA_ERR_UNSUPPORTED, "phase %d: epilogue %d not available in fused phases", i, epi);
-        if (g.n <= 0 || g.n % UNIT_ROWS || g.n > (1 << 26) || g.k <= 0 || g.k % 64 || g.k > (1 << 16))
-            return fail(NOVA_ERR_INVALID, "phase %d: N multiple of 32, K multiple of 64", i);
-        if (!g.x || !g.units || !g.out || (epi == EPI_RESIDUAL && !g.residual))
-            return fail(NOVA_ERR_INVALID, "phase %d: NULL pointer", i);
-        auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
-        if (mis(g.x, 16) || (g.x_stride % 8) || mis(g.norm_weight, 16) || mis(g.units, 16) ||
-            (epi == EPI_F32 && mis(g.out, 4)))
-            return fail(NOVA_ERR_ALIGN, "phase %d: x / norm_weight / units 16-byte aligned, x_stride % 8", i);
-        GemvPhase& o = fp.g[i];
-        o.x = (const __half*)g.x; o.x_stride = g.x_stride; o.norm_w = (const __half*)g.norm_weight;
-        o.units = (const uint8_t*)g.units; o.out = (__half*)g.out; o.out_stride = g.out_stride;
-        o.residual = (const __half*)g.residual; o.res_stride = g.res_stride;
-        o.N = int(g.n); o.K = int(g.k); o.epi = epi;
-        max_xs = std::max<int64_t>(max_xs, (a->m * g.k * 2 + 127) / 128 * 128);
-    }
-    int dev = 0, optin = 0, sms = 0, coop = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess) {
-        cudaGetLastError();
-        return fail(NOVA_ERR_CUDA, "device queries failed");
-    }
-    if (!coop) return fail(NOVA_ERR_UNSUPPORTED, "the device does not support cooperative launches");
-    const int64_t ring_unit = int64_t(NAT_WARPS) * NAT_STAGES * UNIT_BYTES;
-    const int64_t red_bytes = 2 * int64_t(NAT_WARPS) * 32 * 32;
-    const int64_t static_smem = 2048;
-    const int64_t su = std::min<int64_t>(3, (optin - int64_t(LUT_BYTES) - max_xs - red_bytes - static_smem) / ring_unit);
-    if (su < 1) return fail(NOVA_ERR_UNSUPPORTED, "fused phases: K too large for shared memory");
-    fp.stage_units = int(su);
-    fp.xs_bytes = int(max_xs);
-    uint8_t* ws = (uint8_t*)a->workspace;
-    fp.bar_count = (unsigned*)ws;
-    fp.bar_gen = (unsigned*)(ws + 4);
-    fp.err = (int*)(ws + 8);
-    fp.timeout_ns = a->timeout_ns > 0 ? (unsigned long long)a->timeout_ns : 1000000000ull;
-    const int64_t nsmem = int64_t(LUT_BYTES) + max_xs + red_bytes + su * ring_unit;
-    static int64_t smem_set = 0;
-    if (int rc = prepare_smem(nf4_fused_phases_kernel, nsmem, &smem_set)) return rc;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, nf4_fused_phases_kernel, NAT_THREADS, size_t(nsmem)) !=
-            cudaSuccess || per_sm < 1) {
-        cudaGetLastError();
-        return fail(NOVA_ERR_UNSUPPORTED, "fused phases: one CTA per SM does not fit");
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(sms));
-    cfg.blockDim = dim3(NAT_THREADS);
-    cfg.dynamicSmemBytes = size_t(nsmem);
-    cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident at once: the grid barriers rely on it
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, nf4_fused_phases_kernel, fp);
-    if (err != cudaSuccess) {
-        cudaGetLastError();
-        return fail(NOVA_ERR_CUDA, "nova_fused_phases: launch failed: %s", cudaGetErrorString(err));
-    }
-    return NOVA_OK;
-}
-
-extern "C" int nova_qkv_norm_rope_append(const nova_nf4_args* g, const nova_qk_args* q, void* stream) {
-    if (!g || !q) return fail(NOVA_ERR_INVALID, "args must not be NULL");
-    if (g->layout != 1) return fail(NOVA_ERR_UNSUPPORTED, "native-layout weights only");
-    const int64_t heads = q->q_heads + 2 * q->kv_heads;
-    if (q->head_dim != 128 || q->group != 64 || q->q_heads <= 0 || q->kv_heads <= 0 || q->q_heads % q->kv_heads)
-        return fail(NOVA_ERR_UNSUPPORTED, "head_dim 128, group 64, q_heads a multiple of kv_heads");
-    if (g->n != heads * 128) return fail(NOVA_ERR_INVALID, "N must be (q_heads + 2*kv_heads) * 128");
-    if (g->m < 1 || g->m > MAX_M || q->batch != g->m) return fail(NOVA_ERR_INVALID, "M in [1, 8] and batch == M");
-    if (g->k <= 0 || g->k % 64 || g->k > (1 << 16)) return fail(NOVA_ERR_INVALID, "K a multiple of 64");
-    if (!g->x || !g->packed || !g->lut || !g->workspace || !q->q_norm_weight || !q->k_norm_weight || !q->cos ||
-        !q->sin || !q->q_out || !q->tail_k || !q->tail_v || !q->kq || !q->vq || !q->kmn || !q->kst || !q->vmn ||
-        !q->vst || !q->pos || !q->written || !q->qlen || !q->pg || q->rope_len <= 0 || q->max_len <= 0)
-        return fail(NOVA_ERR_INVALID, "NULL pointer or bad length");
-    auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
-    if (mis(g->x, 16) || (g->x_stride % 8) || mis(g->norm_weight, 16) || mis(g->packed, 16) || mis(g->workspace, 256))
-        return fail(NOVA_ERR_ALIGN, "x / norm_weight / packed 16-byte aligned, workspace 256");
-    int64_t need = 0;
-    nova_nf4_workspace_bytes(g->n, &need);
-    if (g->workspace_bytes < need) return fail(NOVA_ERR_INVALID, "workspace too small");
-    Params p;
-    memset(&p, 0, sizeof(p));
-    p.x = (const __half*)g->x;
-    p.x_stride = g->x_stride;
-    p.norm_w = (const __half*)g->norm_weight;
-    p.eps = float(g->eps);
-    p.packed = (const uint8_t*)g->packed;
-    p.lut = (const uint32_t*)g->lut;
-    p.M = int(g->m);
-    p.N = int(g->n);
-    p.K = int(g->k);
-    p.KB = int(g->k / 64);
-    QkPhase o;
-    o.qkv = nullptr; o.qkv_stride = 0;
-    o.q_norm_w = (const __half*)q->q_norm_weight; o.k_norm_w = (const __half*)q->k_norm_weight;
-    o.cos = (const __half*)q->cos; o.sin = (const __half*)q->sin; o.rope_len = q->rope_len;
-    o.q_out = (__half*)q->q_out; o.q_out_stride = q->q_out_stride;
-    o.tail_k = (__half*)q->tail_k; o.tail_v = (__half*)q->tail_v;
-    o.kq = (uint8_t*)q->kq; o.vq = (uint8_t*)q->vq;
-    o.kmn = (__half*)q->kmn; o.kst = (__half*)q->kst; o.vmn = (__half*)q->vmn; o.vst = (__half*)q->vst;
-    o.pos = q->pos; o.written = q->written; o.qlen = q->qlen; o.pg = q->pg;
-    o.q_heads = int(q->q_heads); o.kv_heads = int(q->kv_heads); o.max_len = q->max_len;
-    int dev = 0, optin = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
-        cudaGetLastError();
-        return fail(NOVA_ERR_CUDA, "device queries failed");
-    }
-    const int64_t xs_bytes = (g->m * g->k * 2 + 127) / 128 * 128;
-    const int64_t ring_unit = int64_t(NAT_WARPS) * NAT_STAGES * UNIT_BYTES;
-    const int64_t red_bytes = 2 * int64_t(NAT_WARPS) * 32 * 32;
-    const int64_t su = std::min<int64_t>(3, (optin - int64_t(LUT_BYTES) - xs_bytes - red_bytes - 4096) / ring_unit);
-    if (su < 1) return fail(NOVA_ERR_UNSUPPORTED, "M*K too large for shared memory");
-    const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + red_bytes + su * ring_unit;
-    static int64_t smem_set = 0;
-    if (int rc = prepare_smem(nf4_qkv_heads_kernel, nsmem, &smem_set)) return rc;
-    int* errp = reinterpret_cast<int*>((uint8_t*)g->workspace + partial_bytes() + ((g->n / 16) * 4 + 4));
-    const cudaError_t err = launch(nf4_qkv_heads_kernel, dim3(unsigned(heads)), dim3(NAT_THREADS), size_t(nsmem),
-                                   (cudaStream_t)stream, p, o, int(su), errp);
-    if (err != cudaSuccess) {
-        cudaGetLastError();
-        return fail(NOVA_ERR_CUDA, "nova_qkv_norm_rope_append: launch failed: %s", cudaGetErrorString(err));
-    }
-    return NOVA_OK;
-}
-
 // ---------------------------------------------------------------- batched GEMM (host)
-
-// mma.sync GEMM workspace: [tile counters (up to 1000 tiles), finalize counter, error word | split-K
-// slots].  The counters sit at the same place for every shape, so one workspace sized for the largest
-// GEMM serves them all; the slots start past the tcgen05 GEMM's counter region as well, so the two
-// kernels may also share a workspace (one launch at a time).
-constexpr int64_t GM_COUNTER_BYTES = (256 + int64_t(TC_MAX_TILES) * 16 + 1023) / 1024 * 1024;
 
 // Split count: no more CTAs than SMs (one wave), and about sqrt(3 * k-blocks): each split adds
 // ~KB/S k-block steps of work per CTA but one more 128 KB partial for the last CTA to add.
@@ -2668,26 +1681,16 @@ static int64_t tc_workspace_layout(int64_t n, int64_t k, int64_t* part_off) {
     return off + g * 2 * int64_t(TC_SLOT_FLOATS) * 4;
 }
 
-static void gemm_shape(int64_t n, int64_t k, int64_t* tiles, int64_t* splits) {
-    const int64_t n_rg = n / UNIT_ROWS;
-    const int64_t t = (n_rg + GM_WARPS - 1) / GM_WARPS;
-    const int64_t kb = k / 64;
-    int64_t s = int64_t(sm_count()) / t;
-    s = std::min<int64_t>(s, int64_t(sqrt(3.0 * double(kb))));
-    s = std::max<int64_t>(1, std::min<int64_t>(s, kb / 2));
-    *tiles = t;
-    *splits = s;
-}
-
 extern "C" int nova_nf4_gemm_workspace_bytes(int64_t n, int64_t k, int64_t* bytes) {
     if (!bytes) return fail(NOVA_ERR_INVALID, "bytes must not be NULL");
     if (n <= 0 || n % UNIT_ROWS || k <= 0 || k % 64) return fail(NOVA_ERR_INVALID, "N multiple of 32, K of 64");
-    int64_t t = 0, s = 0;
-    gemm_shape(n, k, &t, &s);
-    const int64_t slots = s > 1 ? t * s * int64_t(GM_SLOT_FLOATS) * 4 : 0;
-    const int64_t legacy = GM_COUNTER_BYTES + slots;   // counters first, then the split slots
-    *bytes = std::max(legacy, tc_workspace_layout(n, k, nullptr));
+    *bytes = tc_workspace_layout(n, k, nullptr);
     return NOVA_OK;
+}
+
+extern "C" int nova_nf4_gemm_read_error(void* workspace, int* host_value) {
+    if (!workspace) return fail(NOVA_ERR_INVALID, "NULL workspace");
+    return read_error_word(reinterpret_cast<int*>((uint8_t*)workspace + 4), host_value, "GEMM");
 }
 
 // tcgen05 path of nova_nf4_gemm (arguments already validated).
@@ -2741,8 +1744,8 @@ static int nf4_gemm_tc(const nova_nf4_args* a, int epi, cudaStream_t stream) {
     using TKern = void (*)(Params, CUtensorMap, TcArgs);
     static const TKern kernels[5] = {nf4_gemm_tc_kernel<0>, nf4_gemm_tc_kernel<1>, nf4_gemm_tc_kernel<2>,
                                      nf4_gemm_tc_kernel<3>, nf4_gemm_tc_kernel<4>};
-    static int64_t smem_set[5] = {};
-    if (int rc = prepare_smem(kernels[epi], nsmem, &smem_set[epi])) return rc;
+    static int64_t smem_set[5][kMaxDevices] = {};
+    if (int rc = prepare_smem(kernels[epi], nsmem, smem_set[epi])) return rc;
     const cudaError_t err = launch(kernels[epi], dim3(unsigned(ta.G)), dim3(TC_THREADS), size_t(nsmem), stream, p,
                                    xmap, ta);
     if (err != cudaSuccess) {
@@ -2755,9 +1758,8 @@ static int nf4_gemm_tc(const nova_nf4_args* a, int epi, cudaStream_t stream) {
 extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
     if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
     const int64_t m = a->m, n = a->n, k = a->k;
-    if (a->layout != 1 && a->layout != 2)
-        return fail(NOVA_ERR_UNSUPPORTED, "native (1) or tcgen05 (2) unit layout only");
-    if (m < 1 || m > GM_MAX_M) return fail(NOVA_ERR_UNSUPPORTED, "M must be in [1, 64], got %lld", (long long)m);
+    if (a->layout != 2) return fail(NOVA_ERR_UNSUPPORTED, "tcgen05 unit layout (2, nova_nf4_pack_tc) only");
+    if (m < 1 || m > TC_MAX_M) return fail(NOVA_ERR_UNSUPPORTED, "M must be in [1, 64], got %lld", (long long)m);
     if (n <= 0 || n % UNIT_ROWS || n > (1 << 30) || k <= 0 || k % 64 || k > (1 << 20))
         return fail(NOVA_ERR_INVALID, "N multiple of 32, K multiple of 64");
     if (a->norm_weight) return fail(NOVA_ERR_UNSUPPORTED, "no norm prologue in the batched GEMM (normalize x first)");
@@ -2777,77 +1779,7 @@ extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
     nova_nf4_gemm_workspace_bytes(n, k, &need);
     if (a->workspace_bytes < need) return fail(NOVA_ERR_INVALID, "workspace too small: %lld < %lld",
                                                (long long)a->workspace_bytes, (long long)need);
-    if (a->layout == 2) {
-        if ((n + TC_ROWS - 1) / TC_ROWS > TC_MAX_TILES)
-            return fail(NOVA_ERR_UNSUPPORTED, "N above %d rows", TC_MAX_TILES * TC_ROWS);
-        return nf4_gemm_tc(a, epi, (cudaStream_t)stream);
-    }
-    int64_t tiles = 0, splits = 0;
-    gemm_shape(n, k, &tiles, &splits);
-    Params p;
-    memset(&p, 0, sizeof(p));
-    p.x = (const __half*)a->x;
-    p.x_stride = a->x_stride;
-    p.packed = (const uint8_t*)a->packed;
-    p.lut = (const uint32_t*)a->lut;
-    p.residual = (const __half*)a->residual;
-    p.res_stride = a->res_stride;
-    p.out = (__half*)a->out;
-    p.out_stride = a->out_stride;
-    p.argmax = (unsigned long long*)a->argmax;
-    p.token_out = a->token_out;
-    p.pos = a->pos;
-    p.embed = (const __half*)a->embed;
-    p.embed_out = (__half*)a->embed_out;
-    p.embed_out_stride = a->embed_out_stride;
-    p.embed_dim = int(a->embed_dim);
-    p.M = int(m);
-    p.N = int(n);
-    p.K = int(k);
-    p.KB = int(k / 64);
-    if (tiles > 500) return fail(NOVA_ERR_INVALID, "N too large for the batched GEMM (at most 256000 rows)");
-    uint8_t* ws = (uint8_t*)a->workspace;
-    float* part = (float*)(ws + GM_COUNTER_BYTES);
-    unsigned* tile_cnt = (unsigned*)ws;   // arrive / depart per tile
-    unsigned* done = tile_cnt + 1000;
-    int* errp = (int*)(done + 1);
-    p.done = done;   // re-armed by the step finalize
-    int dev = 0, optin = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
-        cudaGetLastError();
-        return fail(NOVA_ERR_CUDA, "device queries failed");
-    }
-    const int64_t xt_bytes = (GM_XBUF * m * GM_XSTRIDE * 2 + 127) / 128 * 128;
-    const int64_t ring_unit = int64_t(GM_WARPS) * NAT_STAGES * UNIT_BYTES;
-    const int64_t su = std::min<int64_t>(3, (optin - int64_t(LUT_BYTES) - xt_bytes - 1024) / ring_unit);
-    if (su < 1) return fail(NOVA_ERR_UNSUPPORTED, "shared memory");
-    const int64_t nsmem = int64_t(LUT_BYTES) + xt_bytes + su * ring_unit;
-    using GKern = void (*)(Params, int, int, float*, unsigned*, unsigned*, int*);
-    static const GKern kernels[5] = {nf4_gemm_kernel<0>, nf4_gemm_kernel<1>, nf4_gemm_kernel<2>, nf4_gemm_kernel<3>,
-                                     nf4_gemm_kernel<4>};
-    static int64_t smem_set[5] = {};
-    if (int rc = prepare_smem(kernels[epi], nsmem, &smem_set[epi])) return rc;
-    cudaError_t err;
-    if (splits > 1) {   // the split CTAs of a tile wait for one another: all must be resident
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(unsigned(tiles), unsigned(splits));
-        cfg.blockDim = dim3(GM_THREADS);
-        cfg.dynamicSmemBytes = size_t(nsmem);
-        cfg.stream = (cudaStream_t)stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        err = cudaLaunchKernelEx(&cfg, kernels[epi], p, int(splits), int(su), part, tile_cnt, done, errp);
-    } else {
-        err = launch(kernels[epi], dim3(unsigned(tiles), 1u), dim3(GM_THREADS), size_t(nsmem), (cudaStream_t)stream, p,
-                     1, int(su), part, tile_cnt, done, errp);
-    }
-    if (err != cudaSuccess) {
-        cudaGetLastError();
-        return fail(NOVA_ERR_CUDA, "nova_nf4_gemm: launch failed: %s", cudaGetErrorString(err));
-    }
-    return NOVA_OK;
+    if ((n + TC_ROWS - 1) / TC_ROWS > TC_MAX_TILES)
+        return fail(NOVA_ERR_UNSUPPORTED, "N above %d rows", TC_MAX_TILES * TC_ROWS);
+    return nf4_gemm_tc(a, epi, (cudaStream_t)stream);
 }

@@ -17,8 +17,7 @@ one for the lm_head:
     5. nova_nf4_gemv      down_proj + residual add
 
 (``attn_fused=False`` runs step 2 as nova_qk_norm_rope_append followed by
-nova_attn_decode_int8; ``qkv_fused=True`` merges 1 with the q/k part into
-nova_qkv_norm_rope_append, then the attention alone.)
+nova_attn_decode_int8.)
     final: nova_nf4_gemv  final norm (prologue) + 4-bit lm_head + greedy argmax
            + input_ids / pos update + next-token embedding gather (last warp)
 
@@ -230,8 +229,7 @@ class NovaDecoder:
     """
 
     def __init__(self, weights: DecoderWeights, max_len: int, batch: int = 1, chunk: int | None = None,
-                 device="cuda", pdl: bool = True, tp: TPContext | None = None, fused: bool | None = None,
-                 qkv_fused: bool = False, attn_fused: bool = True) -> None:
+                 device="cuda", pdl: bool = True, tp: TPContext | None = None, attn_fused: bool = True) -> None:
         cfg = weights.cfg
         if batch < 1 or batch > MAX_BATCH:
             raise ValueError(f"the decode path handles batch 1..{MAX_BATCH}")
@@ -280,20 +278,9 @@ class NovaDecoder:
             self.gemm_ws = self.xn = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.pdl = bool(pdl)
-        # fused=True: one cooperative launch per layer for o -> gate|up -> down -> next q|k|v -> q/k norm
-        # (batch <= 2, one GPU).  Off by default: its grid barriers (~1.5-2 us each) and per-phase x
-        # staging cost as much as the kernel boundaries they replace.
-        self.fused = False if fused is None else bool(fused)
-        if self.fused and (self.batch > 2 or self.tp.active):
-            raise ValueError("fused phases need batch <= 2 and no tensor parallelism")
-        self.fused_ws = torch.zeros(256, dtype=torch.uint8, device=dev)
-        # qkv_fused=True: q|k|v projection + q/k norm + RoPE + append in one launch, one CTA per head
-        # (batch <= 8).  Off by default: with 48 head-owning CTAs most SMs idle, and measured in the decode
-        # step the two launches (q|k|v GEMV on every SM, then the q/k kernel) are faster.
-        self.qkv_fused = bool(qkv_fused) and self.batch <= GEMV_ROWS
         # attn_fused=True: the q/k norm + RoPE + ring append runs in the attention's prologue (one launch
         # and one kernel boundary fewer per layer)
-        self.attn_fused = bool(attn_fused) and not self.qkv_fused
+        self.attn_fused = bool(attn_fused)
         self._staged = None   # fp16 K/V per layer of the positions prefilled / injected since the last reset
 
     def _pick_chunk(self) -> int:
@@ -352,19 +339,10 @@ class NovaDecoder:
                 _lib.call("nova_kv_quant_int8", src.data_ptr(), src.stride(1), dst.data_ptr(), self.max_len * d,
                           mn.data_ptr(), st.data_ptr(), mn.shape[2] * d, self.batch * self.hkv, q_full, d, GROUP_T,
                           stream)
-        take = min(total, GROUP_T)
-        slots = torch.remainder(torch.arange(total - take, total, device=self.device), GROUP_T)
-        cache.tail_k[li].index_copy_(2, slots, k[:, :, total - take:total])
-        cache.tail_v[li].index_copy_(2, slots, v[:, :, total - take:total])
+        cache.write_ring(li, k[:, :, :total], v[:, :, :total], total)
 
     def _set_scalars(self, total: int) -> None:
-        cache = self.cache
-        q_full = (total // GROUP_T) * GROUP_T
-        cache.pos.fill_(total)
-        cache.first.fill_(0)
-        cache._written.fill_(total)
-        cache._qlen.fill_(q_full)
-        cache._pg.fill_(q_full // GROUP_T)
+        self.cache.set_lengths(total)
         self.argmax_slot.zero_()
 
     def _dequant_prefix(self, li: int, n: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -434,10 +412,7 @@ class NovaDecoder:
                                   self.max_len * d, mn[:, :, g0:].data_ptr(), st[:, :, g0:].data_ptr(),
                                   mn.shape[2] * d, B * self.hkv, full, d, GROUP_T, stream)
                 if c1 > take0:   # positions of the prompt's last <= 64 tokens into the ring
-                    p0 = max(c0, take0)
-                    slots = torch.remainder(torch.arange(p0, c1, device=self.device), GROUP_T)
-                    cache.tail_k[li].index_copy_(2, slots, k[:, :, p0 - c0:])
-                    cache.tail_v[li].index_copy_(2, slots, v[:, :, p0 - c0:])
+                    cache.write_ring(li, k, v, c1)
         x = fused_rms_norm(h[:, -1], self.w.final_norm, cfg.rms_norm_eps)
         logits = self._linear16(x, self.w.lm_head)
         first = torch.argmax(logits, dim=-1)
@@ -660,58 +635,7 @@ class NovaDecoder:
         qa.head_dim, qa.max_len, qa.group = cfg.head_dim, self.max_len, GROUP_T
         return qa
 
-    def _fused(self, phases: list, qk_layer: int | None = None) -> None:
-        """One nova_fused_phases launch.  phases: ("gemv", x, w, out, epilogue, norm_weight, residual) or
-        ("qk",); the q/k phase uses layer ``qk_layer``."""
-        a = _lib.FusedArgs()
-        a.n_phases = len(phases)
-        for i, ph in enumerate(phases):
-            if ph[0] == "qk":
-                a.kind[i] = _lib.PHASE_QK
-                a.qk = self._qk_args(qk_layer, self.w.layers[qk_layer])
-                continue
-            _, x, w, out, epi, nw, res = ph
-            a.kind[i] = _lib.PHASE_GEMV
-            g = a.gemv[i]
-            g.x, g.x_stride = x.data_ptr(), x.stride(0)
-            g.norm_weight = _lib.ptr(nw)
-            g.units, g.n, g.k = w.units.data_ptr(), w.n, w.shape[1]
-            g.out, g.out_stride = out.data_ptr(), out.stride(0)
-            g.residual, g.res_stride = (_lib.ptr(res), res.stride(0) if res is not None else 0)
-            g.epilogue = epi
-        a.lut, a.eps, a.m = self.lut.data_ptr(), self.cfg.rms_norm_eps, self.batch
-        a.workspace, a.workspace_bytes = self.fused_ws.data_ptr(), self.fused_ws.numel()
-        _lib.check(_lib.lib().nova_fused_phases(_lib.ctypes.byref(a), _lib.stream_of(self.device)), "fused phases")
-
-    def _step_body_fused(self) -> None:
-        cfg, cache = self.cfg, self.cache
-        B = self.batch
-        q3 = self.q_rot.view(B, self.hq, cfg.head_dim)
-        a3 = self.attn.view(B, self.hq, cfg.head_dim)
-        layers = self.w.layers
-        NF4 = _lib
-        self._fused([("gemv", self.resid, layers[0].qkv, self.qkv, NF4.NF4_PLAIN, layers[0].input_ln, None), ("qk",)],
-                    qk_layer=0)
-        for li, lw in enumerate(layers):
-            launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
-                                  cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
-                             cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
-                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window)
-            phases = [("gemv", self.attn, lw.o, self.resid, NF4.NF4_RESIDUAL, None, self.resid),
-                      ("gemv", self.resid, lw.gate_up, self.act, NF4.NF4_SILU_MUL, lw.post_ln, None),
-                      ("gemv", self.act, lw.down, self.resid, NF4.NF4_RESIDUAL, None, self.resid)]
-            if li + 1 < len(layers):
-                nxt = layers[li + 1]
-                phases += [("gemv", self.resid, nxt.qkv, self.qkv, NF4.NF4_PLAIN, nxt.input_ln, None), ("qk",)]
-            self._fused(phases, qk_layer=li + 1 if li + 1 < len(layers) else None)
-        self._gemv(self.resid, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
-                   argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
-                   embed_out=self.resid)
-
     def _step_body(self) -> None:
-        if self.fused:
-            self._step_body_fused()
-            return
         cfg, cache, lut = self.cfg, self.cache, self.lut
         eps = cfg.rms_norm_eps
         B = self.batch
@@ -752,23 +676,42 @@ class NovaDecoder:
                    embed_out=self.resid)
 
     def _qkv_step(self, li: int, lw) -> None:
-        """input norm + q|k|v projection + q/k norm + RoPE + KV append of layer li: one launch
-        (nova_qkv_norm_rope_append) up to 8 rows, else the GEMV in 8-row slices and the q/k kernel."""
+        """input norm + q|k|v projection, then q/k norm + RoPE + KV append of layer li as a launch of
+        its own (the decoder's default runs the latter inside the attention launch)."""
         stream = _lib.stream_of(self.device)
         qa = self._qk_args(li, lw)
-        if self.qkv_fused:
-            ga = _lib.NF4Args()
-            ga.x, ga.x_stride = self.resid.data_ptr(), self.resid.stride(0)
-            ga.norm_weight, ga.eps = lw.input_ln.data_ptr(), self.cfg.rms_norm_eps
-            ga.packed, ga.absmax, ga.absmax_fp32, ga.layout = lw.qkv.units.data_ptr(), None, 0, 1
-            ga.lut = self.lut.data_ptr()
-            ga.workspace, ga.workspace_bytes = self.gemv_ws.data_ptr(), self.gemv_ws.numel()
-            ga.m, ga.n, ga.k, ga.epilogue = self.batch, lw.qkv.n, lw.qkv.shape[1], _lib.NF4_PLAIN
-            _lib.check(_lib.lib().nova_qkv_norm_rope_append(_lib.ctypes.byref(ga), _lib.ctypes.byref(qa), stream),
-                       "qkv_norm_rope_append")
-            return
         self._gemv(self.resid, lw.qkv, self.qkv, norm_weight=lw.input_ln)
         _lib.check(_lib.lib().nova_qk_norm_rope_append(_lib.ctypes.byref(qa), stream), "qk_norm_rope_append")
+
+    def errors(self) -> dict:
+        """Error words of the step's kernels (synchronizes; each is read and
+        cleared): non-zero means a bounded wait inside a launch gave up and that
+        launch's output -- hence the step's tokens -- is not valid."""
+        import ctypes
+
+        torch.cuda.synchronize(self.device)
+        lib = _lib.lib()
+        out = {}
+
+        def word(name, fn, *args):
+            v = ctypes.c_int(0)
+            _lib.check(fn(*args, ctypes.byref(v)), name)
+            out[name] = int(v.value)
+
+        c = self.cache
+        word("attention", lib.nova_attn_read_error, c.workspace.data_ptr(), self.batch, self.hkv)
+        word("gemv", lib.nova_nf4_gemv_read_error, self.gemv_ws.data_ptr())
+        if self.gemm_ws is not None:
+            word("gemm", lib.nova_nf4_gemm_read_error, self.gemm_ws.data_ptr())
+        if self.p2p is not None:
+            out["allreduce"] = self.p2p.error()
+        return out
+
+    def check_errors(self) -> None:
+        """Raise RuntimeError when any error word of the step's kernels is set."""
+        bad = {k: v for k, v in self.errors().items() if v}
+        if bad:
+            raise RuntimeError(f"decode step kernels reported bounded-wait failures: {bad}")
 
     def close(self) -> None:
         """Release the graph and the peer mappings of the tensor-parallel
@@ -780,11 +723,7 @@ class NovaDecoder:
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step (NCCL all-reduces not counted)."""
-        if self.fused:   # q|k|v + q/k of layer 0, then attention + one fused launch per layer, then the lm_head
-            return 1 + 2 * self.cfg.num_hidden_layers + 1
-        if self.qkv_fused:
-            per_layer = 5          # q|k|v + q/k norm-RoPE-append, attention, o, gate|up, down
-        elif self.batch > GEMV_ROWS:
+        if self.batch > GEMV_ROWS:
             per_layer = 8          # 2 norms + 4 GEMMs + q/k norm-RoPE-append + attention
         else:
             per_layer = 6
@@ -814,12 +753,7 @@ class NovaDecoder:
                 t.uniform_(-2.5, -1.5, generator=g)
             for t in (c.tail_k[li], c.tail_v[li]):
                 t.normal_(0.0, 1.0, generator=g)
-        q_full = (ctx // GROUP_T) * GROUP_T
-        c.pos.fill_(ctx)
-        c.first.fill_(0)
-        c._written.fill_(ctx)
-        c._qlen.fill_(q_full)
-        c._pg.fill_(q_full // GROUP_T)
+        c.set_lengths(ctx)
         self.input_ids.copy_(torch.randint(0, self.cfg.vocab_size, (self.batch,), generator=g, device=self.device))
         self.resid.copy_(self.w.embed[self.input_ids])
         self.argmax_slot.zero_()

@@ -189,12 +189,10 @@ def nf4_gemm(x: torch.Tensor, units: torch.Tensor, lut: torch.Tensor, out: torch
              epilogue: int = _lib.NF4_PLAIN, residual: torch.Tensor | None = None,
              argmax: torch.Tensor | None = None, token_out: torch.Tensor | None = None,
              pos: torch.Tensor | None = None, embed: torch.Tensor | None = None,
-             embed_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-             layout: int = 2) -> torch.Tensor:
-    """``nova_nf4_gemm``: x ``[M <= 64, K]`` against the unit stream of an
-    ``[n, K]`` NF4 weight (layout 2: :func:`pack_tc`, tcgen05 tensor cores;
-    layout 1: :func:`pack_native`, mma.sync); out ``[M, n]`` (``[M, n/2]`` for
-    SiLU*up)."""
+             embed_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``nova_nf4_gemm``: x ``[M <= 64, K]`` against the tcgen05 unit stream
+    (:func:`pack_tc`) of an ``[n, K]`` NF4 weight, on the tensor cores; out
+    ``[M, n]`` (``[M, n/2]`` for SiLU*up)."""
     m, k = x.shape
     if x.stride(1) != 1 or out.stride(1) != 1:
         raise ValueError("x/out must have a contiguous last dimension")
@@ -202,7 +200,7 @@ def nf4_gemm(x: torch.Tensor, units: torch.Tensor, lut: torch.Tensor, out: torch
     a = _lib.NF4Args()
     a.x, a.x_stride = x.data_ptr(), x.stride(0)
     a.norm_weight, a.eps = None, 0.0
-    a.packed, a.absmax, a.absmax_fp32, a.layout = units.data_ptr(), None, 0, int(layout)
+    a.packed, a.absmax, a.absmax_fp32, a.layout = units.data_ptr(), None, 0, 2
     a.lut, a.bias = lut.data_ptr(), None
     a.residual, a.res_stride = (_lib.ptr(residual), residual.stride(0) if residual is not None else 0)
     a.out, a.out_stride = out.data_ptr(), out.stride(0)

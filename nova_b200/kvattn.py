@@ -317,10 +317,16 @@ class _Staging:
 class KVInt8Cache:
     r"""Streaming int8 KV cache (src/nova/kvattn.py:488-880), B200 kernels.
 
-    Per layer: uint8 K/V codes ``[B, H_kv, max_len, D]``, fp16 min/step
-    ``[B, H_kv, ceil(max_len/64), D]``, a 64-slot fp16 ring (the <=63 newest
-    tokens whose group is not complete) and shared device scalars
-    ``pos`` / ``first`` / ``_written`` / ``_qlen`` / ``_pg``.
+    Storage: each tensor family is one allocation over all layers --
+    ``codes`` uint8 ``[2, slots, B, H_kv, max_len, D]`` (K then V), ``scales``
+    fp16 ``[4, slots, B, H_kv, ceil(max_len/64), D]`` (K min, K step, V min,
+    V step), ``ring`` fp16 ``[2, slots, B, H_kv, 64, D]`` (the <= 63 newest
+    tokens whose group is not complete, at slot ``pos % 64``) -- and the
+    reference's per-layer attributes (``kq``, ``vq``, ``kmn``, ``kst``, ``vmn``,
+    ``vst``, ``tail_k``, ``tail_v``: lists indexed by layer) are views into
+    them.  The five lengths live in one int64 device vector; ``pos``,
+    ``first``, ``_written``, ``_qlen`` and ``_pg`` are 1-element views of it,
+    so saving or restoring the cache state is a copy of a few tensors.
 
     ``update`` (decode) is one ``nova_kv_append_int8`` launch; ``attend`` is one
     ``nova_attn_decode_int8`` launch that reads prefix and ring and merges them
@@ -328,6 +334,8 @@ class KVInt8Cache:
     prompt and ``finish_prefill`` quantizes its complete groups with
     ``nova_kv_quant_int8`` (bit-identical to ``quantize_int8(..., "token")``).
     """
+
+    _LENGTHS = ("pos", "first", "_written", "_qlen", "_pg")
 
     def __init__(
         self,
@@ -345,63 +353,42 @@ class KVInt8Cache:
         num_stages: int = 2,
         window: int = 0,
     ) -> None:
-        if head_dim != HEAD_DIM:
-            raise ValueError(f"head_dim must be {HEAD_DIM}, got {head_dim}")
-        if num_q_heads % num_kv_heads:
-            raise ValueError(f"q heads {num_q_heads} not divisible by KV heads {num_kv_heads}")
-        if num_q_heads // num_kv_heads > MAX_GQ:
-            raise ValueError(f"{num_q_heads // num_kv_heads} q heads per KV head exceeds {MAX_GQ}")
-        if group != GROUP_T:
-            raise ValueError(f"group must be {GROUP_T}")
-        if chunk % group:
-            raise ValueError(f"chunk {chunk} must be a multiple of group {group}")
-        if dtype != torch.float16:
-            raise ValueError("dtype must be float16")
-        self.num_slots = int(num_slots)
-        self.num_kv_heads = int(num_kv_heads)
-        self.head_dim = int(head_dim)
-        self.max_len = int(max_len)
-        self.num_q_heads = int(num_q_heads)
-        self.batch = int(batch)
-        self.dtype = dtype
-        self.device = torch.device(device)
-        self.group = int(group)
-        self.chunk = int(chunk)
-        self.num_warps = int(num_warps)
-        self.num_stages = int(num_stages)
-        self.window = int(window)
-
-        n_groups = -(-self.max_len // self.group)
-        dshape = (batch, self.num_kv_heads, self.max_len, self.head_dim)
-        sshape = (batch, self.num_kv_heads, n_groups, self.head_dim)
-        tshape = (batch, self.num_kv_heads, self.group, self.head_dim)
-        dev = self.device
-        self.kq = [torch.zeros(dshape, dtype=torch.uint8, device=dev) for _ in range(self.num_slots)]
-        self.vq = [torch.zeros(dshape, dtype=torch.uint8, device=dev) for _ in range(self.num_slots)]
-        self.kmn = [torch.zeros(sshape, dtype=dtype, device=dev) for _ in range(self.num_slots)]
-        self.kst = [torch.zeros(sshape, dtype=dtype, device=dev) for _ in range(self.num_slots)]
-        self.vmn = [torch.zeros(sshape, dtype=dtype, device=dev) for _ in range(self.num_slots)]
-        self.vst = [torch.zeros(sshape, dtype=dtype, device=dev) for _ in range(self.num_slots)]
-        self.tail_k = [torch.zeros(tshape, dtype=dtype, device=dev) for _ in range(self.num_slots)]
-        self.tail_v = [torch.zeros(tshape, dtype=dtype, device=dev) for _ in range(self.num_slots)]
-
-        self.pos = torch.zeros(1, dtype=torch.long, device=dev)
-        self.first = torch.zeros(1, dtype=torch.long, device=dev)
-        self._written = torch.zeros(1, dtype=torch.long, device=dev)
-        self._qlen = torch.zeros(1, dtype=torch.long, device=dev)
-        self._pg = torch.zeros(1, dtype=torch.long, device=dev)
-        self._idx64 = torch.arange(self.group, dtype=torch.long, device=dev)
-        self._arange = torch.arange(self.max_len, dtype=torch.long, device=dev)
-        self._zero = torch.zeros((), dtype=dtype, device=dev)
-        self._ninf = torch.full((), float("-inf"), dtype=dtype, device=dev)
-
-        # split count fixed by capacity (constant grid inside a graph)
+        for ok, msg in ((head_dim == HEAD_DIM, f"head_dim must be {HEAD_DIM}, got {head_dim}"),
+                        (num_q_heads % num_kv_heads == 0,
+                         f"q heads {num_q_heads} not divisible by KV heads {num_kv_heads}"),
+                        (num_q_heads // max(num_kv_heads, 1) <= MAX_GQ,
+                         f"{num_q_heads // max(num_kv_heads, 1)} q heads per KV head exceeds {MAX_GQ}"),
+                        (group == GROUP_T, f"group must be {GROUP_T}"),
+                        (chunk % group == 0, f"chunk {chunk} must be a multiple of group {group}"),
+                        (dtype == torch.float16, "dtype must be float16")):
+            if not ok:
+                raise ValueError(msg)
+        self.num_slots, self.num_kv_heads, self.num_q_heads = int(num_slots), int(num_kv_heads), int(num_q_heads)
+        self.head_dim, self.max_len, self.batch = int(head_dim), int(max_len), int(batch)
+        self.group, self.chunk, self.window = int(group), int(chunk), int(window)
+        self.num_warps, self.num_stages = int(num_warps), int(num_stages)   # Triton knobs, accepted and unused
+        self.dtype, self.device = dtype, torch.device(device)
+        self._alloc()
+        # grid fixed by the capacity (one captured graph serves every length)
         self.n_splits = -(-self.max_len // self.chunk)
-        self.workspace = new_workspace(batch, self.num_q_heads, self.num_kv_heads, self.n_splits, True, dev)
-        self.out = torch.zeros((batch, self.num_q_heads, 1, self.head_dim), dtype=dtype, device=dev)
-        self.lse = torch.zeros((batch, self.num_q_heads), dtype=torch.float32, device=dev)
+        self.workspace = new_workspace(self.batch, self.num_q_heads, self.num_kv_heads, self.n_splits, True,
+                                       self.device)
+        self.out = torch.zeros((self.batch, self.num_q_heads, 1, self.head_dim), dtype=dtype, device=self.device)
+        self.lse = torch.zeros((self.batch, self.num_q_heads), dtype=torch.float32, device=self.device)
         self.merged = self.out  # prefix and ring are merged inside the kernel
         self.staging: Any = None
+
+    def _alloc(self) -> None:
+        L, B, H, D, dev = self.num_slots, self.batch, self.num_kv_heads, self.head_dim, self.device
+        self.codes = torch.zeros((2, L, B, H, self.max_len, D), dtype=torch.uint8, device=dev)
+        self.scales = torch.zeros((4, L, B, H, -(-self.max_len // self.group), D), dtype=self.dtype, device=dev)
+        self.ring = torch.zeros((2, L, B, H, self.group, D), dtype=self.dtype, device=dev)
+        self.lengths = torch.zeros(len(self._LENGTHS), dtype=torch.long, device=dev)
+        self.kq, self.vq = list(self.codes[0]), list(self.codes[1])
+        self.kmn, self.kst, self.vmn, self.vst = (list(self.scales[i]) for i in range(4))
+        self.tail_k, self.tail_v = list(self.ring[0]), list(self.ring[1])
+        for i, name in enumerate(self._LENGTHS):
+            setattr(self, name, self.lengths[i:i + 1])
 
     # ---- StaticKVCache-compatible surface ----
 
@@ -409,13 +396,15 @@ class KVInt8Cache:
         return int(self.pos.item())
 
     def reset(self) -> None:
-        self.pos.zero_()
-        self.first.zero_()
-        self._written.zero_()
-        self._qlen.zero_()
-        self._pg.zero_()
+        self.lengths.zero_()
         if self.staging is not None:
             self.staging.reset()
+
+    def set_lengths(self, total: int) -> None:
+        """Lengths after ``total`` tokens are in the cache: pos = written =
+        total, the int8 prefix the complete groups, no position dropped."""
+        q = total - total % self.group
+        self.lengths.copy_(torch.tensor([total, 0, total, q, q // self.group], dtype=torch.long))
 
     # ---- prefill: fp16 staging ----
 
@@ -458,86 +447,84 @@ class KVInt8Cache:
 
     append_prefill = update
 
-    def _sync_scalars(self) -> None:
-        self._written.copy_(self.pos)
-        self._written.add_(1)
-        self._qlen.copy_(self._written)
-        self._qlen.div_(self.group, rounding_mode="floor")
-        self._qlen.mul_(self.group)
-        self._pg.copy_(self._qlen)
-        self._pg.div_(self.group, rounding_mode="floor")
-
     def refresh_scalars(self) -> None:
-        """Recompute the device scalars from ``pos`` (outside a graph)."""
-        self._sync_scalars()
+        """Recompute written / qlen / pg from ``pos`` as a decode update at
+        ``pos`` leaves them (written = pos + 1); reads ``pos`` on the host, so
+        call it outside a graph (src/nova/kvattn.py:699-714)."""
+        w = int(self.pos.item()) + 1
+        q = w - w % self.group
+        self.lengths[2:].copy_(torch.tensor([w, q, q // self.group], dtype=torch.long))
+
+    def write_ring(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor, end: int) -> None:
+        """Put the last min(end, 64) positions of fp16 K/V ``[B, H_kv, n, D]``
+        (whose last position is ``end - 1``) into the layer's ring: position p
+        goes to slot p % 64, i.e. at most two contiguous slot ranges."""
+        take = min(int(end), self.group, k.shape[2])
+        p0 = end - take
+        s0 = p0 % self.group
+        first = min(take, self.group - s0)
+        for ring, src in ((self.tail_k[layer_idx], k), (self.tail_v[layer_idx], v)):
+            seg = src[:, :, src.shape[2] - take:]
+            ring[:, :, s0:s0 + first].copy_(seg[:, :, :first])
+            if take > first:
+                ring[:, :, :take - first].copy_(seg[:, :, first:])
 
     def finish_prefill(self, total: int) -> None:
         """Quantize the complete groups of the staging area, fill the ring with
-        the last <=64 tokens, set the scalars, free the staging area
+        the last <= 64 tokens, set the lengths, free the staging area
         (src/nova/kvattn.py:745-783)."""
         self._ensure_staging()
         total = int(total)
-        q = total // self.group * self.group
-        n_groups = q // self.group
-        rows = self.batch * self.num_kv_heads
+        full = total - total % self.group
         stream = _lib.stream_of(self.device)
-        ng_cap = self.kmn[0].shape[2]
+        g_cap = self.scales.shape[4]
         for layer in range(self.num_slots):
-            src_k = self.staging.key_cache[layer]
-            src_v = self.staging.value_cache[layer]
-            st_len = src_k.shape[2]
-            if n_groups:
-                for src, dst, mn, st in ((src_k, self.kq[layer], self.kmn[layer], self.kst[layer]),
-                                         (src_v, self.vq[layer], self.vmn[layer], self.vst[layer])):
-                    _lib.call("nova_kv_quant_int8", src.data_ptr(), st_len * self.head_dim, dst.data_ptr(),
-                              self.max_len * self.head_dim, mn.data_ptr(), st.data_ptr(), ng_cap * self.head_dim,
-                              rows, q, self.head_dim, self.group, stream)
-            take = min(total, self.group)
-            if take:
-                slots = torch.remainder(torch.arange(total - take, total, device=self.device), self.group)
-                self.tail_k[layer].index_copy_(2, slots, src_k[:, :, total - take:total])
-                self.tail_v[layer].index_copy_(2, slots, src_v[:, :, total - take:total])
-        self.pos.fill_(total)
-        self.first.fill_(0)
-        self._written.fill_(total)
-        self._qlen.fill_(q)
-        self._pg.fill_(n_groups)
+            staged = (self.staging.key_cache[layer], self.staging.value_cache[layer])
+            if full:
+                for j, src in enumerate(staged):   # j = 0: K, 1: V
+                    _lib.call("nova_kv_quant_int8", src.data_ptr(), src.shape[2] * self.head_dim,
+                              self.codes[j, layer].data_ptr(), self.max_len * self.head_dim,
+                              self.scales[2 * j, layer].data_ptr(), self.scales[2 * j + 1, layer].data_ptr(),
+                              g_cap * self.head_dim, self.batch * self.num_kv_heads, full, self.head_dim,
+                              self.group, stream)
+            if total:
+                self.write_ring(layer, staged[0][:, :, :total], staged[1][:, :, :total], total)
+        self.set_lengths(total)
         self.staging = None
 
     def release_staging(self) -> None:
         self.staging = None
 
     def attend_prefill(self, query: torch.Tensor, layer_idx: int) -> torch.Tensor:
-        """Prefill-chunk attention over the fp16 staging area with a causal
-        mask (src/nova/kvattn.py:791-815); prefill is not on the decode path."""
+        """Causal attention of a prefill chunk (queries at positions off ..
+        off+n-1, ``[B, H_q, n, D]``) over the fp16 staging area up to the
+        chunk's end, one KV head per query group (src/nova/kvattn.py:791-815);
+        with ``window`` a query at q sees only positions p > q - window.
+        Prefill is not on the decode path."""
         self._ensure_staging()
         n = query.shape[2]
         off = int(self.staging.pos.item())
-        hist = off + n
-        b = query.shape[0]
-        key = self.staging.key_cache[layer_idx][:, :, :hist]
-        value = self.staging.value_cache[layer_idx][:, :, :hist]
-        gq = self.num_q_heads // self.num_kv_heads
-        key = key[:, :, None].expand(b, self.num_kv_heads, gq, hist, self.head_dim)
-        key = key.reshape(b, self.num_q_heads, hist, self.head_dim)
-        value = value[:, :, None].expand(b, self.num_kv_heads, gq, hist, self.head_dim)
-        value = value.reshape(b, self.num_q_heads, hist, self.head_dim)
-        rows = off + torch.arange(n, device=query.device)
-        keep = self._arange[:hist].view(1, 1, 1, -1) <= rows.view(1, 1, n, 1)
+        end = off + n
+        keys = self.staging.key_cache[layer_idx][:, :, :end]
+        vals = self.staging.value_cache[layer_idx][:, :, :end]
+        allow = torch.ones((n, end), dtype=torch.bool, device=query.device).tril(diagonal=off)
         if self.window:
-            keep = keep & ((rows.view(1, 1, n, 1) - self._arange[:hist].view(1, 1, 1, -1)) < self.window)
-        mask = torch.where(keep, self._zero, self._ninf)
-        return F.scaled_dot_product_attention(query.contiguous(), key, value, attn_mask=mask, dropout_p=0.0,
-                                              scale=self.head_dim ** -0.5)
+            allow = allow.triu(diagonal=off - self.window + 1)
+        return F.scaled_dot_product_attention(query.contiguous(), keys, vals, attn_mask=allow,
+                                              scale=self.head_dim ** -0.5, enable_gqa=True)
 
     def ring_mask(self) -> torch.Tensor:
-        """Ring validity ``[1,1,1,64]`` (src/nova/kvattn.py:819-833); the kernel
-        evaluates the same predicate itself, this is for callers and tests."""
+        """Which ring slots the next attention reads, ``[1, 1, 1, 64]`` bool
+        (src/nova/kvattn.py:819-833): slot i holds the position u - age with
+        u = written - 1 and age = (u - i) mod 64; it is read when that position
+        is at or after qlen and first (and, with a window, age < window).  The
+        kernel evaluates the same predicate itself; this is for callers."""
         u = self._written - 1
-        p = u.view(1, 1) - torch.remainder(u.view(1, 1) - self._idx64.view(1, -1), self.group)
-        valid = (p >= self._qlen.view(1, 1)) & (p <= u.view(1, 1)) & (p >= self.first.view(1, 1))
+        age = torch.remainder(u - torch.arange(self.group, device=self.device), self.group)
+        newest_allowed = u - torch.maximum(self._qlen, self.first)   # largest age still valid
+        valid = age <= newest_allowed
         if self.window:
-            valid = valid & ((u.view(1, 1) - p) < self.window)
+            valid &= age < self.window
         return valid.view(1, 1, 1, self.group)
 
     def attend(self, query: torch.Tensor, layer_idx: int) -> torch.Tensor:
@@ -557,42 +544,35 @@ class KVInt8Cache:
     def grow(self, new_max_len: int) -> "KVInt8Cache":
         """A cache of capacity ``new_max_len`` holding this cache's contents:
         the int8 codes and min/step scales of every written group, the fp16
-        ring and the device scalars, copied on the device (the reference moves
-        fp16 caches across buckets in ``GraphDecoder.grow``,
-        src/nova/decode.py:444-500, and raises NotImplementedError for the int8
-        cache).  The split size is kept, so the added splits are empty and
-        decoding continues bit-identically; a captured decode graph must be
-        captured again.  The staging area is not carried over."""
+        ring and the lengths, copied on the device (the reference moves fp16
+        caches across buckets in ``GraphDecoder.grow``, src/nova/decode.py:
+        444-500, and raises NotImplementedError for the int8 cache).  The split
+        size is kept, so the added splits are empty and decoding continues
+        bit-identically; a captured decode graph must be captured again.  The
+        staging area is not carried over."""
         new_max_len = int(new_max_len)
         if new_max_len < self.max_len:
             raise ValueError(f"new capacity {new_max_len} is below the current {self.max_len}")
         new = KVInt8Cache(self.num_slots, self.num_kv_heads, self.head_dim, new_max_len, self.num_q_heads,
                           batch=self.batch, dtype=self.dtype, device=self.device, group=self.group, chunk=self.chunk,
                           num_warps=self.num_warps, num_stages=self.num_stages, window=self.window)
-        g_old = self.kmn[0].shape[2]
-        for i in range(self.num_slots):
-            for src, dst in ((self.kq[i], new.kq[i]), (self.vq[i], new.vq[i])):
-                dst[:, :, :self.max_len].copy_(src)
-            for src, dst in ((self.kmn[i], new.kmn[i]), (self.kst[i], new.kst[i]), (self.vmn[i], new.vmn[i]),
-                             (self.vst[i], new.vst[i])):
-                dst[:, :, :g_old].copy_(src)
-            new.tail_k[i].copy_(self.tail_k[i])
-            new.tail_v[i].copy_(self.tail_v[i])
-        for name in ("pos", "first", "_written", "_qlen", "_pg"):
-            getattr(new, name).copy_(getattr(self, name))
+        new.codes[..., :self.max_len, :].copy_(self.codes)
+        new.scales[..., :self.scales.shape[4], :].copy_(self.scales)
+        new.ring.copy_(self.ring)
+        new.lengths.copy_(self.lengths)
         return new
 
     # ---- memory ----
 
     def nbytes(self) -> int:
-        q = sum(t.numel() for t in self.kq) + sum(t.numel() for t in self.vq)
-        scales = sum(t.numel() * t.element_size() for t in self.kmn + self.kst + self.vmn + self.vst)
-        tail = sum(t.numel() * t.element_size() for t in self.tail_k + self.tail_v)
-        return q + scales + tail
+        """Resident bytes of the int8 codes, the scales and the fp16 ring."""
+        return sum(t.numel() * t.element_size() for t in (self.codes, self.scales, self.ring))
 
     def fp16_nbytes(self) -> int:
-        return 2 * self.batch * self.num_slots * self.num_kv_heads * self.max_len * self.head_dim * 2
+        """Bytes an fp16 cache of the same capacity would hold."""
+        return self.codes.numel() * 2
 
     def extra_repr(self) -> str:
-        return (f"max_len={self.max_len}, slots={self.num_slots}, kv={self.nbytes() / 1024 ** 2:.0f}MiB "
-                f"(fp16 same length {self.fp16_nbytes() / 1024 ** 2:.0f}MiB)")
+        mib = 1 << 20
+        return (f"int8 KV, {self.num_slots} layers x {self.batch} x {self.num_kv_heads} heads x {self.max_len} "
+                f"tokens: {self.nbytes() / mib:.0f} MiB ({self.nbytes() / self.fp16_nbytes():.2f} of fp16)")

@@ -18,7 +18,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
-from .kernels import build_nf4_lut, fused_nf4_linear
+from .kernels import MAX_GEMV_M, build_nf4_lut, fused_nf4_linear, nf4_gemv, pack_native
 
 NF4_BLOCK = 64
 _NF4_OFFSET = 0.9677083
@@ -94,27 +94,37 @@ def extract_nf4(weight, quant_state):
 
 
 class NF4Linear(nn.Module):
-    """``nn.Linear``-compatible layer with NF4 weights; forward = one
-    ``nova_nf4_gemv`` launch per 8 input rows (src/nova/quant.py:72-106)."""
+    """``nn.Linear`` replacement holding NF4 weights (the reference's
+    ``NF4Linear(packed, absmax, code, shape, bias)``, src/nova/quant.py:72-106).
+
+    The reference-layout buffers ``packed`` / ``absmax`` / ``code`` / ``lut``
+    are kept under the reference's names (callers and state dicts read them);
+    with fp16 absmax the first forward on a device also packs the B200 unit
+    stream (1088-byte 32 x 64 units, ``nova_nf4_pack_native``) and every later
+    forward streams that, one ``nova_nf4_gemv`` launch per 8 input rows;
+    leading dimensions of ``x`` are kept."""
 
     def __init__(self, packed: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, shape: tuple[int, int],
                  bias: torch.Tensor | None = None) -> None:
         super().__init__()
-        self.out_features, self.in_features = int(shape[0]), int(shape[1])
-        self.register_buffer("packed", packed, persistent=False)
-        self.register_buffer("absmax", absmax, persistent=False)
-        self.register_buffer("code", code, persistent=False)
-        self.register_buffer("lut", build_nf4_lut(code).to(packed.device), persistent=False)
-        if bias is None:
-            self.bias = None
-        else:
-            self.bias = nn.Parameter(bias.detach().clone().to(torch.float16), requires_grad=False)
+        n, k = (int(v) for v in shape)
+        if tuple(packed.shape) != (n, k // 2) or tuple(absmax.shape) != (k // NF4_BLOCK, n):
+            raise ValueError(f"packed {tuple(packed.shape)} / absmax {tuple(absmax.shape)} do not describe a "
+                             f"[{n}, {k}] NF4 weight")
+        self.out_features, self.in_features = n, k
+        tensors = {"packed": packed, "absmax": absmax, "code": code,
+                   "lut": build_nf4_lut(code).to(packed.device),
+                   "bias": None if bias is None else bias.detach().to(torch.float16).clone()}
+        for name, t in tensors.items():
+            self.register_buffer(name, t, persistent=False)
+        self._units: torch.Tensor | None = None
 
     @classmethod
     def from_bnb(cls, lin: nn.Module) -> "NF4Linear":
-        packed, absmax, code, shape = extract_nf4(lin.weight.data, lin.weight.quant_state)
-        bias = lin.bias.data if getattr(lin, "bias", None) is not None else None
-        return cls(packed, absmax, code, shape, bias)
+        """From a bitsandbytes ``Linear4bit`` (duck-typed: ``weight`` with a
+        ``quant_state``, optional ``bias``)."""
+        b = lin.bias.data if getattr(lin, "bias", None) is not None else None
+        return cls(*extract_nf4(lin.weight.data, lin.weight.quant_state), bias=b)
 
     @classmethod
     def from_float(cls, weight: torch.Tensor, bias: torch.Tensor | None = None,
@@ -124,29 +134,55 @@ class NF4Linear(nn.Module):
         packed, absmax = quantize_nf4(weight.to(torch.float16), code, absmax_dtype)
         return cls(packed, absmax, code.to(weight.device), tuple(weight.shape), bias)
 
+    def units(self) -> torch.Tensor:
+        """The B200 unit stream of this weight, packed on first use.  Used when
+        N is a multiple of 32 and absmax is fp16 (the units store fp16 absmax);
+        otherwise forward streams the reference layout as it is."""
+        if self._units is None or self._units.device != self.packed.device:
+            self._units = pack_native(self.packed, self.absmax)
+        return self._units
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return fused_nf4_linear(x, self.packed, self.absmax, self.lut, self.out_features, self.bias)
+        if self.out_features % 32 or self.absmax.dtype != torch.float16:
+            return fused_nf4_linear(x, self.packed, self.absmax, self.lut, self.out_features, self.bias)
+        if x.shape[-1] != self.in_features:
+            raise ValueError(f"x has {x.shape[-1]} features, the layer expects {self.in_features}")
+        rows = x.reshape(-1, self.in_features)
+        if not rows.is_contiguous() or rows.data_ptr() % 16:
+            rows = rows.contiguous()
+        y = torch.empty((rows.shape[0], self.out_features), dtype=torch.float16, device=x.device)
+        units = self.units()
+        for r0 in range(0, rows.shape[0], MAX_GEMV_M):
+            nf4_gemv(rows[r0:r0 + MAX_GEMV_M], units, None, self.lut, y[r0:r0 + MAX_GEMV_M], bias=self.bias,
+                     n=self.out_features)
+        return y.view(*x.shape[:-1], self.out_features)
 
     def extra_repr(self) -> str:
-        return (f"in_features={self.in_features}, out_features={self.out_features}, "
-                f"bias={self.bias is not None}, nf4=sm_100a")
+        return f"{self.in_features} -> {self.out_features}, NF4 blocks of {NF4_BLOCK}, bias={self.bias is not None}"
+
+
+def _quantized_linears(model: nn.Module):
+    """(parent module, attribute name, child) for every child whose weight
+    carries a bitsandbytes ``quant_state``, collected before any replacement."""
+    found = []
+    for parent in model.modules():
+        for attr, child in parent.named_children():
+            if getattr(getattr(child, "weight", None), "quant_state", None) is not None:
+                found.append((parent, attr, child))
+    return found
 
 
 def convert_to_nf4(model: nn.Module, verbose: bool = False, skip: set[str] | None = None) -> int:
-    """Replace every bitsandbytes-style 4-bit linear (a module whose ``weight``
-    carries a ``quant_state``) with :class:`NF4Linear` (src/nova/quant.py:
-    109-135).  Unlike the reference, ``lm_head4`` is converted too by default:
-    the B200 GEMV is faster than the reference's fallback on that shape."""
-    skip = set() if skip is None else skip
-    n_done = 0
-    for name, module in list(model.named_modules()):
-        for child_name, child in list(module.named_children()):
-            if child_name in skip:
-                continue
-            w = getattr(child, "weight", None)
-            if w is not None and getattr(w, "quant_state", None) is not None:
-                setattr(module, child_name, NF4Linear.from_bnb(child))
-                n_done += 1
-                if verbose:
-                    print(f"  nf4: {name}.{child_name} -> {tuple(w.quant_state.shape)}")
-    return n_done
+    """Swap every bitsandbytes-style 4-bit linear in ``model`` for
+    :class:`NF4Linear` and return how many were swapped (the reference's
+    ``convert_to_nf4``, src/nova/quant.py:109-135).  Children named in ``skip``
+    stay as they are; unlike the reference, ``lm_head4`` is not skipped by
+    default (the B200 GEMV is the fast path for that shape too)."""
+    skip = set(skip or ())
+    todo = [(parent, attr, child) for parent, attr, child in _quantized_linears(model) if attr not in skip]
+    for parent, attr, child in todo:
+        setattr(parent, attr, NF4Linear.from_bnb(child))
+    if verbose:
+        shapes = sorted({tuple(child.weight.quant_state.shape) for _, _, child in todo})
+        print(f"nf4: {len(todo)} linears converted, weight shapes {shapes}")
+    return len(todo)

@@ -25,10 +25,43 @@ import numpy as np
 
 from . import kvquant as okv
 from .attention import attend, ring_positions, streaming_attend
-from .nf4 import dequantize_nf4
+from .nf4 import dequantize_nf4, nf4_codebook, quantize_nf4
 from .norm import apply_rope, rms_norm, rope_cos_sin, silu_mul
 
 GT = 64
+LM_HEAD_ROWS = 16384   # lm_head rows dequantized at a time by the batched path (bounds host memory)
+
+
+def random_weights(*, vocab: int, hidden: int, layers: int, q_heads: int, kv_heads: int, inter: int,
+                   head_dim: int = 128, seed: int = 0, std: float = 0.02, norm_jitter: float = 0.1) -> dict:
+    """Seeded random-init decoder weights in the layout ``OracleDecoder`` takes
+    (the dict ``nova_b200.decoder.weights_to_numpy`` produces): every linear
+    N(0, std) in fp32, rounded to fp16, NF4-quantized with fp16 absmax; norm
+    weights 1 + norm_jitter * N(0, 1) in fp16; the embedding N(0, std) fp16
+    with its NF4 copy as the tied lm_head.  numpy's PCG64 stream, so the same
+    seed gives the same weights on any host."""
+    rng = np.random.default_rng(seed)
+    code = nf4_codebook()
+
+    def lin(n, k):
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(std)).astype(np.float16)
+        return quantize_nf4(w, code, absmax_dtype=np.float16)
+
+    def norm(n):
+        return (1.0 + norm_jitter * rng.standard_normal(n, dtype=np.float32)).astype(np.float16)
+
+    out = {"code": code, "layers": []}
+    qd, kvd = q_heads * head_dim, kv_heads * head_dim
+    for _ in range(layers):
+        q, k, v = lin(qd, hidden), lin(kvd, hidden), lin(kvd, hidden)
+        out["layers"].append({
+            "qkv": (np.concatenate([q[0], k[0], v[0]]), np.concatenate([q[1], k[1], v[1]], axis=1)),
+            "o": lin(hidden, qd), "gate": lin(inter, hidden), "up": lin(inter, hidden), "down": lin(hidden, inter),
+            "input_ln": norm(hidden), "post_ln": norm(hidden), "q_norm": norm(head_dim), "k_norm": norm(head_dim)})
+    out["embed"] = (rng.standard_normal((vocab, hidden), dtype=np.float32) * np.float32(std)).astype(np.float16)
+    out["lm_head"] = quantize_nf4(out["embed"], code, absmax_dtype=np.float16)
+    out["final_norm"] = norm(hidden)
+    return out
 
 
 def _f16(a):
@@ -65,6 +98,22 @@ class OracleDecoder:
     def _lin(self, x, key, pa):
         """NF4 linear with fp32 accumulation, fp16 output (src/nova/kernels.py:187-240)."""
         return _f16(np.asarray(x, np.float32) @ self._w(key, pa))
+
+    def _lin_once(self, x, pa, rows: int | None = None):
+        """``_lin`` without keeping the dequantized weight (the batched path
+        uses each weight once); ``rows`` dequantizes that many output rows at a
+        time."""
+        packed, absmax = pa
+        n = packed.shape[0]
+        rows = n if rows is None else rows
+        xf = np.asarray(x, np.float32)
+        out = np.empty((*xf.shape[:-1], n), np.float16)
+        for r0 in range(0, n, rows):
+            r1 = min(n, r0 + rows)
+            w = dequantize_nf4(packed[r0:r1], absmax[:, r0:r1], self.code)
+            out[..., r0:r1] = _f16(xf @ w.T)
+            del w
+        return out
 
     # ---- state exchange with the GPU decoder
     def load_state(self, st: dict) -> None:
@@ -120,6 +169,99 @@ class OracleDecoder:
         x = rms_norm(h, self.W["final_norm"], self.eps)
         logits = self._lin(x, ("lm_head", -1), self.W["lm_head"])
         self.pos = pos + 1
+        return logits, np.argmax(logits.astype(np.float32), axis=-1)
+
+    def decode_teacher_forced(self, tokens: np.ndarray):
+        """``len(tokens)`` decode steps from the current state, step i fed
+        ``tokens[i]`` (``[S, B]`` ids): the same results as calling
+        :meth:`step` S times with those inputs, computed one layer at a time
+        for all steps at once (each weight dequantized once, one matmul per
+        linear).  Step i attends, as the streaming cache does at that step,
+        to the int8 form of every group complete at position p_i = pos + i
+        and to the fp16 K/V of the rest; a group is quantized from the fp16
+        K/V of its 64 positions (the ring the step completing it holds).
+        Returns (logits fp16 ``[S, B, V]``, greedy tokens ``[S, B]``) and leaves
+        the cache and ``pos`` as after the S steps."""
+        tokens = np.asarray(tokens)
+        S, B = tokens.shape
+        hq, hkv, d = self.hq, self.hkv, self.d
+        gq = hq // hkv
+        pos0 = self.pos
+        end = pos0 + S                                   # positions written after the last step
+        q0 = pos0 // GT * GT                             # int8 prefix before the first step
+        if end > self.max_len:
+            raise ValueError(f"{S} steps from position {pos0} exceed the capacity {self.max_len}")
+        steps_pos = pos0 + np.arange(S)
+        cos, sin = rope_cos_sin(steps_pos, d, self.theta)
+        h = np.asarray(self.W["embed"])[tokens]          # fp16 [S, B, H]
+        scale = np.float32(d ** -0.5)
+        for li, lw in enumerate(self.W["layers"]):
+            x = rms_norm(h, lw["input_ln"], self.eps)
+            qkv = self._lin_once(x, lw["qkv"])
+            q = rms_norm(qkv[..., :hq * d].reshape(S, B, hq, d), lw["q_norm"], self.eps)
+            k = rms_norm(qkv[..., hq * d:(hq + hkv) * d].reshape(S, B, hkv, d), lw["k_norm"], self.eps)
+            v = qkv[..., (hq + hkv) * d:].reshape(S, B, hkv, d)
+            q = apply_rope(q, cos[:, None, None], sin[:, None, None])
+            k = apply_rope(k, cos[:, None, None], sin[:, None, None])
+            # fp16 K/V of positions [q0, end): the prompt's open group from the ring, then the steps
+            fk = np.empty((B, hkv, end - q0, d), np.float16)
+            fv = np.empty_like(fk)
+            for p in range(q0, pos0):
+                fk[:, :, p - q0] = self.tail_k[li][:, :, p % GT]
+                fv[:, :, p - q0] = self.tail_v[li][:, :, p % GT]
+            fk[:, :, pos0 - q0:] = k.transpose(1, 2, 0, 3)
+            fv[:, :, pos0 - q0:] = v.transpose(1, 2, 0, 3)
+            for g in range(q0 // GT, end // GT):         # groups completed during these steps
+                for src, codes, mn, st in ((fk, self.kq[li], self.kmn[li], self.kst[li]),
+                                           (fv, self.vq[li], self.vmn[li], self.vst[li])):
+                    c, m_, s_ = okv.quantize_ring(src[:, :, g * GT - q0:(g + 1) * GT - q0])
+                    codes[:, :, g * GT:(g + 1) * GT] = c
+                    mn[:, :, g] = m_
+                    st[:, :, g] = s_
+            qmax = end // GT * GT
+            kd = okv.dequantize_int8_token(self.kq[li][:, :, :qmax], self.kmn[li][:, :, :qmax // GT],
+                                           self.kst[li][:, :, :qmax // GT], GT).astype(np.float32)
+            vd = okv.dequantize_int8_token(self.vq[li][:, :, :qmax], self.vmn[li][:, :, :qmax // GT],
+                                           self.vst[li][:, :, :qmax // GT], GT).astype(np.float32)
+            fkf, fvf = fk.astype(np.float32), fv.astype(np.float32)
+            o = np.empty((S, B, hq * d), np.float16)
+            qf = q.astype(np.float32)                    # [S, B, hq, d]
+            i = 0
+            while i < S:                                 # steps that share one int8 prefix length
+                ql = (steps_pos[i] + 1) // GT * GT
+                j = i
+                while j < S and (steps_pos[j] + 1) // GT * GT == ql:
+                    j += 1
+                last = steps_pos[j - 1]
+                n_f = last + 1 - ql                      # fp16 keys [ql, last]
+                fpos = ql + np.arange(n_f)
+                ok = fpos[None, :] <= steps_pos[i:j, None]          # [steps, n_f] causal
+                for b in range(B):
+                    for hh in range(hkv):
+                        kk = np.concatenate([kd[b, hh, :ql], fkf[b, hh, ql - q0:last + 1 - q0]])
+                        vv = np.concatenate([vd[b, hh, :ql], fvf[b, hh, ql - q0:last + 1 - q0]])
+                        qq = qf[i:j, b, hh * gq:(hh + 1) * gq].reshape(-1, d)        # [steps*gq, d]
+                        sc = (qq @ kk.T) * scale
+                        valid = np.concatenate([np.ones((j - i, ql), bool), ok], axis=1)
+                        sc = np.where(np.repeat(valid, gq, axis=0), sc, -np.inf)
+                        mx = sc.max(axis=-1, keepdims=True)
+                        pr = np.exp(sc - mx).astype(np.float32)
+                        res = (pr @ vv) / pr.sum(axis=-1, keepdims=True)
+                        o[i:j, b, hh * gq * d:(hh + 1) * gq * d] = res.reshape(j - i, gq * d).astype(np.float16)
+                i = j
+            h = _f16(h.astype(np.float32) + self._lin_once(o, lw["o"]).astype(np.float32))
+            x2 = rms_norm(h, lw["post_ln"], self.eps)
+            act = silu_mul(self._lin_once(x2, lw["gate"]), self._lin_once(x2, lw["up"]))
+            h = _f16(h.astype(np.float32) + self._lin_once(act, lw["down"]).astype(np.float32))
+            u = end - 1
+            for slot in range(GT):                       # the ring as the last step leaves it
+                p = u - (u - slot) % GT
+                if p >= q0:
+                    self.tail_k[li][:, :, slot] = fk[:, :, p - q0]
+                    self.tail_v[li][:, :, slot] = fv[:, :, p - q0]
+        x = rms_norm(h, self.W["final_norm"], self.eps)
+        logits = self._lin_once(x, self.W["lm_head"], rows=LM_HEAD_ROWS)
+        self.pos = end
         return logits, np.argmax(logits.astype(np.float32), axis=-1)
 
     def prefill_chunked(self, ids: np.ndarray, chunk: int):

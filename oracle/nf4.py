@@ -68,7 +68,9 @@ def quantize_nf4(w: np.ndarray, code: np.ndarray | None = None, absmax_dtype=np.
     am = np.abs(wf).max(axis=-1)                                   # [N, K/64] fp32
     safe = np.where(am > 0, am, np.float32(1.0)).astype(np.float32)
     v = (wf / safe[..., None]).astype(np.float32)
-    idx = np.searchsorted(nf4_midpoints(code), v, side="left").astype(np.uint8)
+    idx = np.zeros(v.shape, np.uint8)
+    for mid in nf4_midpoints(code):       # level = number of thresholds strictly below v (ties go low)
+        idx += v > mid
     idx = idx.reshape(n, k)
     packed = ((idx[:, 0::2] << 4) | idx[:, 1::2]).astype(np.uint8)
     return packed, np.ascontiguousarray(am.T).astype(absmax_dtype)

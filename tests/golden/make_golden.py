@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory by running the REFERENCE's own
 Python code (captain-wangrun-cn/Nova, ``src/nova``) on seeded inputs.
 
-Run in a checkout that has the reference source available:
+Run with the reference's ``src`` directory named in ``NOVA_REF_SRC`` (required):
 
-    NOVA_REF_SRC=/path/to/Nova/src python tests/golden/make_golden.py
+    NOVA_REF_SRC=/path/to/Nova/src python tests/golden/make_golden.py [fixture ...]
 
 The fixtures pin the CPU oracle (``oracle/``) to the reference; the GPU tests
 then compare the CUDA kernels with the oracle.  Only the reference functions
@@ -11,10 +11,14 @@ that run without Triton/CUDA/bitsandbytes are used (kvquant, the KVInt8Cache
 prefill + ring path on CPU, SDPA math on CPU, LeanRMSNorm "exact",
 apply_rotary_pos_emb with the transformers Qwen3-VL rotary, build_nf4_lut,
 extract_nf4 with a non-nested quant state, the chat CLI's sample_next (its
-candidate ids and final probabilities), and -- for the decoder fixture --
-a random-init reference NovaTextModel whose linears run the NF4 dequant formula
-of tests/test_nf4_linear.py:46-57 and whose KVInt8Cache.attend is the
-reference's own single-softmax ground truth (tests/test_kvattn_stream.py:68-83)).
+candidate ids and final probabilities), and the decoder: the reference's own
+GraphDecoder (prefill + eager decode steps, quant="int8") over its
+NovaForCausalLM / NovaTextModel / LeanDecoderLayer on a transformers
+Qwen3VLTextModel at Qwen3-VL-4B widths, with every linear replaced by the
+arithmetic of the reference's NF4 GEMV (fp16 codebook x absmax, fp32
+accumulation, fp16 out) and KVInt8Cache.attend replaced by the single-softmax
+ground truth of the reference's streaming test (tests/test_kvattn_stream.py:
+68-83); the rest of the cache runs unchanged).
 """
 
 from __future__ import annotations
@@ -31,7 +35,9 @@ import torch.nn.functional as F
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
 sys.path.insert(0, str(REPO))
-sys.path.insert(0, os.environ.get("NOVA_REF_SRC", "/root/reference/src"))
+if not os.environ.get("NOVA_REF_SRC"):
+    raise SystemExit("set NOVA_REF_SRC to the reference's src directory (the one containing nova/)")
+sys.path.insert(0, os.environ["NOVA_REF_SRC"])
 
 from torch.nn.attention import SDPBackend, sdpa_kernel  # noqa: E402
 
@@ -261,8 +267,129 @@ def sampling_fixture() -> None:
     _save("sampling.npz", **out)
 
 
+# decoder fixture: Qwen3-VL-4B widths, 2 layers, a smaller vocabulary (keeps the fixture and the CPU check small)
+DECODER = dict(vocab=4096, hidden=2560, layers=2, q_heads=32, kv_heads=8, inter=9728)
+DECODER_SEED, DECODER_PROMPT, DECODER_STEPS, DECODER_MAX_LEN = 20, 150, 72, 256
+
+
+class _NF4GemvLinear(nn.Module):
+    """The arithmetic of the reference's NF4 linear (src/nova/kernels.py:187-240
+    with build_nf4_lut :170-182): W = fp16(code)[idx] * absmax, x in fp32,
+    fp32 accumulation, fp16 output.  Layout as tests/test_nf4_linear.py:46-57
+    (high nibble = even element)."""
+
+    def __init__(self, packed: np.ndarray, absmax: np.ndarray, code: np.ndarray) -> None:
+        super().__init__()
+        pk = torch.from_numpy(np.ascontiguousarray(packed)).long()
+        n, k2 = pk.shape
+        c16 = torch.from_numpy(code).to(torch.float16).float()
+        vals = torch.empty(n, 2 * k2, dtype=torch.float32)
+        vals[:, 0::2] = c16[pk >> 4]
+        vals[:, 1::2] = c16[pk & 0x0F]
+        am = torch.from_numpy(np.ascontiguousarray(absmax)).float().t().repeat_interleave(64, dim=1)
+        self.register_buffer("w", vals * am)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return (x.float() @ self.w.t()).to(torch.float16)
+
+
+def _streaming_truth(self, query: torch.Tensor, layer_idx: int) -> torch.Tensor:
+    """KVInt8Cache.attend ground truth (tests/test_kvattn_stream.py:68-83): the
+    int8 prefix [0, _qlen) dequantized by the reference's dequantize_int8 and
+    the ring tokens [_qlen, _written) in fp16, one softmax, fp32 math, fp16 out."""
+    qlen, written = int(self._qlen.item()), int(self._written.item())
+    ks, vs = [], []
+    if qlen:
+        g = qlen // self.group
+        ks.append(ref_dequant(self.kq[layer_idx][:, :, :qlen], self.kmn[layer_idx][:, :, :g],
+                              self.kst[layer_idx][:, :, :g], self.group, "token"))
+        vs.append(ref_dequant(self.vq[layer_idx][:, :, :qlen], self.vmn[layer_idx][:, :, :g],
+                              self.vst[layer_idx][:, :, :g], self.group, "token"))
+    slots = torch.arange(qlen, written) % self.group
+    ks.append(self.tail_k[layer_idx][:, :, slots])
+    vs.append(self.tail_v[layer_idx][:, :, slots])
+    k, v = torch.cat(ks, dim=2).float(), torch.cat(vs, dim=2).float()
+    b, h, n, d = k.shape
+    gq = query.shape[1] // h
+    k = k[:, :, None].expand(b, h, gq, n, d).reshape(b, h * gq, n, d)
+    v = v[:, :, None].expand(b, h, gq, n, d).reshape(b, h * gq, n, d)
+    with sdpa_kernel([SDPBackend.MATH]):
+        out = F.scaled_dot_product_attention(query.float(), k, v, scale=d ** -0.5)
+    return out.to(torch.float16)
+
+
+def decoder_fixture() -> None:
+    """The reference's int8 greedy decode (GraphDecoder, src/nova/decode.py:
+    224-320) on a random-init model: prompt prefill, then eager ``_body`` steps
+    (the step the reference captures), logits and greedy tokens saved."""
+    from transformers import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel, Qwen3VLTextRotaryEmbedding
+
+    from nova.config import NovaConfig
+    from nova.decode import GraphDecoder
+    from nova.model import NovaForCausalLM, NovaTextModel
+    from oracle.decoder import random_weights   # inputs only: the seeded NF4 weights
+
+    c = DECODER
+    W = random_weights(**c, seed=DECODER_SEED)
+    hcfg = Qwen3VLTextConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["inter"],
+                             num_hidden_layers=c["layers"], num_attention_heads=c["q_heads"],
+                             num_key_value_heads=c["kv_heads"], head_dim=D, rms_norm_eps=1e-6,
+                             rope_parameters={"rope_type": "default", "rope_theta": 5_000_000.0,
+                                              "mrope_section": [24, 20, 20], "mrope_interleaved": True})
+    torch.manual_seed(0)
+    hf = Qwen3VLTextModel(hcfg).to(torch.float16).eval()
+    # from_pretrained(dtype=float16), as the reference loads the model (src/nova/loader.py:29-42),
+    # leaves the rotary's inv_freq buffer in fp32; .to(float16) above rounded it, so rebuild it
+    hf.rotary_emb = Qwen3VLTextRotaryEmbedding(hcfg)
+    code = W["code"]
+    qd, kvd = c["q_heads"] * D, c["kv_heads"] * D
+    with torch.no_grad():
+        hf.embed_tokens.weight.copy_(torch.from_numpy(W["embed"]))
+        hf.norm.weight.copy_(torch.from_numpy(W["final_norm"]))
+        for layer, lw in zip(hf.layers, W["layers"]):
+            layer.input_layernorm.weight.copy_(torch.from_numpy(lw["input_ln"]))
+            layer.post_attention_layernorm.weight.copy_(torch.from_numpy(lw["post_ln"]))
+            layer.self_attn.q_norm.weight.copy_(torch.from_numpy(lw["q_norm"]))
+            layer.self_attn.k_norm.weight.copy_(torch.from_numpy(lw["k_norm"]))
+            pk, am = lw["qkv"]
+            for name, r0, r1 in (("q_proj", 0, qd), ("k_proj", qd, qd + kvd), ("v_proj", qd + kvd, qd + 2 * kvd)):
+                setattr(layer.self_attn, name, _NF4GemvLinear(pk[r0:r1], am[:, r0:r1], code))
+            layer.self_attn.o_proj = _NF4GemvLinear(*lw["o"], code)
+            layer.mlp.gate_proj = _NF4GemvLinear(*lw["gate"], code)
+            layer.mlp.up_proj = _NF4GemvLinear(*lw["up"], code)
+            layer.mlp.down_proj = _NF4GemvLinear(*lw["down"], code)
+    ncfg = NovaConfig.from_hf(hcfg, num_prefix_layers=1, num_suffix_layers=0, num_paths=1)
+    nova = NovaForCausalLM(NovaTextModel(hf, ncfg, norm_impl="exact")).eval()
+    nova.lm_head4 = _NF4GemvLinear(*W["lm_head"], code)
+    RefCache.attend = _streaming_truth
+    dec = GraphDecoder(nova, max_len=DECODER_MAX_LEN, batch=1, device="cpu", quant="int8")
+    prompt = torch.randint(0, c["vocab"], (1, DECODER_PROMPT), generator=torch.Generator().manual_seed(DECODER_SEED))
+    tokens, logits = [], []
+    with torch.inference_mode():
+        out = dec.prefill(prompt)
+        prefill_logits = out[0, -1].clone()
+        tokens.append(int(dec.input_ids.item()))
+        cache, q = dec.cache, DECODER_PROMPT // GT * GT
+        state = {}   # the cache after the prefill, so the decode steps can be checked on their own
+        for li in range(c["layers"]):
+            for nm in ("kq", "vq"):
+                state[f"state_{nm}{li}"] = getattr(cache, nm)[li][:, :, :q].clone()
+            for nm in ("kmn", "kst", "vmn", "vst"):
+                state[f"state_{nm}{li}"] = getattr(cache, nm)[li][:, :, :q // GT].clone()
+            state[f"state_tail_k{li}"] = cache.tail_k[li].clone()
+            state[f"state_tail_v{li}"] = cache.tail_v[li].clone()
+        for _ in range(DECODER_STEPS):
+            lg = dec._body()
+            logits.append(lg[0, -1].clone())
+            tokens.append(int(dec.input_ids.item()))
+    _save("decoder.npz", prompt=prompt[0], prefill_logits=prefill_logits, tokens=np.array(tokens, np.int64),
+          logits=torch.stack(logits), seed=DECODER_SEED, max_len=DECODER_MAX_LEN,
+          dims=np.array([c[k] for k in ("vocab", "hidden", "layers", "q_heads", "kv_heads", "inter")]), **state)
+
+
 def main() -> None:
-    which = set(sys.argv[1:]) or {"kvquant", "ring", "attention", "nf4", "norm_rope", "sampling"}
+    which = set(sys.argv[1:]) or {"kvquant", "ring", "attention", "nf4", "norm_rope", "sampling", "decoder"}
     if "kvquant" in which:
         kvquant_fixture()
     if "ring" in which:
@@ -275,6 +402,8 @@ def main() -> None:
         norm_rope_fixture()
     if "sampling" in which:
         sampling_fixture()
+    if "decoder" in which:
+        decoder_fixture()
 
 
 if __name__ == "__main__":

@@ -336,3 +336,55 @@ def test_streaming_graph_capture_bit_identical(cuda_lib):
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
     del graph
+
+
+# ---------------------------------------------------------------- BASELINE configs 1 and 3 at full size
+
+
+@pytest.mark.parametrize("ctx,batch,window", [(131072, 1, 0), (32768, 16, 0), (32768, 4, 4096)])
+def test_config3_full_size_matches_oracle(cuda_lib, ctx, batch, window):
+    """BASELINE config 3 shapes (32 q / 8 KV heads, the decoder's split size for
+    that capacity): full-causal decode at ctx 131072 (batch 1) and 32768
+    (batch 16), and the sliding window of 4096 at ctx 32768 (batch 4).  K/V are
+    N(0, 0.7) fp16 quantized on the GPU (nova_kv_quant_int8, bit-exact with the
+    reference quantizer); the oracle dequantizes the same codes and attends in
+    fp32, one batch row at a time."""
+    from nova_b200.kvattn import int8_attn_decode, pack_int8_kv, pick_chunk
+
+    g = torch.Generator(device="cuda").manual_seed(ctx + batch + window)
+    k = (torch.randn(batch, H_KV, ctx, D, generator=g, device="cuda") * 0.7).half()
+    v = (torch.randn(batch, H_KV, ctx, D, generator=g, device="cuda") * 0.7).half()
+    q = (torch.randn(batch, HQ, 1, D, generator=g, device="cuda") * 0.7).half()
+    packed = pack_int8_kv(k, v)
+    del k, v
+    chunk = pick_chunk(ctx, batch, H_KV, HQ, torch.cuda.get_device_properties(0).multi_processor_count)
+    got = int8_attn_decode(q, *packed, used=ctx, chunk=chunk, window=window)[:, :, 0].cpu().numpy()
+    qh = q[:, :, 0].cpu().numpy()
+    for b in range(batch):
+        host = [t[b:b + 1].cpu().numpy() for t in packed]
+        want, _ = oatt.fused_prefix_attend(qh[b:b + 1], *host, ctx, window=window)
+        assert_ulp_or_abs(got[b:b + 1], want, 2.0, 1e-5, f"ctx={ctx} batch row {b} window={window}")
+
+
+def test_config1_append_and_attend_through_the_cache(cuda_lib):
+    """BASELINE config 1 exactly: one layer, batch 1, 32 q / 8 KV heads,
+    ctx 4096, q/K/V N(0, 1) fp16, through KVInt8Cache (prefill of 4095 tokens,
+    then the decode append of token 4096, which completes group 63 and
+    requantizes it, then attend).  The appended group's codes and scales are
+    bit-exact with the token-axis quantizer over those 64 tokens, and the
+    output is within the reference's attention criterion."""
+    g = torch.Generator().manual_seed(4096)
+    k = torch.randn(1, H_KV, 4096, D, generator=g).half()
+    v = torch.randn(1, H_KV, 4096, D, generator=g).half()
+    q = torch.randn(1, HQ, 1, D, generator=g).half()
+    cache, got = _cache_step(k, v, q)
+    assert int(cache._qlen.item()) == 4096 and int(cache._written.item()) == 4096
+    kq, kmn, kst = okv.quantize_int8_token(k[:, :, 4032:].numpy(), 64)
+    vq, vmn, vst = okv.quantize_int8_token(v[:, :, 4032:].numpy(), 64)
+    np.testing.assert_array_equal(cache.kq[0][:, :, 4032:4096].cpu().numpy(), kq)
+    np.testing.assert_array_equal(cache.vq[0][:, :, 4032:4096].cpu().numpy(), vq)
+    for have, want in ((cache.kmn[0][:, :, 63:64], kmn), (cache.kst[0][:, :, 63:64], kst),
+                       (cache.vmn[0][:, :, 63:64], vmn), (cache.vst[0][:, :, 63:64], vst)):
+        np.testing.assert_array_equal(have.cpu().numpy().view(np.uint16), want.view(np.uint16))
+    want, _ = _oracle_stream(cache, q)
+    assert_ulp_or_abs(got[:, :, 0].cpu().numpy(), want, 2.0, 1e-5, "config 1")

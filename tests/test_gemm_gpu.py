@@ -1,5 +1,5 @@
-"""GPU: batched NF4 GEMM (nova_nf4_gemm, M up to 64; tcgen05 units from
-pack_tc and the mma.sync kernel on pack_native units) against the CPU oracle.
+"""GPU: batched NF4 GEMM (nova_nf4_gemm on the tcgen05 tensor cores, M up to
+64, units from pack_tc) against the CPU oracle.
 
 The GEMM computes x @ dequant(W)^T with the reference's dequantized weight
 fp16(code * absmax) and fp32 accumulation, so each fp16 output must be within
@@ -40,23 +40,42 @@ def _oracle(x, packed, absmax):
     return x.float().cpu().numpy() @ w.astype(np.float32).T
 
 
-@pytest.mark.parametrize("layout", [2, 1])
 @pytest.mark.parametrize("m", [9, 16, 37, 64])
 @pytest.mark.parametrize("n,k", [(1024, 2560), (2560, 9728), (6144, 2560), (96, 192), (3072, 2560), (2560, 2048),
                                  (2560, 4864), (2560, 1216)])
-def test_gemm_plain_matches_dequant_matmul(cuda_lib, m, n, k, layout):
-    from nova_b200.kernels import nf4_gemm, pack_native, pack_tc
+def test_gemm_plain_matches_dequant_matmul(cuda_lib, m, n, k):
+    from nova_b200.kernels import nf4_gemm, pack_tc
 
     packed, absmax = _weights(n, k, n + k + m)
     x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).half()
     out = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
-    units = pack_tc(packed, absmax) if layout == 2 else pack_native(packed, absmax)
-    nf4_gemm(x.cuda(), units, _lut(), out, n=n, layout=layout)
+    nf4_gemm(x.cuda(), pack_tc(packed, absmax), _lut(), out, n=n)
     want = _oracle(x, packed, absmax)
     got = out.float().cpu().numpy()
     scale = float(np.abs(want).max())
     assert_ulp_or_abs(got, want.astype(np.float16), 1.0, 1e-5 * scale, f"gemm m={m} {n}x{k}")
     assert np.abs(got - want).max() <= 1e-2 * scale
+
+
+@pytest.mark.parametrize("m", [64, 33])
+def test_gemm_lm_head_shape_sampled_rows(cuda_lib, m):
+    """The 4-bit lm_head of config 5 (N = 151936, K = 2560) at batch 64 and a
+    ragged 33: every row is computed; 3000 sampled rows (the first and last
+    tiles included) are checked against the oracle's dequant-matmul."""
+    from nova_b200.kernels import nf4_gemm, pack_tc
+
+    n, k = 151936, 2560
+    packed, absmax = _weights(n, k, 151936 + m)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).half()
+    out = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
+    nf4_gemm(x.cuda(), pack_tc(packed, absmax), _lut(), out, n=n)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    rows = np.unique(np.concatenate([np.arange(128), np.arange(n - 128, n),
+                                     np.random.default_rng(m).choice(n, 2744, replace=False)]))
+    want = _oracle(x, packed[rows], absmax[:, rows])
+    scale = float(np.abs(want).max())
+    assert_ulp_or_abs(got[:, rows], want.astype(np.float16), 1.0, 1e-5 * scale, f"lm_head m={m}")
 
 
 def test_gemm_epilogues_and_repeat(cuda_lib):

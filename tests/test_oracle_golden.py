@@ -150,3 +150,103 @@ def test_rope_matches_reference():
     ke = onorm.apply_rope(g["rope_k"], cos[None, None], sin[None, None])
     np.testing.assert_array_equal(qe.view(np.uint16), g["rope_qe"].view(np.uint16))
     np.testing.assert_array_equal(ke.view(np.uint16), g["rope_ke"].view(np.uint16))
+
+
+# ---------------------------------------------------------------- decoder
+
+def _decoder_fixture():
+    """The fixture, the seeded weights it was made with and an oracle decoder."""
+    from oracle.decoder import OracleDecoder, random_weights
+
+    g = golden("decoder.npz")
+    vocab, hidden, layers, hq, hkv, inter = (int(x) for x in g["dims"])
+    W = random_weights(vocab=vocab, hidden=hidden, layers=layers, q_heads=hq, kv_heads=hkv, inter=inter,
+                       seed=int(g["seed"]))
+    return g, lambda: OracleDecoder(W, hidden=hidden, q_heads=hq, kv_heads=hkv, max_len=int(g["max_len"]))
+
+
+def _load_reference_state(orc, g) -> None:
+    """Seed the oracle with the reference cache as its prefill left it."""
+    T, L = len(g["prompt"]), orc.max_len
+    q = T // 64 * 64
+    st = {"pos": T}
+    for name in ("kq", "vq", "kmn", "kst", "vmn", "vst", "tail_k", "tail_v"):
+        st[name] = []
+        for li in range(len(orc.W["layers"])):
+            a = g[f"state_{name}{li}"]
+            if name in ("kq", "vq"):
+                full = np.zeros(a.shape[:2] + (L, a.shape[3]), a.dtype)
+                full[:, :, :q] = a
+            elif name in ("kmn", "kst", "vmn", "vst"):
+                full = np.zeros(a.shape[:2] + (-(-L // 64), a.shape[3]), a.dtype)
+                full[:, :, :q // 64] = a
+            else:
+                full = a.copy()
+            st[name].append(full)
+    orc.load_state(st)
+
+
+def _check_steps(got_logits, want_logits, got_tokens, want_tokens, max_frac, mean_frac, what):
+    """Per step: logits within max_frac (max) / mean_frac (mean) of the
+    logit range; tokens equal unless the reference's own top-2 margin is
+    within twice the observed logit error (a genuine near-tie)."""
+    for i in range(len(want_tokens)):
+        want = want_logits[i].astype(np.float32)
+        got = got_logits[i].astype(np.float32)
+        scale = float(np.abs(want).max())
+        d = np.abs(got - want)
+        assert d.max() <= max_frac * scale and d.mean() <= mean_frac * scale, \
+            f"{what} step {i}: logits differ by max {d.max():.3e} mean {d.mean():.3e} (range {scale:.3f})"
+        if got_tokens[i] != want_tokens[i]:
+            top2 = np.sort(want)[-2:]
+            assert top2[1] - top2[0] <= 2 * d.max(), f"{what} step {i}: token differs without a near-tie"
+
+
+def test_decoder_matches_reference_graph_decoder():
+    """The oracle decoder (oracle/decoder.py) against the reference's own int8
+    greedy decode (GraphDecoder prefill + _body steps over NovaTextModel on a
+    random-init Qwen3-VL text model at real widths, 2 layers; fixture from
+    tests/golden/make_golden.py).  (1) prefill: last-position logits and first
+    token; (2) 72 decode steps from the reference's own post-prefill cache,
+    fed the reference's tokens: per-step logits and greedy tokens; (3) the
+    same steps after the oracle's own prefill."""
+    g, make = _decoder_fixture()
+    tokens = g["tokens"]
+    orc = make()
+    plog, ptok = orc.prefill(g["prompt"][None])
+    want = g["prefill_logits"].astype(np.float32)
+    assert np.abs(plog[0].astype(np.float32) - want).max() <= 4e-3 * np.abs(want).max()
+    assert int(ptok[0]) == int(tokens[0])
+    lg, tk = orc.decode_teacher_forced(tokens[:-1, None])
+    _check_steps(lg[:, 0], g["logits"], tk[:, 0], tokens[1:], 3e-3, 5e-4, "after the oracle's prefill")
+    orc = make()
+    _load_reference_state(orc, g)
+    lg, tk = orc.decode_teacher_forced(tokens[:-1, None])
+    _check_steps(lg[:, 0], g["logits"], tk[:, 0], tokens[1:], 2.5e-3, 4e-4, "from the reference's cache")
+    assert np.array_equal(tk[:, 0], tokens[1:]), "greedy tokens differ from the reference's"
+
+
+def test_decoder_batched_steps_equal_single_steps():
+    """decode_teacher_forced (all steps per layer at once) against step() called
+    once per token, on a small model across two group boundaries."""
+    import copy
+
+    from oracle.decoder import OracleDecoder, random_weights
+
+    W = random_weights(vocab=512, hidden=256, layers=2, q_heads=8, kv_heads=2, inter=512, seed=3)
+    a = OracleDecoder(W, hidden=256, q_heads=8, kv_heads=2, max_len=320, batch=2)
+    _, first = a.prefill(np.random.default_rng(1).integers(0, 512, (2, 100)))
+    b = copy.deepcopy(a)
+    toks, logs = [first], []
+    for _ in range(90):
+        lg, t = a.step(toks[-1])
+        logs.append(lg)
+        toks.append(t)
+    lb, tb = b.decode_teacher_forced(np.stack(toks[:-1]))
+    la = np.stack(logs).astype(np.float32)
+    assert np.abs(la - lb.astype(np.float32)).max() <= 2e-3 * np.abs(la).max()
+    assert np.array_equal(np.stack(toks[1:]), tb)
+    assert a.pos == b.pos == 190
+    for li in range(2):   # the groups completed during the steps agree to within one code
+        d = np.abs(a.kq[li][:, :, :128].astype(int) - b.kq[li][:, :, :128].astype(int))
+        assert d.max() <= 1

@@ -59,6 +59,15 @@ def _args(q, kv, tail, scal, out, lse, *, max_len, chunk, n_splits, window, work
     return a
 
 
+def _noalloc_error() -> int:
+    """The no-allocation entry point's error word on the current device (read and cleared)."""
+    from nova_b200 import _lib
+
+    val = ctypes.c_int(-1)
+    _lib.check(_lib.lib().nova_attn_noalloc_read_error(ctypes.byref(val)), "nova_attn_noalloc_read_error")
+    return int(val.value)
+
+
 def _both(b, hq, hkv, max_len, qlen, written, chunk, window, seed):
     from nova_b200 import _lib
     from nova_b200.kvattn import new_workspace
@@ -81,6 +90,7 @@ def _both(b, hq, hkv, max_len, qlen, written, chunk, window, seed):
     assert np.isfinite(o_new).all() and np.isfinite(l_new).all()
     assert_ulp_or_abs(o_new, o_ref.astype(np.float16), 2.0, 1e-5, f"noalloc out b={b} hq={hq}")
     np.testing.assert_allclose(l_new, l_ref, rtol=1e-6, atol=1e-6)
+    assert _noalloc_error() == 0, "a bounded wait of the no-allocation call gave up"
 
 
 def test_noalloc_matches_workspace_entry_two_calls(cuda_lib):
@@ -88,6 +98,15 @@ def test_noalloc_matches_workspace_entry_two_calls(cuda_lib):
     _both(b=2, hq=32, hkv=8, max_len=3072, qlen=2944, written=2990, chunk=256, window=0, seed=1)
     # second call right after: another shape and a sliding window, over the same scratch array
     _both(b=1, hq=8, hkv=4, max_len=1536, qlen=1408, written=1450, chunk=128, window=700, seed=2)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in one process")
+def test_noalloc_on_a_second_device(cuda_lib):
+    """The scratch address and the kernel attributes are per device: the same
+    comparison with device 1 current, after calls on device 0."""
+    _both(b=1, hq=32, hkv=8, max_len=1024, qlen=960, written=1000, chunk=256, window=0, seed=4)
+    with torch.cuda.device(1):
+        _both(b=1, hq=32, hkv=8, max_len=1024, qlen=960, written=1000, chunk=256, window=0, seed=5)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda_lib):
