@@ -104,7 +104,11 @@ NOVA_API int nova_kv_append_int8(const void* k_new, const void* v_new, int64_t n
  * u - ((u - i) mod group), u = written-1, valid when qlen <= p <= u), one
  * softmax over both, split-K over `chunk`-token splits with the combine done
  * by the last CTA of each (batch, kv head).  window > 0 keeps positions
- * p > u - window (prefix and tail); first (optional) drops p < first.
+ * p > u - window (prefix and tail); first (optional) drops p < first.  With a
+ * window and n_splits * chunk >= window + 64 the splits are laid over the
+ * window (split s starts s * chunk tokens after the window's first 64-token
+ * group), so a grid of about (window + 64) / chunk splits suffices whatever
+ * max_len is; otherwise split s covers [s * chunk, (s + 1) * chunk).
  * Lengths are device scalars so a captured graph stays valid; n_splits fixes
  * the grid (ceil(max_len/chunk) for a graph).  lse (optional) receives
  * log-sum-exp of the scaled scores (-inf and out = 0 when nothing is valid).

@@ -139,9 +139,11 @@ def bench_attn(ctx: int, batch: int = 1, q_heads: int = 32, kv_heads: int = 8, w
     written = ctx
     per_set = batch * kv_heads * max_len * 2 * d
     sets = sets or max(2, min(32, (768 << 20) // per_set + 1))
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    span = min(max_len, window + GROUP_T) if window else max_len   # tokens the splits must cover
     if not chunk:
-        chunk = pick_chunk(max_len, batch, kv_heads, q_heads, torch.cuda.get_device_properties(dev).multi_processor_count)
-    n_splits = -(-max_len // chunk)
+        chunk = pick_chunk(span, batch, kv_heads, q_heads, sms)
+    n_splits = -(-span // chunk)
     g = torch.Generator(device=dev).manual_seed(seed)
     ng = -(-max_len // GROUP_T)
     caches = []

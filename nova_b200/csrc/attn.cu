@@ -71,6 +71,7 @@ struct Params {
     float* part;
     int kv_heads, gq, max_len, groups, chunk, n_splits, s_total, window;
     int prefetch_first;       // one-wave launches: each warp's first group is prefetched into L2 before the wait
+    int win_rel;              // window > 0: split s covers [base + s*chunk, ...), base = the window's first group
     float scale_log2;
     // Fused q/k norm + RoPE + ring append (the FUSED kernel only; the
     // standalone kernel's job, src/nova/layers.py:24-36 + kvattn.py append):
@@ -385,7 +386,7 @@ __global__ void __launch_bounds__(THREADS, 3)
     // The group this warp takes first when no prefix is masked (every group
     // of the chunk lies inside the cache allocation, so a copy is in bounds).
     const int spec = int(int64_t(split) * p.chunk / GT) + warp;
-    const bool spec_on = split < p.n_splits && spec < p.groups &&
+    const bool spec_on = !p.win_rel && split < p.n_splits && spec < p.groups &&
                          int64_t(spec) * GT < int64_t(split) * p.chunk + p.chunk;
     __half nwq = __float2half_rn(0.f), nwk = __float2half_rn(0.f);
     if (FUSED) {   // weights: read before the dependency wait
@@ -544,8 +545,10 @@ __global__ void __launch_bounds__(THREADS, 3)
     float m_run = -INFINITY, l_run = 0.f;
 
     if (split < p.n_splits) {
-        const int64_t t_begin = max(int64_t(split) * p.chunk, lo);
-        const int64_t t_end = min(int64_t(split) * p.chunk + p.chunk, pend);
+        // window-relative splits start at the window's first group (known only after the lengths are read)
+        const int64_t s0 = (p.win_rel ? lo / GT * GT : int64_t(0)) + int64_t(split) * p.chunk;
+        const int64_t t_begin = max(s0, lo);
+        const int64_t t_end = min(s0 + p.chunk, pend);
         if (t_begin < t_end) {
             const int g_first = int(t_begin / GT), g_last = int((t_end - 1) / GT);
             int gi = g_first + warp;
@@ -872,6 +875,9 @@ static int attn_launch(const nova_attn_int8_args* a, const nova_qk_args* qk, voi
     p.vq = (const uint8_t*)a->vq;
     // every CTA resident at once (3 per SM): the first groups can be prefetched while the previous kernel ends
     p.prefetch_first = (a->n_splits > 0 && s_total * a->kv_heads * a->batch <= 3 * int64_t(sm_count())) ? 1 : 0;
+    // a window that the splits can cover from its own first group: map the splits onto the window, so a
+    // small window gets all the splits (the grid need not cover the whole capacity)
+    p.win_rel = (a->window > 0 && a->n_splits > 0 && a->n_splits * a->chunk >= a->window + GT) ? 1 : 0;
     p.qkv = nullptr;
     p.qkv_b = 0;
     p.q_norm_w = p.k_norm_w = p.cos = p.sin = nullptr;

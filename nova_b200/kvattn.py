@@ -248,7 +248,10 @@ def int8_attn_decode(
         return out
 
     if n_splits is None:
-        n_splits = -(-(length if used_is_device else used) // chunk)
+        span = length if used_is_device else used
+        if window:   # the kernel lays the splits over the window when they cover it
+            span = min(span, window + group)
+        n_splits = -(-span // chunk)
     n_splits = int(n_splits)
     if n_splits < 1:
         raise ValueError(f"n_splits={n_splits} must be >= 1")
@@ -369,8 +372,10 @@ class KVInt8Cache:
         self.num_warps, self.num_stages = int(num_warps), int(num_stages)   # Triton knobs, accepted and unused
         self.dtype, self.device = dtype, torch.device(device)
         self._alloc()
-        # grid fixed by the capacity (one captured graph serves every length)
-        self.n_splits = -(-self.max_len // self.chunk)
+        # grid fixed by the capacity (one captured graph serves every length); with a window the splits
+        # are laid over the window only
+        span = min(self.max_len, self.window + self.group) if self.window else self.max_len
+        self.n_splits = -(-span // self.chunk)
         self.workspace = new_workspace(self.batch, self.num_q_heads, self.num_kv_heads, self.n_splits, True,
                                        self.device)
         self.out = torch.zeros((self.batch, self.num_q_heads, 1, self.head_dim), dtype=dtype, device=self.device)

@@ -320,6 +320,78 @@ class OracleDecoder:
         self.pos = T
         return logits, np.argmax(logits.astype(np.float32), axis=-1)
 
+    def capture_kv(self, ids: np.ndarray, span: tuple[int, int]):
+        """K after k_norm and before RoPE, and V, of positions [span[0],
+        span[1]) on every layer, from a causal forward over ``ids`` ``[1, T]``
+        that leaves the cache untouched (capture_qkv / capture_kv,
+        src/nova/memory.py:176-217, which hooks LeanAttention before RoPE,
+        src/nova/layers.py:113-122).  Returns fp16 ``[layers, kv_heads, m, d]``."""
+        ids = np.asarray(ids)
+        B, T = ids.shape
+        s0, s1 = int(span[0]), int(span[1])
+        if B != 1 or not 0 <= s0 < s1 <= T:
+            raise ValueError(f"capture needs batch 1 and 0 <= {s0} < {s1} <= {T}")
+        hq, hkv, d = self.hq, self.hkv, self.d
+        cos, sin = rope_cos_sin(np.arange(T), d, self.theta)
+        h = np.asarray(self.W["embed"])[ids]
+        ks, vs = [], []
+        for li, lw in enumerate(self.W["layers"]):
+            x = rms_norm(h, lw["input_ln"], self.eps)
+            qkv = self._lin(x, ("qkv", li), lw["qkv"])
+            q = rms_norm(qkv[..., :hq * d].reshape(B, T, hq, d), lw["q_norm"], self.eps)
+            k = rms_norm(qkv[..., hq * d:(hq + hkv) * d].reshape(B, T, hkv, d), lw["k_norm"], self.eps)
+            v = qkv[..., (hq + hkv) * d:].reshape(B, T, hkv, d)
+            ks.append(k[0, s0:s1].transpose(1, 0, 2))
+            vs.append(v[0, s0:s1].transpose(1, 0, 2))
+            q = apply_rope(q, cos[None, :, None], sin[None, :, None]).transpose(0, 2, 1, 3)
+            kr = apply_rope(k, cos[None, :, None], sin[None, :, None]).transpose(0, 2, 1, 3)
+            vt = v.transpose(0, 2, 1, 3)
+            o = np.empty((B, T, hq * d), np.float16)
+            for t in range(T):
+                ot, _ = attend(q[:, :, t], kr[:, :, :t + 1], vt[:, :, :t + 1])
+                o[:, t] = ot.reshape(B, hq * d)
+            h = _f16(h.astype(np.float32) + self._lin(o, ("o", li), lw["o"]).astype(np.float32))
+            h = _f16(h.astype(np.float32) + self._mlp(li, lw, h).astype(np.float32))
+        return np.stack(ks), np.stack(vs)
+
+    def inject(self, k: np.ndarray, v: np.ndarray, offset: int = 0) -> int:
+        """MemoryStore.inject (src/nova/memory.py:447-475) onto the streaming
+        int8 cache: K (``[layers, kv_heads, m, d]``, before RoPE) rotated to
+        positions [offset, offset + m) with the fp16 op-by-op RoPE
+        (src/nova/layers.py:30-36), K/V appended to the fp16 K/V already
+        written by earlier injections (offset must equal their length; 0
+        starts afresh), then the cache as a prefill of [0, offset + m) leaves
+        it (src/nova/kvattn.py:745-783): every complete 64-token group
+        quantized on the token axis, the last <= 64 positions in the ring.
+        Returns offset + m.  Batch 1."""
+        L, hkv, m, d = k.shape
+        offset = int(offset)
+        have = 0 if offset == 0 or getattr(self, "_staged", None) is None else self._staged[0][0].shape[2]
+        if offset != have:
+            raise ValueError(f"offset {offset}: {have} positions written")
+        total = offset + m
+        cos, sin = rope_cos_sin(np.arange(offset, total), d, self.theta)
+        staged = []
+        for li in range(L):
+            kr = apply_rope(np.asarray(k[li], np.float16), cos[None], sin[None])[None]
+            vv = np.asarray(v[li], np.float16)[None]
+            if offset:
+                kr = np.concatenate([self._staged[li][0], kr], axis=2)
+                vv = np.concatenate([self._staged[li][1], vv], axis=2)
+            staged.append((kr, vv))
+            full = total // GT * GT
+            for src, codes, mn, st in ((kr, self.kq[li], self.kmn[li], self.kst[li]),
+                                       (vv, self.vq[li], self.vmn[li], self.vst[li])):
+                if full:
+                    c, m_, s_ = okv.quantize_int8_token(np.ascontiguousarray(src[:, :, :full]), GT)
+                    codes[:, :, :full], mn[:, :, :full // GT], st[:, :, :full // GT] = c, m_, s_
+            for p in range(max(0, total - GT), total):
+                self.tail_k[li][:, :, p % GT] = kr[:, :, p]
+                self.tail_v[li][:, :, p % GT] = vv[:, :, p]
+        self._staged = staged
+        self.pos = total
+        return total
+
     def prefill(self, ids: np.ndarray):
         """Causal prefill over fp16 K/V from position 0; fills the int8 cache
         and the ring; returns (last-position logits, first greedy token)."""

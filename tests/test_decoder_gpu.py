@@ -222,6 +222,51 @@ def test_injection_reproduces_prefill(cuda_lib):
             assert torch.equal(a[n][li], b[n][li]), (n, li)
 
 
+def test_injection_matches_oracle(cuda_lib):
+    """Memory capture + injection into the int8 cache against the oracle's
+    restatement (OracleDecoder.capture_kv / inject: MemoryStore.inject of
+    src/nova/memory.py:447-475 composed with the int8 quantizer of a prefill).
+    Captured K/V agree within the prefill tolerance; the same K/V injected by
+    both (at 0, then at 130 on top) leave bit-identical int8 codes, scales,
+    ring and length; decoding on from the injected state matches the oracle's
+    decode steps."""
+    from nova_b200.decoder import NovaDecoder
+
+    cfg, W, _, orc, _ = _setup("small", 1, prompt_len=8, max_len=320)
+    dec = NovaDecoder(W, max_len=320, batch=1)
+    ids = torch.randint(0, cfg.vocab_size, (1, 170), generator=torch.Generator().manual_seed(17))
+    k, v = dec.capture_kv(ids, (20, 150))
+    ko, vo = orc.capture_kv(ids.numpy(), (20, 150))
+    for got, want in ((k, ko), (v, vo)):
+        g32, w32 = got.float().cpu().numpy(), want.astype(np.float32)
+        assert np.abs(g32 - w32).max() <= 2e-2 * np.abs(w32).max(), "captured K/V differ from the oracle's"
+    k2, v2 = dec.capture_kv(ids, (150, 170))
+    for off, (kk, vv) in ((0, (k, v)), (130, (k2, v2))):
+        assert dec.inject(kk, vv, offset=off) == orc.inject(kk.cpu().numpy(), vv.cpu().numpy(), offset=off)
+        st = dec.state()
+        total = off + kk.shape[2]
+        assert st["pos"] == orc.pos == total
+        for n in ("kq", "vq", "kmn", "kst", "vmn", "vst", "tail_k", "tail_v"):
+            for li in range(cfg.num_hidden_layers):
+                a, b = st[n][li], getattr(orc, n)[li]
+                if n in ("kq", "vq"):
+                    a, b = a[:, :, :total // 64 * 64], b[:, :, :total // 64 * 64]
+                elif n in ("kmn", "kst", "vmn", "vst"):
+                    a, b = a[:, :, :total // 64], b[:, :, :total // 64]
+                assert np.array_equal(a, b), (off, n, li)
+    tok = np.array([int(ids[0, -1])])
+    dec.input_ids.fill_(int(tok[0]))
+    dec.resid.copy_(dec.w.embed[dec.input_ids])
+    dec.capture()
+    for i in range(8):
+        dec.step()
+        glog = dec.logits.float().cpu().numpy()
+        olog, otok = orc.step(tok)
+        scale = float(np.abs(olog).max())
+        assert np.abs(glog - olog.astype(np.float32)).max() <= 2e-2 * scale, f"step {i}"
+        tok = dec.input_ids.cpu().numpy().copy()
+
+
 def test_segmented_prefill_and_injection(cuda_lib):
     """prefill(history) + inject(memory) + prefill(turn, reset=False) attends to
     every earlier position through the staged fp16 K/V: the cache bytes match a
