@@ -136,3 +136,64 @@ def test_nf4_col_shards_need_whole_blocks():
     nf4_cols(p, a, 0, 64)
     with pytest.raises(ValueError):
         nf4_cols(p, a, 0, 32)
+
+
+# ---------------------------------------------------------------- failure detection on the host
+
+
+def _fault_rank(rank, world, port, out_dir, mode):
+    """One rank of a 2-rank gloo group: a healthy all-reduce, then rank 1 fails
+    before the next collective (``raise``: an exception ends its process;
+    ``absent``: it stays alive but never joins) while rank 0 enters it."""
+    import datetime
+    import json
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=2))
+    from nova_b200.tp import TPContext, all_reduce_sum
+
+    tp = TPContext(rank, world, dist.group.WORLD, allreduce="nccl")
+    t = torch.ones(16)
+    all_reduce_sum(t, tp)
+    if rank == 1:
+        if mode == "raise":
+            raise RuntimeError("injected fault: rank 1 fails before its next collective")
+        time.sleep(10)
+        os._exit(0)
+    t0 = time.time()
+    try:
+        all_reduce_sum(t, tp)
+        status = "completed"
+    except Exception as e:   # noqa: BLE001 -- the point is that it raises instead of hanging
+        status = type(e).__name__
+    with open(os.path.join(out_dir, "rank0.json"), "w") as f:
+        json.dump({"status": status, "seconds": time.time() - t0, "first": float(t[0])}, f)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["raise", "absent"])
+def test_rank_failure_surfaces_as_an_error(tmp_path, mode):
+    """A rank that dies (or never joins) before a collective of the decode
+    step: the surviving rank's all-reduce ends with an error within the
+    process group's timeout instead of hanging, and the healthy step before it
+    was correct."""
+    import json
+
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_rank, args=(r, 2, port, str(tmp_path), mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank did not exit")
+    res = json.loads((tmp_path / "rank0.json").read_text())
+    assert res["first"] == 2.0                  # the healthy all-reduce summed both ranks
+    assert res["status"] != "completed", res
+    assert res["seconds"] < 20, res             # bounded by the 2 s process-group timeout
+    if mode == "raise":
+        assert procs[1].exitcode != 0
