@@ -323,6 +323,7 @@ def _config5(args, rank: int, world: int, dev, use_tp: bool, cpu: bool) -> dict:
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ar_us = _time_allreduce(dec, reps=3)
     dec.check_errors()
     ms = float(t.item()) / steps
     copies = 1 if use_tp else world
@@ -336,6 +337,10 @@ def _config5(args, rank: int, world: int, dev, use_tp: bool, cpu: bool) -> dict:
                                               "ms_at_peak": step_bytes / (peak * 1e9) * 1e3,
                                               "frac": step_bytes / (peak * 1e9) / (ms * 1e-3)},
            "gpu_launches_per_step": dec.launches_per_step()}
+    if ar_us is not None:
+        calls = 2 * cfg.num_hidden_layers
+        rec["tp_breakdown"] = {"allreduce_us_per_call": round(ar_us, 2), "calls_per_step": calls,
+                               "allreduce_share": round(calls * ar_us * 1e-3 / ms, 3)}
     dec.close()
     del dec
     torch.cuda.empty_cache()
@@ -348,6 +353,21 @@ def _config5(args, rank: int, world: int, dev, use_tp: bool, cpu: bool) -> dict:
                       "sample": "best of 2 x one decoder layer for 64 rows at ctx 32768 (linears for all rows, "
                                 "2 rows' attentions timed and scaled to 64) + 1/36 of the lm_head; x 36 layers"}
     return rec
+
+
+def _time_allreduce(dec, reps: int = 10) -> float | None:
+    """Device microseconds per call of the decode step's fused NVLink
+    all-reduce + residual add (tensor parallelism, peer-memory path), from a
+    graph of one call per layer replayed ``reps`` times on every rank at once
+    (every rank makes the same calls in the same order).  None without it."""
+    if dec.p2p is None:
+        return None
+    import torch
+
+    from nova_b200.bench_kernels import _graph_time
+
+    part, resid = torch.zeros_like(dec.part32), dec.resid.clone()
+    return _graph_time(lambda i: dec.p2p(part, resid), dec.cfg.num_hidden_layers, reps)
 
 
 def run_b200(args, rank: int, world: int, local_rank: int) -> None:
@@ -433,6 +453,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     e2e_v = copies * args.batch * args.steps / (float(te.item()) * 1e-3)
 
     kern = _time_kernels(dec)
+    ar_us = _time_allreduce(dec)
     dec.check_errors()   # a bounded wait that gave up in any launch invalidates the numbers
     if world > 1:
         dist.barrier()
@@ -503,6 +524,17 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         "clocks": clk,
         "setup_s": round(setup_s, 1),
     }
+    if ar_us is not None:
+        calls = 2 * cfg.num_hidden_layers
+        step_ms = ms_max / args.steps
+        line["tp_breakdown"] = {
+            "allreduce_us_per_call": round(ar_us, 2), "calls_per_step": calls,
+            "allreduce_ms_per_step": round(calls * ar_us * 1e-3, 3),
+            "allreduce_share": round(calls * ar_us * 1e-3 / step_ms, 3),
+            "lm_head_ms_per_step": round(kern["lm_head"]["ms"], 3),
+            "lm_head_share": round(kern["lm_head"]["ms"] / step_ms, 3),
+            "basis": "each family replayed alone (graph of one call per layer), device time; shares of the measured "
+                     "step time"}
     line.update(configs)
     if world == 1 and not args.no_cpu_baseline:
         from oracle.baseline import LayerSample, host_threads, median_time

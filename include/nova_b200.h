@@ -369,9 +369,76 @@ NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
  * max_len; attn needs the ring (tail_k/tail_v) and n_splits >= 1.  When the
  * new token completes a 64-token group, the group is requantized into the
  * cache and attended in its int8 form, as after the two separate calls.
- * qk->q_out is not written.
+ * qk->q_out is not written.  With programmatic dependent launch on, the first
+ * groups of the int8 prefix are requested before the kernel launched just
+ * before this call has finished: that kernel must not write the int8 cache
+ * (in the decode step it is the q|k|v projection).
  */
 NOVA_API int nova_qk_append_attn_int8(const nova_qk_args* qk, const nova_attn_int8_args* attn, void* stream);
+
+/*
+ * Prefill attention on the int8 cache: the queries of a chunk of n tokens at
+ * positions [prefix, prefix + n) (q fp16 [batch, q_heads, n, 128], RoPE
+ * applied) attend causally to every earlier position and to themselves.
+ * Positions [0, int8_len) are read from the int8 cache in place (dequantized
+ * as fp16(code * step + min) with the reference's two fp32 roundings),
+ * positions [int8_len, prefix + n) from fp16 k / v ([batch, kv_heads, rows,
+ * 128], row r = position int8_len + r).  int8_len is 0 (all fp16: a staged
+ * prefill) or a multiple of 64 up to prefix (the chunked prefill straight into
+ * the int8 cache).  window > 0 keeps positions p > q - window.  fp32 softmax,
+ * out = fp16(O / l) in [batch, n, q_heads * 128] layout (row = token).
+ * Replaces the SDPA of KVInt8Cache.attend_prefill (src/nova/kvattn.py:791-815)
+ * and of the prefill forward (src/nova/layers.py:140-161), and does the
+ * reference's planned chunked int8 prefill (reports/kv-int8-streaming-cache.md
+ * section 5.1).
+ */
+typedef struct nova_prefill_attn_args {
+    const void* q;            /* fp16, element strides below                    */
+    int64_t q_b_stride, q_h_stride, q_t_stride;
+    const void* k;            /* fp16 keys / values of positions [int8_len, prefix + n) */
+    const void* v;
+    int64_t kv_b_stride, kv_h_stride, kv_t_stride;
+    const void* kq;           /* int8 cache as for nova_attn_decode_int8, or NULL */
+    const void* vq;
+    const void* kmn;
+    const void* kst;
+    const void* vmn;
+    const void* vst;
+    int64_t max_len, groups;
+    void* out;                /* fp16 [batch, n, q_heads * 128]                 */
+    int64_t o_b_stride, o_t_stride;
+    int64_t batch, q_heads, kv_heads, head_dim, n, prefix, int8_len, window;
+} nova_prefill_attn_args;
+
+NOVA_API int nova_attn_prefill_int8(const nova_prefill_attn_args* args, void* stream);
+
+/*
+ * The prefill's per-head step for a chunk of n q|k|v rows at positions
+ * pos0 .. pos0 + n - 1: q heads -> q_norm + RoPE -> q_out [batch, q_heads, n,
+ * 128]; k heads -> k_norm (-> k_pre, optional: the captured, un-rotated K of
+ * the memory store) + RoPE -> k_out [batch, kv_heads, n, 128]; v -> v_out
+ * (same layout).  The arithmetic of nova_qk_norm_rope_append.  Replaces
+ * q_norm / k_norm / apply_rotary_pos_emb of LeanAttention.forward for a
+ * prompt (src/nova/layers.py:108-124).
+ */
+typedef struct nova_qk_prefill_args {
+    const void* qkv;            /* fp16 [batch, n, (q_heads + 2*kv_heads)*128]   */
+    int64_t qkv_b_stride, qkv_t_stride;
+    const void* q_norm_weight;
+    const void* k_norm_weight;
+    double eps;
+    const void* cos;            /* fp16 [rope_len, 128]                          */
+    const void* sin;
+    int64_t rope_len;
+    void* q_out;
+    void* k_out;
+    void* k_pre;                /* or NULL                                       */
+    void* v_out;
+    int64_t q_b_stride, q_h_stride, kv_b_stride, kv_h_stride;   /* token stride 128 */
+    int64_t batch, q_heads, kv_heads, head_dim, n, pos0;
+} nova_qk_prefill_args;
+
+NOVA_API int nova_qk_prefill(const nova_qk_prefill_args* args, void* stream);
 
 /*
  * Batched NF4 GEMM for M = 1..64 rows:

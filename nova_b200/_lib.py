@@ -64,6 +64,31 @@ class QKArgs(ctypes.Structure):
     ]
 
 
+class PrefillAttnArgs(ctypes.Structure):
+    """Mirror of ``nova_prefill_attn_args``."""
+
+    _fields_ = [
+        ("q", _P), ("q_b_stride", _I), ("q_h_stride", _I), ("q_t_stride", _I),
+        ("k", _P), ("v", _P), ("kv_b_stride", _I), ("kv_h_stride", _I), ("kv_t_stride", _I),
+        ("kq", _P), ("vq", _P), ("kmn", _P), ("kst", _P), ("vmn", _P), ("vst", _P), ("max_len", _I), ("groups", _I),
+        ("out", _P), ("o_b_stride", _I), ("o_t_stride", _I),
+        ("batch", _I), ("q_heads", _I), ("kv_heads", _I), ("head_dim", _I), ("n", _I), ("prefix", _I),
+        ("int8_len", _I), ("window", _I),
+    ]
+
+
+class QKPrefillArgs(ctypes.Structure):
+    """Mirror of ``nova_qk_prefill_args``."""
+
+    _fields_ = [
+        ("qkv", _P), ("qkv_b_stride", _I), ("qkv_t_stride", _I), ("q_norm_weight", _P), ("k_norm_weight", _P),
+        ("eps", ctypes.c_double), ("cos", _P), ("sin", _P), ("rope_len", _I),
+        ("q_out", _P), ("k_out", _P), ("k_pre", _P), ("v_out", _P),
+        ("q_b_stride", _I), ("q_h_stride", _I), ("kv_b_stride", _I), ("kv_h_stride", _I),
+        ("batch", _I), ("q_heads", _I), ("kv_heads", _I), ("head_dim", _I), ("n", _I), ("pos0", _I),
+    ]
+
+
 class SampleArgs(ctypes.Structure):
     """Mirror of ``nova_sample_args``."""
 
@@ -118,6 +143,8 @@ _SIGNATURES: dict[str, list] = {
     "nova_qk_norm_rope_append": [ctypes.POINTER(QKArgs), _P],
     "nova_qk_append_attn_int8": [ctypes.POINTER(QKArgs), ctypes.POINTER(AttnArgs), _P],
     "nova_sample_topk": [ctypes.POINTER(SampleArgs), _P],
+    "nova_attn_prefill_int8": [ctypes.POINTER(PrefillAttnArgs), _P],
+    "nova_qk_prefill": [ctypes.POINTER(QKPrefillArgs), _P],
 }
 _STRING_FNS = ("nova_version", "nova_last_error")
 _INT_FNS = ("nova_get_launch_flags",)

@@ -389,39 +389,58 @@ __global__ void __launch_bounds__(THREADS, 3)
     const bool spec_on = !p.win_rel && split < p.n_splits && spec < p.groups &&
                          int64_t(spec) * GT < int64_t(split) * p.chunk + p.chunk;
     __half nwq = __float2half_rn(0.f), nwk = __float2half_rn(0.f);
-    if (FUSED) {   // weights: read before the dependency wait
-        nwq = p.q_norm_w[threadIdx.x];
-        if (is_tail) nwk = p.k_norm_w[threadIdx.x];
-        if (threadIdx.x == 32) {
-            // The position read here may be stale (the wait has not happened);
-            // it only picks the RoPE rows to prefetch.
-            const int64_t pg = *reinterpret_cast<const volatile int64_t*>(p.pos);
-            const int64_t cp = pg < 0 ? 0 : (pg < p.rope_len ? pg : p.rope_len - 1);
-            prefetch_l2(p.cos + cp * D);
-            prefetch_l2(p.cos + cp * D + 64);
-            prefetch_l2(p.sin + cp * D);
-            prefetch_l2(p.sin + cp * D + 64);
-        }
-    }
-    if (threadIdx.x == 64 && p.first) prefetch_l2(p.first);
-    if (p.prefetch_first && spec_on && lane == 0) prefetch_group_l2(p, bh, spec);
-    pdl_trigger();
-    pdl_wait();   // q, the cache and the lengths come from the previous kernels
-
-    // Speculative first load, issued before the lengths are read.
     uint8_t* stage = smem + warp * STAGE;
     uint64_t* bar_k = &bars[0][warp];
     uint64_t* bar_v = &bars[1][warp];
-    if (lane == 0) {
-        mbar_init(bar_k, 1);
-        mbar_init(bar_v, 1);
-        fence_mbar_init();
-        if (spec_on) {
-            issue_k(p, &tmK, stage, bar_k, bh, spec);
-            issue_v(p, &tmV, stage, bar_v, bh, spec);
+    // Speculative first load of this warp's group (in bounds whatever the lengths turn out to be).
+    auto spec_issue = [&]() {
+        if (lane == 0) {
+            mbar_init(bar_k, 1);
+            mbar_init(bar_v, 1);
+            fence_mbar_init();
+            if (spec_on) {
+                issue_k(p, &tmK, stage, bar_k, bh, spec);
+                issue_v(p, &tmV, stage, bar_v, bh, spec);
+            }
         }
+        __syncwarp();
+    };
+    int64_t pos_hint = -1;
+    float cos_hint = 0.f, sin_hint = 0.f;
+    if (FUSED) {
+        // Before the dependency wait: the norm weights and the RoPE row of the
+        // position the previous step left (a hint, checked after the wait), and
+        // the first group of the int8 prefix -- the q|k|v projection launched
+        // just before does not write the cache, and the group this step
+        // completes is never read by a prefix split.
+        nwq = p.q_norm_w[threadIdx.x];
+        if (is_tail) nwk = p.k_norm_w[threadIdx.x];
+        pos_hint = *reinterpret_cast<const volatile int64_t*>(p.pos);
+        const int64_t cp = pos_hint < 0 ? 0 : (pos_hint < p.rope_len ? pos_hint : p.rope_len - 1);
+        cos_hint = __half2float(p.cos[cp * D + threadIdx.x]);
+        sin_hint = __half2float(p.sin[cp * D + threadIdx.x]);
+        spec_issue();
     }
-    __syncwarp();
+    if (threadIdx.x == 64 && p.first) prefetch_l2(p.first);
+    if (!FUSED && p.prefetch_first && spec_on && lane == 0) prefetch_group_l2(p, bh, spec);
+    pdl_trigger();
+    pdl_wait();   // q, the cache and the lengths come from the previous kernels
+
+    // FUSED: this CTA's raw q (and, for the ring CTA, k and v) channel, requested first
+    __half xq[MAX_GQ], xk[1] = {__float2half_rn(0.f)}, xv = __float2half_rn(0.f);
+    if (FUSED) {
+        const __half* row = p.qkv + b * p.qkv_b;
+        const int hq_all = p.kv_heads * p.gq;
+#pragma unroll
+        for (int hh = 0; hh < MAX_GQ; ++hh)
+            xq[hh] = hh < p.gq ? row[int64_t(h * p.gq + hh) * D + threadIdx.x] : __float2half_rn(0.f);
+        if (is_tail) {
+            xk[0] = row[int64_t(hq_all + h) * D + threadIdx.x];
+            xv = row[int64_t(hq_all + p.kv_heads + h) * D + threadIdx.x];
+        }
+    } else {
+        spec_issue();
+    }
     uint32_t phase_k = 0, phase_v = 0;   // completed waits on bar_k / bar_v
     bool pend_k = spec_on, pend_v = spec_on;   // a copy is in flight on bar_k / bar_v
 
@@ -457,19 +476,12 @@ __global__ void __launch_bounds__(THREADS, 3)
         static_assert(TX_BYTES % 16 == 0 && STAGE - TX_BYTES >= MAX_GQ * D * 2 && 128 + D * 2 <= STAGE - TX_BYTES,
                       "prologue scratch must fit in the unused stage tails");
         const int d = threadIdx.x;
-        const __half* row = p.qkv + b * p.qkv_b;
-        const int hq_all = p.kv_heads * p.gq;
-        __half xq[MAX_GQ];
-#pragma unroll
-        for (int hh = 0; hh < MAX_GQ; ++hh)
-            xq[hh] = hh < p.gq ? row[int64_t(h * p.gq + hh) * D + d] : __float2half_rn(0.f);
-        __half xk[1] = {__float2half_rn(0.f)}, xv = __float2half_rn(0.f);
-        if (is_tail) {
-            xk[0] = row[int64_t(hq_all + h) * D + d];
-            xv = row[int64_t(hq_all + p.kv_heads + h) * D + d];
+        float c = cos_hint, sn = sin_hint;
+        if (pos != pos_hint) {   // the position moved since the hint: the RoPE row of the real one
+            const int64_t cp = pos < 0 ? 0 : (pos < p.rope_len ? pos : p.rope_len - 1);
+            c = __half2float(p.cos[cp * D + d]);
+            sn = __half2float(p.sin[cp * D + d]);
         }
-        const int64_t cp = pos < 0 ? 0 : (pos < p.rope_len ? pos : p.rope_len - 1);
-        const float c = __half2float(p.cos[cp * D + d]), sn = __half2float(p.sin[cp * D + d]);
         __half eq[MAX_GQ];
         qk::norm_rope<MAX_GQ>(xq, nwq, c, sn, p.eps, qred, qbuf, eq);
 #pragma unroll

@@ -32,26 +32,25 @@ write fp32 partial sums (``NOVA_NF4_F32``), an NCCL all-reduce inside the
 graph sums them and ``nova_residual_add_f32`` adds them to the replicated
 residual stream: 8 launches per layer of this library plus 2 all-reduces.
 
-Prefill (not the hot path) runs the reference's math eagerly on the GPU:
-NF4 -> fp16 dequant + fp16 matmul, fp16 SDPA with the causal mask, then the
-complete 64-token groups of every layer's K/V are quantized with
-``nova_kv_quant_int8`` and the tail goes to the fp16 ring (same result as
-``KVInt8Cache.finish_prefill``).
+Prefill (not the hot path) runs eagerly on this library's kernels: the
+batched NF4 GEMM on the tensor cores in 64-row launches (with the decode
+step's residual / SiLU*up epilogues), nova_rmsnorm, nova_qk_prefill (q/k norm
++ RoPE) and nova_attn_prefill_int8 (causal attention over the int8 prefix in
+place and the fp16 keys); then the complete 64-token groups of every layer's
+K/V are quantized with ``nova_kv_quant_int8`` and the tail goes to the fp16
+ring (same result as ``KVInt8Cache.finish_prefill``).
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass, field
 
-import numpy as np
 import torch
-import torch.nn.functional as F
 
 from . import _lib
-from .kernels import (build_nf4_lut, fused_rms_norm, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native,
-                      pack_tc)
-from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk
-from .quant import dequantize_nf4, nf4_codebook, quantize_nf4
+from .kernels import build_nf4_lut, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native, pack_tc
+from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk, prefill_attention
+from .quant import nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
 
 
@@ -266,16 +265,16 @@ class NovaDecoder:
         self.input_ids = torch.zeros(B, dtype=torch.int64, device=dev)
         n_max = max(cfg.vocab_size, 2 * self.inter, self.q_dim + 2 * self.kv_dim, cfg.hidden_size)
         self.gemv_ws = gemv_workspace(dev, n_max).clone()   # shared by every GEMV of the step
-        if self.batch > GEMV_ROWS:   # batched GEMM: one workspace for every shape, normalized-x scratch
-            shapes = [(self.q_dim + 2 * self.kv_dim, cfg.hidden_size), (cfg.hidden_size, self.q_dim),
-                      (2 * self.inter, cfg.hidden_size), (cfg.hidden_size, self.inter),
-                      (cfg.vocab_size, cfg.hidden_size)]
-            self.gemm_ws = max((gemm_workspace(dev, n, k) for n, k in shapes), key=lambda t: t.numel()).clone()
+        # batched GEMM (decode above 8 rows, and every prefill): one workspace for every shape
+        shapes = [(self.q_dim + 2 * self.kv_dim, cfg.hidden_size), (cfg.hidden_size, self.q_dim),
+                  (2 * self.inter, cfg.hidden_size), (cfg.hidden_size, self.inter), (cfg.vocab_size, cfg.hidden_size)]
+        self.gemm_ws = max((gemm_workspace(dev, n, k) for n, k in shapes), key=lambda t: t.numel()).clone()
+        if self.batch > GEMV_ROWS:   # decode GEMM units packed before any graph capture; normalized-x scratch
             for w in [self.w.lm_head] + [x for lw in self.w.layers for x in (lw.qkv, lw.o, lw.gate_up, lw.down)]:
-                w.tc_units()   # packed before any graph capture
+                w.tc_units()
             self.xn = torch.zeros(B, cfg.hidden_size, dtype=f16, device=dev)
         else:
-            self.gemm_ws = self.xn = None
+            self.xn = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.pdl = bool(pdl)
         # attn_fused=True: the q/k norm + RoPE + ring append runs in the attention's prologue (one launch
@@ -294,37 +293,94 @@ class NovaDecoder:
 
     # ---------------------------------------------------------------- prefill
 
-    def _linear16(self, x: torch.Tensor, w: NF4Weight) -> torch.Tensor:
-        w16 = dequantize_nf4(w.packed, w.absmax, self.lut)
-        return torch.matmul(x, w16.t())
+    PREFILL_ROWS = 64   # rows per batched-GEMM launch in the prefill
 
-    def _row_parallel(self, x: torch.Tensor, w: NF4Weight) -> torch.Tensor:
-        """o_proj / down_proj: one matmul, or with tensor parallelism the fp32
-        partial sums of every rank all-reduced and rounded to fp16 once."""
+    def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """RMSNorm of the rows of x ``[R, n]`` (nova_rmsnorm)."""
+        y = torch.empty_like(x)
+        _lib.call("nova_rmsnorm", x.data_ptr(), x.stride(0), None, 0, None, 0, w.data_ptr(), y.data_ptr(),
+                  y.stride(0), x.shape[0], x.shape[1], float(self.cfg.rms_norm_eps), _lib.stream_of(self.device))
+        return y
+
+    def _gemm_rows(self, x: torch.Tensor, w: NF4Weight, out: torch.Tensor, epilogue: int = _lib.NF4_PLAIN,
+                   residual: torch.Tensor | None = None) -> torch.Tensor:
+        """x ``[R, K]`` @ W^T into out, PREFILL_ROWS rows per nova_nf4_gemm launch
+        (the tcgen05 tensor cores, fp32 accumulation, the decode step's epilogues)."""
+        units = w.tc_units()
+        for r0 in range(0, x.shape[0], self.PREFILL_ROWS):
+            sl = slice(r0, min(x.shape[0], r0 + self.PREFILL_ROWS))
+            nf4_gemm(x[sl], units, self.lut, out[sl], n=w.n, epilogue=epilogue,
+                     residual=None if residual is None else residual[sl], workspace=self.gemm_ws)
+        return out
+
+    def _row_parallel_add(self, x: torch.Tensor, w: NF4Weight, h: torch.Tensor) -> None:
+        """h += x @ W^T for o_proj / down_proj (h ``[R, H]`` fp16, in place): the
+        residual epilogue, or with tensor parallelism the fp32 partial sums of
+        every rank all-reduced, then one fp16 rounding and the residual add."""
         if not self.tp.active:
-            return self._linear16(x, w)
-        w16 = dequantize_nf4(w.packed, w.absmax, self.lut)
-        part = torch.matmul(x.float(), w16.float().t())
+            self._gemm_rows(x, w, h, epilogue=_lib.NF4_RESIDUAL, residual=h)
+            return
+        part = torch.empty(x.shape[0], w.n, dtype=torch.float32, device=self.device)
+        self._gemm_rows(x, w, part, epilogue=_lib.NF4_F32)
         all_reduce_sum(part, self.tp)
-        return part.to(torch.float16)
+        _lib.call("nova_residual_add_f32", part.data_ptr(), part.stride(0), h.data_ptr(), h.stride(0), h.shape[0],
+                  h.shape[1], _lib.stream_of(self.device))
 
-    def _layer_qkv(self, li: int, lw, h: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
-        """Prefill projections of layer li for hidden states h ``[B, T, H]``:
-        q (RoPE applied, ``[B, Hq, T, D]``), k before RoPE (after k_norm) and
-        after RoPE, v (``[B, Hkv, T, D]``)."""
+    def _layer_qkv(self, li: int, lw, h: torch.Tensor, pos0: int, want_pre: bool = False):
+        """Prefill projections of layer li for hidden states h ``[B, T, H]`` at
+        positions pos0 .. pos0 + T - 1: q (RoPE applied, ``[B, Hq, T, D]``), k
+        after k_norm before RoPE (``want_pre``, else None), k after RoPE and v
+        (``[B, Hkv, T, D]``).  Input norm, the q|k|v GEMM and nova_qk_prefill."""
         cfg = self.cfg
-        B, T = h.shape[:2]
-        d, qd, kvd = cfg.head_dim, self.q_dim, self.kv_dim
-        x = fused_rms_norm(h, lw.input_ln, cfg.rms_norm_eps)
-        qkv = self._linear16(x, lw.qkv)
-        q = qkv[..., :qd].reshape(B, T, self.hq, d)
-        k = qkv[..., qd:qd + kvd].reshape(B, T, self.hkv, d)
-        v = qkv[..., qd + kvd:].reshape(B, T, self.hkv, d).transpose(1, 2).contiguous()
-        q = fused_rms_norm(q, lw.q_norm, cfg.rms_norm_eps).transpose(1, 2)
-        k_pre = fused_rms_norm(k, lw.k_norm, cfg.rms_norm_eps).transpose(1, 2)
-        q = q * cos + _rotate_half(q) * sin
-        k = (k_pre * cos + _rotate_half(k_pre) * sin).contiguous()
+        B, T, H = h.shape
+        d = cfg.head_dim
+        x = self._norm(h.view(B * T, H), lw.input_ln)
+        qkv = self._gemm_rows(x, lw.qkv, torch.empty(B * T, lw.qkv.n, dtype=torch.float16, device=self.device))
+        f16 = dict(dtype=torch.float16, device=self.device)
+        q = torch.empty(B, self.hq, T, d, **f16)
+        k = torch.empty(B, self.hkv, T, d, **f16)
+        v = torch.empty(B, self.hkv, T, d, **f16)
+        k_pre = torch.empty(B, self.hkv, T, d, **f16) if want_pre else None
+        a = _lib.QKPrefillArgs()
+        a.qkv, a.qkv_b_stride, a.qkv_t_stride = qkv.data_ptr(), T * lw.qkv.n, lw.qkv.n
+        a.q_norm_weight, a.k_norm_weight, a.eps = lw.q_norm.data_ptr(), lw.k_norm.data_ptr(), cfg.rms_norm_eps
+        a.cos, a.sin, a.rope_len = self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0]
+        a.q_out, a.k_out, a.k_pre, a.v_out = q.data_ptr(), k.data_ptr(), _lib.ptr(k_pre), v.data_ptr()
+        a.q_b_stride, a.q_h_stride = q.stride(0), q.stride(1)
+        a.kv_b_stride, a.kv_h_stride = k.stride(0), k.stride(1)
+        a.batch, a.q_heads, a.kv_heads, a.head_dim, a.n, a.pos0 = B, self.hq, self.hkv, d, T, int(pos0)
+        _lib.check(_lib.lib().nova_qk_prefill(_lib.ctypes.byref(a), _lib.stream_of(self.device)), "nova_qk_prefill")
         return q, k_pre, k, v
+
+    def _attend_prefill(self, li: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, prefix: int,
+                        int8_len: int = 0) -> torch.Tensor:
+        """Causal attention of the chunk queries q ``[B, Hq, n, D]`` at positions
+        [prefix, prefix + n) over positions [0, int8_len) of layer li's int8
+        cache and the fp16 k / v ``[B, Hkv, *, D]`` of [int8_len, prefix + n)
+        (nova_attn_prefill_int8) -> ``[B, n, Hq * D]``."""
+        c = self.cache
+        int8 = (c.kq[li], c.kmn[li], c.kst[li], c.vq[li], c.vmn[li], c.vst[li]) if int8_len else None
+        return prefill_attention(q, k, v, prefix=prefix, int8=int8, int8_len=int8_len)
+
+    def _layer_rest(self, lw, h: torch.Tensor, o: torch.Tensor) -> None:
+        """o_proj + residual, post-attention norm, gate|up with SiLU*up, down_proj
+        + residual, in place on h ``[B, T, H]`` (o ``[B, T, Hq * D]``)."""
+        B, T, H = h.shape
+        h2 = h.view(B * T, H)
+        self._row_parallel_add(o.view(B * T, -1), lw.o, h2)
+        x = self._norm(h2, lw.post_ln)
+        act = self._gemm_rows(x, lw.gate_up, torch.empty(B * T, self.inter, dtype=torch.float16, device=self.device),
+                              epilogue=_lib.NF4_SILU_MUL)
+        self._row_parallel_add(act, lw.down, h2)
+
+    def _first_token(self, h_last: torch.Tensor) -> torch.Tensor:
+        """Final norm + 4-bit lm_head + greedy argmax of the prompt's last
+        position (the decode step's ARGMAX epilogue), the token's embedding as
+        the next step's input."""
+        self.argmax_slot.zero_()
+        self._gemv(h_last, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
+                   argmax=self.argmax_slot, token_out=self.input_ids, embed=self.w.embed, embed_out=self.resid)
+        return self.input_ids.clone()
 
     def _commit_kv(self, li: int, k: torch.Tensor, v: torch.Tensor, total: int) -> None:
         """Quantize the complete 64-token groups of the fp16 K/V ``[B, Hkv, total, D]``
@@ -370,7 +426,6 @@ class NovaDecoder:
         cfg, cache = self.cfg, self.cache
         B, T = input_ids.shape
         ids = input_ids.to(self.device)
-        gq = self.hq // self.hkv
         d = cfg.head_dim
         stream = _lib.stream_of(self.device)
         take0 = T - min(T, GROUP_T)   # first position that goes into the ring
@@ -378,31 +433,11 @@ class NovaDecoder:
         for c0 in range(0, T, chunk):
             c1 = min(T, c0 + chunk)
             n = c1 - c0
-            h = self.w.embed[ids[:, c0:c1]]
-            cos, sin = self.cos[c0:c1][None, None], self.sin[c0:c1][None, None]
+            h = torch.index_select(self.w.embed, 0, ids[:, c0:c1].reshape(-1)).view(B, n, -1)
             for li, lw in enumerate(self.w.layers):
-                q, _, k, v = self._layer_qkv(li, lw, h, cos, sin)
-                if c0:
-                    pk, pv = self._dequant_prefix(li, c0)
-                    kk, vv = torch.cat([pk, k], dim=2), torch.cat([pv, v], dim=2)
-                    rows = torch.arange(c0, c1, device=self.device)
-                    keep = torch.arange(c1, device=self.device).view(1, -1) <= rows.view(-1, 1)
-                    mask = torch.zeros(n, c1, dtype=torch.float16, device=self.device).masked_fill(~keep,
-                                                                                                   float("-inf"))
-                    o = F.scaled_dot_product_attention(q, kk.repeat_interleave(gq, dim=1),
-                                                       vv.repeat_interleave(gq, dim=1), attn_mask=mask,
-                                                       scale=d ** -0.5)
-                    del pk, pv, kk, vv
-                else:
-                    o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1),
-                                                       v.repeat_interleave(gq, dim=1), is_causal=True,
-                                                       scale=d ** -0.5)
-                o = o.transpose(1, 2).reshape(B, n, self.q_dim)
-                h = h + self._row_parallel(o, lw.o)
-                x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
-                gu = self._linear16(x, lw.gate_up).view(B, n, -1, 2, 8)
-                h = h + self._row_parallel(F.silu(gu[:, :, :, 0].reshape(B, n, -1)) * gu[:, :, :, 1].reshape(B, n, -1),
-                                           lw.down)
+                q, _, k, v = self._layer_qkv(li, lw, h, c0)
+                o = self._attend_prefill(li, q, k, v, prefix=c0, int8_len=c0)
+                self._layer_rest(lw, h, o)
                 full = (n // GROUP_T) * GROUP_T   # complete groups of this chunk (chunk starts are group-aligned)
                 if full:
                     g0 = c0 // GROUP_T
@@ -413,12 +448,7 @@ class NovaDecoder:
                                   mn.shape[2] * d, B * self.hkv, full, d, GROUP_T, stream)
                 if c1 > take0:   # positions of the prompt's last <= 64 tokens into the ring
                     cache.write_ring(li, k, v, c1)
-        x = fused_rms_norm(h[:, -1], self.w.final_norm, cfg.rms_norm_eps)
-        logits = self._linear16(x, self.w.lm_head)
-        first = torch.argmax(logits, dim=-1)
-        self.logits.copy_(logits)
-        self.input_ids.copy_(first)
-        self.resid.copy_(self.w.embed[first])
+        first = self._first_token(h[:, -1])
         self._set_scalars(T)
         return first
 
@@ -467,40 +497,20 @@ class NovaDecoder:
         if offset != have:
             raise ValueError(f"offset {offset} must equal the {have} positions written since the last reset")
         total = offset + T
-        h = self.w.embed[input_ids.to(self.device)]                   # [B, T, H]
-        cos, sin = self.cos[offset:total][None, None], self.sin[offset:total][None, None]
-        gq = self.hq // self.hkv
+        ids = input_ids.to(self.device)
+        h = torch.index_select(self.w.embed, 0, ids.reshape(-1)).view(B, T, -1)   # [B, T, H]
         staged = []
         for li, lw in enumerate(self.w.layers):
-            q, _, k, v = self._layer_qkv(li, lw, h, cos, sin)
-            if offset:
+            q, _, k, v = self._layer_qkv(li, lw, h, offset)
+            if offset:   # the staged fp16 K/V of the positions written before
                 k = torch.cat([self._staged[li][0], k], dim=2)
                 v = torch.cat([self._staged[li][1], v], dim=2)
-                rows = torch.arange(offset, total, device=self.device)
-                keep = torch.arange(total, device=self.device).view(1, -1) <= rows.view(-1, 1)
-                mask = torch.zeros(T, total, dtype=torch.float16, device=self.device).masked_fill(~keep,
-                                                                                                  float("-inf"))
-                o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
-                                                   attn_mask=mask, scale=cfg.head_dim ** -0.5)
-            else:
-                o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
-                                                   is_causal=True, scale=cfg.head_dim ** -0.5)
-            o = o.transpose(1, 2).reshape(B, T, self.q_dim)
-            h = h + self._row_parallel(o, lw.o)
-            x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
-            gu = self._linear16(x, lw.gate_up).view(B, T, -1, 2, 8)
-            gate = gu[:, :, :, 0].reshape(B, T, -1)
-            up = gu[:, :, :, 1].reshape(B, T, -1)
-            h = h + self._row_parallel(F.silu(gate) * up, lw.down)
+            o = self._attend_prefill(li, q, k, v, prefix=offset)
+            self._layer_rest(lw, h, o)
             self._commit_kv(li, k, v, total)
             staged.append((k, v))
         self._staged = staged
-        x = fused_rms_norm(h[:, -1], self.w.final_norm, cfg.rms_norm_eps)
-        logits = self._linear16(x, self.w.lm_head)
-        first = torch.argmax(logits, dim=-1)
-        self.logits.copy_(logits)
-        self.input_ids.copy_(first)
-        self.resid.copy_(self.w.embed[first])
+        first = self._first_token(h[:, -1])
         self._set_scalars(total)
         return first
 
@@ -510,27 +520,17 @@ class NovaDecoder:
         on every layer, from a forward over ``input_ids`` ``[1, T]`` that does
         not touch the cache (capture_kv, src/nova/memory.py:176-217):
         ``[layers, kv_heads, m, head_dim]`` fp16 each."""
-        cfg = self.cfg
         B, T = input_ids.shape
         s0, s1 = int(span[0]), int(span[1])
         if B != 1 or not 0 <= s0 < s1 <= T:
             raise ValueError(f"capture needs batch 1 and 0 <= {s0} < {s1} <= {T}")
-        h = self.w.embed[input_ids.to(self.device)]
-        cos, sin = self.cos[:T][None, None], self.sin[:T][None, None]
-        gq = self.hq // self.hkv
+        h = torch.index_select(self.w.embed, 0, input_ids.to(self.device).reshape(-1)).view(B, T, -1)
         ks, vs = [], []
         for li, lw in enumerate(self.w.layers):
-            q, k_pre, k, v = self._layer_qkv(li, lw, h, cos, sin)
+            q, k_pre, k, v = self._layer_qkv(li, lw, h, 0, want_pre=True)
             ks.append(k_pre[0, :, s0:s1].clone())
             vs.append(v[0, :, s0:s1].clone())
-            o = F.scaled_dot_product_attention(q, k.repeat_interleave(gq, dim=1), v.repeat_interleave(gq, dim=1),
-                                               is_causal=True, scale=cfg.head_dim ** -0.5)
-            o = o.transpose(1, 2).reshape(B, T, self.q_dim)
-            h = h + self._row_parallel(o, lw.o)
-            x = fused_rms_norm(h, lw.post_ln, cfg.rms_norm_eps)
-            gu = self._linear16(x, lw.gate_up).view(B, T, -1, 2, 8)
-            h = h + self._row_parallel(F.silu(gu[:, :, :, 0].reshape(B, T, -1)) * gu[:, :, :, 1].reshape(B, T, -1),
-                                       lw.down)
+            self._layer_rest(lw, h, self._attend_prefill(li, q, k, v, prefix=0))
         return torch.stack(ks), torch.stack(vs)
 
     @torch.inference_mode()

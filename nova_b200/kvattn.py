@@ -25,7 +25,6 @@ from __future__ import annotations
 from typing import Any
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from .kvquant import quantize_int8
@@ -266,6 +265,53 @@ def int8_attn_decode(
     return out
 
 
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, prefix: int,
+                      int8: tuple | None = None, int8_len: int = 0, window: int = 0,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of a prefill chunk (``nova_attn_prefill_int8``).
+
+    q fp16 ``[B, Hq, n, D]``: the chunk's queries at positions [prefix,
+    prefix + n), RoPE applied.  k / v fp16 ``[B, Hkv, rows, D]``: positions
+    [int8_len, prefix + n).  ``int8`` = (kq, kmn, kst, vq, vmn, vst) of one
+    layer's cache holding positions [0, int8_len) (int8_len a multiple of 64).
+    Returns fp16 ``[B, n, Hq * D]`` (row = token: the o_proj input)."""
+    b, hq, n, d = q.shape
+    hkv = k.shape[1]
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_any(t, name, torch.float16)
+    if d != HEAD_DIM or k.shape[3] != d or v.shape != k.shape or k.shape[0] != b or hq % hkv:
+        raise ValueError(f"shapes q {tuple(q.shape)} k {tuple(k.shape)} v {tuple(v.shape)} do not match")
+    if k.shape[2] < prefix + n - int8_len:
+        raise ValueError(f"k holds {k.shape[2]} rows, positions [{int8_len}, {prefix + n}) are needed")
+    if q.stride(3) != 1 or k.stride(3) != 1 or v.stride()[:3] != k.stride()[:3] or v.stride(3) != 1:
+        raise ValueError("q / k / v need a contiguous last dimension (and k, v the same strides)")
+    if out is None:
+        out = torch.empty(b, n, hq * d, dtype=torch.float16, device=q.device)
+    a = _lib.PrefillAttnArgs()
+    a.q, a.q_b_stride, a.q_h_stride, a.q_t_stride = q.data_ptr(), q.stride(0), q.stride(1), q.stride(2)
+    a.k, a.v = k.data_ptr(), v.data_ptr()
+    a.kv_b_stride, a.kv_h_stride, a.kv_t_stride = k.stride(0), k.stride(1), k.stride(2)
+    a.max_len, a.groups = 0, 0
+    if int8 is not None and int8_len:
+        kq, kmn, kst, vq, vmn, vst = int8
+        a.kq, a.vq = kq.data_ptr(), vq.data_ptr()
+        a.kmn, a.kst, a.vmn, a.vst = kmn.data_ptr(), kst.data_ptr(), vmn.data_ptr(), vst.data_ptr()
+        a.max_len, a.groups = kq.shape[2], kmn.shape[2]
+    a.out, a.o_b_stride, a.o_t_stride = out.data_ptr(), out.stride(0), out.stride(1)
+    a.batch, a.q_heads, a.kv_heads, a.head_dim = b, hq, hkv, d
+    a.n, a.prefix, a.int8_len, a.window = n, int(prefix), int(int8_len), int(window)
+    _lib.check(_lib.lib().nova_attn_prefill_int8(_lib.ctypes.byref(a), _lib.stream_of(q.device)),
+               "nova_attn_prefill_int8")
+    return out
+
+
+def _check_any(x: torch.Tensor, name: str, dtype: torch.dtype) -> None:
+    if not x.is_cuda:
+        raise ValueError(f"{name} must be on CUDA")
+    if x.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {x.dtype}")
+
+
 def pack_int8_kv(k: torch.Tensor, v: torch.Tensor, group: int = GROUP_T):
     """fp16 K/V ``[B, H, L, D]`` -> the fused kernel's layout, with the same
     quantizer the cache uses (src/nova/kvattn.py:430-441)."""
@@ -503,20 +549,17 @@ class KVInt8Cache:
     def attend_prefill(self, query: torch.Tensor, layer_idx: int) -> torch.Tensor:
         """Causal attention of a prefill chunk (queries at positions off ..
         off+n-1, ``[B, H_q, n, D]``) over the fp16 staging area up to the
-        chunk's end, one KV head per query group (src/nova/kvattn.py:791-815);
-        with ``window`` a query at q sees only positions p > q - window.
-        Prefill is not on the decode path."""
+        chunk's end (src/nova/kvattn.py:791-815), in one
+        ``nova_attn_prefill_int8`` launch; with ``window`` a query at q sees
+        only positions p > q - window.  Returns ``[B, H_q, n, D]`` (a view of
+        the kernel's token-major output)."""
         self._ensure_staging()
-        n = query.shape[2]
+        b, hq, n, d = query.shape
         off = int(self.staging.pos.item())
-        end = off + n
-        keys = self.staging.key_cache[layer_idx][:, :, :end]
-        vals = self.staging.value_cache[layer_idx][:, :, :end]
-        allow = torch.ones((n, end), dtype=torch.bool, device=query.device).tril(diagonal=off)
-        if self.window:
-            allow = allow.triu(diagonal=off - self.window + 1)
-        return F.scaled_dot_product_attention(query.contiguous(), keys, vals, attn_mask=allow,
-                                              scale=self.head_dim ** -0.5, enable_gqa=True)
+        keys = self.staging.key_cache[layer_idx]
+        vals = self.staging.value_cache[layer_idx]
+        out = prefill_attention(query.contiguous(), keys, vals, prefix=off, window=self.window)
+        return out.view(b, n, hq, d).transpose(1, 2)
 
     def ring_mask(self) -> torch.Tensor:
         """Which ring slots the next attention reads, ``[1, 1, 1, 64]`` bool

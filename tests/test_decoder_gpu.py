@@ -88,7 +88,10 @@ def test_prefill_matches_oracle(cuda_lib):
             d = np.abs(a - b)
             # fp16 tensor-core prefill vs the fp32 oracle: K/V differ by fp16 rounding noise, which
             # moves a code across a rounding boundary now and then
-            assert d.max() <= 3 and (d > 0).mean() < 0.25, f"layer {li} {name}: codes differ ({(d > 0).mean():.3f})"
+            print(f"prefill layer {li} {name}: codes differ at {(d > 0).mean():.4f} of positions, max {d.max()}")
+            # both sides accumulate in fp32 (tensor-core GEMM / numpy): a K/V value that lands next to a code
+            # boundary moves by one step (measured: 1.5-2 % of the codes of layer 0, 7-8 % of layer 1)
+            assert d.max() <= 1 and (d > 0).mean() < 0.12, f"layer {li} {name}: codes differ ({(d > 0).mean():.3f})"
     glog = dec.logits.float().cpu().numpy()
     scale = float(np.abs(olog).max())
     assert np.abs(glog - olog.astype(np.float32)).max() <= 3e-2 * scale
@@ -336,7 +339,10 @@ def test_chunked_prefill_matches_oracle(cuda_lib):
             a = st[name][li][:, :, :128].astype(np.int32)
             b = getattr(orc, name)[li][:, :, :128].astype(np.int32)
             diff = np.abs(a - b)
-            assert diff.max() <= 3 and (diff > 0).mean() < 0.25, f"layer {li} {name}: {(diff > 0).mean():.3f}"
+            print(f"chunked layer {li} {name}: codes differ at {(diff > 0).mean():.4f} of positions, max {diff.max()}")
+            # measured: layer 0 1.3-1.9 % by one step, layer 1 14 % by at most two (its chunks attend to an int8
+            # prefix whose codes already moved)
+            assert diff.max() <= 2 and (diff > 0).mean() < 0.2, f"layer {li} {name}: {(diff > 0).mean():.3f}"
     glog = dec.logits.float().cpu().numpy()
     scale = float(np.abs(olog).max())
     assert np.abs(glog - olog.astype(np.float32)).max() <= 3e-2 * scale
