@@ -268,10 +268,11 @@ NOVA_API int nova_nf4_pack_native(const void* packed, const void* absmax, int ab
                                   int64_t k, void* stream);
 
 /*
- * The tcgen05 GEMM's unit layout (nf4 args layout = 2): the same 32-row x
- * 64-k, 1088-byte units, except that MMA lane (g, t) holds for each of its
- * rows the code bytes 2t + 8p and 2t + 8p + 1 (p = 0..3) instead of bytes
- * 8t .. 8t + 7.  Same arguments as nova_nf4_pack_native.
+ * The tcgen05 GEMM's unit layout (nf4 args layout = 2): 32-row x 64-k,
+ * 1088-byte units in the native layout's order, row-major inside: bytes
+ * [16 r, 16 r + 16) = codes of k 0..31 of row r, [512 + 16 r, ...) = k 32..63,
+ * then the 32 fp16 absmax in row order.  Same arguments as
+ * nova_nf4_pack_native.
  */
 NOVA_API int nova_nf4_pack_tc(const void* packed, const void* absmax, int absmax_fp32, void* out, int64_t n,
                               int64_t k, void* stream);
@@ -442,15 +443,16 @@ NOVA_API int nova_qk_prefill(const nova_qk_prefill_args* args, void* stream);
 
 /*
  * Batched NF4 GEMM for M = 1..64 rows:
- * y = x @ dequant(W)^T with dequant = fp16(code * absmax) (the reference's
- * dequantized weight, src/nova/quant.py:39-69 + the dequant-matmul of
- * tests/test_nf4_linear.py), fp32 accumulation, the epilogues of
- * nova_nf4_gemv (PLAIN without bias, RESIDUAL, SILU_MUL, ARGMAX with the
- * step finalize, F32).  No norm prologue (normalize x with nova_rmsnorm).
- * Weights in the tcgen05 unit layout (layout = 2, from nova_nf4_pack_tc):
- * decoded into tensor memory, x tiles by TMA, fp32 accumulators in tensor
- * memory, (tile, k-block) work split evenly over one wave of CTAs with
- * deterministic partial sums.  Other layouts: NOVA_ERR_UNSUPPORTED.
+ * y = x @ dequant(W)^T computed as the reference kernel does
+ * (src/nova/kernels.py:213-232): per 64-element block the fp32 sum of
+ * code * x (fp16 codebook values, products exact), times the block's absmax,
+ * accumulated in fp32; the epilogues of nova_nf4_gemv (PLAIN without bias,
+ * RESIDUAL, SILU_MUL, ARGMAX with the step finalize, F32).  No norm prologue
+ * (normalize x with nova_rmsnorm).  Weights in the tcgen05 unit layout
+ * (layout = 2, from nova_nf4_pack_tc): codes decoded into shared-memory A
+ * tiles, x tiles by TMA, block sums in tensor memory, (tile, k-block) work
+ * split evenly over one wave of CTAs with deterministic partial sums.  Other
+ * layouts: NOVA_ERR_UNSUPPORTED.
  * x needs a 16-byte aligned base and a row stride that is a multiple of 8.
  * Workspace: nova_nf4_gemm_workspace_bytes(), zeroed once.
  * Replaces NF4Linear.forward / fused_nf4_linear for batched rows

@@ -870,58 +870,62 @@ __global__ void __launch_bounds__(REF_THREADS, 1) nf4_gemv_ref_kernel(const __gr
 //
 // Tile = 128 weight rows (four 32-row groups) x all batch rows; the MMA is
 // M = 128 (weight rows) x N = M rounded up to 16 (batch rows) x K = 16, fp16
-// operands, fp32 accumulators in tensor memory.  The work items are the
-// (tile, k-block) pairs, tile-major; CTA c of the one-wave grid takes the
-// contiguous range [W*c/G, W*(c+1)/G) (stream-K), so every SM decodes the
-// same number of weight units whatever N and K are.  Per item:
-//   producer warp   bulk-copies the tile's 4 units of the k-block (4352 B)
-//                   into the weight ring and TMA-loads the x tile [N x 64]
-//                   (128-byte swizzle; rows past M read as zero);
-//   decode warps    warp d decodes row group d % 4 of the items with
-//                   parity d / 4: LUT -> fp16 code, times the row's absmax in
-//                   fp16 (fp16(code * absmax), the reference's dequantized
-//                   weight), stored as the A tile in the UMMA K-major
-//                   128-byte-swizzle layout;
-//   MMA thread      4 x tcgen05.mma (K = 16 slices of the 64-wide k-block)
-//                   into one of two TMEM accumulators, tcgen05.commit frees
-//                   the A and x stages;
-//   epilogue warps  at the end of a tile segment read their TMEM lane quarter
-//                   (thread = weight row, registers = batch rows) and either
-//                   run the epilogue (whole tile) or store the partial; the
-//                   last contributor of a split tile (arrival counter) adds
-//                   all partials in CTA order -- deterministic -- and runs it.
+// operands from shared memory, fp32 accumulators in tensor memory.  The work
+// items are the (tile, 2 k-blocks) pairs, tile-major; CTA c of the one-wave
+// grid takes the contiguous range [W*c/G, W*(c+1)/G) (stream-K), so every SM
+// decodes the same number of weight units whatever N and K are.  Per item:
+//   producer warp   bulk-copies the tile's units of the item's k-blocks into
+//                   the weight ring;
+//   x producer      TMA-loads the x tiles [N x 64] (128-byte swizzle; rows
+//                   past M read as zero);
+//   decode warps    warp d (group d / 4, row group d % 4; group g takes the
+//                   items j with j % 3 == g) turns its unit's codes into the
+//                   fp16 codebook values through a lane-replicated LUT and
+//                   stores them as the A tile in the canonical K-major
+//                   128-byte-swizzle layout (lane = weight row, one 16-byte
+//                   chunk of 8 k per store, bank-conflict free);
+//   MMA thread      per k-block, 4 x tcgen05.mma (K = 16 slices) into a fresh
+//                   accumulator, one of four TMEM buffers; tcgen05.commit
+//                   signals the buffer full and, after the item, frees its A
+//                   and x stages;
+//   epilogue warps  8 warps (lane quarter w % 4, batch-column half): per
+//                   k-block read the buffer (tcgen05.ld), free it, and add
+//                   absmax(row, k-block) x block sum into fp32 registers --
+//                   the reference kernel's per-64-block scaling
+//                   (src/nova/kernels.py:213-232), so the products are exact
+//                   and nothing is rounded to fp16 before the output.  At the
+//                   end of a tile segment they run the epilogue (whole tile)
+//                   or store the partial; the last contributor of a split tile
+//                   (arrival counter) adds all partials in CTA order --
+//                   deterministic -- and runs it.
 // Every wait is bounded; on a failed wait the roles stop, the MMA thread
-// waits for its MMAs and the producer for its copies before TMEM is freed.
-
-__device__ __forceinline__ uint32_t dup_lo(uint32_t v) { return __byte_perm(v, 0, 0x1010); }
-__device__ __forceinline__ uint32_t dup_hi(uint32_t v) { return __byte_perm(v, 0, 0x3232); }
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
+// waits for its MMAs and the producers for their copies before TMEM is freed.
 
 constexpr int TC_ROWS = 128;
 constexpr int TC_GROUPS = 3;                       // decode warp groups (item j -> group j % 3)
 constexpr int TC_DEC_WARPS = 4 * TC_GROUPS;
 constexpr int TC_PROD_WARP = TC_DEC_WARPS;         // weight units
 constexpr int TC_MMA_WARP = TC_DEC_WARPS + 1;
-constexpr int TC_EPI_WARP0 = TC_DEC_WARPS + 2;     // 4 epilogue warps: lane quarters (w % 4) all covered
-constexpr int TC_XPROD_WARP = TC_EPI_WARP0 + 4;    // x tiles
+constexpr int TC_EPI_WARP0 = TC_DEC_WARPS + 2;     // 8 epilogue warps: lane quarter w % 4, column half
+constexpr int TC_EPI_WARPS = 8;
+constexpr int TC_XPROD_WARP = TC_EPI_WARP0 + TC_EPI_WARPS;   // x tiles
 constexpr int TC_WARPS = TC_XPROD_WARP + 1;
 constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_AS = 2 * TC_GROUPS, TC_XS = TC_AS;   // one stage-free barrier for both rings
+constexpr int TC_AS = TC_GROUPS, TC_XS = TC_AS;    // A and x stages: one per decode group, freed together
 constexpr int TC_WS_MAX = 24;                      // weight ring depth: as many stages as shared memory holds
-constexpr int TC_KG = 2;                           // k-blocks per work item (one MMA-thread handoff)
+constexpr int TC_KG = 2;                           // k-blocks per work item
 constexpr int TC_W_BYTES = 4 * TC_KG * UNIT_BYTES;
-constexpr int TC_ACC_COLS = 64;                    // TMEM columns: accumulators [0, 128), A stages from 128
-constexpr int TC_A_COL0 = 2 * TC_ACC_COLS;
-constexpr int TC_A_COLS = 32 * TC_KG;              // 128 rows x 64 k fp16 = 32 columns of fp16x2 per k-block
-constexpr int TC_TMEM_COLS = 512;
+constexpr int TC_A_BYTES = TC_ROWS * 128;          // one k-block of the A tile: 128 rows x 64 fp16
+constexpr int TC_NB = 4;                           // TMEM accumulator buffers (k-blocks in flight)
+constexpr int TC_D_COLS = 64;
+constexpr int TC_TMEM_COLS = TC_NB * TC_D_COLS;
+constexpr int TC_LUT_BYTES = 256 * 32 * 4;         // entry v, lane l at word 32 v + l
+constexpr int TC_HALF = 32;                        // batch columns per epilogue warp
 constexpr int TC_SLOT_FLOATS = 64 * TC_ROWS;       // partial tile [batch row / 4][weight row][4]
 constexpr int TC_MAX_M = 64;
 constexpr int TC_MAX_TILES = 4096;                 // N up to 524288 rows
 constexpr int TC_MIN_ITEMS = 4;                    // work items per CTA at least (bounds the split fan-in)
+constexpr int TC_CNT_PER_TILE = 8;                 // split arrivals per tile: lane quarter x column half
 
 struct TcArgs {
     int n_mma;            // MMA N: M rounded up to 16
@@ -929,25 +933,49 @@ struct TcArgs {
     int G;                // CTAs
     int64_t W;            // work items = tiles * ceil(KB / TC_KG)
     float* part;          // [G][2][TC_SLOT_FLOATS]
-    unsigned* tile_cnt;   // [tiles][4] arrivals of split tiles per lane quarter
+    unsigned* tile_cnt;   // [tiles][8] arrivals of split tiles per lane quarter and column half
     int* err;
 };
 
-// Epilogue of one weight row n for batch rows 0..M-1 (v[m]); every lane of
-// the warp calls it (SiLU*up and argmax exchange values between lanes).
+// The LUT replicated per lane with 128-byte entries (32 KB).
+template <int THREADS>
+__device__ __forceinline__ void build_lut32(uint32_t* lut_s, const uint32_t* lut) {
+    for (int v = threadIdx.x; v < 256 * 4; v += THREADS) {
+        const uint32_t w = __ldg(lut + (v >> 2));
+        uint4* dst = reinterpret_cast<uint4*>(lut_s + (v >> 2) * 32 + 8 * (v & 3));
+        dst[0] = make_uint4(w, w, w, w);
+        dst[1] = make_uint4(w, w, w, w);
+    }
+}
+
+// LUT lookups of the 4 code bytes of `w` (k 2i, 2i+1 from byte i) as one
+// 16-byte chunk of fp16 codebook values; lane_b8 = lane << 3.
+__device__ __forceinline__ uint4 decode_word(uint32_t lut_base, uint32_t w, uint32_t lane_b8) {
+    // byte i -> (byte << 8) | (lane << 3), halved: (byte << 7) | (lane << 2)
+    const uint32_t a0 = __byte_perm(w, lane_b8, 0x5504u) >> 1;
+    const uint32_t a1 = __byte_perm(w, lane_b8, 0x5514u) >> 1;
+    const uint32_t a2 = __byte_perm(w, lane_b8, 0x5524u) >> 1;
+    const uint32_t a3 = __byte_perm(w, lane_b8, 0x5534u) >> 1;
+    return make_uint4(lds32(lut_base + a0), lds32(lut_base + a1), lds32(lut_base + a2), lds32(lut_base + a3));
+}
+
+// Epilogue of one weight row n for the batch rows m0 .. m0 + 31 (v[i] is
+// row m0 + i); every lane of the warp calls it (SiLU*up and argmax exchange
+// values between lanes).
 template <int EPI>
-__device__ __forceinline__ void tc_epilogue_row(const Params& p, int n, int rho, const float (&v)[TC_MAX_M],
+__device__ __forceinline__ void tc_epilogue_row(const Params& p, int n, int rho, const float (&v)[TC_HALF], int m0,
                                                 int lane) {
     const bool valid = n < p.N;
     if constexpr (EPI == EPI_SILU_MUL) {   // rows 16i..16i+7 gate, 16i+8..16i+15 the matching up rows
         const bool gate_row = (rho & 15) < 8;
         const int n_out = (n >> 4) * 8 + (n & 7);
 #pragma unroll
-        for (int m = 0; m < TC_MAX_M; ++m) {
+        for (int i = 0; i < TC_HALF; ++i) {
+            const int m = m0 + i;
             if (m >= p.M) break;
-            const float upv = __shfl_down_sync(0xffffffffu, v[m], 8);
+            const float upv = __shfl_down_sync(0xffffffffu, v[i], 8);
             if (valid && gate_row) {
-                const float gate = __half2float(__float2half_rn(v[m]));
+                const float gate = __half2float(__float2half_rn(v[i]));
                 const float up = __half2float(__float2half_rn(upv));
                 const float s = __half2float(__float2half_rn(__fdiv_rn(gate, 1.0f + expf(-gate))));
                 p.out[m * p.out_stride + n_out] = __float2half_rn(s * up);
@@ -957,16 +985,18 @@ __device__ __forceinline__ void tc_epilogue_row(const Params& p, int n, int rho,
     } else if constexpr (EPI == EPI_F32) {
         float* o = reinterpret_cast<float*>(p.out);
 #pragma unroll
-        for (int m = 0; m < TC_MAX_M; ++m) {
+        for (int i = 0; i < TC_HALF; ++i) {
+            const int m = m0 + i;
             if (m >= p.M) break;
-            if (valid) o[m * p.out_stride + n] = v[m];
+            if (valid) o[m * p.out_stride + n] = v[i];
         }
         return;
     } else {
 #pragma unroll
-        for (int m = 0; m < TC_MAX_M; ++m) {
+        for (int i = 0; i < TC_HALF; ++i) {
+            const int m = m0 + i;
             if (m >= p.M) break;
-            __half h = __float2half_rn(v[m]);
+            __half h = __float2half_rn(v[i]);
             if (EPI == EPI_RESIDUAL && valid)
                 h = __float2half_rn(__half2float(__ldcg(p.residual + m * p.res_stride + n)) + __half2float(h));
             if (valid) p.out[m * p.out_stride + n] = h;
@@ -988,14 +1018,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     nf4_gemm_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap xmap, const TcArgs ta) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_w[TC_WS_MAX], empty_w[TC_WS_MAX], full_x[TC_XS];
-    __shared__ __align__(8) uint64_t full_a[TC_AS], empty_a[TC_AS], acc_full[2], acc_empty[2], drain;
+    __shared__ __align__(8) uint64_t full_a[TC_AS], empty_a[TC_AS], acc_full[TC_NB], acc_empty[TC_NB], drain;
     __shared__ uint32_t tmem_s;
-    // 1024-byte aligned carve-up: x ring | LUT | weight ring
+    // 1024-byte aligned carve-up: x ring | A ring | LUT | weight ring
     const uint32_t raw_s = smem_u32(smem_raw);
     uint8_t* x_ring = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
     const int xs_bytes = ta.n_mma * 128;
-    uint32_t* lut_s = reinterpret_cast<uint32_t*>(x_ring + TC_XS * TC_KG * xs_bytes);
-    uint8_t* w_ring = reinterpret_cast<uint8_t*>(lut_s) + LUT_BYTES;
+    uint8_t* a_ring = x_ring + TC_XS * TC_KG * xs_bytes;
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(a_ring + TC_AS * TC_KG * TC_A_BYTES);
+    uint8_t* w_ring = reinterpret_cast<uint8_t*>(lut_s) + TC_LUT_BYTES;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x;
@@ -1022,16 +1053,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < WS; ++s) {
             mbar_init(&full_w[s], 1);
-            mbar_init(&empty_w[s], 4);
+            mbar_init(&empty_w[s], 4 + TC_EPI_WARPS);   // the item's decode warps and the epilogue warps
         }
         for (int s = 0; s < TC_XS; ++s) mbar_init(&full_x[s], 1);
         for (int s = 0; s < TC_AS; ++s) {
             mbar_init(&full_a[s], 4);
             mbar_init(&empty_a[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < TC_NB; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
+            mbar_init(&acc_empty[b], TC_EPI_WARPS);
         }
         mbar_init(&drain, 1);
         fence_mbar_init();
@@ -1047,7 +1078,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int issued_w = 0;
     if (warp == TC_PROD_WARP && lane == 0)   // weights: independent of every earlier kernel
         for (; issued_w < WS && issued_w < n_items; ++issued_w) issue_w(issued_w);
-    build_lut<TC_THREADS>(lut_s, p.lut);
+    build_lut32<TC_THREADS>(lut_s, p.lut);
     pdl_trigger();
     pdl_wait();
     __syncthreads();
@@ -1088,45 +1119,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     mbar_wait(&full_x[j % TC_XS], uint32_t((j / TC_XS) & 1), ta.err, 21);
         }
     } else if (warp < TC_DEC_WARPS) {
-        const int grp = warp >> 2, r = warp & 3, g = lane >> 2, t = lane & 3;
+        const int grp = warp >> 2, r = warp & 3;
         const uint32_t lut_base = smem_u32(lut_s);
-        const uint32_t laneword = uint32_t(lane) << 2;
+        const uint32_t lane_b8 = uint32_t(lane) << 3;
+        const int row = 32 * r + lane;   // A tile row of this lane
         int T = int((u0 + grp) / NKG), kg = int((u0 + grp) % NKG);
         for (int j = grp; j < n_items; j += TC_GROUPS) {
             const int nk = min(TC_KG, KB - kg * TC_KG);
             if (!mbar_wait(&full_w[j % WS], uint32_t((j / WS) & 1), ta.err, 22)) break;
             if (j >= TC_AS && !mbar_wait(&empty_a[j % TC_AS], uint32_t(((j / TC_AS) + 1) & 1), ta.err, 23)) break;
-            for (int q = 0; q < nk && 4 * T + r < n_rg; ++q) {
-                const uint8_t* unit = w_ring + (j % WS) * TC_W_BYTES + (r * TC_KG + q) * UNIT_BYTES;
-                const uint4 c0 = lds128(unit + 16 * lane), c1 = lds128(unit + 512 + 16 * lane);
-                uint2 am;
-                asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(am.x), "=r"(am.y)
-                             : "r"(smem_u32(unit + UNIT_CODE_BYTES + 8 * g)));
-                // rows g, g+8, g+16, g+24 of the group: code words and fp16x2 absmax; all 32 LUT
-                // loads are issued before the first store
-                const uint32_t rw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                const uint32_t sc[4] = {dup_lo(am.x), dup_hi(am.x), dup_lo(am.y), dup_hi(am.y)};
-                uint32_t d[32];   // row h: d[8h .. 8h+7] = k 16t .. 16t+15, fp16x2 in k order
+            if (4 * T + r < n_rg) {
+                for (int q = 0; q < nk; ++q) {
+                    const uint8_t* unit = w_ring + (j % WS) * TC_W_BYTES + (r * TC_KG + q) * UNIT_BYTES;
+                    const uint4 c0 = lds128(unit + 16 * lane), c1 = lds128(unit + 512 + 16 * lane);
+                    const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    uint8_t* arow = a_ring + ((j % TC_AS) * TC_KG + q) * TC_A_BYTES + row * 128;
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    d[i] = lds32(lut_base + __byte_perm(rw[i >> 2], laneword, 0x5504u | (uint32_t(i & 3) << 4)));
-#pragma unroll
-                for (int i = 0; i < 32; ++i) d[i] = hmul2_u32(d[i], sc[i >> 3]);
-                // rows g, g+8 -> TMEM lanes 32r + {g, g+8}; rows g+16, g+24 -> lanes 32r + 16 + {g, g+8}
-                const uint32_t ta0 =
-                    tmem + (uint32_t(32 * r) << 16) + uint32_t(TC_A_COL0 + TC_A_COLS * (j % TC_AS) + 32 * q);
-                tmem_st_16x256b_x4(ta0, d[0], d[1], d[8], d[9], d[2], d[3], d[10], d[11], d[4], d[5], d[12], d[13],
-                                   d[6], d[7], d[14], d[15]);
-                tmem_st_16x256b_x4(ta0 + (16u << 16), d[16], d[17], d[24], d[25], d[18], d[19], d[26], d[27], d[20],
-                                   d[21], d[28], d[29], d[22], d[23], d[30], d[31]);
-                tmem_wait_st();
+                    for (int ch = 0; ch < 8; ++ch) {   // chunk ch = k 8ch .. 8ch+7
+                        const uint4 v = decode_word(lut_base, cw[ch], lane_b8);
+                        *reinterpret_cast<uint4*>(arow + ((ch ^ (row & 7)) << 4)) = v;
+                    }
+                }
             }
             kg += TC_GROUPS;
             while (kg >= NKG) {
                 kg -= NKG;
                 ++T;
             }
-            tc_fence_before();
+            fence_proxy_async();   // the A tile is read by the tensor cores (async proxy)
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&empty_w[j % WS]);
@@ -1135,112 +1155,143 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else if (warp == TC_MMA_WARP) {   // the whole warp waits, one lane issues (warp kept converged)
         const uint32_t idesc = tc_idesc_f16(TC_ROWS, ta.n_mma);
-        const uint64_t bdesc0 = sw128_kmajor_desc(smem_u32(x_ring));   // start address field steps by 16-byte units
-        int seg = 0;
+        const uint64_t adesc0 = sw128_kmajor_desc(smem_u32(a_ring));   // start address field steps by 16-byte units
+        const uint64_t bdesc0 = sw128_kmajor_desc(smem_u32(x_ring));
+        int kbc = 0;   // k-blocks issued: accumulator buffer kbc % TC_NB
         int kg = int(u0 % NKG);
-        for (int j = 0; j < n_items; ++j, kg = kg + 1 == NKG ? 0 : kg + 1) {
+        bool ok = true;
+        for (int j = 0; j < n_items && ok; ++j, kg = kg + 1 == NKG ? 0 : kg + 1) {
             const int nk = min(TC_KG, KB - kg * TC_KG);
-            const bool seg_first = j == 0 || kg == 0;
-            const bool seg_last = j == n_items - 1 || kg == NKG - 1;
-            const int buf = seg & 1;
-            if (seg_first && seg >= 2 && !mbar_wait(&acc_empty[buf], uint32_t(((seg >> 1) + 1) & 1), ta.err, 24))
-                break;
             if (!mbar_wait(&full_a[j % TC_AS], uint32_t((j / TC_AS) & 1), ta.err, 25)) break;
             if (!mbar_wait(&full_x[j % TC_XS], uint32_t((j / TC_XS) & 1), ta.err, 26)) break;
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t a0 = tmem + uint32_t(TC_A_COL0 + TC_A_COLS * (j % TC_AS));
-                const uint32_t d0 = tmem + uint32_t(buf * TC_ACC_COLS);
-                const uint64_t b0 = bdesc0 + uint64_t(((j % TC_XS) * TC_KG * xs_bytes) >> 4);
-                for (int q = 0; q < nk; ++q)
+            for (int q = 0; q < nk; ++q, ++kbc) {
+                const int buf = kbc % TC_NB;
+                if (kbc >= TC_NB && !mbar_wait(&acc_empty[buf], uint32_t(((kbc / TC_NB) + 1) & 1), ta.err, 24)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint64_t a0 = adesc0 + uint64_t((((j % TC_AS) * TC_KG + q) * TC_A_BYTES) >> 4);
+                    const uint64_t b0 = bdesc0 + uint64_t((((j % TC_XS) * TC_KG + q) * xs_bytes) >> 4);
+                    const uint32_t d0 = tmem + uint32_t(buf * TC_D_COLS);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        tc_mma_f16_ta(d0, a0 + 32 * q + 8 * k, b0 + uint64_t((q * xs_bytes + 32 * k) >> 4), idesc,
-                                      (seg_first && q == 0 && k == 0) ? 0u : 1u);
-                tc_commit(&empty_a[j % TC_AS]);   // frees the item's A stage and x stage
-                if (seg_last) tc_commit(&acc_full[buf]);
+                    for (int k = 0; k < 4; ++k)   // a fresh accumulator per k-block
+                        tc_mma_f16(d0, a0 + uint64_t((32 * k) >> 4), b0 + uint64_t((32 * k) >> 4), idesc,
+                                   k ? 1u : 0u);
+                    tc_commit(&acc_full[buf]);
+                }
+                __syncwarp();
             }
+            if (lane == 0) tc_commit(&empty_a[j % TC_AS]);   // frees the item's A and x stages
             __syncwarp();
-            if (seg_last) ++seg;
         }
         if (lane == 0) tc_commit(&drain);   // every MMA of this CTA has completed before TMEM is freed
         __syncwarp();
         mbar_wait(&drain, 0u, ta.err, 27);
     } else {   // epilogue warps
-        const int q = warp & 3;
-        const int rho = 32 * q + lane;
-        int seg = 0;
-        float v[TC_MAX_M];
-        for (int j = 0; j < n_items;) {
+        const int q4 = warp & 3;                          // TMEM lane quarter
+        const int half = (warp - TC_EPI_WARP0) >> 2;      // batch columns [32 half, 32 half + 32)
+        const int m0 = TC_HALF * half;
+        const bool cols = m0 < ta.n_mma;
+        const int rho = 32 * q4 + lane;                   // weight row within the tile
+        float v[TC_HALF];
+        int kbc = 0;
+        bool ok = true;
+        for (int j = 0; j < n_items && ok;) {
             const int64_t u = u0 + j;
             const int T = int(u / NKG), kg0 = int(u % NKG);
             const int len = min(n_items - j, NKG - kg0);
             const bool whole = kg0 == 0 && len == NKG;
-            const int buf = seg & 1;
-            if (!mbar_wait(&acc_full[buf], uint32_t((seg >> 1) & 1), ta.err, 28)) break;
-            tc_fence_after();
+            const bool row_ok = 4 * T + q4 < n_rg;
 #pragma unroll
-            for (int c16 = 0; c16 < TC_MAX_M / 16; ++c16) {
-                if (16 * c16 < ta.n_mma) {
-                    uint32_t rr[16];
-                    tmem_ld16(tmem + (uint32_t(32 * q) << 16) + uint32_t(buf * TC_ACC_COLS + 16 * c16), rr);
-                    tmem_wait_ld();
+            for (int i = 0; i < TC_HALF; ++i) v[i] = 0.f;
+            for (int jj = j; jj < j + len && ok; ++jj) {
+                const int kb0 = (kg0 + (jj - j)) * TC_KG, nk = min(TC_KG, KB - kb0);
+                const uint8_t* amax = w_ring + (jj % WS) * TC_W_BYTES + q4 * TC_KG * UNIT_BYTES + UNIT_CODE_BYTES +
+                                      2 * lane;
+                for (int q = 0; q < nk; ++q, ++kbc) {
+                    const int buf = kbc % TC_NB;
+                    if (!mbar_wait(&acc_full[buf], uint32_t((kbc / TC_NB) & 1), ta.err, 28)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (cols) {   // 16 columns at a time: v += absmax * block sum
+                        const float am =
+                            row_ok ? __half2float(*reinterpret_cast<const __half*>(amax + q * UNIT_BYTES)) : 0.f;
+                        const uint32_t ta0 = tmem + (uint32_t(32 * q4) << 16) + uint32_t(buf * TC_D_COLS + m0);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) v[16 * c16 + i] = __uint_as_float(rr[i]);
+                        for (int h16 = 0; h16 < TC_HALF / 16; ++h16) {
+                            if (m0 + 16 * h16 < ta.n_mma) {
+                                uint32_t d[16];
+                                tmem_ld16(ta0 + uint32_t(16 * h16), d);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int i = 0; i < 16; ++i)
+                                    v[16 * h16 + i] = fmaf(am, __uint_as_float(d[i]), v[16 * h16 + i]);
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_w[jj % WS]);   // absmax of the item read
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            if (!ok) break;
             const int n = T * TC_ROWS + rho;
-            bool run = true;
-            if (!whole) {   // split tile: partial to this CTA's slot; per lane quarter, the last
-                            // contributing warp adds the partials in CTA order
+            bool run = cols;
+            if (cols && !whole) {   // split tile: partial to this CTA's slot; per lane quarter and column
+                                    // half, the last contributing warp adds the partials in CTA order
                 float4* slot = reinterpret_cast<float4*>(ta.part + (int64_t(c) * 2 + (T == first_tile ? 0 : 1)) *
                                                                          TC_SLOT_FLOATS);   // [m / 4][row][4]
 #pragma unroll
-                for (int q4 = 0; q4 < TC_MAX_M / 4; ++q4)
-                    if (4 * q4 < p.M)
-                        __stcg(slot + q4 * TC_ROWS + rho, make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
+                for (int f = 0; f < TC_HALF / 4; ++f)
+                    if (m0 + 4 * f < p.M)
+                        __stcg(slot + (m0 / 4 + f) * TC_ROWS + rho, make_float4(v[4 * f], v[4 * f + 1], v[4 * f + 2],
+                                                                                v[4 * f + 3]));
                 __threadfence();
                 __syncwarp();
                 const int cf = owner_of(int64_t(T) * NKG, ta.W, ta.G);
                 const int cl = owner_of(int64_t(T) * NKG + NKG - 1, ta.W, ta.G);
+                unsigned* cnt = ta.tile_cnt + TC_CNT_PER_TILE * T + 4 * half + q4;
                 unsigned last = 0;
-                if (lane == 0) last = atomicAdd(ta.tile_cnt + 4 * T + q, 1u) == unsigned(cl - cf);
+                if (lane == 0) last = atomicAdd(cnt, 1u) == unsigned(cl - cf);
                 run = __shfl_sync(0xffffffffu, last, 0) != 0;
                 if (run) {
                     __threadfence();
 #pragma unroll
-                    for (int m = 0; m < TC_MAX_M; ++m) v[m] = 0.f;
+                    for (int i = 0; i < TC_HALF; ++i) v[i] = 0.f;
                     for (int cc = cf; cc <= cl; ++cc) {
                         const int ft = int((ta.W * cc / ta.G) / NKG);
                         const float4* src = reinterpret_cast<const float4*>(
                             ta.part + (int64_t(cc) * 2 + (T == ft ? 0 : 1)) * TC_SLOT_FLOATS);
-                        float4 t4[TC_MAX_M / 4];
+                        float4 t4[TC_HALF / 4];
 #pragma unroll
-                        for (int q4 = 0; q4 < TC_MAX_M / 4; ++q4)
-                            t4[q4] = 4 * q4 < p.M ? __ldcg(src + q4 * TC_ROWS + rho) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int f = 0; f < TC_HALF / 4; ++f)
+                            t4[f] = m0 + 4 * f < p.M ? __ldcg(src + (m0 / 4 + f) * TC_ROWS + rho)
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                        for (int q4 = 0; q4 < TC_MAX_M / 4; ++q4) {
-                            v[4 * q4] += t4[q4].x;
-                            v[4 * q4 + 1] += t4[q4].y;
-                            v[4 * q4 + 2] += t4[q4].z;
-                            v[4 * q4 + 3] += t4[q4].w;
+                        for (int f = 0; f < TC_HALF / 4; ++f) {
+                            v[4 * f] += t4[f].x;
+                            v[4 * f + 1] += t4[f].y;
+                            v[4 * f + 2] += t4[f].z;
+                            v[4 * f + 3] += t4[f].w;
                         }
                     }
-                    if (lane == 0) ta.tile_cnt[4 * T + q] = 0u;   // re-armed for the next launch
+                    if (lane == 0) *cnt = 0u;   // re-armed for the next launch
                 }
             }
-            if (run) tc_epilogue_row<EPI>(p, n, rho, v, lane);
-            ++seg;
+            if (run) tc_epilogue_row<EPI>(p, n, rho, v, m0, lane);
             j += len;
         }
         if (EPI == EPI_ARGMAX && p.token_out) {   // the last epilogue warp to finish runs the step finalize
             __threadfence();
             __syncwarp();
             unsigned last = 0;
-            if (lane == 0) last = atomicAdd(p.done, 1u) == unsigned(4 * ta.G - 1);
+            if (lane == 0) last = atomicAdd(p.done, 1u) == unsigned(TC_EPI_WARPS * ta.G - 1);
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 __threadfence();
                 finalize_step(p, lane);
@@ -1328,22 +1379,28 @@ __global__ void nf4_pack_native_kernel(const uint8_t* __restrict__ packed, const
         const int64_t rg = u / KB;
         const int b = int(u % KB);
         uint8_t* rec = out + u * UNIT_BYTES;
+        if constexpr (TC) {   // GEMM units: row `lane` owns bytes 16 lane (k 0..31) and 512 + 16 lane (k 32..63)
+            const int64_t row = rg * UNIT_ROWS + lane;
+            const uint2* src = reinterpret_cast<const uint2*>(packed + row * row_bytes + 32 * b);
+            uint2* d0 = reinterpret_cast<uint2*>(rec + 16 * lane);
+            uint2* d1 = reinterpret_cast<uint2*>(rec + 512 + 16 * lane);
+            d0[0] = src[0];
+            d0[1] = src[1];
+            d1[0] = src[2];
+            d1[1] = src[3];
+            const float a = absmax_at<AbsT>(absmax, int64_t(b) * N + row);
+            reinterpret_cast<__half*>(rec + UNIT_CODE_BYTES)[lane] = __float2half_rn(a);
+        } else {
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int64_t row = rg * UNIT_ROWS + g + 8 * r;
-            uint2 v;
-            if (TC) {
-                const uint16_t* src = reinterpret_cast<const uint16_t*>(packed + row * row_bytes + 32 * b + 2 * t);
-                v.x = uint32_t(src[0]) | (uint32_t(src[4]) << 16);
-                v.y = uint32_t(src[8]) | (uint32_t(src[12]) << 16);
-            } else {
-                v = *reinterpret_cast<const uint2*>(packed + row * row_bytes + 32 * b + 8 * t);
-            }
-            // rows g, g+8 -> first half, rows g+16, g+24 -> second half; 16 bytes per lane in each
-            *reinterpret_cast<uint2*>(rec + (r >> 1) * 512 + 16 * lane + 8 * (r & 1)) = v;
-            if (t == 0) {
-                const float a = absmax_at<AbsT>(absmax, int64_t(b) * N + row);
-                reinterpret_cast<__half*>(out + u * UNIT_BYTES + UNIT_CODE_BYTES)[4 * g + r] = __float2half_rn(a);
+            for (int r = 0; r < 4; ++r) {
+                const int64_t row = rg * UNIT_ROWS + g + 8 * r;
+                const uint2 v = *reinterpret_cast<const uint2*>(packed + row * row_bytes + 32 * b + 8 * t);
+                // rows g, g+8 -> first half, rows g+16, g+24 -> second half; 16 bytes per lane in each
+                *reinterpret_cast<uint2*>(rec + (r >> 1) * 512 + 16 * lane + 8 * (r & 1)) = v;
+                if (t == 0) {
+                    const float a = absmax_at<AbsT>(absmax, int64_t(b) * N + row);
+                    reinterpret_cast<__half*>(rec + UNIT_CODE_BYTES)[4 * g + r] = __float2half_rn(a);
+                }
             }
         }
     }
@@ -1668,15 +1725,15 @@ static int64_t tc_grid(int64_t items) {
 }
 
 // tcgen05 GEMM workspace: [0] finalize arrivals, [4] error word, [256, 256 +
-// 16 * TC_MAX_TILES) split arrivals per tile and lane quarter, then 2 partial
-// slots per CTA.  The offsets are the same for every shape, so launches of
+// 32 * TC_MAX_TILES) split arrivals per tile, lane quarter and column half,
+// then 2 partial slots per CTA.  The offsets are the same for every shape, so launches of
 // different shapes can share one workspace: each leaves its counters at zero,
 // and no shape's partials reach another's counters.
 static int64_t tc_workspace_layout(int64_t n, int64_t k, int64_t* part_off) {
     const int64_t tiles = (n + TC_ROWS - 1) / TC_ROWS;
     const int64_t w = tiles * ((k / 64 + TC_KG - 1) / TC_KG);
     const int64_t g = tc_grid(w);
-    const int64_t off = (256 + int64_t(TC_MAX_TILES) * 16 + 1023) / 1024 * 1024;
+    const int64_t off = (256 + int64_t(TC_MAX_TILES) * TC_CNT_PER_TILE * 4 + 1023) / 1024 * 1024;
     if (part_off) *part_off = off;
     return off + g * 2 * int64_t(TC_SLOT_FLOATS) * 4;
 }
@@ -1737,7 +1794,8 @@ static int nf4_gemm_tc(const nova_nf4_args* a, int epi, cudaStream_t stream) {
         cudaGetLastError();
         return fail(NOVA_ERR_CUDA, "device queries failed");
     }
-    const int64_t fixed = 1024 + int64_t(TC_XS) * TC_KG * ta.n_mma * 128 + LUT_BYTES;
+    const int64_t fixed =
+        1024 + int64_t(TC_XS) * TC_KG * ta.n_mma * 128 + int64_t(TC_AS) * TC_KG * TC_A_BYTES + TC_LUT_BYTES;
     ta.ws = int(std::min<int64_t>(TC_WS_MAX, (optin - 1024 - fixed) / TC_W_BYTES));   // 1 KB for static smem
     if (ta.ws < 2) return fail(NOVA_ERR_UNSUPPORTED, "shared memory");
     const int64_t nsmem = fixed + int64_t(ta.ws) * TC_W_BYTES;

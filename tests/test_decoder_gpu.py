@@ -89,9 +89,11 @@ def test_prefill_matches_oracle(cuda_lib):
             # fp16 tensor-core prefill vs the fp32 oracle: K/V differ by fp16 rounding noise, which
             # moves a code across a rounding boundary now and then
             print(f"prefill layer {li} {name}: codes differ at {(d > 0).mean():.4f} of positions, max {d.max()}")
-            # both sides accumulate in fp32 (tensor-core GEMM / numpy): a K/V value that lands next to a code
-            # boundary moves by one step (measured: 1.5-2 % of the codes of layer 0, 7-8 % of layer 1)
-            assert d.max() <= 1 and (d > 0).mean() < 0.12, f"layer {li} {name}: codes differ ({(d > 0).mean():.3f})"
+            # the prompt linears use the reference kernel's arithmetic (exact products, fp32 block sums times
+            # absmax), so layer 0's K/V match but for fp32 summation order: measured 0-0.02 % of its codes
+            # move by one step; layer 1 sees layer 0's attention/MLP rounding noise (measured 4-5 %)
+            lim = 0.005 if li == 0 else 0.08
+            assert d.max() <= 1 and (d > 0).mean() < lim, f"layer {li} {name}: codes differ ({(d > 0).mean():.4f})"
     glog = dec.logits.float().cpu().numpy()
     scale = float(np.abs(olog).max())
     assert np.abs(glog - olog.astype(np.float32)).max() <= 3e-2 * scale
@@ -340,9 +342,10 @@ def test_chunked_prefill_matches_oracle(cuda_lib):
             b = getattr(orc, name)[li][:, :, :128].astype(np.int32)
             diff = np.abs(a - b)
             print(f"chunked layer {li} {name}: codes differ at {(diff > 0).mean():.4f} of positions, max {diff.max()}")
-            # measured: layer 0 1.3-1.9 % by one step, layer 1 14 % by at most two (its chunks attend to an int8
-            # prefix whose codes already moved)
-            assert diff.max() <= 2 and (diff > 0).mean() < 0.2, f"layer {li} {name}: {(diff > 0).mean():.3f}"
+            # measured: layer 0 0-0.01 % by one step, layer 1 4-4.6 % by one step (its later chunks attend to an
+            # int8 prefix whose codes already moved)
+            lim = 0.005 if li == 0 else 0.08
+            assert diff.max() <= 1 and (diff > 0).mean() < lim, f"layer {li} {name}: {(diff > 0).mean():.4f}"
     glog = dec.logits.float().cpu().numpy()
     scale = float(np.abs(olog).max())
     assert np.abs(glog - olog.astype(np.float32)).max() <= 3e-2 * scale
