@@ -870,7 +870,7 @@ __global__ void __launch_bounds__(REF_THREADS, 1) nf4_gemv_ref_kernel(const __gr
 //
 // Tile = 128 weight rows (four 32-row groups) x all batch rows; the MMA is
 // M = 128 (weight rows) x N = M rounded up to 16 (batch rows) x K = 16, fp16
-// operands from shared memory, fp32 accumulators in tensor memory.  The work
+// operands, fp32 accumulators in tensor memory.  The work
 // items are the (tile, 2 k-blocks) pairs, tile-major; CTA c of the one-wave
 // grid takes the contiguous range [W*c/G, W*(c+1)/G) (stream-K), so every SM
 // decodes the same number of weight units whatever N and K are.  Per item:
@@ -881,13 +881,13 @@ __global__ void __launch_bounds__(REF_THREADS, 1) nf4_gemv_ref_kernel(const __gr
 //   decode warps    warp d (group d / 4, row group d % 4; group g takes the
 //                   items j with j % 3 == g) turns its unit's codes into the
 //                   fp16 codebook values through a lane-replicated LUT and
-//                   stores them as the A tile in the canonical K-major
-//                   128-byte-swizzle layout (lane = weight row, one 16-byte
-//                   chunk of 8 k per store, bank-conflict free);
-//   MMA thread      per k-block, 4 x tcgen05.mma (K = 16 slices) into a fresh
-//                   accumulator, one of four TMEM buffers; tcgen05.commit
-//                   signals the buffer full and, after the item, frees its A
-//                   and x stages;
+//                   stores them as the A tile in tensor memory (lane = weight
+//                   row, column = two consecutive k: tcgen05.st.32x32b);
+//   MMA thread      per k-block, 4 x tcgen05.mma (K = 16 slices, A from
+//                   tensor memory, x by shared-memory descriptor) into a
+//                   fresh accumulator, one of four TMEM buffers;
+//                   tcgen05.commit signals the buffer full and, after the
+//                   item, frees its A and x stages;
 //   epilogue warps  8 warps (lane quarter w % 4, batch-column half): per
 //                   k-block read the buffer (tcgen05.ld), free it, and add
 //                   absmax(row, k-block) x block sum into fp32 registers --
@@ -911,14 +911,18 @@ constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_XPROD_WARP = TC_EPI_WARP0 + TC_EPI_WARPS;   // x tiles
 constexpr int TC_WARPS = TC_XPROD_WARP + 1;
 constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_AS = TC_GROUPS, TC_XS = TC_AS;    // A and x stages: one per decode group, freed together
+constexpr int TC_AS = 4;                           // A stages (items) in tensor memory
+constexpr int TC_XS = 6;                           // x stages (items): the TMA -> MMA -> release chain
 constexpr int TC_WS_MAX = 24;                      // weight ring depth: as many stages as shared memory holds
 constexpr int TC_KG = 2;                           // k-blocks per work item
+static_assert(TC_KG == 1 || TC_KG == 2, "the epilogue's absmax pipeline holds up to 2 k-blocks per item");
 constexpr int TC_W_BYTES = 4 * TC_KG * UNIT_BYTES;
-constexpr int TC_A_BYTES = TC_ROWS * 128;          // one k-block of the A tile: 128 rows x 64 fp16
 constexpr int TC_NB = 4;                           // TMEM accumulator buffers (k-blocks in flight)
 constexpr int TC_D_COLS = 64;
-constexpr int TC_TMEM_COLS = TC_NB * TC_D_COLS;
+constexpr int TC_A_COL0 = TC_NB * TC_D_COLS;       // A stages after the accumulators
+constexpr int TC_A_KB_COLS = 32;                   // one k-block of A: 64 fp16 per lane = 32 columns
+constexpr int TC_TMEM_COLS = 512;
+static_assert(TC_A_COL0 + TC_AS * TC_KG * TC_A_KB_COLS <= TC_TMEM_COLS, "tensor memory columns");
 constexpr int TC_LUT_BYTES = 256 * 32 * 4;         // entry v, lane l at word 32 v + l
 constexpr int TC_HALF = 32;                        // batch columns per epilogue warp
 constexpr int TC_SLOT_FLOATS = 64 * TC_ROWS;       // partial tile [batch row / 4][weight row][4]
@@ -1017,15 +1021,14 @@ template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     nf4_gemm_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap xmap, const TcArgs ta) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full_w[TC_WS_MAX], empty_w[TC_WS_MAX], full_x[TC_XS];
+    __shared__ __align__(8) uint64_t full_w[TC_WS_MAX], empty_w[TC_WS_MAX], full_x[TC_XS], empty_x[TC_XS];
     __shared__ __align__(8) uint64_t full_a[TC_AS], empty_a[TC_AS], acc_full[TC_NB], acc_empty[TC_NB], drain;
     __shared__ uint32_t tmem_s;
-    // 1024-byte aligned carve-up: x ring | A ring | LUT | weight ring
+    // 1024-byte aligned carve-up: x ring | LUT | weight ring
     const uint32_t raw_s = smem_u32(smem_raw);
     uint8_t* x_ring = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
     const int xs_bytes = ta.n_mma * 128;
-    uint8_t* a_ring = x_ring + TC_XS * TC_KG * xs_bytes;
-    uint32_t* lut_s = reinterpret_cast<uint32_t*>(a_ring + TC_AS * TC_KG * TC_A_BYTES);
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(x_ring + TC_XS * TC_KG * xs_bytes);
     uint8_t* w_ring = reinterpret_cast<uint8_t*>(lut_s) + TC_LUT_BYTES;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1053,9 +1056,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < WS; ++s) {
             mbar_init(&full_w[s], 1);
-            mbar_init(&empty_w[s], 4 + TC_EPI_WARPS);   // the item's decode warps and the epilogue warps
+            mbar_init(&empty_w[s], 4);   // the item's decode warps
         }
-        for (int s = 0; s < TC_XS; ++s) mbar_init(&full_x[s], 1);
+        for (int s = 0; s < TC_XS; ++s) {
+            mbar_init(&full_x[s], 1);
+            mbar_init(&empty_x[s], 1);
+        }
         for (int s = 0; s < TC_AS; ++s) {
             mbar_init(&full_a[s], 4);
             mbar_init(&empty_a[s], 1);
@@ -1103,7 +1109,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int issued_x = 0;
             bool ok = true;
             for (int j = 0; j < n_items; ++j) {
-                if (j >= TC_XS && !mbar_wait(&empty_a[j % TC_AS], uint32_t(((j / TC_AS) + 1) & 1), ta.err, 21)) {
+                if (j >= TC_XS && !mbar_wait(&empty_x[j % TC_XS], uint32_t(((j / TC_XS) + 1) & 1), ta.err, 21)) {
                     ok = false;
                     break;
                 }
@@ -1122,7 +1128,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int grp = warp >> 2, r = warp & 3;
         const uint32_t lut_base = smem_u32(lut_s);
         const uint32_t lane_b8 = uint32_t(lane) << 3;
-        const int row = 32 * r + lane;   // A tile row of this lane
         int T = int((u0 + grp) / NKG), kg = int((u0 + grp) % NKG);
         for (int j = grp; j < n_items; j += TC_GROUPS) {
             const int nk = min(TC_KG, KB - kg * TC_KG);
@@ -1133,20 +1138,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint8_t* unit = w_ring + (j % WS) * TC_W_BYTES + (r * TC_KG + q) * UNIT_BYTES;
                     const uint4 c0 = lds128(unit + 16 * lane), c1 = lds128(unit + 512 + 16 * lane);
                     const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                    uint8_t* arow = a_ring + ((j % TC_AS) * TC_KG + q) * TC_A_BYTES + row * 128;
+                    // lanes 32r .. 32r + 31 of the stage: column i = k 2i, 2i + 1
+                    const uint32_t ta0 = tmem + (uint32_t(32 * r) << 16) +
+                                         uint32_t(TC_A_COL0 + ((j % TC_AS) * TC_KG + q) * TC_A_KB_COLS);
 #pragma unroll
-                    for (int ch = 0; ch < 8; ++ch) {   // chunk ch = k 8ch .. 8ch+7
-                        const uint4 v = decode_word(lut_base, cw[ch], lane_b8);
-                        *reinterpret_cast<uint4*>(arow + ((ch ^ (row & 7)) << 4)) = v;
+                    for (int hh = 0; hh < 2; ++hh) {
+                        uint32_t d[16];
+#pragma unroll
+                        for (int ch = 0; ch < 4; ++ch) {
+                            const uint4 v = decode_word(lut_base, cw[4 * hh + ch], lane_b8);
+                            d[4 * ch] = v.x; d[4 * ch + 1] = v.y; d[4 * ch + 2] = v.z; d[4 * ch + 3] = v.w;
+                        }
+                        tmem_st16(ta0 + uint32_t(16 * hh), d);
                     }
                 }
+                tmem_wait_st();
             }
             kg += TC_GROUPS;
             while (kg >= NKG) {
                 kg -= NKG;
                 ++T;
             }
-            fence_proxy_async();   // the A tile is read by the tensor cores (async proxy)
+            tc_fence_before();   // the A tile's tensor-memory stores before the MMA thread's wait
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&empty_w[j % WS]);
@@ -1155,8 +1168,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else if (warp == TC_MMA_WARP) {   // the whole warp waits, one lane issues (warp kept converged)
         const uint32_t idesc = tc_idesc_f16(TC_ROWS, ta.n_mma);
-        const uint64_t adesc0 = sw128_kmajor_desc(smem_u32(a_ring));   // start address field steps by 16-byte units
-        const uint64_t bdesc0 = sw128_kmajor_desc(smem_u32(x_ring));
+        const uint64_t bdesc0 = sw128_kmajor_desc(smem_u32(x_ring));   // start address field steps by 16-byte units
         int kbc = 0;   // k-blocks issued: accumulator buffer kbc % TC_NB
         int kg = int(u0 % NKG);
         bool ok = true;
@@ -1172,18 +1184,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint64_t a0 = adesc0 + uint64_t((((j % TC_AS) * TC_KG + q) * TC_A_BYTES) >> 4);
+                    const uint32_t a0 = tmem + uint32_t(TC_A_COL0 + ((j % TC_AS) * TC_KG + q) * TC_A_KB_COLS);
                     const uint64_t b0 = bdesc0 + uint64_t((((j % TC_XS) * TC_KG + q) * xs_bytes) >> 4);
                     const uint32_t d0 = tmem + uint32_t(buf * TC_D_COLS);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)   // a fresh accumulator per k-block
-                        tc_mma_f16(d0, a0 + uint64_t((32 * k) >> 4), b0 + uint64_t((32 * k) >> 4), idesc,
-                                   k ? 1u : 0u);
+                        tc_mma_f16_ta(d0, a0 + uint32_t(8 * k), b0 + uint64_t((32 * k) >> 4), idesc, k ? 1u : 0u);
                     tc_commit(&acc_full[buf]);
                 }
                 __syncwarp();
             }
-            if (lane == 0) tc_commit(&empty_a[j % TC_AS]);   // frees the item's A and x stages
+            if (lane == 0) {   // frees the item's A and x stages once its MMAs have completed
+                tc_commit(&empty_a[j % TC_AS]);
+                tc_commit(&empty_x[j % TC_XS]);
+            }
             __syncwarp();
         }
         if (lane == 0) tc_commit(&drain);   // every MMA of this CTA has completed before TMEM is freed
@@ -1204,12 +1218,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int len = min(n_items - j, NKG - kg0);
             const bool whole = kg0 == 0 && len == NKG;
             const bool row_ok = 4 * T + q4 < n_rg;
+            // absmax of this lane's row, k-block kb, read from the unit stream in global memory (L2: the
+            // producer has just fetched it) two items ahead of its use
+            const __half* am_g = reinterpret_cast<const __half*>(
+                p.packed + int64_t(4 * T + q4) * KB * UNIT_BYTES + UNIT_CODE_BYTES + 2 * lane);
+            auto am_load = [&](int kb) -> unsigned short {
+                return (cols && row_ok && kb < KB) ? __ldg(reinterpret_cast<const unsigned short*>(am_g) +
+                                                           int64_t(kb) * (UNIT_BYTES / 2))
+                                                   : (unsigned short)0;
+            };
+            unsigned short am_pipe[3][TC_KG];   // items jj, jj + 1, jj + 2
+#pragma unroll
+            for (int a = 0; a < 2; ++a)
+#pragma unroll
+                for (int q = 0; q < TC_KG; ++q) am_pipe[a][q] = am_load((kg0 + a) * TC_KG + q);
 #pragma unroll
             for (int i = 0; i < TC_HALF; ++i) v[i] = 0.f;
             for (int jj = j; jj < j + len && ok; ++jj) {
                 const int kb0 = (kg0 + (jj - j)) * TC_KG, nk = min(TC_KG, KB - kb0);
-                const uint8_t* amax = w_ring + (jj % WS) * TC_W_BYTES + q4 * TC_KG * UNIT_BYTES + UNIT_CODE_BYTES +
-                                      2 * lane;
+#pragma unroll
+                for (int q = 0; q < TC_KG; ++q) am_pipe[2][q] = am_load(kb0 + 2 * TC_KG + q);
                 for (int q = 0; q < nk; ++q, ++kbc) {
                     const int buf = kbc % TC_NB;
                     if (!mbar_wait(&acc_full[buf], uint32_t((kbc / TC_NB) & 1), ta.err, 28)) {
@@ -1218,8 +1246,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                     tc_fence_after();
                     if (cols) {   // 16 columns at a time: v += absmax * block sum
-                        const float am =
-                            row_ok ? __half2float(*reinterpret_cast<const __half*>(amax + q * UNIT_BYTES)) : 0.f;
+                        const float am = __half2float(__ushort_as_half(q ? am_pipe[0][1] : am_pipe[0][0]));
                         const uint32_t ta0 = tmem + (uint32_t(32 * q4) << 16) + uint32_t(buf * TC_D_COLS + m0);
 #pragma unroll
                         for (int h16 = 0; h16 < TC_HALF / 16; ++h16) {
@@ -1237,8 +1264,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty_w[jj % WS]);   // absmax of the item read
+#pragma unroll
+                for (int q = 0; q < TC_KG; ++q) {
+                    am_pipe[0][q] = am_pipe[1][q];
+                    am_pipe[1][q] = am_pipe[2][q];
+                }
             }
             if (!ok) break;
             const int n = T * TC_ROWS + rho;
@@ -1794,8 +1824,7 @@ static int nf4_gemm_tc(const nova_nf4_args* a, int epi, cudaStream_t stream) {
         cudaGetLastError();
         return fail(NOVA_ERR_CUDA, "device queries failed");
     }
-    const int64_t fixed =
-        1024 + int64_t(TC_XS) * TC_KG * ta.n_mma * 128 + int64_t(TC_AS) * TC_KG * TC_A_BYTES + TC_LUT_BYTES;
+    const int64_t fixed = 1024 + int64_t(TC_XS) * TC_KG * ta.n_mma * 128 + TC_LUT_BYTES;
     ta.ws = int(std::min<int64_t>(TC_WS_MAX, (optin - 1024 - fixed) / TC_W_BYTES));   // 1 KB for static smem
     if (ta.ws < 2) return fail(NOVA_ERR_UNSUPPORTED, "shared memory");
     const int64_t nsmem = fixed + int64_t(ta.ws) * TC_W_BYTES;
