@@ -5,6 +5,8 @@ weight / KV set so that the working set exceeds the 126 MB L2).
     python -m nova_b200.bench_kernels gemv --n 19456 --k 2560 --epilogue silu --norm
     python -m nova_b200.bench_kernels attn --ctx 32768 --batch 1
     python -m nova_b200.bench_kernels gemm --n 151936 --k 2560 --m 64   # batched tcgen05 GEMM
+    python -m nova_b200.bench_kernels prefill --n 512 --prefix 8192      # prefill attention
+    python -m nova_b200.bench_kernels prefill_e2e --prompt 8192          # decoder prefill
     python -m nova_b200.bench_kernels all          # the config-2 shapes + config-3 sweep
 
 Prints one JSON line per case with the launch time and achieved GB/s
@@ -227,6 +229,66 @@ def bench_append_attn(ctx: int = 4096, batch: int = 1, q_heads: int = 32, kv_hea
             "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
 
 
+def bench_prefill_attn(n: int, prefix: int, batch: int = 1, q_heads: int = 32, kv_heads: int = 8,
+                       iters: int = 10, seed: int = 0) -> dict:
+    """nova_attn_prefill_int8: a chunk of ``n`` queries at positions [prefix,
+    prefix + n) attending causally to an int8 prefix of ``prefix`` tokens
+    (read in place) and to the chunk's own fp16 keys.  Algorithmic work: 4 *
+    q_heads * 128 FLOPs per (query, key) pair attended (QK and PV); bytes =
+    the int8 prefix (272 B per token and KV head) + the chunk's fp16 q/k/v/out."""
+    from .kvattn import prefill_attention
+
+    dev = torch.device("cuda")
+    d = 128
+    g = torch.Generator(device=dev).manual_seed(seed)
+    max_len = prefix + n + GROUP_T
+    ng = -(-max_len // GROUP_T)
+    kq = torch.randint(0, 256, (batch, kv_heads, max_len, d), generator=g, device=dev, dtype=torch.uint8)
+    vq = torch.randint(0, 256, (batch, kv_heads, max_len, d), generator=g, device=dev, dtype=torch.uint8)
+    sc = [(torch.rand(batch, kv_heads, ng, d, generator=g, device=dev) * 0.01).half() for _ in range(4)]
+    q = torch.randn(batch, q_heads, n, d, generator=g, device=dev).half()
+    k = torch.randn(batch, kv_heads, n, d, generator=g, device=dev).half()
+    v = torch.randn(batch, kv_heads, n, d, generator=g, device=dev).half()
+    out = torch.empty(batch, n, q_heads * d, dtype=torch.float16, device=dev)
+    int8 = (kq, sc[0], sc[1], vq, sc[2], sc[3])
+
+    def fn(i):
+        prefill_attention(q, k, v, prefix=prefix, int8=int8 if prefix else None, int8_len=prefix, out=out)
+
+    us = _graph_time(fn, 1, iters)
+    pairs = n * prefix + n * (n + 1) // 2
+    flops = 4.0 * batch * q_heads * d * pairs
+    nbytes = batch * kv_heads * prefix * 272 + 2 * batch * (q_heads + 2 * kv_heads) * n * d * 2
+    return {"kernel": "attn_prefill_int8", "n": n, "prefix": prefix, "batch": batch, "us": round(us, 3),
+            "tflops": round(flops / (us * 1e-6) / 1e12, 2), "bytes": nbytes,
+            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+
+
+def bench_prefill_e2e(prompt: int, chunk: int = 512, seed: int = 0) -> dict:
+    """NovaDecoder.prefill of a ``prompt``-token prompt in ``chunk``-token
+    chunks (36-layer config, random weights): prompt tokens per second,
+    wall time around the call with a device synchronize."""
+    import time
+
+    from .decoder import DecoderConfig, DecoderWeights, NovaDecoder
+
+    cfg = DecoderConfig()
+    W = DecoderWeights.random_init(cfg, seed=seed)
+    dec = NovaDecoder(W, max_len=prompt + 64, batch=1)
+    ids = torch.randint(0, cfg.vocab_size, (1, prompt), generator=torch.Generator().manual_seed(seed))
+    dec.prefill(ids, chunk=chunk)   # warm-up (and GEMM unit packing)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        dec.prefill(ids, chunk=chunk)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    t = sorted(times)[1]
+    return {"kernel": "prefill_e2e", "prompt": prompt, "chunk": chunk, "s": round(t, 4),
+            "tok_s": round(prompt / t, 1)}
+
+
 CONFIG2 = [("q_proj", 4096, 2560), ("k_proj", 1024, 2560), ("v_proj", 1024, 2560), ("o_proj", 2560, 4096),
            ("gate_proj", 9728, 2560), ("up_proj", 9728, 2560), ("down_proj", 2560, 9728),
            ("lm_head", 151936, 2560)]
@@ -261,6 +323,13 @@ def main() -> None:
     b.add_argument("--chunk", type=int, default=0)
     b.add_argument("--sets", type=int, default=0)
     b.add_argument("--iters", type=int, default=20)
+    f = sub.add_parser("prefill")
+    f.add_argument("--n", type=int, default=512, help="queries in the chunk")
+    f.add_argument("--prefix", type=int, default=8192, help="int8 prefix tokens")
+    f.add_argument("--iters", type=int, default=10)
+    e = sub.add_parser("prefill_e2e")
+    e.add_argument("--prompt", type=int, default=8192)
+    e.add_argument("--chunk", type=int, default=512)
     sub.add_parser("all")
     args = ap.parse_args()
     _lib.lib()
@@ -272,6 +341,11 @@ def main() -> None:
     elif args.cmd == "gemm":
         _lib.set_launch_flags(_lib.LAUNCH_PDL)
         print(json.dumps(bench_gemm(args.n, args.k, args.m, args.epilogue, args.sets, args.iters)))
+    elif args.cmd == "prefill":
+        _lib.set_launch_flags(_lib.LAUNCH_PDL)
+        print(json.dumps(bench_prefill_attn(args.n, args.prefix, iters=args.iters)))
+    elif args.cmd == "prefill_e2e":
+        print(json.dumps(bench_prefill_e2e(args.prompt, args.chunk)))
     elif args.cmd == "attn":
         print(json.dumps(bench_attn(args.ctx, args.batch, window=args.window, chunk=args.chunk, sets=args.sets,
                                     iters=args.iters)))
