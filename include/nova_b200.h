@@ -442,17 +442,20 @@ typedef struct nova_qk_prefill_args {
 NOVA_API int nova_qk_prefill(const nova_qk_prefill_args* args, void* stream);
 
 /*
- * Batched NF4 GEMM for M = 1..64 rows:
+ * Batched NF4 GEMM for M >= 1 rows (M <= 64: batched decode; above: prefill):
  * y = x @ dequant(W)^T computed as the reference kernel does
  * (src/nova/kernels.py:213-232): per 64-element block the fp32 sum of
  * code * x (fp16 codebook values, products exact), times the block's absmax,
  * accumulated in fp32; the epilogues of nova_nf4_gemv (PLAIN without bias,
  * RESIDUAL, SILU_MUL, ARGMAX with the step finalize, F32).  No norm prologue
  * (normalize x with nova_rmsnorm).  Weights in the tcgen05 unit layout
- * (layout = 2, from nova_nf4_pack_tc): codes decoded into shared-memory A
+ * (layout = 2, from nova_nf4_pack_tc): codes decoded into tensor-memory A
  * tiles, x tiles by TMA, block sums in tensor memory, (tile, k-block) work
- * split evenly over one wave of CTAs with deterministic partial sums.  Other
- * layouts: NOVA_ERR_UNSUPPORTED.
+ * split evenly over one wave of CTAs with deterministic partial sums.  M > 64
+ * (no ARGMAX epilogue, no step finalize): 128 x 256 tiles, each weight
+ * k-block as fp16 hi + lo terms (code * absmax = hi + lo to ~2^-22) so that
+ * all of K accumulates in tensor memory in fp32.  Other layouts:
+ * NOVA_ERR_UNSUPPORTED.
  * x needs a 16-byte aligned base and a row stride that is a multiple of 8.
  * Workspace: nova_nf4_gemm_workspace_bytes(), zeroed once.
  * Replaces NF4Linear.forward / fused_nf4_linear for batched rows

@@ -1336,6 +1336,341 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Wide NF4 GEMM for M > 64 rows (prefill chunks): a dense contraction, so the
+// tile is 128 weight rows x 128 token rows and every MMA is M 128 x N 128 x
+// K 16 (full tcgen05 rate per flop).  Each k-block's A tile carries the
+// weights as two fp16 terms, hi = fp16(code * absmax) and lo = fp16(code *
+// absmax - hi) (the product of two fp16 values is exact in fp32, and so is the
+// difference), both multiplied by x into the same TMEM accumulator: code *
+// absmax * x to ~2^-22 per product, so K need not be cut at every 64-block
+// boundary.  The tensor cores accumulate a group of TW_G k-blocks (64 MMAs)
+// into one of two TMEM buffers; the epilogue warps add each group's sums into
+// fp32 registers (round to nearest), which keeps the long-K error at the
+// level of the reference kernel's per-block fp32 sums
+// (src/nova/kernels.py:213-232).  Work items = (weight tile, 128-row token
+// tile) pairs, dealt round-robin to a persistent grid; no split-K.
+//   producer warp   bulk-copies each k-block's 4 units into the weight ring;
+//   x producer      TMA-loads the [128 x 64] x tile of each k-block;
+//   decode warps    2 groups (k-block parity) x 4 row groups: LUT -> code,
+//                   x absmax in fp32, split into hi/lo, tcgen05.st.32x32b
+//                   into the k-block's A stage (hi columns, then lo);
+//   MMA thread      per k-block 4 K slices x (hi, lo) MMAs into the group's
+//                   buffer; commits free the A / x stages and hand a finished
+//                   group to the epilogue;
+//   epilogue warps  8 warps (lane quarter x 64 token columns): per group
+//                   tcgen05.ld + fp32 add into registers; after the item's
+//                   last group the plain / residual / SiLU*up / fp32 epilogue.
+
+constexpr int TW_MT = 128;                         // token rows per tile (MMA N)
+constexpr int TW_G = 8;                            // k-blocks per TMEM accumulation group
+constexpr int TW_DEC_WARPS = 8;                    // 2 groups x 4 row groups
+constexpr int TW_PROD_WARP = TW_DEC_WARPS;
+constexpr int TW_MMA_WARP = TW_DEC_WARPS + 1;
+constexpr int TW_EPI_WARP0 = TW_DEC_WARPS + 2;     // 8 epilogue warps
+constexpr int TW_EPI_WARPS = 8;
+constexpr int TW_XPROD_WARP = TW_EPI_WARP0 + TW_EPI_WARPS;
+constexpr int TW_WARPS = TW_XPROD_WARP + 1;
+constexpr int TW_THREADS = TW_WARPS * 32;
+constexpr int TW_COLS = TW_MT / 2;                 // token columns per epilogue warp
+constexpr int TW_AS = 4;                           // A stages (k-blocks) in tensor memory
+constexpr int TW_XS = 6;                           // x stages (k-blocks), 16 KB each
+constexpr int TW_WS_MAX = 16;
+constexpr int TW_W_BYTES = 4 * UNIT_BYTES;         // one k-block of a 128-row tile
+constexpr int TW_X_BYTES = TW_MT * 128;
+constexpr int TW_A_COL0 = 2 * TW_MT;               // accumulators [0, 256), A stages after them
+constexpr int TW_A_COLS = 64;                      // hi 32 + lo 32 columns per k-block
+static_assert(TW_A_COL0 + TW_AS * TW_A_COLS <= 512, "tensor memory columns");
+
+struct TwArgs {
+    int ws;               // weight ring stages
+    int m_tiles;
+    int64_t items;        // weight tiles * m_tiles
+    int* err;
+};
+
+// fp16x2 codebook values (k, k+1) times absmax -> hi and lo fp16x2 words
+__device__ __forceinline__ void split_hi_lo(uint32_t code2, float am, uint32_t& hi, uint32_t& lo) {
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&code2));
+    const float p0 = c.x * am, p1 = c.y * am;   // exact: 11-bit x 11-bit significands
+    const __half2 h = __floats2half2_rn(p0, p1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(p0 - hf.x, p1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Epilogue of weight row n for token rows m0 .. m0 + 15 (v[i] = row m0 + i).
+template <int EPI>
+__device__ __forceinline__ void tw_epilogue16(const Params& p, int n, int rho, const float* v, int m0) {
+    const bool valid = n < p.N;
+    if constexpr (EPI == EPI_SILU_MUL) {   // rows 16i..16i+7 gate, 16i+8..16i+15 the matching up rows
+        const bool gate_row = (rho & 15) < 8;
+        const int n_out = (n >> 4) * 8 + (n & 7);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int m = m0 + i;
+            const float upv = __shfl_down_sync(0xffffffffu, v[i], 8);
+            if (m < p.M && valid && gate_row) {
+                const float gate = __half2float(__float2half_rn(v[i]));
+                const float up = __half2float(__float2half_rn(upv));
+                const float s = __half2float(__float2half_rn(__fdiv_rn(gate, 1.0f + expf(-gate))));
+                p.out[int64_t(m) * p.out_stride + n_out] = __float2half_rn(s * up);
+            }
+        }
+    } else if constexpr (EPI == EPI_F32) {
+        float* o = reinterpret_cast<float*>(p.out);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int m = m0 + i;
+            if (m < p.M && valid) o[int64_t(m) * p.out_stride + n] = v[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int m = m0 + i;
+            if (m >= p.M || !valid) continue;
+            __half h = __float2half_rn(v[i]);
+            if (EPI == EPI_RESIDUAL)
+                h = __float2half_rn(__half2float(__ldcg(p.residual + int64_t(m) * p.res_stride + n)) +
+                                    __half2float(h));
+            p.out[int64_t(m) * p.out_stride + n] = h;
+        }
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(TW_THREADS, 1)
+    nf4_gemm_wide_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap xmap, const TwArgs ta) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_w[TW_WS_MAX], empty_w[TW_WS_MAX], full_x[TW_XS], empty_x[TW_XS];
+    __shared__ __align__(8) uint64_t full_a[TW_AS], empty_a[TW_AS], acc_full[2], acc_empty[2], drain;
+    __shared__ uint32_t tmem_s;
+    // 1024-byte aligned carve-up: x ring | LUT | weight ring
+    const uint32_t raw_s = smem_u32(smem_raw);
+    uint8_t* x_ring = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(x_ring + TW_XS * TW_X_BYTES);
+    uint8_t* w_ring = reinterpret_cast<uint8_t*>(lut_s) + TC_LUT_BYTES;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KB = p.KB;
+    const int NG = (KB + TW_G - 1) / TW_G;   // accumulation groups per item
+    const int n_rg = p.N / UNIT_ROWS;
+    const int WS = ta.ws;
+    // this CTA's items: i = blockIdx.x + j * gridDim.x; item -> (weight tile, token tile)
+    const int n_items = ta.items > blockIdx.x ? int((ta.items - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    const int total_kb = n_items * KB;   // k-blocks of all this CTA's items, in order
+    auto item_of = [&](int j, int& T, int& mt) {
+        const int64_t i = int64_t(blockIdx.x) + int64_t(j) * gridDim.x;
+        T = int(i / ta.m_tiles);
+        mt = int(i % ta.m_tiles);
+    };
+
+    auto issue_w = [&](int g) {   // producer lane 0: the 4 units of global k-block g of this CTA
+        int T, mt;
+        item_of(g / KB, T, mt);
+        const int kb = g % KB;
+        const int rgs = min(4, n_rg - 4 * T);
+        const int s = g % WS;
+        mbar_arrive_expect_tx(&full_w[s], uint32_t(rgs) * UNIT_BYTES);
+        for (int r = 0; r < rgs; ++r)
+            bulk_g2s(w_ring + s * TW_W_BYTES + r * UNIT_BYTES, p.packed + (int64_t(4 * T + r) * KB + kb) * UNIT_BYTES,
+                     UNIT_BYTES, &full_w[s]);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < WS; ++s) {
+            mbar_init(&full_w[s], 1);
+            mbar_init(&empty_w[s], 4);
+        }
+        for (int s = 0; s < TW_XS; ++s) {
+            mbar_init(&full_x[s], 1);
+            mbar_init(&empty_x[s], 1);
+        }
+        for (int s = 0; s < TW_AS; ++s) {
+            mbar_init(&full_a[s], 4);
+            mbar_init(&empty_a[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], TW_EPI_WARPS);
+        }
+        mbar_init(&drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == TW_MMA_WARP) {
+        tmem_alloc(&tmem_s, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_s;
+    int issued_w = 0;
+    if (warp == TW_PROD_WARP && lane == 0)   // weights: independent of every earlier kernel
+        for (; issued_w < WS && issued_w < total_kb; ++issued_w) issue_w(issued_w);
+    build_lut32<TW_THREADS>(lut_s, p.lut);
+    pdl_trigger();
+    pdl_wait();
+    __syncthreads();
+
+    if (warp == TW_PROD_WARP) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int g = issued_w; g < total_kb; ++g) {
+                if (!mbar_wait(&empty_w[g % WS], uint32_t(((g / WS) + 1) & 1), ta.err, 30)) {
+                    ok = false;
+                    break;
+                }
+                issue_w(g);
+                ++issued_w;
+            }
+            if (!ok)
+                for (int g = max(0, issued_w - WS); g < issued_w; ++g)
+                    mbar_wait(&full_w[g % WS], uint32_t((g / WS) & 1), ta.err, 30);
+        }
+    } else if (warp == TW_XPROD_WARP) {
+        if (lane == 0) {
+            int issued_x = 0;
+            bool ok = true;
+            for (int g = 0; g < total_kb; ++g) {
+                if (g >= TW_XS && !mbar_wait(&empty_x[g % TW_XS], uint32_t(((g / TW_XS) + 1) & 1), ta.err, 31)) {
+                    ok = false;
+                    break;
+                }
+                int T, mt;
+                item_of(g / KB, T, mt);
+                const int s = g % TW_XS;
+                mbar_arrive_expect_tx(&full_x[s], uint32_t(TW_X_BYTES));
+                tma_load_2d(x_ring + s * TW_X_BYTES, &xmap, (g % KB) * 64, mt * TW_MT, &full_x[s]);
+                ++issued_x;
+            }
+            if (!ok)
+                for (int g = max(0, issued_x - TW_XS); g < issued_x; ++g)
+                    mbar_wait(&full_x[g % TW_XS], uint32_t((g / TW_XS) & 1), ta.err, 31);
+        }
+    } else if (warp < TW_DEC_WARPS) {
+        const int grp = warp >> 2, r = warp & 3;
+        const uint32_t lut_base = smem_u32(lut_s);
+        const uint32_t lane_b8 = uint32_t(lane) << 3;
+        for (int g = grp; g < total_kb; g += 2) {
+            int T, mt;
+            item_of(g / KB, T, mt);
+            if (!mbar_wait(&full_w[g % WS], uint32_t((g / WS) & 1), ta.err, 32)) break;
+            if (g >= TW_AS && !mbar_wait(&empty_a[g % TW_AS], uint32_t(((g / TW_AS) + 1) & 1), ta.err, 33)) break;
+            if (4 * T + r < n_rg) {
+                const uint8_t* unit = w_ring + (g % WS) * TW_W_BYTES + r * UNIT_BYTES;
+                const uint4 c0 = lds128(unit + 16 * lane), c1 = lds128(unit + 512 + 16 * lane);
+                const float am = __half2float(*reinterpret_cast<const __half*>(unit + UNIT_CODE_BYTES + 2 * lane));
+                const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const uint32_t ta0 =
+                    tmem + (uint32_t(32 * r) << 16) + uint32_t(TW_A_COL0 + (g % TW_AS) * TW_A_COLS);
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t dh[16], dl[16];
+#pragma unroll
+                    for (int ch = 0; ch < 4; ++ch) {
+                        const uint4 v = decode_word(lut_base, cw[4 * hh + ch], lane_b8);
+                        split_hi_lo(v.x, am, dh[4 * ch], dl[4 * ch]);
+                        split_hi_lo(v.y, am, dh[4 * ch + 1], dl[4 * ch + 1]);
+                        split_hi_lo(v.z, am, dh[4 * ch + 2], dl[4 * ch + 2]);
+                        split_hi_lo(v.w, am, dh[4 * ch + 3], dl[4 * ch + 3]);
+                    }
+                    tmem_st16(ta0 + uint32_t(16 * hh), dh);
+                    tmem_st16(ta0 + uint32_t(32 + 16 * hh), dl);
+                }
+                tmem_wait_st();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty_w[g % WS]);
+                mbar_arrive(&full_a[g % TW_AS]);
+            }
+        }
+    } else if (warp == TW_MMA_WARP) {   // the whole warp waits, one lane issues
+        const uint32_t idesc = tc_idesc_f16(TC_ROWS, TW_MT);
+        const uint64_t bdesc0 = sw128_kmajor_desc(smem_u32(x_ring));
+        int gc = 0;   // accumulation groups started: buffer gc % 2
+        for (int g = 0; g < total_kb; ++g) {
+            const int kb = g % KB;
+            const bool first = kb % TW_G == 0, last = kb % TW_G == TW_G - 1 || kb == KB - 1;
+            const int buf = gc & 1;
+            if (first && gc >= 2 && !mbar_wait(&acc_empty[buf], uint32_t(((gc >> 1) + 1) & 1), ta.err, 34)) break;
+            if (!mbar_wait(&full_a[g % TW_AS], uint32_t((g / TW_AS) & 1), ta.err, 35)) break;
+            if (!mbar_wait(&full_x[g % TW_XS], uint32_t((g / TW_XS) & 1), ta.err, 36)) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a0 = tmem + uint32_t(TW_A_COL0 + (g % TW_AS) * TW_A_COLS);
+                const uint64_t b0 = bdesc0 + uint64_t(((g % TW_XS) * TW_X_BYTES) >> 4);
+                const uint32_t d0 = tmem + uint32_t(buf * TW_MT);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint64_t bk = b0 + uint64_t((32 * k) >> 4);
+                    tc_mma_f16_ta(d0, a0 + uint32_t(8 * k), bk, idesc, (first && k == 0) ? 0u : 1u);
+                    tc_mma_f16_ta(d0, a0 + uint32_t(32 + 8 * k), bk, idesc, 1u);
+                }
+                tc_commit(&empty_a[g % TW_AS]);
+                tc_commit(&empty_x[g % TW_XS]);
+                if (last) tc_commit(&acc_full[buf]);
+            }
+            __syncwarp();
+            if (last) ++gc;
+        }
+        if (lane == 0) tc_commit(&drain);   // every MMA of this CTA has completed before TMEM is freed
+        __syncwarp();
+        mbar_wait(&drain, 0u, ta.err, 37);
+    } else if (warp < TW_EPI_WARP0 + TW_EPI_WARPS) {   // epilogue warps
+        const int q4 = warp & 3;
+        const int half = (warp - TW_EPI_WARP0) >> 2;
+        const int rho = 32 * q4 + lane;
+        float v[TW_COLS];
+        int gc = 0;
+        bool ok = true;
+        for (int j = 0; j < n_items && ok; ++j) {
+            int T, mt;
+            item_of(j, T, mt);
+            const int m0 = mt * TW_MT + half * TW_COLS;   // first token row of this warp's columns
+            const int ncols = min(TW_COLS, p.M - m0);       // may be <= 0 for a ragged token tile
+#pragma unroll
+            for (int i = 0; i < TW_COLS; ++i) v[i] = 0.f;
+            for (int grp = 0; grp < NG; ++grp, ++gc) {
+                const int buf = gc & 1;
+                if (!mbar_wait(&acc_full[buf], uint32_t((gc >> 1) & 1), ta.err, 38)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c16 = 0; c16 < TW_COLS / 16; ++c16) {
+                    if (16 * c16 < ncols) {
+                        uint32_t d[16];
+                        tmem_ld16(tmem + (uint32_t(32 * q4) << 16) + uint32_t(buf * TW_MT + half * TW_COLS + 16 * c16),
+                                  d);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[16 * c16 + i] += __uint_as_float(d[i]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            }
+            if (!ok) break;
+            const int n = T * TC_ROWS + rho;
+#pragma unroll
+            for (int c16 = 0; c16 < TW_COLS / 16; ++c16)
+                if (16 * c16 < ncols) tw_epilogue16<EPI>(p, n, rho, v + 16 * c16, m0 + 16 * c16);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == TW_MMA_WARP) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 // ---------------------------------------------------------------- quantizer / packer
 
 __global__ void nf4_quantize_kernel(const __half* __restrict__ w, int64_t n_blocks, int kb, int N,
@@ -1842,11 +2177,59 @@ static int nf4_gemm_tc(const nova_nf4_args* a, int epi, cudaStream_t stream) {
     return NOVA_OK;
 }
 
+// Wide path of nova_nf4_gemm (M > 64; arguments already validated).
+static int nf4_gemm_wide(const nova_nf4_args* a, int epi, cudaStream_t stream) {
+    const int64_t m = a->m, n = a->n, k = a->k;
+    Params p{};
+    p.x = (const __half*)a->x;
+    p.x_stride = a->x_stride;
+    p.packed = (const uint8_t*)a->packed;
+    p.lut = (const uint32_t*)a->lut;
+    p.residual = (const __half*)a->residual;
+    p.res_stride = a->res_stride;
+    p.out = (__half*)a->out;
+    p.out_stride = a->out_stride;
+    p.M = int(m);
+    p.N = int(n);
+    p.K = int(k);
+    p.KB = int(k / 64);
+    TwArgs ta;
+    ta.m_tiles = int((m + TW_MT - 1) / TW_MT);
+    ta.items = ((n + TC_ROWS - 1) / TC_ROWS) * ta.m_tiles;
+    ta.err = (int*)((uint8_t*)a->workspace + 4);
+    CUtensorMap xmap;
+    if (int rc = make_tmap_f16_rows64(&xmap, a->x, uint64_t(m), uint64_t(k), uint64_t(a->x_stride), uint32_t(TW_MT)))
+        return rc;
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "device queries failed");
+    }
+    const int64_t fixed = 1024 + int64_t(TW_XS) * TW_X_BYTES + TC_LUT_BYTES;
+    ta.ws = int(std::min<int64_t>(TW_WS_MAX, (optin - 1024 - fixed) / TW_W_BYTES));   // 1 KB for static smem
+    if (ta.ws < 2) return fail(NOVA_ERR_UNSUPPORTED, "shared memory");
+    const int64_t nsmem = fixed + int64_t(ta.ws) * TW_W_BYTES;
+    using TKern = void (*)(Params, CUtensorMap, TwArgs);
+    static const TKern kernels[5] = {nf4_gemm_wide_kernel<0>, nf4_gemm_wide_kernel<1>, nf4_gemm_wide_kernel<2>,
+                                     nullptr, nf4_gemm_wide_kernel<4>};
+    static int64_t smem_set[5][kMaxDevices] = {};
+    if (!kernels[epi]) return fail(NOVA_ERR_UNSUPPORTED, "the argmax epilogue needs M <= 64");
+    if (int rc = prepare_smem(kernels[epi], nsmem, smem_set[epi])) return rc;
+    const unsigned grid = unsigned(std::min<int64_t>(sm_count(), ta.items));
+    const cudaError_t err = launch(kernels[epi], dim3(grid), dim3(TW_THREADS), size_t(nsmem), stream, p, xmap, ta);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NOVA_ERR_CUDA, "nova_nf4_gemm: launch failed: %s", cudaGetErrorString(err));
+    }
+    return NOVA_OK;
+}
+
 extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
     if (!a) return fail(NOVA_ERR_INVALID, "args must not be NULL");
     const int64_t m = a->m, n = a->n, k = a->k;
     if (a->layout != 2) return fail(NOVA_ERR_UNSUPPORTED, "tcgen05 unit layout (2, nova_nf4_pack_tc) only");
-    if (m < 1 || m > TC_MAX_M) return fail(NOVA_ERR_UNSUPPORTED, "M must be in [1, 64], got %lld", (long long)m);
+    if (m < 1 || m > (1 << 20)) return fail(NOVA_ERR_UNSUPPORTED, "M must be in [1, 2^20], got %lld", (long long)m);
     if (n <= 0 || n % UNIT_ROWS || n > (1 << 30) || k <= 0 || k % 64 || k > (1 << 20))
         return fail(NOVA_ERR_INVALID, "N multiple of 32, K multiple of 64");
     if (a->norm_weight) return fail(NOVA_ERR_UNSUPPORTED, "no norm prologue in the batched GEMM (normalize x first)");
@@ -1868,5 +2251,10 @@ extern "C" int nova_nf4_gemm(const nova_nf4_args* a, void* stream) {
                                                (long long)a->workspace_bytes, (long long)need);
     if ((n + TC_ROWS - 1) / TC_ROWS > TC_MAX_TILES)
         return fail(NOVA_ERR_UNSUPPORTED, "N above %d rows", TC_MAX_TILES * TC_ROWS);
+    if (m > TC_MAX_M) {
+        if (epi == EPI_ARGMAX || a->token_out || a->embed)
+            return fail(NOVA_ERR_UNSUPPORTED, "the argmax epilogue and the step finalize need M <= 64");
+        return nf4_gemm_wide(a, epi, (cudaStream_t)stream);
+    }
     return nf4_gemm_tc(a, epi, (cudaStream_t)stream);
 }

@@ -293,7 +293,7 @@ class NovaDecoder:
 
     # ---------------------------------------------------------------- prefill
 
-    PREFILL_ROWS = 64   # rows per batched-GEMM launch in the prefill
+    PREFILL_ROWS = 4096   # rows per batched-GEMM launch in the prefill (the wide tcgen05 kernel above 64)
 
     def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """RMSNorm of the rows of x ``[R, n]`` (nova_rmsnorm)."""

@@ -190,9 +190,10 @@ def nf4_gemm(x: torch.Tensor, units: torch.Tensor, lut: torch.Tensor, out: torch
              argmax: torch.Tensor | None = None, token_out: torch.Tensor | None = None,
              pos: torch.Tensor | None = None, embed: torch.Tensor | None = None,
              embed_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """``nova_nf4_gemm``: x ``[M <= 64, K]`` against the tcgen05 unit stream
+    """``nova_nf4_gemm``: x ``[M, K]`` against the tcgen05 unit stream
     (:func:`pack_tc`) of an ``[n, K]`` NF4 weight, on the tensor cores; out
-    ``[M, n]`` (``[M, n/2]`` for SiLU*up)."""
+    ``[M, n]`` (``[M, n/2]`` for SiLU*up).  M <= 64: batched decode (every
+    epilogue, the step finalize); M > 64: the wide prefill kernel (no argmax)."""
     m, k = x.shape
     if x.stride(1) != 1 or out.stride(1) != 1:
         raise ValueError("x/out must have a contiguous last dimension")
