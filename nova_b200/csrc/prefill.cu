@@ -52,6 +52,7 @@ struct Params {
     __half* out;                   // [b][t][q_heads * d]
     int64_t o_b, o_t;
     int q_heads, kv_heads, n, prefix, int8_len, window;
+    int kv_vec;                    // fp16 k / v rows 16-byte aligned: 8-channel vector loads
     float scale_log2;
 };
 
@@ -100,31 +101,75 @@ __global__ void __launch_bounds__(THREADS) attn_prefill_kernel(const __grid_cons
     for (int tile = tile_lo; tile < tile_hi; ++tile) {
         const int64_t p0 = int64_t(tile) * KT;
         __syncthreads();   // the previous tile's fragments have been read
-        // ---- stage 64 keys: thread d owns channel d of every key row of the tile
+        // ---- stage 64 keys: thread i owns channels 8c .. 8c+7 (c = i % 16) of rows i / 16 + 8j
         {
-            const int d = threadIdx.x;
+            const int c = threadIdx.x & 15, rb = threadIdx.x >> 4;
             if (p0 < p.int8_len) {   // int8 tile (int8_len is a multiple of 64)
                 const int64_t gi = p0 / GT;
-                const int64_t so = (bh * p.groups + gi) * D + d;
-                const float kst = __half2float(p.kst[so]), kmn = __half2float(p.kmn[so]);
-                const float vst = __half2float(p.vst[so]), vmn = __half2float(p.vmn[so]);
-                const uint8_t* kc = p.kq + (bh * p.max_len + p0) * D + d;
-                const uint8_t* vc = p.vq + (bh * p.max_len + p0) * D + d;
-#pragma unroll 8
-                for (int r = 0; r < KT; ++r) {
-                    Ks[r * LD + d] = __float2half_rn(__fadd_rn(__fmul_rn(float(kc[r * D]), kst), kmn));
-                    Vs[r * LD + d] = __float2half_rn(__fadd_rn(__fmul_rn(float(vc[r * D]), vst), vmn));
+                const int64_t so = (bh * p.groups + gi) * D + 8 * c;
+                float ks[8], km[8], vs[8], vm[8];
+                {
+                    const uint4 a = *reinterpret_cast<const uint4*>(p.kst + so);
+                    const uint4 b = *reinterpret_cast<const uint4*>(p.kmn + so);
+                    const uint4 e = *reinterpret_cast<const uint4*>(p.vst + so);
+                    const uint4 f = *reinterpret_cast<const uint4*>(p.vmn + so);
+                    const __half* ah = reinterpret_cast<const __half*>(&a);
+                    const __half* bh2 = reinterpret_cast<const __half*>(&b);
+                    const __half* eh = reinterpret_cast<const __half*>(&e);
+                    const __half* fh = reinterpret_cast<const __half*>(&f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        ks[i] = __half2float(ah[i]);
+                        km[i] = __half2float(bh2[i]);
+                        vs[i] = __half2float(eh[i]);
+                        vm[i] = __half2float(fh[i]);
+                    }
+                }
+                const uint8_t* kc = p.kq + (bh * p.max_len + p0) * D + 8 * c;
+                const uint8_t* vc = p.vq + (bh * p.max_len + p0) * D + 8 * c;
+#pragma unroll 2
+                for (int j = 0; j < KT / 8; ++j) {
+                    const int r = rb + 8 * j;
+                    const uint2 kb = *reinterpret_cast<const uint2*>(kc + r * D);
+                    const uint2 vb = *reinterpret_cast<const uint2*>(vc + r * D);
+                    uint4 ko, vo;
+                    __half* kh = reinterpret_cast<__half*>(&ko);
+                    __half* vh = reinterpret_cast<__half*>(&vo);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {   // the reference's dequant: fp32 code * step + min, to fp16
+                        const uint32_t kw = i < 4 ? kb.x : kb.y, vw = i < 4 ? vb.x : vb.y;
+                        const float kcode = float((kw >> (8 * (i & 3))) & 0xFFu);
+                        const float vcode = float((vw >> (8 * (i & 3))) & 0xFFu);
+                        kh[i] = __float2half_rn(__fadd_rn(__fmul_rn(kcode, ks[i]), km[i]));
+                        vh[i] = __float2half_rn(__fadd_rn(__fmul_rn(vcode, vs[i]), vm[i]));
+                    }
+                    *reinterpret_cast<uint4*>(Ks + r * LD + 8 * c) = ko;
+                    *reinterpret_cast<uint4*>(Vs + r * LD + 8 * c) = vo;
                 }
             } else {
                 const __half* kp = p.k + b * p.kv_b + int64_t(kvh) * p.kv_h;
                 const __half* vp = p.v + b * p.kv_b + int64_t(kvh) * p.kv_h;
                 const int64_t nk = int64_t(p.prefix) + p.n - p.int8_len;   // fp16 keys held
-#pragma unroll 8
-                for (int r = 0; r < KT; ++r) {
+#pragma unroll 2
+                for (int j = 0; j < KT / 8; ++j) {
+                    const int r = rb + 8 * j;
                     const int64_t kr = p0 + r - p.int8_len;
                     const bool in = kr >= 0 && kr < nk;
-                    Ks[r * LD + d] = in ? kp[kr * p.kv_t + d] : __float2half_rn(0.f);
-                    Vs[r * LD + d] = in ? vp[kr * p.kv_t + d] : __float2half_rn(0.f);
+                    uint4 ko = make_uint4(0u, 0u, 0u, 0u), vo = ko;
+                    if (in && p.kv_vec) {
+                        ko = *reinterpret_cast<const uint4*>(kp + kr * p.kv_t + 8 * c);
+                        vo = *reinterpret_cast<const uint4*>(vp + kr * p.kv_t + 8 * c);
+                    } else if (in) {
+                        __half* kh = reinterpret_cast<__half*>(&ko);
+                        __half* vh = reinterpret_cast<__half*>(&vo);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            kh[i] = kp[kr * p.kv_t + 8 * c + i];
+                            vh[i] = vp[kr * p.kv_t + 8 * c + i];
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(Ks + r * LD + 8 * c) = ko;
+                    *reinterpret_cast<uint4*>(Vs + r * LD + 8 * c) = vo;
                 }
             }
         }
@@ -308,6 +353,9 @@ extern "C" int nova_attn_prefill_int8(const nova_prefill_attn_args* a, void* str
         return fail(NOVA_ERR_INVALID, "the int8 prefix needs the cache buffers, int8_len <= max_len and "
                                       "groups = ceil(max_len / 64)");
     auto mis = [](const void* ptr, int al) { return ptr && (reinterpret_cast<uintptr_t>(ptr) % al); };
+    if (a->int8_len && (mis(a->kq, 8) || mis(a->vq, 8) || mis(a->kmn, 16) || mis(a->kst, 16) || mis(a->vmn, 16) ||
+                        mis(a->vst, 16)))
+        return fail(NOVA_ERR_ALIGN, "int8 codes 8-byte and scale vectors 16-byte aligned");
     if (mis(a->q, 4) || mis(a->out, 4) || (a->q_t_stride % 2) || (a->q_h_stride % 2) || (a->q_b_stride % 2) ||
         (a->o_t_stride % 2) || (a->o_b_stride % 2))
         return fail(NOVA_ERR_ALIGN, "q / out need 4-byte alignment and even strides");
@@ -338,6 +386,8 @@ extern "C" int nova_attn_prefill_int8(const nova_prefill_attn_args* a, void* str
     p.prefix = int(a->prefix);
     p.int8_len = int(a->int8_len);
     p.window = int(std::min<int64_t>(a->window, 0x7fffffff));
+    p.kv_vec = (!mis(a->k, 16) && !mis(a->v, 16) && a->kv_t_stride % 8 == 0 && a->kv_h_stride % 8 == 0 &&
+                a->kv_b_stride % 8 == 0) ? 1 : 0;
     p.scale_log2 = float(1.0 / sqrt(double(D))) * LOG2E;
     const dim3 grid(unsigned((a->n + QB - 1) / QB), unsigned(a->q_heads), unsigned(a->batch));
     const cudaError_t err = launch(attn_prefill_kernel, grid, dim3(THREADS), 0, (cudaStream_t)stream, p);
