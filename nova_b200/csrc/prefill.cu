@@ -61,6 +61,19 @@ __device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Four 8x8 fp16 matrices from shared memory (lane l gives a row address of
+// matrix l / 8); .trans hands each thread the transposed fragment.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
 __global__ void __launch_bounds__(THREADS) attn_prefill_kernel(const __grid_constant__ Params p) {
     __shared__ __align__(16) __half Ks[KT * LD];
     __shared__ __align__(16) __half Vs[KT * LD];
@@ -176,16 +189,18 @@ __global__ void __launch_bounds__(THREADS) attn_prefill_kernel(const __grid_cons
         __syncthreads();
         if (q0 >= p.n) continue;   // a ragged last block: warps past n only help staging
         // ---- S = Q K^T: 8 n-tiles of 8 keys
+        // B fragments by ldmatrix: matrix i of lane l = keys 8j .. 8j+7, dims 16s + 8i (two k-steps per load)
         float sc[8][4];
+        const uint32_t ks_base = smem_u32(Ks) + uint32_t(((lane & 7) * LD + 8 * (lane >> 3)) * 2);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-            const __half* kr = Ks + (8 * j + g) * LD;
 #pragma unroll
-            for (int s = 0; s < 8; ++s) {
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 16 * s + 2 * t);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 16 * s + 8 + 2 * t);
+            for (int s = 0; s < 8; s += 2) {
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(ks_base + uint32_t((8 * j * LD + 16 * s) * 2), b0, b1, b2, b3);
                 mma_16816(sc[j], qa[s][0], qa[s][1], qa[s][2], qa[s][3], b0, b1);
+                mma_16816(sc[j], qa[s + 1][0], qa[s + 1][1], qa[s + 1][2], qa[s + 1][3], b2, b3);
             }
         }
         // ---- mask, online softmax (rows g: sc[j][0..1], row g + 8: sc[j][2..3])
@@ -251,14 +266,18 @@ __global__ void __launch_bounds__(THREADS) attn_prefill_kernel(const __grid_cons
             ah[2] = pack_h2(hv[4], hv[5]); ah[3] = pack_h2(hv[6], hv[7]);
             al[0] = pack_h2(lv[0], lv[1]); al[1] = pack_h2(lv[2], lv[3]);
             al[2] = pack_h2(lv[4], lv[5]); al[3] = pack_h2(lv[6], lv[7]);
-            const __half* v0 = Vs + (16 * s + 2 * t) * LD;
+            // matrix i of lane l = keys 16s + 8 (i & 1) .. +7, dims 8j + 8 (i >> 1): transposed, the B
+            // fragments of n-tiles j and j + 1
+            const uint32_t vs_base = smem_u32(Vs) +
+                                     uint32_t(((16 * s + 8 * ((lane >> 3) & 1) + (lane & 7)) * LD + 8 * (lane >> 4)) * 2);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int col = 8 * j + g;
-                const uint32_t b0 = pack_h2(v0[col], v0[LD + col]);
-                const uint32_t b1 = pack_h2(v0[8 * LD + col], v0[9 * LD + col]);
+            for (int j = 0; j < 16; j += 2) {
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_trans(vs_base + uint32_t(16 * j), b0, b1, b2, b3);
                 mma_16816(acc[j], ah[0], ah[1], ah[2], ah[3], b0, b1);
                 mma_16816(acc[j], al[0], al[1], al[2], al[3], b0, b1);
+                mma_16816(acc[j + 1], ah[0], ah[1], ah[2], ah[3], b2, b3);
+                mma_16816(acc[j + 1], al[0], al[1], al[2], al[3], b2, b3);
             }
         }
     }
