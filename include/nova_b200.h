@@ -189,8 +189,14 @@ enum nova_nf4_epilogue {
                               out has N/2 columns (LeanMLP act_fn(gate) * up)              */
     NOVA_NF4_ARGMAX = 3,   /* PLAIN, plus atomicMax of a packed (fp16 logit, -index) key
                               into argmax[m] (uint64, zero before the call): greedy token  */
-    NOVA_NF4_F32 = 4       /* out is fp32 [M, out_stride]: the accumulators unrounded, the
+    NOVA_NF4_F32 = 4,      /* out is fp32 [M, out_stride]: the accumulators unrounded, the
                               partial sum of one tensor-parallel rank before the all-reduce */
+    NOVA_NF4_SLOTS = 5     /* native layout, N/32 <= SMs, M <= 8: the k-blocks of all row
+                              groups are split evenly over one CTA per SM and each CTA
+                              writes its fp32 sums of the (at most two) row groups it
+                              touches into out = float [SMs][2][M][32] (no residual add,
+                              no cross-CTA reduction): the next GEMV adds them while it
+                              stages its input (add_slots)                              */
 };
 
 /* Workspace bytes for nova_nf4_gemv with N output rows on the current device
@@ -245,6 +251,14 @@ typedef struct nova_nf4_args {
     int64_t m, n, k;
     int64_t epilogue;         /* enum nova_nf4_epilogue                        */
     int64_t layout;           /* 0: reference packed/absmax; 1: native units   */
+    /* Deferred row-parallel reduction (with a norm prologue, K <= 8 * 512):
+       x = fp16(x + fp16(sum of the SLOTS written by the previous GEMV, whose
+       N is this K and whose K is add_k)), summed in a fixed CTA order, is what
+       this launch normalizes; CTA 0 also stores it to resid_out (fp16 [m, k],
+       stride x_stride; must not alias x).  NULL add_slots: off.             */
+    const void* add_slots;
+    int64_t add_k;
+    void* resid_out;
 } nova_nf4_args;
 
 NOVA_API int nova_nf4_gemv(const nova_nf4_args* args, void* stream);

@@ -15,7 +15,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().with_name("libnova_b200.so")
 
 NOVA_OK, NOVA_ERR_INVALID, NOVA_ERR_ALIGN, NOVA_ERR_UNSUPPORTED, NOVA_ERR_CUDA = range(5)
-NF4_PLAIN, NF4_RESIDUAL, NF4_SILU_MUL, NF4_ARGMAX, NF4_F32 = range(5)
+NF4_PLAIN, NF4_RESIDUAL, NF4_SILU_MUL, NF4_ARGMAX, NF4_F32, NF4_SLOTS = range(6)
 NOVA_ATTN_NOALLOC_SCRATCH_BYTES = 4 << 20   # built-in scratch of nova_attn_decode_int8_noalloc
 
 _P = ctypes.c_void_p
@@ -49,6 +49,7 @@ class NF4Args(ctypes.Structure):
         ("token_out", _P), ("pos", _P), ("embed", _P), ("embed_out", _P), ("embed_out_stride", _I),
         ("embed_dim", _I), ("workspace", _P), ("workspace_bytes", _I),
         ("m", _I), ("n", _I), ("k", _I), ("epilogue", _I), ("layout", _I),
+        ("add_slots", _P), ("add_k", _I), ("resid_out", _P),
     ]
 
 

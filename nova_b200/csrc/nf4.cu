@@ -45,7 +45,7 @@ constexpr int UNIT_ROWS = 32;
 constexpr int UNIT_CODE_BYTES = 1024;
 constexpr int UNIT_BYTES = 1088;
 
-enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_F32 = 4 };
+enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_F32 = 4, EPI_SLOTS = 5 };
 
 struct Params {
     const __half* x;          // fp16 [M, K] (the residual when norm_w != nullptr)
@@ -73,6 +73,12 @@ struct Params {
     int M, N, K, KB, n_tiles, total_warps;
     int64_t units;
     int res_rows = 0;         // CTA kernel: residual rows staged in shared memory per CTA (0: read in the epilogue)
+    // deferred row-parallel reduction: x += the slots of the previous GEMV (its units, grid, k-blocks per row
+    // group), stored to resid_out by CTA 0
+    const float* add_slots = nullptr;
+    int64_t add_units = 0;
+    int add_G = 0, add_KB = 0;
+    __half* resid_out = nullptr;
 };
 
 template <typename T>
@@ -228,9 +234,72 @@ __device__ __forceinline__ uint4 norm_w_chunk(const Params& p) {
     return make_uint4(0u, 0u, 0u, 0u);
 }
 
+// Deferred row-parallel reduction for the 8 columns 8i .. 8i+7 of row 0: the
+// previous GEMV's CTAs c in [cf, cl] each left fp32 sums of their k-blocks of
+// this row group in slot (c, row group == their first ? 0 : 1); they are added
+// in CTA order, rounded to fp16 (the projection's output) and added to the
+// residual chunk xv as the reference's fp16 residual add does.  CTA 0 stores
+// the result for the later kernels.
+struct SlotPlan {
+    const float4* src[4];   // contributors in CTA order (n of them)
+    int n;
+};
+
+// The slot addresses of chunk i (static: computed before the dependency wait).
+__device__ __forceinline__ SlotPlan slot_plan(const Params& p, int i) {
+    SlotPlan sp;
+    sp.n = 0;
+    const int kv8 = p.K / 8;
+    if (!p.add_slots || i >= kv8) return sp;
+    const int rg = i >> 2, r0 = 8 * (i & 3);
+    const int U = int(p.add_units), G = p.add_G, KB = p.add_KB;   // U * G < 2^31 (host-checked)
+    const int u0 = rg * KB;
+    const int cf = ((u0 + 1) * G - 1) / U;
+    const int cl = ((u0 + KB) * G - 1) / U;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int cc = cf + q;
+        const int first = ((U * cc) / G) / KB;
+        sp.src[q] = reinterpret_cast<const float4*>(p.add_slots + (int64_t(cc) * 2 + (first == rg ? 0 : 1)) * 32 + r0);
+    }
+    sp.n = cl - cf + 1;
+    return sp;
+}
+
+// Deferred row-parallel reduction for the 8 columns 8i .. 8i+7 of row 0: the
+// previous GEMV's CTAs each left fp32 sums of their k-blocks of this row group
+// in a slot (SlotPlan); they are added in CTA order, rounded to fp16 (the
+// projection's output) and added to the residual chunk xv as the reference's
+// fp16 residual add does.  CTA 0 stores the result for the later kernels.
+__device__ __forceinline__ void add_slots_chunk(const Params& p, const SlotPlan& sp, int i, uint4& xv) {
+    float4 a[4][2];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        if (q < sp.n) {
+            a[q][0] = __ldcg(sp.src[q]);
+            a[q][1] = __ldcg(sp.src[q] + 1);
+        }
+    float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (q >= sp.n) break;
+        sum[0] += a[q][0].x; sum[1] += a[q][0].y; sum[2] += a[q][0].z; sum[3] += a[q][0].w;
+        sum[4] += a[q][1].x; sum[5] += a[q][1].y; sum[6] += a[q][1].z; sum[7] += a[q][1].w;
+    }
+    __half2* h = reinterpret_cast<__half2*>(&xv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 r = __half22float2(h[e]);
+        const float o0 = __half2float(__float2half_rn(sum[2 * e])), o1 = __half2float(__float2half_rn(sum[2 * e + 1]));
+        h[e] = __floats2half2_rn(r.x + o0, r.y + o1);
+    }
+    if (blockIdx.x == 0 && p.resid_out) *reinterpret_cast<uint4*>(p.resid_out + 8 * i) = xv;
+}
+
 // `wpre`: norm_w_chunk() loaded earlier (nullptr: loaded here).
 template <int THREADS>
-__device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4* wpre = nullptr) {
+__device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4* wpre = nullptr,
+                                        const SlotPlan* sp = nullptr) {
     __shared__ float red[THREADS / 32][MAX_M];
     __shared__ float rstd[MAX_M];
     const int kv8 = p.K / 8;
@@ -261,6 +330,7 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4
                     if (m >= p.M) break;
                     xv[m] = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i));
                 }
+                if (sp && sp->n) add_slots_chunk(p, *sp, i, xv[0]);   // M == 1
 #pragma unroll
                 for (int m = 0; m < MAX_M; ++m) {
                     if (m >= p.M) break;
@@ -496,10 +566,11 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         for (int c = 0; c < NAT_STAGES && c < n_chunks; ++c) issue(c);
     }
     const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);   // in flight with the LUT loads
+    const SlotPlan sp = slot_plan(p, threadIdx.x);
     build_lut<NAT_THREADS>(lut_s, p.lut);
     pdl_trigger();
     pdl_wait();
-    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre);
+    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre, &sp);
     __syncthreads();
     if (!active) return;
 
@@ -606,7 +677,9 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     const int G = gridDim.x;
     const int KB = p.KB;
     const int64_t n_rg = p.units / KB;
-    const int64_t u_begin = n_rg * c / G * KB, u_end = n_rg * (c + 1) / G * KB;   // whole row groups
+    // whole row groups; SLOTS: an equal share of all units (at most two row groups, N / 32 <= G)
+    const int64_t u_begin = EPI == EPI_SLOTS ? p.units * c / G : n_rg * c / G * KB;
+    const int64_t u_end = EPI == EPI_SLOTS ? p.units * (c + 1) / G : n_rg * (c + 1) / G * KB;
     const int rg_first = int(u_begin / KB);
     const int rg_last = u_end > u_begin ? int((u_end - 1) / KB) : rg_first - 1;
 
@@ -663,6 +736,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             if (!issue_next()) break;
     }
     const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);   // in flight with the LUT loads
+    const SlotPlan sp = slot_plan(p, threadIdx.x);
     build_lut<NAT_THREADS>(lut_s, p.lut);
     pdl_trigger();
     pdl_wait();
@@ -683,7 +757,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             if (i < p.M * res_n) rv[u] = __ldcg(p.residual + (i / res_n) * p.res_stride + res_row0 + i % res_n);
         }
     }
-    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre);
+    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre, &sp);
     if (res_staged) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -762,7 +836,18 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_empty);
             const int64_t base = int64_t(rg) * KB;
-            if (u_begin <= base && u_end >= base + KB) {
+            if (EPI == EPI_SLOTS) {   // this CTA's sums of row group rg, rows 16 tile + g (+8), batch rows 2t, 2t+1
+                float* slot = reinterpret_cast<float*>(p.out) + (int64_t(c) * 2 + (rg == rg_first ? 0 : 1)) * p.M * 32;
+#pragma unroll
+                for (int tl = 0; tl < 2; ++tl)
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int m = 2 * t + e;
+                            if (m < p.M) slot[m * 32 + 16 * tl + g + 8 * hr] = r[tl][2 * hr + e];
+                        }
+            } else if (u_begin <= base && u_end >= base + KB) {
                 const __half* rs = res_staged ? res_s : nullptr;
                 epilogue<EPI>(p, 2 * rg, r[0], g, t, 0, rs, res_row0, p.res_rows);
                 epilogue<EPI>(p, 2 * rg + 1, r[1], g, t, 0, rs, res_row0, p.res_rows);
@@ -1899,9 +1984,22 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     if (!a->x || !a->packed || (!native && !a->absmax) || !a->lut || !a->out || !a->workspace)
         return fail(NOVA_ERR_INVALID, "NULL pointer");
     const int epi = int(a->epilogue);
-    if (epi < EPI_PLAIN || epi > EPI_F32) return fail(NOVA_ERR_INVALID, "bad epilogue %d", epi);
-    if (epi == EPI_F32 && (reinterpret_cast<uintptr_t>(a->out) % 4))
-        return fail(NOVA_ERR_ALIGN, "the fp32 epilogue needs a 4-byte aligned out");
+    if (epi < EPI_PLAIN || epi > EPI_SLOTS) return fail(NOVA_ERR_INVALID, "bad epilogue %d", epi);
+    if ((epi == EPI_F32 || epi == EPI_SLOTS) && (reinterpret_cast<uintptr_t>(a->out) % 16))
+        return fail(NOVA_ERR_ALIGN, "the fp32 and slot epilogues need a 16-byte aligned out");
+    if (epi == EPI_SLOTS && (!native || n / UNIT_ROWS > sm_count()))
+        return fail(NOVA_ERR_UNSUPPORTED, "the slot epilogue needs the native layout and N / 32 <= %d", sm_count());
+    if (a->add_slots) {   // deferred reduction of a SLOTS launch with N = this K, K = add_k
+        const int64_t akb = a->add_k / 64, units = (k / UNIT_ROWS) * akb, G = sm_count();
+        if (m != 1 || !native || !a->norm_weight || k / 8 > NAT_THREADS || k % UNIT_ROWS || a->add_k <= 0 ||
+            a->add_k % 64 || k / UNIT_ROWS > G || (akb - 1) * G / units + 2 > 4 || (units + akb) * G >= (1ll << 31))
+            return fail(NOVA_ERR_UNSUPPORTED, "add_slots needs M = 1, the native layout, a norm prologue, K <= %d "
+                                              "and a SLOTS producer with at most 4 CTAs per row group",
+                        8 * NAT_THREADS);
+        if (reinterpret_cast<uintptr_t>(a->add_slots) % 16 || (a->resid_out && reinterpret_cast<uintptr_t>(a->resid_out) % 16))
+            return fail(NOVA_ERR_ALIGN, "add_slots and resid_out must be 16-byte aligned");
+        if (a->resid_out == a->x) return fail(NOVA_ERR_INVALID, "resid_out must not alias x");
+    }
     if (epi == EPI_RESIDUAL && !a->residual) return fail(NOVA_ERR_INVALID, "residual epilogue needs residual");
     if (epi == EPI_ARGMAX && !a->argmax) return fail(NOVA_ERR_INVALID, "argmax epilogue needs argmax");
     if (epi != EPI_PLAIN && a->bias) return fail(NOVA_ERR_UNSUPPORTED, "bias only with the plain epilogue");
@@ -1950,6 +2048,13 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     //  workspace finds them at the same place) | per-row-tile counters]
     p.done = (unsigned*)(ws + partial_bytes());
     p.counters = (unsigned*)(ws + partial_bytes() + 256);
+    if (a->add_slots) {
+        p.add_slots = (const float*)a->add_slots;
+        p.add_KB = int(a->add_k / 64);
+        p.add_units = int64_t(k / UNIT_ROWS) * p.add_KB;
+        p.add_G = sm_count();
+        p.resid_out = (__half*)a->resid_out;
+    }
 
     using Kern = void (*)(Params);
     cudaError_t err;
@@ -1996,7 +2101,8 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         // lm_head: with several row groups per CTA the CTA-level schedule
         // would synchronise its 16 warps once per row group); CTA-level
         // split-K on whole row groups below that (no cross-CTA reduction).
-        const bool warp_level = (launch_flags() & 2) || n / UNIT_ROWS >= 2 * int64_t(sm_count());
+        const bool warp_level =
+            epi != EPI_SLOTS && ((launch_flags() & 2) || n / UNIT_ROWS >= 2 * int64_t(sm_count()));
         if (warp_level) {
             NKern kern = kernels[xg][epi];
             const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + stage_units * ring_unit;
@@ -2007,14 +2113,15 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
             err = launch(kern, dim3(grid), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p, int(stage_units),
                          errp);
         } else {   // CTA-level split-K
-            static const NKern cta_kernels[2][5] = {
+            static const NKern cta_kernels[2][6] = {
                 {nf4_gemv_cta_kernel<0, false>, nf4_gemv_cta_kernel<1, false>, nf4_gemv_cta_kernel<2, false>,
-                 nf4_gemv_cta_kernel<3, false>, nf4_gemv_cta_kernel<4, false>},
+                 nf4_gemv_cta_kernel<3, false>, nf4_gemv_cta_kernel<4, false>, nf4_gemv_cta_kernel<5, false>},
                 {nf4_gemv_cta_kernel<0, true>, nf4_gemv_cta_kernel<1, true>, nf4_gemv_cta_kernel<2, true>,
-                 nf4_gemv_cta_kernel<3, true>, nf4_gemv_cta_kernel<4, true>}};
-            static int64_t cta_smem_set[2][5][kMaxDevices] = {};
+                 nf4_gemv_cta_kernel<3, true>, nf4_gemv_cta_kernel<4, true>, nf4_gemv_cta_kernel<5, true>}};
+            static int64_t cta_smem_set[2][6][kMaxDevices] = {};
             const int64_t red_bytes = int64_t(NAT_WARPS) * 32 * 32;
-            const int64_t grid = std::min<int64_t>(sm_count(), n / UNIT_ROWS);
+            // SLOTS: one CTA per SM over an equal share of all units; otherwise whole row groups
+            const int64_t grid = epi == EPI_SLOTS ? int64_t(sm_count()) : std::min<int64_t>(sm_count(), n / UNIT_ROWS);
             const int64_t rg_max = (n / UNIT_ROWS + grid - 1) / grid;   // row groups of the largest CTA share
             // residual rows staged per CTA when they fit in 4 values per thread
             p.res_rows = (epi == EPI_RESIDUAL && rg_max * UNIT_ROWS * m <= 4 * NAT_THREADS) ? int(rg_max * UNIT_ROWS) : 0;

@@ -48,7 +48,8 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib
-from .kernels import build_nf4_lut, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native, pack_tc
+from .kernels import (build_nf4_lut, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native, pack_tc,
+                      slots_buffer)
 from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk, prefill_attention
 from .quant import nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
@@ -280,7 +281,29 @@ class NovaDecoder:
         # attn_fused=True: the q/k norm + RoPE + ring append runs in the attention's prologue (one launch
         # and one kernel boundary fewer per layer)
         self.attn_fused = bool(attn_fused)
+        # batch 1 on one GPU (when the shapes fit): o_proj and down_proj run on every SM over equal shares of
+        # their k-blocks and leave fp32 sums per CTA (NF4_SLOTS); the next GEMV adds them to the residual while
+        # it stages its input, alternating between two residual buffers.  Otherwise (tensor parallelism,
+        # batches above 1) they add into the residual in their own epilogue.
+        self.deferred = self.batch == 1 and not self.tp.active and self._deferred_fits()
+        self.slots = slots_buffer(self.device) if self.deferred else None
+        self.resid_alt = torch.zeros_like(self.resid) if self.deferred else None
         self._staged = None   # fp16 K/V per layer of the positions prefilled / injected since the last reset
+
+    def _deferred_fits(self) -> bool:
+        """The deferred reduction's shape limits (nova_nf4_gemv with NF4_SLOTS /
+        add_slots): at most one row group per SM, at most four CTAs per row
+        group, and the consumer's input in one 8-column chunk per thread."""
+        h = self.cfg.hidden_size
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        if h % 32 or h // 32 > sms or h // 8 > 512:
+            return False
+        for k in (self.q_dim, self.inter):
+            kb = k // 64
+            units = (h // 32) * kb
+            if k % 64 or (kb - 1) * sms // units + 2 > 4 or (units + kb) * sms >= 2 ** 31:
+                return False
+        return True
 
     def _pick_chunk(self) -> int:
         """Split size for the attention (``kvattn.pick_chunk``)."""
@@ -594,7 +617,7 @@ class NovaDecoder:
     # ---------------------------------------------------------------- decode
 
     def _gemv(self, x, w: NF4Weight, out, *, epilogue: int = _lib.NF4_PLAIN, norm_weight=None, residual=None,
-              argmax=None, token_out=None, pos=None, embed=None, embed_out=None) -> None:
+              argmax=None, token_out=None, pos=None, embed=None, embed_out=None, add=None, resid_out=None) -> None:
         """The step's NF4 projection: nova_nf4_gemv up to GEMV_ROWS rows, else
         nova_nf4_gemm (after nova_rmsnorm when the projection has a norm prologue)."""
         B = x.shape[0]
@@ -611,12 +634,14 @@ class NovaDecoder:
         for r in range(0, B, GEMV_ROWS):
             sl = slice(r, min(B, r + GEMV_ROWS))
             last = sl.stop == B
-            nf4_gemv(x[sl], w.units, None, self.lut, out[sl], epilogue=epilogue, norm_weight=norm_weight, eps=eps,
+            o = out if epilogue == _lib.NF4_SLOTS else out[sl]   # the slot buffer is per launch, not per row
+            nf4_gemv(x[sl], w.units, None, self.lut, o, epilogue=epilogue, norm_weight=norm_weight, eps=eps,
                      residual=None if residual is None else residual[sl],
                      argmax=None if argmax is None else argmax[sl],
                      token_out=None if token_out is None else token_out[sl], pos=pos if last else None,
                      embed=embed, embed_out=None if embed_out is None else embed_out[sl],
-                     workspace=self.gemv_ws, n=w.n)
+                     workspace=self.gemv_ws, n=w.n, add_slots=None if add is None else add[0],
+                     add_k=0 if add is None else add[1], resid_out=resid_out)
 
     def _qk_args(self, li: int, lw) -> "_lib.QKArgs":
         cfg, cache = self.cfg, self.cache
@@ -657,6 +682,9 @@ class NovaDecoder:
             _lib.call("nova_residual_add_f32", self.part32.data_ptr(), self.part32.stride(0), self.resid.data_ptr(),
                       self.resid.stride(0), B, cfg.hidden_size, stream)
 
+        if self.deferred:
+            self._step_body_deferred(q3, a3)
+            return
         for li, lw in enumerate(self.w.layers):
             qk = None
             if self.attn_fused:
@@ -674,6 +702,32 @@ class NovaDecoder:
         self._gemv(self.resid, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
                    argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
                    embed_out=self.resid)
+
+    def _step_body_deferred(self, q3, a3) -> None:
+        """The step with o_proj / down_proj reductions deferred into the next
+        GEMV's input staging: the residual lives in resid (step input, R0) and
+        resid_alt (R1); q|k|v of layer l >= 1 reads R1 + down(l-1) and writes
+        R0, gate|up reads R0 + o(l) and writes R1, the lm_head reads R1 +
+        down(35) (and its step finalize writes the next embedding to R0)."""
+        cfg, cache = self.cfg, self.cache
+        r0, r1, slots = self.resid, self.resid_alt, self.slots
+        for li, lw in enumerate(self.w.layers):
+            if li == 0:
+                self._gemv(r0, lw.qkv, self.qkv, norm_weight=lw.input_ln)
+            else:
+                self._gemv(r1, lw.qkv, self.qkv, norm_weight=lw.input_ln, add=(slots, self.inter), resid_out=r0)
+            launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
+                                  cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
+                             cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
+                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window,
+                             qk=self._qk_args(li, lw))
+            self._gemv(self.attn, lw.o, slots, epilogue=_lib.NF4_SLOTS)
+            self._gemv(r0, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln,
+                       add=(slots, self.q_dim), resid_out=r1)
+            self._gemv(self.act, lw.down, slots, epilogue=_lib.NF4_SLOTS)
+        self._gemv(r1, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
+                   argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
+                   embed_out=r0, add=(slots, self.inter))
 
     def _qkv_step(self, li: int, lw) -> None:
         """input norm + q|k|v projection, then q/k norm + RoPE + KV append of layer li as a launch of

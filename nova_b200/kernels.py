@@ -129,12 +129,18 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
              norm_weight: torch.Tensor | None = None, eps: float = 1e-6, argmax: torch.Tensor | None = None,
              token_out: torch.Tensor | None = None, pos: torch.Tensor | None = None,
              embed: torch.Tensor | None = None, embed_out: torch.Tensor | None = None,
-             workspace: torch.Tensor | None = None, n: int | None = None) -> torch.Tensor:
+             workspace: torch.Tensor | None = None, n: int | None = None,
+             add_slots: torch.Tensor | None = None, add_k: int = 0,
+             resid_out: torch.Tensor | None = None) -> torch.Tensor:
     """Launch ``nova_nf4_gemv`` on 2-D views (x ``[M, K]``, out ``[M, N or N/2]``).
 
     Reference layout: ``packed`` uint8 ``[N, K/2]`` with ``absmax``
     ``[K/64, N]``.  Native layout: ``packed`` is the 1-D unit stream from
-    :func:`pack_native`, ``absmax`` is None and ``n`` gives N."""
+    :func:`pack_native`, ``absmax`` is None and ``n`` gives N.
+    ``epilogue=NF4_SLOTS``: out is a :func:`slots_buffer` that receives each
+    CTA's fp32 sums; a following launch with ``add_slots`` (that buffer) and
+    ``add_k`` (the slot launch's K) adds them to its input x (fp16 residual
+    add) before its norm prologue and stores the sum to ``resid_out``."""
     m, k = x.shape
     native = absmax is None
     if native:
@@ -169,8 +175,17 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
     a.embed_dim = embed.shape[1] if embed is not None else 0
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     a.m, a.n, a.k, a.epilogue = m, n, k, int(epilogue)
+    if add_slots is not None:
+        a.add_slots, a.add_k, a.resid_out = add_slots.data_ptr(), int(add_k), _lib.ptr(resid_out)
     _lib.check(_lib.lib().nova_nf4_gemv(_lib.ctypes.byref(a), _lib.stream_of(x.device)), "nova_nf4_gemv")
     return out
+
+
+def slots_buffer(device: torch.device) -> torch.Tensor:
+    """fp32 ``[SMs * 2 * 8, 32]`` buffer for ``NF4_SLOTS`` launches (per
+    CTA the sums of the two row groups it may touch, up to 8 batch rows)."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    return torch.zeros(sms * 2 * 8, 32, dtype=torch.float32, device=device)
 
 
 def gemm_workspace(device: torch.device, n: int, k: int) -> torch.Tensor:

@@ -375,3 +375,38 @@ def test_native_split_k_variants(cuda_lib, variant, n, k, epi):
                 dev = np.maximum(dev, np.abs(alt - want))
         assert np.all(np.abs(got - want) <= dev + 2 * fp16_ulp(want)), f"silu {variant}"
         assert (got == want).mean() > 0.99, f"silu {variant}: too few exact"
+
+
+@pytest.mark.parametrize("n_prev,k_prev", [(2560, 4096), (2560, 9728)])
+def test_slot_epilogue_and_deferred_residual_add(cuda_lib, n_prev, k_prev):
+    """o_proj / down_proj as NF4_SLOTS (every SM takes an equal share of the
+    k-blocks, fp32 sums per CTA) and the next GEMV adding them to the residual
+    while it stages its normed input: the stored residual equals
+    fp16(res + fp16(x @ W^T)) within one fp16 ULP of the oracle, and the next
+    projection matches the oracle on it; run twice (no state left behind)."""
+    from nova_b200 import _lib
+    from nova_b200.kernels import gemv_workspace, nf4_gemv, pack_native, slots_buffer
+
+    _, pp, pa = _weights(n_prev, k_prev, 21)
+    _, qp, qa = _weights(6144, n_prev, 22)
+    a = torch.randn(1, k_prev, generator=torch.Generator().manual_seed(23)).half()
+    res = (torch.randn(1, n_prev, generator=torch.Generator().manual_seed(24)) * 2).half()
+    w = (1 + 0.1 * torch.randn(n_prev, generator=torch.Generator().manual_seed(25))).half()
+    up, uq = pack_native(pp, pa), pack_native(qp, qa)
+    slots = slots_buffer(torch.device("cuda"))
+    ws = gemv_workspace(torch.device("cuda"), 6144)
+    lut = _lut()
+    o16 = _oracle_y(a, pp, pa).astype(np.float16)
+    want_res = (res.float().numpy() + o16.astype(np.float32)).astype(np.float16)
+    for _ in range(2):
+        resid_out = torch.full((1, n_prev), float("nan"), dtype=torch.float16, device="cuda")
+        out = torch.empty(1, 6144, dtype=torch.float16, device="cuda")
+        nf4_gemv(a.cuda(), up, None, lut, slots, epilogue=_lib.NF4_SLOTS, workspace=ws, n=n_prev)
+        nf4_gemv(res.cuda(), uq, None, lut, out, norm_weight=w.cuda(), eps=1e-6, workspace=ws, n=6144,
+                 add_slots=slots, add_k=k_prev, resid_out=resid_out)
+        got_res = resid_out.float().cpu().numpy()
+        w16 = want_res
+        ulp = np.maximum(fp16_ulp(w16), fp16_ulp(-w16)) + fp16_ulp(o16)
+        assert np.all(np.abs(got_res - w16.astype(np.float32)) <= ulp), "deferred residual add"
+        xn = onorm.rms_norm(resid_out.cpu().numpy(), w.numpy(), 1e-6)
+        _check(out, _oracle_y(torch.from_numpy(xn), qp, qa), "projection after the deferred add")
