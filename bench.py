@@ -173,16 +173,22 @@ def _time_kernels(dec, reps: int = 10) -> dict:
 
         def row_par(x, w):
             dec._gemv(x, w, part, epilogue=_lib.NF4_F32)
+    elif dec.deferred:   # batch 1: fp32 sums per CTA, added by the next GEMV's staging
+        slots, r_alt = dec.slots.clone(), scratch["resid"].clone()
+
+        def row_par(x, w):
+            dec._gemv(x, w, slots, epilogue=_lib.NF4_SLOTS)
     else:
         def row_par(x, w):
             dec._gemv(x, w, scratch["resid"], epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"])
+    gate_up_add = dict(add=(slots, dec.q_dim), resid_out=r_alt) if (dec.deferred and not dec.tp.active) else {}
     fams = {
         # the step's q|k|v launch (with q/k norm + RoPE + ring write; pos does not move, so the same ring slot
         # is rewritten)
         "qkv": (lambda lw: dec._qkv_step(layer_index[id(lw)], lw), lambda lw: bytes_of(lw.qkv)),
         "o_proj": (lambda lw: row_par(scratch["attn"], lw.o), lambda lw: bytes_of(lw.o)),
         "gate_up": (lambda lw: dec._gemv(scratch["resid"], lw.gate_up, scratch["act"], epilogue=_lib.NF4_SILU_MUL,
-                                         norm_weight=lw.post_ln),
+                                         norm_weight=lw.post_ln, **gate_up_add),
                     lambda lw: bytes_of(lw.gate_up)),
         "down": (lambda lw: row_par(scratch["act"], lw.down), lambda lw: bytes_of(lw.down)),
     }

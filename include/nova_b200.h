@@ -36,6 +36,11 @@ enum nova_status {
 
 /* Library identification and the last error message of the calling thread. */
 NOVA_API const char* nova_version(void);
+/* sizeof of the argument structs, in this order: nova_attn_int8_args,
+ * nova_nf4_args, nova_qk_args, nova_prefill_attn_args, nova_qk_prefill_args,
+ * nova_sample_args, nova_tp_allreduce_args (n entries at most are written;
+ * returns how many there are).  Lets a binding check its struct mirrors. */
+NOVA_API int nova_abi_sizes(int64_t* out, int n);
 NOVA_API const char* nova_last_error(void);
 
 /* Process-wide launch flags.  Bit 0: launch every kernel with programmatic

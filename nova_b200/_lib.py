@@ -113,6 +113,7 @@ class TPAllReduceArgs(ctypes.Structure):
 
 # name -> argtypes (every entry point returns int status unless noted)
 _SIGNATURES: dict[str, list] = {
+    "nova_abi_sizes": [_P, _i],
     "nova_kv_quant_int8": [_P, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P],
     "nova_kv_dequant_int8": [_P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
     "nova_kv_append_int8": [_P, _P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
@@ -149,6 +150,7 @@ _SIGNATURES: dict[str, list] = {
 }
 _STRING_FNS = ("nova_version", "nova_last_error")
 _INT_FNS = ("nova_get_launch_flags",)
+ABI_STRUCTS = ("AttnArgs", "NF4Args", "QKArgs", "PrefillAttnArgs", "QKPrefillArgs", "SampleArgs", "TPAllReduceArgs")
 
 _lib: ctypes.CDLL | None = None
 

@@ -87,6 +87,16 @@ extern "C" const char* nova_version(void) { return "nova_b200 0.1 (sm_100a, abi 
 
 extern "C" const char* nova_last_error(void) { return nova::g_last_error; }
 
+extern "C" int nova_abi_sizes(int64_t* out, int n) {
+    const int64_t sizes[] = {int64_t(sizeof(nova_attn_int8_args)),    int64_t(sizeof(nova_nf4_args)),
+                             int64_t(sizeof(nova_qk_args)),           int64_t(sizeof(nova_prefill_attn_args)),
+                             int64_t(sizeof(nova_qk_prefill_args)),   int64_t(sizeof(nova_sample_args)),
+                             int64_t(sizeof(nova_tp_allreduce_args))};
+    const int count = int(sizeof(sizes) / sizeof(sizes[0]));
+    for (int i = 0; i < n && i < count && out; ++i) out[i] = sizes[i];
+    return count;
+}
+
 extern "C" int nova_set_launch_flags(int flags) {
     if (flags & ~3) return nova::fail(NOVA_ERR_INVALID, "unknown launch flags 0x%x", flags);
     __atomic_store_n(&nova::g_launch_flags, flags, __ATOMIC_RELAXED);

@@ -79,3 +79,18 @@ def test_fused_append_attention_checks_need_no_gpu():
     assert rc == _lib.NOVA_ERR_INVALID and "tail ring" in _lib.last_error()
     qk.head_dim = 64
     assert lib.nova_qk_append_attn_int8(ctypes.byref(qk), ctypes.byref(at), None) == _lib.NOVA_ERR_UNSUPPORTED
+
+
+def test_ctypes_mirrors_match_the_header_structs():
+    """Every ctypes mirror in nova_b200/_lib.py has the size of the C struct it
+    stands for (nova_abi_sizes), so a field added on one side only is caught
+    without a GPU."""
+    import ctypes
+
+    from nova_b200 import _lib
+
+    n = len(_lib.ABI_STRUCTS)
+    out = (ctypes.c_int64 * n)()
+    assert _lib.lib().nova_abi_sizes(out, n) == n
+    for i, name in enumerate(_lib.ABI_STRUCTS):
+        assert ctypes.sizeof(getattr(_lib, name)) == out[i], f"{name}: {ctypes.sizeof(getattr(_lib, name))} != {out[i]}"
