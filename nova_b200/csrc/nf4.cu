@@ -220,8 +220,7 @@ __device__ __forceinline__ void build_lut(uint32_t* lut_s, const uint32_t* lut) 
 }
 
 // Stage x in shared memory, optionally RMS-normalised in HF order (x read
-// through L2 only: in the fused phase program it was written by other CTAs
-// earlier in the same launch).  When
+// through L2 only: the previous kernel wrote it from other SMs).  When
 // every thread holds at most one 8-element chunk per row (K <= 8 * THREADS),
 // the chunk stays in registers between the sum of squares and the scaling,
 // so x and the norm weight are read once.
