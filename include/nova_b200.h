@@ -196,12 +196,12 @@ enum nova_nf4_epilogue {
                               into argmax[m] (uint64, zero before the call): greedy token  */
     NOVA_NF4_F32 = 4,      /* out is fp32 [M, out_stride]: the accumulators unrounded, the
                               partial sum of one tensor-parallel rank before the all-reduce */
-    NOVA_NF4_SLOTS = 5     /* native layout, N/32 <= SMs, M <= 8: the k-blocks of all row
-                              groups are split evenly over one CTA per SM and each CTA
-                              writes its fp32 sums of the (at most two) row groups it
-                              touches into out = float [SMs][2][M][32] (no residual add,
-                              no cross-CTA reduction): the next GEMV adds them while it
-                              stages its input (add_slots)                              */
+    NOVA_NF4_SLOTS = 5     /* native layout, M <= 8: the k-blocks of all row groups are
+                              split evenly over one CTA per SM and each CTA writes its
+                              fp32 sums of the (at most four) row groups it touches into
+                              out = float [SMs][4][M][32], slot = row group - the CTA's
+                              first (no residual add, no cross-CTA reduction): the next
+                              GEMV adds them while it stages its input (add_slots)      */
 };
 
 /* Workspace bytes for nova_nf4_gemv with N output rows on the current device

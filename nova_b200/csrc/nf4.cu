@@ -46,6 +46,7 @@ constexpr int UNIT_CODE_BYTES = 1024;
 constexpr int UNIT_BYTES = 1088;
 
 enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_F32 = 4, EPI_SLOTS = 5 };
+constexpr int SLOTS_PER_CTA = 4;   // NF4_SLOTS: row groups one CTA's share of the k-blocks may touch
 
 struct Params {
     const __half* x;          // fp16 [M, K] (the residual when norm_w != nullptr)
@@ -259,7 +260,7 @@ __device__ __forceinline__ SlotPlan slot_plan(const Params& p, int i) {
     for (int q = 0; q < 4; ++q) {
         const int cc = cf + q;
         const int first = ((U * cc) / G) / KB;
-        sp.src[q] = reinterpret_cast<const float4*>(p.add_slots + (int64_t(cc) * 2 + (first == rg ? 0 : 1)) * 32 + r0);
+        sp.src[q] = reinterpret_cast<const float4*>(p.add_slots + (int64_t(cc) * SLOTS_PER_CTA + (rg - first)) * 32 + r0);
     }
     sp.n = cl - cf + 1;
     return sp;
@@ -836,7 +837,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             if (lane == 0) mbar_arrive(&bar_empty);
             const int64_t base = int64_t(rg) * KB;
             if (EPI == EPI_SLOTS) {   // this CTA's sums of row group rg, rows 16 tile + g (+8), batch rows 2t, 2t+1
-                float* slot = reinterpret_cast<float*>(p.out) + (int64_t(c) * 2 + (rg == rg_first ? 0 : 1)) * p.M * 32;
+                float* slot = reinterpret_cast<float*>(p.out) + (int64_t(c) * SLOTS_PER_CTA + (rg - rg_first)) * p.M * 32;
 #pragma unroll
                 for (int tl = 0; tl < 2; ++tl)
 #pragma unroll
@@ -1986,12 +1987,15 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
     if (epi < EPI_PLAIN || epi > EPI_SLOTS) return fail(NOVA_ERR_INVALID, "bad epilogue %d", epi);
     if ((epi == EPI_F32 || epi == EPI_SLOTS) && (reinterpret_cast<uintptr_t>(a->out) % 16))
         return fail(NOVA_ERR_ALIGN, "the fp32 and slot epilogues need a 16-byte aligned out");
-    if (epi == EPI_SLOTS && (!native || n / UNIT_ROWS > sm_count()))
-        return fail(NOVA_ERR_UNSUPPORTED, "the slot epilogue needs the native layout and N / 32 <= %d", sm_count());
+    if (epi == EPI_SLOTS &&
+        (!native || ((n / UNIT_ROWS) * (k / 64) / sm_count() + (k / 64) - 1) / (k / 64) + 1 > SLOTS_PER_CTA))
+        return fail(NOVA_ERR_UNSUPPORTED, "the slot epilogue needs the native layout and at most %d row groups per "
+                                          "SM's share of the k-blocks", SLOTS_PER_CTA);
     if (a->add_slots) {   // deferred reduction of a SLOTS launch with N = this K, K = add_k
         const int64_t akb = a->add_k / 64, units = (k / UNIT_ROWS) * akb, G = sm_count();
         if (m != 1 || !native || !a->norm_weight || k / 8 > NAT_THREADS || k % UNIT_ROWS || a->add_k <= 0 ||
-            a->add_k % 64 || k / UNIT_ROWS > G || (akb - 1) * G / units + 2 > 4 || (units + akb) * G >= (1ll << 31))
+            a->add_k % 64 || (units / G + akb - 1) / akb + 1 > SLOTS_PER_CTA || (akb - 1) * G / units + 2 > 4 ||
+            (units + akb) * G >= (1ll << 31))
             return fail(NOVA_ERR_UNSUPPORTED, "add_slots needs M = 1, the native layout, a norm prologue, K <= %d "
                                               "and a SLOTS producer with at most 4 CTAs per row group",
                         8 * NAT_THREADS);

@@ -716,11 +716,11 @@ class NovaDecoder:
                 self._gemv(r0, lw.qkv, self.qkv, norm_weight=lw.input_ln)
             else:
                 self._gemv(r1, lw.qkv, self.qkv, norm_weight=lw.input_ln, add=(slots, self.inter), resid_out=r0)
+            qa = self._qk_args(li, lw)
             launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
                                   cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
-                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window,
-                             qk=self._qk_args(li, lw))
+                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window, qk=qa)
             self._gemv(self.attn, lw.o, slots, epilogue=_lib.NF4_SLOTS)
             self._gemv(r0, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln,
                        add=(slots, self.q_dim), resid_out=r1)

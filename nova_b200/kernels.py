@@ -182,10 +182,11 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
 
 
 def slots_buffer(device: torch.device) -> torch.Tensor:
-    """fp32 ``[SMs * 2 * 8, 32]`` buffer for ``NF4_SLOTS`` launches (per
-    CTA the sums of the two row groups it may touch, up to 8 batch rows)."""
+    """fp32 ``[SMs * 4 * 8, 32]`` buffer for ``NF4_SLOTS`` launches (per
+    CTA the sums of the up to four row groups it may touch, up to 8 batch
+    rows)."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    return torch.zeros(sms * 2 * 8, 32, dtype=torch.float32, device=device)
+    return torch.zeros(sms * 4 * 8, 32, dtype=torch.float32, device=device)
 
 
 def gemm_workspace(device: torch.device, n: int, k: int) -> torch.Tensor:
