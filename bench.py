@@ -171,17 +171,22 @@ def _time_kernels(dec, reps: int = 10) -> dict:
     if dec.tp.active:   # row-parallel projections write fp32 partial sums
         part = dec.part32.clone()
 
-        def row_par(x, w):
+        def row_par(x, w, **kw):
             dec._gemv(x, w, part, epilogue=_lib.NF4_F32)
     elif dec.deferred:   # batch 1: fp32 sums per CTA, added by the next GEMV's staging
         slots, r_alt = dec.slots.clone(), scratch["resid"].clone()
 
-        def row_par(x, w):
-            dec._gemv(x, w, slots, epilogue=_lib.NF4_SLOTS)
+        def row_par(x, w, **kw):
+            dec._gemv(x, w, slots, epilogue=_lib.NF4_SLOTS, **kw)
     else:
-        def row_par(x, w):
+        def row_par(x, w, **kw):
             dec._gemv(x, w, scratch["resid"], epilogue=_lib.NF4_RESIDUAL, residual=scratch["resid"])
     gate_up_add = dict(add=(slots, dec.q_dim), resid_out=r_alt) if (dec.deferred and not dec.tp.active) else {}
+    down_edges = {}
+    if dec.edges is not None:   # gate|up leaves its CTA-edge row groups to down_proj's staging
+        edges = dec.edges.clone()
+        gate_up_add["edge_out"] = edges
+        down_edges = {"edge_in": (edges, dec.cfg.hidden_size)}
     fams = {
         # the step's q|k|v launch (with q/k norm + RoPE + ring write; pos does not move, so the same ring slot
         # is rewritten)
@@ -190,7 +195,7 @@ def _time_kernels(dec, reps: int = 10) -> dict:
         "gate_up": (lambda lw: dec._gemv(scratch["resid"], lw.gate_up, scratch["act"], epilogue=_lib.NF4_SILU_MUL,
                                          norm_weight=lw.post_ln, **gate_up_add),
                     lambda lw: bytes_of(lw.gate_up)),
-        "down": (lambda lw: row_par(scratch["act"], lw.down), lambda lw: bytes_of(lw.down)),
+        "down": (lambda lw: row_par(scratch["act"], lw.down, **down_edges), lambda lw: bytes_of(lw.down)),
     }
     from nova_b200.bench_kernels import _graph_time
 

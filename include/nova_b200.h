@@ -264,6 +264,19 @@ typedef struct nova_nf4_args {
     const void* add_slots;
     int64_t add_k;
     void* resid_out;
+    /* SiLU·mul split at CTA edges (batch-1 decode, gate|up -> down_proj):
+       with edge_out (fp32 [SMs * 2, 32], SILU_MUL, native layout, M = 1) the
+       launch writes out only where one CTA holds all k-blocks of a row group
+       and leaves, per CTA, the fp32 sums of its first and last row group that
+       a neighbouring CTA shares in edge_out[CTA][0 / 1]; a following launch
+       with edge_in (that buffer) and edge_k (the producer's K; its own K must
+       be the producer's N / 2; no norm prologue; SLOTS or the CTA-level
+       schedule) completes those outputs, summed in CTA order with the SiLU·mul
+       arithmetic, while it stages x.  The producer's out is then incomplete on
+       its own.  NULL: off.                                                   */
+    void* edge_out;
+    const void* edge_in;
+    int64_t edge_k;
 } nova_nf4_args;
 
 NOVA_API int nova_nf4_gemv(const nova_nf4_args* args, void* stream);

@@ -50,6 +50,7 @@ class NF4Args(ctypes.Structure):
         ("embed_dim", _I), ("workspace", _P), ("workspace_bytes", _I),
         ("m", _I), ("n", _I), ("k", _I), ("epilogue", _I), ("layout", _I),
         ("add_slots", _P), ("add_k", _I), ("resid_out", _P),
+        ("edge_out", _P), ("edge_in", _P), ("edge_k", _I),
     ]
 
 

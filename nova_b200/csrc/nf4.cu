@@ -80,6 +80,13 @@ struct Params {
     int64_t add_units = 0;
     int add_G = 0, add_KB = 0;
     __half* resid_out = nullptr;
+    // SiLU·mul split at CTA edges (M = 1): edge_out receives, per CTA, the fp32 sums of its first and
+    // last row group when a neighbouring CTA shares them; edge_in (the next launch) completes those
+    // outputs while staging x (producer units, grid, k-blocks per row group)
+    float* edge_out = nullptr;
+    const float* edge_in = nullptr;
+    int64_t edge_units = 0;
+    int edge_G = 0, edge_KB = 0;
 };
 
 template <typename T>
@@ -102,6 +109,15 @@ __device__ __forceinline__ unsigned long long argmax_key(__half v, int idx) {
     unsigned short b = __half_as_ushort(v);
     unsigned short o = (b & 0x8000) ? (unsigned short)(~b) : (unsigned short)(b | 0x8000);
     return (static_cast<unsigned long long>(o) << 32) | static_cast<unsigned long long>(0xffffffffu - unsigned(idx));
+}
+
+// fp16(silu(fp16(gate)) * fp16(up)) from the fp32 sums, silu rounded to fp16 as
+// the reference's fp16 activation does (src/nova/layers.py:173-174).
+__device__ __forceinline__ __half silu_mul_h(float gate_sum, float up_sum) {
+    const float gate = __half2float(__float2half_rn(gate_sum));
+    const float up = __half2float(__float2half_rn(up_sum));
+    const float s = __half2float(__float2half_rn(__fdiv_rn(gate, 1.0f + expf(-gate))));
+    return __float2half_rn(s * up);
 }
 
 // Epilogue of one 16-row tile: lane (g, t) holds rows 16*tile+g (c[0], c[1])
@@ -129,10 +145,7 @@ __device__ __forceinline__ void epilogue(const Params& p, int tile, const float 
         for (int e = 0; e < 2; ++e) {
             const int m = m0 + 2 * t + e;
             if (m >= p.M) continue;
-            const float gate = __half2float(__float2half_rn(c[e]));
-            const float up = __half2float(__float2half_rn(c[2 + e]));
-            const float s = __half2float(__float2half_rn(__fdiv_rn(gate, 1.0f + expf(-gate))));
-            p.out[m * p.out_stride + n] = __float2half_rn(s * up);
+            p.out[m * p.out_stride + n] = silu_mul_h(c[e], c[2 + e]);
         }
         return;
     }
@@ -296,10 +309,36 @@ __device__ __forceinline__ void add_slots_chunk(const Params& p, const SlotPlan&
     if (blockIdx.x == 0 && p.resid_out) *reinterpret_cast<uint4*>(p.resid_out + 8 * i) = xv;
 }
 
+// The output chunk (8 columns) that thread j completes from the previous
+// launch's CTA edges, and its two contributors (static: computed before the
+// dependency wait).  Boundary j / 2 + 1 lies between producer CTAs bnd - 1 and
+// bnd; when it falls inside a row group, that group's 16 outputs (two chunks,
+// j & 1) are summed from the last-row-group slot of CTA bnd - 1 and the
+// first-row-group slot of CTA bnd.
+struct EdgePlan {
+    const float4* a;   // contributors in CTA order: gate sums [0, 2), up sums [2, 4)
+    const float4* b;
+    int i;             // chunk index (outputs 8i .. 8i+7), -1: none
+};
+
+__device__ __forceinline__ EdgePlan edge_plan(const Params& p, int j) {
+    EdgePlan e;
+    e.a = e.b = nullptr;
+    e.i = -1;
+    if (!p.edge_in || j >= 2 * (p.edge_G - 1)) return e;
+    const int bnd = j / 2 + 1, tl = j & 1;
+    const int u = int(p.edge_units) * bnd / p.edge_G;   // units * G < 2^31 (host-checked)
+    if (u % p.edge_KB == 0) return e;
+    e.i = 2 * (u / p.edge_KB) + tl;
+    e.a = reinterpret_cast<const float4*>(p.edge_in + ((bnd - 1) * 2 + 1) * 32 + 16 * tl);
+    e.b = reinterpret_cast<const float4*>(p.edge_in + (bnd * 2) * 32 + 16 * tl);
+    return e;
+}
+
 // `wpre`: norm_w_chunk() loaded earlier (nullptr: loaded here).
 template <int THREADS>
 __device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4* wpre = nullptr,
-                                        const SlotPlan* sp = nullptr) {
+                                        const SlotPlan* sp = nullptr, const EdgePlan* ep = nullptr) {
     __shared__ float red[THREADS / 32][MAX_M];
     __shared__ float rstd[MAX_M];
     const int kv8 = p.K / 8;
@@ -408,6 +447,40 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4
                 if (i < total) *reinterpret_cast<uint4*>(xs + (i / kv8) * p.K + 8 * (i % kv8)) = v[u];
             }
         }
+        if (ep && p.edge_in) {   // uniform: the chunks split at the producer's CTA edges replace what x held
+            // (M = 1; the contributors' loads wait out the barrier, which orders these stores after x's)
+            const bool fix = ep->i >= 0;
+            float4 ea[4], eb[4];
+            if (fix) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    ea[q] = __ldcg(ep->a + q);
+                    eb[q] = __ldcg(ep->b + q);
+                }
+            }
+            __syncthreads();
+            if (fix) {
+                // silu_mul_h's arithmetic, with the eight exponentials issued before the divisions
+                const float ga[8] = {ea[0].x + eb[0].x, ea[0].y + eb[0].y, ea[0].z + eb[0].z, ea[0].w + eb[0].w,
+                                     ea[1].x + eb[1].x, ea[1].y + eb[1].y, ea[1].z + eb[1].z, ea[1].w + eb[1].w};
+                const float ua[8] = {ea[2].x + eb[2].x, ea[2].y + eb[2].y, ea[2].z + eb[2].z, ea[2].w + eb[2].w,
+                                     ea[3].x + eb[3].x, ea[3].y + eb[3].y, ea[3].z + eb[3].z, ea[3].w + eb[3].w};
+                float gt[8], den[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    gt[e] = __half2float(__float2half_rn(ga[e]));
+                    den[e] = 1.0f + expf(-gt[e]);
+                }
+                uint4 o;
+                __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float sl = __half2float(__float2half_rn(__fdiv_rn(gt[e], den[e])));
+                    oh[e] = __float2half_rn(sl * __half2float(__float2half_rn(ua[e])));
+                }
+                *reinterpret_cast<uint4*>(xs + 8 * ep->i) = o;
+            }
+        }
     }
 }
 
@@ -488,8 +561,63 @@ __device__ __forceinline__ void finish_launch(const Params& p, int lane) {
 
 constexpr int NAT_WARPS = 16;
 constexpr int NAT_THREADS = NAT_WARPS * 32;
+constexpr int EDGE_RED_BYTES = NAT_WARPS * 2 * 32 * 4;   // [warp][first / last row group][32 rows] fp32
 constexpr int NAT_STAGES = 2;
 constexpr int NAT_MIN_UNITS = 8;   // units per warp at least (few contributors per row group)
+
+// SiLU·mul with CTA edges (M = 1): the 16 warps of a CTA own consecutive
+// unit ranges, and each leaves its sums of a row group it shares with another
+// warp in edge_red[warp][0 = its first row group, 1 = its last].  After the
+// CTA's last barrier warp j adds the contributors of the CTA's j-th row group
+// in warp order; a row group inside the CTA's units gets the SiLU·mul
+// epilogue, the first and last one, when a neighbouring CTA has the rest of
+// their k-blocks, go to edge_out[CTA][0 / 1] as fp32 sums that the next launch
+// completes (EdgePlan).  Row groups one warp covered alone were finished in
+// its loop.  No cross-CTA reduction, no fence, no counter.
+struct EdgeRed {
+    int rg;          // row group, -1: nothing to add
+    int w0, n;       // contributors: CTA warps w0 .. w0 + n - 1
+    unsigned slots;  // bit k: contributor w0 + k left it in its slot 1
+    int dst;         // -1: SiLU·mul epilogue; else edge_out slot index (CTA * 2 + 0 / 1)
+};
+
+// Static (int32, computed before the dependency wait; units * W < 2^31 host-checked).
+__device__ __forceinline__ EdgeRed edge_red_plan(const Params& p, int warp) {
+    EdgeRed e;
+    e.rg = -1;
+    e.w0 = e.n = 0;
+    e.slots = 0u;
+    e.dst = -1;
+    const int U = int(p.units), W = p.total_warps, KB = p.KB, c = int(blockIdx.x);
+    const int cu0 = U * (c * NAT_WARPS) / W, cu1 = U * ((c + 1) * NAT_WARPS) / W;
+    const int r0 = cu0 / KB, r1 = (cu1 - 1) / KB;
+    const int rg = r0 + warp;
+    if (rg > r1) return e;
+    const int base = rg * KB;
+    const int s0 = max(cu0, base), s1 = min(cu1, base + KB);
+    const int wf = ((s0 + 1) * W - 1) / U, wl = (s1 * W - 1) / U;   // owners of s0 and s1 - 1
+    if (wf == wl && s0 == base && s1 == base + KB) return e;
+    e.rg = rg;
+    e.w0 = wf - c * NAT_WARPS;
+    e.n = wl - wf + 1;
+    for (int k = 0; k < e.n; ++k)
+        if ((U * (wf + k) / W) / KB != rg) e.slots |= 1u << k;
+    if (!(cu0 <= base && cu1 >= base + KB)) e.dst = c * 2 + (rg == r0 ? 0 : 1);
+    return e;
+}
+
+__device__ __forceinline__ void edge_finish(const Params& p, const EdgeRed& e, const float* edge_red, int lane) {
+    if (e.rg < 0) return;
+    float v = 0.f;
+    for (int k = 0; k < e.n; ++k) v += edge_red[((e.w0 + k) * 2 + ((e.slots >> k) & 1u)) * 32 + lane];
+    if (e.dst < 0) {
+        // lane l holds row 16 tile + g + 8 hr (l = 16 tl + 8 hr + g): gate rows hr = 0, up rows hr = 1
+        const float up = __shfl_down_sync(0xffffffffu, v, 8);
+        if ((lane & 8) == 0) p.out[(2 * e.rg + (lane >> 4)) * 8 + (lane & 7)] = silu_mul_h(v, up);
+    } else {
+        p.edge_out[e.dst * 32 + lane] = v;
+    }
+}
 
 __device__ __forceinline__ void mma_unit_smem(const uint8_t* unit, const uint32_t (&xb)[8], uint32_t lut_base,
                                               uint32_t laneword, int lane, int g, float (&acc)[2][4]) {
@@ -542,7 +670,13 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     const int stage_bytes = stage_units * UNIT_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     uint8_t* ring = smem_raw + LUT_BYTES + xs_bytes + size_t(warp) * NAT_STAGES * stage_bytes;
-    const int w = warp * int(gridDim.x) + int(blockIdx.x);
+    // EDGE (SiLU·mul with edge_out, M = 1, every warp active): the warps of a CTA take consecutive
+    // ranges, so most shared row groups are added in shared memory (edge_finish); otherwise warp w
+    // of the grid is warp w / G of CTA w % G
+    const bool edge = EPI == EPI_SILU_MUL && p.edge_out != nullptr;
+    float* edge_red = reinterpret_cast<float*>(smem_raw + LUT_BYTES + xs_bytes +
+                                               size_t(NAT_WARPS) * NAT_STAGES * stage_bytes);
+    const int w = edge ? int(blockIdx.x) * NAT_WARPS + warp : warp * int(gridDim.x) + int(blockIdx.x);
     const int W = p.total_warps;
     const bool active = w < W;
     const int64_t u_begin = active ? unit_begin(p.units, w, W) : 0;
@@ -567,6 +701,9 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     }
     const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);   // in flight with the LUT loads
     const SlotPlan sp = slot_plan(p, threadIdx.x);
+    EdgeRed er;
+    er.rg = -1;
+    if (EPI == EPI_SILU_MUL && edge) er = edge_red_plan(p, warp);
     build_lut<NAT_THREADS>(lut_s, p.lut);
     pdl_trigger();
     pdl_wait();
@@ -584,6 +721,17 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     int cur_rg = first_rg;
     int seg_b0 = int(u_begin - int64_t(first_rg) * p.KB);
     int rg = first_rg, b = seg_b0;   // (row group, block) of the next unit, advanced incrementally
+    // EDGE: this warp's sums of a row group it shares (rows 16 tile + g (+8), batch row 0)
+    auto keep = [&](int r) {
+        float* d = edge_red + (warp * 2 + (r == first_rg ? 0 : 1)) * 32;
+        if (t == 0) {
+            d[g] = acc[0][0];
+            d[8 + g] = acc[0][2];
+            d[16 + g] = acc[1][0];
+            d[24 + g] = acc[1][2];
+        }
+    };
+    bool ok = true;
 
     for (int c = 0; c < n_chunks; ++c) {
         const int stage = c % NAT_STAGES;
@@ -591,7 +739,8 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             // give the other copies in flight a bounded chance to land, then leave
             for (int c2 = c + 1; c2 < n_chunks && c2 < c + NAT_STAGES; ++c2)
                 mbar_wait(&bars[warp][c2 % NAT_STAGES], uint32_t((c2 / NAT_STAGES) & 1), err, 2);
-            return;
+            ok = false;
+            break;
         }
         const int64_t u0 = u_begin + int64_t(c) * stage_units;
         const int cnt = int(min(int64_t(stage_units), u_end - u0));
@@ -601,6 +750,8 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
                 if (seg_b0 == 0) {
                     epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
                     epilogue<EPI>(p, 2 * cur_rg + 1, acc[1], g, t);
+                } else if (edge) {
+                    keep(cur_rg);
                 } else {
                     flush_partial<EPI, 2>(p, cur_rg, acc, w, first_rg, lane, g, t);
                 }
@@ -633,15 +784,22 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             issue(c + NAT_STAGES);
         }
     }
-    if (u_end > u_begin) {
+    if (ok && u_end > u_begin) {
         if (seg_b0 == 0 && b == 0) {   // the range ended exactly at the end of cur_rg
             epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
             epilogue<EPI>(p, 2 * cur_rg + 1, acc[1], g, t);
+        } else if (edge) {
+            keep(cur_rg);
         } else {
             flush_partial<EPI, 2>(p, cur_rg, acc, w, first_rg, lane, g, t);
         }
     }
-    finish_launch<EPI>(p, lane);
+    if (EPI == EPI_SILU_MUL && edge) {   // every warp of the CTA is active (host-checked) and gets here
+        __syncthreads();
+        edge_finish(p, er, edge_red, lane);
+        return;
+    }
+    if (ok) finish_launch<EPI>(p, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -737,6 +895,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     }
     const uint4 wpre = norm_w_chunk<NAT_THREADS>(p);   // in flight with the LUT loads
     const SlotPlan sp = slot_plan(p, threadIdx.x);
+    const EdgePlan ep = edge_plan(p, threadIdx.x);
     build_lut<NAT_THREADS>(lut_s, p.lut);
     pdl_trigger();
     pdl_wait();
@@ -757,7 +916,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
             if (i < p.M * res_n) rv[u] = __ldcg(p.residual + (i / res_n) * p.res_stride + res_row0 + i % res_n);
         }
     }
-    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre, &sp);
+    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre, &sp, &ep);
     if (res_staged) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -2003,6 +2162,26 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
             return fail(NOVA_ERR_ALIGN, "add_slots and resid_out must be 16-byte aligned");
         if (a->resid_out == a->x) return fail(NOVA_ERR_INVALID, "resid_out must not alias x");
     }
+    const int64_t G_sm = sm_count();
+    if (a->edge_out) {   // SiLU·mul leaving the row groups split between CTAs as fp32 sums
+        const int64_t kb = k / 64, units = (n / UNIT_ROWS) * kb, per = (units + G_sm - 1) / G_sm;
+        if (epi != EPI_SILU_MUL || !native || m != 1 || units < int64_t(NAT_MIN_UNITS) * NAT_WARPS * G_sm ||
+            units / G_sm < 2 * kb || (per + kb - 1) / kb + 1 > NAT_WARPS ||
+            (units + 1) * NAT_WARPS * G_sm >= (1ll << 31))
+            return fail(NOVA_ERR_UNSUPPORTED, "edge_out needs SILU_MUL, the native layout, M = 1, at least %d units "
+                                              "per SM and 2 to %d row groups per SM",
+                        NAT_MIN_UNITS * NAT_WARPS, NAT_WARPS - 1);
+        if (reinterpret_cast<uintptr_t>(a->edge_out) % 16) return fail(NOVA_ERR_ALIGN, "edge_out must be 16-byte aligned");
+    }
+    if (a->edge_in) {   // x completed from a SiLU·mul launch's edges (its N = 2 * this K, its K = edge_k)
+        const int64_t kb = a->edge_k / 64, units = (2 * k / UNIT_ROWS) * kb;
+        if (!native || m != 1 || a->norm_weight || a->add_slots || a->edge_k <= 0 || a->edge_k % 64 ||
+            units < int64_t(NAT_MIN_UNITS) * NAT_WARPS * G_sm || units / G_sm < 2 * kb ||
+            2 * (G_sm - 1) > NAT_THREADS || units * G_sm >= (1ll << 31))
+            return fail(NOVA_ERR_UNSUPPORTED, "edge_in needs the native layout, M = 1, no norm prologue or add_slots, "
+                                              "and an edge_out producer of N = 2K, K = edge_k");
+        if (reinterpret_cast<uintptr_t>(a->edge_in) % 16) return fail(NOVA_ERR_ALIGN, "edge_in must be 16-byte aligned");
+    }
     if (epi == EPI_RESIDUAL && !a->residual) return fail(NOVA_ERR_INVALID, "residual epilogue needs residual");
     if (epi == EPI_ARGMAX && !a->argmax) return fail(NOVA_ERR_INVALID, "argmax epilogue needs argmax");
     if (epi != EPI_PLAIN && a->bias) return fail(NOVA_ERR_UNSUPPORTED, "bias only with the plain epilogue");
@@ -2058,6 +2237,13 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         p.add_G = sm_count();
         p.resid_out = (__half*)a->resid_out;
     }
+    p.edge_out = (float*)a->edge_out;
+    if (a->edge_in) {
+        p.edge_in = (const float*)a->edge_in;
+        p.edge_KB = int(a->edge_k / 64);
+        p.edge_units = int64_t(2 * k / UNIT_ROWS) * p.edge_KB;
+        p.edge_G = int(G_sm);
+    }
 
     using Kern = void (*)(Params);
     cudaError_t err;
@@ -2084,8 +2270,9 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         // leave less than 2 units per stage and there is no norm prologue.
         const int64_t ring_unit = int64_t(NAT_WARPS) * NAT_STAGES * UNIT_BYTES;
         const int64_t slack = 1024;   // static shared memory
+        const int64_t edge_bytes = a->edge_out ? EDGE_RED_BYTES : 0;   // after the rings
         auto units_for = [&](int64_t xs_bytes) {
-            return std::min<int64_t>(4, (optin - int64_t(LUT_BYTES) - xs_bytes - slack) / ring_unit);
+            return std::min<int64_t>(4, (optin - int64_t(LUT_BYTES) - xs_bytes - edge_bytes - slack) / ring_unit);
         };
         int64_t xs_bytes = (m * k * 2 + 127) / 128 * 128;
         int64_t stage_units = units_for(xs_bytes);
@@ -2104,13 +2291,17 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         // lm_head: with several row groups per CTA the CTA-level schedule
         // would synchronise its 16 warps once per row group); CTA-level
         // split-K on whole row groups below that (no cross-CTA reduction).
-        const bool warp_level =
-            epi != EPI_SLOTS && ((launch_flags() & 2) || n / UNIT_ROWS >= 2 * int64_t(sm_count()));
+        const bool warp_level = a->edge_out || (epi != EPI_SLOTS && ((launch_flags() & 2) ||
+                                                                      n / UNIT_ROWS >= 2 * int64_t(sm_count())));
+        if (a->edge_in && (warp_level || xg))
+            return fail(NOVA_ERR_UNSUPPORTED, "edge_in needs the CTA-level schedule with x staged (SLOTS or fewer "
+                                              "than two row groups per SM)");
         if (warp_level) {
             NKern kern = kernels[xg][epi];
-            const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + stage_units * ring_unit;
+            const int64_t nsmem = int64_t(LUT_BYTES) + xs_bytes + stage_units * ring_unit + edge_bytes;
             if (int rc = prepare_smem(kern, nsmem, smem_set[xg][epi])) return rc;
             const int64_t want = (p.units + NAT_MIN_UNITS - 1) / NAT_MIN_UNITS;
+            // edge_out: every warp of every CTA active (checked above: want >= SMs x 16)
             p.total_warps = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sm_count()) * NAT_WARPS, want)));
             const unsigned grid = unsigned(std::min<int64_t>(sm_count(), p.total_warps));
             err = launch(kern, dim3(grid), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p, int(stage_units),

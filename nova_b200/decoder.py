@@ -49,7 +49,7 @@ import torch
 
 from . import _lib
 from .kernels import (build_nf4_lut, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native, pack_tc,
-                      slots_buffer)
+                      slots_buffer, edge_buffer)
 from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk, prefill_attention
 from .quant import nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
@@ -288,6 +288,9 @@ class NovaDecoder:
         self.deferred = self.batch == 1 and not self.tp.active and self._deferred_fits()
         self.slots = slots_buffer(self.device) if self.deferred else None
         self.resid_alt = torch.zeros_like(self.resid) if self.deferred else None
+        # with the deferred reductions, gate|up also leaves the row groups split between its CTAs as fp32
+        # sums (edge_out) that down_proj completes while staging its input: no cross-CTA reduction
+        self.edges = edge_buffer(self.device) if self.deferred and self._edges_fit() else None
         self._staged = None   # fp16 K/V per layer of the positions prefilled / injected since the last reset
 
     def _deferred_fits(self) -> bool:
@@ -304,6 +307,16 @@ class NovaDecoder:
             if k % 64 or (kb - 1) * sms // units + 2 > 4 or (units + kb) * sms >= 2 ** 31:
                 return False
         return True
+
+    def _edges_fit(self) -> bool:
+        """gate|up's edge_out limits (nova_nf4_gemv): every warp of every SM
+        busy (8 units each at least), 2 to 15 row groups per SM."""
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        kb = self.cfg.hidden_size // 64
+        units = (2 * self.inter // 32) * kb
+        per = -(-units // sms)
+        return (units >= 8 * 16 * sms and units // sms >= 2 * kb and -(-per // kb) + 1 <= 16
+                and 2 * (sms - 1) <= 512 and (units + 1) * 16 * sms < 2 ** 31)
 
     def _pick_chunk(self) -> int:
         """Split size for the attention (``kvattn.pick_chunk``)."""
@@ -617,7 +630,8 @@ class NovaDecoder:
     # ---------------------------------------------------------------- decode
 
     def _gemv(self, x, w: NF4Weight, out, *, epilogue: int = _lib.NF4_PLAIN, norm_weight=None, residual=None,
-              argmax=None, token_out=None, pos=None, embed=None, embed_out=None, add=None, resid_out=None) -> None:
+              argmax=None, token_out=None, pos=None, embed=None, embed_out=None, add=None, resid_out=None,
+              edge_out=None, edge_in=None) -> None:
         """The step's NF4 projection: nova_nf4_gemv up to GEMV_ROWS rows, else
         nova_nf4_gemm (after nova_rmsnorm when the projection has a norm prologue)."""
         B = x.shape[0]
@@ -641,7 +655,8 @@ class NovaDecoder:
                      token_out=None if token_out is None else token_out[sl], pos=pos if last else None,
                      embed=embed, embed_out=None if embed_out is None else embed_out[sl],
                      workspace=self.gemv_ws, n=w.n, add_slots=None if add is None else add[0],
-                     add_k=0 if add is None else add[1], resid_out=resid_out)
+                     add_k=0 if add is None else add[1], resid_out=resid_out, edge_out=edge_out,
+                     edge_in=None if edge_in is None else edge_in[0], edge_k=0 if edge_in is None else edge_in[1])
 
     def _qk_args(self, li: int, lw) -> "_lib.QKArgs":
         cfg, cache = self.cfg, self.cache
@@ -722,9 +737,11 @@ class NovaDecoder:
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
                              n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window, qk=qa)
             self._gemv(self.attn, lw.o, slots, epilogue=_lib.NF4_SLOTS)
+            edges = self.edges
             self._gemv(r0, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln,
-                       add=(slots, self.q_dim), resid_out=r1)
-            self._gemv(self.act, lw.down, slots, epilogue=_lib.NF4_SLOTS)
+                       add=(slots, self.q_dim), resid_out=r1, edge_out=edges)
+            self._gemv(self.act, lw.down, slots, epilogue=_lib.NF4_SLOTS,
+                       edge_in=None if edges is None else (edges, cfg.hidden_size))
         self._gemv(r1, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,
                    argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
                    embed_out=r0, add=(slots, self.inter))

@@ -131,7 +131,8 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
              embed: torch.Tensor | None = None, embed_out: torch.Tensor | None = None,
              workspace: torch.Tensor | None = None, n: int | None = None,
              add_slots: torch.Tensor | None = None, add_k: int = 0,
-             resid_out: torch.Tensor | None = None) -> torch.Tensor:
+             resid_out: torch.Tensor | None = None, edge_out: torch.Tensor | None = None,
+             edge_in: torch.Tensor | None = None, edge_k: int = 0) -> torch.Tensor:
     """Launch ``nova_nf4_gemv`` on 2-D views (x ``[M, K]``, out ``[M, N or N/2]``).
 
     Reference layout: ``packed`` uint8 ``[N, K/2]`` with ``absmax``
@@ -140,7 +141,12 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
     ``epilogue=NF4_SLOTS``: out is a :func:`slots_buffer` that receives each
     CTA's fp32 sums; a following launch with ``add_slots`` (that buffer) and
     ``add_k`` (the slot launch's K) adds them to its input x (fp16 residual
-    add) before its norm prologue and stores the sum to ``resid_out``."""
+    add) before its norm prologue and stores the sum to ``resid_out``.
+    ``edge_out`` (an :func:`edge_buffer`, with ``NF4_SILU_MUL`` at M = 1): the
+    row groups split between CTAs are left there as fp32 sums instead of being
+    reduced across CTAs, so ``out`` is incomplete until a following launch with
+    ``edge_in`` (that buffer) and ``edge_k`` (this launch's K) completes them
+    while it stages x (its K = this launch's N / 2)."""
     m, k = x.shape
     native = absmax is None
     if native:
@@ -177,6 +183,9 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
     a.m, a.n, a.k, a.epilogue = m, n, k, int(epilogue)
     if add_slots is not None:
         a.add_slots, a.add_k, a.resid_out = add_slots.data_ptr(), int(add_k), _lib.ptr(resid_out)
+    a.edge_out = _lib.ptr(edge_out)
+    if edge_in is not None:
+        a.edge_in, a.edge_k = edge_in.data_ptr(), int(edge_k)
     _lib.check(_lib.lib().nova_nf4_gemv(_lib.ctypes.byref(a), _lib.stream_of(x.device)), "nova_nf4_gemv")
     return out
 
@@ -187,6 +196,13 @@ def slots_buffer(device: torch.device) -> torch.Tensor:
     rows)."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     return torch.zeros(sms * 4 * 8, 32, dtype=torch.float32, device=device)
+
+
+def edge_buffer(device: torch.device) -> torch.Tensor:
+    """fp32 ``[SMs * 2, 32]`` buffer for ``edge_out`` / ``edge_in`` (per CTA
+    the sums of its first and last row group, batch row 0)."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    return torch.zeros(sms * 2, 32, dtype=torch.float32, device=device)
 
 
 def gemm_workspace(device: torch.device, n: int, k: int) -> torch.Tensor:

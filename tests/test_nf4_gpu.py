@@ -66,6 +66,28 @@ def _check(got, want32, tag):
     assert np.abs(got - want32).max() <= 1e-2 * scale, f"{tag}: beyond 1e-2 relative"
 
 
+def _assert_silu(got, g32, u32, tag):
+    """SiLU·mul outputs against the oracle.  gate and up are rounded to fp16
+    before SiLU*up, and each may sit one ulp (or, where the dot product cancels,
+    1e-5 * max|y|: the GEMV criterion) away from the oracle's; SiLU amplifies
+    that by up to |g| where it is flat.  Bound: the oracle evaluated at gate/up
+    moved by that much either way, plus 2 ulp; over 99 % exact."""
+    g16, u16 = g32.astype(np.float16), u32.astype(np.float16)
+    want = onorm.silu_mul(g16, u16).astype(np.float32)
+    eg = np.maximum(fp16_ulp(g16), 1e-5 * np.abs(g32).max())
+    eu = np.maximum(fp16_ulp(u16), 1e-5 * np.abs(u32).max())
+    dev = np.zeros_like(want)
+    for dg in (-1, 0, 1):
+        for du in (-1, 0, 1):
+            gg = g16.astype(np.float32) + dg * eg
+            uu = u16.astype(np.float32) + du * eu
+            alt = gg / (1.0 + np.exp(-gg)) * uu
+            dev = np.maximum(dev, np.abs(alt - want))
+    assert np.all(np.abs(got - want) <= dev + 2 * fp16_ulp(want)), tag
+    assert (got == want).mean() > 0.99, f"{tag}: too few exact"
+    return want
+
+
 def test_codebook_matches_oracle(cuda_lib):
     from nova_b200.quant import nf4_codebook
 
@@ -358,23 +380,7 @@ def test_native_split_k_variants(cuda_lib, variant, n, k, epi):
         bound = fp16_ulp(y) + fp16_ulp(want) + 1e-5 * np.abs(y).max()
         assert np.all(np.abs(got - want.astype(np.float32)) <= bound), variant
     else:
-        # gate and up are rounded to fp16 before SiLU*up, and each may sit one ulp (or, where the dot product
-        # cancels, 1e-5 * max|y|: the GEMV criterion) away from the oracle's; SiLU amplifies that by up to |g|
-        # where it is flat.  Bound: the oracle evaluated at gate/up moved by that much either way.
-        g32, u32 = _oracle_y(x, gp, ga), _oracle_y(x, up, ua)
-        g16, u16 = g32.astype(np.float16), u32.astype(np.float16)
-        want = onorm.silu_mul(g16, u16).astype(np.float32)
-        eg = np.maximum(fp16_ulp(g16), 1e-5 * np.abs(g32).max())
-        eu = np.maximum(fp16_ulp(u16), 1e-5 * np.abs(u32).max())
-        dev = np.zeros_like(want)
-        for dg in (-1, 0, 1):
-            for du in (-1, 0, 1):
-                gg = g16.astype(np.float32) + dg * eg
-                uu = u16.astype(np.float32) + du * eu
-                alt = gg / (1.0 + np.exp(-gg)) * uu
-                dev = np.maximum(dev, np.abs(alt - want))
-        assert np.all(np.abs(got - want) <= dev + 2 * fp16_ulp(want)), f"silu {variant}"
-        assert (got == want).mean() > 0.99, f"silu {variant}: too few exact"
+        _assert_silu(got, _oracle_y(x, gp, ga), _oracle_y(x, up, ua), f"silu {variant}")
 
 
 @pytest.mark.parametrize("n_prev,k_prev", [(2560, 4096), (2560, 9728)])
@@ -410,3 +416,76 @@ def test_slot_epilogue_and_deferred_residual_add(cuda_lib, n_prev, k_prev):
         assert np.all(np.abs(got_res - w16.astype(np.float32)) <= ulp), "deferred residual add"
         xn = onorm.rms_norm(resid_out.cpu().numpy(), w.numpy(), 1e-6)
         _check(out, _oracle_y(torch.from_numpy(xn), qp, qa), "projection after the deferred add")
+
+
+def test_gate_up_edges_completed_by_down(cuda_lib):
+    """gate|up (19456 x 2560, SiLU·mul) with edge_out: the row groups split
+    between its CTAs stay fp32 sums, and down_proj (2560 x 9728) with edge_in
+    completes them while staging its input.  The edge sums plus the written
+    outputs give the activation within the SiLU·mul bound of the oracle (the
+    edges are added in CTA order on the host the way the consumer does), and the
+    down projection matches the oracle over that completed activation; run
+    twice (no state left behind)."""
+    from nova_b200 import _lib
+    from nova_b200.decoder import interleave_gate_up
+    from nova_b200.kernels import edge_buffer, gemv_workspace, nf4_gemv, pack_native
+
+    hidden, inter = 2560, 9728
+    _, gp, ga = _weights(inter, hidden, 31)
+    _, upk, ua = _weights(inter, hidden, 32)
+    _, dp, da = _weights(hidden, inter, 33)
+    packed, absmax = interleave_gate_up(gp, ga, upk, ua)
+    gu, dn = pack_native(packed, absmax), pack_native(dp, da)
+    x = torch.randn(1, hidden, generator=torch.Generator().manual_seed(34)).half()
+    lut = _lut()
+    ws = gemv_workspace(torch.device("cuda"), 2 * inter)
+    edges = edge_buffer(torch.device("cuda"))
+    g32, u32 = _oracle_y(x, gp, ga), _oracle_y(x, upk, ua)
+
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    kb = hidden // 64
+    units = (2 * inter // 32) * kb
+    gate_ix = [0, 1, 2, 3, 4, 5, 6, 7, 16, 17, 18, 19, 20, 21, 22, 23]
+    up_ix = [8, 9, 10, 11, 12, 13, 14, 15, 24, 25, 26, 27, 28, 29, 30, 31]
+    for _ in range(2):
+        edges.fill_(float("nan"))
+        h = torch.full((1, inter), float("nan"), dtype=torch.float16, device="cuda")
+        nf4_gemv(x.cuda(), gu, None, lut, h, epilogue=_lib.NF4_SILU_MUL, workspace=ws, n=2 * inter, edge_out=edges)
+        y = torch.empty(1, hidden, dtype=torch.float16, device="cuda")
+        nf4_gemv(h, dn, None, lut, y, workspace=ws, n=hidden, edge_in=edges, edge_k=hidden)
+        got_h = h.float().cpu().numpy()[0].copy()
+        e = edges.cpu().numpy()
+        split = np.zeros(inter, dtype=bool)
+        for bnd in range(1, sms):
+            u = units * bnd // sms
+            if u % kb == 0:
+                continue
+            rg = u // kb
+            a, b = e[2 * (bnd - 1) + 1], e[2 * bnd]
+            gs, us = a[gate_ix] + b[gate_ix], a[up_ix] + b[up_ix]
+            got_h[16 * rg:16 * rg + 16] = onorm.silu_mul(gs.astype(np.float16), us.astype(np.float16))
+            split[16 * rg:16 * rg + 16] = True
+        assert split.sum() > 100 * 16, "expected row groups split between CTAs"
+        assert not np.isnan(got_h).any(), "an activation was neither written nor left as an edge"
+        _assert_silu(got_h, g32[0], u32[0], "silu_mul with edges")
+        # down over the activation the launches produced (completed by the consumer as on the host)
+        _check(y, _oracle_y(torch.from_numpy(got_h[None].astype(np.float32)), dp, da), "down_proj completing the edges")
+
+
+def test_edges_rejected_outside_their_shapes(cuda_lib):
+    from nova_b200 import _lib
+    from nova_b200.kernels import edge_buffer, gemv_workspace, nf4_gemv, pack_native
+
+    _, p, a = _weights(4096, 2560, 41)
+    units = pack_native(p, a)
+    x = torch.zeros(1, 2560, dtype=torch.float16, device="cuda")
+    out = torch.empty(1, 4096, dtype=torch.float16, device="cuda")
+    edges = edge_buffer(torch.device("cuda"))
+    ws = gemv_workspace(torch.device("cuda"), 4096)
+    with pytest.raises(ValueError, match="edge_out"):   # not SiLU·mul
+        nf4_gemv(x, units, None, _lut(), out, workspace=ws, n=4096, edge_out=edges)
+    with pytest.raises(ValueError, match="edge_out"):   # SiLU·mul, but too few units for every warp
+        nf4_gemv(x, units, None, _lut(), out[:, :2048], epilogue=_lib.NF4_SILU_MUL, workspace=ws, n=4096,
+                 edge_out=edges)
+    with pytest.raises(ValueError, match="edge_in"):   # with a norm prologue
+        nf4_gemv(x, units, None, _lut(), out, workspace=ws, n=4096, norm_weight=x[0], edge_in=edges, edge_k=2560)
