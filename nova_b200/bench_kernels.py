@@ -23,7 +23,8 @@ import torch
 
 from . import _lib
 from .decoder import interleave_gate_up
-from .kernels import build_nf4_lut, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native, pack_tc
+from .kernels import (build_nf4_lut, edge_buffer, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native,
+                      pack_tc)
 from .kvattn import GROUP_T, launch_attention, new_workspace, pick_chunk
 from .quant import nf4_codebook, quantize_nf4
 
@@ -55,7 +56,7 @@ def _graph_time(fn, sets: int, iters: int) -> float:
 
 
 def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool = False, sets: int = 0,
-               iters: int = 20, seed: int = 0, layout: str = "native") -> dict:
+               iters: int = 20, seed: int = 0, layout: str = "native", edges: bool = False) -> dict:
     dev = torch.device("cuda")
     code = nf4_codebook()
     lut = build_nf4_lut(code).to(dev)
@@ -83,6 +84,8 @@ def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool =
         kw["residual"] = out
     if epilogue == "argmax":
         kw["argmax"] = torch.zeros(m, dtype=torch.int64, device=dev)
+    if edges:   # SiLU·mul leaving its CTA-edge row groups as fp32 sums (the batch-1 decode's gate|up)
+        kw["edge_out"] = edge_buffer(dev)
 
     def fn(i):
         p, a = weights[i]
@@ -90,7 +93,7 @@ def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool =
 
     us = _graph_time(fn, sets, iters)
     return {"kernel": "nf4_gemv", "layout": layout, "n": n, "k": k, "m": m, "epilogue": epilogue, "norm": norm,
-            "sets": sets, "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+            "edges": edges, "sets": sets, "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
 
 
 def bench_gemm(n: int, k: int, m: int = 64, epilogue: str = "plain", sets: int = 0, iters: int = 20,
@@ -309,6 +312,7 @@ def main() -> None:
     a.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
     a.add_argument("--variant", choices=["cta", "warp"], default="cta",
                    help="native GEMV split-K at CTA level (default) or warp level")
+    a.add_argument("--edges", action="store_true", help="SiLU·mul at M = 1 with CTA edges (edge_out)")
     c = sub.add_parser("gemm")
     c.add_argument("--n", type=int, required=True)
     c.add_argument("--k", type=int, required=True)
@@ -337,7 +341,7 @@ def main() -> None:
         _lib.set_launch_flags((_lib.LAUNCH_PDL if args.pdl else 0) |
                               (_lib.LAUNCH_WARP_SPLITK if args.variant == "warp" else 0))
         print(json.dumps(bench_gemv(args.n, args.k, args.m, args.epilogue, args.norm, args.sets, args.iters,
-                                    layout=args.layout)))
+                                    layout=args.layout, edges=args.edges)))
     elif args.cmd == "gemm":
         _lib.set_launch_flags(_lib.LAUNCH_PDL)
         print(json.dumps(bench_gemm(args.n, args.k, args.m, args.epilogue, args.sets, args.iters)))
