@@ -402,7 +402,11 @@ NOVA_API int nova_qk_norm_rope_append(const nova_qk_args* args, void* stream);
  * max_len; attn needs the ring (tail_k/tail_v) and n_splits >= 1.  When the
  * new token completes a 64-token group, the group is requantized into the
  * cache and attended in its int8 form, as after the two separate calls.
- * qk->q_out is not written.  With programmatic dependent launch on, the first
+ * qk->q_out is not written.  Without a window-relative layout, attn->chunk is
+ * an upper bound here: the launch splits the prefix it attends into the
+ * smallest multiple of 256 tokens that covers it with attn->n_splits splits
+ * (at most chunk), so a cache filled far below max_len still gives each warp
+ * one 64-token group per split.  With programmatic dependent launch on, the first
  * groups of the int8 prefix are requested before the kernel launched just
  * before this call has finished: that kernel must not write the int8 cache
  * (in the decode step it is the q|k|v projection).

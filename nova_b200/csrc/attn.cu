@@ -383,11 +383,28 @@ __global__ void __launch_bounds__(THREADS, 3)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
     }
+    // Split size.  The host's chunk covers the whole capacity with the launched splits; the fused decode
+    // step (absolute splits) uses the smallest multiple of one group per warp that covers the current
+    // prefix instead, at most that chunk, so a cache filled far below its capacity still gives every
+    // warp one group per split rather than several in a row.
+    auto chunk_for = [&](int64_t pend_) -> int64_t {
+        if (!FUSED || p.win_rel) return p.chunk;
+        const int64_t step = int64_t(GT) * NW;
+        int64_t c = (max(pend_, int64_t(1)) + p.n_splits - 1) / p.n_splits;
+        c = (c + step - 1) / step * step;
+        return c < p.chunk ? c : int64_t(p.chunk);
+    };
+    int64_t chunk = p.chunk;
     // The group this warp takes first when no prefix is masked (every group
     // of the chunk lies inside the cache allocation, so a copy is in bounds).
-    const int spec = int(int64_t(split) * p.chunk / GT) + warp;
-    const bool spec_on = !p.win_rel && split < p.n_splits && spec < p.groups &&
-                         int64_t(spec) * GT < int64_t(split) * p.chunk + p.chunk;
+    int spec = 0;
+    bool spec_on = false;
+    auto set_spec = [&]() {
+        spec = int(int64_t(split) * chunk / GT) + warp;
+        spec_on = !p.win_rel && split < p.n_splits && spec < p.groups &&
+                  int64_t(spec) * GT < int64_t(split) * chunk + chunk;
+    };
+    if (!FUSED) set_spec();
     __half nwq = __float2half_rn(0.f), nwk = __float2half_rn(0.f);
     uint8_t* stage = smem + warp * STAGE;
     uint64_t* bar_k = &bars[0][warp];
@@ -416,6 +433,12 @@ __global__ void __launch_bounds__(THREADS, 3)
         nwq = p.q_norm_w[threadIdx.x];
         if (is_tail) nwk = p.k_norm_w[threadIdx.x];
         pos_hint = *reinterpret_cast<const volatile int64_t*>(p.pos);
+        {   // the prefix this step will attend if the position is still pos_hint
+            const int64_t ql = (pos_hint + 1) / GT * GT;
+            const bool rq = pos_hint >= 0 && pos_hint < p.max_len && pos_hint % GT == GT - 1;
+            chunk = chunk_for(min(rq ? ql - GT : ql, int64_t(p.max_len)));
+            set_spec();
+        }
         const int64_t cp = pos_hint < 0 ? 0 : (pos_hint < p.rope_len ? pos_hint : p.rope_len - 1);
         cos_hint = __half2float(p.cos[cp * D + threadIdx.x]);
         sin_hint = __half2float(p.sin[cp * D + threadIdx.x]);
@@ -462,6 +485,7 @@ __global__ void __launch_bounds__(THREADS, 3)
     int64_t lo = first > 0 ? first : 0;
     if (p.window > 0) lo = max(lo, u - p.window + 1);
     const int64_t pend = min(min(requant ? qlen - GT : qlen, pgv * GT), int64_t(p.max_len));
+    chunk = chunk_for(pend);   // FUSED: from the real position (a different spec group is drained and reloaded)
 
     // Q^T B-fragments: column g carries head g>>1; dims 32t..32t+31.
     uint32_t qf[16];
@@ -558,9 +582,9 @@ __global__ void __launch_bounds__(THREADS, 3)
 
     if (split < p.n_splits) {
         // window-relative splits start at the window's first group (known only after the lengths are read)
-        const int64_t s0 = (p.win_rel ? lo / GT * GT : int64_t(0)) + int64_t(split) * p.chunk;
+        const int64_t s0 = (p.win_rel ? lo / GT * GT : int64_t(0)) + int64_t(split) * chunk;
         const int64_t t_begin = max(s0, lo);
-        const int64_t t_end = min(s0 + p.chunk, pend);
+        const int64_t t_end = min(s0 + chunk, pend);
         if (t_begin < t_end) {
             const int g_first = int(t_begin / GT), g_last = int((t_end - 1) / GT);
             int gi = g_first + warp;

@@ -5,7 +5,10 @@ The ring, the int8 cache and the lengths must come out bit-identical; the
 attention output within the attention criterion of tests/test_attn_gpu.py
 (2 fp16 ULP or 1e-5): when a token completes a group, the fused launch attends
 that group in its int8 form from the ring CTA instead of a prefix split, so
-the split partials are merged in another order."""
+the split partials are merged in another order.  With a capacity far above
+the prefix the fused launch also lays its splits over the prefix (256-token
+splits instead of the host's chunk), so the partials differ and only the
+elementwise criterion applies."""
 
 from __future__ import annotations
 
@@ -55,15 +58,17 @@ def _state(cache):
                                       cache._pg)]
 
 
-@pytest.mark.parametrize("b,hq,hkv,window,chunk,start,steps", [
-    (2, 32, 8, 0, 64, 0, 140),       # two group completions (positions 63 and 127), small splits
-    (1, 32, 8, 100, 128, 180, 90),   # sliding window across the completion at 255
-    (3, 16, 8, 0, 256, 250, 20),     # gq = 2, completion at 255 inside a larger split
+@pytest.mark.parametrize("b,hq,hkv,window,chunk,start,steps,max_len", [
+    (2, 32, 8, 0, 64, 0, 140, 512),       # two group completions (positions 63 and 127), small splits
+    (1, 32, 8, 100, 128, 180, 90, 512),   # sliding window across the completion at 255
+    (3, 16, 8, 0, 256, 250, 20, 512),     # gq = 2, completion at 255 inside a larger split
+    # capacity far above the prefix: the fused launch splits the prefix into 256-token splits
+    # (not the host's 1024), across the completions at 703 and 767
+    (1, 32, 8, 0, 1024, 690, 90, 4096),
 ])
-def test_fused_append_attention_matches_two_launches(cuda_lib, b, hq, hkv, window, chunk, start, steps):
+def test_fused_append_attention_matches_two_launches(cuda_lib, b, hq, hkv, window, chunk, start, steps, max_len):
     from nova_b200.kvattn import KVInt8Cache
 
-    max_len = 512
     g = torch.Generator().manual_seed(11 + b)
     cos_np, sin_np = onorm.rope_cos_sin(np.arange(max_len + 1))
     cos, sin = torch.from_numpy(cos_np).cuda(), torch.from_numpy(sin_np).cuda()
@@ -103,7 +108,8 @@ def test_fused_append_attention_matches_two_launches(cuda_lib, b, hq, hkv, windo
         for i, (x, y) in enumerate(zip(_state(sep), _state(fus))):
             np.testing.assert_array_equal(x, y, err_msg=f"state {i} at pos {pos}")
         st = assert_ulp_or_abs(outs[1].cpu().numpy(), outs[0].cpu().numpy(), 2.0, 1e-5, f"out pos={pos}")
-        assert st["max_ulp"] <= 2.0 or st["max_abs"] <= 1e-5
+        if max_len == 512:   # same split layout on both paths: every element within 2 ULP, or all within 1e-5
+            assert st["max_ulp"] <= 2.0 or st["max_abs"] <= 1e-5
         completions += pos % 64 == 63
     assert completions >= 1
 
