@@ -24,6 +24,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -81,23 +82,56 @@ class ClockSampler:
     def __init__(self, gpu_index: int) -> None:
         self.gpu = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, str]] = []   # (host time, csv line)
+        self.t_begin = self.t_end = None
+        self._reader = None
 
     def start(self) -> None:
+        """Start nvidia-smi (every 20 ms) and return once its first sample
+        arrived (its start-up can take longer than a short timed region)."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+
+        def read() -> None:
+            for line in self.proc.stdout:
+                if line.strip():
+                    self.samples.append((time.monotonic(), line.strip()))
+
+        self._reader = threading.Thread(target=read, daemon=True)
+        self._reader.start()
+        t0 = time.monotonic()
+        while not self.samples and time.monotonic() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.005)
+
+    def mark_begin(self) -> None:
+        self.t_begin = time.monotonic()
+
+    def mark_end(self) -> None:
+        self.t_end = time.monotonic()
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        time.sleep(0.05)
+        t0 = time.monotonic()   # one more sample after the timed region (the last one may straddle its end)
+        while time.monotonic() - t0 < 0.5 and not any(t > (self.t_end or 0.0) for t, _ in self.samples):
+            time.sleep(0.005)
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
-        rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._reader is not None:
+            self._reader.join(timeout=5)
+        lines = self.samples
+        if self.t_begin is not None and self.t_end is not None:   # the samples taken while the steps ran
+            inside = [x for x in lines if self.t_begin - 0.005 <= x[0] <= self.t_end + 0.025]
+            lines = inside or lines
+        rows = [r.split(", ") for _, r in lines]
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
         smax = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -420,10 +454,10 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank)
     clocks.start()
-    time.sleep(0.1)
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    clocks.mark_begin()
     torch.cuda.nvtx.range_push("timed_steps")   # lets ncu select the timed launches (--nvtx-include timed_steps/)
     e0.record(stream)
     for _ in range(args.steps):
@@ -431,6 +465,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     e1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
+    clocks.mark_end()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
