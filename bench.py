@@ -221,11 +221,16 @@ def _time_kernels(dec, reps: int = 10) -> dict:
         edges = dec.edges.clone()
         gate_up_add["edge_out"] = edges
         down_edges = {"edge_in": (edges, dec.cfg.hidden_size)}
+    o_fn = lambda lw: row_par(scratch["attn"], lw.o)
+    if dec.heads:   # o_proj over the attention's split partials (those the last step left), per-head sums
+        o_fn = lambda lw: dec._o_heads(layer_index[id(lw)])
+        gate_up_add.pop("add", None)
+        gate_up_add["add_heads"] = dec.y_heads
     fams = {
         # the step's q|k|v launch (with q/k norm + RoPE + ring write; pos does not move, so the same ring slot
         # is rewritten)
         "qkv": (lambda lw: dec._qkv_step(layer_index[id(lw)], lw), lambda lw: bytes_of(lw.qkv)),
-        "o_proj": (lambda lw: row_par(scratch["attn"], lw.o), lambda lw: bytes_of(lw.o)),
+        "o_proj": (o_fn, lambda lw: bytes_of(lw.o)),
         "gate_up": (lambda lw: dec._gemv(scratch["resid"], lw.gate_up, scratch["act"], epilogue=_lib.NF4_SILU_MUL,
                                          norm_weight=lw.post_ln, **gate_up_add),
                     lambda lw: bytes_of(lw.gate_up)),

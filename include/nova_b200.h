@@ -144,6 +144,13 @@ typedef struct nova_attn_int8_args {
     void* workspace;        /* nova_attn_workspace_bytes() bytes, zeroed once  */
     int64_t workspace_bytes;
     int64_t batch, q_heads, kv_heads, max_len, groups, head_dim, group, chunk, n_splits, window;
+    /* nova_qk_append_attn_int8 only (ignored elsewhere): non-zero leaves the
+       split partials in the workspace for nova_nf4_gemv's attn_part (batch-1
+       decode) and writes neither out nor lse.  Partials: floats from byte
+       256 + align_up(batch * kv_heads * 4, 256), [batch * kv_heads][n_splits
+       + 1][q_heads / kv_heads][132] = m, l, 2 unused, acc[128] (m = -inf:
+       nothing valid in that split, acc not written).                        */
+    int64_t defer_merge;
 } nova_attn_int8_args;
 
 /* Bytes of workspace nova_attn_decode_int8 needs (split partials, per-head
@@ -277,6 +284,21 @@ typedef struct nova_nf4_args {
     void* edge_out;
     const void* edge_in;
     int64_t edge_k;
+    /* o_proj over the decode attention's split partials (batch-1 decode): with
+       attn_part (the partials nova_qk_append_attn_int8 left with defer_merge),
+       attn_splits (its n_splits + 1) and attn_heads (its kv_heads), an
+       NF4_F32 launch at M = 1 takes the head-major unit stream of o_proj (the
+       [N, attn_heads * K] matrix with each head's K-column block as rows
+       h * N / attn_heads ..: n = attn_heads * N rows, k = the 128 * q_heads /
+       kv_heads columns of one head), merges each head's x from the partials
+       with the attention's merge arithmetic, and writes fp32 out[h][N] per
+       head (x is not read).  add_heads / add_nheads: a launch with a norm
+       prologue first adds fp16(sum over h of add_heads[h][0..k)) to x (head
+       order), as add_slots does; CTA 0 stores the result to resid_out.      */
+    const void* attn_part;
+    int64_t attn_splits, attn_heads;
+    const void* add_heads;
+    int64_t add_nheads;
 } nova_nf4_args;
 
 NOVA_API int nova_nf4_gemv(const nova_nf4_args* args, void* stream);

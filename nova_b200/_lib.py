@@ -36,6 +36,7 @@ class AttnArgs(ctypes.Structure):
         ("workspace", _P), ("workspace_bytes", _I),
         ("batch", _I), ("q_heads", _I), ("kv_heads", _I), ("max_len", _I), ("groups", _I),
         ("head_dim", _I), ("group", _I), ("chunk", _I), ("n_splits", _I), ("window", _I),
+        ("defer_merge", _I),
     ]
 
 
@@ -51,6 +52,7 @@ class NF4Args(ctypes.Structure):
         ("m", _I), ("n", _I), ("k", _I), ("epilogue", _I), ("layout", _I),
         ("add_slots", _P), ("add_k", _I), ("resid_out", _P),
         ("edge_out", _P), ("edge_in", _P), ("edge_k", _I),
+        ("attn_part", _P), ("attn_splits", _I), ("attn_heads", _I), ("add_heads", _P), ("add_nheads", _I),
     ]
 
 

@@ -71,6 +71,7 @@ struct Params {
     float* part;
     int kv_heads, gq, max_len, groups, chunk, n_splits, s_total, window;
     int prefetch_first;       // one-wave launches: each warp's first group is prefetched into L2 before the wait
+    int defer_merge;          // FUSED: leave the split partials to the next kernel (no counters, no merge, no out)
     int win_rel;              // window > 0: split s covers [base + s*chunk, ...), base = the window's first group
     float scale_log2;
     // Fused q/k norm + RoPE + ring append (the FUSED kernel only; the
@@ -690,6 +691,7 @@ __global__ void __launch_bounds__(THREADS, 3)
         }
         if (M != -INFINITY) *reinterpret_cast<float4*>(dst + 4 + d0) = o;
     }
+    if (FUSED && p.defer_merge) return;   // complete for the next kernel once this launch has finished
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -905,6 +907,7 @@ static int attn_launch(const nova_attn_int8_args* a, const nova_qk_args* qk, voi
     p.chunk = int(a->chunk);
     p.n_splits = int(a->n_splits);
     p.s_total = int(s_total);
+    p.defer_merge = (qk && a->defer_merge) ? 1 : 0;
     p.window = int(std::min<int64_t>(a->window, 0x7fffffff));
     p.scale_log2 = float(1.0 / sqrt(double(D))) * LOG2E;
     p.kq = (const uint8_t*)a->kq;

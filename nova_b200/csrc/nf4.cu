@@ -87,6 +87,14 @@ struct Params {
     const float* edge_in = nullptr;
     int64_t edge_units = 0;
     int edge_G = 0, edge_KB = 0;
+    // o_proj over the decode attention's split partials (EPI_F32, M = 1): the rows are (KV head, output
+    // row) pairs of one head's K-column block (the head-major unit stream), each CTA owns whole row groups
+    // of one head and merges that head's partials ([heads][splits][K / 128][132] floats) into x
+    const float* mrg_part = nullptr;
+    int mrg_splits = 0, mrg_heads = 0;
+    // x += fp16(sum of the add_nheads fp32 rows add_heads[h][K] in head order) before the norm prologue
+    const float* add_heads = nullptr;
+    int add_nheads = 0;
 };
 
 template <typename T>
@@ -279,11 +287,14 @@ __device__ __forceinline__ SlotPlan slot_plan(const Params& p, int i) {
     return sp;
 }
 
+__device__ __forceinline__ void add_residual_chunk(const Params& p, int i, const float (&sum)[8], uint4& xv);
+
 // Deferred row-parallel reduction for the 8 columns 8i .. 8i+7 of row 0: the
 // previous GEMV's CTAs each left fp32 sums of their k-blocks of this row group
 // in a slot (SlotPlan); they are added in CTA order, rounded to fp16 (the
 // projection's output) and added to the residual chunk xv as the reference's
 // fp16 residual add does.  CTA 0 stores the result for the later kernels.
+
 __device__ __forceinline__ void add_slots_chunk(const Params& p, const SlotPlan& sp, int i, uint4& xv) {
     float4 a[4][2];
 #pragma unroll
@@ -299,6 +310,35 @@ __device__ __forceinline__ void add_slots_chunk(const Params& p, const SlotPlan&
         sum[0] += a[q][0].x; sum[1] += a[q][0].y; sum[2] += a[q][0].z; sum[3] += a[q][0].w;
         sum[4] += a[q][1].x; sum[5] += a[q][1].y; sum[6] += a[q][1].z; sum[7] += a[q][1].w;
     }
+    add_residual_chunk(p, i, sum, xv);
+}
+
+// x chunk i (8 columns, row 0) += fp16(the per-head sums of the previous o_proj), added in head order.
+__device__ __forceinline__ void add_heads_chunk(const Params& p, int i, uint4& xv) {
+    float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+    for (int q0 = 0; q0 < p.add_nheads; q0 += 4) {   // four heads' loads in flight at a time
+        float4 a[4][2];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (q0 + q < p.add_nheads) {
+                const float4* src = reinterpret_cast<const float4*>(p.add_heads + int64_t(q0 + q) * p.K + 8 * i);
+                a[q][0] = __ldcg(src);
+                a[q][1] = __ldcg(src + 1);
+            }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (q0 + q >= p.add_nheads) break;
+            sum[0] += a[q][0].x; sum[1] += a[q][0].y; sum[2] += a[q][0].z; sum[3] += a[q][0].w;
+            sum[4] += a[q][1].x; sum[5] += a[q][1].y; sum[6] += a[q][1].z; sum[7] += a[q][1].w;
+        }
+    }
+    add_residual_chunk(p, i, sum, xv);
+}
+
+// The projection's 8 fp32 sums rounded to fp16 and added to the residual chunk xv (fp16 add, the
+// reference's residual arithmetic); CTA 0 stores the result for the later kernels.
+__device__ __forceinline__ void add_residual_chunk(const Params& p, int i, const float (&sum)[8], uint4& xv) {
     __half2* h = reinterpret_cast<__half2*>(&xv);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -336,7 +376,8 @@ __device__ __forceinline__ EdgePlan edge_plan(const Params& p, int j) {
 }
 
 // `wpre`: norm_w_chunk() loaded earlier (nullptr: loaded here).
-template <int THREADS>
+// ADD_HEADS: the add_heads prologue is compiled in (only the gate|up kernel takes it).
+template <int THREADS, bool ADD_HEADS = false>
 __device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4* wpre = nullptr,
                                         const SlotPlan* sp = nullptr, const EdgePlan* ep = nullptr) {
     __shared__ float red[THREADS / 32][MAX_M];
@@ -370,6 +411,7 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4
                     xv[m] = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i));
                 }
                 if (sp && sp->n) add_slots_chunk(p, *sp, i, xv[0]);   // M == 1
+                else if (ADD_HEADS && p.add_heads) add_heads_chunk(p, i, xv[0]);
 #pragma unroll
                 for (int m = 0; m < MAX_M; ++m) {
                     if (m >= p.M) break;
@@ -619,6 +661,104 @@ __device__ __forceinline__ void edge_finish(const Params& p, const EdgeRed& e, c
     }
 }
 
+// o_proj over the attention's split partials (M = 1): the rows of the launch
+// are (KV head h, output row) pairs over head h's K-column block, so row group
+// h * R + r (R = row groups per head) is output row group r restricted to the
+// columns of head h.  The CTAs of head h (G*h/heads .. G*(h+1)/heads - 1) own
+// consecutive whole row groups of it, their warps consecutive unit ranges.
+__device__ __forceinline__ void heads_cta_range(const Params& p, int c, int& cu0, int& cu1, int& head) {
+    const int G = int(gridDim.x), nh = p.mrg_heads;
+    const int h = ((c + 1) * nh - 1) / G;
+    const int c0 = G * h / nh, n = G * (h + 1) / nh - c0;
+    const int R = (p.N / UNIT_ROWS) / nh, j = c - c0;
+    cu0 = (h * R + R * j / n) * p.KB;
+    cu1 = (h * R + R * (j + 1) / n) * p.KB;
+    head = h;
+}
+
+// The row group of the CTA's that warp `warp` adds after the CTA's last
+// barrier (whole row groups: no CTA edges; the sum goes out as fp32).
+__device__ __forceinline__ EdgeRed heads_red_plan(const Params& p, int warp) {
+    EdgeRed e;
+    e.rg = -1;
+    e.w0 = e.n = 0;
+    e.slots = 0u;
+    e.dst = -1;
+    int cu0, cu1, h;
+    heads_cta_range(p, int(blockIdx.x), cu0, cu1, h);
+    const int KB = p.KB, len = cu1 - cu0;
+    const int rg = cu0 / KB + warp;
+    if (rg > (cu1 - 1) / KB) return e;
+    const int base = rg * KB;
+    const int wf = ((base - cu0 + 1) * NAT_WARPS - 1) / len, wl = ((base + KB - cu0) * NAT_WARPS - 1) / len;
+    if (wf == wl) return e;   // one warp had all of it: finished in its loop
+    e.rg = rg;
+    e.w0 = wf;
+    e.n = wl - wf + 1;
+    for (int k = 0; k < e.n; ++k)
+        if ((cu0 + len * (wf + k) / NAT_WARPS) / KB != rg) e.slots |= 1u << k;
+    return e;
+}
+
+__device__ __forceinline__ void heads_finish(const Params& p, const EdgeRed& e, const float* red, int lane) {
+    if (e.rg < 0) return;
+    float v = 0.f;
+    for (int k = 0; k < e.n; ++k) v += red[((e.w0 + k) * 2 + ((e.slots >> k) & 1u)) * 32 + lane];
+    reinterpret_cast<float*>(p.out)[int64_t(e.rg) * 32 + lane] = v;
+}
+
+// x of head `head` (K = 128 * q heads per KV head columns) merged from the
+// decode attention's split partials, with the attention's own merge
+// arithmetic: M = the largest split maximum, weights exp2(m_s - M) (0 for an
+// empty split), L and the accumulator summed in split order, then one
+// rounding of acc / L to fp16 (0 when L is 0).  `scratch` holds 3 * 160 + 4
+// floats of shared memory.
+constexpr int MRG_MAX_SPLITS = 40;
+constexpr int MRG_PART = 132;   // floats per (split, q head): m, l, 2 pad, acc[128]
+__device__ __forceinline__ void stage_merge(const Params& p, __half* xs, int head, float* scratch) {
+    float* sm = scratch;                            // [S * gq] split maxima
+    float* sl = scratch + MRG_MAX_SPLITS * 4;       // [S * gq] split sums
+    float* sw = scratch + 2 * MRG_MAX_SPLITS * 4;   // [S * gq] weights
+    float* sM = scratch + 3 * MRG_MAX_SPLITS * 4;   // [gq]
+    const int gq = p.K / 128, S = p.mrg_splits, tid = threadIdx.x;
+    const int qh = tid >> 7, d = tid & 127;
+    const float* base = p.mrg_part + int64_t(head) * S * gq * MRG_PART;
+    float a[MRG_MAX_SPLITS];   // this thread's channel, split by split (requested with m and l: one round trip)
+#pragma unroll
+    for (int s = 0; s < MRG_MAX_SPLITS; ++s)
+        a[s] = (s < S && qh < gq) ? __ldcg(base + (s * gq + qh) * MRG_PART + 4 + d) : 0.f;
+    if (tid < S * gq) {
+        sm[tid] = __ldcg(base + tid * MRG_PART);
+        sl[tid] = __ldcg(base + tid * MRG_PART + 1);
+    }
+    __syncthreads();
+    if (tid < gq) {
+        float M = -INFINITY;
+        for (int s = 0; s < S; ++s) M = fmaxf(M, sm[s * gq + tid]);
+        sM[tid] = M;
+    }
+    __syncthreads();
+    if (tid < S * gq) {
+        const float M = sM[tid % gq], m = sm[tid];
+        sw[tid] = (M == -INFINITY || m == -INFINITY) ? 0.f : exp2f(m - M);
+    }
+    __syncthreads();
+    if (qh < gq) {
+        float L = 0.f, o = 0.f;
+        if (sM[qh] != -INFINITY) {
+#pragma unroll
+            for (int s = 0; s < MRG_MAX_SPLITS; ++s) {
+                if (s >= S) break;
+                const float wt = sw[s * gq + qh];
+                if (wt == 0.f) continue;
+                L += wt * sl[s * gq + qh];
+                o += wt * a[s];
+            }
+        }
+        xs[tid] = L > 0.f ? __float2half_rn(__fdiv_rn(o, L)) : __float2half_rn(0.f);
+    }
+}
+
 __device__ __forceinline__ void mma_unit_smem(const uint8_t* unit, const uint32_t (&xb)[8], uint32_t lut_base,
                                               uint32_t laneword, int lane, int g, float (&acc)[2][4]) {
     const uint4 c0 = lds128(unit + 16 * lane);          // rows g, g+8
@@ -674,13 +814,22 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     // ranges, so most shared row groups are added in shared memory (edge_finish); otherwise warp w
     // of the grid is warp w / G of CTA w % G
     const bool edge = EPI == EPI_SILU_MUL && p.edge_out != nullptr;
+    // HEADS (EPI_F32 over the attention's partials, M = 1, every warp active): head-aligned CTAs, the
+    // same consecutive warp ranges and shared-memory sums
+    const bool heads = EPI == EPI_F32 && p.mrg_part != nullptr;
     float* edge_red = reinterpret_cast<float*>(smem_raw + LUT_BYTES + xs_bytes +
                                                size_t(NAT_WARPS) * NAT_STAGES * stage_bytes);
-    const int w = edge ? int(blockIdx.x) * NAT_WARPS + warp : warp * int(gridDim.x) + int(blockIdx.x);
+    const int w = (edge || heads) ? int(blockIdx.x) * NAT_WARPS + warp : warp * int(gridDim.x) + int(blockIdx.x);
     const int W = p.total_warps;
     const bool active = w < W;
-    const int64_t u_begin = active ? unit_begin(p.units, w, W) : 0;
-    const int64_t u_end = active ? unit_begin(p.units, w + 1, W) : 0;
+    int h_cu0 = 0, h_cu1 = 0, h_head = 0;
+    if (EPI == EPI_F32 && heads) heads_cta_range(p, int(blockIdx.x), h_cu0, h_cu1, h_head);
+    const int64_t u_begin = !active ? 0
+                            : heads ? h_cu0 + int64_t(h_cu1 - h_cu0) * warp / NAT_WARPS
+                                    : unit_begin(p.units, w, W);
+    const int64_t u_end = !active ? 0
+                          : heads ? h_cu0 + int64_t(h_cu1 - h_cu0) * (warp + 1) / NAT_WARPS
+                                  : unit_begin(p.units, w + 1, W);
     const int n_chunks = int((u_end - u_begin + stage_units - 1) / stage_units);
 
     auto issue = [&](int chunk) {   // lane 0 only
@@ -704,10 +853,15 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     EdgeRed er;
     er.rg = -1;
     if (EPI == EPI_SILU_MUL && edge) er = edge_red_plan(p, warp);
+    if (EPI == EPI_F32 && heads) er = heads_red_plan(p, warp);
     build_lut<NAT_THREADS>(lut_s, p.lut);
     pdl_trigger();
     pdl_wait();
-    if (!XG) stage_x<NAT_THREADS>(p, xs, &wpre, &sp);
+    if (EPI == EPI_F32 && heads) {
+        if (!XG) stage_merge(p, xs, h_head, edge_red);   // edge_red is free until the loop ends
+    } else if (!XG) {
+        stage_x<NAT_THREADS, EPI == EPI_SILU_MUL>(p, xs, &wpre, &sp);
+    }
     __syncthreads();
     if (!active) return;
 
@@ -750,7 +904,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
                 if (seg_b0 == 0) {
                     epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
                     epilogue<EPI>(p, 2 * cur_rg + 1, acc[1], g, t);
-                } else if (edge) {
+                } else if (edge || heads) {
                     keep(cur_rg);
                 } else {
                     flush_partial<EPI, 2>(p, cur_rg, acc, w, first_rg, lane, g, t);
@@ -788,7 +942,7 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
         if (seg_b0 == 0 && b == 0) {   // the range ended exactly at the end of cur_rg
             epilogue<EPI>(p, 2 * cur_rg, acc[0], g, t);
             epilogue<EPI>(p, 2 * cur_rg + 1, acc[1], g, t);
-        } else if (edge) {
+        } else if (edge || heads) {
             keep(cur_rg);
         } else {
             flush_partial<EPI, 2>(p, cur_rg, acc, w, first_rg, lane, g, t);
@@ -797,6 +951,11 @@ __global__ void __launch_bounds__(NAT_THREADS, 1)
     if (EPI == EPI_SILU_MUL && edge) {   // every warp of the CTA is active (host-checked) and gets here
         __syncthreads();
         edge_finish(p, er, edge_red, lane);
+        return;
+    }
+    if (EPI == EPI_F32 && heads) {
+        __syncthreads();
+        heads_finish(p, er, edge_red, lane);
         return;
     }
     if (ok) finish_launch<EPI>(p, lane);
@@ -2182,6 +2341,27 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
                                               "and an edge_out producer of N = 2K, K = edge_k");
         if (reinterpret_cast<uintptr_t>(a->edge_in) % 16) return fail(NOVA_ERR_ALIGN, "edge_in must be 16-byte aligned");
     }
+    if (a->attn_part) {   // o_proj over the attention's split partials, head-aligned CTAs
+        const int64_t nh = a->attn_heads, kb = k / 64;
+        const int64_t R = nh > 0 ? n / UNIT_ROWS / nh : 0, nmax = nh > 0 ? (G_sm + nh - 1) / nh : 0;
+        if (epi != EPI_F32 || !native || m != 1 || a->norm_weight || a->add_slots || a->add_heads || a->edge_out ||
+            a->edge_in || k % 128 || k / 128 > 4 || a->attn_splits < 1 || a->attn_splits > MRG_MAX_SPLITS ||
+            nh < 1 || nh > G_sm || n % (UNIT_ROWS * nh) || R < nmax || (R / (G_sm / nh)) + 1 > NAT_WARPS ||
+            (R / nmax) * kb < NAT_WARPS)
+            return fail(NOVA_ERR_UNSUPPORTED, "attn_part needs F32, the native layout, M = 1, no other prologue, "
+                                              "K = 128 x (1..4) q heads, 1..%d splits, and N / attn_heads row groups "
+                                              "per head for 1..15 row groups per SM", MRG_MAX_SPLITS);
+        if (reinterpret_cast<uintptr_t>(a->attn_part) % 16) return fail(NOVA_ERR_ALIGN, "attn_part must be 16-byte aligned");
+    }
+    if (a->add_heads) {   // x += the per-head sums of an attn_part launch (its N / attn_heads = this K)
+        if (m != 1 || !native || !a->norm_weight || a->add_slots || k / 8 > NAT_THREADS || a->add_nheads < 1 ||
+            a->add_nheads > 8)
+            return fail(NOVA_ERR_UNSUPPORTED, "add_heads needs M = 1, the native layout, a norm prologue, K <= %d, "
+                                              "no add_slots and 1..8 heads", 8 * NAT_THREADS);
+        if (reinterpret_cast<uintptr_t>(a->add_heads) % 16 || (a->resid_out && reinterpret_cast<uintptr_t>(a->resid_out) % 16))
+            return fail(NOVA_ERR_ALIGN, "add_heads and resid_out must be 16-byte aligned");
+        if (a->resid_out == a->x) return fail(NOVA_ERR_INVALID, "resid_out must not alias x");
+    }
     if (epi == EPI_RESIDUAL && !a->residual) return fail(NOVA_ERR_INVALID, "residual epilogue needs residual");
     if (epi == EPI_ARGMAX && !a->argmax) return fail(NOVA_ERR_INVALID, "argmax epilogue needs argmax");
     if (epi != EPI_PLAIN && a->bias) return fail(NOVA_ERR_UNSUPPORTED, "bias only with the plain epilogue");
@@ -2238,6 +2418,16 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         p.resid_out = (__half*)a->resid_out;
     }
     p.edge_out = (float*)a->edge_out;
+    if (a->attn_part) {
+        p.mrg_part = (const float*)a->attn_part;
+        p.mrg_splits = int(a->attn_splits);
+        p.mrg_heads = int(a->attn_heads);
+    }
+    if (a->add_heads) {
+        p.add_heads = (const float*)a->add_heads;
+        p.add_nheads = int(a->add_nheads);
+        p.resid_out = (__half*)a->resid_out;
+    }
     if (a->edge_in) {
         p.edge_in = (const float*)a->edge_in;
         p.edge_KB = int(a->edge_k / 64);
@@ -2270,7 +2460,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         // leave less than 2 units per stage and there is no norm prologue.
         const int64_t ring_unit = int64_t(NAT_WARPS) * NAT_STAGES * UNIT_BYTES;
         const int64_t slack = 1024;   // static shared memory
-        const int64_t edge_bytes = a->edge_out ? EDGE_RED_BYTES : 0;   // after the rings
+        const int64_t edge_bytes = (a->edge_out || a->attn_part) ? EDGE_RED_BYTES : 0;   // after the rings
         auto units_for = [&](int64_t xs_bytes) {
             return std::min<int64_t>(4, (optin - int64_t(LUT_BYTES) - xs_bytes - edge_bytes - slack) / ring_unit);
         };
@@ -2291,8 +2481,9 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
         // lm_head: with several row groups per CTA the CTA-level schedule
         // would synchronise its 16 warps once per row group); CTA-level
         // split-K on whole row groups below that (no cross-CTA reduction).
-        const bool warp_level = a->edge_out || (epi != EPI_SLOTS && ((launch_flags() & 2) ||
+        const bool warp_level = a->edge_out || a->attn_part || (epi != EPI_SLOTS && ((launch_flags() & 2) ||
                                                                       n / UNIT_ROWS >= 2 * int64_t(sm_count())));
+        if (a->attn_part && xg) return fail(NOVA_ERR_UNSUPPORTED, "attn_part needs x staged in shared memory");
         if (a->edge_in && (warp_level || xg))
             return fail(NOVA_ERR_UNSUPPORTED, "edge_in needs the CTA-level schedule with x staged (SLOTS or fewer "
                                               "than two row groups per SM)");
@@ -2303,6 +2494,7 @@ extern "C" int nova_nf4_gemv(const nova_nf4_args* a, void* stream) {
             const int64_t want = (p.units + NAT_MIN_UNITS - 1) / NAT_MIN_UNITS;
             // edge_out: every warp of every CTA active (checked above: want >= SMs x 16)
             p.total_warps = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sm_count()) * NAT_WARPS, want)));
+            if (a->attn_part) p.total_warps = int(sm_count()) * NAT_WARPS;   // head-aligned CTAs, every warp busy
             const unsigned grid = unsigned(std::min<int64_t>(sm_count(), p.total_warps));
             err = launch(kern, dim3(grid), dim3(NAT_THREADS), size_t(nsmem), (cudaStream_t)stream, p, int(stage_units),
                          errp);

@@ -49,8 +49,8 @@ import torch
 
 from . import _lib
 from .kernels import (build_nf4_lut, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native, pack_tc,
-                      slots_buffer, edge_buffer)
-from .kvattn import CHUNK, GROUP_T, KVInt8Cache, launch_attention, pick_chunk, prefill_attention
+                      slots_buffer, edge_buffer, heads_major)
+from .kvattn import CHUNK, GROUP_T, KVInt8Cache, attn_partials, launch_attention, pick_chunk, prefill_attention
 from .quant import nf4_codebook, quantize_nf4
 from .tp import P2PAllReduce, TPContext, all_reduce_sum, shard_ranges, shard_weights
 
@@ -264,7 +264,8 @@ class NovaDecoder:
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=f16, device=dev)
         self.argmax_slot = torch.zeros(B, dtype=torch.int64, device=dev)
         self.input_ids = torch.zeros(B, dtype=torch.int64, device=dev)
-        n_max = max(cfg.vocab_size, 2 * self.inter, self.q_dim + 2 * self.kv_dim, cfg.hidden_size)
+        n_max = max(cfg.vocab_size, 2 * self.inter, self.q_dim + 2 * self.kv_dim, cfg.hidden_size,
+                    self.hkv * cfg.hidden_size)
         self.gemv_ws = gemv_workspace(dev, n_max).clone()   # shared by every GEMV of the step
         # batched GEMM (decode above 8 rows, and every prefill): one workspace for every shape
         shapes = [(self.q_dim + 2 * self.kv_dim, cfg.hidden_size), (cfg.hidden_size, self.q_dim),
@@ -291,6 +292,14 @@ class NovaDecoder:
         # with the deferred reductions, gate|up also leaves the row groups split between its CTAs as fp32
         # sums (edge_out) that down_proj completes while staging its input: no cross-CTA reduction
         self.edges = edge_buffer(self.device) if self.deferred and self._edges_fit() else None
+        # and the attention leaves its split partials to o_proj, which merges each KV head's while staging
+        # its input (head-aligned CTAs over a head-major copy of o_proj) and writes fp32 sums per head that
+        # gate|up adds: the attention launch has no arrival counters and no per-head merge
+        self.heads = self.deferred and self._heads_fit()
+        self.y_heads = (torch.zeros(self.hkv, cfg.hidden_size, dtype=torch.float32, device=self.device)
+                        if self.heads else None)
+        self.o_heads = ([heads_major(lw.o.units, cfg.hidden_size, self.q_dim, self.hkv) for lw in self.w.layers]
+                        if self.heads else None)
         self._staged = None   # fp16 K/V per layer of the positions prefilled / injected since the last reset
 
     def _deferred_fits(self) -> bool:
@@ -317,6 +326,18 @@ class NovaDecoder:
         per = -(-units // sms)
         return (units >= 8 * 16 * sms and units // sms >= 2 * kb and -(-per // kb) + 1 <= 16
                 and 2 * (sms - 1) <= 512 and (units + 1) * 16 * sms < 2 ** 31)
+
+    def _heads_fit(self) -> bool:
+        """o_proj's attn_part limits (nova_nf4_gemv): head_dim 128, 1 to 4 q
+        heads per KV head, at most 40 splits (with the ring), and 1 to 15 row
+        groups of each head per SM with 16 units per SM at least."""
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        h, hkv = self.cfg.hidden_size, self.hkv
+        gq = self.hq // hkv
+        if self.cfg.head_dim != 128 or not 1 <= gq <= 4 or self.cache.n_splits + 1 > 40 or hkv > sms or h % 32:
+            return False
+        rg, nmax = h // 32, -(-sms // hkv)
+        return rg >= nmax and rg // (sms // hkv) + 1 <= 16 and (rg // nmax) * 2 * gq >= 16
 
     def _pick_chunk(self) -> int:
         """Split size for the attention (``kvattn.pick_chunk``)."""
@@ -631,7 +652,7 @@ class NovaDecoder:
 
     def _gemv(self, x, w: NF4Weight, out, *, epilogue: int = _lib.NF4_PLAIN, norm_weight=None, residual=None,
               argmax=None, token_out=None, pos=None, embed=None, embed_out=None, add=None, resid_out=None,
-              edge_out=None, edge_in=None) -> None:
+              edge_out=None, edge_in=None, attn_part=None, add_heads=None) -> None:
         """The step's NF4 projection: nova_nf4_gemv up to GEMV_ROWS rows, else
         nova_nf4_gemm (after nova_rmsnorm when the projection has a norm prologue)."""
         B = x.shape[0]
@@ -656,7 +677,10 @@ class NovaDecoder:
                      embed=embed, embed_out=None if embed_out is None else embed_out[sl],
                      workspace=self.gemv_ws, n=w.n, add_slots=None if add is None else add[0],
                      add_k=0 if add is None else add[1], resid_out=resid_out, edge_out=edge_out,
-                     edge_in=None if edge_in is None else edge_in[0], edge_k=0 if edge_in is None else edge_in[1])
+                     edge_in=None if edge_in is None else edge_in[0], edge_k=0 if edge_in is None else edge_in[1],
+                     attn_part=None if attn_part is None else attn_part[0],
+                     attn_splits=0 if attn_part is None else attn_part[1],
+                     attn_heads=0 if attn_part is None else attn_part[2], add_heads=add_heads)
 
     def _qk_args(self, li: int, lw) -> "_lib.QKArgs":
         cfg, cache = self.cfg, self.cache
@@ -718,6 +742,15 @@ class NovaDecoder:
                    argmax=self.argmax_slot, token_out=self.input_ids, pos=cache.pos, embed=self.w.embed,
                    embed_out=self.resid)
 
+    def _o_heads(self, li: int) -> None:
+        """o_proj of layer li over the attention's split partials (one KV head per CTA, fp32 sums per head
+        into y_heads; nova_nf4_gemv attn_part)."""
+        cache, k = self.cache, self.q_dim // self.hkv
+        nf4_gemv(self.attn[:, :k], self.o_heads[li], None, self.lut, self.y_heads.view(1, -1),
+                 epilogue=_lib.NF4_F32, workspace=self.gemv_ws, n=self.hkv * self.cfg.hidden_size,
+                 attn_part=attn_partials(cache.workspace, self.batch, self.hkv), attn_splits=cache.n_splits + 1,
+                 attn_heads=self.hkv)
+
     def _step_body_deferred(self, q3, a3) -> None:
         """The step with o_proj / down_proj reductions deferred into the next
         GEMV's input staging: the residual lives in resid (step input, R0) and
@@ -735,11 +768,17 @@ class NovaDecoder:
             launch_attention(q3, (cache.kq[li], cache.kmn[li], cache.kst[li], cache.vq[li], cache.vmn[li],
                                   cache.vst[li]), (cache.tail_k[li], cache.tail_v[li]), a3, None, cache._qlen,
                              cache._pg, cache._written, cache.first, cache.workspace, max_len=self.max_len,
-                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window, qk=qa)
-            self._gemv(self.attn, lw.o, slots, epilogue=_lib.NF4_SLOTS)
+                             n_splits=cache.n_splits, chunk=cache.chunk, window=cache.window, qk=qa,
+                             defer_merge=self.heads)
             edges = self.edges
-            self._gemv(r0, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln,
-                       add=(slots, self.q_dim), resid_out=r1, edge_out=edges)
+            if self.heads:
+                self._o_heads(li)
+                self._gemv(r0, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln,
+                           resid_out=r1, edge_out=edges, add_heads=self.y_heads)
+            else:
+                self._gemv(self.attn, lw.o, slots, epilogue=_lib.NF4_SLOTS)
+                self._gemv(r0, lw.gate_up, self.act, epilogue=_lib.NF4_SILU_MUL, norm_weight=lw.post_ln,
+                           add=(slots, self.q_dim), resid_out=r1, edge_out=edges)
             self._gemv(self.act, lw.down, slots, epilogue=_lib.NF4_SLOTS,
                        edge_in=None if edges is None else (edges, cfg.hidden_size))
         self._gemv(r1, self.w.lm_head, self.logits, epilogue=_lib.NF4_ARGMAX, norm_weight=self.w.final_norm,

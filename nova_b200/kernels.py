@@ -132,7 +132,8 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
              workspace: torch.Tensor | None = None, n: int | None = None,
              add_slots: torch.Tensor | None = None, add_k: int = 0,
              resid_out: torch.Tensor | None = None, edge_out: torch.Tensor | None = None,
-             edge_in: torch.Tensor | None = None, edge_k: int = 0) -> torch.Tensor:
+             edge_in: torch.Tensor | None = None, edge_k: int = 0, attn_part: int | None = None,
+             attn_splits: int = 0, attn_heads: int = 0, add_heads: torch.Tensor | None = None) -> torch.Tensor:
     """Launch ``nova_nf4_gemv`` on 2-D views (x ``[M, K]``, out ``[M, N or N/2]``).
 
     Reference layout: ``packed`` uint8 ``[N, K/2]`` with ``absmax``
@@ -146,7 +147,12 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
     row groups split between CTAs are left there as fp32 sums instead of being
     reduced across CTAs, so ``out`` is incomplete until a following launch with
     ``edge_in`` (that buffer) and ``edge_k`` (this launch's K) completes them
-    while it stages x (its K = this launch's N / 2)."""
+    while it stages x (its K = this launch's N / 2).
+    ``attn_part`` (a device address, :func:`nova_b200.kvattn.attn_partials`)
+    with ``attn_splits`` / ``attn_heads``: ``NF4_F32`` over the head-major unit
+    stream of o_proj (:func:`heads_major`), x merged from the decode
+    attention's split partials, ``out`` the fp32 ``[attn_heads, N / attn_heads]``
+    per-head sums; ``add_heads`` (those sums) is added to x like ``add_slots``."""
     m, k = x.shape
     native = absmax is None
     if native:
@@ -184,6 +190,10 @@ def nf4_gemv(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor | None,
     if add_slots is not None:
         a.add_slots, a.add_k, a.resid_out = add_slots.data_ptr(), int(add_k), _lib.ptr(resid_out)
     a.edge_out = _lib.ptr(edge_out)
+    if attn_part is not None:
+        a.attn_part, a.attn_splits, a.attn_heads = int(attn_part), int(attn_splits), int(attn_heads)
+    if add_heads is not None:
+        a.add_heads, a.add_nheads, a.resid_out = add_heads.data_ptr(), int(add_heads.shape[0]), _lib.ptr(resid_out)
     if edge_in is not None:
         a.edge_in, a.edge_k = edge_in.data_ptr(), int(edge_k)
     _lib.check(_lib.lib().nova_nf4_gemv(_lib.ctypes.byref(a), _lib.stream_of(x.device)), "nova_nf4_gemv")
@@ -196,6 +206,14 @@ def slots_buffer(device: torch.device) -> torch.Tensor:
     rows)."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     return torch.zeros(sms * 4 * 8, 32, dtype=torch.float32, device=device)
+
+
+def heads_major(units: torch.Tensor, n: int, k: int, heads: int) -> torch.Tensor:
+    """The native unit stream of an [n, k] matrix reordered head-major: the
+    k columns split into ``heads`` blocks, block h's row groups first (the
+    layout ``attn_part`` launches read)."""
+    rg, kb = n // 32, k // 64
+    return units.view(rg, heads, kb // heads, -1).permute(1, 0, 2, 3).contiguous().view(-1)
 
 
 def edge_buffer(device: torch.device) -> torch.Tensor:

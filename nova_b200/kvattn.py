@@ -97,11 +97,17 @@ def _check(x: torch.Tensor, name: str, dtype: torch.dtype) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
+def attn_partials(workspace: torch.Tensor, batch: int, kv_heads: int) -> int:
+    """Device address of the split partials inside an attention workspace
+    (``defer_merge``): byte 256 + align_up(batch * kv_heads * 4, 256)."""
+    return workspace.data_ptr() + 256 + (batch * kv_heads * 4 + 255) // 256 * 256
+
+
 def launch_attention(q: torch.Tensor, kv: tuple | None, tail: tuple | None, out: torch.Tensor,
                      lse: torch.Tensor | None, qlen_t: torch.Tensor, pg_t: torch.Tensor,
                      written_t: torch.Tensor | None, first_t: torch.Tensor | None, workspace: torch.Tensor,
                      *, max_len: int, n_splits: int, chunk: int = CHUNK, window: int = 0,
-                     qk: "_lib.QKArgs | None" = None) -> None:
+                     qk: "_lib.QKArgs | None" = None, defer_merge: bool = False) -> None:
     """Thin launcher for ``nova_attn_decode_int8``; with ``qk`` (the
     arguments of ``nova_qk_norm_rope_append`` for the same ring and cache) the
     q/k norm + RoPE + ring append runs in the same launch
@@ -138,6 +144,7 @@ def launch_attention(q: torch.Tensor, kv: tuple | None, tail: tuple | None, out:
     a.batch, a.q_heads, a.kv_heads = B, Hq, Hkv
     a.max_len, a.groups, a.head_dim, a.group = int(max_len), int(groups), D, GROUP_T
     a.chunk, a.n_splits, a.window = int(chunk), int(n_splits), int(window)
+    a.defer_merge = int(bool(defer_merge))   # with qk: the split partials stay for the o_proj launch
     if qk is not None:
         _lib.check(_lib.lib().nova_qk_append_attn_int8(_lib.ctypes.byref(qk), _lib.ctypes.byref(a),
                                                        _lib.stream_of(q.device)), "nova_qk_append_attn_int8")
