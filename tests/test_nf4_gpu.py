@@ -489,3 +489,31 @@ def test_edges_rejected_outside_their_shapes(cuda_lib):
                  edge_out=edges)
     with pytest.raises(ValueError, match="edge_in"):   # with a norm prologue
         nf4_gemv(x, units, None, _lut(), out, workspace=ws, n=4096, norm_weight=x[0], edge_in=edges, edge_k=2560)
+
+
+def test_attention_partials_and_head_sums_rejected_outside_their_shapes(cuda_lib):
+    """attn_part (o_proj over the decode attention's split partials) takes only
+    NF4_F32 at M = 1 on a K of 128 x (1..4) columns with at most 40 splits;
+    add_heads needs a norm prologue."""
+    from nova_b200 import _lib
+    from nova_b200.kernels import gemv_workspace, heads_major, nf4_gemv, pack_native
+
+    _, p, a = _weights(2560, 4096, 51)
+    units = heads_major(pack_native(p, a), 2560, 4096, 8)
+    x = torch.zeros(1, 512, dtype=torch.float16, device="cuda")
+    part = torch.zeros(8 * 34 * 4 * 132, dtype=torch.float32, device="cuda")
+    y = torch.zeros(1, 8 * 2560, dtype=torch.float32, device="cuda")
+    ws = gemv_workspace(torch.device("cuda"), 8 * 2560)
+    kw = dict(workspace=ws, n=8 * 2560, attn_part=part.data_ptr(), attn_heads=8)
+    nf4_gemv(x, units, None, _lut(), y, epilogue=_lib.NF4_F32, attn_splits=34, **kw)   # accepted
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError, match="attn_part"):   # not the fp32 epilogue
+        nf4_gemv(x, units, None, _lut(), y.half(), attn_splits=34, **kw)
+    with pytest.raises(ValueError, match="attn_part"):   # more splits than the merge holds
+        nf4_gemv(x, units, None, _lut(), y, epilogue=_lib.NF4_F32, attn_splits=41, **kw)
+    heads = torch.zeros(8, 2560, dtype=torch.float32, device="cuda")
+    xr = torch.zeros(1, 2560, dtype=torch.float16, device="cuda")
+    out = torch.empty(1, 4096, dtype=torch.float16, device="cuda")
+    _, qp, qa = _weights(4096, 2560, 52)
+    with pytest.raises(ValueError, match="add_heads"):   # no norm prologue
+        nf4_gemv(xr, pack_native(qp, qa), None, _lut(), out, workspace=ws, n=4096, add_heads=heads)
