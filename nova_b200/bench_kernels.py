@@ -23,12 +23,13 @@ import torch
 
 from . import _lib
 from .decoder import interleave_gate_up
-from .kernels import (build_nf4_lut, edge_buffer, gemm_workspace, gemv_workspace, nf4_gemm, nf4_gemv, pack_native,
-                      pack_tc)
+from .kernels import (build_nf4_lut, edge_buffer, gemm_workspace, gemv_workspace, heads_major, nf4_gemm, nf4_gemv,
+                      pack_native, pack_tc)
 from .kvattn import GROUP_T, launch_attention, new_workspace, pick_chunk
 from .quant import nf4_codebook, quantize_nf4
 
-EPI = {"plain": _lib.NF4_PLAIN, "residual": _lib.NF4_RESIDUAL, "silu": _lib.NF4_SILU_MUL, "argmax": _lib.NF4_ARGMAX}
+EPI = {"plain": _lib.NF4_PLAIN, "residual": _lib.NF4_RESIDUAL, "silu": _lib.NF4_SILU_MUL, "argmax": _lib.NF4_ARGMAX,
+       "f32": _lib.NF4_F32}
 
 
 def _graph_time(fn, sets: int, iters: int) -> float:
@@ -56,7 +57,8 @@ def _graph_time(fn, sets: int, iters: int) -> float:
 
 
 def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool = False, sets: int = 0,
-               iters: int = 20, seed: int = 0, layout: str = "native", edges: bool = False) -> dict:
+               iters: int = 20, seed: int = 0, layout: str = "native", edges: bool = False,
+               heads: int = 0, splits: int = 34) -> dict:
     dev = torch.device("cuda")
     code = nf4_codebook()
     lut = build_nf4_lut(code).to(dev)
@@ -72,13 +74,16 @@ def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool =
             pa = interleave_gate_up(gp, ga, up, ua)
         else:
             pa = quantize_nf4(w, code)
-        weights.append((pack_native(*pa), None) if layout == "native" else pa)
+        if heads:   # o_proj over the attention's split partials: the head-major unit stream
+            weights.append((heads_major(pack_native(*pa), n, k, heads), None))
+        else:
+            weights.append((pack_native(*pa), None) if layout == "native" else pa)
         del w
-    x = torch.randn(m, k, generator=g, device=dev).half()
+    x = torch.randn(m, k // max(1, heads), generator=g, device=dev).half()
     nw = torch.ones(k, dtype=torch.float16, device=dev) if norm else None
     nout = n // 2 if epilogue == "silu" else n
     out = torch.zeros(m, nout, dtype=torch.float16, device=dev)
-    ws = gemv_workspace(dev, n).clone()
+    ws = gemv_workspace(dev, max(n, n * heads)).clone()
     kw = {}
     if epilogue == "residual":
         kw["residual"] = out
@@ -86,14 +91,23 @@ def bench_gemv(n: int, k: int, m: int = 1, epilogue: str = "plain", norm: bool =
         kw["argmax"] = torch.zeros(m, dtype=torch.int64, device=dev)
     if edges:   # SiLU·mul leaving its CTA-edge row groups as fp32 sums (the batch-1 decode's gate|up)
         kw["edge_out"] = edge_buffer(dev)
+    if heads:   # partials of a decode attention with `splits` splits (random m, l, acc), fp32 sums per head
+        gq = (k // heads) // 128
+        part = torch.randn(heads * splits * gq * 132, generator=g, device=dev).abs() + 0.5
+        kw.update(attn_part=part.data_ptr(), attn_splits=splits, attn_heads=heads, n=n * heads)
+        out = torch.zeros(m, n * heads, dtype=torch.float32, device=dev)
+        kw["_part"] = part
+
+    part_keep = kw.pop("_part", None)   # keeps the partials alive
+    kw.setdefault("n", n)
 
     def fn(i):
         p, a = weights[i]
-        nf4_gemv(x, p, a, lut, out, epilogue=EPI[epilogue], norm_weight=nw, workspace=ws, n=n, **kw)
+        nf4_gemv(x, p, a, lut, out, epilogue=EPI[epilogue], norm_weight=nw, workspace=ws, **kw)
 
     us = _graph_time(fn, sets, iters)
     return {"kernel": "nf4_gemv", "layout": layout, "n": n, "k": k, "m": m, "epilogue": epilogue, "norm": norm,
-            "edges": edges, "sets": sets, "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+            "edges": edges, "heads": heads, "sets": sets, "us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
 
 
 def bench_gemm(n: int, k: int, m: int = 64, epilogue: str = "plain", sets: int = 0, iters: int = 20,
@@ -313,6 +327,8 @@ def main() -> None:
     a.add_argument("--variant", choices=["cta", "warp"], default="cta",
                    help="native GEMV split-K at CTA level (default) or warp level")
     a.add_argument("--edges", action="store_true", help="SiLU·mul at M = 1 with CTA edges (edge_out)")
+    a.add_argument("--heads", type=int, default=0,
+                   help="o_proj over a decode attention's split partials: KV heads (N = output rows, K = all heads)")
     c = sub.add_parser("gemm")
     c.add_argument("--n", type=int, required=True)
     c.add_argument("--k", type=int, required=True)
@@ -341,7 +357,7 @@ def main() -> None:
         _lib.set_launch_flags((_lib.LAUNCH_PDL if args.pdl else 0) |
                               (_lib.LAUNCH_WARP_SPLITK if args.variant == "warp" else 0))
         print(json.dumps(bench_gemv(args.n, args.k, args.m, args.epilogue, args.norm, args.sets, args.iters,
-                                    layout=args.layout, edges=args.edges)))
+                                    layout=args.layout, edges=args.edges, heads=args.heads)))
     elif args.cmd == "gemm":
         _lib.set_launch_flags(_lib.LAUNCH_PDL)
         print(json.dumps(bench_gemm(args.n, args.k, args.m, args.epilogue, args.sets, args.iters)))
