@@ -313,29 +313,6 @@ __device__ __forceinline__ void add_slots_chunk(const Params& p, const SlotPlan&
     add_residual_chunk(p, i, sum, xv);
 }
 
-// x chunk i (8 columns, row 0) += fp16(the per-head sums of the previous o_proj), added in head order.
-__device__ __forceinline__ void add_heads_chunk(const Params& p, int i, uint4& xv) {
-    float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-    for (int q0 = 0; q0 < p.add_nheads; q0 += 4) {   // four heads' loads in flight at a time
-        float4 a[4][2];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (q0 + q < p.add_nheads) {
-                const float4* src = reinterpret_cast<const float4*>(p.add_heads + int64_t(q0 + q) * p.K + 8 * i);
-                a[q][0] = __ldcg(src);
-                a[q][1] = __ldcg(src + 1);
-            }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            if (q0 + q >= p.add_nheads) break;
-            sum[0] += a[q][0].x; sum[1] += a[q][0].y; sum[2] += a[q][0].z; sum[3] += a[q][0].w;
-            sum[4] += a[q][1].x; sum[5] += a[q][1].y; sum[6] += a[q][1].z; sum[7] += a[q][1].w;
-        }
-    }
-    add_residual_chunk(p, i, sum, xv);
-}
-
 // The projection's 8 fp32 sums rounded to fp16 and added to the residual chunk xv (fp16 add, the
 // reference's residual arithmetic); CTA 0 stores the result for the later kernels.
 __device__ __forceinline__ void add_residual_chunk(const Params& p, int i, const float (&sum)[8], uint4& xv) {
@@ -383,6 +360,65 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4
     __shared__ float red[THREADS / 32][MAX_M];
     __shared__ float rstd[MAX_M];
     const int kv8 = p.K / 8;
+    if (ADD_HEADS && p.add_heads && p.norm_w) {
+        // M = 1 and one chunk per thread (host-checked): x += fp16(the heads' sums), then the norm; only one
+        // row's registers live, so the 8 heads' loads are in flight together with x's
+        const int i = threadIdx.x;
+        float ss = 0.f;
+        uint4 xv = make_uint4(0u, 0u, 0u, 0u), wv = make_uint4(0u, 0u, 0u, 0u);
+        if (i < kv8) {
+            wv = wpre ? *wpre : *reinterpret_cast<const uint4*>(p.norm_w + 8 * i);
+            xv = __ldcg(reinterpret_cast<const uint4*>(p.x + 8 * i));
+            float4 a[8][2];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (q < p.add_nheads) {
+                    const float4* src = reinterpret_cast<const float4*>(p.add_heads + int64_t(q) * p.K + 8 * i);
+                    a[q][0] = __ldcg(src);
+                    a[q][1] = __ldcg(src + 1);
+                }
+            float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (q >= p.add_nheads) break;
+                sum[0] += a[q][0].x; sum[1] += a[q][0].y; sum[2] += a[q][0].z; sum[3] += a[q][0].w;
+                sum[4] += a[q][1].x; sum[5] += a[q][1].y; sum[6] += a[q][1].z; sum[7] += a[q][1].w;
+            }
+            add_residual_chunk(p, i, sum, xv);
+            const __half2* h = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 f = __half22float2(h[q]);
+                ss += f.x * f.x + f.y * f.y;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5][0] = ss;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float v = 0.f;
+            for (int w = 0; w < THREADS / 32; ++w) v += red[w][0];
+            rstd[0] = rsqrt_ieee(__fdiv_rn(v, float(p.K)) + p.eps);
+        }
+        __syncthreads();
+        if (i < kv8) {
+            const float r = rstd[0];
+            const __half2* h = reinterpret_cast<const __half2*>(&xv);
+            const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+            uint4 o;
+            __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 f = __half22float2(h[q]);
+                const float2 wf = __half22float2(wh[q]);
+                const float2 nf = __half22float2(__floats2half2_rn(f.x * r, f.y * r));
+                oh[q] = __floats2half2_rn(wf.x * nf.x, wf.y * nf.y);
+            }
+            *reinterpret_cast<uint4*>(xs + 8 * i) = o;
+        }
+        return;
+    }
     if (p.norm_w) {
         const bool one = kv8 <= THREADS;
         float ss[MAX_M];
@@ -411,7 +447,6 @@ __device__ __forceinline__ void stage_x(const Params& p, __half* xs, const uint4
                     xv[m] = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.x_stride + 8 * i));
                 }
                 if (sp && sp->n) add_slots_chunk(p, *sp, i, xv[0]);   // M == 1
-                else if (ADD_HEADS && p.add_heads) add_heads_chunk(p, i, xv[0]);
 #pragma unroll
                 for (int m = 0; m < MAX_M; ++m) {
                     if (m >= p.M) break;
