@@ -646,6 +646,8 @@ class NovaDecoder:
         self.cache = self.cache.grow(new_max_len)
         self.max_len = new_max_len
         self.cos, self.sin = rope_tables(self.max_len + 1, self.cfg.head_dim, self.cfg.rope_theta, self.device)
+        if self.heads and not self._heads_fit():   # more splits than o_proj's merge holds: the slots path
+            self.heads = False
         self.graph = None
 
     # ---------------------------------------------------------------- decode
