@@ -85,3 +85,36 @@ def test_pick_chunk_properties(max_len, batch):
     assert n_splits <= cap
     if -(-max_len // 8192) <= cap:
         assert chunk <= 8192
+
+
+def test_heads_major_reorders_units_by_column_block():
+    """o_proj's head-major unit stream: native unit (row group r, k-block b)
+    of an [N, K] matrix moves to block h = b // (K / 64 / heads), position
+    (h * N / 32 + r) * (K / 64 / heads) + b % (K / 64 / heads)."""
+    from nova_b200.kernels import heads_major
+
+    n, k, heads, unit = 2560, 4096, 8, 1088
+    rg, kb = n // 32, k // 64
+    per = kb // heads
+    ids = torch.arange(rg * kb, dtype=torch.int32)
+    stream = ids.view(-1, 1).expand(-1, unit // 4).contiguous().view(torch.uint8).view(-1)   # unit u filled with u
+    out = heads_major(stream, n, k, heads).view(-1, unit).view(torch.int32)[:, 0]
+    r, b = ids // kb, ids % kb
+    want_pos = ((b // per) * rg + r) * per + b % per
+    assert torch.equal(out[want_pos.long()], ids)
+
+
+def test_attention_partials_address():
+    """The split partials start at byte 256 + align_up(batch * kv_heads * 4,
+    256) of the attention workspace (the error word, then the per-head
+    arrival counters), the layout nova_attn_workspace_bytes sizes."""
+    from nova_b200.kvattn import attn_partials
+
+    ws = torch.zeros(1 << 20, dtype=torch.uint8)
+    base = ws.data_ptr()
+    assert attn_partials(ws, 1, 8) - base == 256 + 256
+    assert attn_partials(ws, 64, 8) - base == 256 + 2048
+    assert attn_partials(ws, 3, 7) - base == 256 + 256
+    from nova_b200.kvattn import attn_workspace_bytes   # the library sizes partials right after that offset
+
+    assert attn_workspace_bytes(1, 32, 8, 33, True) == 256 + 256 + 8 * 34 * 4 * 132 * 4
