@@ -118,3 +118,50 @@ def test_attention_partials_address():
     from nova_b200.kvattn import attn_workspace_bytes   # the library sizes partials right after that offset
 
     assert attn_workspace_bytes(1, 32, 8, 33, True) == 256 + 256 + 8 * 34 * 4 * 132 * 4
+
+
+def _heads_cta_range(c, G, nh, R, KB):
+    """Python restatement of the head-aligned CTA range of nf4.cu (heads_cta_range)."""
+    h = ((c + 1) * nh - 1) // G
+    c0 = G * h // nh
+    n = G * (h + 1) // nh - c0
+    j = c - c0
+    return (h * R + R * j // n) * KB, (h * R + R * (j + 1) // n) * KB, h
+
+
+@pytest.mark.parametrize("G,nh,R,KB", [(148, 8, 80, 8), (132, 8, 80, 8), (148, 4, 80, 16), (148, 8, 64, 8)])
+def test_head_aligned_o_proj_schedule_covers_every_row_group_once(G, nh, R, KB):
+    """o_proj over the attention's partials, on shapes nova_nf4_gemv accepts
+    (at least 16 units per CTA): the CTAs tile the (head, row group) stream
+    exactly, each CTA inside one head with whole row groups, and its 16
+    warps' consecutive ranges (1+ units each) tile the CTA's."""
+    assert (R // -(-G // nh)) * KB >= 16   # the host check of attn_part
+    seen = []
+    for c in range(G):
+        u0, u1, h = _heads_cta_range(c, G, nh, R, KB)
+        assert u0 % KB == 0 and u1 % KB == 0 and u1 > u0
+        assert h * R * KB <= u0 and u1 <= (h + 1) * R * KB, "a CTA crosses a head"
+        assert (u1 - u0) // KB + 1 <= 16, "more row groups than warps to sum them"
+        ws = [u0 + (u1 - u0) * w // 16 for w in range(17)]
+        assert ws[0] == u0 and ws[-1] == u1 and all(b - a >= 1 for a, b in zip(ws, ws[1:]))
+        seen.extend(range(u0, u1))
+    assert seen == list(range(nh * R * KB))
+
+
+def test_gate_up_cta_edges_match_the_consumer_boundaries():
+    """gate|up with CTA edges (19456 x 2560 on 148 SMs): every row group split
+    between CTAs has exactly two contributors (the last row group of one CTA,
+    the first of the next), and these are exactly the boundaries the
+    down_proj staging completes (edge_plan: u = units * b / G not a multiple
+    of the k-blocks per row group)."""
+    G, KB = 148, 40
+    units = (19456 // 32) * KB
+    ranges = [(units * c // G, units * (c + 1) // G) for c in range(G)]
+    split = {}
+    for c, (u0, u1) in enumerate(ranges):
+        for rg in range(u0 // KB, (u1 - 1) // KB + 1):
+            if not (u0 <= rg * KB and u1 >= (rg + 1) * KB):
+                split.setdefault(rg, []).append(c)
+    assert all(len(v) == 2 and v[1] == v[0] + 1 for v in split.values())
+    plan = {units * b // G // KB: (b - 1, b) for b in range(1, G) if (units * b // G) % KB}
+    assert plan == {rg: tuple(v) for rg, v in split.items()}
