@@ -655,7 +655,8 @@ struct EdgeRed {
     int rg;          // row group, -1: nothing to add
     int w0, n;       // contributors: CTA warps w0 .. w0 + n - 1
     unsigned slots;  // bit k: contributor w0 + k left it in its slot 1
-    int dst;         // -1: SiLU·mul epilogue; else edge_out slot index (CTA * 2 + 0 / 1)
+    int dst;         // -1: the launch's own epilogue (SiLU·mul; fp32 sums per head for o_proj over the
+                     // attention's partials); else edge_out slot index (CTA * 2 + 0 / 1)
 };
 
 // Static (int32, computed before the dependency wait; units * W < 2^31 host-checked).
